@@ -1,0 +1,29 @@
+// capi.cu — library-level entry points: version, status strings, PDL switch.
+
+#include <atomic>
+
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace iq36 {
+static std::atomic<int> g_pdl{1};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+}  // namespace iq36
+
+extern "C" const char* iq36_version(void) { return "iq36-b200 0.1.0 sm_100a"; }
+
+extern "C" const char* iq36_status_string(int status) {
+  switch (status) {
+    case IQ36_OK: return "ok";
+    case IQ36_ERR_ARG: return "invalid argument (null pointer or bad enum)";
+    case IQ36_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case IQ36_ERR_ALIGN: return "pointer alignment requirement violated";
+    case IQ36_ERR_WORKSPACE: return "workspace missing or too small";
+    case IQ36_ERR_CUDA: return "CUDA runtime error at launch";
+    case IQ36_ERR_TIMEOUT: return "bounded device wait expired";
+    case IQ36_ERR_DEVICE: return "device-side check failed";
+    default: return "unknown status";
+  }
+}
+
+extern "C" void iq36_set_pdl(int enabled) { iq36::g_pdl.store(enabled ? 1 : 0); }

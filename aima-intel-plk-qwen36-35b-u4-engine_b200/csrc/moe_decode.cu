@@ -1,0 +1,493 @@
+// moe_decode.cu — batch-1 router and routed/shared expert FFN.
+//
+// Reference semantics: run_qwen36_moe_ffn_layer (engine/src/gguf_loader.cpp:
+// 5654-5782) = select_router_topk (:3733-3743) -> gate_up matvec per selected
+// expert (:4316) -> apply_swiglu_from_gate_up (:4640-4668) -> down matvec
+// (:4467) -> apply_expert_weights (:3773-3797) -> aggregate_experts in rank
+// order (:3799-3819) -> + sigmoid(shared gate) * shared expert (:5767-5779).
+// The product runs the routed part in OpenVINO moe_3gemm_swiglu_opt
+// (engine/openvino/iq36-pr35924-grouped-postops.patch:86-124) and the router /
+// shared projections as the router_shared_input FC4 group
+// (tools/intel_qwen36_openvino_fixed_fc.py:166-177).
+//
+// Kernels (all launched with programmatic dependent launch):
+//   router_logits  — fp16 [E(+1), H] GEMV, warp per row, fp32 FMA, fixed order;
+//   router_select  — warp per token: fp64 softmax, top-k by (prob, -id) 64-bit
+//                    keys, fp32 renormalisation in rank order;
+//   moe_gate_up    — u4 dot engine; each warp's row A = gate row j, row B =
+//                    up row I+j of the same expert, so SwiGLU fuses into the
+//                    epilogue; writes act [slots, I] fp16 to the workspace;
+//   moe_down       — one CTA per 16 output rows, one warp per expert slot;
+//                    the weighted sum over slots runs in rank order in shared
+//                    memory (deterministic), shared expert added last.
+
+#include "launch.cuh"
+#include "u4_core.cuh"
+
+namespace iq36 {
+
+// ---------------------------------------------------------------------------
+// Router
+
+// Stage x (fp16, optionally RMS-normalised from fp32) in plain order.
+__device__ __forceinline__ void stage_x_plain(__half* xs, const __half* x16, const float* x32,
+                                              const float* nw, float eps, int H, float* red) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  float scale = 1.0f;
+  if (x32 != nullptr) {
+    float ss = 0.0f;
+    for (int i = tid; i < H; i += nt) ss = fmaf(x32[i], x32[i], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+      float v = tid < (nt >> 5) ? red[tid] : 0.0f;
+      v = warp_sum(v);
+      if (tid == 0) red[32] = rsqrtf(v / (float)H + eps);
+    }
+    __syncthreads();
+    scale = red[32];
+    for (int i = tid; i < H; i += nt) xs[i] = __float2half_rn(x32[i] * scale * nw[i]);
+  } else {
+    for (int i = tid; i < H; i += nt) xs[i] = x16[i];
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, const float* x32,
+                                                            const float* nw, float eps, int H,
+                                                            const __half* W, int E,
+                                                            const __half* wsg, float* logits,
+                                                            float* slogit) {
+  extern __shared__ __align__(16) __half xsh[];
+  __shared__ float nred[33];
+  pdl_wait();
+  const int tok = blockIdx.y;
+  stage_x_plain(xsh, x16 ? x16 + (size_t)tok * H : nullptr, x32 ? x32 + (size_t)tok * H : nullptr,
+                nw, eps, H, nred);
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  const __half* wr = nullptr;
+  if (row < E) wr = W + (size_t)row * H;
+  else if (row == E && wsg != nullptr) wr = wsg;
+  if (wr == nullptr) return;
+  float acc = 0.f;
+  const uint4* xv4 = reinterpret_cast<const uint4*>(xsh);
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 wv = ld_stream_v4(wr + c * 8);
+    const uint4 xv = xv4[c];
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 wf = __half22float2(wh[j]);
+      const float2 xf = __half22float2(xh[j]);
+      acc = fmaf(wf.x, xf.x, acc);
+      acc = fmaf(wf.y, xf.y, acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    if (row < E) logits[(size_t)tok * E + row] = acc;
+    else slogit[tok] = acc;
+  }
+}
+
+// Warp per token. E <= 256 (8 logits per lane), k <= 16.
+__global__ void __launch_bounds__(256) router_select_kernel(const float* logits, int T, int E,
+                                                            int k, int32_t* ids, float* weights) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= T) return;
+  const float* l = logits + (size_t)tok * E;
+  const int per = (E + 31) / 32;
+  float lv[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = lane + 32 * i;
+    lv[i] = (i < per && idx < E) ? l[idx] : -INFINITY;
+    mx = fmaxf(mx, lv[i]);
+  }
+  mx = warp_max(mx);
+  // softmax (gguf_loader.cpp:3646-3670): fp64 exp(l - max), fp64 sum,
+  // probabilities rounded to fp32.
+  double ev[8];
+  double s = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = lane + 32 * i;
+    ev[i] = (i < per && idx < E) ? exp((double)lv[i] - (double)mx) : 0.0;
+    s += ev[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  uint64_t key[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = lane + 32 * i;
+    const float p = (float)(ev[i] / s);
+    key[i] = (i < per && idx < E)
+                 ? (((uint64_t)__float_as_uint(p) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)idx))
+                 : 0ull;
+  }
+  // top_k_indices (:3672-3697): descending probability, lower id on ties —
+  // the larger 64-bit key (prob bits, inverted id) wins.
+  uint32_t sel_id[16];
+  float sel_p[16];
+  for (int r = 0; r < k; ++r) {
+    uint64_t best = 0ull;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best = key[i] > best ? key[i] : best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (key[i] == best) key[i] = 0ull;
+    sel_id[r] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+    sel_p[r] = __uint_as_float((uint32_t)(best >> 32));
+  }
+  if (lane == 0) {
+    // normalize_weights (:3712-3731), min sum 6.103515625e-5 (:5665).
+    float sum = 0.0f;
+    for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sel_p[r]);
+    const float den = fmaxf(sum, 6.103515625e-5f);
+    for (int r = 0; r < k; ++r) {
+      ids[(size_t)tok * k + r] = (int32_t)sel_id[r];
+      weights[(size_t)tok * k + r] = __fdiv_rn(sel_p[r], den);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Experts
+
+struct ExpertArgs {
+  const uint8_t* gu_w;
+  const __half* gu_s;
+  const uint8_t* gu_z;
+  const uint8_t* d_w;
+  const __half* d_s;
+  const uint8_t* d_z;
+  const uint8_t* sgu_w;
+  const __half* sgu_s;
+  const uint8_t* sgu_z;
+  const uint8_t* sd_w;
+  const __half* sd_s;
+  const uint8_t* sd_z;
+  int H, I, k, n_slots, num_experts;
+};
+
+template <int G>
+__global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const int32_t* ids,
+                                                          const __half* x16, __half* act,
+                                                          int ks_log2) {
+  extern __shared__ uint4 xs[];
+  __shared__ float red[8][16];
+  __shared__ float nred[33];
+  pdl_wait();
+  stage_x_perm(xs, x16, nullptr, nullptr, 0.f, a.H, nred);
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int KS = 1 << ks_log2;
+  const int rb = blockIdx.x * (8 >> ks_log2) + (warp >> ks_log2);
+  const int ks = warp & (KS - 1);
+  const int rb_per_exp = a.I / 8;
+  const int H = a.H, I = a.I, ng = H / G;
+  const bool valid = rb < a.n_slots * rb_per_exp;
+  const int slot = valid ? rb / rb_per_exp : 0;
+  const int j0 = (rb - slot * rb_per_exp) * 8;
+  float accA = 0.f, accB = 0.f;
+  if (valid) {
+    const uint8_t* w;
+    const __half* s;
+    const uint8_t* z;
+    int64_t zbase;
+    if (slot < a.k) {
+      const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
+      w = a.gu_w + e * (int64_t)(2 * I) * (H / 2);
+      s = a.gu_s + e * (int64_t)(2 * I) * ng;
+      z = a.gu_z;
+      zbase = e * (int64_t)(2 * I) * ng;
+    } else {
+      w = a.sgu_w;
+      s = a.sgu_s;
+      z = a.sgu_z;
+      zbase = 0;
+    }
+    const int rowA = j0 + g, rowB = I + j0 + g;
+    const int per = ng >> ks_log2;
+    u4_dot2<G, 4>(w + (size_t)rowA * (H / 2), w + (size_t)rowB * (H / 2), s + (size_t)rowA * ng,
+                  s + (size_t)rowB * ng, z, zbase + (int64_t)rowA * ng,
+                  zbase + (int64_t)rowB * ng, xs, ks * per, (ks + 1) * per, t, accA, accB);
+  }
+  if (KS > 1) {
+    if (t == 0) {
+      red[warp][g] = accA;
+      red[warp][g + 8] = accB;
+    }
+    __syncthreads();
+    if (ks == 0) {
+      accA = 0.f;
+      accB = 0.f;
+      for (int j = 0; j < KS; ++j) {
+        accA += red[warp + j][g];
+        accB += red[warp + j][g + 8];
+      }
+    }
+  }
+  if (valid && ks == 0 && t == 0) {
+    // SwiGLU: gate * sigmoid(gate) * up, rounded to fp16 (input of the down GEMV).
+    const float gate = accA, up = accB;
+    act[(size_t)slot * I + j0 + g] = __float2half_rn(gate * sigmoidf_acc(gate) * up);
+  }
+}
+
+template <int G>
+__global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* wts,
+                                const float* slogit, const __half* act, void* out, int out_dtype,
+                                int accumulate) {
+  extern __shared__ uint4 xs[];
+  __shared__ float red[16][16];
+  __shared__ float nred[33];
+  pdl_wait();
+  const int H = a.H, I = a.I, ngi = I / G;
+  stage_x_perm(xs, act, nullptr, nullptr, 0.f, a.n_slots * I, nred);
+  pdl_launch_dependents();
+  const int slot = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int h0 = blockIdx.x * 16;
+  const int rowA = min(h0 + g, H - 1), rowB = min(h0 + g + 8, H - 1);
+  const uint8_t* w;
+  const __half* s;
+  const uint8_t* z;
+  int64_t zbase;
+  if (slot < a.k) {
+    const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
+    w = a.d_w + e * (int64_t)H * (I / 2);
+    s = a.d_s + e * (int64_t)H * ngi;
+    z = a.d_z;
+    zbase = e * (int64_t)H * ngi;
+  } else {
+    w = a.sd_w;
+    s = a.sd_s;
+    z = a.sd_z;
+    zbase = 0;
+  }
+  float accA = 0.f, accB = 0.f;
+  u4_dot2<G, 4>(w + (size_t)rowA * (I / 2), w + (size_t)rowB * (I / 2), s + (size_t)rowA * ngi,
+                s + (size_t)rowB * ngi, z, zbase + (int64_t)rowA * ngi,
+                zbase + (int64_t)rowB * ngi, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+  if (t == 0) {
+    red[slot][g] = accA;
+    red[slot][g + 8] = accB;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x, row = h0 + r;
+    if (row < H) {
+      float y = 0.0f;
+      for (int j = 0; j < a.k; ++j) y = __fadd_rn(y, __fmul_rn(red[j][r], wts[j]));
+      if (a.n_slots > a.k) y = __fadd_rn(y, __fmul_rn(red[a.k][r], sigmoidf_acc(slogit[0])));
+      if (out_dtype == IQ36_F16) {
+        reinterpret_cast<__half*>(out)[row] = __float2half_rn(y);
+      } else if (accumulate) {
+        float* o = reinterpret_cast<float*>(out);
+        o[row] = o[row] + __half2float(__float2half_rn(y));
+      } else {
+        reinterpret_cast<float*>(out)[row] = y;
+      }
+    }
+  }
+}
+
+int u4_ks_log2(int total_rb, int ng);
+
+static int check_bank(const iq36_expert_bank* b) {
+  if (!b || !b->gate_up_weight || !b->gate_up_scale || !b->gate_up_zp || !b->down_weight ||
+      !b->down_scale || !b->down_zp)
+    return IQ36_ERR_ARG;
+  const int G = b->group, H = b->hidden, I = b->intermediate;
+  if (G != 64 && G != 128) return IQ36_ERR_SHAPE;
+  if (b->num_experts < 1 || H < G || I < G || H % G || I % G || H % 16 || I % 8 || H > 16384)
+    return IQ36_ERR_SHAPE;
+  if (!aligned(b->gate_up_weight, 16) || !aligned(b->down_weight, 16)) return IQ36_ERR_ALIGN;
+  return IQ36_OK;
+}
+
+size_t moe_decode_ws(int k, int hidden, int intermediate) {
+  (void)hidden;
+  return (((size_t)(k + 1) * intermediate * 2) + 255) / 256 * 256;
+}
+
+int moe_decode_launch(const void* x_f16, const int32_t* ids, const float* weights, int k,
+                      const iq36_expert_bank* routed, const iq36_expert_bank* shared,
+                      const float* shared_logit, void* out, int out_dtype, int accumulate,
+                      void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int st = check_bank(routed);
+  if (st != IQ36_OK) return st;
+  if (!x_f16 || !ids || !weights || !out) return IQ36_ERR_ARG;
+  if (!aligned(x_f16, 16)) return IQ36_ERR_ALIGN;
+  if (k < 1 || k > 15 || k > routed->num_experts) return IQ36_ERR_SHAPE;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
+  if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
+  ExpertArgs a = {};
+  a.gu_w = routed->gate_up_weight;
+  a.gu_s = reinterpret_cast<const __half*>(routed->gate_up_scale);
+  a.gu_z = routed->gate_up_zp;
+  a.d_w = routed->down_weight;
+  a.d_s = reinterpret_cast<const __half*>(routed->down_scale);
+  a.d_z = routed->down_zp;
+  a.H = routed->hidden;
+  a.I = routed->intermediate;
+  a.k = k;
+  a.n_slots = k;
+  a.num_experts = routed->num_experts;
+  if (shared) {
+    st = check_bank(shared);
+    if (st != IQ36_OK) return st;
+    if (shared->hidden != a.H || shared->intermediate != a.I || shared->group != routed->group)
+      return IQ36_ERR_SHAPE;
+    if (!shared_logit) return IQ36_ERR_ARG;
+    a.sgu_w = shared->gate_up_weight;
+    a.sgu_s = reinterpret_cast<const __half*>(shared->gate_up_scale);
+    a.sgu_z = shared->gate_up_zp;
+    a.sd_w = shared->down_weight;
+    a.sd_s = reinterpret_cast<const __half*>(shared->down_scale);
+    a.sd_z = shared->down_zp;
+    a.n_slots = k + 1;
+  }
+  if (!ws || ws_bytes < moe_decode_ws(k, a.H, a.I)) return IQ36_ERR_WORKSPACE;
+  if (!aligned(ws, 16)) return IQ36_ERR_ALIGN;
+  __half* act = reinterpret_cast<__half*>(ws);
+  const int G = routed->group;
+  const int ng = a.H / G;
+  const int total_rb = a.n_slots * (a.I / 8);
+  const int ks_log2 = u4_ks_log2(total_rb, ng);
+  const dim3 grid1(ceil_div(total_rb, 8 >> ks_log2));
+  const size_t smem1 = (size_t)a.H / 8 * sizeof(uint4);
+  const __half* xh = reinterpret_cast<const __half*>(x_f16);
+  cudaError_t e;
+  if (G == 128)
+    e = launch(moe_gate_up_kernel<128>, grid1, dim3(256), smem1, stream, a, ids, xh, act, ks_log2);
+  else
+    e = launch(moe_gate_up_kernel<64>, grid1, dim3(256), smem1, stream, a, ids, xh, act, ks_log2);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  const dim3 grid2(ceil_div(a.H, 16));
+  const size_t smem2 = (size_t)a.n_slots * a.I / 8 * sizeof(uint4);
+  const __half* acth = act;
+  if (G == 128)
+    e = launch(moe_down_kernel<128>, grid2, dim3(32 * a.n_slots), smem2, stream, a, ids, weights,
+               shared_logit, acth, out, out_dtype, accumulate);
+  else
+    e = launch(moe_down_kernel<64>, grid2, dim3(32 * a.n_slots), smem2, stream, a, ids, weights,
+               shared_logit, acth, out, out_dtype, accumulate);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw, float eps, int T,
+                         int H, const void* w_router, int E, const void* w_sg, float* logits,
+                         float* slogit, cudaStream_t stream) {
+  if (!w_router || !logits || T < 1 || E < 1 || H < 8 || H % 8) return IQ36_ERR_ARG;
+  if (w_sg && !slogit) return IQ36_ERR_ARG;
+  if (x_f32) {
+    if (x_f16 || !nw) return IQ36_ERR_ARG;
+  } else if (!x_f16) {
+    return IQ36_ERR_ARG;
+  }
+  if (!aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) || (x_f16 && !aligned(x_f16, 16)))
+    return IQ36_ERR_ALIGN;
+  const int rows = E + (w_sg ? 1 : 0);
+  const dim3 grid(ceil_div(rows, 8), T);
+  const cudaError_t e = launch(router_logits_kernel, grid, dim3(256), (size_t)H * 2, stream,
+                               reinterpret_cast<const __half*>(x_f16), x_f32, nw, eps, H,
+                               reinterpret_cast<const __half*>(w_router), E,
+                               reinterpret_cast<const __half*>(w_sg), logits, slogit);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+int router_select_launch(const float* logits, int T, int E, int k, int32_t* ids, float* weights,
+                         cudaStream_t stream) {
+  if (!logits || !ids || !weights) return IQ36_ERR_ARG;
+  if (T < 1 || E < 1 || E > 256 || k < 1 || k > 16 || k > E) return IQ36_ERR_SHAPE;
+  const cudaError_t e = launch(router_select_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream,
+                               logits, T, E, k, ids, weights);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+}  // namespace iq36
+
+extern "C" int iq36_router_logits(const void* x_f16, const float* x_f32, const float* norm_weight,
+                                  float norm_eps, int32_t T, int32_t H, const void* w_router_f16,
+                                  int32_t E, const void* w_shared_gate_f16, float* logits,
+                                  float* shared_logit, iq36_stream_t stream) {
+  return iq36::router_logits_launch(x_f16, x_f32, norm_weight, norm_eps, T, H, w_router_f16, E,
+                                    w_shared_gate_f16, logits, shared_logit,
+                                    iq36::as_stream(stream));
+}
+
+extern "C" int iq36_router_select(const float* logits, int32_t T, int32_t E, int32_t k,
+                                  int32_t* ids, float* weights, iq36_stream_t stream) {
+  return iq36::router_select_launch(logits, T, E, k, ids, weights, iq36::as_stream(stream));
+}
+
+extern "C" size_t iq36_moe_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate) {
+  return iq36::moe_decode_ws(k, hidden, intermediate);
+}
+
+extern "C" int iq36_moe_decode(const void* x_f16, const int32_t* ids, const float* weights,
+                               int32_t k, const iq36_expert_bank* routed,
+                               const iq36_expert_bank* shared, const float* shared_logit,
+                               void* out, int32_t out_dtype, int32_t accumulate, void* workspace,
+                               size_t workspace_bytes, iq36_stream_t stream) {
+  return iq36::moe_decode_launch(x_f16, ids, weights, k, routed, shared, shared_logit, out,
+                                 out_dtype, accumulate, workspace, workspace_bytes,
+                                 iq36::as_stream(stream));
+}
+
+extern "C" size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden,
+                                                        int32_t intermediate) {
+  return iq36::moe_decode_ws(k, hidden, intermediate) + 256;
+}
+
+extern "C" int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16,
+                                     const void* w_shared_gate_f16, int32_t k,
+                                     const iq36_expert_bank* routed,
+                                     const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                                     float* logits, void* out, int32_t out_dtype, void* workspace,
+                                     size_t workspace_bytes, iq36_stream_t stream) {
+  using namespace iq36;
+  if (!routed || !workspace || !x_f16 || !w_router_f16 || !ids || !weights || !logits || !out)
+    return IQ36_ERR_ARG;
+  if (shared && !w_shared_gate_f16) return IQ36_ERR_ARG;
+  // Validate everything before the first launch so a failed call enqueues nothing.
+  int st0 = check_bank(routed);
+  if (st0 == IQ36_OK && shared) st0 = check_bank(shared);
+  if (st0 != IQ36_OK) return st0;
+  if (shared && (shared->hidden != routed->hidden || shared->intermediate != routed->intermediate ||
+                 shared->group != routed->group))
+    return IQ36_ERR_SHAPE;
+  if (k < 1 || k > 15 || k > routed->num_experts || routed->num_experts > 256)
+    return IQ36_ERR_SHAPE;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
+  if (!aligned(x_f16, 16) || !aligned(w_router_f16, 16) ||
+      (shared && !aligned(w_shared_gate_f16, 16)) || !aligned(workspace, 256))
+    return IQ36_ERR_ALIGN;
+  const size_t need = iq36_moe_block_decode_workspace_bytes(k, routed->hidden, routed->intermediate);
+  if (workspace_bytes < need) return IQ36_ERR_WORKSPACE;
+  float* slogit = reinterpret_cast<float*>(workspace);
+  void* ws2 = reinterpret_cast<char*>(workspace) + 256;
+  const cudaStream_t s = as_stream(stream);
+  int st = router_logits_launch(x_f16, nullptr, nullptr, 0.f, 1, routed->hidden, w_router_f16,
+                                routed->num_experts, shared ? w_shared_gate_f16 : nullptr, logits,
+                                slogit, s);
+  if (st != IQ36_OK) return st;
+  st = router_select_launch(logits, 1, routed->num_experts, k, ids, weights, s);
+  if (st != IQ36_OK) return st;
+  return moe_decode_launch(x_f16, ids, weights, k, routed, shared, shared ? slogit : nullptr, out,
+                           out_dtype, 0, ws2, workspace_bytes - 256, s);
+}

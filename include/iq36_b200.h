@@ -1,0 +1,256 @@
+/*
+ * iq36_b200.h — C ABI of the B200 (sm_100a) batch-1 hot path of a
+ * Qwen3.6-35B-A3B-shaped hybrid MoE.
+ *
+ * Conventions shared by every entry point:
+ *   - all tensor pointers are caller-owned DEVICE memory;
+ *   - work is enqueued on the caller's stream (cudaStream_t passed as void*;
+ *     NULL = legacy default stream); no entry point synchronises or allocates;
+ *   - the return value is 0 (IQ36_OK) or a negative iq36_status; shape and
+ *     pointer checks happen on the host before any launch, so a failed call has
+ *     enqueued nothing;
+ *   - fp16 tensors are IEEE binary16 passed as uint16_t / void*.
+ *
+ * u4 matrix layout (the OpenVINO compressed-constant layout before the
+ * reference's group-major repack; reference
+ * tools/intel_qwen36_openvino_fixed_fc.py:107-144, shapes [M, K/G, G]):
+ *   weight [rows, K/2] u8, two codes per byte, LOW nibble = even k
+ *          (engine/openvino/custom/iq36_fixed_fc_multi_output.cl:122-124);
+ *   scale  [rows, K/G] fp16;
+ *   zp     [rows*K/G/2] u8, code (row, g) at element row*(K/G)+g, low nibble =
+ *          even element (fixed_fc.py:240-248 unpacks the same way).
+ *   w[row, k] = (q[row, k] - zp[row, k/G]) * scale[row, k/G].
+ */
+#ifndef IQ36_B200_H
+#define IQ36_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* iq36_stream_t; /* cudaStream_t */
+
+enum iq36_status {
+  IQ36_OK = 0,
+  IQ36_ERR_ARG = -1,       /* null pointer or bad enum value */
+  IQ36_ERR_SHAPE = -2,     /* unsupported or inconsistent shape */
+  IQ36_ERR_ALIGN = -3,     /* pointer alignment requirement violated */
+  IQ36_ERR_WORKSPACE = -4, /* workspace missing or too small */
+  IQ36_ERR_CUDA = -5,      /* CUDA runtime error at launch */
+  IQ36_ERR_TIMEOUT = -6,   /* a bounded device-side wait expired */
+  IQ36_ERR_DEVICE = -7     /* a device-side check wrote an error word */
+};
+
+enum iq36_dtype { IQ36_F32 = 0, IQ36_F16 = 1, IQ36_BF16 = 2 };
+
+typedef struct {
+  const uint8_t* weight;
+  const uint16_t* scale;
+  const uint8_t* zp;
+  int32_t rows;
+} iq36_u4_matrix;
+
+/* One output of a multi-output u4 GEMV launch. accumulate=1 adds into an fp32
+ * output (residual update) instead of overwriting it. */
+typedef struct {
+  iq36_u4_matrix m;
+  void* out;
+  int32_t out_dtype;
+  int32_t accumulate;
+} iq36_u4_projection;
+
+/* A bank of E experts, each gate_up [2I, H] (rows 0..I-1 = gate, I..2I-1 = up)
+ * and down [H, I], all u4 group-G, expert-major contiguous. */
+typedef struct {
+  const uint8_t* gate_up_weight;  /* [E, 2I, H/2]      */
+  const uint16_t* gate_up_scale;  /* [E, 2I, H/G]      */
+  const uint8_t* gate_up_zp;      /* [E, 2I*H/G/2]     */
+  const uint8_t* down_weight;     /* [E, H, I/2]       */
+  const uint16_t* down_scale;     /* [E, H, I/G]       */
+  const uint8_t* down_zp;         /* [E, H*I/G/2]      */
+  int32_t num_experts;
+  int32_t hidden;
+  int32_t intermediate;
+  int32_t group;
+} iq36_expert_bank;
+
+const char* iq36_version(void);
+const char* iq36_status_string(int status);
+
+/* ---- (1) u4 group-wise asymmetric GEMV -------------------------------------
+ * out[n] = sum_k x[k] * (q[n,k] - zp[n,k/G]) * scale[n,k/G]; fp32 accumulate,
+ * out fp32 or fp16 (RTE).
+ * Replaces the custom op IQ36FixedFC1 (engine/openvino/custom/
+ * iq36_fixed_fc_multi_output.cl:36-44, scalar semantics :112-167; op class
+ * tools/intel_qwen36_openvino_fixed_fc.py:31-92).
+ * Requirements: G in {64,128}; K % G == 0; 16 <= K <= 16384; rows >= 1;
+ * weight 16-byte aligned and K/2 % 16 == 0; x 16-byte aligned. */
+int iq36_u4_gemv(const void* x_f16, int32_t K, int32_t G, const iq36_u4_matrix* w,
+                 void* out, int32_t out_dtype, iq36_stream_t stream);
+
+/* Arity-1..4 multi-output launch sharing one activation: replaces
+ * IQ36FixedFC{1,3,4} (iq36_fixed_fc_multi_output.cl:6-29,45-85; grouping
+ * fixed_fc.py:180-215). The optional fused prologue applies RMSNorm to an fp32
+ * input before the GEMV (norm_weight != NULL): x = f16(in * rsqrt(mean(in^2) +
+ * eps) * norm_weight), as gguf_loader.cpp:3368-3391 then the f16 Convert of
+ * fixed_fc.py:292-296. x_f16 must be NULL in that case, and x_f32 set. */
+int iq36_u4_gemv_multi(const void* x_f16, const float* x_f32, const float* norm_weight,
+                       float norm_eps, int32_t K, int32_t G, int32_t n_proj,
+                       const iq36_u4_projection* proj, iq36_stream_t stream);
+
+/* ---- (4) router -------------------------------------------------------------
+ * logits[t, e] = sum_h x[t,h] * W[e,h] (fp16 weights, fp32 accumulate); the
+ * optional extra fp16 row (shared-expert gate, 2048->1) writes
+ * shared_logit[t]. Replaces the router/shared-gate outputs of the
+ * router_shared_input FC4 group (fixed_fc.py:166-177). */
+int iq36_router_logits(const void* x_f16, const float* x_f32, const float* norm_weight,
+                       float norm_eps, int32_t T, int32_t H, const void* w_router_f16,
+                       int32_t E, const void* w_shared_gate_f16, float* logits,
+                       float* shared_logit, iq36_stream_t stream);
+
+/* Selection on fp32 logits, per token: probs = softmax (fp64 exp and sum,
+ * rounded to fp32), ids = top-k by (prob desc, id asc), weights = probs[ids] /
+ * max(sum_fp32(probs[ids]), 6.103515625e-5). Bit-exact restatement of
+ * select_router_topk (engine/src/gguf_loader.cpp:3646-3743).
+ * Requirements: 1 <= k <= 16, k <= E <= 256. */
+int iq36_router_select(const float* logits, int32_t T, int32_t E, int32_t k,
+                       int32_t* ids, float* weights, iq36_stream_t stream);
+
+/* ---- (2a) MoE decode (batch 1) ---------------------------------------------
+ * out = sum_{r<k} weights[r] * Down_{ids[r]}(SwiGLU(GateUp_{ids[r]}(x)))
+ *       [+ sigmoid(shared_logit) * Down_s(SwiGLU(GateUp_s(x)))]
+ * SwiGLU(g,u) = g*sigmoid(g)*u, rounded to fp16 as the down GEMV input; expert
+ * sum in fp32 in rank order, shared expert added last.
+ * Follows run_qwen36_moe_ffn_layer (engine/src/gguf_loader.cpp:5654-5782) and
+ * the routed part of OpenVINO moe_3gemm_swiglu_opt (patch
+ * engine/openvino/iq36-pr35924-grouped-postops.patch:86-124).
+ * accumulate=1: out must be fp32 and receives out += result (residual). */
+int iq36_moe_decode(const void* x_f16, const int32_t* ids, const float* weights, int32_t k,
+                    const iq36_expert_bank* routed, const iq36_expert_bank* shared,
+                    const float* shared_logit, void* out, int32_t out_dtype,
+                    int32_t accumulate, void* workspace, size_t workspace_bytes,
+                    iq36_stream_t stream);
+size_t iq36_moe_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
+
+/* Config-1 block: router logits -> select -> routed + shared experts.
+ * ids/weights/logits are outputs (device). */
+int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16, const void* w_shared_gate_f16,
+                          int32_t k, const iq36_expert_bank* routed,
+                          const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                          float* logits, void* out, int32_t out_dtype, void* workspace,
+                          size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
+
+/* ---- (2b) grouped MoE prefill ----------------------------------------------
+ * For T tokens with top-k routing (ids, weights [T,k]): permute token rows by
+ * expert (stable: by expert, then token, then rank), per expert
+ * Y = SwiGLU(X W_gu^T) W_d^T on tcgen05 tensor cores (u4 dequantised to bf16 in
+ * shared memory), then out[t] = sum_{r<k} weights[t,r] * Y[row(t,r)] in rank
+ * order. Follows the Gen-1 schedule grouped_s8_u4_f16_contribution_moe.cl:13-222
+ * and scatter :847-861, and the stock gather/GEMM/scatter of
+ * iq36-pr35924-grouped-postops.patch:15-124. x bf16 [T, H]; out fp32/bf16.
+ * Requirements: H % 128 == 0, I % 128 == 0, G == 128. */
+int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids, const float* weights,
+                     int32_t k, const iq36_expert_bank* routed, void* out, int32_t out_dtype,
+                     void* workspace, size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_moe_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
+                                        int32_t hidden, int32_t intermediate);
+
+/* ---- (3) paged GQA decode attention ----------------------------------------
+ * o[h] = sum_t softmax_t(q[h].k[t,h/grp] * scale) v[t,h/grp], then
+ * o *= sigmoid(gate[h]) when gate != NULL. KV cache fp16
+ * [num_blocks, block_size, n_kv_heads, head_dim] (K and V separate); token t
+ * lives in block block_table[t / block_size], slot t % block_size.
+ * Split-K flash decode; follows run_qwen36_full_attention_core
+ * (gguf_loader.cpp:6071-6137), the gate run_qwen36_full_attention_gate
+ * (:6034-6069) and the split/reduce structure of
+ * engine/gpu/opencl/fused_gqa_fp16_kv_decode.cl:16-115.
+ * ctx_len_dev (optional, device int32) overrides ctx_len at run time so a
+ * captured CUDA graph can be replayed as the context grows; ctx_len is then the
+ * capacity that sizes the launch.
+ * Requirements: head_dim == 256, n_q_heads / n_kv_heads == 8, block_size == 16. */
+int iq36_paged_gqa_decode(const void* q_f16, const void* k_cache, const void* v_cache,
+                          const int32_t* block_table, int32_t ctx_len, const int32_t* ctx_len_dev,
+                          int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                          int32_t block_size, float scale, const void* gate_f16, void* out,
+                          int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                          iq36_stream_t stream);
+size_t iq36_paged_gqa_workspace_bytes(int32_t max_ctx, int32_t n_q_heads, int32_t n_kv_heads,
+                                      int32_t head_dim);
+
+/* ---- config-4 support ops ---------------------------------------------------*/
+
+/* out[r] = f(in[r] * rsqrt(mean(in[r]^2) + eps) * weight); gguf_loader.cpp:3368-3391
+ * (rows of dim), apply_repeated_rms_norm :3410-3439 when weight_len < dim. */
+int iq36_rms_norm(const float* in, int32_t rows, int32_t dim, const float* weight,
+                  int32_t weight_len, float eps, void* out, int32_t out_dtype,
+                  iq36_stream_t stream);
+
+/* Full-attention pre-step for one token: split q_full [n_q, 2, D] into q and
+ * gate, per-head RMSNorm of q and k (weights [D]), partial rotate-half RoPE on
+ * the first rope_dim dims at position *pos_dev (base rope_base), write q_out
+ * [n_q, D] f16 and gate_out [n_q, D] f16, and append k, v (f16 [n_kv, D]) at
+ * token *pos_dev of the paged cache. gguf_loader.cpp:5928-5950 (split/norm),
+ * engine/openvino/custom/iq36_qk_rope_layout.cl:12-60 (rotate-half on dims <
+ * 64), iq36_hot_ring_update.cl:7-28 (slot write). */
+int iq36_attn_prep(const void* q_full_f16, const void* k_f16, const void* v_f16,
+                   const float* q_norm_w, const float* k_norm_w, float eps,
+                   const int32_t* pos_dev, int32_t n_q_heads, int32_t n_kv_heads,
+                   int32_t head_dim, int32_t rope_dim, float rope_base,
+                   const int32_t* block_table, int32_t block_size, void* k_cache,
+                   void* v_cache, void* q_out_f16, void* gate_out_f16, iq36_stream_t stream);
+
+/* DeltaNet pre-step for one token: causal depthwise conv (width 4, carried
+ * state [C,4]) + SiLU with the fp16 rounding points of
+ * engine/openvino/custom/iq36_linear_conv_swish.cl:12-64, and the gate/beta
+ * transform g = -exp(A_log) * softplus(a + dt_bias), beta = sigmoid(b)
+ * (gguf_loader.cpp:4875-4912). qkv_act_f16 [C]; g_out, beta_out fp32 [nv]. */
+int iq36_delta_prep(const void* qkv_f16, int32_t channels, float* conv_state,
+                    const float* conv_w, const void* a_f16, const void* b_f16,
+                    const float* a_log, const float* dt_bias, int32_t n_v_heads,
+                    void* qkv_act_f16, float* g_out, float* beta_out, iq36_stream_t stream);
+
+/* Gated DeltaNet recurrence for one token, OpenVINO head mapping (key head =
+ * value head / (nv/nk)), L2 norm rsqrt(sum+1e-6), q * 1/sqrt(D); state
+ * [nv, D(key), D(value)] fp32 updated in place; then gated RMSNorm
+ * o * rsqrt(mean(o^2)+eps) * norm_w * silu(z) -> f16.
+ * engine/openvino/custom/iq36_gated_delta_net.cl:36-150,
+ * gguf_loader.cpp:4770-4786. */
+int iq36_delta_step(const void* qkv_act_f16, const float* g, const float* beta, float* state,
+                    const void* z_f16, const float* norm_w, float eps, int32_t n_k_heads,
+                    int32_t n_v_heads, int32_t head_dim, void* out_f16, iq36_stream_t stream);
+
+/* h[:] = float(embedding[*token_dev, :]) (fp16 table [vocab, H]). */
+int iq36_embed(const void* table_f16, int32_t vocab, int32_t hidden, const int32_t* token_dev,
+               float* h, iq36_stream_t stream);
+
+/* Greedy top-1 over fp32 logits, lowest id on ties: per-block maxima of the
+ * 64-bit key (order-preserving fp32 bits, inverted id), then one merge block
+ * (engine/openvino/custom/iq36_greedy_top1.cl:8-46 and
+ * iq36_greedy_top1_merge.cl). token_out int32[1]; workspace holds the
+ * per-block keys (no initialisation needed). */
+int iq36_argmax(const float* logits, int32_t n, int32_t* token_out, void* workspace,
+                size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_argmax_workspace_bytes(void);
+
+/* Fill device buffers with the synthetic generator of iq36_synth.h.
+ * kind: 0 = u8 codes, 1 = fp16 uniform [lo,hi), 2 = fp16 normal(std=lo),
+ * 3 = fp32 uniform [lo,hi), 4 = fp32 normal(std=lo). */
+int iq36_synth_fill(void* dst, int64_t count, int32_t kind, uint64_t seed, uint64_t tensor,
+                    float lo, float hi, iq36_stream_t stream);
+/* Tensor naming and distributions of the synthetic model (iq36_synth.h). */
+uint64_t iq36_synth_tensor_id(int32_t layer, int32_t slot, int32_t sub);
+void iq36_synth_tensor_spec(int32_t slot, int32_t sub, int32_t* kind, float* lo, float* hi);
+
+/* Programmatic dependent launch on (default) or off for every later launch
+ * of this library in the process. */
+void iq36_set_pdl(int enabled);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IQ36_B200_H */

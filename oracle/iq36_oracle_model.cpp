@@ -1,0 +1,296 @@
+// iq36_oracle_model.cpp — CPU restatement of the batch-1 decode step of the
+// synthetic Qwen3.6-35B-A3B-shaped model.
+//
+// TEST INFRASTRUCTURE ONLY (see iq36_oracle.cpp). Composes the per-op
+// restatements in the order of the reference graph (SURVEY call stack; per
+// layer: RMSNorm -> attention or DeltaNet -> residual -> RMSNorm -> router +
+// routed/shared experts -> residual; then final RMSNorm -> LM head -> greedy),
+// following gguf_loader.cpp run_qwen36_layer_with_external_attention_state
+// (:6207-6242), run_qwen36_stateful_full_attention_layer (:6140-6205) and
+// run_qwen36_moe_ffn_layer (:5654-5782), with the OpenVINO fp16 rounding points
+// (every fixed-FC output rounded to fp16: iq36_fixed_fc_multi_output.cl:198).
+// Weights come from the shared synthetic generator (include/iq36_synth.h).
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "../include/iq36_synth.h"
+
+extern "C" {
+void orc_synth_fill(void* dst, int64_t count, int kind, uint64_t seed, uint64_t tensor, float lo,
+                    float hi);
+void orc_u4_gemv(const uint16_t* x_f16, int K, int G, const uint8_t* w, const uint16_t* scale,
+                 const uint8_t* zp, int64_t N, float* out, int precise, int threads);
+void orc_f16_linear(const uint16_t* x_f16, int H, const uint16_t* W, int E, float* out);
+void orc_router_select(const float* logits, int T, int E, int k, int32_t* ids, float* weights);
+void orc_moe_decode(const uint16_t* x_f16, const int32_t* ids, const float* weights, int k,
+                    const uint8_t* gu_w, const uint16_t* gu_s, const uint8_t* gu_z,
+                    const uint8_t* d_w, const uint16_t* d_s, const uint8_t* d_z,
+                    const uint8_t* sgu_w, const uint16_t* sgu_s, const uint8_t* sgu_z,
+                    const uint8_t* sd_w, const uint16_t* sd_s, const uint8_t* sd_z,
+                    const float* shared_logit, int H, int I, int G, float* out, int precise,
+                    int threads);
+void orc_paged_gqa(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* bt,
+                   int ctx, int nq, int nkv, int D, int bs, float scale, const uint16_t* gate,
+                   float* out, int threads);
+void orc_rms_norm(const float* in, int rows, int dim, const float* w, int wlen, float eps,
+                  float* out);
+void orc_attn_prep(const uint16_t* q_full, const uint16_t* k, const uint16_t* v,
+                   const float* qn_w, const float* kn_w, float eps, int pos, int nq, int nkv,
+                   int D, int rope_dim, float base, float* q_out, float* gate_out, float* k_new,
+                   float* v_new);
+void orc_delta_prep(const uint16_t* qkv, int C, float* conv_state, const float* conv_w,
+                    const uint16_t* a, const uint16_t* b, const float* a_log,
+                    const float* dt_bias, int nv, float* act_out, float* g_out, float* beta_out);
+void orc_delta_step(const float* act, const float* g, const float* beta, float* state,
+                    const uint16_t* z, const float* norm_w, float eps, int nk, int nv, int D,
+                    float* out);
+int orc_argmax(const float* logits, int64_t n);
+}
+
+namespace {
+
+inline uint16_t f2h(float f) {
+  _Float16 v = (_Float16)f;
+  uint16_t h;
+  std::memcpy(&h, &v, 2);
+  return h;
+}
+inline float h2f(uint16_t h) {
+  _Float16 v;
+  std::memcpy(&v, &h, 2);
+  return (float)v;
+}
+
+}  // namespace
+
+// Model dimensions; the field order is part of the C ABI of this file.
+struct OrcModelConfig {
+  int32_t hidden, layers, attn_interval, nq, nkv, head_dim, rope_dim, nk, nv, dk, conv, experts,
+      topk, inter, shared_inter, vocab, group;
+  float rope_base, eps;
+};
+
+namespace {
+
+struct U4 {
+  std::vector<uint8_t> w, z;
+  std::vector<uint16_t> s;
+  int64_t rows = 0;
+  int K = 0;
+};
+
+struct Layer {
+  bool attn = false;
+  std::vector<float> in_norm, post_norm;
+  U4 q, k, v, o;                                  // attention
+  std::vector<float> qn, kn;
+  U4 qkv, z, a, b, out;                           // DeltaNet
+  std::vector<float> conv_w, a_log, dt_bias, dnorm;
+  std::vector<uint16_t> router, sgate;            // MoE
+  U4 gu, down, sgu, sdown;
+  // state
+  std::vector<float> conv_state, rec_state;
+  std::vector<uint16_t> kc, vc;
+};
+
+struct Model {
+  OrcModelConfig c;
+  uint64_t seed;
+  int max_ctx;
+  std::vector<Layer> layers;
+  std::vector<float> final_norm;
+  U4 lm_head;
+  std::vector<int32_t> bt;
+};
+
+void fill_f32(std::vector<float>& v, int64_t n, uint64_t seed, int layer, int slot) {
+  int kind;
+  float lo, hi;
+  iq36_synth_spec(slot, 0, &kind, &lo, &hi);
+  v.resize(n);
+  orc_synth_fill(v.data(), n, kind, seed, iq36_tensor_id(layer, slot, 0), lo, hi);
+}
+
+void fill_f16(std::vector<uint16_t>& v, int64_t n, uint64_t seed, int layer, int slot) {
+  int kind;
+  float lo, hi;
+  iq36_synth_spec(slot, 0, &kind, &lo, &hi);
+  v.resize(n);
+  orc_synth_fill(v.data(), n, kind, seed, iq36_tensor_id(layer, slot, 0), lo, hi);
+}
+
+void fill_u4(U4& m, int64_t rows, int K, int G, uint64_t seed, int layer, int slot) {
+  m.rows = rows;
+  m.K = K;
+  const int64_t nw = rows * K / 2, ns = rows * K / G, nz = rows * K / G / 2;
+  m.w.resize(nw);
+  m.s.resize(ns);
+  m.z.resize(nz);
+  int kind;
+  float lo, hi;
+  iq36_synth_spec(slot, 0, &kind, &lo, &hi);
+  orc_synth_fill(m.w.data(), nw, kind, seed, iq36_tensor_id(layer, slot, 0), lo, hi);
+  iq36_synth_spec(slot, 1, &kind, &lo, &hi);
+  orc_synth_fill(m.s.data(), ns, kind, seed, iq36_tensor_id(layer, slot, 1), lo, hi);
+  iq36_synth_spec(slot, 2, &kind, &lo, &hi);
+  orc_synth_fill(m.z.data(), nz, kind, seed, iq36_tensor_id(layer, slot, 2), lo, hi);
+}
+
+void gemv16(const U4& m, const uint16_t* x, int G, std::vector<float>& y, int threads) {
+  y.resize(m.rows);
+  orc_u4_gemv(x, m.K, G, m.w.data(), m.s.data(), m.z.data(), m.rows, y.data(), 0, threads);
+}
+
+std::vector<uint16_t> to_f16(const std::vector<float>& v) {
+  std::vector<uint16_t> r(v.size());
+  for (size_t i = 0; i < v.size(); ++i) r[i] = f2h(v[i]);
+  return r;
+}
+
+}  // namespace
+
+extern "C" {
+
+void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
+  auto* M = new Model();
+  M->c = *cfg;
+  M->seed = seed;
+  M->max_ctx = max_ctx;
+  const OrcModelConfig& c = *cfg;
+  const int H = c.hidden, G = c.group;
+  M->layers.resize(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    Layer& L = M->layers[l];
+    L.attn = (l % c.attn_interval) == (c.attn_interval - 1);
+    fill_f32(L.in_norm, H, seed, l, IQ36_T_IN_NORM);
+    fill_f32(L.post_norm, H, seed, l, IQ36_T_POST_NORM);
+    if (L.attn) {
+      fill_u4(L.q, (int64_t)2 * c.nq * c.head_dim, H, G, seed, l, IQ36_T_Q);
+      fill_u4(L.k, (int64_t)c.nkv * c.head_dim, H, G, seed, l, IQ36_T_K);
+      fill_u4(L.v, (int64_t)c.nkv * c.head_dim, H, G, seed, l, IQ36_T_V);
+      fill_u4(L.o, H, c.nq * c.head_dim, G, seed, l, IQ36_T_O);
+      fill_f32(L.qn, c.head_dim, seed, l, IQ36_T_QNORM);
+      fill_f32(L.kn, c.head_dim, seed, l, IQ36_T_KNORM);
+      const int64_t blocks = (max_ctx + 15) / 16;
+      L.kc.assign(blocks * 16 * c.nkv * c.head_dim, 0);
+      L.vc.assign(blocks * 16 * c.nkv * c.head_dim, 0);
+    } else {
+      const int64_t C = (int64_t)(2 * c.nk + c.nv) * c.dk;
+      fill_u4(L.qkv, C, H, G, seed, l, IQ36_T_QKV);
+      fill_u4(L.z, (int64_t)c.nv * c.dk, H, G, seed, l, IQ36_T_Z);
+      fill_u4(L.a, c.nv, H, G, seed, l, IQ36_T_A);
+      fill_u4(L.b, c.nv, H, G, seed, l, IQ36_T_B);
+      fill_u4(L.out, H, c.nv * c.dk, G, seed, l, IQ36_T_OUT);
+      fill_f32(L.conv_w, C * c.conv, seed, l, IQ36_T_CONV);
+      fill_f32(L.a_log, c.nv, seed, l, IQ36_T_ALOG);
+      fill_f32(L.dt_bias, c.nv, seed, l, IQ36_T_DTB);
+      fill_f32(L.dnorm, c.dk, seed, l, IQ36_T_DNORM);
+      L.conv_state.assign(C * c.conv, 0.0f);
+      L.rec_state.assign((int64_t)c.nv * c.dk * c.dk, 0.0f);
+    }
+    fill_f16(L.router, (int64_t)c.experts * H, seed, l, IQ36_T_ROUTER);
+    fill_f16(L.sgate, H, seed, l, IQ36_T_SGATE);
+    fill_u4(L.gu, (int64_t)c.experts * 2 * c.inter, H, G, seed, l, IQ36_T_GU);
+    fill_u4(L.down, (int64_t)c.experts * H, c.inter, G, seed, l, IQ36_T_DOWN);
+    fill_u4(L.sgu, (int64_t)2 * c.shared_inter, H, G, seed, l, IQ36_T_SGU);
+    fill_u4(L.sdown, H, c.shared_inter, G, seed, l, IQ36_T_SDOWN);
+  }
+  fill_f32(M->final_norm, H, seed, -1, IQ36_T_FINAL_NORM);
+  fill_u4(M->lm_head, c.vocab, H, G, seed, -1, IQ36_T_LM_HEAD);
+  M->bt.resize((max_ctx + 15) / 16);
+  for (size_t i = 0; i < M->bt.size(); ++i) M->bt[i] = (int32_t)i;
+  return M;
+}
+
+void orc_model_destroy(void* m) { delete static_cast<Model*>(m); }
+
+// One decode step at position pos (the KV cache and recurrent states hold
+// positions < pos). Writes fp32 logits [vocab] when logits != NULL and returns
+// the greedy token.
+int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
+  Model& M = *static_cast<Model*>(mp);
+  const OrcModelConfig& c = M.c;
+  const int H = c.hidden, G = c.group;
+  std::vector<float> h(H), xn(H), y, y2, y3, y4;
+  {
+    int kind;
+    float lo, hi;
+    iq36_synth_spec(IQ36_T_EMBED, 0, &kind, &lo, &hi);
+    std::vector<uint16_t> row(H);
+    // Row `token` of the fp16 [vocab, H] embedding table: elements
+    // token*H .. token*H+H-1 of that tensor.
+    for (int i = 0; i < H; ++i)
+      row[i] = f2h(iq36_synth_normal(M.seed, iq36_tensor_id(-1, IQ36_T_EMBED, 0),
+                                     (uint64_t)token * H + i, lo));
+    for (int i = 0; i < H; ++i) h[i] = h2f(row[i]);
+  }
+  for (int l = 0; l < c.layers; ++l) {
+    Layer& L = M.layers[l];
+    orc_rms_norm(h.data(), 1, H, L.in_norm.data(), H, c.eps, xn.data());
+    const auto x16 = to_f16(xn);
+    if (L.attn) {
+      const int D = c.head_dim;
+      gemv16(L.q, x16.data(), G, y, threads);
+      gemv16(L.k, x16.data(), G, y2, threads);
+      gemv16(L.v, x16.data(), G, y3, threads);
+      const auto qf = to_f16(y), kf = to_f16(y2), vf = to_f16(y3);
+      std::vector<float> qo(c.nq * D), go(c.nq * D), kn(c.nkv * D), vn(c.nkv * D);
+      orc_attn_prep(qf.data(), kf.data(), vf.data(), L.qn.data(), L.kn.data(), c.eps, pos, c.nq,
+                    c.nkv, D, c.rope_dim, c.rope_base, qo.data(), go.data(), kn.data(),
+                    vn.data());
+      const int64_t slot = ((int64_t)M.bt[pos / 16] * 16 + pos % 16) * c.nkv * D;
+      for (int i = 0; i < c.nkv * D; ++i) {
+        L.kc[slot + i] = f2h(kn[i]);
+        L.vc[slot + i] = f2h(vn[i]);
+      }
+      const auto q16 = to_f16(qo), g16 = to_f16(go);
+      std::vector<float> att(c.nq * D);
+      orc_paged_gqa(q16.data(), L.kc.data(), L.vc.data(), M.bt.data(), pos + 1, c.nq, c.nkv, D,
+                    16, 1.0f / std::sqrt((float)D), g16.data(), att.data(), threads);
+      const auto a16 = to_f16(att);
+      gemv16(L.o, a16.data(), G, y4, threads);
+    } else {
+      const int C = (2 * c.nk + c.nv) * c.dk;
+      gemv16(L.qkv, x16.data(), G, y, threads);
+      gemv16(L.z, x16.data(), G, y2, threads);
+      std::vector<float> ya, yb;
+      gemv16(L.a, x16.data(), G, ya, threads);
+      gemv16(L.b, x16.data(), G, yb, threads);
+      const auto qkv16 = to_f16(y), z16 = to_f16(y2), a16 = to_f16(ya), b16 = to_f16(yb);
+      std::vector<float> act(C), g(c.nv), beta(c.nv), o(c.nv * c.dk);
+      orc_delta_prep(qkv16.data(), C, L.conv_state.data(), L.conv_w.data(), a16.data(),
+                     b16.data(), L.a_log.data(), L.dt_bias.data(), c.nv, act.data(), g.data(),
+                     beta.data());
+      orc_delta_step(act.data(), g.data(), beta.data(), L.rec_state.data(), z16.data(),
+                     L.dnorm.data(), c.eps, c.nk, c.nv, c.dk, o.data());
+      const auto o16 = to_f16(o);
+      gemv16(L.out, o16.data(), G, y4, threads);
+    }
+    for (int i = 0; i < H; ++i) h[i] += h2f(f2h(y4[i]));
+    orc_rms_norm(h.data(), 1, H, L.post_norm.data(), H, c.eps, xn.data());
+    const auto x2 = to_f16(xn);
+    std::vector<float> lg(c.experts), w(c.topk), mo(H);
+    std::vector<int32_t> ids(c.topk);
+    float sl = 0.0f;
+    orc_f16_linear(x2.data(), H, L.router.data(), c.experts, lg.data());
+    orc_f16_linear(x2.data(), H, L.sgate.data(), 1, &sl);
+    orc_router_select(lg.data(), 1, c.experts, c.topk, ids.data(), w.data());
+    orc_moe_decode(x2.data(), ids.data(), w.data(), c.topk, L.gu.w.data(), L.gu.s.data(),
+                   L.gu.z.data(), L.down.w.data(), L.down.s.data(), L.down.z.data(),
+                   L.sgu.w.data(), L.sgu.s.data(), L.sgu.z.data(), L.sdown.w.data(),
+                   L.sdown.s.data(), L.sdown.z.data(), &sl, H, c.inter, G, mo.data(), 0,
+                   threads);
+    for (int i = 0; i < H; ++i) h[i] += h2f(f2h(mo[i]));
+  }
+  orc_rms_norm(h.data(), 1, H, M.final_norm.data(), H, c.eps, xn.data());
+  const auto xf = to_f16(xn);
+  std::vector<float> lo;
+  gemv16(M.lm_head, xf.data(), G, lo, threads);
+  if (logits) std::memcpy(logits, lo.data(), sizeof(float) * c.vocab);
+  return orc_argmax(lo.data(), c.vocab);
+}
+
+}  // extern "C"
