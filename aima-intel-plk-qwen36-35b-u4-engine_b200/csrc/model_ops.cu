@@ -487,3 +487,22 @@ extern "C" void iq36_synth_tensor_spec(int32_t slot, int32_t sub, int32_t* kind,
   iq36_synth_spec(slot, sub, &k, lo, hi);
   *kind = k;
 }
+
+namespace iq36 {
+__global__ void decode_positions_kernel(int32_t* pos, int32_t* ctx, int advance) {
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    const int p = *pos + (advance ? 1 : 0);
+    *pos = p;
+    *ctx = p + 1;
+  }
+}
+}  // namespace iq36
+
+extern "C" int iq36_decode_positions(int32_t* pos_dev, int32_t* ctx_dev, int32_t advance,
+                                     iq36_stream_t stream) {
+  if (!pos_dev || !ctx_dev) return IQ36_ERR_ARG;
+  const cudaError_t e = launch(decode_positions_kernel, dim3(1), dim3(32), 0, as_stream(stream),
+                               pos_dev, ctx_dev, (int)advance);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}

@@ -1,0 +1,347 @@
+#!/usr/bin/env python
+"""Benchmark: batch-1 decode of the synthetic Qwen3.6-35B-A3B-shaped model on B200.
+
+Workload: random-init 40-layer model (10 x (3 DeltaNet +
+1 gated GQA), each followed by the 256-expert top-8 MoE, u4 g128 weights,
+vocab 248320). A seeded uniform-random prompt of --ctx tokens (default 4096)
+is fed through the decode step, then --warmup untimed and --steps timed greedy
+decode steps run as CUDA-graph replays. One step reads ~1.77 GB (> L2), so no
+L2 flush is needed between steps.
+
+JSON line (rank 0): value = decode tok/s over all ranks (device time, CUDA
+events, max over ranks); e2e = the same through the public API with the input
+token copied from pinned host memory and the greedy token read back every
+step; roofline = the dominant kernel (multi-output u4 GEMV) measured live;
+cpu_baseline = the CPU restatement (oracle/) on a bounded sample.
+
+--impl reference: the reference path's CPU implementation (the oracle port;
+OpenVINO is not installable here) on the host cores, same metric.
+Multi-GPU: replicas only (each rank decodes its own sequence; no collective on
+the data path), value summed over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "aima-intel-plk-qwen36-35b-u4-engine_b200"
+for p in (str(ROOT), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
+METRIC = BASELINE["metric"]
+PUBLISHED_DECODE_4K = 50.57  # Arc B390, 4k prompt, batch-1 decode tok/s
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)], stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        rows = [ln.split(",") for ln in open(self.path).read().strip().splitlines() if ln.strip()]
+        os.unlink(self.path)
+        sm = sorted(float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().isdigit())
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) >= 9:
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+def cpu_baseline(ctx: int, threads: int) -> dict:
+    """Time the CPU restatement on a bounded sample of the decode step: a
+    4-layer slice (3 DeltaNet + 1 attention, all 256 experts, full vocab) and a
+    0-layer model (embedding + LM head), plus the attention op at ctx; the
+    40-layer step is extrapolated as t0 + 10 * (t4 - t0) + 10 * t_attn(ctx)."""
+    import numpy as np
+    from engine.runtime import ModelConfig
+    from oracle import oracle
+
+    full = ModelConfig()
+    c4 = ModelConfig(layers=4).as_dict()
+    c0 = ModelConfig(layers=0).as_dict()
+    m4 = oracle.OracleModel(c4, 1234, 32)
+    m0 = oracle.OracleModel(c0, 1234, 32)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, full.vocab, 8).tolist()
+
+    def tstep(m, n):
+        m.step(toks[0], 0, want_logits=False, threads=threads)  # warm
+        t = time.perf_counter()
+        for i in range(n):
+            m.step(toks[i + 1], i + 1, want_logits=False, threads=threads)
+        return (time.perf_counter() - t) / n
+
+    t4 = tstep(m4, 3)
+    t0 = tstep(m0, 3)
+    m4.close()
+    m0.close()
+    q = rng.standard_normal((16, 256)).astype(np.float16)
+    nblk = (ctx + 15) // 16
+    kc = rng.standard_normal((nblk, 16, 2, 256)).astype(np.float16)
+    vc = rng.standard_normal((nblk, 16, 2, 256)).astype(np.float16)
+    bt = np.arange(nblk, dtype=np.int32)
+    t = time.perf_counter()
+    oracle.paged_gqa(q, kc, vc, bt, ctx, 1 / 16, threads=threads)
+    ta = time.perf_counter() - t
+    n_attn = sum(full.is_attn(l) for l in range(full.layers))
+    per_tok = t0 + (full.layers / 4) * (t4 - t0) + n_attn * ta
+    return {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": threads,
+            "kind": "port",
+            "sample": (f"3 decode steps of a 4-layer slice (3 DeltaNet + 1 GQA, 256 experts) and "
+                       f"of a 0-layer model (LM head), plus one {ctx}-token attention, "
+                       f"extrapolated to 40 layers: {per_tok * 1e3:.1f} ms/token")}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, world, rank) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = max(1, args.steps)
+    vals = []
+    for _ in range(max(1, min(args.warmup, 1))):
+        cpu_baseline(args.ctx, threads)  # warm-up sample (untimed)
+    t = time.perf_counter()
+    for _ in range(min(steps, 2)):
+        vals.append(cpu_baseline(args.ctx, threads))
+    elapsed = time.perf_counter() - t
+    v = vals[-1]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v["value"], "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": len(vals), "warmup": 1,
+        "ms_per_step": round(1e3 / v["value"], 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(v["value"] / PUBLISHED_DECODE_4K, 4), "dtype": "u4xf16",
+        "data": "synthetic",
+        "config": {"workload": f"config4 batch-1 decode, ctx {args.ctx}",
+                   "note": "OpenVINO CPU u4 path unavailable here (not installable); the "
+                           "reference arm is the CPU restatement in oracle/",
+                   "wall_s": round(elapsed, 2)},
+        "cpu_baseline": {**v},
+        "e2e": {"value": v["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local) -> None:
+    import torch
+    from engine import ops
+    from engine.runtime import ModelConfig, Qwen36Runtime
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig()
+    max_ctx = args.ctx + args.warmup + 2 * args.steps + 32
+    rt = Qwen36Runtime(cfg, seed=1234, max_ctx=max_ctx, device=dev)
+    rt.capture()
+    gen = torch.Generator().manual_seed(4096 + rank)
+    prompt = torch.randint(0, cfg.vocab, (args.ctx,), generator=gen, dtype=torch.int32)
+
+    # prefill through the same captured step (token-serial)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rt.prefill(prompt)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    prefill_s = e0.elapsed_time(e1) / 1e3
+
+    for _ in range(args.warmup):
+        rt.step()
+    torch.cuda.synchronize(dev)
+
+    # timed region: device-resident decode steps (graph replays)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        rt.step()
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    t_dev = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    value = world * args.steps / t_dev
+    ms_per_step = t_dev / args.steps * 1e3
+
+    # e2e: host-resident token in, greedy token out, every step
+    pin_in = torch.empty(1, dtype=torch.int32).pin_memory()
+    pin_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    pin_in.copy_(rt.token.cpu())
+    cur = torch.cuda.current_stream(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s.record()
+    for _ in range(args.steps):
+        rt.token.copy_(pin_in, non_blocking=True)
+        rt.step()
+        pin_out.copy_(rt.token, non_blocking=True)
+        cur.synchronize()
+        pin_in.copy_(pin_out)
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    e2e = {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s",
+           "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
+
+    # dominant kernel: every multi-output u4 GEMV of one step, replayed alone
+    gemv_bytes, gemv_launches = 0, 0
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=rt.stream):
+        gemv_bytes, gemv_launches = rt.enqueue_gemvs_only()
+    for _ in range(3):
+        g2.replay()
+    torch.cuda.synchronize(dev)
+    reps = 20
+    s.record()
+    for _ in range(reps):
+        g2.replay()
+    e.record()
+    torch.cuda.synchronize(dev)
+    per_launch_s = s.elapsed_time(e) / 1e3 / (reps * gemv_launches)
+    hbm, src = peaks()
+    achieved = gemv_bytes / gemv_launches / per_launch_s / 1e9
+    ctx_mid = args.ctx + args.warmup + args.steps // 2
+    step_bytes = cfg.decode_bytes_per_token(ctx_mid)
+    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(value / PUBLISHED_DECODE_4K, 3), "dtype": "u4xf16",
+        "data": "synthetic",
+        "config": {"workload": f"config4 batch-1 greedy decode after a {args.ctx}-token prompt "
+                               "(Qwen3.6-35B-A3B-shaped, random-init u4 g128)",
+                   "ctx": args.ctx, "decode_steps": args.steps, "parallelism": "replicas",
+                   "l2": "inputs larger than L2 (~1.77 GB of weights per step)",
+                   "prefill_tok_s": round(world * args.ctx / max_over_ranks(prefill_s, world), 1),
+                   "prefill_mode": "token-serial through the decode graph",
+                   "step_bytes": step_bytes,
+                   "step_hbm_gbs": round(step_gbs, 1),
+                   "step_hbm_frac": round(step_gbs / hbm, 4)},
+        "e2e": e2e,
+        "gpu_launches": rt.launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "u4_gemv_multi_kernel",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "peak_source": src,
+                     "bytes_per_launch": gemv_bytes // gemv_launches,
+                     "launches": gemv_launches},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.ctx, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

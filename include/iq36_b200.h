@@ -223,6 +223,13 @@ int iq36_delta_step(const void* qkv_act_f16, const float* g, const float* beta, 
                     const void* z_f16, const float* norm_w, float eps, int32_t n_k_heads,
                     int32_t n_v_heads, int32_t head_dim, void* out_f16, iq36_stream_t stream);
 
+/* Decode-loop position state on the device: if advance, *pos_dev += 1; then
+ * *ctx_dev = *pos_dev + 1 (the attention context of the step at *pos_dev).
+ * Lets one captured CUDA graph serve every step of the loop
+ * (the reference's per-token loop: engine/service/iq36_server/runtime.py:533-561). */
+int iq36_decode_positions(int32_t* pos_dev, int32_t* ctx_dev, int32_t advance,
+                          iq36_stream_t stream);
+
 /* h[:] = float(embedding[*token_dev, :]) (fp16 table [vocab, H]). */
 int iq36_embed(const void* table_f16, int32_t vocab, int32_t hidden, const int32_t* token_dev,
                float* h, iq36_stream_t stream);
