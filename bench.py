@@ -231,6 +231,17 @@ def run_ours(args, world, rank, local) -> None:
         rt.step()
     torch.cuda.synchronize(dev)
 
+    if args.profile_step:
+        # One decode step between cudaProfilerStart/Stop, for
+        # `ncu --profile-from-start off` (launch lists and kernel captures).
+        torch.cuda.profiler.start()
+        rt.step()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "launches": rt.launches_per_step}))
+        return
+
     # timed region: device-resident decode steps (graph replays)
     sampler = ClockSampler(local)
     barrier(world)
@@ -329,6 +340,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="run one decode step inside cudaProfilerStart/Stop and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
