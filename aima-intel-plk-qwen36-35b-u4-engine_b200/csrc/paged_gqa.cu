@@ -23,6 +23,8 @@
 // Kernel 2 (combine): per query head merge the S partials (max, sum, output),
 // normalise, apply sigmoid(gate), store fp32 or fp16.
 
+#include <atomic>
+
 #include "launch.cuh"
 #include "common.cuh"
 
@@ -253,12 +255,15 @@ int gqa_launch(const void* q, const void* kc, const void* vc, const int32_t* bt,
   const size_t need = gqa_ws_bytes(ctx, n_q, n_kv);
   if (!ws || ws_bytes < need) return IQ36_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return IQ36_ERR_ALIGN;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // The dynamic shared-memory opt-in is a per-device function attribute.
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              4 * kWarpSmem) != cudaSuccess)
       return IQ36_ERR_CUDA;
-    attr_set = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int S = gqa_splits(ctx);
   const size_t meta = (size_t)n_kv * S * kGrp;
