@@ -309,3 +309,69 @@ extern "C" int iq36_paged_gqa_decode(const void* q_f16, const void* k_cache, con
                           n_kv_heads, head_dim, block_size, scale, gate_f16, out, out_dtype,
                           workspace, workspace_bytes, iq36::as_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free paged GQA decode.
+//
+// For hosts that can hand a kernel only its input and output buffers — for
+// example a graph-plugin ABI where the plugin owns every buffer, or a service
+// running under a fixed device-memory budget with no allocator reachable from
+// the op — this variant keeps the split-K partials (per split and head: max,
+// sum and the 256-wide unnormalised output) in one file-scope device array
+// instead of a caller workspace. The array is sized for at most 2 KV heads
+// (16 query heads) at the largest split count, 4,887,552 bytes; every GPU that
+// loads this library holds it until the process exits. All calls on a device
+// share it and it keeps the last call's contents; nothing in it needs to start
+// at zero because the split kernel writes every max/sum it later reads and the
+// combine reads an output partial only for splits that wrote one. Two calls
+// whose kernels overlap on the GPU race on the array.
+namespace iq36 {
+
+constexpr int kNoAllocMaxKv = 2;
+constexpr size_t kNoAllocMeta = (size_t)kNoAllocMaxKv * kMaxSplits * kGrp;
+constexpr size_t kNoAllocMetaBytes = (kNoAllocMeta * 4 + 255) / 256 * 256;
+constexpr size_t kNoAllocScratchBytes = 2 * kNoAllocMetaBytes + kNoAllocMeta * kD * 4;
+
+static __device__ __align__(256) unsigned char g_gqa_noalloc_scratch[kNoAllocScratchBytes];
+
+// Host code cannot use g_gqa_noalloc_scratch as a device address: resolve it
+// once per device, with that device current.
+static int noalloc_scratch(void** ptr) {
+  static std::atomic<void*> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  void* p = cached[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    if (cudaGetSymbolAddress(&p, g_gqa_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return IQ36_ERR_CUDA;
+    cached[dev].store(p, std::memory_order_release);
+  }
+  *ptr = p;
+  return IQ36_OK;
+}
+
+}  // namespace iq36
+
+extern "C" int iq36_paged_gqa_decode_noalloc(const void* q_f16, const void* k_cache,
+                                             const void* v_cache, const int32_t* block_table,
+                                             int32_t ctx_len, const int32_t* ctx_len_dev,
+                                             int32_t n_q_heads, int32_t n_kv_heads,
+                                             int32_t head_dim, int32_t block_size, float scale,
+                                             const void* gate_f16, void* out, int32_t out_dtype,
+                                             iq36_stream_t stream) {
+  using namespace iq36;
+  if (!q_f16 || !k_cache || !v_cache || !block_table || !out) return IQ36_ERR_ARG;
+  if (head_dim != kD || block_size != kBS || n_kv_heads < 1 || n_q_heads != n_kv_heads * kGrp ||
+      ctx_len < 1 || !(scale > 0.f))
+    return IQ36_ERR_SHAPE;
+  // Beyond the array's stated maximum: reject before touching the device.
+  if (n_kv_heads > kNoAllocMaxKv ||
+      gqa_ws_bytes(ctx_len, n_q_heads, n_kv_heads) > kNoAllocScratchBytes)
+    return IQ36_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != IQ36_OK) return st;
+  return gqa_launch(q_f16, k_cache, v_cache, block_table, ctx_len, ctx_len_dev, n_q_heads,
+                    n_kv_heads, head_dim, block_size, scale, gate_f16, out, out_dtype, scratch,
+                    kNoAllocScratchBytes, as_stream(stream));
+}

@@ -67,6 +67,8 @@ _SIGS: dict[str, tuple] = {
     "iq36_paged_gqa_decode": (c_int, [_P, _P, _P, _P, c_int32, _P, c_int32, c_int32, c_int32,
                                       c_int32, c_float, _P, _P, c_int32, _P, c_size_t, _P]),
     "iq36_paged_gqa_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
+    "iq36_paged_gqa_decode_noalloc": (c_int, [_P, _P, _P, _P, c_int32, _P, c_int32, c_int32,
+                                              c_int32, c_int32, c_float, _P, _P, c_int32, _P]),
     "iq36_rms_norm": (c_int, [_P, c_int32, c_int32, _P, c_int32, c_float, _P, c_int32, _P]),
     "iq36_attn_prep": (c_int, [_P, _P, _P, _P, _P, c_float, _P, c_int32, c_int32, c_int32,
                                c_int32, c_float, _P, c_int32, _P, _P, _P, _P, _P]),

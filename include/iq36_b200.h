@@ -181,6 +181,25 @@ int iq36_paged_gqa_decode(const void* q_f16, const void* k_cache, const void* v_
 size_t iq36_paged_gqa_workspace_bytes(int32_t max_ctx, int32_t n_q_heads, int32_t n_kv_heads,
                                       int32_t head_dim);
 
+/* Allocation-free form of iq36_paged_gqa_decode. It has no counterpart in the
+ * reference. Some callers cannot allocate device memory for a workspace: a
+ * graph-plugin host that passes an op only its input and output buffers, or a
+ * service held to a fixed device-memory budget with no allocator available to
+ * the op. Here the split partials live in one static device array inside the
+ * library (4,887,552 bytes, held by every GPU that loads the library until the
+ * process exits), sized for n_kv_heads <= 2 (n_q_heads <= 16) at any ctx_len;
+ * larger head counts return IQ36_ERR_WORKSPACE. The call allocates nothing.
+ * The first call on each device looks up the array's device address (with that
+ * device current), so make that first call before any stream capture. All
+ * calls share the array and it keeps the last call's contents (nothing in it
+ * has to start zeroed); calls whose kernels overlap on the GPU race on it. */
+int iq36_paged_gqa_decode_noalloc(const void* q_f16, const void* k_cache, const void* v_cache,
+                                  const int32_t* block_table, int32_t ctx_len,
+                                  const int32_t* ctx_len_dev, int32_t n_q_heads,
+                                  int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                                  float scale, const void* gate_f16, void* out, int32_t out_dtype,
+                                  iq36_stream_t stream);
+
 /* ---- config-4 support ops ---------------------------------------------------*/
 
 /* out[r] = f(in[r] * rsqrt(mean(in[r]^2) + eps) * weight); gguf_loader.cpp:3368-3391
