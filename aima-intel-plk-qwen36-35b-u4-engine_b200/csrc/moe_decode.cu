@@ -61,22 +61,31 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
                                                             float* slogit) {
   extern __shared__ __align__(16) __half xsh[];
   __shared__ float nred[33];
-  pdl_wait();
-  const int tok = blockIdx.y;
-  stage_x_plain(xsh, x16 ? x16 + (size_t)tok * H : nullptr, x32 ? x32 + (size_t)tok * H : nullptr,
-                nw, eps, H, nred);
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   const __half* wr = nullptr;
   if (row < E) wr = W + (size_t)row * H;
   else if (row == E && wsg != nullptr) wr = wsg;
+  // Router weights do not depend on the previous kernel: fetch the first
+  // 8 x 16 bytes of this lane's row before waiting on it.
+  constexpr int kPre = 8;
+  uint4 pre[kPre];
+  if (wr != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = lane + 32 * j;
+      if (c < H / 8) pre[j] = ld_stream_v4(wr + c * 8);
+    }
+  }
+  pdl_wait();
+  const int tok = blockIdx.y;
+  stage_x_plain(xsh, x16 ? x16 + (size_t)tok * H : nullptr, x32 ? x32 + (size_t)tok * H : nullptr,
+                nw, eps, H, nred);
+  pdl_launch_dependents();
   if (wr == nullptr) return;
   float acc = 0.f;
   const uint4* xv4 = reinterpret_cast<const uint4*>(xsh);
-  for (int c = lane; c < H / 8; c += 32) {
-    const uint4 wv = ld_stream_v4(wr + c * 8);
-    const uint4 xv = xv4[c];
+  auto dot8 = [&](const uint4& wv, const uint4& xv) {
     const __half2* wh = reinterpret_cast<const __half2*>(&wv);
     const __half2* xh = reinterpret_cast<const __half2*>(&xv);
 #pragma unroll
@@ -86,7 +95,13 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
       acc = fmaf(wf.x, xf.x, acc);
       acc = fmaf(wf.y, xf.y, acc);
     }
+  };
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = lane + 32 * j;
+    if (c < H / 8) dot8(pre[j], xv4[c]);
   }
+  for (int c = lane + 32 * kPre; c < H / 8; c += 32) dot8(ld_stream_v4(wr + c * 8), xv4[c]);
   acc = warp_sum(acc);
   if (lane == 0) {
     if (row < E) logits[(size_t)tok * E + row] = acc;
@@ -183,49 +198,66 @@ struct ExpertArgs {
   int H, I, k, n_slots, num_experts;
 };
 
+// Row pair (gate row j, up row I+j) of one gate_up warp task.
+template <int G>
+__device__ __forceinline__ U4Rows gate_up_rows(const ExpertArgs& a, const int32_t* ids, int slot,
+                                               int j, int g) {
+  const int H = a.H, I = a.I, ng = H / G;
+  const uint8_t* w;
+  const __half* s;
+  const uint8_t* z;
+  int64_t zbase;
+  if (slot < a.k) {
+    const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
+    w = a.gu_w + e * (int64_t)(2 * I) * (H / 2);
+    s = a.gu_s + e * (int64_t)(2 * I) * ng;
+    z = a.gu_z;
+    zbase = e * (int64_t)(2 * I) * ng;
+  } else {
+    w = a.sgu_w;
+    s = a.sgu_s;
+    z = a.sgu_z;
+    zbase = 0;
+  }
+  const int rowA = j + g, rowB = I + j + g;
+  return U4Rows{w + (size_t)rowA * (H / 2), w + (size_t)rowB * (H / 2), s + (size_t)rowA * ng,
+                s + (size_t)rowB * ng, z, zbase + (int64_t)rowA * ng, zbase + (int64_t)rowB * ng};
+}
+
 template <int G>
 __global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const int32_t* ids,
-                                                          const __half* x16, __half* act,
-                                                          int ks_log2) {
+                                                          const __half* x16, const float* x32,
+                                                          const float* nw, float eps,
+                                                          __half* act, int ks_log2) {
   extern __shared__ uint4 xs[];
   __shared__ float red[8][16];
   __shared__ float nred[33];
-  pdl_wait();
-  stage_x_perm(xs, x16, nullptr, nullptr, 0.f, a.H, nred);
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int KS = 1 << ks_log2;
   const int rb = blockIdx.x * (8 >> ks_log2) + (warp >> ks_log2);
   const int ks = warp & (KS - 1);
   const int rb_per_exp = a.I / 8;
-  const int H = a.H, I = a.I, ng = H / G;
+  const int I = a.I, ng = a.H / G, per = ng >> ks_log2;
   const bool valid = rb < a.n_slots * rb_per_exp;
   const int slot = valid ? rb / rb_per_exp : 0;
   const int j0 = (rb - slot * rb_per_exp) * 8;
   float accA = 0.f, accB = 0.f;
-  if (valid) {
-    const uint8_t* w;
-    const __half* s;
-    const uint8_t* z;
-    int64_t zbase;
-    if (slot < a.k) {
-      const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
-      w = a.gu_w + e * (int64_t)(2 * I) * (H / 2);
-      s = a.gu_s + e * (int64_t)(2 * I) * ng;
-      z = a.gu_z;
-      zbase = e * (int64_t)(2 * I) * ng;
-    } else {
-      w = a.sgu_w;
-      s = a.sgu_s;
-      z = a.sgu_z;
-      zbase = 0;
-    }
-    const int rowA = j0 + g, rowB = I + j0 + g;
-    const int per = ng >> ks_log2;
-    u4_dot2<G, 4>(w + (size_t)rowA * (H / 2), w + (size_t)rowB * (H / 2), s + (size_t)rowA * ng,
-                  s + (size_t)rowB * ng, z, zbase + (int64_t)rowA * ng,
-                  zbase + (int64_t)rowB * ng, xs, ks * per, (ks + 1) * per, t, accA, accB);
+  U4Rows rows{};
+  U4Chunk<G, 2> first;
+  // The shared expert's weights are known up front: stream them before the
+  // wait. Routed experts depend on the router output of the previous kernel.
+  if (valid && slot >= a.k) {
+    rows = gate_up_rows<G>(a, ids, slot, j0, g);
+    u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
   }
+  pdl_wait();
+  if (valid && slot < a.k) {
+    rows = gate_up_rows<G>(a, ids, slot, j0, g);
+    u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
+  }
+  stage_x_perm(xs, x16, x32, nw, eps, a.H, nred);
+  pdl_launch_dependents();
+  if (valid) u4_dot2_pipelined<G, 2>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
   if (KS > 1) {
     if (t == 0) {
       red[warp][g] = accA;
@@ -255,13 +287,13 @@ __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* w
   extern __shared__ uint4 xs[];
   __shared__ float red[16][16];
   __shared__ float nred[33];
-  pdl_wait();
   const int H = a.H, I = a.I, ngi = I / G;
-  stage_x_perm(xs, act, nullptr, nullptr, 0.f, a.n_slots * I, nred);
-  pdl_launch_dependents();
   const int slot = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int h0 = blockIdx.x * 16;
   const int rowA = min(h0 + g, H - 1), rowB = min(h0 + g + 8, H - 1);
+  // The expert ids were written by the router two launches back (every kernel
+  // waits on its predecessor before releasing its dependents), so they, and
+  // the expert weights they select, can be read before this kernel's wait.
   const uint8_t* w;
   const __half* s;
   const uint8_t* z;
@@ -278,10 +310,16 @@ __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* w
     z = a.sd_z;
     zbase = 0;
   }
+  const U4Rows rows{w + (size_t)rowA * (I / 2), w + (size_t)rowB * (I / 2),
+                    s + (size_t)rowA * ngi, s + (size_t)rowB * ngi, z,
+                    zbase + (int64_t)rowA * ngi, zbase + (int64_t)rowB * ngi};
+  U4Chunk<G, 2> first;
+  u4_load_chunk<G, 2>(first, rows, 0, ngi, t);
+  pdl_wait();
+  stage_x_perm(xs, act, nullptr, nullptr, 0.f, a.n_slots * I, nred);
+  pdl_launch_dependents();
   float accA = 0.f, accB = 0.f;
-  u4_dot2<G, 4>(w + (size_t)rowA * (I / 2), w + (size_t)rowB * (I / 2), s + (size_t)rowA * ngi,
-                s + (size_t)rowB * ngi, z, zbase + (int64_t)rowA * ngi,
-                zbase + (int64_t)rowB * ngi, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+  u4_dot2_pipelined<G, 2>(first, rows, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
   if (t == 0) {
     red[slot][g] = accA;
     red[slot][g + 8] = accB;
@@ -324,14 +362,20 @@ size_t moe_decode_ws(int k, int hidden, int intermediate) {
   return (((size_t)(k + 1) * intermediate * 2) + 255) / 256 * 256;
 }
 
-int moe_decode_launch(const void* x_f16, const int32_t* ids, const float* weights, int k,
+int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, float eps,
+                      const int32_t* ids, const float* weights, int k,
                       const iq36_expert_bank* routed, const iq36_expert_bank* shared,
                       const float* shared_logit, void* out, int out_dtype, int accumulate,
                       void* ws, size_t ws_bytes, cudaStream_t stream) {
   int st = check_bank(routed);
   if (st != IQ36_OK) return st;
-  if (!x_f16 || !ids || !weights || !out) return IQ36_ERR_ARG;
-  if (!aligned(x_f16, 16)) return IQ36_ERR_ALIGN;
+  if (!ids || !weights || !out) return IQ36_ERR_ARG;
+  if (x_f32) {
+    if (x_f16 || !nw) return IQ36_ERR_ARG;
+  } else {
+    if (!x_f16) return IQ36_ERR_ARG;
+    if (!aligned(x_f16, 16)) return IQ36_ERR_ALIGN;
+  }
   if (k < 1 || k > 15 || k > routed->num_experts) return IQ36_ERR_SHAPE;
   if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
   if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
@@ -373,9 +417,11 @@ int moe_decode_launch(const void* x_f16, const int32_t* ids, const float* weight
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
   cudaError_t e;
   if (G == 128)
-    e = launch(moe_gate_up_kernel<128>, grid1, dim3(256), smem1, stream, a, ids, xh, act, ks_log2);
+    e = launch(moe_gate_up_kernel<128>, grid1, dim3(256), smem1, stream, a, ids, xh, x_f32, nw,
+               eps, act, ks_log2);
   else
-    e = launch(moe_gate_up_kernel<64>, grid1, dim3(256), smem1, stream, a, ids, xh, act, ks_log2);
+    e = launch(moe_gate_up_kernel<64>, grid1, dim3(256), smem1, stream, a, ids, xh, x_f32, nw, eps,
+               act, ks_log2);
   if (e != cudaSuccess) return IQ36_ERR_CUDA;
   const dim3 grid2(ceil_div(a.H, 16));
   const size_t smem2 = (size_t)a.n_slots * a.I / 8 * sizeof(uint4);
@@ -439,14 +485,15 @@ extern "C" size_t iq36_moe_decode_workspace_bytes(int32_t k, int32_t hidden, int
   return iq36::moe_decode_ws(k, hidden, intermediate);
 }
 
-extern "C" int iq36_moe_decode(const void* x_f16, const int32_t* ids, const float* weights,
+extern "C" int iq36_moe_decode(const void* x_f16, const float* x_f32, const float* norm_weight,
+                               float norm_eps, const int32_t* ids, const float* weights,
                                int32_t k, const iq36_expert_bank* routed,
                                const iq36_expert_bank* shared, const float* shared_logit,
                                void* out, int32_t out_dtype, int32_t accumulate, void* workspace,
                                size_t workspace_bytes, iq36_stream_t stream) {
-  return iq36::moe_decode_launch(x_f16, ids, weights, k, routed, shared, shared_logit, out,
-                                 out_dtype, accumulate, workspace, workspace_bytes,
-                                 iq36::as_stream(stream));
+  return iq36::moe_decode_launch(x_f16, x_f32, norm_weight, norm_eps, ids, weights, k, routed,
+                                 shared, shared_logit, out, out_dtype, accumulate, workspace,
+                                 workspace_bytes, iq36::as_stream(stream));
 }
 
 extern "C" size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden,
@@ -488,6 +535,7 @@ extern "C" int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16
   if (st != IQ36_OK) return st;
   st = router_select_launch(logits, 1, routed->num_experts, k, ids, weights, s);
   if (st != IQ36_OK) return st;
-  return moe_decode_launch(x_f16, ids, weights, k, routed, shared, shared ? slogit : nullptr, out,
-                           out_dtype, 0, ws2, workspace_bytes - 256, s);
+  return moe_decode_launch(x_f16, nullptr, nullptr, 0.f, ids, weights, k, routed, shared,
+                           shared ? slogit : nullptr, out, out_dtype, 0, ws2, workspace_bytes - 256,
+                           s);
 }

@@ -92,6 +92,111 @@ __device__ __forceinline__ uint32_t zp_nibble(const uint8_t* zp, int64_t e) {
   return (uint32_t)(__ldg(zp + (e >> 1)) >> ((e & 1) * 4)) & 15u;
 }
 
+// One prefetched chunk: U quant groups of the lane's two rows (codes, scales,
+// zero points) held in registers.
+template <int G, int U>
+struct U4Chunk {
+  uint32_t ra[U][G / 32], rb[U][G / 32];
+  uint32_t za[U], zb[U];
+  float sa[U], sb[U];
+};
+
+// Row pair of one warp task: row starts, scale row starts, zp element index of
+// (row, group 0).
+struct U4Rows {
+  const uint8_t* wA;
+  const uint8_t* wB;
+  const __half* sA;
+  const __half* sB;
+  const uint8_t* zp;
+  int64_t zeA, zeB;
+};
+
+template <int G, int U>
+__device__ __forceinline__ void u4_load_chunk(U4Chunk<G, U>& c, const U4Rows& r, int g0, int g_end,
+                                              int t) {
+  constexpr int W = G / 32;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int gi = min(g0 + u, g_end - 1);
+    const int off = gi * (G / 2) + t * (G / 8);
+    if constexpr (W == 4) {
+      const uint4 va = ld_stream_v4(r.wA + off);
+      const uint4 vb = ld_stream_v4(r.wB + off);
+      c.ra[u][0] = va.x; c.ra[u][1] = va.y; c.ra[u][2] = va.z; c.ra[u][3] = va.w;
+      c.rb[u][0] = vb.x; c.rb[u][1] = vb.y; c.rb[u][2] = vb.z; c.rb[u][3] = vb.w;
+    } else {
+      const uint2 va = ld_stream_v2(r.wA + off);
+      const uint2 vb = ld_stream_v2(r.wB + off);
+      c.ra[u][0] = va.x; c.ra[u][1] = va.y;
+      c.rb[u][0] = vb.x; c.rb[u][1] = vb.y;
+    }
+    c.sa[u] = __half2float(r.sA[gi]);
+    c.sb[u] = __half2float(r.sB[gi]);
+    c.za[u] = zp_nibble(r.zp, r.zeA + gi);
+    c.zb[u] = zp_nibble(r.zp, r.zeB + gi);
+  }
+}
+
+template <int G, int U>
+__device__ __forceinline__ void u4_compute_chunk(const U4Chunk<G, U>& c,
+                                                 const uint4* __restrict__ xs, int g0, int g_end,
+                                                 int t, float& accA, float& accB) {
+  constexpr int W = G / 32;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (g0 + u < g_end) {
+      const int gi = g0 + u;
+      const uint32_t zloA = kMagic | c.za[u] | (c.za[u] << 16);
+      const uint32_t zhiA = kMagic | (c.za[u] << 4) | (c.za[u] << 20);
+      const uint32_t zloB = kMagic | c.zb[u] | (c.zb[u] << 16);
+      const uint32_t zhiB = kMagic | (c.zb[u] << 4) | (c.zb[u] << 20);
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+#pragma unroll
+      for (int i = 0; i < W; ++i) {
+        const uint4 xv = xs[gi * (G / 8) + t * W + i];
+        uint32_t a = c.ra[u][i], b = c.rb[u][i];
+        mma_16816(c0, c1, c2, c3, hsub2_u32(lop3_and_or(a, 0x000F000Fu, kMagic), zloA),
+                  hsub2_u32(lop3_and_or(b, 0x000F000Fu, kMagic), zloB),
+                  hsub2_u32(lop3_and_or(a, 0x00F000F0u, kMagic), zhiA),
+                  hsub2_u32(lop3_and_or(b, 0x00F000F0u, kMagic), zhiB), xv.x, xv.y);
+        a >>= 8;
+        b >>= 8;
+        mma_16816(c0, c1, c2, c3, hsub2_u32(lop3_and_or(a, 0x000F000Fu, kMagic), zloA),
+                  hsub2_u32(lop3_and_or(b, 0x000F000Fu, kMagic), zloB),
+                  hsub2_u32(lop3_and_or(a, 0x00F000F0u, kMagic), zhiA),
+                  hsub2_u32(lop3_and_or(b, 0x00F000F0u, kMagic), zhiB), xv.z, xv.w);
+      }
+      accA = fmaf(c.sa[u], c0, accA);
+      accB = fmaf(c.sb[u], c2, accB);
+    }
+  }
+}
+
+// Software-pipelined walk over [g_begin, g_end): the caller has already loaded
+// the first chunk into `first` (typically before griddepcontrol.wait, since
+// weights never depend on the previous kernel); each step loads the next
+// chunk before computing the current one.
+template <int G, int U>
+__device__ __forceinline__ void u4_dot2_pipelined(U4Chunk<G, U>& first, const U4Rows& r,
+                                                  const uint4* __restrict__ xs, int g_begin,
+                                                  int g_end, int t, float& accA, float& accB) {
+  U4Chunk<G, U> next;
+  int g0 = g_begin;
+  while (g0 < g_end) {
+    const int g1 = g0 + U;
+    if (g1 < g_end) u4_load_chunk<G, U>(next, r, g1, g_end, t);
+    u4_compute_chunk<G, U>(first, xs, g0, g_end, t, accA, accB);
+    if (g1 >= g_end) break;
+    g0 = g1;
+    if (g0 + U < g_end) {
+      u4_load_chunk<G, U>(first, r, g0 + U, g_end, t);
+    }
+    u4_compute_chunk<G, U>(next, xs, g0, g_end, t, accA, accB);
+    g0 += U;
+  }
+}
+
 // Dot products of two weight rows (A, B) with the staged activation over
 // quant groups [g_begin, g_end). wA/wB: row starts (K/2 bytes each); sA/sB:
 // row scale starts; zeA/zeB: zp element index of (row, group 0). Results are

@@ -48,29 +48,34 @@ __global__ void __launch_bounds__(256) u4_gemv_multi_kernel(ProjSet ps, const __
   extern __shared__ uint4 xs[];
   __shared__ float red[8][16];
   __shared__ float nred[33];
-  pdl_wait();
-  stage_x_perm(xs, x16, x32, nw, eps, K, nred);
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int KS = 1 << ks_log2;
   const int rb = blockIdx.x * (8 >> ks_log2) + (warp >> ks_log2);
   const int ks = warp & (KS - 1);
   const int ng = K / G;
+  const int per = ng >> ks_log2;
   const bool valid = rb < ps.rb_start[ps.n_proj];
   float accA = 0.f, accB = 0.f;
   int p = 0, r0 = 0;
+  U4Rows rows{};
+  U4Chunk<G, 2> first;
   if (valid) {
+    // Weights never depend on the previous kernel: start streaming them
+    // before waiting on it.
     while (p + 1 < ps.n_proj && rb >= ps.rb_start[p + 1]) ++p;
     r0 = (rb - ps.rb_start[p]) * 16;
-    const int rows = ps.rows[p];
-    const int rowA = min(r0 + g, rows - 1), rowB = min(r0 + g + 8, rows - 1);
-    const int per = ng >> ks_log2;
+    const int nrows = ps.rows[p];
+    const int rowA = min(r0 + g, nrows - 1), rowB = min(r0 + g + 8, nrows - 1);
     const uint8_t* w = ps.w[p];
     const __half* s = ps.s[p];
-    u4_dot2<G, 4>(w + (size_t)rowA * (K / 2), w + (size_t)rowB * (K / 2), s + (size_t)rowA * ng,
-                  s + (size_t)rowB * ng, ps.z[p], (int64_t)rowA * ng, (int64_t)rowB * ng, xs,
-                  ks * per, (ks + 1) * per, t, accA, accB);
+    rows = U4Rows{w + (size_t)rowA * (K / 2), w + (size_t)rowB * (K / 2), s + (size_t)rowA * ng,
+                  s + (size_t)rowB * ng, ps.z[p], (int64_t)rowA * ng, (int64_t)rowB * ng};
+    u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
   }
+  pdl_wait();
+  stage_x_perm(xs, x16, x32, nw, eps, K, nred);
+  pdl_launch_dependents();
+  if (valid) u4_dot2_pipelined<G, 2>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
   if (KS > 1) {
     if (t == 0) {
       red[warp][g] = accA;
@@ -93,9 +98,12 @@ __global__ void __launch_bounds__(256) u4_gemv_multi_kernel(ProjSet ps, const __
   }
 }
 
+// K-split factor (log2): split each row block over up to 8 warps while the
+// whole grid still fits one wave of 2 CTAs x 8 warps on each of the 148 SMs.
 int u4_ks_log2(int total_rb, int ng) {
+  constexpr int kWaveWarps = 148 * 2 * 8;
   int l = 0;
-  while (l < 3 && (total_rb << l) < 2048 && (ng % (2 << l)) == 0) ++l;
+  while (l < 3 && (total_rb << (l + 1)) <= kWaveWarps && (ng % (2 << l)) == 0) ++l;
   return l;
 }
 

@@ -216,27 +216,39 @@ def router_topk(x: torch.Tensor, w_router: torch.Tensor, k: int = 8):
 # (2) experts
 
 
-def moe_expert_ffn(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+def moe_expert_ffn(x: torch.Tensor | None, ids: torch.Tensor, weights: torch.Tensor,
                    routed: ExpertBank, shared: ExpertBank | None = None,
                    shared_logit: torch.Tensor | None = None,
                    out_dtype: torch.dtype = torch.float16, out: torch.Tensor | None = None,
-                   accumulate: bool = False) -> torch.Tensor:
-    """Batch-1 routed (+ shared) expert FFN: sum_r w_r Down(SwiGLU(GateUp(x)))."""
-    _cuda(x, "x", torch.float16)
+                   accumulate: bool = False, x_f32: torch.Tensor | None = None,
+                   norm_weight: torch.Tensor | None = None,
+                   norm_eps: float = 1e-6,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Batch-1 routed (+ shared) expert FFN: sum_r w_r Down(SwiGLU(GateUp(x))).
+
+    With ``x_f32`` and ``norm_weight`` (and ``x`` None) the fp32 residual is
+    RMS-normalised in the kernel prologue."""
+    if x is not None:
+        _cuda(x, "x", torch.float16)
+    else:
+        _cuda(x_f32, "x_f32", torch.float32)
+    dev = (x if x is not None else x_f32).device
     _cuda(ids, "ids", torch.int32)
     _cuda(weights, "weights", torch.float32)
     k = ids.numel()
     h, i = routed.hidden, routed.intermediate
     if out is None:
-        out = torch.empty(h, dtype=out_dtype, device=x.device)
-    ws = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(k, h, i), dtype=torch.uint8,
-                     device=x.device)
+        out = torch.empty(h, dtype=out_dtype, device=dev)
+    if workspace is None:
+        workspace = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(k, h, i),
+                                dtype=torch.uint8, device=dev)
     rb = routed.c()
     sb = shared.c() if shared is not None else None
-    N.call("iq36_moe_decode", x.data_ptr(), ids.data_ptr(), weights.data_ptr(), k,
-           ctypes.byref(rb), ctypes.byref(sb) if sb is not None else None, _ptr(shared_logit),
-           out.data_ptr(), _dtype_code(out.dtype), int(accumulate), ws.data_ptr(), ws.numel(),
-           _stream(x.device))
+    N.call("iq36_moe_decode", _ptr(x), _ptr(x_f32), _ptr(norm_weight), norm_eps,
+           ids.data_ptr(), weights.data_ptr(), k, ctypes.byref(rb),
+           ctypes.byref(sb) if sb is not None else None, _ptr(shared_logit), out.data_ptr(),
+           _dtype_code(out.dtype), int(accumulate), workspace.data_ptr(), workspace.numel(),
+           _stream(dev))
     return out
 
 

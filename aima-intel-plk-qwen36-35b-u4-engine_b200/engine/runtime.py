@@ -275,16 +275,18 @@ class Qwen36Runtime:
                                L["dnorm"], c.eps, c.nk, c.nv, self.b_dout, head_dim=c.dk)
                 ops.u4_matvec_multi(self.b_dout, [L["out"]], [self.hres], accumulate=[True])
                 n += 4
-            ops.rms_norm(self.hres, L["post_norm"], c.eps, out=self.b_x2)
-            N.call("iq36_router_logits", self.b_x2.data_ptr(), None, None, 0.0, 1, c.hidden,
-                   L["router"].data_ptr(), c.experts, L["sgate"].data_ptr(),
+            # post-attention RMSNorm fused into the router and gate_up prologues
+            N.call("iq36_router_logits", None, self.hres.data_ptr(), L["post_norm"].data_ptr(),
+                   c.eps, 1, c.hidden, L["router"].data_ptr(), c.experts, L["sgate"].data_ptr(),
                    self.b_logits_r.data_ptr(), self.b_slogit.data_ptr(),
                    ops._stream(self.dev))
             N.call("iq36_router_select", self.b_logits_r.data_ptr(), 1, c.experts, c.topk,
                    self.b_ids.data_ptr(), self.b_wts.data_ptr(), ops._stream(self.dev))
-            ops.moe_expert_ffn(self.b_x2, self.b_ids, self.b_wts, L["bank"], L["shared"],
-                               self.b_slogit, out=self.hres, accumulate=True)
-            n += 5
+            ops.moe_expert_ffn(None, self.b_ids, self.b_wts, L["bank"], L["shared"],
+                               self.b_slogit, out=self.hres, accumulate=True, x_f32=self.hres,
+                               norm_weight=L["post_norm"], norm_eps=c.eps,
+                               workspace=self.ws_moe)
+            n += 4
         ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
                             norm_weight=W.final_norm, norm_eps=c.eps)
         ops.argmax(self.logits, self.token, self.ws_argmax)

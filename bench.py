@@ -69,10 +69,16 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.index)], stdout=open(self.path, "w"),
+                 "-lms", "100", "-i", str(self.index)], stdout=open(self.path, "w"),
                 stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait for its first sample so the
+        # samples cover the timed region that follows.
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -335,7 +341,7 @@ def run_ours(args, world, rank, local) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=4096)

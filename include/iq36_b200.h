@@ -127,8 +127,11 @@ int iq36_router_select(const float* logits, int32_t T, int32_t E, int32_t k,
  * Follows run_qwen36_moe_ffn_layer (engine/src/gguf_loader.cpp:5654-5782) and
  * the routed part of OpenVINO moe_3gemm_swiglu_opt (patch
  * engine/openvino/iq36-pr35924-grouped-postops.patch:86-124).
- * accumulate=1: out must be fp32 and receives out += result (residual). */
-int iq36_moe_decode(const void* x_f16, const int32_t* ids, const float* weights, int32_t k,
+ * accumulate=1: out must be fp32 and receives out += result (residual).
+ * The activation is x_f16, or (x_f16 NULL) the fp32 residual x_f32 normalised
+ * in the kernel prologue with norm_weight/norm_eps as in iq36_u4_gemv_multi. */
+int iq36_moe_decode(const void* x_f16, const float* x_f32, const float* norm_weight,
+                    float norm_eps, const int32_t* ids, const float* weights, int32_t k,
                     const iq36_expert_bank* routed, const iq36_expert_bank* shared,
                     const float* shared_logit, void* out, int32_t out_dtype,
                     int32_t accumulate, void* workspace, size_t workspace_bytes,

@@ -97,11 +97,14 @@ def test_paged_gqa_rejects_bad_shapes(native):
 
 def test_moe_decode_rejects_bad_bank(native):
     bank = native.ExpertBankC(16, 16, 16, 16, 16, 16, 256, 2048, 500, 128)  # I % G != 0
-    assert _status(native, "iq36_moe_decode", 16, 16, 16, 8, ctypes.byref(bank), None, None, 16,
-                   1, 0, 256, 1 << 20, None) == -2
+    assert _status(native, "iq36_moe_decode", 16, None, None, 0.0, 16, 16, 8, ctypes.byref(bank),
+                   None, None, 16, 1, 0, 256, 1 << 20, None) == -2
     bank = native.ExpertBankC(16, 16, 16, 16, 16, 16, 256, 2048, 512, 128)
-    assert _status(native, "iq36_moe_decode", 16, 16, 16, 8, ctypes.byref(bank), None, None, 16,
-                   1, 0, 256, 8, None) == -4
+    assert _status(native, "iq36_moe_decode", 16, None, None, 0.0, 16, 16, 8, ctypes.byref(bank),
+                   None, None, 16, 1, 0, 256, 8, None) == -4
+    # fp32 input without a norm weight
+    assert _status(native, "iq36_moe_decode", None, 16, None, 0.0, 16, 16, 8, ctypes.byref(bank),
+                   None, None, 16, 1, 0, 256, 1 << 20, None) == -1
 
 
 def test_status_strings(native):
