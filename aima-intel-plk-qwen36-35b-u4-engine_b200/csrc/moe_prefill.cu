@@ -1,7 +1,704 @@
-// moe_prefill.cu — placeholder while the grouped tcgen05 path is written.
+// moe_prefill.cu — grouped MoE prefill on tcgen05 tensor cores.
+//
+// Dataflow (reference: Gen-1 schedule grouped_s8_u4_f16_contribution_moe.cl:
+// 13-222 -> grouped GEMMs -> deterministic scatter :847-861; the stock
+// OpenVINO path gather -> up/gate GEMM with swish*up post-op -> down GEMM ->
+// scatter, iq36-pr35924-grouped-postops.patch:15-124), all on the device with
+// no host readback:
+//   1. pf_hist     per-CTA expert histograms of the T*k assignments;
+//   2. pf_scan     expert offsets, per-CTA bases, and the 128-row tile table;
+//   3. pf_place    stable position of each assignment (by expert, then token,
+//                  then rank), inverse map, permuted token ids and weights;
+//   4. pf_gather   Xp[p] = fp16(x[token(p)]) in the permuted operand order;
+//   5. GEMM1       per tile: [128 x H] . W_gu,e^T -> [128 x 256] fp32 in TMEM
+//                  (128 gate + the matching 128 up columns), SwiGLU epilogue,
+//                  act fp16;
+//   6. GEMM2       per tile: [128 x I] . W_d,e^T -> [128 x 256] fp32, times the
+//                  router weight, contributions Y fp32;
+//   7. pf_scatter  out[t] = sum over ranks r (in order) of Y[inv(t, r)].
+//
+// GEMM kernel (one 128x256 output tile per CTA, 6 warps):
+//   warp 0      TMA producer of the activation tile (SWIZZLE_128B, 64 fp16 of
+//               K per row per stage, no multicast);
+//   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
+//               (kind::f16, M=128 N=256 K=16, fp32 accumulate in TMEM);
+//   warps 2..5  u4 -> fp16 dequant producers during the main loop (codes,
+//               scales, zero points streamed from HBM; (q - zp) * scale with
+//               one fp16 rounding, written to shared memory in the canonical
+//               SW128 K-major layout), then the epilogue (tcgen05.ld).
+// A 4-stage shared-memory ring (48 KB per stage) is synchronised with
+// mbarriers; every wait is bounded and writes an error word on expiry.
+//
+// Operand order: inside each 8-element K chunk both operands hold the
+// elements in the order (0,4,1,5,2,6,3,7) — the natural order of the nibble
+// unpack — so the dequant needs no permute; the gather (activations) and the
+// GEMM1 epilogue (act) write that order.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "launch.cuh"
 #include "common.cuh"
-extern "C" size_t iq36_moe_prefill_workspace_bytes(int32_t, int32_t, int32_t, int32_t, int32_t) { return 256; }
-extern "C" int iq36_moe_prefill(const void*, int32_t, const int32_t*, const float*, int32_t,
-                                const iq36_expert_bank*, void*, int32_t, void*, size_t, iq36_stream_t) {
-  return IQ36_ERR_SHAPE;
+
+namespace iq36 {
+
+constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64, kPfStages = 4;
+constexpr int kPfAStage = kPfBM * kPfBK * 2;  // 16 KB
+constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
+constexpr int kPfStageBytes = kPfAStage + kPfBStage;
+constexpr int kPfSmem = kPfStages * kPfStageBytes + 1024 + 256;
+constexpr int kPfThreads = 192;
+constexpr int kPfChunk = 2048;  // assignments per schedule CTA
+constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kTmemCols = 256;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers: mbarrier, TMA, tcgen05
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t tx) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(tx)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Bounded wait: false once 200 ms have passed (a legitimate wait here lasts
+// microseconds) or after kSpinLimit polls, whichever comes first.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > 200000000ull) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];\n" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(dst_smem),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: canonical K-major, SWIZZLE_128B, 8-row
+// atoms 1024 bytes apart (SBO), descriptor version 1, base offset 0 (atoms
+// are 1024-byte aligned).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // SBO
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor, kind::f16: D fp32, A and B fp16, both K-major,
+// N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPfBN >> 3) << 17) | ((uint32_t)(kPfBM >> 4) << 24);
+
+// ---------------------------------------------------------------------------
+// Schedule kernels
+
+struct PfWork {
+  int32_t* hist;      // [nC, E]
+  int32_t* cbase;     // [nC, E]
+  int32_t* offset;    // [E]
+  int32_t* tile_count;
+  int32_t* tile_expert;
+  int32_t* tile_row0;
+  int32_t* tile_rows;
+  int32_t* inv;       // [P]
+  int32_t* perm_tok;  // [P]
+  float* perm_w;      // [P]
+  int32_t* err;
+  __half* xp;         // [P + 128, H]
+  __half* act;        // [P + 128, I]
+  float* y;           // [P + 128, H]
+};
+
+__global__ void __launch_bounds__(256) pf_hist_kernel(const int32_t* ids, int P, int E,
+                                                      PfWork w) {
+  __shared__ int32_t h[256];
+  pdl_wait();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int a0 = blockIdx.x * kPfChunk;
+  for (int a = a0 + threadIdx.x; a < min(a0 + kPfChunk, P); a += blockDim.x) {
+    const int e = min(max(ids[a], 0), E - 1);
+    atomicAdd(&h[e], 1);
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) w.hist[(size_t)blockIdx.x * E + e] = h[e];
+}
+
+// One CTA, thread e = expert (E <= 256).
+__global__ void __launch_bounds__(256) pf_scan_kernel(int nC, int E, PfWork w) {
+  __shared__ int32_t s_tot[256], s_tiles[256];
+  pdl_wait();
+  const int e = threadIdx.x;
+  int tot = 0;
+  if (e < E)
+    for (int c = 0; c < nC; ++c) tot += w.hist[(size_t)c * E + e];
+  s_tot[e] = e < E ? tot : 0;
+  s_tiles[e] = e < E ? (tot + kPfBM - 1) / kPfBM : 0;
+  __syncthreads();
+  if (e == 0) {  // sequential exclusive scans over <= 256 experts
+    int run = 0, trun = 0;
+    for (int i = 0; i < 256; ++i) {
+      const int t0 = s_tot[i], n0 = s_tiles[i];
+      s_tot[i] = run;
+      s_tiles[i] = trun;
+      run += t0;
+      trun += n0;
+    }
+    *w.tile_count = trun;
+  }
+  __syncthreads();
+  if (e < E) {
+    const int off = s_tot[e];
+    w.offset[e] = off;
+    int run = off;
+    for (int c = 0; c < nC; ++c) {
+      w.cbase[(size_t)c * E + e] = run;
+      run += w.hist[(size_t)c * E + e];
+    }
+    const int t0 = s_tiles[e];
+    for (int i = 0; off + i * kPfBM < run; ++i) {
+      w.tile_expert[t0 + i] = e;
+      w.tile_row0[t0 + i] = off + i * kPfBM;
+      w.tile_rows[t0 + i] = min(kPfBM, run - (off + i * kPfBM));
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Stable placement: CTA c owns assignments [c*2048, (c+1)*2048) in order; in
+// 8 rounds of 256 it ranks each assignment among earlier ones of its expert.
+__global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* ids, const float* weights,
+                                                       int P, int E, int k, PfWork w) {
+  __shared__ int32_t run[256];
+  __shared__ int32_t wc[8][256];
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += 256) run[e] = w.cbase[(size_t)blockIdx.x * E + e];
+  const int a0 = blockIdx.x * kPfChunk;
+  for (int r = 0; r < kPfChunk / 256; ++r) {
+    for (int i = tid; i < 8 * 256; i += 256) (&wc[0][0])[i] = 0;
+    __syncthreads();
+    const int a = a0 + r * 256 + tid;
+    const bool valid = a < P;
+    const int e = valid ? min(max(ids[a], 0), E - 1) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_w = __popc(peers & ((1u << lane) - 1u));
+    if (valid && rank_w == 0) wc[warp][e] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int before = 0;
+      for (int v = 0; v < warp; ++v) before += wc[v][e];
+      const int p = run[e] + before + rank_w;
+      w.inv[a] = p;
+      w.perm_tok[p] = a / k;
+      w.perm_w[p] = weights[a];
+    }
+    __syncthreads();
+    for (int e2 = tid; e2 < E; e2 += 256) {
+      int add = 0;
+      for (int v = 0; v < 8; ++v) add += wc[v][e2];
+      run[e2] += add;
+    }
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+}
+
+// Xp[p][:] = fp16(x[token(p)][:]) with each 8-chunk stored as (0,4,1,5,2,6,3,7).
+__global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* x, int P, int H,
+                                                        PfWork w) {
+  pdl_wait();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= P) return;
+  const int t = w.perm_tok[warp];
+  const __nv_bfloat16* src = x + (size_t)t * H;
+  __half* dst = w.xp + (size_t)warp * H;
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + c * 8);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(b[j]));
+    uint4 o;
+    o.x = pack_half2(h[0], h[4]);
+    o.y = pack_half2(h[1], h[5]);
+    o.z = pack_half2(h[2], h[6]);
+    o.w = pack_half2(h[3], h[7]);
+    *reinterpret_cast<uint4*>(dst + c * 8) = o;
+  }
+  pdl_launch_dependents();
+}
+
+// out[t][h] = sum_r Y[inv(t,r)][h], ranks in order.
+__global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, void* out,
+                                                         int out_dtype, PfWork w) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  int rows[16];
+  for (int r = 0; r < k; ++r) rows[r] = w.inv[(size_t)t * k + r];
+  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < k; ++r) {
+      const float4 v = *reinterpret_cast<const float4*>(w.y + (size_t)rows[r] * H + h);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (out_dtype == IQ36_BF16) {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H + h;
+      o[0] = __float2bfloat16_rn(acc.x);
+      o[1] = __float2bfloat16_rn(acc.y);
+      o[2] = __float2bfloat16_rn(acc.z);
+      o[3] = __float2bfloat16_rn(acc.w);
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + h) = acc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMM
+
+struct GemmArgs {
+  const uint8_t* w;     // expert bank codes
+  const __half* s;      // scales
+  const uint8_t* z;     // zero points
+  int64_t exp_rows;     // weight rows per expert (2I for gate_up, H for down)
+  int K;                // reduction length (H or I)
+  int I;                // intermediate size (gate_up row split)
+  int H;
+  PfWork work;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_wait();
+  const int mt = blockIdx.x, nt = blockIdx.y;
+  if (mt >= *g.work.tile_count) return;  // uniform per CTA
+  const int e = g.work.tile_expert[mt];
+  const int row0 = g.work.tile_row0[mt];
+  const int rows = g.work.tile_rows[mt];
+
+  const uint32_t base_raw = smem_u32(smem_raw);
+  const uint32_t base = (base_raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - base_raw);
+  const uint32_t bar_full = base + kPfStages * kPfStageBytes;  // kPfStages x 8 B
+  const uint32_t bar_empty = bar_full + kPfStages * 8;
+  const uint32_t bar_acc = bar_empty + kPfStages * 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPfStages * kPfStageBytes + 3 * kPfStages * 8 + 8);
+  const uint32_t tmem_slot_s = smem_u32(tmem_slot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1 + 128);  // A producer (with tx) + 128 dequant threads
+      mbar_init(bar_empty + 8 * s, 1);       // tcgen05.commit
+    }
+    mbar_init(bar_acc, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot_s, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nkb = g.K / kPfBK;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---- activation producer (TMA) ----
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % kPfStages;
+        const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
+        ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
+        if (!ok) break;
+        mbar_arrive_tx(bar_full + 8 * s, kPfAStage);
+        tma_load_2d(base + s * kPfStageBytes, &tmA, kb * kPfBK, row0, bar_full + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % kPfStages;
+        const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
+        ok = mbar_wait(bar_full + 8 * s, ph);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_s = base + s * kPfStageBytes;
+        const uint32_t b_s = a_s + kPfAStage;
+#pragma unroll
+        for (int kk = 0; kk < kPfBK / 16; ++kk)
+          umma_f16(tmem, sw128_desc(a_s + kk * 32), sw128_desc(b_s + kk * 32), kIdesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(bar_empty + 8 * s);  // stage free once these MMAs complete
+      }
+      umma_commit(bar_acc);  // accumulator complete
+    }
+  } else {
+    // ---- u4 -> fp16 dequant producers (128 threads), rows p and p + 128 ----
+    const int p = threadIdx.x - 64;
+    const int ng = g.K / 128;
+    const uint8_t* wrow[2];
+    const __half* srow[2];
+    int64_t zrow[2];
+    for (int h = 0; h < 2; ++h) {
+      const int n = p + 128 * h;
+      int gr;
+      if (MODE == 0) gr = (n < 128) ? (nt * 128 + n) : (g.I + nt * 128 + (n - 128));
+      else gr = nt * kPfBN + n;
+      const int64_t er = (int64_t)e * g.exp_rows + gr;
+      wrow[h] = g.w + er * (g.K / 2);
+      srow[h] = g.s + er * ng;
+      zrow[h] = er * ng;
+    }
+    const __half2 sixteenth = __float2half2_rn(0.0625f);
+    for (int kb = 0; kb < nkb && ok; ++kb) {
+      const int s = kb % kPfStages;
+      const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
+      // fetch codes before waiting for the slot
+      uint4 v[2][2];
+      uint32_t zz[2];
+      __half2 s2[2], s16[2];
+      for (int h = 0; h < 2; ++h) {
+        v[h][0] = ld_stream_v4(wrow[h] + kb * 32);
+        v[h][1] = ld_stream_v4(wrow[h] + kb * 32 + 16);
+        const int grp = kb >> 1;
+        const __half sc = srow[h][grp];
+        s2[h] = __halves2half2(sc, sc);
+        s16[h] = __hmul2(s2[h], sixteenth);
+        const int64_t ze = zrow[h] + grp;
+        zz[h] = (uint32_t)(__ldg(g.z + (ze >> 1)) >> ((ze & 1) * 4)) & 15u;
+      }
+      ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
+      if (!ok) break;
+      uint8_t* bst = smem + s * kPfStageBytes + kPfAStage;
+      for (int h = 0; h < 2; ++h) {
+        const int n = p + 128 * h;
+        const uint32_t zlo = 0x64006400u | zz[h] | (zz[h] << 16);
+        const uint32_t zhi = 0x64006400u | (zz[h] << 4) | (zz[h] << 20);
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[h][0]);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t wd = wv[c];
+          uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+          uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+          wd >>= 8;
+          uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+          uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+          __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2[h]);
+          __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16[h]);
+          __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2[h]);
+          __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16[h]);
+          uint4 o;
+          o.x = *reinterpret_cast<uint32_t*>(&r0);
+          o.y = *reinterpret_cast<uint32_t*>(&r1);
+          o.z = *reinterpret_cast<uint32_t*>(&r2);
+          o.w = *reinterpret_cast<uint32_t*>(&r3);
+          *reinterpret_cast<uint4*>(bst + n * 128 + ((c ^ (n & 7)) << 4)) = o;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar_full + 8 * s);
+    }
+
+    // ---- epilogue: TMEM -> registers -> global ----
+    if (ok) ok = mbar_wait(bar_acc, 0);
+    tc_fence_after();
+    const int sp = warp & 3;            // TMEM sub-partition of this warp
+    const int m = sp * 32 + lane;       // tile row = TMEM lane
+    const uint32_t tl = tmem + ((uint32_t)(sp * 32) << 16);
+    if (ok) {
+      if (MODE == 0) {
+        for (int j = 0; j < 128; j += 32) {
+          uint32_t gv[32], uv[32];
+          tmem_ld32(tl + j, gv);
+          tmem_ld32(tl + 128 + j, uv);
+          tmem_ld_wait();
+          if (m < rows) {
+            __half* dst = g.work.act + (size_t)(row0 + m) * g.I + nt * 128 + j;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              __half a8[8];
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const float gt = __uint_as_float(gv[8 * q + c]);
+                const float up = __uint_as_float(uv[8 * q + c]);
+                a8[c] = __float2half_rn(gt * sigmoidf_acc(gt) * up);
+              }
+              uint4 o;
+              o.x = pack_half2(a8[0], a8[4]);
+              o.y = pack_half2(a8[1], a8[5]);
+              o.z = pack_half2(a8[2], a8[6]);
+              o.w = pack_half2(a8[3], a8[7]);
+              *reinterpret_cast<uint4*>(dst + 8 * q) = o;
+            }
+          }
+        }
+      } else {
+        const float wt = m < rows ? g.work.perm_w[row0 + m] : 0.f;
+        for (int j = 0; j < kPfBN; j += 32) {
+          uint32_t yv[32];
+          tmem_ld32(tl + j, yv);
+          tmem_ld_wait();
+          if (m < rows) {
+            float* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 o = make_float4(__uint_as_float(yv[4 * q]) * wt,
+                                     __uint_as_float(yv[4 * q + 1]) * wt,
+                                     __uint_as_float(yv[4 * q + 2]) * wt,
+                                     __uint_as_float(yv[4 * q + 3]) * wt);
+              *reinterpret_cast<float4*>(dst + 4 * q) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!ok) atomicExch(g.work.err, 1);
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+struct PfLayout {
+  size_t hist, cbase, offset, tile_count, tile_expert, tile_row0, tile_rows, inv, perm_tok,
+      perm_w, err, xp, act, y, total;
+};
+
+static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+static PfLayout pf_layout(int T, int k, int E, int H, int I) {
+  const size_t P = (size_t)T * k;
+  const size_t nC = (P + kPfChunk - 1) / kPfChunk;
+  const size_t maxt = (P + kPfBM - 1) / kPfBM + E;
+  PfLayout L{};
+  size_t o = 0;
+  L.hist = o; o += up256(nC * E * 4);
+  L.cbase = o; o += up256(nC * E * 4);
+  L.offset = o; o += up256((size_t)E * 4);
+  L.tile_count = o; o += 256;
+  L.tile_expert = o; o += up256(maxt * 4);
+  L.tile_row0 = o; o += up256(maxt * 4);
+  L.tile_rows = o; o += up256(maxt * 4);
+  L.inv = o; o += up256(P * 4);
+  L.perm_tok = o; o += up256(P * 4);
+  L.perm_w = o; o += up256(P * 4);
+  L.err = o; o += 256;
+  L.xp = o; o += up256((P + kPfBM) * (size_t)H * 2);
+  L.act = o; o += up256((P + kPfBM) * (size_t)I * 2);
+  L.y = o; o += up256((P + kPfBM) * (size_t)H * 4);
+  L.total = o;
+  return L;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor [rows, cols] (cols contiguous), box 64 x 128, SWIZZLE_128B.
+static bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kPfBK, (cuuint32_t)kPfBM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t moe_prefill_ws(int T, int k, int E, int H, int I) { return pf_layout(T, k, E, H, I).total; }
+
+int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* weights, int k,
+                       const iq36_expert_bank* b, void* out, int out_dtype, void* ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+  if (!x || !ids || !weights || !b || !out) return IQ36_ERR_ARG;
+  if (!b->gate_up_weight || !b->gate_up_scale || !b->gate_up_zp || !b->down_weight ||
+      !b->down_scale || !b->down_zp)
+    return IQ36_ERR_ARG;
+  const int E = b->num_experts, H = b->hidden, I = b->intermediate;
+  if (b->group != 128 || T < 1 || k < 1 || k > 16 || E < 1 || E > 256) return IQ36_ERR_SHAPE;
+  if (H % 256 || I % 128 || H < 256 || I < 128 || (int64_t)T * k > (1 << 28)) return IQ36_ERR_SHAPE;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16) return IQ36_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(b->gate_up_weight, 16) ||
+      !aligned(b->down_weight, 16))
+    return IQ36_ERR_ALIGN;
+  const PfLayout L = pf_layout(T, k, E, H, I);
+  if (!ws || ws_bytes < L.total) return IQ36_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return IQ36_ERR_ALIGN;
+  char* base = reinterpret_cast<char*>(ws);
+  PfWork w;
+  w.hist = reinterpret_cast<int32_t*>(base + L.hist);
+  w.cbase = reinterpret_cast<int32_t*>(base + L.cbase);
+  w.offset = reinterpret_cast<int32_t*>(base + L.offset);
+  w.tile_count = reinterpret_cast<int32_t*>(base + L.tile_count);
+  w.tile_expert = reinterpret_cast<int32_t*>(base + L.tile_expert);
+  w.tile_row0 = reinterpret_cast<int32_t*>(base + L.tile_row0);
+  w.tile_rows = reinterpret_cast<int32_t*>(base + L.tile_rows);
+  w.inv = reinterpret_cast<int32_t*>(base + L.inv);
+  w.perm_tok = reinterpret_cast<int32_t*>(base + L.perm_tok);
+  w.perm_w = reinterpret_cast<float*>(base + L.perm_w);
+  w.err = reinterpret_cast<int32_t*>(base + L.err);
+  w.xp = reinterpret_cast<__half*>(base + L.xp);
+  w.act = reinterpret_cast<__half*>(base + L.act);
+  w.y = reinterpret_cast<float*>(base + L.y);
+  const int P = T * k;
+  const int nC = (P + kPfChunk - 1) / kPfChunk;
+  const int maxt = (P + kPfBM - 1) / kPfBM + E;
+
+  CUtensorMap map_x, map_act;
+  if (!make_map(&map_x, w.xp, (uint64_t)P + kPfBM, (uint64_t)H) ||
+      !make_map(&map_act, w.act, (uint64_t)P + kPfBM, (uint64_t)I))
+    return IQ36_ERR_CUDA;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (!attr_set[dev].load()) {
+    if (cudaFuncSetAttribute(pf_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPfSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPfSmem) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+    attr_set[dev].store(true);
+  }
+  if (cudaMemsetAsync(w.err, 0, 4, stream) != cudaSuccess) return IQ36_ERR_CUDA;
+
+  cudaError_t e = launch(pf_hist_kernel, dim3(nC), dim3(256), 0, stream, ids, P, E, w);
+  if (e == cudaSuccess) e = launch(pf_scan_kernel, dim3(1), dim3(256), 0, stream, nC, E, w);
+  if (e == cudaSuccess)
+    e = launch(pf_place_kernel, dim3(nC), dim3(256), 0, stream, ids, weights, P, E, k, w);
+  if (e == cudaSuccess)
+    e = launch(pf_gather_kernel, dim3(ceil_div(P, 8)), dim3(256), 0, stream,
+               reinterpret_cast<const __nv_bfloat16*>(x), P, H, w);
+  GemmArgs g1{b->gate_up_weight, reinterpret_cast<const __half*>(b->gate_up_scale),
+              b->gate_up_zp, (int64_t)2 * I, H, I, H, w};
+  if (e == cudaSuccess)
+    e = launch(pf_gemm_kernel<0>, dim3(maxt, I / 128), dim3(kPfThreads), (size_t)kPfSmem, stream,
+               map_x, g1);
+  GemmArgs g2{b->down_weight, reinterpret_cast<const __half*>(b->down_scale), b->down_zp,
+              (int64_t)H, I, I, H, w};
+  if (e == cudaSuccess)
+    e = launch(pf_gemm_kernel<1>, dim3(maxt, H / kPfBN), dim3(kPfThreads), (size_t)kPfSmem,
+               stream, map_act, g2);
+  if (e == cudaSuccess)
+    e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, T, H, k, out, out_dtype, w);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+}  // namespace iq36
+
+extern "C" size_t iq36_moe_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
+                                                   int32_t hidden, int32_t intermediate) {
+  return iq36::moe_prefill_ws(T, k, num_experts, hidden, intermediate);
+}
+
+extern "C" int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids,
+                                const float* weights, int32_t k, const iq36_expert_bank* routed,
+                                void* out, int32_t out_dtype, void* workspace,
+                                size_t workspace_bytes, iq36_stream_t stream) {
+  return iq36::moe_prefill_launch(x_bf16, T, ids, weights, k, routed, out, out_dtype, workspace,
+                                  workspace_bytes, iq36::as_stream(stream));
 }

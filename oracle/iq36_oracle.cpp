@@ -454,8 +454,10 @@ void orc_delta_step(const float* act, const float* g, const float* beta, float* 
 // :847-861 (scatter, fixed rank order), stock gather/GEMM/scatter
 // iq36-pr35924-grouped-postops.patch:15-124. Rounding points of the tensor-core
 // path: gate_up and down accumulate in fp32 (fp64 here), SwiGLU output rounded
-// to bf16 (the second GEMM's operand), contribution = down * weight in fp32,
-// out = sum over ranks in rank order.
+// to fp16 (the second GEMM's operand type), contribution = down * weight in
+// fp32, out = sum over ranks in rank order. Weights are dequantised exactly
+// (the tensor-core path rounds each dequantised weight to fp16; the tolerance
+// covers that).
 void orc_moe_prefill(const uint16_t* x_bf16, const int32_t* tokens, int n_tokens, int H,
                      const int32_t* ids, const float* weights, int k, const uint8_t* gu_w,
                      const uint16_t* gu_s, const uint8_t* gu_z, const uint8_t* d_w,
@@ -478,7 +480,7 @@ void orc_moe_prefill(const uint16_t* x_bf16, const int32_t* tokens, int n_tokens
                                           gu_z + e * gu_zb, n);
       for (int j = 0; j < I; ++j) {
         const double gg = gu[j], uu = gu[I + j];
-        act[j] = round_bf16((float)(gg * sigmoid_d(gg) * uu));
+        act[j] = round_f16((float)(gg * sigmoid_d(gg) * uu));
       }
       for (int n = 0; n < H; ++n)
         dn[n] = (float)u4_row_dot_precise(act.data(), I, G, d_w + e * d_wb, d_s + e * d_sn,

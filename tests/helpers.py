@@ -65,6 +65,16 @@ def make_bank(rng, experts: int, hidden: int, inter: int, group: int = 128) -> d
     }
 
 
+def zipf_router_logits(rng: np.random.Generator, tokens: int, experts: int = 256,
+                       s: float = 1.1, span: float = 2.0) -> np.ndarray:
+    """BASELINE config 3 router logits: N(0,1) plus a per-expert bias from a
+    Zipf(s) ranking (a seeded permutation assigns ranks), scaled to [-span, span]."""
+    ranks = rng.permutation(experts) + 1
+    w = ranks.astype(np.float64) ** (-s)
+    bias = -span + 2 * span * (w - w.min()) / (w.max() - w.min())
+    return (rng.standard_normal((tokens, experts)) + bias[None, :]).astype(np.float32)
+
+
 def bank_to_torch(bank: dict, device, group: int = 128):
     import torch
     from engine.ops import ExpertBank
