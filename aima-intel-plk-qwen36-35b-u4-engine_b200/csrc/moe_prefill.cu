@@ -17,17 +17,22 @@
 //                  router weight, contributions Y fp32;
 //   7. pf_scatter  out[t] = sum over ranks r (in order) of Y[inv(t, r)].
 //
-// GEMM kernel (one 128x256 output tile per CTA, 6 warps):
+// GEMM kernel (one 128x256 output tile per CTA, 7 warps):
 //   warp 0      TMA producer of the activation tile (SWIZZLE_128B, 64 fp16 of
 //               K per row per stage, no multicast);
 //   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
 //               (kind::f16, M=128 N=256 K=16, fp32 accumulate in TMEM);
-//   warps 2..5  u4 -> fp16 dequant producers during the main loop (codes,
-//               scales, zero points streamed from HBM; (q - zp) * scale with
-//               one fp16 rounding, written to shared memory in the canonical
-//               SW128 K-major layout), then the epilogue (tcgen05.ld).
-// A 4-stage shared-memory ring (48 KB per stage) is synchronised with
-// mbarriers; every wait is bounded and writes an error word on expiry.
+//   warp 2      TMA producer of the raw u4 codes (32 bytes x 256 rows per
+//               k-block) into a 6-deep ring that runs ahead of the MMA;
+//   warps 3..6  dequant producers during the main loop: codes from shared
+//               memory, scales and zero points staged once per tile,
+//               (q - zp) * scale with one fp16 rounding, written in the
+//               canonical SW128 K-major layout; then the epilogue
+//               (tcgen05.ld -> registers -> global).
+// The A/B ring has 3 stages (48 KB each); all rings are synchronised with
+// mbarriers; every wait is time-bounded and writes an error word on expiry.
+// Grid: blockIdx.x = N tile (fastest) so the N tiles of one M tile run
+// together and share the activation tile in L2.
 //
 // Operand order: inside each 8-element K chunk both operands hold the
 // elements in the order (0,4,1,5,2,6,3,7) — the natural order of the nibble
@@ -45,12 +50,18 @@
 
 namespace iq36 {
 
-constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64, kPfStages = 4;
+constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64, kPfStages = 3, kPfCodeStages = 6;
 constexpr int kPfAStage = kPfBM * kPfBK * 2;  // 16 KB
 constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
 constexpr int kPfStageBytes = kPfAStage + kPfBStage;
-constexpr int kPfSmem = kPfStages * kPfStageBytes + 1024 + 256;
-constexpr int kPfThreads = 192;
+constexpr int kPfCodeStage = kPfBN * (kPfBK / 2);  // 8 KB of u4 codes
+constexpr int kPfMaxGroups = 16;                   // K <= 2048 with G = 128
+constexpr int kPfOffCodes = kPfStages * kPfStageBytes;
+constexpr int kPfOffScale = kPfOffCodes + kPfCodeStages * kPfCodeStage;
+constexpr int kPfOffZp = kPfOffScale + kPfBN * kPfMaxGroups * 2;
+constexpr int kPfOffBar = kPfOffZp + kPfBN * kPfMaxGroups;
+constexpr int kPfSmem = kPfOffBar + 256 + 1024;
+constexpr int kPfThreads = 224;
 constexpr int kPfChunk = 2048;  // assignments per schedule CTA
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr uint32_t kTmemCols = 256;
@@ -337,9 +348,8 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, vo
 // Grouped GEMM
 
 struct GemmArgs {
-  const uint8_t* w;     // expert bank codes
-  const __half* s;      // scales
-  const uint8_t* z;     // zero points
+  const __half* s;      // scales of the bank
+  const uint8_t* z;     // zero points of the bank
   int64_t exp_rows;     // weight rows per expert (2I for gate_up, H for down)
   int K;                // reduction length (H or I)
   int I;                // intermediate size (gate_up row split)
@@ -348,11 +358,12 @@ struct GemmArgs {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                                GemmArgs g) {
+__global__ void __launch_bounds__(kPfThreads, 1)
+    pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   pdl_wait();
-  const int mt = blockIdx.x, nt = blockIdx.y;
+  const int nt = blockIdx.x, mt = blockIdx.y;
   if (mt >= *g.work.tile_count) return;  // uniform per CTA
   const int e = g.work.tile_expert[mt];
   const int row0 = g.work.tile_row0[mt];
@@ -361,17 +372,35 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - base_raw);
-  const uint32_t bar_full = base + kPfStages * kPfStageBytes;  // kPfStages x 8 B
-  const uint32_t bar_empty = bar_full + kPfStages * 8;
-  const uint32_t bar_acc = bar_empty + kPfStages * 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPfStages * kPfStageBytes + 3 * kPfStages * 8 + 8);
+  const uint32_t bar_full = base + kPfOffBar;              // kPfStages x 8 B
+  const uint32_t bar_empty = bar_full + kPfStages * 8;     // kPfStages x 8 B
+  const uint32_t bar_cfull = bar_empty + kPfStages * 8;    // kPfCodeStages x 8 B
+  const uint32_t bar_cempty = bar_cfull + kPfCodeStages * 8;
+  const uint32_t bar_acc = bar_cempty + kPfCodeStages * 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPfOffBar + 8 * (2 * kPfStages + 2 * kPfCodeStages + 1));
   const uint32_t tmem_slot_s = smem_u32(tmem_slot);
+  __half* s_scale = reinterpret_cast<__half*>(smem + kPfOffScale);  // [256][16]
+  uint8_t* s_zp = smem + kPfOffZp;                                   // [256][16]
+
+  // weight rows of this tile: two 128-row halves
+  int64_t wrow0, wrow1;
+  if (MODE == 0) {
+    wrow0 = (int64_t)e * g.exp_rows + nt * 128;           // gate rows
+    wrow1 = (int64_t)e * g.exp_rows + g.I + nt * 128;     // matching up rows
+  } else {
+    wrow0 = (int64_t)e * g.exp_rows + nt * kPfBN;
+    wrow1 = wrow0 + 128;
+  }
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(bar_full + 8 * s, 1 + 128);  // A producer (with tx) + 128 dequant threads
       mbar_init(bar_empty + 8 * s, 1);       // tcgen05.commit
+    }
+    for (int s = 0; s < kPfCodeStages; ++s) {
+      mbar_init(bar_cfull + 8 * s, 1);       // code producer (with tx)
+      mbar_init(bar_cempty + 8 * s, 128);    // dequant threads
     }
     mbar_init(bar_acc, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -418,48 +447,62 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
       }
       umma_commit(bar_acc);  // accumulator complete
     }
+  } else if (warp == 2) {
+    // ---- raw u4 code producer (TMA), runs up to 6 k-blocks ahead ----
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int cs = kb % kPfCodeStages;
+        const uint32_t ph = (uint32_t)((kb / kPfCodeStages) & 1);
+        ok = mbar_wait(bar_cempty + 8 * cs, ph ^ 1u);
+        if (!ok) break;
+        const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
+        mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
+        tma_load_2d(dst, &tmW, kb * (kPfBK / 2), (int)wrow0, bar_cfull + 8 * cs);
+        tma_load_2d(dst + kPfCodeStage / 2, &tmW, kb * (kPfBK / 2), (int)wrow1,
+                    bar_cfull + 8 * cs);
+      }
+    }
   } else {
-    // ---- u4 -> fp16 dequant producers (128 threads), rows p and p + 128 ----
-    const int p = threadIdx.x - 64;
+    // ---- dequant producers (128 threads), tile rows p and p + 128 ----
+    const int p = threadIdx.x - 96;
     const int ng = g.K / 128;
-    const uint8_t* wrow[2];
-    const __half* srow[2];
-    int64_t zrow[2];
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < 2; ++h) {  // scales / zero points of this thread's rows, once per tile
+      const int64_t er = (h == 0 ? wrow0 : wrow1) + p;
       const int n = p + 128 * h;
-      int gr;
-      if (MODE == 0) gr = (n < 128) ? (nt * 128 + n) : (g.I + nt * 128 + (n - 128));
-      else gr = nt * kPfBN + n;
-      const int64_t er = (int64_t)e * g.exp_rows + gr;
-      wrow[h] = g.w + er * (g.K / 2);
-      srow[h] = g.s + er * ng;
-      zrow[h] = er * ng;
+      for (int grp = 0; grp < ng; ++grp) {
+        s_scale[n * kPfMaxGroups + grp] = g.s[er * ng + grp];
+        const int64_t ze = er * ng + grp;
+        s_zp[n * kPfMaxGroups + grp] = (uint8_t)((__ldg(g.z + (ze >> 1)) >> ((ze & 1) * 4)) & 15u);
+      }
     }
     const __half2 sixteenth = __float2half2_rn(0.0625f);
     for (int kb = 0; kb < nkb && ok; ++kb) {
       const int s = kb % kPfStages;
       const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
-      // fetch codes before waiting for the slot
+      const int cs = kb % kPfCodeStages;
+      const uint32_t cph = (uint32_t)((kb / kPfCodeStages) & 1);
+      ok = mbar_wait(bar_cfull + 8 * cs, cph);
+      if (!ok) break;
       uint4 v[2][2];
-      uint32_t zz[2];
-      __half2 s2[2], s16[2];
+      const uint8_t* cst = smem + kPfOffCodes + cs * kPfCodeStage;
       for (int h = 0; h < 2; ++h) {
-        v[h][0] = ld_stream_v4(wrow[h] + kb * 32);
-        v[h][1] = ld_stream_v4(wrow[h] + kb * 32 + 16);
-        const int grp = kb >> 1;
-        const __half sc = srow[h][grp];
-        s2[h] = __halves2half2(sc, sc);
-        s16[h] = __hmul2(s2[h], sixteenth);
-        const int64_t ze = zrow[h] + grp;
-        zz[h] = (uint32_t)(__ldg(g.z + (ze >> 1)) >> ((ze & 1) * 4)) & 15u;
+        const int n = p + 128 * h;
+        v[h][0] = *reinterpret_cast<const uint4*>(cst + n * 32);
+        v[h][1] = *reinterpret_cast<const uint4*>(cst + n * 32 + 16);
       }
+      mbar_arrive(bar_cempty + 8 * cs);  // codes are in registers: release the slot
       ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
       if (!ok) break;
       uint8_t* bst = smem + s * kPfStageBytes + kPfAStage;
+      const int grp = kb >> 1;
       for (int h = 0; h < 2; ++h) {
         const int n = p + 128 * h;
-        const uint32_t zlo = 0x64006400u | zz[h] | (zz[h] << 16);
-        const uint32_t zhi = 0x64006400u | (zz[h] << 4) | (zz[h] << 20);
+        const __half sc = s_scale[n * kPfMaxGroups + grp];
+        const __half2 s2 = __halves2half2(sc, sc);
+        const __half2 s16 = __hmul2(s2, sixteenth);
+        const uint32_t zz = s_zp[n * kPfMaxGroups + grp];
+        const uint32_t zlo = 0x64006400u | zz | (zz << 16);
+        const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
         const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[h][0]);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -469,10 +512,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
           wd >>= 8;
           uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
           uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
-          __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2[h]);
-          __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16[h]);
-          __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2[h]);
-          __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16[h]);
+          __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2);
+          __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16);
+          __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2);
+          __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16);
           uint4 o;
           o.x = *reinterpret_cast<uint32_t*>(&r0);
           o.y = *reinterpret_cast<uint32_t*>(&r1);
@@ -597,8 +640,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 2-D fp16 tensor [rows, cols] (cols contiguous), box 64 x 128, SWIZZLE_128B.
-static bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols) {
+// 2-D fp16 activation tensor [rows, cols] (cols contiguous), box 64 x 128,
+// SWIZZLE_128B (lands in the canonical SW128 K-major layout).
+static bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols) {
   auto enc = get_encode();
   if (!enc) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -607,6 +651,19 @@ static bool make_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t co
   const cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D u8 code tensor [rows, bytes_per_row], box 32 bytes x 128 rows, no swizzle.
+static bool make_code_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t row_bytes) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)(kPfBK / 2), 128u};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -621,7 +678,9 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
     return IQ36_ERR_ARG;
   const int E = b->num_experts, H = b->hidden, I = b->intermediate;
   if (b->group != 128 || T < 1 || k < 1 || k > 16 || E < 1 || E > 256) return IQ36_ERR_SHAPE;
-  if (H % 256 || I % 128 || H < 256 || I < 128 || (int64_t)T * k > (1 << 28)) return IQ36_ERR_SHAPE;
+  if (H % 256 || I % 128 || H < 256 || I < 128 || H > 2048 || I > 2048 ||
+      (int64_t)T * k > (1 << 28))
+    return IQ36_ERR_SHAPE;
   if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16) return IQ36_ERR_ARG;
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(b->gate_up_weight, 16) ||
       !aligned(b->down_weight, 16))
@@ -649,9 +708,11 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   const int nC = (P + kPfChunk - 1) / kPfChunk;
   const int maxt = (P + kPfBM - 1) / kPfBM + E;
 
-  CUtensorMap map_x, map_act;
-  if (!make_map(&map_x, w.xp, (uint64_t)P + kPfBM, (uint64_t)H) ||
-      !make_map(&map_act, w.act, (uint64_t)P + kPfBM, (uint64_t)I))
+  CUtensorMap map_x, map_act, map_gu, map_d;
+  if (!make_act_map(&map_x, w.xp, (uint64_t)P + kPfBM, (uint64_t)H) ||
+      !make_act_map(&map_act, w.act, (uint64_t)P + kPfBM, (uint64_t)I) ||
+      !make_code_map(&map_gu, b->gate_up_weight, (uint64_t)E * 2 * I, (uint64_t)H / 2) ||
+      !make_code_map(&map_d, b->down_weight, (uint64_t)E * H, (uint64_t)I / 2))
     return IQ36_ERR_CUDA;
   static std::atomic<bool> attr_set[64];
   int dev = 0;
@@ -673,16 +734,15 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   if (e == cudaSuccess)
     e = launch(pf_gather_kernel, dim3(ceil_div(P, 8)), dim3(256), 0, stream,
                reinterpret_cast<const __nv_bfloat16*>(x), P, H, w);
-  GemmArgs g1{b->gate_up_weight, reinterpret_cast<const __half*>(b->gate_up_scale),
-              b->gate_up_zp, (int64_t)2 * I, H, I, H, w};
+  GemmArgs g1{reinterpret_cast<const __half*>(b->gate_up_scale), b->gate_up_zp, (int64_t)2 * I,
+              H, I, H, w};
   if (e == cudaSuccess)
-    e = launch(pf_gemm_kernel<0>, dim3(maxt, I / 128), dim3(kPfThreads), (size_t)kPfSmem, stream,
-               map_x, g1);
-  GemmArgs g2{b->down_weight, reinterpret_cast<const __half*>(b->down_scale), b->down_zp,
-              (int64_t)H, I, I, H, w};
+    e = launch(pf_gemm_kernel<0>, dim3(I / 128, maxt), dim3(kPfThreads), (size_t)kPfSmem, stream,
+               map_x, map_gu, g1);
+  GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
   if (e == cudaSuccess)
-    e = launch(pf_gemm_kernel<1>, dim3(maxt, H / kPfBN), dim3(kPfThreads), (size_t)kPfSmem,
-               stream, map_act, g2);
+    e = launch(pf_gemm_kernel<1>, dim3(H / kPfBN, maxt), dim3(kPfThreads), (size_t)kPfSmem,
+               stream, map_act, map_d, g2);
   if (e == cudaSuccess)
     e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, T, H, k, out, out_dtype, w);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;

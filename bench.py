@@ -338,8 +338,120 @@ def run_ours(args, world, rank, local) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_moe_prefill(args, world, rank, local) -> None:
+    """grouped MoE prefill of T tokens (bf16 ~N(0,1)) over
+    256 u4 g128 experts, router logits N(0,1) + Zipf(1.1)-ranked bias (+-2),
+    top-8. Value: tokens/s; roofline: tensor (T * 50,331,648 FLOP per call)."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    from engine import _native as N
+    from engine import ops
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    E, H, I, k, T = 256, 2048, 512, 8, args.tokens
+    t = {}
+    t["gu_w"] = torch.empty(E, 2 * I, H // 2, dtype=torch.uint8, device=dev)
+    t["gu_s"] = torch.empty(E, 2 * I, H // 128, dtype=torch.float16, device=dev)
+    t["gu_z"] = torch.empty(E, 2 * I * H // 256, dtype=torch.uint8, device=dev)
+    t["d_w"] = torch.empty(E, H, I // 2, dtype=torch.uint8, device=dev)
+    t["d_s"] = torch.empty(E, H, I // 128, dtype=torch.float16, device=dev)
+    t["d_z"] = torch.empty(E, H * I // 256, dtype=torch.uint8, device=dev)
+    for j, v in enumerate(t.values()):
+        ops.synth_fill(v, 1 if v.dtype == torch.float16 else 0, 77, 1000 + j, 0.005, 0.02)
+    bank = ops.ExpertBank(*t.values(), 128)
+    rng = np.random.default_rng(T + rank)
+    ranks = rng.permutation(E) + 1
+    zw = ranks.astype(np.float64) ** -1.1
+    bias = -2 + 4 * (zw - zw.min()) / (zw.max() - zw.min())
+    logits = torch.from_numpy((rng.standard_normal((T, E)) + bias).astype(np.float32)).to(dev)
+    ids, wts = ops.router_select(logits, k)
+    x = torch.randn(T, H, device=dev, generator=torch.Generator(dev).manual_seed(5)).to(
+        torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.float32, device=dev)
+    ws = torch.empty(N.lib().iq36_moe_prefill_workspace_bytes(T, k, E, H, I), dtype=torch.uint8,
+                     device=dev)
+    rb = bank.c()
+    stream = torch.cuda.current_stream(dev)
+
+    def call():
+        N.call("iq36_moe_prefill", x.data_ptr(), T, ids.data_ptr(), wts.data_ptr(), k,
+               ctypes.byref(rb), out.data_ptr(), 0, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    if args.profile_step:
+        torch.cuda.profiler.start()
+        call()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "workload": "moe_prefill", "T": T}))
+        return
+    # the expert weights (418 MB) exceed L2; flush L2 between calls anyway
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        call()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    per_call = max_over_ranks(sum(s.elapsed_time(e) for s, e in evs) / len(evs) / 1e3, world)
+    flops = T * 50331648
+    tflops = flops / per_call / 1e12
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    # e2e: activations and routing from pinned host memory, output back to host
+    hx = x.cpu().pin_memory()
+    hids, hw = ids.cpu().pin_memory(), wts.cpu().pin_memory()
+    hout = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        x.copy_(hx, non_blocking=True)
+        ids.copy_(hids, non_blocking=True)
+        wts.copy_(hw, non_blocking=True)
+        call()
+        hout.copy_(out, non_blocking=True)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    line = {
+        "metric": "grouped MoE prefill tok/s (BASELINE config 3)", "value": round(
+            world * T / per_call, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_call * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->fp16 mma, fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": f"config3 grouped MoE prefill T={T}, 256 experts, top-8, "
+                               "Zipf(1.1)-skewed routing", "T": T, "l2": "flushed between calls"},
+        "e2e": {"value": round(world * T / t_e2e, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": T * H * 2 + T * k * 8, "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": 7 * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "iq36_moe_prefill (all 7 launches)",
+                     "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "traffic": None},
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--workload", choices=["decode", "moe_prefill"], default="decode")
+    ap.add_argument("--tokens", type=int, default=4096, help="T for --workload moe_prefill")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
@@ -354,6 +466,8 @@ def main() -> None:
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "moe_prefill":
+            run_moe_prefill(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
