@@ -196,7 +196,16 @@ struct ExpertArgs {
   const __half* sd_s;
   const uint8_t* sd_z;
   int H, I, k, n_slots, num_experts;
+  int e_lo;  // global id of the bank's expert 0 (expert-sharded decode)
 };
+
+// Local index of the expert routed to `slot`, or -1 when the bank does not
+// hold it (another rank owns it, or the id is out of range): such slots read
+// no weights and contribute zero.
+__device__ __forceinline__ int owned_expert(const ExpertArgs& a, const int32_t* ids, int slot) {
+  const int e = ids[slot] - a.e_lo;
+  return (e >= 0 && e < a.num_experts) ? e : -1;
+}
 
 // Row pair (gate row j, up row I+j) of one gate_up warp task.
 template <int G>
@@ -208,7 +217,7 @@ __device__ __forceinline__ U4Rows gate_up_rows(const ExpertArgs& a, const int32_
   const uint8_t* z;
   int64_t zbase;
   if (slot < a.k) {
-    const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
+    const int64_t e = max(owned_expert(a, ids, slot), 0);
     w = a.gu_w + e * (int64_t)(2 * I) * (H / 2);
     s = a.gu_s + e * (int64_t)(2 * I) * ng;
     z = a.gu_z;
@@ -251,13 +260,14 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const in
     u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
   }
   pdl_wait();
-  if (valid && slot < a.k) {
+  const bool work = valid && (slot >= a.k || owned_expert(a, ids, slot) >= 0);
+  if (work && slot < a.k) {
     rows = gate_up_rows<G>(a, ids, slot, j0, g);
     u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
   }
   stage_x_perm(xs, x16, x32, nw, eps, a.H, nred);
   pdl_launch_dependents();
-  if (valid) u4_dot2_pipelined<G, 2>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
+  if (work) u4_dot2_pipelined<G, 2>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
   if (KS > 1) {
     if (t == 0) {
       red[warp][g] = accA;
@@ -298,8 +308,9 @@ __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* w
   const __half* s;
   const uint8_t* z;
   int64_t zbase;
+  const int owned = slot < a.k ? owned_expert(a, ids, slot) : 0;
   if (slot < a.k) {
-    const int64_t e = min(max(ids[slot], 0), a.num_experts - 1);  // never address outside the bank
+    const int64_t e = max(owned, 0);
     w = a.d_w + e * (int64_t)H * (I / 2);
     s = a.d_s + e * (int64_t)H * ngi;
     z = a.d_z;
@@ -314,12 +325,13 @@ __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* w
                     s + (size_t)rowA * ngi, s + (size_t)rowB * ngi, z,
                     zbase + (int64_t)rowA * ngi, zbase + (int64_t)rowB * ngi};
   U4Chunk<G, 2> first;
-  u4_load_chunk<G, 2>(first, rows, 0, ngi, t);
+  if (owned >= 0) u4_load_chunk<G, 2>(first, rows, 0, ngi, t);
   pdl_wait();
   stage_x_perm(xs, act, nullptr, nullptr, 0.f, a.n_slots * I, nred);
   pdl_launch_dependents();
   float accA = 0.f, accB = 0.f;
-  u4_dot2_pipelined<G, 2>(first, rows, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+  if (owned >= 0)
+    u4_dot2_pipelined<G, 2>(first, rows, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
   if (t == 0) {
     red[slot][g] = accA;
     red[slot][g + 8] = accB;
@@ -366,7 +378,7 @@ int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, fl
                       const int32_t* ids, const float* weights, int k,
                       const iq36_expert_bank* routed, const iq36_expert_bank* shared,
                       const float* shared_logit, void* out, int out_dtype, int accumulate,
-                      void* ws, size_t ws_bytes, cudaStream_t stream) {
+                      void* ws, size_t ws_bytes, cudaStream_t stream, int e_lo = 0) {
   int st = check_bank(routed);
   if (st != IQ36_OK) return st;
   if (!ids || !weights || !out) return IQ36_ERR_ARG;
@@ -376,10 +388,12 @@ int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, fl
     if (!x_f16) return IQ36_ERR_ARG;
     if (!aligned(x_f16, 16)) return IQ36_ERR_ALIGN;
   }
-  if (k < 1 || k > 15 || k > routed->num_experts) return IQ36_ERR_SHAPE;
+  if (k < 1 || k > 15 || e_lo < 0 || (e_lo == 0 && k > routed->num_experts))
+    return IQ36_ERR_SHAPE;
   if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
   if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
   ExpertArgs a = {};
+  a.e_lo = e_lo;
   a.gu_w = routed->gate_up_weight;
   a.gu_s = reinterpret_cast<const __half*>(routed->gate_up_scale);
   a.gu_z = routed->gate_up_zp;
@@ -494,6 +508,19 @@ extern "C" int iq36_moe_decode(const void* x_f16, const float* x_f32, const floa
   return iq36::moe_decode_launch(x_f16, x_f32, norm_weight, norm_eps, ids, weights, k, routed,
                                  shared, shared_logit, out, out_dtype, accumulate, workspace,
                                  workspace_bytes, iq36::as_stream(stream));
+}
+
+extern "C" int iq36_moe_decode_sharded(const void* x_f16, const float* x_f32,
+                                       const float* norm_weight, float norm_eps,
+                                       const int32_t* ids, const float* weights, int32_t k,
+                                       const iq36_expert_bank* local_bank, int32_t expert_lo,
+                                       const iq36_expert_bank* shared, const float* shared_logit,
+                                       void* out, int32_t out_dtype, int32_t accumulate,
+                                       void* workspace, size_t workspace_bytes,
+                                       iq36_stream_t stream) {
+  return iq36::moe_decode_launch(x_f16, x_f32, norm_weight, norm_eps, ids, weights, k, local_bank,
+                                 shared, shared_logit, out, out_dtype, accumulate, workspace,
+                                 workspace_bytes, iq36::as_stream(stream), expert_lo);
 }
 
 extern "C" size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden,

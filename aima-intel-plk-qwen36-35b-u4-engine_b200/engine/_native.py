@@ -56,6 +56,9 @@ _SIGS: dict[str, tuple] = {
     "iq36_moe_decode": (c_int, [_P, _P, _P, c_float, _P, _P, c_int32, POINTER(ExpertBankC),
                                 POINTER(ExpertBankC), _P, _P, c_int32, c_int32, _P, c_size_t, _P]),
     "iq36_moe_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "iq36_moe_decode_sharded": (c_int, [_P, _P, _P, c_float, _P, _P, c_int32,
+                                        POINTER(ExpertBankC), c_int32, POINTER(ExpertBankC), _P,
+                                        _P, c_int32, c_int32, _P, c_size_t, _P]),
     "iq36_moe_block_decode": (c_int, [_P, _P, _P, c_int32, POINTER(ExpertBankC),
                                       POINTER(ExpertBankC), _P, _P, _P, _P, c_int32, _P,
                                       c_size_t, _P]),

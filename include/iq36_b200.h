@@ -138,6 +138,19 @@ int iq36_moe_decode(const void* x_f16, const float* x_f32, const float* norm_wei
                     iq36_stream_t stream);
 size_t iq36_moe_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
 
+/* Expert-sharded form of iq36_moe_decode for expert-parallel decode (no
+ * counterpart in the reference, which runs on one device): local_bank holds
+ * the experts with global ids [expert_lo, expert_lo + local_bank->num_experts);
+ * routed slots whose expert lies outside that range read no weights and
+ * contribute zero, so summing the outputs of all ranks (one allreduce) gives
+ * the full block. Pass the shared expert on exactly one rank. */
+int iq36_moe_decode_sharded(const void* x_f16, const float* x_f32, const float* norm_weight,
+                            float norm_eps, const int32_t* ids, const float* weights, int32_t k,
+                            const iq36_expert_bank* local_bank, int32_t expert_lo,
+                            const iq36_expert_bank* shared, const float* shared_logit, void* out,
+                            int32_t out_dtype, int32_t accumulate, void* workspace,
+                            size_t workspace_bytes, iq36_stream_t stream);
+
 /* Config-1 block: router logits -> select -> routed + shared experts.
  * ids/weights/logits are outputs (device). */
 int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16, const void* w_shared_gate_f16,

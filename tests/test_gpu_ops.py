@@ -174,6 +174,39 @@ def test_moe_decode_without_shared_and_accumulate(cuda, config1):
     assert_close(_np(out), ref, "moe no-shared")
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_moe_decode_sharded_partials_sum_to_full(cuda, config1, world):
+    """Expert-sharded decode emulated on one GPU: the per-shard partial sums
+    (shared expert on shard 0) add up to the full block."""
+    import ctypes
+    import torch
+    from engine import _native as N
+    from engine.ops import moe_expert_ffn
+    from engine.parallel_tp import shard_expert_bank
+    c = config1
+    rb, sb = bank_to_torch(c["bank"], cuda), bank_to_torch(c["shared"], cuda)
+    ids = _t(np.array([5, 250, 17, 81, 128, 3, 99, 200], np.int32), cuda)
+    wts = _t(np.array([0.3, 0.2, 0.15, 0.1, 0.1, 0.06, 0.05, 0.04], np.float32), cuda)
+    sl = _t(np.array([0.7], np.float32), cuda)
+    x = _t(c["x"], cuda)
+    full = moe_expert_ffn(x, ids, wts, rb, sb, sl, out_dtype=torch.float32)
+    total = torch.zeros_like(full)
+    ws = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(8, 2048, 512), dtype=torch.uint8,
+                     device=cuda)
+    for r in range(world):
+        local, e0 = shard_expert_bank(rb, r, world)
+        part = torch.empty_like(full)
+        lb = local.c()
+        sbc = sb.c()
+        N.call("iq36_moe_decode_sharded", x.data_ptr(), None, None, 0.0, ids.data_ptr(),
+               wts.data_ptr(), 8, ctypes.byref(lb), e0,
+               ctypes.byref(sbc) if r == 0 else None, sl.data_ptr() if r == 0 else None,
+               part.data_ptr(), 0, 0, ws.data_ptr(), ws.numel(),
+               torch.cuda.current_stream(cuda).cuda_stream)
+        total += part
+    assert_close(_np(total), _np(full), f"sharded x{world}", max_rel=1e-5)
+
+
 # ---------------------------------------------------------------------------
 # (3) paged GQA decode (BASELINE config 2)
 

@@ -1,0 +1,65 @@
+"""Multi-rank paths: expert-parallel prefill exchange and TP/EP decode.
+
+CPU tests run 2 gloo ranks (the exchange and sharding logic, with the CPU
+reference as the local expert/GEMV function); GPU tests run one NCCL rank per
+GPU and are skipped with fewer than 2 GPUs.
+"""
+
+import multiprocessing as mp
+import socket
+
+import pytest
+
+import _mp_workers as W
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(fn, world: int, timeout: float = 240.0):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            rank, status = q.get(timeout=timeout)
+            results[rank] = status
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    bad = {r: s for r, s in results.items() if s != "ok"}
+    assert not bad, "\n".join(f"rank {r}:\n{s}" for r, s in bad.items())
+
+
+def test_ep_prefill_exchange_gloo():
+    _run(W.ep_prefill_cpu, 2)
+
+
+def test_tp_gemv_sharding_gloo():
+    _run(W.tp_gemv_cpu, 2)
+
+
+def _gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_ep_prefill_nccl_matches_single_gpu():
+    _run(W.ep_prefill_gpu, 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_ep_decode_nccl_matches_single_gpu():
+    _run(W.ep_decode_gpu, 2)
