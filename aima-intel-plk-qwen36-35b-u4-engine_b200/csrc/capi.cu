@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "launch.cuh"
+#include "u4_stream.cuh"
 
 namespace iq36 {
 static std::atomic<int> g_pdl{1};
@@ -27,3 +28,11 @@ extern "C" const char* iq36_status_string(int status) {
 }
 
 extern "C" void iq36_set_pdl(int enabled) { iq36::g_pdl.store(enabled ? 1 : 0); }
+
+extern "C" int iq36_wait_timeouts(int32_t* count, int32_t reset) {
+  if (count == nullptr) return IQ36_ERR_ARG;
+  int c = 0;
+  const int st = iq36::stream_wait_timeouts(&c, reset);
+  *count = c;
+  return st;
+}

@@ -13,6 +13,7 @@
 
 #include "launch.cuh"
 #include "u4_core.cuh"
+#include "u4_stream.cuh"
 
 namespace iq36 {
 
@@ -148,6 +149,10 @@ int u4_gemv_multi_launch(const void* x_f16, const float* x_f32, const float* nor
     rb += ceil_div(p.m.rows, 16);
   }
   ps.rb_start[n_proj] = rb;
+  // Row counts in whole 16-row chunks and 16-byte aligned tensors take the
+  // bulk-copy streaming kernel (u4_stream.cu); other shapes this one.
+  if (stream_proj_ok(K, G, n_proj, proj))
+    return stream_proj_launch(x_f16, x_f32, norm_w, eps, K, G, n_proj, proj, stream);
   const int ng = K / G;
   const int ks_log2 = u4_ks_log2(rb, ng);
   const int rb_per_cta = 8 >> ks_log2;

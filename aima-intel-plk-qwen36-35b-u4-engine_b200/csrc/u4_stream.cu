@@ -1,0 +1,304 @@
+// u4_stream.cu — streaming (cp.async.bulk ring) version of the decode
+// multi-output projections (fixed-FC family, LM head). Semantics are those of
+// u4_gemv.cu (same quantisation arithmetic and rounding points); the
+// difference is how weights reach the SM and the zero-point handling (see
+// u4_stream.cuh). MoE experts stay on the register kernels of moe_decode.cu:
+// routed weights cannot be fetched before the router has run, and right after
+// the wait those kernels' many independent loads beat one producer thread.
+//
+// Work split: chunk = 16 rows x full K. Every consumer warp of a CTA works
+// on every chunk, a slice of the quant groups each, so a ring stage is
+// released a slice-time after it lands and the whole ring stays in flight. The per-warp partial
+// sums go to shared memory and are summed in fixed warp order every
+// kRedChunks chunks (double-buffered, one named barrier per batch).
+
+#include "launch.cuh"
+#include "u4_stream.cuh"
+
+namespace iq36 {
+
+constexpr int kStreamCtas = 148;
+constexpr int kRedChunks = 8;  // chunks per deferred cross-warp reduction
+
+// Count of bounded waits that gave up, per device (read by iq36_wait_timeouts).
+__device__ int g_stream_wait_timeouts;
+
+__device__ __forceinline__ void stream_note_timeout(int* err) {
+  if (threadIdx.x % 32 == 0) atomicAdd(&g_stream_wait_timeouts, 1);
+  if (err) atomicExch(err, 1);
+}
+
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;\n" ::"r"(kStreamConsumers * 32) : "memory");
+}
+
+// Stage the activation for the consumer threads only (named barrier 1):
+// xs[c] = permuted fp16 chunk c (see u4_core.cuh), and per quant group
+// xc[g] = {1024*E + 64*O, E + O} over the fp16 values actually staged.
+template <int G>
+__device__ __forceinline__ void stream_stage_x(uint4* xs, float2* xc, const __half* x16,
+                                               const float* x32, const float* nw, float eps,
+                                               int K, float* red) {
+  const int tid = threadIdx.x, nt = kStreamConsumers * 32;
+  float scale = 1.0f;
+  if (x32 != nullptr) {
+    float ss = 0.0f;
+    for (int i = tid; i < K; i += nt) ss = fmaf(x32[i], x32[i], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumer_sync();
+    float v = 0.f;
+    for (int i = 0; i < kStreamConsumers; ++i) v += red[i];
+    scale = rsqrtf(v / (float)K + eps);
+  }
+  const __half2 sixteenth = __float2half2_rn(0.0625f);
+  constexpr int kPerGroup = G / 8;  // chunks per quant group (a power of two <= 16)
+  for (int base = 0; base < K / 8; base += nt) {
+    const int c = base + tid;
+    float e = 0.f, o = 0.f;
+    if (c < K / 8) {
+      __half h[8];
+      if (x32 != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          h[j] = __float2half_rn(x32[c * 8 + j] * scale * nw[c * 8 + j]);
+      } else {
+        const uint4 raw = *reinterpret_cast<const uint4*>(x16 + c * 8);
+        const __half* hp = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = hp[j];
+      }
+      __half2 p0 = __halves2half2(h[0], h[4]);
+      __half2 p1 = __hmul2(__halves2half2(h[1], h[5]), sixteenth);
+      __half2 p2 = __halves2half2(h[2], h[6]);
+      __half2 p3 = __hmul2(__halves2half2(h[3], h[7]), sixteenth);
+      uint4 q;
+      q.x = *reinterpret_cast<uint32_t*>(&p0);
+      q.y = *reinterpret_cast<uint32_t*>(&p1);
+      q.z = *reinterpret_cast<uint32_t*>(&p2);
+      q.w = *reinterpret_cast<uint32_t*>(&p3);
+      xs[c] = q;
+      e = (__half2float(h[0]) + __half2float(h[2])) + (__half2float(h[4]) + __half2float(h[6]));
+      o = (__half2float(h[1]) + __half2float(h[3])) + (__half2float(h[5]) + __half2float(h[7]));
+    }
+#pragma unroll
+    for (int m = kPerGroup / 2; m > 0; m >>= 1) {
+      e += __shfl_xor_sync(0xffffffffu, e, m);
+      o += __shfl_xor_sync(0xffffffffu, o, m);
+    }
+    if (c < K / 8 && (c % kPerGroup) == 0) xc[c / kPerGroup] = make_float2(1024.f * e + 64.f * o, e + o);
+  }
+  consumer_sync();
+}
+
+// Shared-memory layout of every streaming kernel:
+//   [ring: stages x stage_bytes][xs: K/8 x 16 B][xc: K/G x 8 B]
+//   [red: 2 x kRedChunks x consumer warps x 16 floats][misc: 16 floats]
+//   [barriers: full[8], empty[8]]
+//   [seq: chunk armed per stage [8], abort flag]
+struct StreamSmem {
+  uint32_t ring, xs, xc, red, misc, full, empty, seq;
+  int total;
+};
+
+__host__ __device__ inline StreamSmem stream_smem(const StreamGeom& g, int xs_k, int G) {
+  StreamSmem s;
+  s.ring = 0;
+  s.xs = g.stages * g.stage_bytes;
+  s.xc = s.xs + xs_k / 8 * 16;
+  s.red = s.xc + (xs_k / G) * 8;
+  s.misc = s.red + 2 * kRedChunks * kStreamConsumers * 16 * 4;
+  s.full = s.misc + 64;
+  s.empty = s.full + 64;
+  s.seq = s.empty + 64;
+  s.total = s.seq + 64;
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// Multi-output projections
+
+struct StreamProj {
+  const uint8_t* w[4];
+  const __half* s[4];
+  const uint8_t* z[4];
+  void* out[4];
+  int dtype[4];
+  int acc[4];
+  int chunk_start[5];
+  int n_proj;
+};
+
+__device__ __forceinline__ void store_row(void* out, int dtype, int acc, int row, float v) {
+  if (dtype == IQ36_F16) {
+    reinterpret_cast<__half*>(out)[row] = __float2half_rn(v);
+  } else if (acc) {
+    float* o = reinterpret_cast<float*>(out);
+    o[row] = o[row] + __half2float(__float2half_rn(v));
+  } else {
+    reinterpret_cast<float*>(out)[row] = v;
+  }
+}
+
+__device__ __forceinline__ ChunkSrc proj_chunk(const StreamProj& ps, int q, int K, int ng, int& p,
+                                               int& r0) {
+  p = 0;
+  while (p + 1 < ps.n_proj && q >= ps.chunk_start[p + 1]) ++p;
+  r0 = (q - ps.chunk_start[p]) * 16;
+  ChunkSrc c;
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + 8 * h;
+    c.w[h] = ps.w[p] + (size_t)r * (K / 2);
+    c.s[h] = ps.s[p] + (size_t)r * ng;
+    c.z[h] = ps.z[p] + (size_t)r * ng / 2;
+    c.rows[h] = 8;
+  }
+  return c;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    u4_stream_proj_kernel(StreamProj ps, const __half* x16, const float* x32, const float* nw,
+                          float eps, int K, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const StreamGeom geo = stream_geom(K, G);
+  const StreamSmem L = stream_smem(geo, K, G);
+  const uint32_t sbase = smem_u32(smem);
+  volatile int* seq = reinterpret_cast<volatile int*>(smem + L.seq);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = ps.chunk_start[ps.n_proj];
+  const int per = (total + gridDim.x - 1) / gridDim.x;
+  const int c0 = blockIdx.x * per, nloc = max(min(c0 + per, total) - c0, 0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < geo.stages; ++s) {
+      sm_mbar_init(sbase + L.full + 8 * s, 1);
+      sm_mbar_init(sbase + L.empty + 8 * s, kStreamConsumers);
+    }
+    for (int s = 0; s < 8; ++s) seq[s] = -1;  // no chunk armed yet
+    seq[8] = 0;                                // abort flag
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  bool ok = true;
+  if (warp == kStreamConsumers) {
+    // producer: weights only, no dependency on the previous kernel
+    pdl_launch_dependents();
+    if (lane == 0) {
+      for (int c = 0; c < nloc && ok; ++c) {
+        const int s = c % geo.stages;
+        const uint32_t ph = (uint32_t)((c / geo.stages) & 1);
+        ok = sm_mbar_wait(sbase + L.empty + 8 * s, ph ^ 1u);
+        if (!ok) break;
+        int p, r0;
+        const ChunkSrc src = proj_chunk(ps, c0 + c, K, geo.ng, p, r0);
+        sm_mbar_arrive_tx(sbase + L.full + 8 * s, chunk_bytes(geo, src));
+        ring_publish(seq, s, c);
+        issue_chunk(geo, src, sbase + L.ring + s * geo.stage_bytes, sbase + L.full + 8 * s);
+      }
+    }
+  } else {
+    pdl_wait();
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    uint4* xs = reinterpret_cast<uint4*>(smem + L.xs);
+    float2* xc = reinterpret_cast<float2*>(smem + L.xc);
+    stream_stage_x<G>(xs, xc, x16, x32, nw, eps, K, reinterpret_cast<float*>(smem + L.misc));
+    pdl_launch_dependents();
+    const int g = lane >> 2, t = lane & 3;
+    const int gb = warp * geo.ng / kStreamConsumers, ge = (warp + 1) * geo.ng / kStreamConsumers;
+    for (int c = 0; c < nloc; ++c) {
+      const int s = c % geo.stages, j = c % kRedChunks;
+      float accA = 0.f, accB = 0.f;
+      if (__all_sync(0xffffffffu, ring_wait(seq, sbase + L.full + 8 * s, s, c, geo.stages))) {
+        chunk_dot_range<G>(geo, smem + L.ring + s * geo.stage_bytes, xs, xc, lane, gb, ge, accA,
+                           accB);
+        __syncwarp();
+        if (lane == 0) sm_mbar_arrive(sbase + L.empty + 8 * s);
+      } else if (lane == 0) {
+        seq[8] = 1;  // shared so that every consumer warp leaves at the barrier below
+      }
+      float* rbuf = red + ((c / kRedChunks) & 1) * kRedChunks * kStreamConsumers * 16;
+      if (t == 0) {
+        rbuf[(j * kStreamConsumers + warp) * 16 + g] = accA;
+        rbuf[(j * kStreamConsumers + warp) * 16 + g + 8] = accB;
+      }
+      if (j == kRedChunks - 1 || c == nloc - 1) {
+        consumer_sync();
+        if (seq[8] != 0) {
+          ok = false;
+          break;
+        }
+        for (int i = threadIdx.x; i < (j + 1) * 16; i += kStreamConsumers * 32) {
+          const int jj = i >> 4, r = i & 15;
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kStreamConsumers; ++w) v += rbuf[(jj * kStreamConsumers + w) * 16 + r];
+          int p, r0;
+          proj_chunk(ps, c0 + c - j + jj, K, geo.ng, p, r0);
+          store_row(ps.out[p], ps.dtype[p], ps.acc[p], r0 + r, v);
+        }
+      }
+    }
+  }
+  if (!ok) stream_note_timeout(err);
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+
+static int stream_attr(const void* fn, int bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+                 cudaSuccess
+             ? IQ36_OK
+             : IQ36_ERR_CUDA;
+}
+
+bool stream_proj_ok(int K, int G, int n_proj, const iq36_u4_projection* proj) {
+  if (G != 128 || K % 512 || K > 4096) return false;
+  for (int i = 0; i < n_proj; ++i) {
+    const iq36_u4_projection& p = proj[i];
+    if (p.m.rows % 16 || !aligned(p.m.weight, 16) || !aligned(p.m.scale, 16) ||
+        !aligned(p.m.zp, 16))
+      return false;
+  }
+  return true;
+}
+
+int stream_proj_launch(const void* x_f16, const float* x_f32, const float* nw, float eps, int K,
+                       int G, int n_proj, const iq36_u4_projection* proj, cudaStream_t stream) {
+  StreamProj ps = {};
+  ps.n_proj = n_proj;
+  int ch = 0;
+  for (int i = 0; i < n_proj; ++i) {
+    ps.w[i] = proj[i].m.weight;
+    ps.s[i] = reinterpret_cast<const __half*>(proj[i].m.scale);
+    ps.z[i] = proj[i].m.zp;
+    ps.out[i] = proj[i].out;
+    ps.dtype[i] = proj[i].out_dtype;
+    ps.acc[i] = proj[i].accumulate;
+    ps.chunk_start[i] = ch;
+    ch += proj[i].m.rows / 16;
+  }
+  ps.chunk_start[n_proj] = ch;
+  const StreamGeom geo = stream_geom(K, G);
+  const StreamSmem L = stream_smem(geo, K, G);
+  const int grid = std::min(kStreamCtas, ch);
+  if (stream_attr((const void*)u4_stream_proj_kernel<128>, L.total) != IQ36_OK)
+    return IQ36_ERR_CUDA;
+  const cudaError_t e =
+      launch(u4_stream_proj_kernel<128>, dim3(grid), dim3(kStreamThreads), (size_t)L.total, stream,
+             ps, reinterpret_cast<const __half*>(x_f16), x_f32, nw, eps, K, (int*)nullptr);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+int stream_wait_timeouts(int* count, int reset) {
+  if (cudaMemcpyFromSymbol(count, g_stream_wait_timeouts, sizeof(int)) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_stream_wait_timeouts, &zero, sizeof(int)) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+  }
+  return IQ36_OK;
+}
+
+}  // namespace iq36

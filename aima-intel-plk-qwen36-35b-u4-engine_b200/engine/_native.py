@@ -47,6 +47,7 @@ _SIGS: dict[str, tuple] = {
     "iq36_version": (c_char_p, []),
     "iq36_status_string": (c_char_p, [c_int]),
     "iq36_set_pdl": (None, [c_int]),
+    "iq36_wait_timeouts": (c_int, [POINTER(c_int32), c_int32]),
     "iq36_u4_gemv": (c_int, [_P, c_int32, c_int32, POINTER(U4Matrix), _P, c_int32, _P]),
     "iq36_u4_gemv_multi": (c_int, [_P, _P, _P, c_float, c_int32, c_int32, c_int32,
                                    POINTER(U4Projection), _P]),
@@ -114,6 +115,13 @@ def call(name: str, *args) -> None:
     if st != 0:
         text = lib().iq36_status_string(st).decode()
         raise Iq36Error(name, st, text)
+
+
+def wait_timeouts(reset: bool = True) -> int:
+    """Bounded device waits that gave up on the current device (see the header)."""
+    n = c_int32(0)
+    call("iq36_wait_timeouts", ctypes.byref(n), 1 if reset else 0)
+    return int(n.value)
 
 
 def exported_symbols() -> list[str]:

@@ -324,7 +324,9 @@ def run_ours(args, world, rank, local) -> None:
                    "step_hbm_frac": round(step_gbs / hbm, 4)},
         "e2e": e2e,
         "gpu_launches": rt.launches_per_step * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "u4_gemv_multi_kernel",
+        "roofline": {"bound": "hbm",
+                     "kernel": "u4 multi-output GEMV (u4_stream_proj_kernel; ragged shapes "
+                               "u4_gemv_multi_kernel), all launches of one step",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
                      "peak_source": src,
@@ -376,9 +378,20 @@ def run_moe_prefill(args, world, rank, local) -> None:
     rb = bank.c()
     stream = torch.cuda.current_stream(dev)
 
-    def call():
-        N.call("iq36_moe_prefill", x.data_ptr(), T, ids.data_ptr(), wts.data_ptr(), k,
-               ctypes.byref(rb), out.data_ptr(), 0, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+    if world > 1:
+        # expert parallel: this rank owns E/world experts and its own T tokens
+        from engine.parallel_ep import ep_moe_prefill, gpu_expert_fn
+        from engine.parallel_tp import shard_expert_bank
+        local, _ = shard_expert_bank(bank, rank, world)
+        efn = gpu_expert_fn(local)
+
+        def call():
+            out.copy_(ep_moe_prefill(x, ids, wts, E, efn))
+    else:
+        def call():
+            N.call("iq36_moe_prefill", x.data_ptr(), T, ids.data_ptr(), wts.data_ptr(), k,
+                   ctypes.byref(rb), out.data_ptr(), 0, ws.data_ptr(), ws.numel(),
+                   stream.cuda_stream)
 
     for _ in range(args.warmup):
         call()
@@ -435,7 +448,9 @@ def run_moe_prefill(args, world, rank, local) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->fp16 mma, fp32 accumulate",
         "data": "synthetic",
         "config": {"workload": f"config3 grouped MoE prefill T={T}, 256 experts, top-8, "
-                               "Zipf(1.1)-skewed routing", "T": T, "l2": "flushed between calls"},
+                               "Zipf(1.1)-skewed routing", "T": T, "l2": "flushed between calls",
+                   "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                   else "single GPU"},
         "e2e": {"value": round(world * T / t_e2e, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": T * H * 2 + T * k * 8, "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": 7 * args.steps,

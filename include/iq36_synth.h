@@ -44,12 +44,23 @@ IQ36_HD uint8_t iq36_synth_u8(uint64_t seed, uint64_t tensor, uint64_t index) {
   return (uint8_t)(iq36_hash(seed, tensor, index) >> 24);
 }
 
+/* Separately rounded multiply and add: a compiler may not fuse them into an
+ * FMA on one side only (nvcc contracts by default; the CPU checker is built
+ * with -ffp-contract=off). */
+#if defined(__CUDA_ARCH__)
+#define IQ36_SYNTH_MUL(a, b) __fmul_rn((a), (b))
+#define IQ36_SYNTH_ADD(a, b) __fadd_rn((a), (b))
+#else
+#define IQ36_SYNTH_MUL(a, b) ((a) * (b))
+#define IQ36_SYNTH_ADD(a, b) ((a) + (b))
+#endif
+
 /* Uniform in [lo, hi) as fp32: 24-bit integer times 2^-24 is exact. */
 IQ36_HD float iq36_synth_uniform(uint64_t seed, uint64_t tensor, uint64_t index,
                                  float lo, float hi) {
   const uint32_t u = (uint32_t)(iq36_hash(seed, tensor, index) >> 40);
   const float unit = (float)u * (1.0f / 16777216.0f);
-  return lo + (hi - lo) * unit;
+  return IQ36_SYNTH_ADD(lo, IQ36_SYNTH_MUL(hi - lo, unit));
 }
 
 /* Approximately N(0, std^2): centred Irwin-Hall(4) of 16-bit uniforms.
@@ -62,8 +73,8 @@ IQ36_HD float iq36_synth_normal(uint64_t seed, uint64_t tensor, uint64_t index,
                     (int32_t)((h >> 32) & 0xFFFFu) + (int32_t)((h >> 48) & 0xFFFFu);
   /* Var of one 16-bit uniform = (65536^2 - 1)/12; four of them: (65536^2-1)/3.
    * 1/sqrt((65536^2-1)/3) ~= sqrt(3)/65536. */
-  const float z = (float)(s - 131070) * 2.6429309e-05f;
-  return z * std_dev;
+  const float z = IQ36_SYNTH_MUL((float)(s - 131070), 2.6429309e-05f);
+  return IQ36_SYNTH_MUL(z, std_dev);
 }
 
 /* ---- synthetic model tensor spec (BASELINE config 4 shapes) ----------------

@@ -28,3 +28,18 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _no_device_wait_timeouts(request):
+    """Every GPU test also fails if a bounded device wait gave up during it."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from engine import _native
+    torch.cuda.synchronize()
+    n = _native.wait_timeouts(reset=True)
+    assert n == 0, f"{n} bounded device waits gave up during this test"

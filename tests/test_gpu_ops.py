@@ -35,6 +35,8 @@ def _np(t):
     (2048, 4096, 128, "f32"),   # o_proj / out_proj shape
     (32, 2048, 128, "f16"),     # DeltaNet a/b projections
     (2048, 512, 128, "f32"),    # expert down shape (K = 512, 4 groups)
+    (16384, 4096, 128, "f32"),  # many chunks per CTA with a 2-stage ring (wraps)
+    (248320, 2048, 128, "f32"), # LM head: ~105 chunks per CTA, ring wraps ~20 times
 ])
 def test_u4_gemv_matches_oracle(cuda, n, k, g, out):
     import torch
