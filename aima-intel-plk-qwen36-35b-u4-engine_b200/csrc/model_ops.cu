@@ -80,20 +80,43 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
   for (int j = 0; j < 8; ++j) x[j] = x[j] * sc * nw[8 * lane + j];
   const int half = rope_dim / 2;
   const int xo = half / 8;  // partner lane offset
+  // Frequency i's angle is computed in fp64 by lane i % 32 (register i / 32):
+  // at most four pow + sincos per lane, all lanes at once; element d takes
+  // frequency d % half.
+  const int nr = (half + 31) / 32;  // <= 4 (rope_dim <= 256)
+  float cr[4], sr[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    cr[r] = 1.f;
+    sr[r] = 0.f;
+    const int i = lane + 32 * r;
+    if (r < nr && i < half) {
+      const double inv = pow((double)rope_base, -2.0 * (double)i / (double)rope_dim);
+      double sn, cs;
+      sincos((double)pos * inv, &sn, &cs);
+      cr[r] = (float)cs;
+      sr[r] = (float)sn;
+    }
+  }
   float y[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float partner = __shfl_xor_sync(0xffffffffu, x[j], xo);
-    const int d = 8 * lane + j;
-    y[j] = x[j];
-    if (d < rope_dim) {
-      const int i = d % half;
-      const double inv = pow((double)rope_base, -2.0 * (double)i / (double)rope_dim);
-      double sn, cs;
-      sincos((double)pos * inv, &sn, &cs);
-      const float c = (float)cs, s = (float)sn;
-      y[j] = d < half ? x[j] * c - partner * s : x[j] * c + partner * s;
+    const int d = 8 * lane + j, i = d % half;
+    float c = 1.f, sn = 0.f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      if (r < nr) {  // warp-uniform
+        const float cc = __shfl_sync(0xffffffffu, cr[r], i & 31);
+        const float ss = __shfl_sync(0xffffffffu, sr[r], i & 31);
+        if ((i >> 5) == r) {
+          c = cc;
+          sn = ss;
+        }
+      }
     }
+    y[j] = x[j];
+    if (d < rope_dim) y[j] = d < half ? x[j] * c - partner * sn : x[j] * c + partner * sn;
   }
   uint4 packed;
   __half* ph = reinterpret_cast<__half*>(&packed);

@@ -20,8 +20,8 @@
 //   O^T += V^T P^T m16n8k16: M = 16 dims (x16 tiles), N = 8 heads, K = 16 tokens;
 // the P tile is transposed in registers with movmatrix. Scores are kept in
 // log2 units (scale * log2 e folded in), fp32 throughout, P in fp16.
-// Kernel 2 (combine): per query head merge the S partials (max, sum, output),
-// normalise, apply sigmoid(gate), store fp32 or fp16.
+// Kernel 2 (combine): per (query head, 32-dim slice) merge the S partials
+// (max, sum, output), normalise, apply sigmoid(gate), store fp32 or fp16.
 
 #include <atomic>
 
@@ -198,38 +198,74 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaArgs a) {
   }
 }
 
-__global__ void __launch_bounds__(256) gqa_combine_kernel(const float* ws_m, const float* ws_l,
-                                                          const float* ws_acc, int S,
-                                                          const __half* gate, void* out,
-                                                          int out_dtype) {
+// Combine: one CTA per (query head, 32-dim slice), 8 warps. The split
+// maxima, weights exp2(m_s - M) and row sums are reduced block-wide; warp w
+// then sums the partial outputs of splits w, w+8, ... for its lane's
+// dimension, and the 8 warp sums are added in fixed order. Splits that saw
+// no page (m = -inf) carry weight 0 and their output rows are never read.
+constexpr int kCombWarps = 8;
+
+__global__ void __launch_bounds__(kCombWarps * 32) gqa_combine_kernel(
+    const float* ws_m, const float* ws_l, const float* ws_acc, int S, const __half* gate,
+    void* out, int out_dtype) {
+  __shared__ float sw[kMaxSplits];
+  __shared__ float red_m[kCombWarps], red_l[kCombWarps];
+  __shared__ float red_o[kCombWarps][32];
   pdl_wait();
-  const int h = blockIdx.x, d = threadIdx.x;
+  const int h = blockIdx.x, d = blockIdx.y * 32 + (threadIdx.x & 31);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = h / kGrp, hl = h % kGrp;
-  float M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, ws_m[((size_t)kvh * S + s) * kGrp + hl]);
-  float L = 0.f, O = 0.f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < S; ++s) {
-      const size_t meta = ((size_t)kvh * S + s) * kGrp + hl;
-      const float m = ws_m[meta];
-      if (m == -INFINITY) continue;
-      const float w = exp2f(m - M);
-      L = fmaf(ws_l[meta], w, L);
-      O = fmaf(ws_acc[meta * kD + d], w, O);
-    }
+  const size_t mbase = (size_t)kvh * S * kGrp + hl;
+  float m = -INFINITY;
+  for (int s = threadIdx.x; s < S; s += kCombWarps * 32) m = fmaxf(m, ws_m[mbase + (size_t)s * kGrp]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red_m[warp] = m;
+  __syncthreads();
+  float M = red_m[0];
+#pragma unroll
+  for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, red_m[w]);
+  float l = 0.f;
+  for (int s = threadIdx.x; s < S; s += kCombWarps * 32) {
+    const float ms = ws_m[mbase + (size_t)s * kGrp];
+    const float w = ms == -INFINITY ? 0.f : exp2f(ms - M);
+    sw[s] = w;
+    if (w != 0.f) l = fmaf(ws_l[mbase + (size_t)s * kGrp], w, l);
   }
+  l = warp_sum(l);
+  if (lane == 0) red_l[warp] = l;
+  __syncthreads();
+  float o = 0.f;
+#pragma unroll 4
+  for (int s = warp; s < S; s += kCombWarps) {
+    const float w = sw[s];
+    if (w != 0.f) o = fmaf(ws_acc[(mbase + (size_t)s * kGrp) * kD + d], w, o);
+  }
+  red_o[warp][lane] = o;
+  __syncthreads();
   pdl_launch_dependents();
-  float v = L > 0.f ? O / L : 0.f;
-  if (gate) v = v * sigmoidf_acc(__half2float(gate[h * kD + d]));
-  if (out_dtype == IQ36_F16)
-    reinterpret_cast<__half*>(out)[h * kD + d] = __float2half_rn(v);
-  else
-    reinterpret_cast<float*>(out)[h * kD + d] = v;
+  if (warp == 0) {
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombWarps; ++w) {
+      O += red_o[w][lane];
+      L += red_l[w];
+    }
+    float v = L > 0.f ? O / L : 0.f;
+    if (gate) v = v * sigmoidf_acc(__half2float(gate[h * kD + d]));
+    if (out_dtype == IQ36_F16)
+      reinterpret_cast<__half*>(out)[h * kD + d] = __float2half_rn(v);
+    else
+      reinterpret_cast<float*>(out)[h * kD + d] = v;
+  }
 }
 
+// Splits per kv head: about two 16-token pages per warp at max_ctx (a warp
+// streams its pages through its ring back to back), a multiple of 4 (warps
+// per CTA), at most kMaxSplits (longer contexts give each warp more pages).
 int gqa_splits(int max_ctx) {
   const int n_pages = (max_ctx + kBS - 1) / kBS;
-  int s = ((n_pages + 3) / 4) * 4;
+  int s = (((n_pages + 1) / 2 + 3) / 4) * 4;
   if (s < 4) s = 4;
   if (s > kMaxSplits) s = kMaxSplits;
   return s;
@@ -284,7 +320,8 @@ int gqa_launch(const void* q, const void* kc, const void* vc, const int32_t* bt,
   cudaError_t e = launch(gqa_split_kernel, dim3(S / 4, n_kv), dim3(128), (size_t)4 * kWarpSmem,
                          stream, a);
   if (e != cudaSuccess) return IQ36_ERR_CUDA;
-  e = launch(gqa_combine_kernel, dim3(n_q), dim3(kD), 0, stream, (const float*)a.ws_m,
+  e = launch(gqa_combine_kernel, dim3(n_q, kD / 32), dim3(kCombWarps * 32), 0, stream,
+             (const float*)a.ws_m,
              (const float*)a.ws_l, (const float*)a.ws_acc, S,
              reinterpret_cast<const __half*>(gate), out, out_dtype);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;

@@ -284,7 +284,8 @@ def test_rms_norm_matches_oracle(cuda):
     assert_close(_np(y), oracle.rms_norm(x, w, 1e-6), "rms_norm", max_rel=1e-5)
 
 
-def test_attn_prep_matches_oracle(cuda):
+@pytest.mark.parametrize("rope_dim", [64, 256])
+def test_attn_prep_matches_oracle(cuda, rope_dim):
     import torch
     from engine.ops import attn_prep
     rng = np.random.default_rng(6)
@@ -302,8 +303,8 @@ def test_attn_prep_matches_oracle(cuda):
         go = torch.empty_like(qo)
         attn_prep(_t(qf, cuda), _t(k, cuda), _t(v, cuda), _t(qn, cuda), _t(kn, cuda), 1e-6,
                   torch.tensor([pos], dtype=torch.int32, device=cuda), _t(bt, cuda), kc, vc,
-                  qo, go)
-        rq, rg, rk, rv = oracle.attn_prep(qf, k, v, qn, kn, 1e-6, pos)
+                  qo, go, rope_dim=rope_dim)
+        rq, rg, rk, rv = oracle.attn_prep(qf, k, v, qn, kn, 1e-6, pos, rope_dim=rope_dim)
         assert_close(_np(qo), rq, f"q rope pos={pos}", max_rel=1e-3)
         np.testing.assert_array_equal(_np(go), rg)
         blk = bt[pos // 16]
