@@ -82,7 +82,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
   stage_x_plain(xsh, x16 ? x16 + (size_t)tok * H : nullptr, x32 ? x32 + (size_t)tok * H : nullptr,
                 nw, eps, H, nred);
   pdl_launch_dependents();
-  if (wr == nullptr) return;
   float acc = 0.f;
   const uint4* xv4 = reinterpret_cast<const uint4*>(xsh);
   auto dot8 = [&](const uint4& wv, const uint4& xv) {
@@ -96,27 +95,26 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
       acc = fmaf(wf.y, xf.y, acc);
     }
   };
+  if (wr != nullptr) {
 #pragma unroll
-  for (int j = 0; j < kPre; ++j) {
-    const int c = lane + 32 * j;
-    if (c < H / 8) dot8(pre[j], xv4[c]);
-  }
-  for (int c = lane + 32 * kPre; c < H / 8; c += 32) dot8(ld_stream_v4(wr + c * 8), xv4[c]);
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    if (row < E) logits[(size_t)tok * E + row] = acc;
-    else slogit[tok] = acc;
+    for (int j = 0; j < kPre; ++j) {
+      const int c = lane + 32 * j;
+      if (c < H / 8) dot8(pre[j], xv4[c]);
+    }
+    for (int c = lane + 32 * kPre; c < H / 8; c += 32) dot8(ld_stream_v4(wr + c * 8), xv4[c]);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      if (row < E) logits[(size_t)tok * E + row] = acc;
+      else slogit[tok] = acc;
+    }
   }
 }
 
-// Warp per token. E <= 256 (8 logits per lane), k <= 16.
-__global__ void __launch_bounds__(256) router_select_kernel(const float* logits, int T, int E,
-                                                            int k, int32_t* ids, float* weights) {
-  pdl_wait();
+// Top-k of one token's E router logits by one warp (E <= 256: 8 logits per
+// lane; k <= 16). Every lane ends with the same sel_id / sel_w (rank order).
+__device__ __forceinline__ void router_topk_warp(const float* l, int E, int k, uint32_t* sel_id,
+                                                 float* sel_w) {
   const int lane = threadIdx.x & 31;
-  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (tok >= T) return;
-  const float* l = logits + (size_t)tok * E;
   const int per = (E + 31) / 32;
   float lv[8];
   float mx = -INFINITY;
@@ -150,8 +148,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(const float* logits,
   }
   // top_k_indices (:3672-3697): descending probability, lower id on ties —
   // the larger 64-bit key (prob bits, inverted id) wins.
-  uint32_t sel_id[16];
-  float sel_p[16];
+  float sum = 0.0f;
   for (int r = 0; r < k; ++r) {
     uint64_t best = 0ull;
 #pragma unroll
@@ -165,16 +162,28 @@ __global__ void __launch_bounds__(256) router_select_kernel(const float* logits,
     for (int i = 0; i < 8; ++i)
       if (key[i] == best) key[i] = 0ull;
     sel_id[r] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
-    sel_p[r] = __uint_as_float((uint32_t)(best >> 32));
+    sel_w[r] = __uint_as_float((uint32_t)(best >> 32));
+    sum = __fadd_rn(sum, sel_w[r]);
   }
+  // normalize_weights (:3712-3731), min sum 6.103515625e-5 (:5665).
+  const float den = fmaxf(sum, 6.103515625e-5f);
+  for (int r = 0; r < k; ++r) sel_w[r] = __fdiv_rn(sel_w[r], den);
+}
+
+// Warp per token. E <= 256, k <= 16.
+__global__ void __launch_bounds__(256) router_select_kernel(const float* logits, int T, int E,
+                                                            int k, int32_t* ids, float* weights) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= T) return;
+  uint32_t sel_id[16];
+  float sel_w[16];
+  router_topk_warp(logits + (size_t)tok * E, E, k, sel_id, sel_w);
   if (lane == 0) {
-    // normalize_weights (:3712-3731), min sum 6.103515625e-5 (:5665).
-    float sum = 0.0f;
-    for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sel_p[r]);
-    const float den = fmaxf(sum, 6.103515625e-5f);
     for (int r = 0; r < k; ++r) {
       ids[(size_t)tok * k + r] = (int32_t)sel_id[r];
-      weights[(size_t)tok * k + r] = __fdiv_rn(sel_p[r], den);
+      weights[(size_t)tok * k + r] = sel_w[r];
     }
   }
 }
@@ -374,6 +383,10 @@ size_t moe_decode_ws(int k, int hidden, int intermediate) {
   return (((size_t)(k + 1) * intermediate * 2) + 255) / 256 * 256;
 }
 
+size_t moe_layer_ws(int k, int hidden, int intermediate) {
+  return moe_decode_ws(k, hidden, intermediate);
+}
+
 int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, float eps,
                       const int32_t* ids, const float* weights, int k,
                       const iq36_expert_bank* routed, const iq36_expert_bank* shared,
@@ -565,4 +578,49 @@ extern "C" int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16
   return moe_decode_launch(x_f16, nullptr, nullptr, 0.f, ids, weights, k, routed, shared,
                            shared ? slogit : nullptr, out, out_dtype, 0, ws2, workspace_bytes - 256,
                            s);
+}
+
+extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_weight,
+                                     float norm_eps, const void* w_router_f16,
+                                     const void* w_shared_gate_f16, int32_t k,
+                                     const iq36_expert_bank* routed,
+                                     const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                                     float* logits, float* shared_logit, void* workspace,
+                                     size_t workspace_bytes, iq36_stream_t stream) {
+  using namespace iq36;
+  if (!residual || !norm_weight || !w_router_f16 || !routed || !ids || !weights || !logits ||
+      !workspace)
+    return IQ36_ERR_ARG;
+  if (shared && (!w_shared_gate_f16 || !shared_logit)) return IQ36_ERR_ARG;
+  int st0 = check_bank(routed);
+  if (st0 == IQ36_OK && shared) st0 = check_bank(shared);
+  if (st0 != IQ36_OK) return st0;
+  if (hidden != routed->hidden || hidden % 8) return IQ36_ERR_SHAPE;
+  if (shared && (shared->hidden != routed->hidden || shared->intermediate != routed->intermediate ||
+                 shared->group != routed->group))
+    return IQ36_ERR_SHAPE;
+  if (k < 1 || k > 15 || k > routed->num_experts || routed->num_experts > 256)
+    return IQ36_ERR_SHAPE;
+  if (!aligned(w_router_f16, 16) || (shared && !aligned(w_shared_gate_f16, 16)) ||
+      !aligned(workspace, 16))
+    return IQ36_ERR_ALIGN;
+  if (workspace_bytes < moe_layer_ws(k, routed->hidden, routed->intermediate))
+    return IQ36_ERR_WORKSPACE;
+  const cudaStream_t s = as_stream(stream);
+  int st = router_logits_launch(nullptr, residual, norm_weight, norm_eps, 1, hidden, w_router_f16,
+                                routed->num_experts, shared ? w_shared_gate_f16 : nullptr, logits,
+                                shared_logit, s);
+  if (st != IQ36_OK) return st;
+  // A separate selection launch measured faster than running the top-k in
+  // the router's last CTA or inside the expert kernels.
+  st = router_select_launch(logits, 1, routed->num_experts, k, ids, weights, s);
+  if (st != IQ36_OK) return st;
+  return moe_decode_launch(nullptr, residual, norm_weight, norm_eps, ids, weights, k, routed,
+                           shared, shared ? shared_logit : nullptr, residual, IQ36_F32, 1,
+                           workspace, workspace_bytes, s);
+}
+
+extern "C" size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden,
+                                                        int32_t intermediate) {
+  return iq36::moe_layer_ws(k, hidden, intermediate);
 }

@@ -64,6 +64,10 @@ _SIGS: dict[str, tuple] = {
                                       POINTER(ExpertBankC), _P, _P, _P, _P, c_int32, _P,
                                       c_size_t, _P]),
     "iq36_moe_block_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "iq36_moe_layer_decode": (c_int, [_P, c_int32, _P, c_float, _P, _P, c_int32,
+                                      POINTER(ExpertBankC), POINTER(ExpertBankC), _P, _P, _P, _P,
+                                      _P, c_size_t, _P]),
+    "iq36_moe_layer_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "iq36_moe_prefill": (c_int, [_P, c_int32, _P, _P, c_int32, POINTER(ExpertBankC), _P, c_int32,
                                  _P, c_size_t, _P]),
     "iq36_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32,

@@ -275,6 +275,38 @@ def moe_block_decode(x: torch.Tensor, w_router: torch.Tensor, w_shared_gate: tor
     return out, ids, wts, logits
 
 
+def moe_layer_workspace(k: int, hidden: int, intermediate: int, device) -> torch.Tensor:
+    """Workspace of iq36_moe_layer_decode (reusable across calls on one stream)."""
+    n = N.lib().iq36_moe_layer_decode_workspace_bytes(k, hidden, intermediate)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def moe_layer_decode(residual: torch.Tensor, norm_weight: torch.Tensor, w_router: torch.Tensor,
+                     w_shared_gate: torch.Tensor | None, routed: ExpertBank,
+                     shared: ExpertBank | None, ids: torch.Tensor, weights: torch.Tensor,
+                     logits: torch.Tensor, shared_logit: torch.Tensor | None,
+                     workspace: torch.Tensor | None = None, k: int = 8,
+                     norm_eps: float = 1e-6) -> None:
+    """One decode MoE FFN layer on the fp32 residual (in place): RMSNorm ->
+    router logits -> top-k -> routed + shared experts -> residual += f16(out).
+    ids / weights / logits / shared_logit receive the router outputs."""
+    _cuda(residual, "residual", torch.float32)
+    dev = residual.device
+    _cuda(ids, "ids", torch.int32)
+    _cuda(weights, "weights", torch.float32)
+    _cuda(logits, "logits", torch.float32)
+    h, i = routed.hidden, routed.intermediate
+    if workspace is None:
+        workspace = moe_layer_workspace(k, h, i, dev)
+    rb = routed.c()
+    sb = shared.c() if shared is not None else None
+    N.call("iq36_moe_layer_decode", residual.data_ptr(), h, norm_weight.data_ptr(), norm_eps,
+           w_router.data_ptr(), _ptr(w_shared_gate), k, ctypes.byref(rb),
+           ctypes.byref(sb) if sb is not None else None, ids.data_ptr(), weights.data_ptr(),
+           logits.data_ptr(), _ptr(shared_logit), workspace.data_ptr(), workspace.numel(),
+           _stream(dev))
+
+
 def moe_expert_ffn_prefill(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                            routed: ExpertBank, out_dtype: torch.dtype = torch.float32,
                            out: torch.Tensor | None = None) -> torch.Tensor:

@@ -221,8 +221,7 @@ class Qwen36Runtime:
         self.b_wts = torch.empty(c.topk, dtype=f32, device=dev)
         self.logits = torch.empty(c.vocab, dtype=f32, device=dev)
         self.ws_gqa = ops.paged_gqa_workspace(max_ctx, c.nq, c.nkv, c.head_dim, dev)
-        self.ws_moe = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(c.topk, h, c.inter),
-                                  dtype=torch.uint8, device=dev)
+        self.ws_moe = ops.moe_layer_workspace(c.topk, h, c.inter, dev)
         self.ws_argmax = torch.empty(N.lib().iq36_argmax_workspace_bytes(), dtype=torch.uint8,
                                      device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
@@ -276,16 +275,10 @@ class Qwen36Runtime:
                 ops.u4_matvec_multi(self.b_dout, [L["out"]], [self.hres], accumulate=[True])
                 n += 4
             # post-attention RMSNorm fused into the router and gate_up prologues
-            N.call("iq36_router_logits", None, self.hres.data_ptr(), L["post_norm"].data_ptr(),
-                   c.eps, 1, c.hidden, L["router"].data_ptr(), c.experts, L["sgate"].data_ptr(),
-                   self.b_logits_r.data_ptr(), self.b_slogit.data_ptr(),
-                   ops._stream(self.dev))
-            N.call("iq36_router_select", self.b_logits_r.data_ptr(), 1, c.experts, c.topk,
-                   self.b_ids.data_ptr(), self.b_wts.data_ptr(), ops._stream(self.dev))
-            ops.moe_expert_ffn(None, self.b_ids, self.b_wts, L["bank"], L["shared"],
-                               self.b_slogit, out=self.hres, accumulate=True, x_f32=self.hres,
-                               norm_weight=L["post_norm"], norm_eps=c.eps,
-                               workspace=self.ws_moe)
+            # (reference run_qwen36_moe_ffn_layer)
+            ops.moe_layer_decode(self.hres, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                                 L["shared"], self.b_ids, self.b_wts, self.b_logits_r,
+                                 self.b_slogit, workspace=self.ws_moe, k=c.topk, norm_eps=c.eps)
             n += 4
         ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
                             norm_weight=W.final_norm, norm_eps=c.eps)

@@ -160,6 +160,25 @@ int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16, const voi
                           size_t workspace_bytes, iq36_stream_t stream);
 size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
 
+/* One decode MoE FFN layer on the fp32 residual stream, as
+ * run_qwen36_moe_ffn_layer (engine/src/gguf_loader.cpp:5654-5782) with the
+ * post-attention RMSNorm in front (:3368-3391):
+ *   x = rms_norm(residual) * norm_weight, rounded to fp16;
+ *   logits = W_router x (fp32, [E]); shared_logit = w_shared_gate . x;
+ *   ids, weights = top-k of softmax(logits) (as iq36_router_select);
+ *   residual += f16(sum_r weights[r] * Expert_{ids[r]}(x)
+ *                   + sigmoid(shared_logit) * Shared(x)).
+ * Four launches (router, top-k, gate_up + SwiGLU, down + combine). ids /
+ * weights / logits / shared_logit are device outputs; workspace: 16-byte
+ * aligned, iq36_moe_layer_decode_workspace_bytes long. */
+int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_weight,
+                          float norm_eps, const void* w_router_f16, const void* w_shared_gate_f16,
+                          int32_t k, const iq36_expert_bank* routed,
+                          const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                          float* logits, float* shared_logit, void* workspace,
+                          size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
+
 /* ---- (2b) grouped MoE prefill ----------------------------------------------
  * For T tokens with top-k routing (ids, weights [T,k]): permute token rows by
  * expert (stable: by expert, then token, then rank), per expert

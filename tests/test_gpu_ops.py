@@ -159,6 +159,36 @@ def test_moe_block_decode_config1(cuda, config1):
     assert_close(_np(out), ref, "moe block config 1")
 
 
+def test_moe_layer_decode_matches_oracle(cuda, config1):
+    """RMSNorm -> router -> top-8 (inside the expert kernels) -> experts ->
+    residual += f16(out), as the reference's MoE FFN layer."""
+    import torch
+    from engine.ops import moe_layer_decode
+    c = config1
+    rng = np.random.default_rng(11)
+    rb, sb = bank_to_torch(c["bank"], cuda), bank_to_torch(c["shared"], cuda)
+    res0 = (rng.standard_normal(2048) * 3).astype(np.float32)
+    nw = rng.uniform(0.9, 1.1, 2048).astype(np.float32)
+    res = _t(res0.copy(), cuda)
+    ids = torch.empty(8, dtype=torch.int32, device=cuda)
+    wts = torch.empty(8, dtype=torch.float32, device=cuda)
+    logits = torch.empty(256, dtype=torch.float32, device=cuda)
+    sl = torch.empty(1, dtype=torch.float32, device=cuda)
+    moe_layer_decode(res, _t(nw, cuda), _t(c["w_router"], cuda), _t(c["w_sg"], cuda), rb, sb,
+                     ids, wts, logits, sl)
+    x16 = oracle.rms_norm(res0, nw, 1e-6).astype(np.float16)
+    ref_logits = oracle.f16_linear(x16, c["w_router"])
+    assert np.max(np.abs(_np(logits) - ref_logits)) <= 1e-4
+    oid, ow = oracle.router_select(_np(logits)[None], 8)
+    np.testing.assert_array_equal(_np(ids).astype(np.int32), oid[0])  # bit-exact selection
+    np.testing.assert_array_equal(_np(wts), ow[0])
+    np.testing.assert_array_equal(oid, oracle.router_select(ref_logits[None], 8)[0])
+    ref_sl = oracle.f16_linear(x16, c["w_sg"])[0]
+    sh0 = {k: v[0] for k, v in c["shared"].items()}
+    ref = oracle.moe_decode(x16, oid[0], ow[0], c["bank"], sh0, ref_sl, 128)
+    assert_close(_np(res), res0 + ref.astype(np.float16).astype(np.float32), "moe layer")
+
+
 def test_moe_decode_without_shared_and_accumulate(cuda, config1):
     import torch
     from engine.ops import moe_expert_ffn
