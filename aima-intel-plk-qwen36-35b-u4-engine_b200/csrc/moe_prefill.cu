@@ -14,26 +14,31 @@
 //                  (128 gate + the matching 128 up columns), SwiGLU epilogue,
 //                  act fp16;
 //   6. GEMM2       per tile: [128 x I] . W_d,e^T -> [128 x 256] fp32, times the
-//                  router weight, contributions Y fp32;
+//                  router weight, contributions Y rounded to fp16;
 //   7. pf_scatter  out[t] = sum over ranks r (in order) of Y[inv(t, r)].
 //
-// GEMM kernel (one 128x256 output tile per CTA, 7 warps):
+// GEMM kernel: persistent, one CTA per SM (grid min(148, units)); a unit is
+// one 128x256 output tile (M tile of one expert x N tile), taken round-robin.
+// Warp roles (15 warps):
 //   warp 0      TMA producer of the activation tile (SWIZZLE_128B, 64 fp16 of
 //               K per row per stage, no multicast);
-//   warp 1      TMEM allocator and the single-thread tcgen05.mma issuer
-//               (kind::f16, M=128 N=256 K=16, fp32 accumulate in TMEM);
-//   warp 2      TMA producer of the raw u4 codes (32 bytes x 256 rows per
-//               k-block) into a 6-deep ring that runs ahead of the MMA;
-//   warps 3..6  dequant producers during the main loop: codes from shared
-//               memory, scales and zero points staged once per tile,
-//               (q - zp) * scale with one fp16 rounding, written in the
-//               canonical SW128 K-major layout; then the epilogue
-//               (tcgen05.ld -> registers -> global).
+//   warp 1      TMEM allocator (2 x 256 columns) and the single-thread
+//               tcgen05.mma issuer (kind::f16, M=128 N=256 K=16, fp32
+//               accumulate); units alternate accumulators;
+//   warp 2      B-side producer: per unit the scales and zero points of its
+//               256 weight rows (contiguous runs, cp.async.bulk, double
+//               buffer), then the raw u4 codes (TMA, 32 bytes x 256 rows per
+//               k-block) into a 6-deep ring;
+//   warps 3-10  dequant, one B-tile row per thread: (q - zp) * scale with one
+//               fp16 rounding, written in the canonical SW128 K-major layout;
+//   warps 11-14 epilogue of the previous unit (tcgen05.ld -> registers ->
+//               global) while the next unit's mainloop runs.
 // The A/B ring has 3 stages (48 KB each); all rings are synchronised with
 // mbarriers; every wait is time-bounded and writes an error word on expiry.
-// Grid: blockIdx.x = N tile (fastest) so the N tiles of one M tile run
-// together and share the activation tile in L2.
-//
+// Buffers that threads read with generic loads and the TMA / bulk-copy engine
+// refills (codes, scales) are released only after fence.proxy.async.
+// GEMM2 stores fp16 contributions (the reference's f16-contribution scatter).
+
 // Operand order: inside each 8-element K chunk both operands hold the
 // elements in the order (0,4,1,5,2,6,3,7) — the natural order of the nibble
 // unpack — so the dequant needs no permute; the gather (activations) and the
@@ -56,15 +61,20 @@ constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
 constexpr int kPfStageBytes = kPfAStage + kPfBStage;
 constexpr int kPfCodeStage = kPfBN * (kPfBK / 2);  // 8 KB of u4 codes
 constexpr int kPfMaxGroups = 16;                   // K <= 2048 with G = 128
+constexpr int kPfScaleBuf = kPfBN * kPfMaxGroups * 2;  // one unit's scales, 8 KB
+constexpr int kPfZpBuf = kPfBN * kPfMaxGroups / 2;     // one unit's zero points, 2 KB
 constexpr int kPfOffCodes = kPfStages * kPfStageBytes;
 constexpr int kPfOffScale = kPfOffCodes + kPfCodeStages * kPfCodeStage;
-constexpr int kPfOffZp = kPfOffScale + kPfBN * kPfMaxGroups * 2;
-constexpr int kPfOffBar = kPfOffZp + kPfBN * kPfMaxGroups;
+constexpr int kPfOffZp = kPfOffScale + 2 * kPfScaleBuf;
+constexpr int kPfOffBar = kPfOffZp + 2 * kPfZpBuf;
 constexpr int kPfSmem = kPfOffBar + 256 + 1024;
-constexpr int kPfThreads = 224;
+constexpr int kPfDqWarps = 8, kPfEpiWarps = 4;
+constexpr int kPfWarpDq0 = 3, kPfWarpEpi0 = kPfWarpDq0 + kPfDqWarps;
+constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 480
+constexpr int kPfDqThreads = kPfDqWarps * 32;                 // one B-tile row each
 constexpr int kPfChunk = 2048;  // assignments per schedule CTA
 constexpr uint32_t kSpinLimit = 1u << 26;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 
 // ---------------------------------------------------------------------------
 // PTX wrappers: mbarrier, TMA, tcgen05
@@ -111,6 +121,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
       "%3}], [%4];\n" ::"r"(dst),
       "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -192,7 +210,7 @@ struct PfWork {
   int32_t* err;
   __half* xp;         // [P + 128, H]
   __half* act;        // [P + 128, I]
-  float* y;           // [P + 128, H]
+  __half* y;          // [P + 128, H] fp16 contributions
 };
 
 __global__ void __launch_bounds__(256) pf_hist_kernel(const int32_t* ids, int P, int E,
@@ -316,7 +334,9 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* x, 
   pdl_launch_dependents();
 }
 
-// out[t][h] = sum_r Y[inv(t,r)][h], ranks in order.
+// out[t][h] = sum_r float(Y[inv(t,r)][h]), ranks in order, fp32 accumulate
+// over fp16 contributions (iq36_scatter_f16_contributions,
+// grouped_s8_u4_f16_contribution_moe.cl:831-845).
 __global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, void* out,
                                                          int out_dtype, PfWork w) {
   pdl_wait();
@@ -326,11 +346,13 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, vo
   for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < k; ++r) {
-      const float4 v = *reinterpret_cast<const float4*>(w.y + (size_t)rows[r] * H + h);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+      const uint2 raw = *reinterpret_cast<const uint2*>(w.y + (size_t)rows[r] * H + h);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      acc.x += a.x;
+      acc.y += a.y;
+      acc.z += b.x;
+      acc.w += b.y;
     }
     if (out_dtype == IQ36_BF16) {
       __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H + h;
@@ -357,153 +379,195 @@ struct GemmArgs {
   PfWork work;
 };
 
+// Work unit u (persistent CTAs take u = blockIdx.x, + gridDim.x, ...):
+// M tile u / nN of the tile table, N tile u % nN, so the N tiles of one M
+// tile (same expert, same activation rows) run side by side.
+struct PfUnit {
+  int row0, rows;
+  int64_t wr0, wr1;  // first weight row of each 128-row half of the B tile
+};
+
+template <int MODE>
+__device__ __forceinline__ PfUnit pf_unit(const GemmArgs& g, int u, int nN) {
+  const int mt = u / nN, nt = u - mt * nN;
+  const int e = g.work.tile_expert[mt];
+  PfUnit r;
+  r.row0 = g.work.tile_row0[mt];
+  r.rows = g.work.tile_rows[mt];
+  if (MODE == 0) {
+    r.wr0 = (int64_t)e * g.exp_rows + nt * 128;  // gate rows
+    r.wr1 = r.wr0 + g.I;                         // the matching up rows
+  } else {
+    r.wr0 = (int64_t)e * g.exp_rows + nt * kPfBN;
+    r.wr1 = r.wr0 + 128;
+  }
+  return r;
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
     pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
-  pdl_wait();
-  const int nt = blockIdx.x, mt = blockIdx.y;
-  if (mt >= *g.work.tile_count) return;  // uniform per CTA
-  const int e = g.work.tile_expert[mt];
-  const int row0 = g.work.tile_row0[mt];
-  const int rows = g.work.tile_rows[mt];
-
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - base_raw);
-  const uint32_t bar_full = base + kPfOffBar;              // kPfStages x 8 B
-  const uint32_t bar_empty = bar_full + kPfStages * 8;     // kPfStages x 8 B
-  const uint32_t bar_cfull = bar_empty + kPfStages * 8;    // kPfCodeStages x 8 B
-  const uint32_t bar_cempty = bar_cfull + kPfCodeStages * 8;
-  const uint32_t bar_acc = bar_cempty + kPfCodeStages * 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPfOffBar + 8 * (2 * kPfStages + 2 * kPfCodeStages + 1));
-  const uint32_t tmem_slot_s = smem_u32(tmem_slot);
-  __half* s_scale = reinterpret_cast<__half*>(smem + kPfOffScale);  // [256][16]
-  uint8_t* s_zp = smem + kPfOffZp;                                   // [256][16]
-
-  // weight rows of this tile: two 128-row halves
-  int64_t wrow0, wrow1;
-  if (MODE == 0) {
-    wrow0 = (int64_t)e * g.exp_rows + nt * 128;           // gate rows
-    wrow1 = (int64_t)e * g.exp_rows + g.I + nt * 128;     // matching up rows
-  } else {
-    wrow0 = (int64_t)e * g.exp_rows + nt * kPfBN;
-    wrow1 = wrow0 + 128;
-  }
-
+  const uint32_t bar_full = base + kPfOffBar;                  // [kPfStages]
+  const uint32_t bar_empty = bar_full + 8 * kPfStages;         // [kPfStages]
+  const uint32_t bar_cfull = bar_empty + 8 * kPfStages;        // [kPfCodeStages]
+  const uint32_t bar_cempty = bar_cfull + 8 * kPfCodeStages;   // [kPfCodeStages]
+  const uint32_t bar_sfull = bar_cempty + 8 * kPfCodeStages;   // [2]
+  const uint32_t bar_sempty = bar_sfull + 16;                  // [2]
+  const uint32_t bar_accf = bar_sempty + 16;                   // [2]
+  const uint32_t bar_acce = bar_accf + 16;                     // [2]
+  const uint32_t bar_done = bar_acce + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_done + 8 - base));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(bar_full + 8 * s, 1 + 128);  // A producer (with tx) + 128 dequant threads
-      mbar_init(bar_empty + 8 * s, 1);       // tcgen05.commit
+      mbar_init(bar_full + 8 * s, 1 + kPfDqThreads);  // A producer (with tx) + dequant threads
+      mbar_init(bar_empty + 8 * s, 1);                // tcgen05.commit
     }
     for (int s = 0; s < kPfCodeStages; ++s) {
-      mbar_init(bar_cfull + 8 * s, 1);       // code producer (with tx)
-      mbar_init(bar_cempty + 8 * s, 128);    // dequant threads
+      mbar_init(bar_cfull + 8 * s, 1);                // code producer (with tx)
+      mbar_init(bar_cempty + 8 * s, kPfDqThreads);
     }
-    mbar_init(bar_acc, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_sfull + 8 * b, 1);                // scale / zp producer (with tx)
+      mbar_init(bar_sempty + 8 * b, kPfDqThreads);
+      mbar_init(bar_accf + 8 * b, 1);                 // tcgen05.commit
+      mbar_init(bar_acce + 8 * b, kPfEpiWarps * 32);  // epilogue threads
+    }
+    mbar_init(bar_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot_s, kTmemCols);
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the tile table and both operands come from earlier launches
+  const int nN = MODE == 0 ? g.I / 128 : g.H / kPfBN;
+  const int total = *g.work.tile_count * nN;
   const int nkb = g.K / kPfBK;
+  const int ng = g.K / 128;
   bool ok = true;
 
   if (warp == 0) {
-    // ---- activation producer (TMA) ----
+    // ---- activation producer (TMA, SWIZZLE_128B) ----
     if (lane == 0) {
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int s = kb % kPfStages;
-        const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
-        ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
-        if (!ok) break;
-        mbar_arrive_tx(bar_full + 8 * s, kPfAStage);
-        tma_load_2d(base + s * kPfStageBytes, &tmA, kb * kPfBK, row0, bar_full + 8 * s);
+      int it = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int row0 = g.work.tile_row0[u / nN];
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPfStages;
+          ok = mbar_wait(bar_empty + 8 * s, ((it / kPfStages) & 1) ^ 1u);
+          if (!ok) break;
+          mbar_arrive_tx(bar_full + 8 * s, kPfAStage);
+          tma_load_2d(base + s * kPfStageBytes, &tmA, kb * kPfBK, row0, bar_full + 8 * s);
+        }
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer: one thread, accumulators alternate between two
+    // 256-column TMEM buffers so the epilogue of a unit overlaps the next ----
     if (lane == 0) {
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int s = kb % kPfStages;
-        const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
-        ok = mbar_wait(bar_full + 8 * s, ph);
+      int it = 0, i = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
+        const int a = i & 1;
+        ok = mbar_wait(bar_acce + 8 * a, ((i >> 1) & 1) ^ 1u);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a_s = base + s * kPfStageBytes;
-        const uint32_t b_s = a_s + kPfAStage;
+        const uint32_t acc = tmem + (uint32_t)(a * kPfBN);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPfStages;
+          ok = mbar_wait(bar_full + 8 * s, (it / kPfStages) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_s = base + s * kPfStageBytes;
+          const uint32_t b_s = a_s + kPfAStage;
 #pragma unroll
-        for (int kk = 0; kk < kPfBK / 16; ++kk)
-          umma_f16(tmem, sw128_desc(a_s + kk * 32), sw128_desc(b_s + kk * 32), kIdesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar_empty + 8 * s);  // stage free once these MMAs complete
+          for (int kk = 0; kk < kPfBK / 16; ++kk)
+            umma_f16(acc, sw128_desc(a_s + kk * 32), sw128_desc(b_s + kk * 32), kIdesc,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar_empty + 8 * s);  // stage free once these MMAs complete
+        }
+        if (ok) umma_commit(bar_accf + 8 * a);  // accumulator complete
       }
-      umma_commit(bar_acc);  // accumulator complete
+      // every MMA issued above has completed before the teardown
+      umma_commit(bar_done);
+      if (!mbar_wait(bar_done, 0)) ok = false;
     }
   } else if (warp == 2) {
-    // ---- raw u4 code producer (TMA), runs up to 6 k-blocks ahead ----
+    // ---- B-side producer: each unit's scales and zero points (bulk copies,
+    // double-buffered), then its raw u4 codes (TMA, 6-deep ring) ----
     if (lane == 0) {
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int cs = kb % kPfCodeStages;
-        const uint32_t ph = (uint32_t)((kb / kPfCodeStages) & 1);
-        ok = mbar_wait(bar_cempty + 8 * cs, ph ^ 1u);
+      const uint32_t sbytes = 128u * ng * 2u, zbytes = 128u * ng / 2u;
+      int it = 0, i = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
+        const PfUnit un = pf_unit<MODE>(g, u, nN);
+        const int b = i & 1;
+        ok = mbar_wait(bar_sempty + 8 * b, ((i >> 1) & 1) ^ 1u);
         if (!ok) break;
-        const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
-        mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
-        tma_load_2d(dst, &tmW, kb * (kPfBK / 2), (int)wrow0, bar_cfull + 8 * cs);
-        tma_load_2d(dst + kPfCodeStage / 2, &tmW, kb * (kPfBK / 2), (int)wrow1,
-                    bar_cfull + 8 * cs);
+        const uint32_t sdst = base + kPfOffScale + b * kPfScaleBuf;
+        const uint32_t zdst = base + kPfOffZp + b * kPfZpBuf;
+        mbar_arrive_tx(bar_sfull + 8 * b, 2u * (sbytes + zbytes));
+        bulk_load(sdst, g.s + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
+        bulk_load(sdst + sbytes, g.s + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
+        bulk_load(zdst, g.z + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
+        bulk_load(zdst + zbytes, g.z + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int cs = it % kPfCodeStages;
+          ok = mbar_wait(bar_cempty + 8 * cs, ((it / kPfCodeStages) & 1) ^ 1u);
+          if (!ok) break;
+          const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
+          mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
+          tma_load_2d(dst, &tmW, kb * (kPfBK / 2), (int)un.wr0, bar_cfull + 8 * cs);
+          tma_load_2d(dst + kPfCodeStage / 2, &tmW, kb * (kPfBK / 2), (int)un.wr1,
+                      bar_cfull + 8 * cs);
+        }
       }
     }
-  } else {
-    // ---- dequant producers (128 threads), tile rows p and p + 128 ----
-    const int p = threadIdx.x - 96;
-    const int ng = g.K / 128;
-    for (int h = 0; h < 2; ++h) {  // scales / zero points of this thread's rows, once per tile
-      const int64_t er = (h == 0 ? wrow0 : wrow1) + p;
-      const int n = p + 128 * h;
-      for (int grp = 0; grp < ng; ++grp) {
-        s_scale[n * kPfMaxGroups + grp] = g.s[er * ng + grp];
-        const int64_t ze = er * ng + grp;
-        s_zp[n * kPfMaxGroups + grp] = (uint8_t)((__ldg(g.z + (ze >> 1)) >> ((ze & 1) * 4)) & 15u);
-      }
-    }
+  } else if (warp < kPfWarpEpi0) {
+    // ---- dequant: thread n owns row n of the 256-row B tile ----
+    const int n = threadIdx.x - kPfWarpDq0 * 32;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
-    for (int kb = 0; kb < nkb && ok; ++kb) {
-      const int s = kb % kPfStages;
-      const uint32_t ph = (uint32_t)((kb / kPfStages) & 1);
-      const int cs = kb % kPfCodeStages;
-      const uint32_t cph = (uint32_t)((kb / kPfCodeStages) & 1);
-      ok = mbar_wait(bar_cfull + 8 * cs, cph);
+    int it = 0, i = 0;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
+      const int b = i & 1;
+      ok = mbar_wait(bar_sfull + 8 * b, (i >> 1) & 1);
       if (!ok) break;
-      uint4 v[2][2];
-      const uint8_t* cst = smem + kPfOffCodes + cs * kPfCodeStage;
-      for (int h = 0; h < 2; ++h) {
-        const int n = p + 128 * h;
-        v[h][0] = *reinterpret_cast<const uint4*>(cst + n * 32);
-        v[h][1] = *reinterpret_cast<const uint4*>(cst + n * 32 + 16);
-      }
-      mbar_arrive(bar_cempty + 8 * cs);  // codes are in registers: release the slot
-      ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
-      if (!ok) break;
-      uint8_t* bst = smem + s * kPfStageBytes + kPfAStage;
-      const int grp = kb >> 1;
-      for (int h = 0; h < 2; ++h) {
-        const int n = p + 128 * h;
-        const __half sc = s_scale[n * kPfMaxGroups + grp];
+      // rows 0..127 then 128..255 are consecutive in both buffers
+      const __half* ssc =
+          reinterpret_cast<const __half*>(smem + kPfOffScale + b * kPfScaleBuf) + n * ng;
+      const uint8_t* szp = smem + kPfOffZp + b * kPfZpBuf + n * ng / 2;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % kPfStages, cs = it % kPfCodeStages;
+        ok = mbar_wait(bar_cfull + 8 * cs, (it / kPfCodeStages) & 1);
+        if (!ok) break;
+        const uint8_t* cst = smem + kPfOffCodes + cs * kPfCodeStage + n * 32;
+        uint4 v[2];
+        v[0] = *reinterpret_cast<const uint4*>(cst);
+        v[1] = *reinterpret_cast<const uint4*>(cst + 16);
+        // The next TMA into this slot is an async-proxy write: without the
+        // proxy fence it can land before these generic reads (observed as
+        // corrupted rows once units pipeline back to back).
+        fence_proxy_async_smem();
+        mbar_arrive(bar_cempty + 8 * cs);  // codes are in registers: release the slot
+        ok = mbar_wait(bar_empty + 8 * s, ((it / kPfStages) & 1) ^ 1u);
+        if (!ok) break;
+        uint8_t* bst = smem + s * kPfStageBytes + kPfAStage + n * 128;
+        const int grp = kb >> 1;
+        const __half sc = ssc[grp];
         const __half2 s2 = __halves2half2(sc, sc);
         const __half2 s16 = __hmul2(s2, sixteenth);
-        const uint32_t zz = s_zp[n * kPfMaxGroups + grp];
+        const uint32_t zz = (uint32_t)(szp[grp >> 1] >> ((grp & 1) * 4)) & 15u;
         const uint32_t zlo = 0x64006400u | zz | (zz << 16);
         const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
-        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[h][0]);
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[0]);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t wd = wv[c];
@@ -521,20 +585,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           o.y = *reinterpret_cast<uint32_t*>(&r1);
           o.z = *reinterpret_cast<uint32_t*>(&r2);
           o.w = *reinterpret_cast<uint32_t*>(&r3);
-          *reinterpret_cast<uint4*>(bst + n * 128 + ((c ^ (n & 7)) << 4)) = o;
+          *reinterpret_cast<uint4*>(bst + ((c ^ (n & 7)) << 4)) = o;
         }
+        fence_proxy_async_smem();
+        mbar_arrive(bar_full + 8 * s);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(bar_full + 8 * s);
+      if (ok) {
+        fence_proxy_async_smem();  // generic reads before the next bulk copy into the buffer
+        mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales
+      }
     }
-
-    // ---- epilogue: TMEM -> registers -> global ----
-    if (ok) ok = mbar_wait(bar_acc, 0);
-    tc_fence_after();
-    const int sp = warp & 3;            // TMEM sub-partition of this warp
-    const int m = sp * 32 + lane;       // tile row = TMEM lane
-    const uint32_t tl = tmem + ((uint32_t)(sp * 32) << 16);
-    if (ok) {
+  } else {
+    // ---- epilogue: TMEM -> registers -> global, one tile row per thread ----
+    const int sp = warp & 3;       // TMEM sub-partition of this warp
+    const int m = sp * 32 + lane;  // tile row = TMEM lane
+    int i = 0;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
+      const int a = i & 1;
+      // warp-uniform: the TMEM loads below are warp-collective
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_accf + 8 * a, (i >> 1) & 1));
+      if (!ok) break;
+      tc_fence_after();
+      const int mt = u / nN, nt = u - mt * nN;
+      const int row0 = g.work.tile_row0[mt], rows = g.work.tile_rows[mt];
+      const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
       if (MODE == 0) {
         for (int j = 0; j < 128; j += 32) {
           uint32_t gv[32], uv[32];
@@ -568,18 +642,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tmem_ld32(tl + j, yv);
           tmem_ld_wait();
           if (m < rows) {
-            float* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
+            __half* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 o = make_float4(__uint_as_float(yv[4 * q]) * wt,
-                                     __uint_as_float(yv[4 * q + 1]) * wt,
-                                     __uint_as_float(yv[4 * q + 2]) * wt,
-                                     __uint_as_float(yv[4 * q + 3]) * wt);
-              *reinterpret_cast<float4*>(dst + 4 * q) = o;
+            for (int q = 0; q < 4; ++q) {
+              uint4 o;
+              o.x = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q]) * wt),
+                               __float2half_rn(__uint_as_float(yv[8 * q + 1]) * wt));
+              o.y = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 2]) * wt),
+                               __float2half_rn(__uint_as_float(yv[8 * q + 3]) * wt));
+              o.z = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 4]) * wt),
+                               __float2half_rn(__uint_as_float(yv[8 * q + 5]) * wt));
+              o.w = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 6]) * wt),
+                               __float2half_rn(__uint_as_float(yv[8 * q + 7]) * wt));
+              *reinterpret_cast<uint4*>(dst + 8 * q) = o;
             }
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(bar_acce + 8 * a);  // this accumulator may be overwritten
     }
   }
   if (!ok) atomicExch(g.work.err, 1);
@@ -621,7 +702,7 @@ static PfLayout pf_layout(int T, int k, int E, int H, int I) {
   L.err = o; o += 256;
   L.xp = o; o += up256((P + kPfBM) * (size_t)H * 2);
   L.act = o; o += up256((P + kPfBM) * (size_t)I * 2);
-  L.y = o; o += up256((P + kPfBM) * (size_t)H * 4);
+  L.y = o; o += up256((P + kPfBM) * (size_t)H * 2);
   L.total = o;
   return L;
 }
@@ -683,7 +764,8 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
     return IQ36_ERR_SHAPE;
   if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16) return IQ36_ERR_ARG;
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(b->gate_up_weight, 16) ||
-      !aligned(b->down_weight, 16))
+      !aligned(b->down_weight, 16) || !aligned(b->gate_up_scale, 16) ||
+      !aligned(b->down_scale, 16) || !aligned(b->gate_up_zp, 16) || !aligned(b->down_zp, 16))
     return IQ36_ERR_ALIGN;
   const PfLayout L = pf_layout(T, k, E, H, I);
   if (!ws || ws_bytes < L.total) return IQ36_ERR_WORKSPACE;
@@ -703,7 +785,7 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   w.err = reinterpret_cast<int32_t*>(base + L.err);
   w.xp = reinterpret_cast<__half*>(base + L.xp);
   w.act = reinterpret_cast<__half*>(base + L.act);
-  w.y = reinterpret_cast<float*>(base + L.y);
+  w.y = reinterpret_cast<__half*>(base + L.y);
   const int P = T * k;
   const int nC = (P + kPfChunk - 1) / kPfChunk;
   const int maxt = (P + kPfBM - 1) / kPfBM + E;
@@ -736,13 +818,19 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
                reinterpret_cast<const __nv_bfloat16*>(x), P, H, w);
   GemmArgs g1{reinterpret_cast<const __half*>(b->gate_up_scale), b->gate_up_zp, (int64_t)2 * I,
               H, I, H, w};
+  // persistent grids: at most one CTA per SM, never more than the units
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  const int grid1 = std::max(1, std::min(sms, maxt * (I / 128)));
+  const int grid2 = std::max(1, std::min(sms, maxt * (H / kPfBN)));
   if (e == cudaSuccess)
-    e = launch(pf_gemm_kernel<0>, dim3(I / 128, maxt), dim3(kPfThreads), (size_t)kPfSmem, stream,
+    e = launch(pf_gemm_kernel<0>, dim3(grid1), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_x, map_gu, g1);
   GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
   if (e == cudaSuccess)
-    e = launch(pf_gemm_kernel<1>, dim3(H / kPfBN, maxt), dim3(kPfThreads), (size_t)kPfSmem,
-               stream, map_act, map_d, g2);
+    e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
+               map_act, map_d, g2);
   if (e == cudaSuccess)
     e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, T, H, k, out, out_dtype, w);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;

@@ -211,6 +211,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       if (__all_sync(0xffffffffu, ring_wait(seq, sbase + L.full + 8 * s, s, c, geo.stages))) {
         chunk_dot_range<G>(geo, smem + L.ring + s * geo.stage_bytes, xs, xc, lane, gb, ge, accA,
                            accB);
+        // generic reads of the stage before the producer's next bulk copy
+        // (async proxy) into it
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         __syncwarp();
         if (lane == 0) sm_mbar_arrive(sbase + L.empty + 8 * s);
       } else if (lane == 0) {
