@@ -1,6 +1,6 @@
 """Expert-parallel grouped MoE prefill across ranks (one process per GPU).
 
-No counterpart in the reference (it runs on one Intel iGPU, SURVEY 2.4); this
+No counterpart in the reference (it runs on one Intel iGPU); this
 is the north star's expert-parallel prefill. Rank r owns the contiguous
 experts [r*E/P, (r+1)*E/P) and its own token shard. Per call:
 

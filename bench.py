@@ -40,7 +40,7 @@ for p in (str(ROOT), str(PKG)):
 
 BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
-PUBLISHED_DECODE_4K = 50.57  # Arc B390, 4k prompt, batch-1 decode tok/s
+PUBLISHED_DECODE_4K = 50.57  # reference's published figure: Arc B390, 4k prompt, batch-1 decode tok/s
 
 
 def peaks() -> tuple[float, str]:

@@ -2,7 +2,7 @@
 // synthetic Qwen3.6-35B-A3B-shaped model.
 //
 // TEST INFRASTRUCTURE ONLY (see iq36_oracle.cpp). Composes the per-op
-// restatements in the order of the reference graph (SURVEY call stack; per
+// restatements in the order of the reference graph (its call stack; per
 // layer: RMSNorm -> attention or DeltaNet -> residual -> RMSNorm -> router +
 // routed/shared experts -> residual; then final RMSNorm -> LM head -> greedy),
 // following gguf_loader.cpp run_qwen36_layer_with_external_attention_state
