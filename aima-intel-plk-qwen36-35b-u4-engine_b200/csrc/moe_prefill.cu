@@ -19,21 +19,23 @@
 //
 // GEMM kernel: persistent, one CTA per SM (grid min(148, units)); a unit is
 // one 128x256 output tile (M tile of one expert x N tile), taken round-robin.
-// Warp roles (15 warps):
+// Warp roles (23 warps):
 //   warp 0      TMA producer of the activation tile (SWIZZLE_128B, 64 fp16 of
-//               K per row per stage, no multicast);
+//               K per row per stage, no multicast) into its own 3-deep ring,
+//               so activation fetches run ahead of the dequantised B tiles;
 //   warp 1      TMEM allocator (2 x 256 columns) and the single-thread
 //               tcgen05.mma issuer (kind::f16, M=128 N=256 K=16, fp32
 //               accumulate); units alternate accumulators;
 //   warp 2      B-side producer: per unit the scales and zero points of its
 //               256 weight rows (contiguous runs, cp.async.bulk, double
-//               buffer), then the raw u4 codes (TMA, 32 bytes x 256 rows per
-//               k-block) into a 6-deep ring;
-//   warps 3-10  dequant, one B-tile row per thread: (q - zp) * scale with one
-//               fp16 rounding, written in the canonical SW128 K-major layout;
-//   warps 11-14 epilogue of the previous unit (tcgen05.ld -> registers ->
+//               buffer), then the raw u4 codes (TMA, 64 bytes x 256 rows per
+//               two k-blocks) into a 3-deep ring;
+//   warps 3-18  dequant, half a B-tile row per thread: (q - zp) * scale with
+//               one fp16 rounding, written in the canonical SW128 K-major
+//               layout;
+//   warps 19-22 epilogue of the previous unit (tcgen05.ld -> registers ->
 //               global) while the next unit's mainloop runs.
-// The A/B ring has 3 stages (48 KB each); all rings are synchronised with
+// A ring 3 x 16 KB, B ring 3 x 32 KB, code ring 3 x 16 KB; all rings are synchronised with
 // mbarriers; every wait is time-bounded and writes an error word on expiry.
 // Buffers that threads read with generic loads and the TMA / bulk-copy engine
 // refills (codes, scales) are released only after fence.proxy.async.
@@ -55,23 +57,29 @@
 
 namespace iq36 {
 
-constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64, kPfStages = 3, kPfCodeStages = 6;
+constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64;
+constexpr int kPfAStages = 3, kPfBStages = 3, kPfCodeStages = 3;
+// A code stage holds kPfCodeKB k-blocks of u4 codes for the 256 B-tile rows:
+// TMA rows of 64 bytes (two k-blocks) halve the row requests of 32-byte rows,
+// and the TMA engine's row-request rate, not bytes, bounded the GEMMs.
+constexpr int kPfCodeKB = 2;
+constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;  // 64 bytes per row
 constexpr int kPfAStage = kPfBM * kPfBK * 2;  // 16 KB
 constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
-constexpr int kPfStageBytes = kPfAStage + kPfBStage;
-constexpr int kPfCodeStage = kPfBN * (kPfBK / 2);  // 8 KB of u4 codes
+constexpr int kPfCodeStage = kPfBN * kPfCodeRow;  // 16 KB of u4 codes
 constexpr int kPfMaxGroups = 16;                   // K <= 2048 with G = 128
 constexpr int kPfScaleBuf = kPfBN * kPfMaxGroups * 2;  // one unit's scales, 8 KB
 constexpr int kPfZpBuf = kPfBN * kPfMaxGroups / 2;     // one unit's zero points, 2 KB
-constexpr int kPfOffCodes = kPfStages * kPfStageBytes;
+constexpr int kPfOffB = kPfAStages * kPfAStage;  // B ring after the A ring
+constexpr int kPfOffCodes = kPfOffB + kPfBStages * kPfBStage;
 constexpr int kPfOffScale = kPfOffCodes + kPfCodeStages * kPfCodeStage;
 constexpr int kPfOffZp = kPfOffScale + 2 * kPfScaleBuf;
 constexpr int kPfOffBar = kPfOffZp + 2 * kPfZpBuf;
 constexpr int kPfSmem = kPfOffBar + 256 + 1024;
-constexpr int kPfDqWarps = 8, kPfEpiWarps = 4;
+constexpr int kPfDqWarps = 16, kPfEpiWarps = 4;
 constexpr int kPfWarpDq0 = 3, kPfWarpEpi0 = kPfWarpDq0 + kPfDqWarps;
-constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 480
-constexpr int kPfDqThreads = kPfDqWarps * 32;                 // one B-tile row each
+constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 736
+constexpr int kPfDqThreads = kPfDqWarps * 32;                 // half a B-tile row each
 constexpr int kPfChunk = 2048;  // assignments per schedule CTA
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
@@ -163,15 +171,13 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];\n"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() {
@@ -412,9 +418,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - base_raw);
-  const uint32_t bar_full = base + kPfOffBar;                  // [kPfStages]
-  const uint32_t bar_empty = bar_full + 8 * kPfStages;         // [kPfStages]
-  const uint32_t bar_cfull = bar_empty + 8 * kPfStages;        // [kPfCodeStages]
+  const uint32_t bar_afull = base + kPfOffBar;                 // [kPfAStages]
+  const uint32_t bar_aempty = bar_afull + 8 * kPfAStages;      // [kPfAStages]
+  const uint32_t bar_full = bar_aempty + 8 * kPfAStages;       // B stages [kPfBStages]
+  const uint32_t bar_empty = bar_full + 8 * kPfBStages;        // [kPfBStages]
+  const uint32_t bar_cfull = bar_empty + 8 * kPfBStages;       // [kPfCodeStages]
   const uint32_t bar_cempty = bar_cfull + 8 * kPfCodeStages;   // [kPfCodeStages]
   const uint32_t bar_sfull = bar_cempty + 8 * kPfCodeStages;   // [2]
   const uint32_t bar_sempty = bar_sfull + 16;                  // [2]
@@ -424,8 +432,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_done + 8 - base));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(bar_full + 8 * s, 1 + kPfDqThreads);  // A producer (with tx) + dequant threads
+    for (int s = 0; s < kPfAStages; ++s) {
+      mbar_init(bar_afull + 8 * s, 1);                // A producer (with tx)
+      mbar_init(bar_aempty + 8 * s, 1);               // tcgen05.commit
+    }
+    for (int s = 0; s < kPfBStages; ++s) {
+      mbar_init(bar_full + 8 * s, kPfDqThreads);      // dequant threads
       mbar_init(bar_empty + 8 * s, 1);                // tcgen05.commit
     }
     for (int s = 0; s < kPfCodeStages; ++s) {
@@ -463,11 +475,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const int row0 = g.work.tile_row0[u / nN];
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kPfStages;
-          ok = mbar_wait(bar_empty + 8 * s, ((it / kPfStages) & 1) ^ 1u);
+          const int s = it % kPfAStages;
+          ok = mbar_wait(bar_aempty + 8 * s, ((it / kPfAStages) & 1) ^ 1u);
           if (!ok) break;
-          mbar_arrive_tx(bar_full + 8 * s, kPfAStage);
-          tma_load_2d(base + s * kPfStageBytes, &tmA, kb * kPfBK, row0, bar_full + 8 * s);
+          mbar_arrive_tx(bar_afull + 8 * s, kPfAStage);
+          tma_load_2d(base + s * kPfAStage, &tmA, kb * kPfBK, row0, bar_afull + 8 * s);
         }
       }
     }
@@ -483,17 +495,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(a * kPfBN);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kPfStages;
-          ok = mbar_wait(bar_full + 8 * s, (it / kPfStages) & 1);
+          const int sa = it % kPfAStages, s = it % kPfBStages;
+          ok = mbar_wait(bar_afull + 8 * sa, (it / kPfAStages) & 1) &&
+               mbar_wait(bar_full + 8 * s, (it / kPfBStages) & 1);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t a_s = base + s * kPfStageBytes;
-          const uint32_t b_s = a_s + kPfAStage;
+          const uint32_t a_s = base + sa * kPfAStage;
+          const uint32_t b_s = base + kPfOffB + s * kPfBStage;
 #pragma unroll
           for (int kk = 0; kk < kPfBK / 16; ++kk)
             umma_f16(acc, sw128_desc(a_s + kk * 32), sw128_desc(b_s + kk * 32), kIdesc,
                      (kb > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(bar_empty + 8 * s);  // stage free once these MMAs complete
+          umma_commit(bar_aempty + 8 * sa);  // stages free once these MMAs complete
+          umma_commit(bar_empty + 8 * s);
         }
         if (ok) umma_commit(bar_accf + 8 * a);  // accumulator complete
       }
@@ -519,21 +533,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         bulk_load(sdst + sbytes, g.s + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
         bulk_load(zdst, g.z + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
         bulk_load(zdst + zbytes, g.z + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        // nkb is a multiple of kPfCodeKB, so code blocks never straddle units
+        for (int cb = 0; cb < nkb / kPfCodeKB; ++cb, ++it) {
           const int cs = it % kPfCodeStages;
           ok = mbar_wait(bar_cempty + 8 * cs, ((it / kPfCodeStages) & 1) ^ 1u);
           if (!ok) break;
           const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
           mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
-          tma_load_2d(dst, &tmW, kb * (kPfBK / 2), (int)un.wr0, bar_cfull + 8 * cs);
-          tma_load_2d(dst + kPfCodeStage / 2, &tmW, kb * (kPfBK / 2), (int)un.wr1,
+          tma_load_2d(dst, &tmW, cb * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
+          tma_load_2d(dst + kPfCodeStage / 2, &tmW, cb * kPfCodeRow, (int)un.wr1,
                       bar_cfull + 8 * cs);
         }
       }
     }
   } else if (warp < kPfWarpEpi0) {
-    // ---- dequant: thread n owns row n of the 256-row B tile ----
-    const int n = threadIdx.x - kPfWarpDq0 * 32;
+    // ---- dequant: thread pair (2n, 2n+1) owns row n of the 256-row B tile,
+    // k 0..31 and 32..63 of each k-block ----
+    const int dt = threadIdx.x - kPfWarpDq0 * 32;
+    const int n = dt >> 1, hk = dt & 1;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
     int it = 0, i = 0;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
@@ -545,21 +562,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           reinterpret_cast<const __half*>(smem + kPfOffScale + b * kPfScaleBuf) + n * ng;
       const uint8_t* szp = smem + kPfOffZp + b * kPfZpBuf + n * ng / 2;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % kPfStages, cs = it % kPfCodeStages;
-        ok = mbar_wait(bar_cfull + 8 * cs, (it / kPfCodeStages) & 1);
+        const int s = it % kPfBStages;
+        const int ic = it / kPfCodeKB, cs = ic % kPfCodeStages, sub = it % kPfCodeKB;
+        ok = mbar_wait(bar_cfull + 8 * cs, (ic / kPfCodeStages) & 1);
         if (!ok) break;
-        const uint8_t* cst = smem + kPfOffCodes + cs * kPfCodeStage + n * 32;
-        uint4 v[2];
-        v[0] = *reinterpret_cast<const uint4*>(cst);
-        v[1] = *reinterpret_cast<const uint4*>(cst + 16);
-        // The next TMA into this slot is an async-proxy write: without the
-        // proxy fence it can land before these generic reads (observed as
-        // corrupted rows once units pipeline back to back).
-        fence_proxy_async_smem();
-        mbar_arrive(bar_cempty + 8 * cs);  // codes are in registers: release the slot
-        ok = mbar_wait(bar_empty + 8 * s, ((it / kPfStages) & 1) ^ 1u);
+        const uint4 v = *reinterpret_cast<const uint4*>(smem + kPfOffCodes + cs * kPfCodeStage +
+                                                        n * kPfCodeRow + sub * 32 + hk * 16);
+        ok = mbar_wait(bar_empty + 8 * s, ((it / kPfBStages) & 1) ^ 1u);
         if (!ok) break;
-        uint8_t* bst = smem + s * kPfStageBytes + kPfAStage + n * 128;
+        uint8_t* bst = smem + kPfOffB + s * kPfBStage + n * 128;
         const int grp = kb >> 1;
         const __half sc = ssc[grp];
         const __half2 s2 = __halves2half2(sc, sc);
@@ -567,10 +578,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t zz = (uint32_t)(szp[grp >> 1] >> ((grp & 1) * 4)) & 15u;
         const uint32_t zlo = 0x64006400u | zz | (zz << 16);
         const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
-        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[0]);
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t wd = wv[c];
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = hk * 4 + cc;  // 16-byte chunk of the 128-byte B row
+          uint32_t wd = wv[cc];
           uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
           uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
           wd >>= 8;
@@ -587,13 +599,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           o.w = *reinterpret_cast<uint32_t*>(&r3);
           *reinterpret_cast<uint4*>(bst + ((c ^ (n & 7)) << 4)) = o;
         }
+        // One proxy fence orders this k-block's generic accesses against the
+        // async proxy both ways: the B-tile stores before the MMA reads them,
+        // and the code / scale loads before the next TMA or bulk copy
+        // overwrites their slot (without it such a write was observed to
+        // land first, corrupting rows once units ran back to back).
         fence_proxy_async_smem();
+        if (sub == kPfCodeKB - 1) mbar_arrive(bar_cempty + 8 * cs);  // release the code slot
         mbar_arrive(bar_full + 8 * s);
       }
-      if (ok) {
-        fence_proxy_async_smem();  // generic reads before the next bulk copy into the buffer
-        mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales
-      }
+      if (ok) mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales (fenced above)
     }
   } else {
     // ---- epilogue: TMEM -> registers -> global, one tile row per thread ----
@@ -610,15 +625,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int row0 = g.work.tile_row0[mt], rows = g.work.tile_rows[mt];
       const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
       if (MODE == 0) {
-        for (int j = 0; j < 128; j += 32) {
-          uint32_t gv[32], uv[32];
-          tmem_ld32(tl + j, gv);
-          tmem_ld32(tl + 128 + j, uv);
+        for (int j = 0; j < 128; j += 16) {
+          uint32_t gv[16], uv[16];
+          tmem_ld16(tl + j, gv);
+          tmem_ld16(tl + 128 + j, uv);
           tmem_ld_wait();
           if (m < rows) {
             __half* dst = g.work.act + (size_t)(row0 + m) * g.I + nt * 128 + j;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 2; ++q) {
               __half a8[8];
 #pragma unroll
               for (int c = 0; c < 8; ++c) {
@@ -637,14 +652,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       } else {
         const float wt = m < rows ? g.work.perm_w[row0 + m] : 0.f;
-        for (int j = 0; j < kPfBN; j += 32) {
-          uint32_t yv[32];
-          tmem_ld32(tl + j, yv);
+        for (int j = 0; j < kPfBN; j += 16) {
+          uint32_t yv[16];
+          tmem_ld16(tl + j, yv);
           tmem_ld_wait();
           if (m < rows) {
             __half* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < 2; ++q) {
               uint4 o;
               o.x = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q]) * wt),
                                __float2half_rn(__uint_as_float(yv[8 * q + 1]) * wt));
@@ -735,13 +750,13 @@ static bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 2-D u8 code tensor [rows, bytes_per_row], box 32 bytes x 128 rows, no swizzle.
+// 2-D u8 code tensor [rows, bytes_per_row], box 64 bytes x 128 rows, no swizzle.
 static bool make_code_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t row_bytes) {
   auto enc = get_encode();
   if (!enc) return false;
   const cuuint64_t dims[2] = {row_bytes, rows};
   const cuuint64_t strides[1] = {row_bytes};
-  const cuuint32_t box[2] = {(cuuint32_t)(kPfBK / 2), 128u};
+  const cuuint32_t box[2] = {(cuuint32_t)kPfCodeRow, 128u};
   const cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
