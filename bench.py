@@ -18,6 +18,10 @@ cpu_baseline = the CPU restatement (oracle/) on a bounded sample.
 OpenVINO is not installable here) on the host cores, same metric.
 Multi-GPU: replicas only (each rank decodes its own sequence; no collective on
 the data path), value summed over ranks.
+
+Other workloads: --workload moe_prefill (grouped MoE
+prefill; expert-parallel over NCCL at --gpus > 1) and --workload gemv
+(one u4 GEMV per step, --rows / --k for other shapes).
 """
 
 from __future__ import annotations
@@ -111,7 +115,7 @@ def dist_setup():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device(f"cuda:{local}"))
     return world, rank, local
 
@@ -463,9 +467,126 @@ def run_moe_prefill(args, world, rank, local) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_gemv(args, world, rank, local) -> None:
+    """BASELINE config 0 (default 1024 x 2048) or any --rows x --k shape: one
+    u4 g128 GEMV per step (fp16 x ~N(0,1), fp32 out) through iq36_u4_gemv.
+    Weights rotate through a pool of copies larger than twice the L2, so every
+    step reads its weights from HBM. Value: algorithmic GB/s (codes + scales +
+    zero points + x + out) over all ranks; roofline: the same per GPU against
+    the measured HBM copy bandwidth."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    from engine import _native as N
+    from engine import ops
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    rows, K, G = args.rows, args.k, 128
+    one = rows * K // 2 + rows * (K // G) * 2 + rows * (K // G) // 2
+    step_bytes = one + K * 2 + rows * 4
+    copies = max(2, math.ceil(2 * 126e6 / one))
+    pool = []
+    for c in range(copies):
+        w = torch.empty(rows, K // 2, dtype=torch.uint8, device=dev)
+        sc = torch.empty(rows, K // G, dtype=torch.float16, device=dev)
+        z = torch.empty(rows * (K // G) // 2, dtype=torch.uint8, device=dev)
+        ops.synth_fill(w, 0, 11, 3 * c + 1, 0, 0)
+        ops.synth_fill(sc, 1, 11, 3 * c + 2, 0.005, 0.02)
+        ops.synth_fill(z, 0, 11, 3 * c + 3, 0, 0)
+        pool.append(ops.U4Weight(w, sc, z, G))
+    gen = torch.Generator().manual_seed(rank)
+    x_host = torch.randn(K, generator=gen).to(torch.float16).pin_memory()
+    x = x_host.to(dev)
+    out = torch.empty(rows, dtype=torch.float32, device=dev)
+    out_host = torch.empty(rows, dtype=torch.float32).pin_memory()
+    mats = [N.U4Matrix(wt.weight.data_ptr(), wt.scale.data_ptr(), wt.zp.data_ptr(), rows)
+            for wt in pool]
+    stream = torch.cuda.current_stream(dev)
+
+    def call(i):
+        N.call("iq36_u4_gemv", x.data_ptr(), K, G, ctypes.byref(mats[i % copies]),
+               out.data_ptr(), 0, stream.cuda_stream)
+
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize(dev)
+    if args.profile_step:
+        torch.cuda.profiler.start()
+        call(args.warmup)
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "workload": "gemv", "rows": rows, "k": K}))
+        return
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        call(i)
+    e.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier(world)
+    per_call = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    # end to end: x from pinned host memory, out read back, every step
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s.record()
+    for i in range(args.steps):
+        x.copy_(x_host, non_blocking=True)
+        call(i)
+        out_host.copy_(out, non_blocking=True)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    hbm, src = peaks()
+    gbs = step_bytes / per_call / 1e9
+    line = {
+        "metric": "u4 GEMV HBM GB/s (BASELINE config 0 shape unless --rows/--k)",
+        "value": round(world * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_call * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4xf16",
+        "data": "synthetic",
+        "config": {"workload": f"u4 g128 GEMV {rows} x {K}, fp16 x, fp32 out",
+                   "rows": rows, "k": K, "bytes_per_step": step_bytes,
+                   "l2": f"weights rotate over {copies} copies (> 2x L2)",
+                   "parallelism": "replicas" if world > 1 else "single GPU"},
+        "e2e": {"value": round(world * step_bytes / t_e2e / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": K * 2, "d2h_bytes_per_step": rows * 4},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "kernel": "u4_stream_proj_kernel" if rows % 16 == 0 and
+                     K % 512 == 0 and K <= 4096 else "u4_gemv_multi_kernel",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        w0 = pool[0]
+        wn, sn, zn = (w0.weight.cpu().numpy(), w0.scale.cpu().numpy(), w0.zp.cpu().numpy())
+        xn = x_host.numpy()
+        reps, t0 = 0, time.time()
+        while time.time() - t0 < 10.0 and reps < 200:
+            oracle.u4_gemv(xn, wn, sn, zn, G, precise=True)
+            reps += 1
+        dt = (time.time() - t0) / reps
+        line["cpu_baseline"] = {"value": round(step_bytes / dt / 1e9, 3), "unit": "GB/s",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"{reps} oracle GEMVs of the same shape"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["decode", "moe_prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "moe_prefill", "gemv"], default="decode")
+    ap.add_argument("--rows", type=int, default=1024, help="output rows for --workload gemv")
+    ap.add_argument("--k", type=int, default=2048, help="input length for --workload gemv")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload moe_prefill")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
@@ -483,6 +604,8 @@ def main() -> None:
             run_reference(args, world, rank)
         elif args.workload == "moe_prefill":
             run_moe_prefill(args, world, rank, local)
+        elif args.workload == "gemv":
+            run_gemv(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
