@@ -342,17 +342,18 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* x, 
 
 // out[t][h] = sum_r float(Y[inv(t,r)][h]), ranks in order, fp32 accumulate
 // over fp16 contributions (iq36_scatter_f16_contributions,
-// grouped_s8_u4_f16_contribution_moe.cl:831-845).
-__global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, void* out,
-                                                         int out_dtype, PfWork w) {
+// grouped_s8_u4_f16_contribution_moe.cl:831-845). Output fp32, bf16 or fp16.
+__global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, const __half* y,
+                                                         int T, int H, int k, void* out,
+                                                         int out_dtype) {
   pdl_wait();
   const int t = blockIdx.x;
   int rows[16];
-  for (int r = 0; r < k; ++r) rows[r] = w.inv[(size_t)t * k + r];
+  for (int r = 0; r < k; ++r) rows[r] = inv[(size_t)t * k + r];
   for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < k; ++r) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(w.y + (size_t)rows[r] * H + h);
+      const uint2 raw = *reinterpret_cast<const uint2*>(y + (size_t)rows[r] * H + h);
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
       const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
       acc.x += a.x;
@@ -366,6 +367,11 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int T, int H, int k, vo
       o[1] = __float2bfloat16_rn(acc.y);
       o[2] = __float2bfloat16_rn(acc.z);
       o[3] = __float2bfloat16_rn(acc.w);
+    } else if (out_dtype == IQ36_F16) {
+      uint2 o;
+      o.x = pack_half2(__float2half_rn(acc.x), __float2half_rn(acc.y));
+      o.y = pack_half2(__float2half_rn(acc.z), __float2half_rn(acc.w));
+      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(out) + (size_t)t * H + h) = o;
     } else {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + h) = acc;
     }
@@ -777,7 +783,8 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   if (H % 256 || I % 128 || H < 256 || I < 128 || H > 2048 || I > 2048 ||
       (int64_t)T * k > (1 << 28))
     return IQ36_ERR_SHAPE;
-  if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16) return IQ36_ERR_ARG;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16 && out_dtype != IQ36_F16)
+    return IQ36_ERR_ARG;
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(b->gate_up_weight, 16) ||
       !aligned(b->down_weight, 16) || !aligned(b->gate_up_scale, 16) ||
       !aligned(b->down_scale, 16) || !aligned(b->gate_up_zp, 16) || !aligned(b->down_zp, 16))
@@ -847,11 +854,28 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
     e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_act, map_d, g2);
   if (e == cudaSuccess)
-    e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, T, H, k, out, out_dtype, w);
+    e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, (const int32_t*)w.inv,
+               (const __half*)w.y, T, H, k, out, out_dtype);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
 }  // namespace iq36
+
+extern "C" int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int32_t T,
+                                int32_t H, int32_t k, void* out, int32_t out_dtype,
+                                iq36_stream_t stream) {
+  using namespace iq36;
+  if (!contrib_f16 || !inv || !out) return IQ36_ERR_ARG;
+  if (T < 0 || k < 1 || k > 16 || H < 4 || H % 4) return IQ36_ERR_SHAPE;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_BF16 && out_dtype != IQ36_F16)
+    return IQ36_ERR_ARG;
+  if (!aligned(contrib_f16, 8) || !aligned(out, 16)) return IQ36_ERR_ALIGN;
+  if (T == 0) return IQ36_OK;
+  const cudaError_t e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, as_stream(stream), inv,
+                               reinterpret_cast<const __half*>(contrib_f16), (int)T, (int)H,
+                               (int)k, out, (int)out_dtype);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
 
 extern "C" size_t iq36_moe_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
                                                    int32_t hidden, int32_t intermediate) {

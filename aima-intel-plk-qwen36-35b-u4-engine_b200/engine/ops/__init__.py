@@ -329,6 +329,19 @@ def moe_expert_ffn_prefill(x: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     return out
 
 
+def moe_combine(contrib: torch.Tensor, inv: torch.Tensor, k: int,
+                out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """out[t] = sum_r float(contrib[inv[t*k + r]]) in rank order (fp16 rows)."""
+    _cuda(contrib, "contrib", torch.float16)
+    _cuda(inv, "inv", torch.int32)
+    _need(inv.numel() % k == 0, "inv must hold T*k rows")
+    t, h = inv.numel() // k, contrib.shape[1]
+    out = torch.empty(t, h, dtype=out_dtype, device=contrib.device)
+    N.call("iq36_moe_combine", contrib.data_ptr(), inv.data_ptr(), t, h, k, out.data_ptr(),
+           _dtype_code(out_dtype), _stream(contrib.device))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # (3) attention
 

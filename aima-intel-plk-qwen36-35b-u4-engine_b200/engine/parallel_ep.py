@@ -10,11 +10,12 @@ experts [r*E/P, (r+1)*E/P) and its own token shard. Per call:
      the token rows (bf16 [n, H]), local expert ids and router weights
      (all-to-all with those split sizes, NCCL over NVLink on GPUs);
   3. the owner runs the grouped prefill on its received rows, one
-     assignment per row (k = 1), producing weight * expert(x) in fp32;
-  4. the results return by the reverse all-to-all;
-  5. the source places each row back at its assignment index and sums the k
-     contributions of each token in slot order — the same fp32 sums as the
-     single-GPU scatter, so the result is bitwise the single-GPU result.
+     assignment per row (k = 1), producing the fp16 contribution
+     fp16(weight * expert(x)) — exactly the single-GPU contribution;
+  4. the contributions return by the reverse all-to-all (fp16);
+  5. the source sums the k contributions of each token in slot order in fp32
+     (iq36_moe_combine, the single-GPU scatter kernel), so the result is
+     bitwise the single-GPU result.
 
 The local expert computation is a parameter (``expert_fn``), so the exchange
 logic can be tested on CPU ranks (gloo) with a reference expert function;
@@ -37,10 +38,10 @@ def gpu_expert_fn(local_bank) -> ExpertFn:
 
     def fn(x_rows: torch.Tensor, local_ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
         if x_rows.shape[0] == 0:
-            return torch.empty(0, x_rows.shape[1], dtype=torch.float32, device=x_rows.device)
+            return torch.empty(0, x_rows.shape[1], dtype=torch.float16, device=x_rows.device)
         return ops.moe_expert_ffn_prefill(x_rows.contiguous(), local_ids.view(-1, 1).contiguous(),
                                           weights.view(-1, 1).contiguous(), local_bank,
-                                          out_dtype=torch.float32)
+                                          out_dtype=torch.float16)
     return fn
 
 
@@ -66,21 +67,29 @@ def ep_moe_prefill(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, nu
     n_recv = int(sum(r_split))
 
     send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
-    send_id = (flat_e.index_select(0, order) - dest.index_select(0, order) * e_local).to(torch.int32)
-    send_w = weights.reshape(-1).index_select(0, order).to(torch.float32)
+    # local expert id and router weight travel together as two int32 words
+    send_meta = torch.stack([
+        (flat_e.index_select(0, order) - dest.index_select(0, order) * e_local).to(torch.int32),
+        weights.reshape(-1).index_select(0, order).to(torch.float32).view(torch.int32)], dim=1)
     recv_x = torch.empty(n_recv, hidden, dtype=x.dtype, device=dev)
-    recv_id = torch.empty(n_recv, dtype=torch.int32, device=dev)
-    recv_w = torch.empty(n_recv, dtype=torch.float32, device=dev)
+    recv_meta = torch.empty(n_recv, 2, dtype=torch.int32, device=dev)
     dist.all_to_all_single(recv_x, send_x, r_split, s_split, group=group)
-    dist.all_to_all_single(recv_id, send_id, r_split, s_split, group=group)
-    dist.all_to_all_single(recv_w, send_w, r_split, s_split, group=group)
+    dist.all_to_all_single(recv_meta, send_meta, r_split, s_split, group=group)
+    recv_id = recv_meta[:, 0].contiguous()
+    recv_w = recv_meta[:, 1].contiguous().view(torch.float32)
 
-    y = expert_fn(recv_x, recv_id, recv_w)                           # [n_recv, H] fp32
+    y = expert_fn(recv_x, recv_id, recv_w)                           # [n_recv, H]
 
-    back = torch.empty(order.numel(), hidden, dtype=torch.float32, device=dev)
+    back = torch.empty(order.numel(), hidden, dtype=y.dtype, device=dev)
     dist.all_to_all_single(back, y.contiguous(), s_split, r_split, group=group)
-    contrib = torch.empty_like(back)
-    contrib.index_copy_(0, order, back)                             # back to assignment order
+    if back.is_cuda and back.dtype == torch.float16:
+        from . import ops
+        # inv[a] = row of assignment a in `back`; slot-order fp32 sums on device
+        inv = torch.empty(order.numel(), dtype=torch.int32, device=dev)
+        inv[order] = torch.arange(order.numel(), dtype=torch.int32, device=dev)
+        return ops.moe_combine(back, inv, k)
+    contrib = torch.empty_like(back, dtype=torch.float32)
+    contrib.index_copy_(0, order, back.float())                    # back to assignment order
     contrib = contrib.view(t_tokens, k, hidden)
     out = contrib[:, 0].clone()
     for j in range(1, k):                                           # slot order, fp32

@@ -20,7 +20,7 @@ Multi-GPU: replicas only (each rank decodes its own sequence; no collective on
 the data path), value summed over ranks.
 
 Other workloads: --workload moe_prefill (grouped MoE
-prefill; expert-parallel over NCCL at --gpus > 1) and --workload gemv
+prefill; replicas at --gpus > 1, expert-parallel over NCCL with --ep) and --workload gemv
 (one u4 GEMV per step, --rows / --k for other shapes).
 """
 
@@ -382,7 +382,7 @@ def run_moe_prefill(args, world, rank, local) -> None:
     rb = bank.c()
     stream = torch.cuda.current_stream(dev)
 
-    if world > 1:
+    if world > 1 and args.ep:
         # expert parallel: this rank owns E/world experts and its own T tokens
         from engine.parallel_ep import ep_moe_prefill, gpu_expert_fn
         from engine.parallel_tp import shard_expert_bank
@@ -453,8 +453,9 @@ def run_moe_prefill(args, world, rank, local) -> None:
         "data": "synthetic",
         "config": {"workload": f"config3 grouped MoE prefill T={T}, 256 experts, top-8, "
                                "Zipf(1.1)-skewed routing", "T": T, "l2": "flushed between calls",
-                   "parallelism": f"ep{world} (NCCL all-to-all dispatch/combine)" if world > 1
-                   else "single GPU"},
+                   "parallelism": (f"ep{world} (NCCL all-to-all dispatch/combine)" if args.ep
+                                   else "replicas (every GPU holds all 256 experts, 17 GB)")
+                   if world > 1 else "single GPU"},
         "e2e": {"value": round(world * T / t_e2e, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": T * H * 2 + T * k * 8, "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": 7 * args.steps,
@@ -588,6 +589,8 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=1024, help="output rows for --workload gemv")
     ap.add_argument("--k", type=int, default=2048, help="input length for --workload gemv")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload moe_prefill")
+    ap.add_argument("--ep", action="store_true",
+                    help="--workload moe_prefill at --gpus > 1: expert parallel instead of replicas")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)

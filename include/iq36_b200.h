@@ -182,15 +182,24 @@ size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t 
 /* ---- (2b) grouped MoE prefill ----------------------------------------------
  * For T tokens with top-k routing (ids, weights [T,k]): permute token rows by
  * expert (stable: by expert, then token, then rank), per expert
- * Y = SwiGLU(X W_gu^T) W_d^T on tcgen05 tensor cores (u4 dequantised to bf16 in
- * shared memory), then out[t] = sum_{r<k} weights[t,r] * Y[row(t,r)] in rank
- * order. Follows the Gen-1 schedule grouped_s8_u4_f16_contribution_moe.cl:13-222
- * and scatter :847-861, and the stock gather/GEMM/scatter of
- * iq36-pr35924-grouped-postops.patch:15-124. x bf16 [T, H]; out fp32/bf16.
- * Requirements: H % 128 == 0, I % 128 == 0, G == 128. */
+ * Y = fp16(weights * SwiGLU(X W_gu^T) W_d^T) on tcgen05 tensor cores (x as fp16,
+ * u4 dequantised to fp16 in shared memory, fp32 accumulate), then
+ * out[t] = sum_{r<k} Y[row(t,r)] in rank order in fp32. Follows the Gen-1
+ * schedule grouped_s8_u4_f16_contribution_moe.cl:13-222 with its fp16
+ * contribution scatter :831-845, and the stock gather/GEMM/scatter of
+ * iq36-pr35924-grouped-postops.patch:15-124. x bf16 [T, H]; out fp32, bf16 or
+ * fp16 (with k = 1 the fp16 output is the contribution itself, exactly).
+ * Requirements: H % 256 == 0, I % 128 == 0, H, I <= 2048, G == 128. */
 int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids, const float* weights,
                      int32_t k, const iq36_expert_bank* routed, void* out, int32_t out_dtype,
                      void* workspace, size_t workspace_bytes, iq36_stream_t stream);
+/* out[t] = sum_{r<k} float(contrib[inv[t*k + r]]) in rank order (fp32 sums of
+ * fp16 contribution rows [*, H]); out fp32, bf16 or fp16 [T, H]. The
+ * contribution scatter of the grouped prefill on its own, for callers that
+ * compute contributions elsewhere (the expert-parallel combine):
+ * iq36_scatter_f16_contributions, grouped_s8_u4_f16_contribution_moe.cl:831-845. */
+int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int32_t T, int32_t H, int32_t k,
+                     void* out, int32_t out_dtype, iq36_stream_t stream);
 size_t iq36_moe_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
                                         int32_t hidden, int32_t intermediate);
 

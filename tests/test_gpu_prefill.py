@@ -78,3 +78,34 @@ def test_prefill_deterministic(cuda):
     a = moe_expert_ffn_prefill(x, ids, wts, bank)
     b = moe_expert_ffn_prefill(x, ids, wts, bank)
     assert torch.equal(a, b)
+
+
+def test_moe_combine_matches_slot_order_sum(cuda):
+    """iq36_moe_combine: fp32 sums of fp16 contribution rows in slot order,
+    bitwise equal to the same additions done one slot at a time."""
+    import torch
+    from engine.ops import moe_combine
+    g = torch.Generator(device="cpu").manual_seed(3)
+    T, H, k = 37, 2048, 8
+    contrib = (torch.randn(T * k + 5, H, generator=g) * 4).to(torch.float16).to(cuda)
+    inv = torch.randperm(T * k + 5, generator=g)[:T * k].to(torch.int32).to(cuda)
+    out = moe_combine(contrib, inv, k)
+    rows = contrib.float()[inv.long()].view(T, k, H)
+    ref = rows[:, 0].clone()
+    for r in range(1, k):
+        ref += rows[:, r]
+    assert torch.equal(out, ref)
+
+
+def test_prefill_fp16_output_is_the_contribution(cuda):
+    """With k = 1 the fp16 output of the grouped prefill is the fp16
+    contribution itself: the fp32 output rounds to it exactly."""
+    import torch
+    from engine.ops import moe_expert_ffn_prefill, router_select
+    rng = np.random.default_rng(12)
+    bank = bank_to_torch(make_bank(rng, 16, 2048, 512), cuda)
+    ids, w = router_select(_t(zipf_router_logits(rng, 200, 16), cuda), 1)
+    x = torch.randn(200, 2048, device=cuda).to(torch.bfloat16)
+    o32 = moe_expert_ffn_prefill(x, ids, w, bank, out_dtype=torch.float32)
+    o16 = moe_expert_ffn_prefill(x, ids, w, bank, out_dtype=torch.float16)
+    assert torch.equal(o16.float(), o32)
