@@ -58,7 +58,7 @@
 namespace iq36 {
 
 constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64;
-constexpr int kPfAStages = 3, kPfBStages = 3, kPfCodeStages = 3;
+constexpr int kPfAStages = 3, kPfBStages = 2, kPfCodeStages = 3;
 // A code stage holds kPfCodeKB k-blocks of u4 codes for the 256 B-tile rows:
 // TMA rows of 64 bytes (two k-blocks) halve the row requests of 32-byte rows,
 // and the TMA engine's row-request rate, not bytes, bounded the GEMMs.
@@ -67,9 +67,9 @@ constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;  // 64 bytes per row
 constexpr int kPfAStage = kPfBM * kPfBK * 2;  // 16 KB
 constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
 constexpr int kPfCodeStage = kPfBN * kPfCodeRow;  // 16 KB of u4 codes
-constexpr int kPfMaxGroups = 16;                   // K <= 2048 with G = 128
-constexpr int kPfScaleBuf = kPfBN * kPfMaxGroups * 2;  // one unit's scales, 8 KB
-constexpr int kPfZpBuf = kPfBN * kPfMaxGroups / 2;     // one unit's zero points, 2 KB
+constexpr int kPfMaxGroups = 32;                   // K <= 4096 with G = 128
+constexpr int kPfScaleBuf = kPfBN * kPfMaxGroups * 2;  // one unit's scales, 16 KB
+constexpr int kPfZpBuf = kPfBN * kPfMaxGroups / 2;     // one unit's zero points, 4 KB
 constexpr int kPfOffB = kPfAStages * kPfAStage;  // B ring after the A ring
 constexpr int kPfOffCodes = kPfOffB + kPfBStages * kPfBStage;
 constexpr int kPfOffScale = kPfOffCodes + kPfCodeStages * kPfCodeStage;
@@ -381,15 +381,38 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, con
 // ---------------------------------------------------------------------------
 // Grouped GEMM
 
+// MODE 0: grouped gate_up + SwiGLU; MODE 1: grouped down x router weight
+// (fp16 contributions); MODE 2: dense u4 GEMM out[T, N] = x W^T (tiles of the
+// T rows in order, weight rows nt*256 ..), fp16 store or fp32 accumulate.
 struct GemmArgs {
-  const __half* s;      // scales of the bank
-  const uint8_t* z;     // zero points of the bank
+  const __half* s;      // scales of the bank (or matrix)
+  const uint8_t* z;     // zero points
   int64_t exp_rows;     // weight rows per expert (2I for gate_up, H for down)
-  int K;                // reduction length (H or I)
+  int K;                // reduction length (H or I; the input length for MODE 2)
   int I;                // intermediate size (gate_up row split)
-  int H;
+  int H;                // output rows of the down GEMM; N for MODE 2
   PfWork work;
+  int T;                // MODE 2: rows of x
+  void* out;            // MODE 2: [T, N]
+  int out_dtype;        // MODE 2: IQ36_F16 store or IQ36_F32
+  int accumulate;       // MODE 2, fp32: out += f16(x W^T)
 };
+
+template <int MODE>
+__device__ __forceinline__ int pf_units(const GemmArgs& g) {
+  if (MODE == 2) return (g.T + kPfBM - 1) / kPfBM * (g.H / kPfBN);
+  return *g.work.tile_count * (MODE == 0 ? g.I / 128 : g.H / kPfBN);
+}
+template <int MODE>
+__device__ __forceinline__ void pf_rows(const GemmArgs& g, int mt, int& row0, int& rows) {
+  if (MODE == 2) {
+    row0 = mt * kPfBM;
+    rows = min(kPfBM, g.T - row0);
+  } else {
+    row0 = g.work.tile_row0[mt];
+    rows = g.work.tile_rows[mt];
+  }
+}
 
 // Work unit u (persistent CTAs take u = blockIdx.x, + gridDim.x, ...):
 // M tile u / nN of the tile table, N tile u % nN, so the N tiles of one M
@@ -402,10 +425,14 @@ struct PfUnit {
 template <int MODE>
 __device__ __forceinline__ PfUnit pf_unit(const GemmArgs& g, int u, int nN) {
   const int mt = u / nN, nt = u - mt * nN;
-  const int e = g.work.tile_expert[mt];
   PfUnit r;
-  r.row0 = g.work.tile_row0[mt];
-  r.rows = g.work.tile_rows[mt];
+  pf_rows<MODE>(g, mt, r.row0, r.rows);
+  if (MODE == 2) {
+    r.wr0 = (int64_t)nt * kPfBN;
+    r.wr1 = r.wr0 + 128;
+    return r;
+  }
+  const int e = g.work.tile_expert[mt];
   if (MODE == 0) {
     r.wr0 = (int64_t)e * g.exp_rows + nt * 128;  // gate rows
     r.wr1 = r.wr0 + g.I;                         // the matching up rows
@@ -469,7 +496,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // the tile table and both operands come from earlier launches
   const int nN = MODE == 0 ? g.I / 128 : g.H / kPfBN;
-  const int total = *g.work.tile_count * nN;
+  const int total = pf_units<MODE>(g);
   const int nkb = g.K / kPfBK;
   const int ng = g.K / 128;
   bool ok = true;
@@ -479,7 +506,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (lane == 0) {
       int it = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const int row0 = g.work.tile_row0[u / nN];
+        int row0, rows_unused;
+        pf_rows<MODE>(g, u / nN, row0, rows_unused);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % kPfAStages;
           ok = mbar_wait(bar_aempty + 8 * s, ((it / kPfAStages) & 1) ^ 1u);
@@ -628,7 +656,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int mt = u / nN, nt = u - mt * nN;
-      const int row0 = g.work.tile_row0[mt], rows = g.work.tile_rows[mt];
+      int row0, rows;
+      pf_rows<MODE>(g, mt, row0, rows);
       const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
       if (MODE == 0) {
         for (int j = 0; j < 128; j += 16) {
@@ -653,6 +682,43 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               o.z = pack_half2(a8[2], a8[6]);
               o.w = pack_half2(a8[3], a8[7]);
               *reinterpret_cast<uint4*>(dst + 8 * q) = o;
+            }
+          }
+        }
+      } else if (MODE == 2) {
+        for (int j = 0; j < kPfBN; j += 16) {
+          uint32_t yv[16];
+          tmem_ld16(tl + j, yv);
+          tmem_ld_wait();
+          if (m < rows) {
+            const size_t o = (size_t)(row0 + m) * g.H + nt * kPfBN + j;
+            if (g.out_dtype == IQ36_F16) {
+              uint4 h[2];
+              uint32_t* hw = reinterpret_cast<uint32_t*>(h);
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                hw[q] = pack_half2(__float2half_rn(__uint_as_float(yv[2 * q])),
+                                   __float2half_rn(__uint_as_float(yv[2 * q + 1])));
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g.out) + o);
+              dst[0] = h[0];
+              dst[1] = h[1];
+            } else {
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(g.out) + o);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float4 v = make_float4(__uint_as_float(yv[4 * q]), __uint_as_float(yv[4 * q + 1]),
+                                       __uint_as_float(yv[4 * q + 2]),
+                                       __uint_as_float(yv[4 * q + 3]));
+                if (g.accumulate) {
+                  // residual += the fp16-rounded projection output
+                  const float4 r = dst[q];
+                  v.x = r.x + __half2float(__float2half_rn(v.x));
+                  v.y = r.y + __half2float(__float2half_rn(v.y));
+                  v.z = r.z + __half2float(__float2half_rn(v.z));
+                  v.w = r.w + __half2float(__float2half_rn(v.w));
+                }
+                dst[q] = v;
+              }
             }
           }
         }
@@ -859,7 +925,123 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------------------
+// Dense u4 GEMM (batched projections): out[T, N] = x W^T.
+
+// Row t of x (fp32, optionally RMS-normalised with weight nw; or fp16) to the
+// permuted fp16 operand layout of the GEMM (each 8-chunk as 0,4,1,5,2,6,3,7).
+__global__ void __launch_bounds__(256) gemm_xprep_kernel(const void* x, int x_dtype,
+                                                         const float* nw, float eps, int K,
+                                                         __half* xp) {
+  __shared__ float red[9];
+  pdl_wait();
+  const int t = blockIdx.x, tid = threadIdx.x;
+  __half h[8];
+  float scale = 1.f;
+  const float* xf = reinterpret_cast<const float*>(x) + (size_t)t * K;
+  const __half* xh = reinterpret_cast<const __half*>(x) + (size_t)t * K;
+  if (x_dtype == IQ36_F32 && nw != nullptr) {
+    float ss = 0.f;
+    for (int i = tid; i < K; i += 256) ss = fmaf(xf[i], xf[i], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float v = 0.f;
+      for (int w = 0; w < 8; ++w) v += red[w];
+      red[8] = rsqrtf(v / (float)K + eps);
+    }
+    __syncthreads();
+    scale = red[8];
+  }
+  for (int c = tid; c < K / 8; c += 256) {
+    if (x_dtype == IQ36_F32) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = xf[c * 8 + j];
+        h[j] = __float2half_rn(nw != nullptr ? v * scale * nw[c * 8 + j] : v);
+      }
+    } else {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xh + c * 8);
+      const __half* hp = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = hp[j];
+    }
+    uint4 o;
+    o.x = pack_half2(h[0], h[4]);
+    o.y = pack_half2(h[1], h[5]);
+    o.z = pack_half2(h[2], h[6]);
+    o.w = pack_half2(h[3], h[7]);
+    *reinterpret_cast<uint4*>(xp + (size_t)t * K + c * 8) = o;
+  }
+  pdl_launch_dependents();
+}
+
+size_t u4_gemm_ws(int T, int K) { return up256((size_t)(T + kPfBM) * K * 2) + 256; }
+
+int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T, int K, int G,
+                   const iq36_u4_matrix* w, void* out, int out_dtype, int accumulate, void* ws,
+                   size_t ws_bytes, cudaStream_t stream) {
+  if (!x || !w || !w->weight || !w->scale || !w->zp || !out) return IQ36_ERR_ARG;
+  if (x_dtype != IQ36_F32 && x_dtype != IQ36_F16) return IQ36_ERR_ARG;
+  if (nw && x_dtype != IQ36_F32) return IQ36_ERR_ARG;
+  if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
+  if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
+  if (G != 128 || T < 1 || K < 256 || K % 256 || K > 4096 || w->rows < kPfBN ||
+      w->rows % kPfBN)
+    return IQ36_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w->weight, 16) ||
+      !aligned(w->scale, 16) || !aligned(w->zp, 16))
+    return IQ36_ERR_ALIGN;
+  if (!ws || ws_bytes < u4_gemm_ws(T, K)) return IQ36_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return IQ36_ERR_ALIGN;
+  __half* xp = reinterpret_cast<__half*>(ws);
+  int32_t* err = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) +
+                                            up256((size_t)(T + kPfBM) * K * 2));
+  CUtensorMap map_x, map_w;
+  if (!make_act_map(&map_x, xp, (uint64_t)T + kPfBM, (uint64_t)K) ||
+      !make_code_map(&map_w, w->weight, (uint64_t)w->rows, (uint64_t)K / 2))
+    return IQ36_ERR_CUDA;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (!attr_set[dev].load()) {
+    if (cudaFuncSetAttribute(pf_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPfSmem) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+    attr_set[dev].store(true);
+  }
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  if (cudaMemsetAsync(err, 0, 4, stream) != cudaSuccess) return IQ36_ERR_CUDA;
+  cudaError_t e = launch(gemm_xprep_kernel, dim3(T), dim3(256), 0, stream, x, x_dtype, nw, eps, K,
+                         xp);
+  PfWork wk{};
+  wk.err = err;
+  GemmArgs g{reinterpret_cast<const __half*>(w->scale), w->zp, 0, K, 0, w->rows, wk,
+             T, out, out_dtype, accumulate};
+  const int units = (T + kPfBM - 1) / kPfBM * (w->rows / kPfBN);
+  if (e == cudaSuccess)
+    e = launch(pf_gemm_kernel<2>, dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads),
+               (size_t)kPfSmem, stream, map_x, map_w, g);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
 }  // namespace iq36
+
+extern "C" size_t iq36_u4_gemm_workspace_bytes(int32_t T, int32_t K) {
+  return iq36::u4_gemm_ws(T, K);
+}
+
+extern "C" int iq36_u4_gemm(const void* x, int32_t x_dtype, const float* norm_weight,
+                            float norm_eps, int32_t T, int32_t K, int32_t group,
+                            const iq36_u4_matrix* w, void* out, int32_t out_dtype,
+                            int32_t accumulate, void* workspace, size_t workspace_bytes,
+                            iq36_stream_t stream) {
+  return iq36::u4_gemm_launch(x, x_dtype, norm_weight, norm_eps, T, K, group, w, out, out_dtype,
+                              accumulate, workspace, workspace_bytes, iq36::as_stream(stream));
+}
 
 extern "C" int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int32_t T,
                                 int32_t H, int32_t k, void* out, int32_t out_dtype,

@@ -329,6 +329,28 @@ def moe_expert_ffn_prefill(x: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     return out
 
 
+def u4_gemm(x: torch.Tensor, w: U4Weight, out: torch.Tensor | None = None,
+            out_dtype: torch.dtype = torch.float16, accumulate: bool = False,
+            norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+            workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Batched u4 projection out[T, N] = x W^T (x fp16, or fp32 with an optional
+    fused RMSNorm); out fp16, or fp32 (accumulate: out += f16(x W^T))."""
+    _cuda(x, "x")
+    _need(x.dim() == 2 and x.dtype in (torch.float16, torch.float32), "x must be [T, K] fp16/fp32")
+    t, k = x.shape
+    n = w.rows
+    if out is None:
+        out = torch.empty(t, n, dtype=out_dtype, device=x.device)
+    if workspace is None:
+        workspace = torch.empty(N.lib().iq36_u4_gemm_workspace_bytes(t, k), dtype=torch.uint8,
+                                device=x.device)
+    m = w.c()
+    N.call("iq36_u4_gemm", x.data_ptr(), _dtype_code(x.dtype), _ptr(norm_weight), norm_eps, t, k,
+           w.group, ctypes.byref(m), out.data_ptr(), _dtype_code(out.dtype), int(accumulate),
+           workspace.data_ptr(), workspace.numel(), _stream(x.device))
+    return out
+
+
 def moe_combine(contrib: torch.Tensor, inv: torch.Tensor, k: int,
                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """out[t] = sum_r float(contrib[inv[t*k + r]]) in rank order (fp16 rows)."""

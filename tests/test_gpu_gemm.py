@@ -1,0 +1,63 @@
+"""Batched u4 projections (iq36_u4_gemm, tcgen05) against the CPU oracle.
+
+Each output row is the u4 GEMV of the matching input row, so the oracle runs
+its GEMV per row. Shapes follow the batched prefill projections: DeltaNet and
+attention in-projections (K = 2048, fused RMSNorm of the fp32 residual, fp16
+out) and the out/o projections (K = 4096, fp16 in, fp32 residual update).
+Tolerance: tests/helpers.py (max rel 2e-3).
+"""
+
+import numpy as np
+import pytest
+
+from helpers import assert_close, make_u4, u4_to_torch
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+@pytest.mark.parametrize("T,N", [(300, 512), (129, 256), (1, 768)])
+def test_u4_gemm_fused_norm_f16_out(cuda, T, N):
+    import torch
+    from engine.ops import u4_gemm
+    rng = np.random.default_rng(T * 31 + N)
+    K = 2048
+    w, s, z = make_u4(rng, N, K)
+    x = (rng.standard_normal((T, K)) * 2).astype(np.float32)
+    nw = rng.uniform(0.9, 1.1, K).astype(np.float32)
+    out = u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda), out_dtype=torch.float16,
+                  norm_weight=_t(nw, cuda))
+    got = out.float().cpu().numpy()
+    for t in range(T):
+        x16 = oracle.rms_norm(x[t], nw, 1e-6).astype(np.float16)
+        assert_close(got[t], oracle.u4_gemv(x16, w, s, z, 128), f"gemm row {t}")
+
+
+def test_u4_gemm_k4096_residual_accumulate(cuda):
+    from engine.ops import u4_gemm
+    rng = np.random.default_rng(9)
+    T, K, N = 200, 4096, 512
+    w, s, z = make_u4(rng, N, K)
+    x = rng.standard_normal((T, K)).astype(np.float16)
+    res0 = rng.standard_normal((T, N)).astype(np.float32)
+    res = _t(res0.copy(), cuda)
+    u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda), out=res, accumulate=True)
+    got = res.cpu().numpy()
+    for t in range(0, T, 7):
+        ref = res0[t] + oracle.u4_gemv(x[t], w, s, z, 128).astype(np.float16).astype(np.float32)
+        assert_close(got[t], ref, f"gemm accumulate row {t}")
+
+
+def test_u4_gemm_rejects_bad_shapes(cuda):
+    import torch
+    from engine import _native as N
+    from engine.ops import u4_gemm
+    rng = np.random.default_rng(1)
+    w, s, z = make_u4(rng, 128, 2048)                  # N not a multiple of 256
+    with pytest.raises(N.Iq36Error):
+        u4_gemm(torch.zeros(4, 2048, dtype=torch.float16, device=cuda), u4_to_torch(w, s, z, cuda))
