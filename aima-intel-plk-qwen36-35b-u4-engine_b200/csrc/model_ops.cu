@@ -49,7 +49,9 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* in, int dim,
 // Split q/gate (gguf_loader.cpp:5928-5950), per-head RMSNorm, rotate-half RoPE
 // on the first rope_dim dims (iq36_qk_rope_layout.cl:37-60) with angles
 // evaluated in fp64, fp16 store; K/V appended at *pos_dev through the block
-// table (iq36_hot_ring_update.cl:7-28).
+// table (iq36_hot_ring_update.cl:7-28). Block x handles token x of a batch
+// (position *pos_dev + x; rows of q_full, k, v, q_out, gate_out per token);
+// the decode step launches one block.
 __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __half* v,
                                  const float* qn_w, const float* kn_w, float eps,
                                  const int32_t* pos_dev, int n_q, int n_kv, int rope_dim,
@@ -59,7 +61,12 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= n_q + n_kv) return;
   const int D = 256;
-  const int pos = *pos_dev;
+  const int pos = *pos_dev + blockIdx.x;
+  q_full += (size_t)blockIdx.x * 2 * n_q * D;
+  k += (size_t)blockIdx.x * n_kv * D;
+  v += (size_t)blockIdx.x * n_kv * D;
+  q_out += (size_t)blockIdx.x * n_q * D;
+  gate_out += (size_t)blockIdx.x * n_q * D;
   const bool is_q = warp < n_q;
   const int h = is_q ? warp : warp - n_q;
   const __half* src = is_q ? q_full + (size_t)(2 * h) * D : k + (size_t)h * D;
@@ -399,18 +406,18 @@ extern "C" int iq36_rms_norm(const float* in, int32_t rows, int32_t dim, const f
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
-extern "C" int iq36_attn_prep(const void* q_full_f16, const void* k_f16, const void* v_f16,
-                              const float* q_norm_w, const float* k_norm_w, float eps,
-                              const int32_t* pos_dev, int32_t n_q_heads, int32_t n_kv_heads,
-                              int32_t head_dim, int32_t rope_dim, float rope_base,
-                              const int32_t* block_table, int32_t block_size, void* k_cache,
-                              void* v_cache, void* q_out_f16, void* gate_out_f16,
-                              iq36_stream_t stream) {
+static int attn_prep_launch(const void* q_full_f16, const void* k_f16, const void* v_f16,
+                            const float* q_norm_w, const float* k_norm_w, float eps,
+                            const int32_t* pos_dev, int32_t tokens, int32_t n_q_heads,
+                            int32_t n_kv_heads, int32_t head_dim, int32_t rope_dim,
+                            float rope_base, const int32_t* block_table, int32_t block_size,
+                            void* k_cache, void* v_cache, void* q_out_f16, void* gate_out_f16,
+                            iq36_stream_t stream) {
   if (!q_full_f16 || !k_f16 || !v_f16 || !q_norm_w || !k_norm_w || !pos_dev || !block_table ||
       !k_cache || !v_cache || !q_out_f16 || !gate_out_f16)
     return IQ36_ERR_ARG;
   if (head_dim != 256 || n_q_heads < 1 || n_kv_heads < 1 || n_q_heads + n_kv_heads > 32 ||
-      block_size < 1)
+      block_size < 1 || tokens < 1)
     return IQ36_ERR_SHAPE;
   if (rope_dim != 16 && rope_dim != 32 && rope_dim != 64 && rope_dim != 128 && rope_dim != 256)
     return IQ36_ERR_SHAPE;
@@ -419,13 +426,38 @@ extern "C" int iq36_attn_prep(const void* q_full_f16, const void* k_f16, const v
       !aligned(gate_out_f16, 16))
     return IQ36_ERR_ALIGN;
   const cudaError_t e = launch(
-      attn_prep_kernel, dim3(1), dim3(32 * (n_q_heads + n_kv_heads)), 0, as_stream(stream),
+      attn_prep_kernel, dim3(tokens), dim3(32 * (n_q_heads + n_kv_heads)), 0, as_stream(stream),
       reinterpret_cast<const __half*>(q_full_f16), reinterpret_cast<const __half*>(k_f16),
       reinterpret_cast<const __half*>(v_f16), q_norm_w, k_norm_w, eps, pos_dev, n_q_heads,
       n_kv_heads, rope_dim, rope_base, block_table, block_size,
       reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache),
       reinterpret_cast<__half*>(q_out_f16), reinterpret_cast<__half*>(gate_out_f16));
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+extern "C" int iq36_attn_prep(const void* q_full_f16, const void* k_f16, const void* v_f16,
+                              const float* q_norm_w, const float* k_norm_w, float eps,
+                              const int32_t* pos_dev, int32_t n_q_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t rope_dim, float rope_base,
+                              const int32_t* block_table, int32_t block_size, void* k_cache,
+                              void* v_cache, void* q_out_f16, void* gate_out_f16,
+                              iq36_stream_t stream) {
+  return attn_prep_launch(q_full_f16, k_f16, v_f16, q_norm_w, k_norm_w, eps, pos_dev, 1,
+                          n_q_heads, n_kv_heads, head_dim, rope_dim, rope_base, block_table,
+                          block_size, k_cache, v_cache, q_out_f16, gate_out_f16, stream);
+}
+
+extern "C" int iq36_attn_prep_batch(const void* q_full_f16, const void* k_f16,
+                                    const void* v_f16, const float* q_norm_w,
+                                    const float* k_norm_w, float eps, const int32_t* pos_dev,
+                                    int32_t tokens, int32_t n_q_heads, int32_t n_kv_heads,
+                                    int32_t head_dim, int32_t rope_dim, float rope_base,
+                                    const int32_t* block_table, int32_t block_size,
+                                    void* k_cache, void* v_cache, void* q_out_f16,
+                                    void* gate_out_f16, iq36_stream_t stream) {
+  return attn_prep_launch(q_full_f16, k_f16, v_f16, q_norm_w, k_norm_w, eps, pos_dev, tokens,
+                          n_q_heads, n_kv_heads, head_dim, rope_dim, rope_base, block_table,
+                          block_size, k_cache, v_cache, q_out_f16, gate_out_f16, stream);
 }
 
 extern "C" int iq36_delta_prep(const void* qkv_f16, int32_t channels, float* conv_state,

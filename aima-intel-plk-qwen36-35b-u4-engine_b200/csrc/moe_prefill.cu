@@ -315,21 +315,28 @@ __global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* ids, const
   pdl_launch_dependents();
 }
 
-// Xp[p][:] = fp16(x[token(p)][:]) with each 8-chunk stored as (0,4,1,5,2,6,3,7).
-__global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* x, int P, int H,
+// Xp[p][:] = fp16(x[token(p)][:]) with each 8-chunk stored as (0,4,1,5,2,6,3,7);
+// x is bf16 (x_f16 == 0) or fp16.
+__global__ void __launch_bounds__(256) pf_gather_kernel(const void* x, int x_f16, int P, int H,
                                                         PfWork w) {
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= P) return;
   const int t = w.perm_tok[warp];
-  const __nv_bfloat16* src = x + (size_t)t * H;
+  const uint16_t* src = reinterpret_cast<const uint16_t*>(x) + (size_t)t * H;
   __half* dst = w.xp + (size_t)warp * H;
   for (int c = lane; c < H / 8; c += 32) {
     const uint4 raw = *reinterpret_cast<const uint4*>(src + c * 8);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
     __half h[8];
+    if (x_f16) {
+      const __half* hp = reinterpret_cast<const __half*>(&raw);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(b[j]));
+      for (int j = 0; j < 8; ++j) h[j] = hp[j];
+    } else {
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(__bfloat162float(b[j]));
+    }
     uint4 o;
     o.x = pack_half2(h[0], h[4]);
     o.y = pack_half2(h[1], h[5]);
@@ -342,10 +349,11 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const __nv_bfloat16* x, 
 
 // out[t][h] = sum_r float(Y[inv(t,r)][h]), ranks in order, fp32 accumulate
 // over fp16 contributions (iq36_scatter_f16_contributions,
-// grouped_s8_u4_f16_contribution_moe.cl:831-845). Output fp32, bf16 or fp16.
+// grouped_s8_u4_f16_contribution_moe.cl:831-845). Output fp32, bf16 or fp16;
+// with accumulate (fp32 only) the sum is added to out (the residual stream).
 __global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, const __half* y,
                                                          int T, int H, int k, void* out,
-                                                         int out_dtype) {
+                                                         int out_dtype, int accumulate) {
   pdl_wait();
   const int t = blockIdx.x;
   int rows[16];
@@ -373,7 +381,15 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, con
       o.y = pack_half2(__float2half_rn(acc.z), __float2half_rn(acc.w));
       *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(out) + (size_t)t * H + h) = o;
     } else {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + h) = acc;
+      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + h);
+      if (accumulate) {
+        const float4 r = *o;
+        acc.x += r.x;
+        acc.y += r.y;
+        acc.z += r.z;
+        acc.w += r.w;
+      }
+      *o = acc;
     }
   }
 }
@@ -383,7 +399,9 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, con
 
 // MODE 0: grouped gate_up + SwiGLU; MODE 1: grouped down x router weight
 // (fp16 contributions); MODE 2: dense u4 GEMM out[T, N] = x W^T (tiles of the
-// T rows in order, weight rows nt*256 ..), fp16 store or fp32 accumulate.
+// T rows in order, weight rows nt*256 ..), fp16 store or fp32 accumulate,
+// optionally scaled per row by sigmoid(row_gate[t]); MODE 3: dense gate_up +
+// SwiGLU, out[T, I] fp16 = SwiGLU(x W[0:I]^T, x W[I:2I]^T).
 struct GemmArgs {
   const __half* s;      // scales of the bank (or matrix)
   const uint8_t* z;     // zero points
@@ -396,16 +414,18 @@ struct GemmArgs {
   void* out;            // MODE 2: [T, N]
   int out_dtype;        // MODE 2: IQ36_F16 store or IQ36_F32
   int accumulate;       // MODE 2, fp32: out += f16(x W^T)
+  const float* row_gate;  // MODE 2: optional per-row logit; output *= sigmoid(logit)
 };
 
 template <int MODE>
 __device__ __forceinline__ int pf_units(const GemmArgs& g) {
   if (MODE == 2) return (g.T + kPfBM - 1) / kPfBM * (g.H / kPfBN);
+  if (MODE == 3) return (g.T + kPfBM - 1) / kPfBM * (g.I / 128);
   return *g.work.tile_count * (MODE == 0 ? g.I / 128 : g.H / kPfBN);
 }
 template <int MODE>
 __device__ __forceinline__ void pf_rows(const GemmArgs& g, int mt, int& row0, int& rows) {
-  if (MODE == 2) {
+  if (MODE >= 2) {
     row0 = mt * kPfBM;
     rows = min(kPfBM, g.T - row0);
   } else {
@@ -430,6 +450,11 @@ __device__ __forceinline__ PfUnit pf_unit(const GemmArgs& g, int u, int nN) {
   if (MODE == 2) {
     r.wr0 = (int64_t)nt * kPfBN;
     r.wr1 = r.wr0 + 128;
+    return r;
+  }
+  if (MODE == 3) {
+    r.wr0 = (int64_t)nt * 128;  // gate rows
+    r.wr1 = r.wr0 + g.I;        // the matching up rows
     return r;
   }
   const int e = g.work.tile_expert[mt];
@@ -495,7 +520,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // the tile table and both operands come from earlier launches
-  const int nN = MODE == 0 ? g.I / 128 : g.H / kPfBN;
+  const int nN = (MODE == 0 || MODE == 3) ? g.I / 128 : g.H / kPfBN;
   const int total = pf_units<MODE>(g);
   const int nkb = g.K / kPfBK;
   const int ng = g.K / 128;
@@ -659,13 +684,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int row0, rows;
       pf_rows<MODE>(g, mt, row0, rows);
       const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
-      if (MODE == 0) {
+      if (MODE == 0 || MODE == 3) {
         for (int j = 0; j < 128; j += 16) {
           uint32_t gv[16], uv[16];
           tmem_ld16(tl + j, gv);
           tmem_ld16(tl + 128 + j, uv);
           tmem_ld_wait();
-          if (m < rows) {
+          if (m < rows && MODE == 3) {
+            // natural column order, [T, I] fp16
+            __half* dst = reinterpret_cast<__half*>(g.out) + (size_t)(row0 + m) * g.I + nt * 128 + j;
+            uint32_t hw[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const float g0 = __uint_as_float(gv[2 * c]), u0 = __uint_as_float(uv[2 * c]);
+              const float g1 = __uint_as_float(gv[2 * c + 1]), u1 = __uint_as_float(uv[2 * c + 1]);
+              hw[c] = pack_half2(__float2half_rn(g0 * sigmoidf_acc(g0) * u0),
+                                 __float2half_rn(g1 * sigmoidf_acc(g1) * u1));
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            d4[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            d4[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+          } else if (m < rows) {
             __half* dst = g.work.act + (size_t)(row0 + m) * g.I + nt * 128 + j;
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
@@ -686,10 +725,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
       } else if (MODE == 2) {
+        const float rg =
+            (g.row_gate != nullptr && m < rows) ? sigmoidf_acc(g.row_gate[row0 + m]) : 1.f;
         for (int j = 0; j < kPfBN; j += 16) {
           uint32_t yv[16];
           tmem_ld16(tl + j, yv);
           tmem_ld_wait();
+          if (g.row_gate != nullptr) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) yv[q] = __float_as_uint(__uint_as_float(yv[q]) * rg);
+          }
           if (m < rows) {
             const size_t o = (size_t)(row0 + m) * g.H + nt * kPfBN + j;
             if (g.out_dtype == IQ36_F16) {
@@ -837,10 +882,13 @@ static bool make_code_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64
 
 size_t moe_prefill_ws(int T, int k, int E, int H, int I) { return pf_layout(T, k, E, H, I).total; }
 
-int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* weights, int k,
-                       const iq36_expert_bank* b, void* out, int out_dtype, void* ws,
-                       size_t ws_bytes, cudaStream_t stream) {
+int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
+                       const float* weights, int k, const iq36_expert_bank* b, void* out,
+                       int out_dtype, int accumulate, void* ws, size_t ws_bytes,
+                       cudaStream_t stream) {
   if (!x || !ids || !weights || !b || !out) return IQ36_ERR_ARG;
+  if (x_dtype != IQ36_BF16 && x_dtype != IQ36_F16) return IQ36_ERR_ARG;
+  if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
   if (!b->gate_up_weight || !b->gate_up_scale || !b->gate_up_zp || !b->down_weight ||
       !b->down_scale || !b->down_zp)
     return IQ36_ERR_ARG;
@@ -902,8 +950,8 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
   if (e == cudaSuccess)
     e = launch(pf_place_kernel, dim3(nC), dim3(256), 0, stream, ids, weights, P, E, k, w);
   if (e == cudaSuccess)
-    e = launch(pf_gather_kernel, dim3(ceil_div(P, 8)), dim3(256), 0, stream,
-               reinterpret_cast<const __nv_bfloat16*>(x), P, H, w);
+    e = launch(pf_gather_kernel, dim3(ceil_div(P, 8)), dim3(256), 0, stream, x,
+               x_dtype == IQ36_F16 ? 1 : 0, P, H, w);
   GemmArgs g1{reinterpret_cast<const __half*>(b->gate_up_scale), b->gate_up_zp, (int64_t)2 * I,
               H, I, H, w};
   // persistent grids: at most one CTA per SM, never more than the units
@@ -921,7 +969,7 @@ int moe_prefill_launch(const void* x, int T, const int32_t* ids, const float* we
                map_act, map_d, g2);
   if (e == cudaSuccess)
     e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, (const int32_t*)w.inv,
-               (const __half*)w.y, T, H, k, out, out_dtype);
+               (const __half*)w.y, T, H, k, out, out_dtype, accumulate);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
@@ -979,10 +1027,16 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const void* x, int x_dt
 
 size_t u4_gemm_ws(int T, int K) { return up256((size_t)(T + kPfBM) * K * 2) + 256; }
 
+// swiglu: W holds [gate; up] (2I rows); out[T, I] fp16 = SwiGLU of the two halves.
+// row_gate (fp32 [T], optional, fp32 out only): each output row * sigmoid(row_gate[t]).
 int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T, int K, int G,
                    const iq36_u4_matrix* w, void* out, int out_dtype, int accumulate, void* ws,
-                   size_t ws_bytes, cudaStream_t stream) {
+                   size_t ws_bytes, cudaStream_t stream, int swiglu = 0,
+                   const float* row_gate = nullptr) {
   if (!x || !w || !w->weight || !w->scale || !w->zp || !out) return IQ36_ERR_ARG;
+  if (swiglu && (out_dtype != IQ36_F16 || accumulate || row_gate || w->rows % 256))
+    return IQ36_ERR_ARG;
+  if (row_gate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
   if (x_dtype != IQ36_F32 && x_dtype != IQ36_F16) return IQ36_ERR_ARG;
   if (nw && x_dtype != IQ36_F32) return IQ36_ERR_ARG;
   if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
@@ -1007,6 +1061,8 @@ int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
   if (!attr_set[dev].load()) {
     if (cudaFuncSetAttribute(pf_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPfSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(pf_gemm_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kPfSmem) != cudaSuccess)
       return IQ36_ERR_CUDA;
     attr_set[dev].store(true);
@@ -1019,12 +1075,13 @@ int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T
                          xp);
   PfWork wk{};
   wk.err = err;
-  GemmArgs g{reinterpret_cast<const __half*>(w->scale), w->zp, 0, K, 0, w->rows, wk,
-             T, out, out_dtype, accumulate};
+  GemmArgs g{reinterpret_cast<const __half*>(w->scale), w->zp, 0, K, w->rows / 2, w->rows, wk,
+             T, out, out_dtype, accumulate, row_gate};
   const int units = (T + kPfBM - 1) / kPfBM * (w->rows / kPfBN);
   if (e == cudaSuccess)
-    e = launch(pf_gemm_kernel<2>, dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads),
-               (size_t)kPfSmem, stream, map_x, map_w, g);
+    e = launch(swiglu ? pf_gemm_kernel<3> : pf_gemm_kernel<2>,
+               dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads), (size_t)kPfSmem, stream,
+               map_x, map_w, g);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
@@ -1055,7 +1112,7 @@ extern "C" int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int
   if (T == 0) return IQ36_OK;
   const cudaError_t e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, as_stream(stream), inv,
                                reinterpret_cast<const __half*>(contrib_f16), (int)T, (int)H,
-                               (int)k, out, (int)out_dtype);
+                               (int)k, out, (int)out_dtype, 0);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
@@ -1068,6 +1125,91 @@ extern "C" int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* id
                                 const float* weights, int32_t k, const iq36_expert_bank* routed,
                                 void* out, int32_t out_dtype, void* workspace,
                                 size_t workspace_bytes, iq36_stream_t stream) {
-  return iq36::moe_prefill_launch(x_bf16, T, ids, weights, k, routed, out, out_dtype, workspace,
-                                  workspace_bytes, iq36::as_stream(stream));
+  return iq36::moe_prefill_launch(x_bf16, IQ36_BF16, T, ids, weights, k, routed, out, out_dtype,
+                                  0, workspace, workspace_bytes, iq36::as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// The MoE block of one layer over T prompt tokens, residual updated in place:
+// router logits on the RMS-normalised fp32 residual (same kernel and order of
+// sums as the decode step, so the routing matches token for token), top-k
+// selection, the grouped routed experts (fp16 contributions summed in rank
+// order into the residual), and the shared expert as two dense u4 GEMMs
+// (gate_up with SwiGLU, then down scaled by sigmoid(shared logit) and added to
+// the residual). run_qwen36_moe_ffn_layer (gguf_loader.cpp:5654-5782) with the
+// grouped prefill schedule of grouped_s8_u4_f16_contribution_moe.cl:13-222.
+
+namespace iq36 {
+int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw, float eps, int T,
+                         int H, const void* w_router, int E, const void* w_sg, float* logits,
+                         float* slogit, cudaStream_t stream);
+int router_select_launch(const float* logits, int T, int E, int k, int32_t* ids, float* weights,
+                         cudaStream_t stream);
+
+struct MoeLayerPfLayout {
+  size_t slogit, xn, act, gemm, moe, total;
+};
+static MoeLayerPfLayout moe_layer_pf_layout(int T, int k, int E, int H, int I) {
+  MoeLayerPfLayout L{};
+  size_t o = 0;
+  L.slogit = o; o += up256((size_t)T * 4);
+  L.xn = o; o += up256((size_t)T * H * 2);
+  L.act = o; o += up256((size_t)T * I * 2);
+  L.gemm = o; o += up256(u4_gemm_ws(T, std::max(H, I)));
+  L.moe = o; o += up256(pf_layout(T, k, E, H, I).total);
+  L.total = o;
+  return L;
+}
+}  // namespace iq36
+
+extern "C" size_t iq36_moe_layer_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
+                                                         int32_t hidden, int32_t intermediate) {
+  if (T < 1 || k < 1 || num_experts < 1 || hidden < 1 || intermediate < 1) return 0;
+  return iq36::moe_layer_pf_layout(T, k, num_experts, hidden, intermediate).total;
+}
+
+extern "C" int iq36_moe_layer_prefill(float* residual, int32_t T, int32_t hidden,
+                                      const float* norm_weight, float norm_eps,
+                                      const void* w_router_f16, const void* w_shared_gate_f16,
+                                      int32_t k, const iq36_expert_bank* routed,
+                                      const iq36_expert_bank* shared, int32_t* ids,
+                                      float* weights, float* logits, void* workspace,
+                                      size_t workspace_bytes, iq36_stream_t stream) {
+  using namespace iq36;
+  if (!residual || !norm_weight || !w_router_f16 || !routed || !ids || !weights || !logits ||
+      !workspace)
+    return IQ36_ERR_ARG;
+  if (shared && !w_shared_gate_f16) return IQ36_ERR_ARG;
+  const int E = routed->num_experts, H = routed->hidden, I = routed->intermediate;
+  if (T < 1 || hidden != H) return IQ36_ERR_SHAPE;
+  if (shared && (shared->hidden != H || shared->intermediate != I || shared->group != routed->group))
+    return IQ36_ERR_SHAPE;
+  const MoeLayerPfLayout L = moe_layer_pf_layout(T, k, E, H, I);
+  if (workspace_bytes < L.total) return IQ36_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(residual, 16)) return IQ36_ERR_ALIGN;
+  char* ws = static_cast<char*>(workspace);
+  float* slogit = reinterpret_cast<float*>(ws + L.slogit);
+  __half* xn = reinterpret_cast<__half*>(ws + L.xn);
+  __half* act = reinterpret_cast<__half*>(ws + L.act);
+  const cudaStream_t s = as_stream(stream);
+  int st = router_logits_launch(nullptr, residual, norm_weight, norm_eps, T, H, w_router_f16, E,
+                                shared ? w_shared_gate_f16 : nullptr, logits,
+                                shared ? slogit : nullptr, s);
+  if (st == IQ36_OK) st = router_select_launch(logits, T, E, k, ids, weights, s);
+  if (st == IQ36_OK)
+    st = iq36_rms_norm(residual, T, H, norm_weight, H, norm_eps, xn, IQ36_F16, stream);
+  if (st == IQ36_OK)
+    st = moe_prefill_launch(xn, IQ36_F16, T, ids, weights, k, routed, residual, IQ36_F32, 1,
+                            ws + L.moe, L.total - L.moe, s);
+  if (st == IQ36_OK && shared) {
+    const iq36_u4_matrix gu{shared->gate_up_weight, shared->gate_up_scale, shared->gate_up_zp,
+                            2 * I};
+    const iq36_u4_matrix dn{shared->down_weight, shared->down_scale, shared->down_zp, H};
+    st = u4_gemm_launch(xn, IQ36_F16, nullptr, 0.f, T, H, shared->group, &gu, act, IQ36_F16, 0,
+                        ws + L.gemm, L.moe - L.gemm, s, 1, nullptr);
+    if (st == IQ36_OK)
+      st = u4_gemm_launch(act, IQ36_F16, nullptr, 0.f, T, I, shared->group, &dn, residual,
+                          IQ36_F32, 1, ws + L.gemm, L.moe - L.gemm, s, 0, slogit);
+  }
+  return st;
 }

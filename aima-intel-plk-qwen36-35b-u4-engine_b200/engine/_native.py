@@ -70,6 +70,11 @@ _SIGS: dict[str, tuple] = {
     "iq36_moe_layer_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "iq36_moe_prefill": (c_int, [_P, c_int32, _P, _P, c_int32, POINTER(ExpertBankC), _P, c_int32,
                                  _P, c_size_t, _P]),
+    "iq36_moe_layer_prefill": (c_int, [_P, c_int32, c_int32, _P, c_float, _P, _P, c_int32,
+                                       POINTER(ExpertBankC), POINTER(ExpertBankC), _P, _P, _P,
+                                       _P, c_size_t, _P]),
+    "iq36_moe_layer_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32,
+                                                          c_int32]),
     "iq36_u4_gemm": (c_int, [_P, c_int32, _P, c_float, c_int32, c_int32, c_int32,
                              POINTER(U4Matrix), _P, c_int32, c_int32, _P, c_size_t, _P]),
     "iq36_u4_gemm_workspace_bytes": (c_size_t, [c_int32, c_int32]),
@@ -84,9 +89,16 @@ _SIGS: dict[str, tuple] = {
     "iq36_rms_norm": (c_int, [_P, c_int32, c_int32, _P, c_int32, c_float, _P, c_int32, _P]),
     "iq36_attn_prep": (c_int, [_P, _P, _P, _P, _P, c_float, _P, c_int32, c_int32, c_int32,
                                c_int32, c_float, _P, c_int32, _P, _P, _P, _P, _P]),
+    "iq36_attn_prep_batch": (c_int, [_P, _P, _P, _P, _P, c_float, _P, c_int32, c_int32, c_int32,
+                                     c_int32, c_int32, c_float, _P, c_int32, _P, _P, _P, _P, _P]),
+    "iq36_attn_prefill": (c_int, [_P, _P, _P, _P, c_int32, _P, c_int32, c_int32, c_int32, c_int32,
+                                  c_float, _P, _P, c_int32, _P]),
     "iq36_delta_prep": (c_int, [_P, c_int32, _P, _P, _P, _P, _P, _P, c_int32, _P, _P, _P, _P]),
     "iq36_delta_step": (c_int, [_P, _P, _P, _P, _P, _P, c_float, c_int32, c_int32, c_int32, _P,
                                 _P]),
+    "iq36_delta_prefill": (c_int, [_P, c_int32, c_int32, c_int32, c_int32, _P, _P, _P, _P,
+                                   c_int32, _P, _P, _P, _P, _P, c_float, _P, _P, c_size_t, _P]),
+    "iq36_delta_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "iq36_embed": (c_int, [_P, c_int32, c_int32, _P, _P, _P]),
     "iq36_decode_positions": (c_int, [_P, _P, c_int32, _P]),
     "iq36_argmax": (c_int, [_P, c_int32, _P, _P, c_size_t, _P]),

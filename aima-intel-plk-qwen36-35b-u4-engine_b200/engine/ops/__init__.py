@@ -425,6 +425,47 @@ def attn_prep(q_full, k, v, q_norm_w, k_norm_w, eps, pos_dev, block_table, k_cac
            q_out.data_ptr(), gate_out.data_ptr(), _stream(q_full.device))
 
 
+def attn_prep_batch(q_full, k, v, q_norm_w, k_norm_w, eps, pos_dev, block_table, k_cache,
+                    v_cache, q_out, gate_out, rope_dim: int = 64, rope_base: float = 1e7):
+    """attn_prep for T tokens at positions pos_dev + t: q_full [T, n_q*2*256],
+    k, v [T, n_kv*256], q_out, gate_out [T, n_q*256] (fp16, contiguous)."""
+    T = q_full.shape[0]
+    for t_, nm in ((q_full, "q_full"), (k, "k"), (v, "v"), (q_out, "q_out"),
+                   (gate_out, "gate_out")):
+        _cuda(t_, nm, torch.float16)
+        _need(t_.shape[0] == T, f"{nm} must have {T} rows")
+    nq = q_full[0].numel() // (2 * 256)
+    nkv = k[0].numel() // 256
+    N.call("iq36_attn_prep_batch", q_full.data_ptr(), k.data_ptr(), v.data_ptr(),
+           q_norm_w.data_ptr(), k_norm_w.data_ptr(), eps, pos_dev.data_ptr(), T, nq, nkv, 256,
+           rope_dim, rope_base, block_table.data_ptr(), k_cache.shape[1], k_cache.data_ptr(),
+           v_cache.data_ptr(), q_out.data_ptr(), gate_out.data_ptr(), _stream(q_full.device))
+
+
+def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 block_table: torch.Tensor, pos_dev: torch.Tensor, scale: float,
+                 gate: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of T prompt queries q [T, n_q, 256] (positions
+    pos_dev + t) over the fp16 paged cache; out [T, n_q, 256]."""
+    _cuda(q, "q", torch.float16)
+    _cuda(k_cache, "k_cache", torch.float16)
+    _cuda(v_cache, "v_cache", torch.float16)
+    _cuda(block_table, "block_table", torch.int32)
+    _cuda(pos_dev, "pos_dev", torch.int32)
+    _need(q.dim() == 3, "q must be [T, n_q, head_dim]")
+    T, nq, d = q.shape
+    bs, nkv = k_cache.shape[1], k_cache.shape[2]
+    if gate is not None:
+        _cuda(gate, "gate", torch.float16)
+    if out is None:
+        out = torch.empty(T, nq, d, dtype=out_dtype, device=q.device)
+    N.call("iq36_attn_prefill", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+           block_table.data_ptr(), bs, pos_dev.data_ptr(), T, nq, nkv, d, scale, _ptr(gate),
+           out.data_ptr(), _dtype_code(out.dtype), _stream(q.device))
+    return out
+
+
 def delta_prep(qkv, conv_state, conv_w, a, b, a_log, dt_bias, act_out, g_out, beta_out):
     N.call("iq36_delta_prep", qkv.data_ptr(), qkv.numel(), conv_state.data_ptr(),
            conv_w.data_ptr(), a.data_ptr(), b.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
@@ -437,6 +478,32 @@ def delta_step(act, g, beta, state, z, norm_w, eps, n_k_heads, n_v_heads, out,
     N.call("iq36_delta_step", act.data_ptr(), g.data_ptr(), beta.data_ptr(), state.data_ptr(),
            z.data_ptr(), norm_w.data_ptr(), eps, n_k_heads, n_v_heads, head_dim, out.data_ptr(),
            _stream(act.device))
+
+
+def delta_prefill_workspace(tokens: int, n_k_heads: int, n_v_heads: int,
+                            device) -> torch.Tensor:
+    n = N.lib().iq36_delta_prefill_workspace_bytes(tokens, n_k_heads, n_v_heads)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def delta_prefill(qkv, conv_state, conv_w, a, b, a_log, dt_bias, state, z, norm_w, eps,
+                  n_k_heads, n_v_heads, out, workspace=None, head_dim: int = 128):
+    """DeltaNet block over T tokens (qkv [T, C] fp16; a, b [T, >=nv] fp16 views
+    sharing one row stride; z, out [T, nv*D] fp16); conv_state and state are
+    updated in place as if the T tokens were decoded one by one."""
+    T = qkv.shape[0]
+    for t_, nm in ((qkv, "qkv"), (z, "z"), (out, "out")):
+        _cuda(t_, nm, torch.float16)
+    _need(a.stride(0) == b.stride(0) and a.stride(1) == 1 and b.stride(1) == 1,
+          "a and b must be row views with one common row stride")
+    if workspace is None:
+        workspace = delta_prefill_workspace(T, n_k_heads, n_v_heads, qkv.device)
+    N.call("iq36_delta_prefill", qkv.data_ptr(), T, n_k_heads, n_v_heads, head_dim,
+           conv_state.data_ptr(), conv_w.data_ptr(), a.data_ptr(), b.data_ptr(), a.stride(0),
+           a_log.data_ptr(), dt_bias.data_ptr(), state.data_ptr(), z.data_ptr(),
+           norm_w.data_ptr(), eps, out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+           _stream(qkv.device))
+    return out
 
 
 def embed(table: torch.Tensor, token_dev: torch.Tensor, h: torch.Tensor):

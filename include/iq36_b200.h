@@ -193,6 +193,28 @@ size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t 
 int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids, const float* weights,
                      int32_t k, const iq36_expert_bank* routed, void* out, int32_t out_dtype,
                      void* workspace, size_t workspace_bytes, iq36_stream_t stream);
+/* The MoE block of one decoder layer over T prompt tokens, fp32 residual
+ * [T, hidden] updated in place: router logits on RMSNorm(residual) (the
+ * iq36_router_logits kernel, so routing equals the decode step's), top-k
+ * selection (ids, weights [T, k]; logits [T, E] kept for inspection), the
+ * routed experts as in iq36_moe_prefill (x = fp16 RMSNorm(residual); fp16
+ * contributions summed in rank order, added to the residual), and the shared
+ * expert (when `shared` is set) as dense tcgen05 GEMMs: SwiGLU(x Wgu^T), then
+ * residual += fp16(sigmoid(x . w_shared_gate) * (act Wd^T)).
+ * run_qwen36_moe_ffn_layer (gguf_loader.cpp:5654-5782) over a prompt, grouped
+ * schedule of grouped_s8_u4_f16_contribution_moe.cl:13-222.
+ * Requirements: those of iq36_moe_prefill; the shared bank has the routed
+ * bank's hidden, intermediate and group. workspace:
+ * iq36_moe_layer_prefill_workspace_bytes. */
+int iq36_moe_layer_prefill(float* residual, int32_t T, int32_t hidden, const float* norm_weight,
+                           float norm_eps, const void* w_router_f16,
+                           const void* w_shared_gate_f16, int32_t k,
+                           const iq36_expert_bank* routed, const iq36_expert_bank* shared,
+                           int32_t* ids, float* weights, float* logits, void* workspace,
+                           size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_moe_layer_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
+                                              int32_t hidden, int32_t intermediate);
+
 /* Dense u4 GEMM for batched (prefill) projections: out[T, N] = x W^T with
  * W = (q - zp) * s (group 128 along K), fp16 operands on tcgen05 tensor cores,
  * fp32 accumulate. x is fp16 [T, K], or fp32 [T, K] optionally RMS-normalised
@@ -282,6 +304,31 @@ int iq36_attn_prep(const void* q_full_f16, const void* k_f16, const void* v_f16,
                    const int32_t* block_table, int32_t block_size, void* k_cache,
                    void* v_cache, void* q_out_f16, void* gate_out_f16, iq36_stream_t stream);
 
+/* iq36_attn_prep for `tokens` consecutive tokens at positions *pos_dev + t
+ * (t = 0..tokens-1) in one launch: per token, rows q_full [n_q, 2, D],
+ * k/v [n_kv, D], q_out/gate_out [n_q, D] (row-contiguous over tokens). The
+ * batched form of the reference's per-token prompt loop over this pre-step. */
+int iq36_attn_prep_batch(const void* q_full_f16, const void* k_f16, const void* v_f16,
+                         const float* q_norm_w, const float* k_norm_w, float eps,
+                         const int32_t* pos_dev, int32_t tokens, int32_t n_q_heads,
+                         int32_t n_kv_heads, int32_t head_dim, int32_t rope_dim,
+                         float rope_base, const int32_t* block_table, int32_t block_size,
+                         void* k_cache, void* v_cache, void* q_out_f16, void* gate_out_f16,
+                         iq36_stream_t stream);
+
+/* Causal prompt attention: queries q_f16 [T, n_q, D] at positions
+ * *pos_dev + t attend to cache keys 0 .. *pos_dev + t (K/V of the prompt
+ * already appended by iq36_attn_prep_batch); out [T, n_q, D] (f32 or f16) =
+ * softmax(q k^T * scale) v, times sigmoid(gate [T, n_q, D]) when gate_f16 is
+ * not NULL. Equal to iq36_paged_gqa_decode run for each prompt token in turn
+ * (run_qwen36_full_attention_core, gguf_loader.cpp:6071-6137; gate :6034-6069).
+ * head_dim 256, n_q_heads == 8 * n_kv_heads. Allocates nothing. */
+int iq36_attn_prefill(const void* q_f16, const void* k_cache, const void* v_cache,
+                      const int32_t* block_table, int32_t block_size, const int32_t* pos_dev,
+                      int32_t tokens, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                      float scale, const void* gate_f16, void* out, int32_t out_dtype,
+                      iq36_stream_t stream);
+
 /* DeltaNet pre-step for one token: causal depthwise conv (width 4, carried
  * state [C,4]) + SiLU with the fp16 rounding points of
  * engine/openvino/custom/iq36_linear_conv_swish.cl:12-64, and the gate/beta
@@ -301,6 +348,26 @@ int iq36_delta_prep(const void* qkv_f16, int32_t channels, float* conv_state,
 int iq36_delta_step(const void* qkv_act_f16, const float* g, const float* beta, float* state,
                     const void* z_f16, const float* norm_w, float eps, int32_t n_k_heads,
                     int32_t n_v_heads, int32_t head_dim, void* out_f16, iq36_stream_t stream);
+
+/* The DeltaNet block over T prompt tokens: the arithmetic of iq36_delta_prep
+ * followed by iq36_delta_step for tokens 0..T-1 in order (conv state and
+ * recurrent state carried in and out), in four launches. Replaces the
+ * per-token loop over the reference's linear-attention layer during prompt
+ * processing (iq36_linear_conv_swish.cl:12-64, iq36_gated_delta_net.cl:36-150,
+ * gguf_loader.cpp:4770-4786 and :4875-4912).
+ * qkv_f16 [T, (2nk+nv)*D] (row-contiguous); a_f16/b_f16 [T, *] with row
+ * stride gate_stride >= nv halves (the a and b projections may share one
+ * padded matrix); z_f16 [T, nv*D]; out_f16 [T, nv*D]. head_dim must be 128;
+ * nv % nk == 0; nv <= 256. workspace: iq36_delta_prefill_workspace_bytes. */
+int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n_k_heads,
+                       int32_t n_v_heads, int32_t head_dim, float* conv_state,
+                       const float* conv_w, const void* a_f16, const void* b_f16,
+                       int32_t gate_stride, const float* a_log, const float* dt_bias,
+                       float* state, const void* z_f16, const float* norm_w, float eps,
+                       void* out_f16, void* workspace, size_t workspace_bytes,
+                       iq36_stream_t stream);
+size_t iq36_delta_prefill_workspace_bytes(int32_t tokens, int32_t n_k_heads,
+                                          int32_t n_v_heads);
 
 /* Decode-loop position state on the device: if advance, *pos_dev += 1; then
  * *ctx_dev = *pos_dev + 1 (the attention context of the step at *pos_dev).
