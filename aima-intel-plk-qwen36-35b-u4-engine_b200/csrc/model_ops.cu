@@ -313,10 +313,12 @@ __global__ void __cluster_dims__(1, 8, 1) __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
+// Row y of h [T, hidden] = float(table[tok[y]]) (grid y = token; decode: T = 1).
 __global__ void embed_kernel(const __half* table, int hidden, const int32_t* tok, float* h) {
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < hidden) h[i] = __half2float(table[(size_t)(*tok) * hidden + i]);
+  if (i < hidden)
+    h[(size_t)blockIdx.y * hidden + i] = __half2float(table[(size_t)tok[blockIdx.y] * hidden + i]);
 }
 
 // Greedy top-1 keys: (order-preserving fp32 bits, inverted id); the larger key
@@ -503,6 +505,17 @@ extern "C" int iq36_embed(const void* table_f16, int32_t vocab, int32_t hidden,
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
+extern "C" int iq36_embed_batch(const void* table_f16, int32_t vocab, int32_t hidden,
+                                const int32_t* tokens_dev, int32_t T, float* h,
+                                iq36_stream_t stream) {
+  if (!table_f16 || !tokens_dev || !h) return IQ36_ERR_ARG;
+  if (vocab < 1 || hidden < 1 || T < 1 || T > 65535) return IQ36_ERR_SHAPE;
+  const cudaError_t e = launch(embed_kernel, dim3(ceil_div(hidden, 256), T), dim3(256), 0,
+                               as_stream(stream), reinterpret_cast<const __half*>(table_f16),
+                               hidden, tokens_dev, h);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
 extern "C" size_t iq36_argmax_workspace_bytes(void) { return kArgmaxBlocks * sizeof(uint64_t); }
 
 extern "C" int iq36_argmax(const float* logits, int32_t n, int32_t* token_out, void* workspace,
@@ -547,7 +560,7 @@ namespace iq36 {
 __global__ void decode_positions_kernel(int32_t* pos, int32_t* ctx, int advance) {
   pdl_wait();
   if (threadIdx.x == 0) {
-    const int p = *pos + (advance ? 1 : 0);
+    const int p = *pos + advance;
     *pos = p;
     *ctx = p + 1;
   }
@@ -557,6 +570,7 @@ __global__ void decode_positions_kernel(int32_t* pos, int32_t* ctx, int advance)
 extern "C" int iq36_decode_positions(int32_t* pos_dev, int32_t* ctx_dev, int32_t advance,
                                      iq36_stream_t stream) {
   if (!pos_dev || !ctx_dev) return IQ36_ERR_ARG;
+  if (advance < 0) return IQ36_ERR_SHAPE;
   const cudaError_t e = launch(decode_positions_kernel, dim3(1), dim3(32), 0, as_stream(stream),
                                pos_dev, ctx_dev, (int)advance);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;

@@ -21,6 +21,8 @@
 //                    the weighted sum over slots runs in rank order in shared
 //                    memory (deterministic), shared expert added last.
 
+#include <atomic>
+
 #include "launch.cuh"
 #include "u4_core.cuh"
 
@@ -106,6 +108,113 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
     if (lane == 0) {
       if (row < E) logits[(size_t)tok * E + row] = acc;
       else slogit[tok] = acc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Router over T prompt tokens. Same arithmetic, bit for bit, as
+// router_logits_kernel run once per token: the RMS-normalised fp16 input of
+// stage_x_plain (256-thread reduction order), the per-lane chunk order and
+// fp32 FMA sequence of its dot product, and the same warp butterfly.
+
+// xn[t] = fp16(x[t] * rsqrt(mean(x[t]^2) + eps) * nw). One warp per token
+// replays the reduction of stage_x_plain's 256 threads: virtual thread
+// 32w + lane sums x[i]^2 over i = 32w + lane + 256m in order, each virtual
+// warp is butterfly-summed, then the 8 warp sums are butterfly-summed as
+// lanes 0..7 of one warp.
+__global__ void __launch_bounds__(256) x_norm_plain_kernel(const float* x32, const float* nw,
+                                                           float eps, int T, int H,
+                                                           __half* xn) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t < T) {
+    const float* x = x32 + (size_t)t * H;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float p = 0.0f;
+      for (int i = 32 * w + lane; i < H; i += 256) p = fmaf(x[i], x[i], p);
+      p = warp_sum(p);
+      if (lane == w) v = p;
+    }
+    v = warp_sum(v);
+    const float scale = rsqrtf(v / (float)H + eps);
+    __half* o = xn + (size_t)t * H;
+    for (int i = lane; i < H; i += 32) o[i] = __float2half_rn(x[i] * scale * nw[i]);
+  }
+  pdl_launch_dependents();
+}
+
+constexpr int kRbTok = 32;   // tokens per CTA (staged in shared memory)
+constexpr int kRbRows = 16;  // router rows per CTA: 2 per warp
+
+// logits[t, e] (and slogit[t] for the extra shared-gate row) for a tile of 32
+// tokens x 16 rows; each warp keeps its two weight rows in registers.
+// Requires H % 256 == 0, H <= 2048.
+__global__ void __launch_bounds__(256) router_logits_batch_kernel(const __half* xn, int T, int H,
+                                                                  const __half* W, int E,
+                                                                  const __half* wsg,
+                                                                  float* logits, float* slogit) {
+  extern __shared__ __align__(16) uint4 xs4[];  // [kRbTok][H / 8]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * kRbTok;
+  const int nt = min(kRbTok, T - t0);
+  const int hc = H / 8, nch = H / 256;
+  const int rows = E + (wsg != nullptr ? 1 : 0);
+  const int r0 = blockIdx.x * kRbRows + 2 * warp;
+  uint4 w[2][8];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int r = r0 + q;
+    const __half* wr = r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[q][j] = (wr != nullptr && j < nch) ? ld_stream_v4(wr + (lane + 32 * j) * 8)
+                                           : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  for (int i = threadIdx.x; i < nt * hc; i += blockDim.x)
+    cp_async_16(smem_u32(xs4 + i), xn + (size_t)t0 * H + (size_t)i * 8, 16);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  pdl_launch_dependents();
+  if (r0 >= rows) return;
+  auto dot8 = [](const uint4& wv, const uint4& xv, float& acc) {
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 wf = __half22float2(wh[j]);
+      const float2 xf = __half22float2(xh[j]);
+      acc = fmaf(wf.x, xf.x, acc);
+      acc = fmaf(wf.y, xf.y, acc);
+    }
+  };
+  for (int tt = 0; tt < nt; ++tt) {
+    float a0 = 0.f, a1 = 0.f;
+    const uint4* xr = xs4 + (size_t)tt * hc;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < nch) {
+        const uint4 xv = xr[lane + 32 * j];
+        dot8(w[0][j], xv, a0);
+        dot8(w[1][j], xv, a1);
+      }
+    }
+    a0 = warp_sum(a0);
+    a1 = warp_sum(a1);
+    if (lane == 0) {
+      const int t = t0 + tt;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int r = r0 + q;
+        const float a = q ? a1 : a0;
+        if (r < E) logits[(size_t)t * E + r] = a;
+        else if (r == E && wsg != nullptr) slogit[t] = a;
+      }
     }
   }
 }
@@ -480,6 +589,38 @@ int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw,
                                reinterpret_cast<const __half*>(x_f16), x_f32, nw, eps, H,
                                reinterpret_cast<const __half*>(w_router), E,
                                reinterpret_cast<const __half*>(w_sg), logits, slogit);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+// xn [T, H] fp16 = the router's normalised input; logits / slogit as
+// router_logits_launch with x_f32 + nw, bit for bit.
+int router_logits_batch_launch(const float* x32, const float* nw, float eps, int T, int H,
+                               const void* w_router, int E, const void* w_sg, float* logits,
+                               float* slogit, __half* xn, cudaStream_t stream) {
+  if (!x32 || !nw || !w_router || !logits || !xn || T < 1 || E < 1) return IQ36_ERR_ARG;
+  if (w_sg && !slogit) return IQ36_ERR_ARG;
+  if (H < 256 || H % 256 || H > 2048) return IQ36_ERR_SHAPE;
+  if (!aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) || !aligned(xn, 16))
+    return IQ36_ERR_ALIGN;
+  const size_t smem = (size_t)kRbTok * H * 2;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (!attr_set[dev].load()) {
+    if (cudaFuncSetAttribute(router_logits_batch_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRbTok * 2048 * 2) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+    attr_set[dev].store(true);
+  }
+  cudaError_t e = launch(x_norm_plain_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream, x32, nw,
+                         eps, T, H, xn);
+  const int rows = E + (w_sg ? 1 : 0);
+  if (e == cudaSuccess)
+    e = launch(router_logits_batch_kernel, dim3(ceil_div(rows, kRbRows), ceil_div(T, kRbTok)),
+               dim3(256), smem, stream, (const __half*)xn, T, H,
+               reinterpret_cast<const __half*>(w_router), E,
+               reinterpret_cast<const __half*>(w_sg), logits, slogit);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 

@@ -1131,8 +1131,9 @@ extern "C" int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* id
 
 // ---------------------------------------------------------------------------
 // The MoE block of one layer over T prompt tokens, residual updated in place:
-// router logits on the RMS-normalised fp32 residual (same kernel and order of
-// sums as the decode step, so the routing matches token for token), top-k
+// router logits on the RMS-normalised fp32 residual (same arithmetic, bit for
+// bit, as the decode step's router, so the routing matches token for token;
+// the normalised fp16 input also feeds the experts), top-k
 // selection, the grouped routed experts (fp16 contributions summed in rank
 // order into the residual), and the shared expert as two dense u4 GEMMs
 // (gate_up with SwiGLU, then down scaled by sigmoid(shared logit) and added to
@@ -1145,6 +1146,9 @@ int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw,
                          float* slogit, cudaStream_t stream);
 int router_select_launch(const float* logits, int T, int E, int k, int32_t* ids, float* weights,
                          cudaStream_t stream);
+int router_logits_batch_launch(const float* x32, const float* nw, float eps, int T, int H,
+                               const void* w_router, int E, const void* w_sg, float* logits,
+                               float* slogit, __half* xn, cudaStream_t stream);
 
 struct MoeLayerPfLayout {
   size_t slogit, xn, act, gemm, moe, total;
@@ -1192,12 +1196,10 @@ extern "C" int iq36_moe_layer_prefill(float* residual, int32_t T, int32_t hidden
   __half* xn = reinterpret_cast<__half*>(ws + L.xn);
   __half* act = reinterpret_cast<__half*>(ws + L.act);
   const cudaStream_t s = as_stream(stream);
-  int st = router_logits_launch(nullptr, residual, norm_weight, norm_eps, T, H, w_router_f16, E,
-                                shared ? w_shared_gate_f16 : nullptr, logits,
-                                shared ? slogit : nullptr, s);
+  int st = router_logits_batch_launch(residual, norm_weight, norm_eps, T, H, w_router_f16, E,
+                                      shared ? w_shared_gate_f16 : nullptr, logits,
+                                      shared ? slogit : nullptr, xn, s);
   if (st == IQ36_OK) st = router_select_launch(logits, T, E, k, ids, weights, s);
-  if (st == IQ36_OK)
-    st = iq36_rms_norm(residual, T, H, norm_weight, H, norm_eps, xn, IQ36_F16, stream);
   if (st == IQ36_OK)
     st = moe_prefill_launch(xn, IQ36_F16, T, ids, weights, k, routed, residual, IQ36_F32, 1,
                             ws + L.moe, L.total - L.moe, s);

@@ -100,6 +100,7 @@ _SIGS: dict[str, tuple] = {
                                    c_int32, _P, _P, _P, _P, _P, c_float, _P, _P, c_size_t, _P]),
     "iq36_delta_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "iq36_embed": (c_int, [_P, c_int32, c_int32, _P, _P, _P]),
+    "iq36_embed_batch": (c_int, [_P, c_int32, c_int32, _P, c_int32, _P, _P]),
     "iq36_decode_positions": (c_int, [_P, _P, c_int32, _P]),
     "iq36_argmax": (c_int, [_P, c_int32, _P, _P, c_size_t, _P]),
     "iq36_argmax_workspace_bytes": (c_size_t, []),

@@ -307,6 +307,38 @@ def moe_layer_decode(residual: torch.Tensor, norm_weight: torch.Tensor, w_router
            _stream(dev))
 
 
+def moe_layer_prefill_workspace(T: int, k: int, num_experts: int, hidden: int,
+                                intermediate: int, device) -> torch.Tensor:
+    n = N.lib().iq36_moe_layer_prefill_workspace_bytes(T, k, num_experts, hidden, intermediate)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def moe_layer_prefill(residual: torch.Tensor, norm_weight: torch.Tensor, w_router: torch.Tensor,
+                      w_shared_gate: torch.Tensor | None, routed: ExpertBank,
+                      shared: ExpertBank | None, ids: torch.Tensor, weights: torch.Tensor,
+                      logits: torch.Tensor, workspace: torch.Tensor | None = None, k: int = 8,
+                      norm_eps: float = 1e-6) -> None:
+    """The MoE FFN block over T prompt tokens on the fp32 residual [T, H] (in
+    place): RMSNorm -> router -> top-k -> grouped routed experts + shared
+    expert, added to the residual. ids / weights [T, k] and logits [T, E]
+    receive the router outputs."""
+    _cuda(residual, "residual", torch.float32)
+    _cuda(ids, "ids", torch.int32)
+    _cuda(weights, "weights", torch.float32)
+    _cuda(logits, "logits", torch.float32)
+    dev = residual.device
+    T, h = residual.shape
+    if workspace is None:
+        workspace = moe_layer_prefill_workspace(T, k, routed.num_experts, h, routed.intermediate,
+                                                dev)
+    rb = routed.c()
+    sb = shared.c() if shared is not None else None
+    N.call("iq36_moe_layer_prefill", residual.data_ptr(), T, h, norm_weight.data_ptr(), norm_eps,
+           w_router.data_ptr(), _ptr(w_shared_gate), k, ctypes.byref(rb),
+           ctypes.byref(sb) if sb is not None else None, ids.data_ptr(), weights.data_ptr(),
+           logits.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream(dev))
+
+
 def moe_expert_ffn_prefill(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                            routed: ExpertBank, out_dtype: torch.dtype = torch.float32,
                            out: torch.Tensor | None = None) -> torch.Tensor:
@@ -509,6 +541,14 @@ def delta_prefill(qkv, conv_state, conv_w, a, b, a_log, dt_bias, state, z, norm_
 def embed(table: torch.Tensor, token_dev: torch.Tensor, h: torch.Tensor):
     N.call("iq36_embed", table.data_ptr(), table.shape[0], table.shape[1], token_dev.data_ptr(),
            h.data_ptr(), _stream(table.device))
+
+
+def embed_batch(table: torch.Tensor, tokens_dev: torch.Tensor, h: torch.Tensor):
+    """h [T, H] fp32 = embedding rows of tokens_dev [T] int32."""
+    _cuda(tokens_dev, "tokens", torch.int32)
+    _cuda(h, "h", torch.float32)
+    N.call("iq36_embed_batch", table.data_ptr(), table.shape[0], table.shape[1],
+           tokens_dev.data_ptr(), tokens_dev.numel(), h.data_ptr(), _stream(table.device))
 
 
 def argmax(logits: torch.Tensor, token_out: torch.Tensor, workspace: torch.Tensor | None = None):

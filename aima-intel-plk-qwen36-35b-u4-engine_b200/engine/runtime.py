@@ -122,6 +122,7 @@ class SyntheticWeights:
                 L["z"] = self._u4(c.nv * c.dk, h, l, T_Z)
                 L["a"] = self._u4(c.nv, h, l, T_A)
                 L["b"] = self._u4(c.nv, h, l, T_B)
+                L["ab"] = self._gate_pair(L["a"], L["b"])
                 L["out"] = self._u4(h, c.nv * c.dk, l, T_OUT)
                 L["conv_w"] = self._f32(ch * c.conv, l, T_CONV)
                 L["a_log"] = self._f32(c.nv, l, T_ALOG)
@@ -158,6 +159,19 @@ class SyntheticWeights:
 
     def _f16(self, shape, layer, slot):
         return self._fill(torch.empty(shape, dtype=torch.float16, device=self.dev), layer, slot, 0)
+
+    @staticmethod
+    def _gate_pair(a: ops.U4Weight, b: ops.U4Weight) -> ops.U4Weight:
+        """[a; b; 0] padded to 256 rows: one batched GEMM (whose row count is a
+        multiple of 256) produces both DeltaNet gate projections for the prompt.
+        Zero scales make the padding rows exactly 0."""
+        n = a.rows + b.rows
+        pad = (-n) % 256
+        w = torch.cat([a.weight, b.weight, a.weight.new_zeros(pad, a.weight.shape[1])])
+        sc = torch.cat([a.scale, b.scale, a.scale.new_zeros(pad, a.scale.shape[1])])
+        zp = torch.cat([a.zp.view(-1), b.zp.view(-1),
+                        a.zp.new_zeros(pad * a.scale.shape[1] // 2)])
+        return ops.U4Weight(w, sc, zp, a.group)
 
     def _u4(self, rows, k, layer, slot) -> ops.U4Weight:
         g = self.cfg.group
@@ -224,6 +238,7 @@ class Qwen36Runtime:
         self.ws_moe = ops.moe_layer_workspace(c.topk, h, c.inter, dev)
         self.ws_argmax = torch.empty(N.lib().iq36_argmax_workspace_bytes(), dtype=torch.uint8,
                                      device=dev)
+        self._pf: dict | None = None  # batched-prefill buffers (sized on first use)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(device=dev)
         self.launches_per_step = 0
@@ -347,6 +362,111 @@ class Qwen36Runtime:
             self.graph.replay()
         else:
             self.enqueue_step()
+
+    # -- batched prefill ------------------------------------------------------
+    def _prefill_buffers(self, T: int) -> dict:
+        if self._pf is not None and self._pf["T"] >= T:
+            return self._pf
+        c, dev = self.cfg, self.dev
+        f16, f32, i32 = torch.float16, torch.float32, torch.int32
+        h, hd = c.hidden, c.head_dim
+        ch = (2 * c.nk + c.nv) * c.dk
+        gemm_k = max(h, c.nq * hd, c.nv * c.dk)
+        self._pf = {
+            "T": T,
+            "tok": torch.empty(T, dtype=i32, device=dev),
+            "h": torch.empty(T, h, dtype=f32, device=dev),
+            "qfull": torch.empty(T, 2 * c.nq * hd, dtype=f16, device=dev),
+            "k": torch.empty(T, c.nkv * hd, dtype=f16, device=dev),
+            "v": torch.empty(T, c.nkv * hd, dtype=f16, device=dev),
+            "q": torch.empty(T, c.nq * hd, dtype=f16, device=dev),
+            "gate": torch.empty(T, c.nq * hd, dtype=f16, device=dev),
+            "attn": torch.empty(T, c.nq * hd, dtype=f16, device=dev),
+            "qkv": torch.empty(T, ch, dtype=f16, device=dev),
+            "z": torch.empty(T, c.nv * c.dk, dtype=f16, device=dev),
+            "ab": torch.empty(T, 256 * ((2 * c.nv + 255) // 256), dtype=f16, device=dev),
+            "dout": torch.empty(T, c.nv * c.dk, dtype=f16, device=dev),
+            "ids": torch.empty(T, c.topk, dtype=i32, device=dev),
+            "wts": torch.empty(T, c.topk, dtype=f32, device=dev),
+            "logits_r": torch.empty(T, c.experts, dtype=f32, device=dev),
+            "gws": torch.empty(N.lib().iq36_u4_gemm_workspace_bytes(T, gemm_k), dtype=torch.uint8,
+                               device=dev),
+            "dws": ops.delta_prefill_workspace(T, c.nk, c.nv, dev),
+            "mws": ops.moe_layer_prefill_workspace(T, c.topk, c.experts, h, c.inter, dev),
+        }
+        return self._pf
+
+    def enqueue_prefill_chunk(self, T: int) -> int:
+        """Enqueue the batched forward of the T prompt tokens already in the
+        prefill buffer's ``tok`` rows, at positions pos .. pos+T-1: every
+        projection as a tcgen05 u4 GEMM over the T rows, the DeltaNet and
+        attention cores over the whole chunk, the MoE block as the grouped
+        prefill; then the LM head and argmax of the last row, and pos += T.
+        Returns the number of launches."""
+        c, W, B = self.cfg, self.w, self._pf
+        assert B is not None and B["T"] >= T
+        hd = c.head_dim
+        sl = lambda name: B[name][:T]
+        h = sl("h")
+        ws = B["gws"]
+        ops.embed_batch(W.embed, sl("tok"), h)
+        n = 1
+        for l in range(c.layers):
+            L = W.layers[l]
+            if c.is_attn(l):
+                for name, wt in (("qfull", L["q"]), ("k", L["k"]), ("v", L["v"])):
+                    ops.u4_gemm(h, wt, out=sl(name), norm_weight=L["in_norm"], norm_eps=c.eps,
+                                workspace=ws)
+                kc, vc = self.kv[l]
+                ops.attn_prep_batch(sl("qfull"), sl("k"), sl("v"), L["qn"], L["kn"], c.eps,
+                                    self.pos, self.block_table, kc, vc, sl("q"), sl("gate"),
+                                    rope_dim=c.rope_dim, rope_base=c.rope_base)
+                ops.attn_prefill(sl("q").view(T, c.nq, hd), kc, vc, self.block_table, self.pos,
+                                 1.0 / math.sqrt(hd), gate=sl("gate").view(T, c.nq, hd),
+                                 out=sl("attn").view(T, c.nq, hd))
+                ops.u4_gemm(sl("attn"), L["o"], out=h, accumulate=True, workspace=ws)
+                n += 10
+            else:
+                for name, wt in (("qkv", L["qkv"]), ("z", L["z"]), ("ab", L["ab"])):
+                    ops.u4_gemm(h, wt, out=sl(name), norm_weight=L["in_norm"], norm_eps=c.eps,
+                                workspace=ws)
+                ab = sl("ab")
+                ops.delta_prefill(sl("qkv"), self.conv_state[l], L["conv_w"], ab[:, :c.nv],
+                                  ab[:, c.nv:2 * c.nv], L["a_log"], L["dt_bias"],
+                                  self.rec_state[l], sl("z"), L["dnorm"], c.eps, c.nk, c.nv,
+                                  sl("dout"), workspace=B["dws"])
+                ops.u4_gemm(sl("dout"), L["out"], out=h, accumulate=True, workspace=ws)
+                n += 12
+            ops.moe_layer_prefill(h, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                                  L["shared"], sl("ids"), sl("wts"), sl("logits_r"),
+                                  workspace=B["mws"], k=c.topk, norm_eps=c.eps)
+            n += 14
+        ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=h[T - 1],
+                            norm_weight=W.final_norm, norm_eps=c.eps)
+        ops.argmax(self.logits, self.token, self.ws_argmax)
+        N.call("iq36_decode_positions", self.pos.data_ptr(), self.ctx.data_ptr(), T,
+               ops._stream(self.dev))
+        return n + 4
+
+    def prefill_batched(self, tokens: list[int] | torch.Tensor, chunk: int = 8192) -> int:
+        """Batched prefill of the prompt in chunks of at most ``chunk`` tokens
+        (state, KV cache and position carry across chunks); leaves the greedy
+        token after the last prompt token in ``self.token``. Returns the number
+        of launches enqueued. The reference prefills in tile-aligned chunks of
+        8192/4096/2048/32 tokens and finishes the last 0..31 tokens with
+        one-token calls (engine/service/iq36_server/runtime.py:25, 334-352,
+        501); every kernel here takes any token count, so a chunk is simply up
+        to 8192 tokens and the tail needs no special case."""
+        toks = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1)
+        total = toks.numel()
+        B = self._prefill_buffers(min(chunk, total))
+        src = toks if toks.is_cuda else toks.pin_memory()
+        n = 0
+        for s0 in range(0, total, chunk):
+            T = min(chunk, total - s0)
+            B["tok"][:T].copy_(src[s0:s0 + T], non_blocking=True)
+            n += self.enqueue_prefill_chunk(T)
+        return n
 
     # -- host loop (reference runtime.py:461-585) ----------------------------
     def prefill(self, tokens: list[int] | torch.Tensor, keep_logits: bool = False):

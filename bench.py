@@ -19,7 +19,9 @@ OpenVINO is not installable here) on the host cores, same metric.
 Multi-GPU: replicas only (each rank decodes its own sequence; no collective on
 the data path), value summed over ranks.
 
-Other workloads: --workload moe_prefill (grouped MoE
+Other workloads: --workload prefill (BASELINE config 4 prefill tok/s: the batched
+prefill of a --ctx-token prompt, 4096 or 32768; a step is one whole prompt),
+--workload moe_prefill (grouped MoE
 prefill; replicas at --gpus > 1, expert-parallel over NCCL with --ep) and --workload gemv
 (one u4 GEMV per step, --rows / --k for other shapes).
 """
@@ -45,6 +47,7 @@ for p in (str(ROOT), str(PKG)):
 BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
 PUBLISHED_DECODE_4K = 50.57  # reference's published figure: Arc B390, 4k prompt, batch-1 decode tok/s
+PUBLISHED_PREFILL = {4096: 2367.89, 32768: 2065.28}  # reference prefill tok/s, Arc B390
 
 
 def peaks() -> tuple[float, str]:
@@ -228,11 +231,13 @@ def run_ours(args, world, rank, local) -> None:
     gen = torch.Generator().manual_seed(4096 + rank)
     prompt = torch.randint(0, cfg.vocab, (args.ctx,), generator=gen, dtype=torch.int32)
 
-    # prefill through the same captured step (token-serial)
+    # batched prefill of the prompt (one untimed pass sizes the buffers)
+    rt.prefill_batched(prompt)
+    rt.reset()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    rt.prefill(prompt)
+    rt.prefill_batched(prompt)
     e1.record()
     torch.cuda.synchronize(dev)
     prefill_s = e0.elapsed_time(e1) / 1e3
@@ -322,7 +327,8 @@ def run_ours(args, world, rank, local) -> None:
                    "ctx": args.ctx, "decode_steps": args.steps, "parallelism": "replicas",
                    "l2": "inputs larger than L2 (~1.77 GB of weights per step)",
                    "prefill_tok_s": round(world * args.ctx / max_over_ranks(prefill_s, world), 1),
-                   "prefill_mode": "token-serial through the decode graph",
+                   "prefill_mode": "batched: tcgen05 u4 GEMMs, DeltaNet scan, causal "
+                                   "flash attention, grouped MoE; one pass, device-timed",
                    "step_bytes": step_bytes,
                    "step_hbm_gbs": round(step_gbs, 1),
                    "step_hbm_frac": round(step_gbs / hbm, 4)},
@@ -340,6 +346,125 @@ def run_ours(args, world, rank, local) -> None:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ctx, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_prefill(args, world, rank, local) -> None:
+    """BASELINE config 4 prefill: the batched prefill of a seeded uniform-random
+    prompt of --ctx tokens (4096 or 32768) through the full 40-layer model,
+    from an empty state. A step is one whole prompt; the state is reset
+    between steps outside the timed region. value: prompt tokens/s (token ids
+    already on the device); e2e: token ids from pinned host memory and the
+    greedy next token read back, every step."""
+    import torch
+    from engine.runtime import ModelConfig, Qwen36Runtime
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig()
+    rt = Qwen36Runtime(cfg, seed=1234, max_ctx=args.ctx + 32, device=dev)
+    gen = torch.Generator().manual_seed(4096 + rank)
+    prompt = torch.randint(0, cfg.vocab, (args.ctx,), generator=gen, dtype=torch.int32)
+    dprompt = prompt.to(dev)
+    launches = 0
+    for _ in range(args.warmup):
+        rt.reset()
+        launches = rt.prefill_batched(dprompt)
+    torch.cuda.synchronize(dev)
+    if args.profile_step:
+        rt.reset()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.start()
+        rt.prefill_batched(dprompt)
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "workload": "prefill", "ctx": args.ctx}))
+        return
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    total = 0.0
+    for _ in range(args.steps):
+        rt.reset()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        rt.prefill_batched(dprompt)
+        e.record()
+        e.synchronize()
+        total += s.elapsed_time(e) / 1e3
+    barrier(world)
+    clocks = sampler.stop()
+    per_step = max_over_ranks(total / args.steps, world)
+    # e2e through the public API: host token ids in, greedy next token out
+    pin_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    t_e2e = 0.0
+    for _ in range(args.steps):
+        rt.reset()
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        rt.prefill_batched(prompt)
+        pin_out.copy_(rt.token, non_blocking=True)
+        e.record()
+        e.synchronize()
+        t_e2e += s.elapsed_time(e) / 1e3
+    t_e2e = max_over_ranks(t_e2e / args.steps, world)
+    # dominant kernel group: the MoE block of one layer over the whole prompt
+    # (router + grouped routed experts + shared expert), timed alone
+    T = min(args.ctx, 8192)
+    h = torch.randn(T, cfg.hidden, device=dev, generator=torch.Generator(dev).manual_seed(3))
+    L = rt.w.layers[0]
+    from engine import ops
+    B = rt._prefill_buffers(T)
+    ids, wts, lg = B["ids"][:T], B["wts"][:T], B["logits_r"][:T]
+
+    def moe():
+        ops.moe_layer_prefill(h, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                              L["shared"], ids, wts, lg, workspace=B["mws"], k=cfg.topk)
+    for _ in range(3):
+        moe()
+    reps = 10
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        moe()
+    e.record()
+    torch.cuda.synchronize(dev)
+    moe_s = s.elapsed_time(e) / 1e3 / reps
+    flops = T * (cfg.topk * 2 * (2 * cfg.inter * cfg.hidden + cfg.hidden * cfg.inter)
+                 + 2 * (2 * cfg.shared_inter * cfg.hidden + cfg.hidden * cfg.shared_inter))
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    tflops = flops / moe_s / 1e12
+    line = {
+        "metric": METRIC, "value": round(world * args.ctx / per_step, 1), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(args.ctx / per_step / PUBLISHED_PREFILL.get(args.ctx, float("nan")),
+                             2) if args.ctx in PUBLISHED_PREFILL else None,
+        "dtype": "u4xf16", "data": "synthetic",
+        "config": {"workload": f"config4 batch-1 prefill of a {args.ctx}-token prompt "
+                               "(Qwen3.6-35B-A3B-shaped, random-init u4 g128), batched",
+                   "ctx": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (17.6 GB of weights per pass)",
+                   "chunk_tokens": 8192},
+        "e2e": {"value": round(world * args.ctx / t_e2e, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": args.ctx * 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches * args.steps,
+        "roofline": {"bound": "tensor",
+                     "kernel": "MoE block of one layer over the prompt (router, grouped "
+                               "experts, shared expert; 14 launches), timed alone",
+                     "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "traffic": None,
+                     "tokens": T, "ms": round(moe_s * 1e3, 3)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.ctx // 2, os.cpu_count() or 1)
+        line["cpu_baseline"]["sample"] += " (prefill: the same per-token work at the mean context)"
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -585,7 +710,8 @@ def run_gemv(args, world, rank, local) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["decode", "moe_prefill", "gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "moe_prefill", "gemv"],
+                    default="decode")
     ap.add_argument("--rows", type=int, default=1024, help="output rows for --workload gemv")
     ap.add_argument("--k", type=int, default=2048, help="input length for --workload gemv")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload moe_prefill")
@@ -605,6 +731,8 @@ def main() -> None:
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "prefill":
+            run_prefill(args, world, rank, local)
         elif args.workload == "moe_prefill":
             run_moe_prefill(args, world, rank, local)
         elif args.workload == "gemv":

@@ -369,16 +369,23 @@ int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n_k_heads,
 size_t iq36_delta_prefill_workspace_bytes(int32_t tokens, int32_t n_k_heads,
                                           int32_t n_v_heads);
 
-/* Decode-loop position state on the device: if advance, *pos_dev += 1; then
+/* Decode-loop position state on the device: *pos_dev += advance (1 after a
+ * decode step, the prompt length after a batched prefill, 0 to refresh); then
  * *ctx_dev = *pos_dev + 1 (the attention context of the step at *pos_dev).
  * Lets one captured CUDA graph serve every step of the loop
- * (the reference's per-token loop: engine/service/iq36_server/runtime.py:533-561). */
+ * (the reference's per-token loop: engine/service/iq36_server/runtime.py:533-561).
+ * advance < 0 returns IQ36_ERR_SHAPE. */
 int iq36_decode_positions(int32_t* pos_dev, int32_t* ctx_dev, int32_t advance,
                           iq36_stream_t stream);
 
 /* h[:] = float(embedding[*token_dev, :]) (fp16 table [vocab, H]). */
 int iq36_embed(const void* table_f16, int32_t vocab, int32_t hidden, const int32_t* token_dev,
                float* h, iq36_stream_t stream);
+
+/* h[t, :] = float(embedding[tokens_dev[t], :]) for t < T (1 <= T <= 65535):
+ * the prompt's embedding rows for the batched prefill. */
+int iq36_embed_batch(const void* table_f16, int32_t vocab, int32_t hidden,
+                     const int32_t* tokens_dev, int32_t T, float* h, iq36_stream_t stream);
 
 /* Greedy top-1 over fp32 logits, lowest id on ties: per-block maxima of the
  * 64-bit key (order-preserving fp32 bits, inverted id), then one merge block

@@ -43,3 +43,19 @@ def _no_device_wait_timeouts(request):
     torch.cuda.synchronize()
     n = _native.wait_timeouts(reset=True)
     assert n == 0, f"{n} bounded device waits gave up during this test"
+
+
+@pytest.fixture(scope="session")
+def config1():
+    """BASELINE config 1 weights: 256 experts (gate_up [1024, 2048], down
+    [2048, 512], u4 g128), one shared expert, fp16 router and shared gate."""
+    import numpy as np
+    from helpers import make_bank
+    rng = np.random.default_rng(101)
+    h, i, e = 2048, 512, 256
+    bank = make_bank(rng, e, h, i)
+    shared = make_bank(rng, 1, h, i)
+    w_router = (rng.standard_normal((e, h)) * 0.02).astype(np.float16)
+    w_sg = (rng.standard_normal((1, h)) * 0.02).astype(np.float16)
+    x = rng.standard_normal(h).astype(np.float16)
+    return dict(bank=bank, shared=shared, w_router=w_router, w_sg=w_sg, x=x)

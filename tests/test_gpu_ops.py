@@ -130,18 +130,6 @@ def test_router_select_ties_and_batches(cuda):
 # (2a) MoE decode block
 
 
-@pytest.fixture(scope="module")
-def config1():
-    rng = np.random.default_rng(101)
-    h, i, e = 2048, 512, 256
-    bank = make_bank(rng, e, h, i)
-    shared = make_bank(rng, 1, h, i)
-    w_router = (rng.standard_normal((e, h)) * 0.02).astype(np.float16)
-    w_sg = (rng.standard_normal((1, h)) * 0.02).astype(np.float16)
-    x = rng.standard_normal(h).astype(np.float16)
-    return dict(bank=bank, shared=shared, w_router=w_router, w_sg=w_sg, x=x)
-
-
 def test_moe_block_decode_config1(cuda, config1):
     from engine.ops import moe_block_decode
     c = config1
