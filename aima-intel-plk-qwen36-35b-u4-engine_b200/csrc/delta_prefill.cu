@@ -138,11 +138,23 @@ __global__ void __launch_bounds__(256) delta_conv_state_kernel(const __half* qkv
 // r = 32m + 4rg + e (m, e in 0..3), so q/k row loads are 16-byte vectors that
 // eight lane groups read as one contiguous 128-byte line. Sums over key rows
 // are a per-lane 16-term partial plus three xor-shuffles (lane bits 2..4).
-__global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* qk, const __half* v,
-                                                            const float* decay,
-                                                            const float* beta, float* state,
-                                                            float* o_out, int T, int nk, int nv) {
+// Per token, both sums are taken on the state before the update,
+//   pk = S^T k, pq = S^T q  (reduced together),
+//   delta = beta (v - a pk),  o = a pq + delta (k . q),  S = a S + k delta^T,
+// which is the step above rearranged (S^T q after the update equals
+// a S^T q + delta (k . q)), so only pk -> delta -> S is on the token-to-token
+// chain. k . q per token is computed once per chunk; outputs are staged in
+// shared memory and written per chunk.
+__global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* __restrict__ qk,
+                                                            const __half* __restrict__ v,
+                                                            const float* __restrict__ decay,
+                                                            const float* __restrict__ beta,
+                                                            float* __restrict__ state,
+                                                            float* __restrict__ o_out, int T,
+                                                            int nk, int nv) {
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float kq_s[kScanTC];
+  __shared__ __align__(16) float o_s[kScanTC][kScanCols];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = lane >> 2, cl = lane & 3;
   const int vh = blockIdx.y, j0 = blockIdx.x * kScanCols;
@@ -209,6 +221,14 @@ __global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* qk, con
     const __half* vs = sv(buf);
     const float* ds = sd(buf);
     const float* bs = sb(buf);
+    // k . q of the chunk's tokens: warp w takes tokens w, w + 8, ...
+    for (int u = warp; u < n; u += kScanWarps) {
+      const float4 a = *reinterpret_cast<const float4*>(qs + u * kDhd + 4 * lane);
+      const float4 b = *reinterpret_cast<const float4*>(ks + u * kDhd + 4 * lane);
+      const float d = warp_sum(a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w);
+      if (lane == 0) kq_s[u] = d;
+    }
+    __syncthreads();
 #pragma unroll 2
     for (int u = 0; u < n; ++u) {
       float kv[16], qv[16];
@@ -225,40 +245,39 @@ __global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* qk, con
         qv[4 * m + 2] = q4.z;
         qv[4 * m + 3] = q4.w;
       }
-      const float d = ds[u], bt = bs[u];
+      const float a = ds[u], bt = bs[u], kq = kq_s[u];
       const float vv = __half2float(vs[u * kScanCols + 4 * warp + cl]);
-#pragma unroll
-      for (int m = 0; m < 16; ++m) S[m] *= d;
-      float p0 = S[0] * kv[0], p1 = S[1] * kv[1], p2 = S[2] * kv[2], p3 = S[3] * kv[3];
-#pragma unroll
-      for (int m = 4; m < 16; m += 4) {
-        p0 = fmaf(S[m], kv[m], p0);
-        p1 = fmaf(S[m + 1], kv[m + 1], p1);
-        p2 = fmaf(S[m + 2], kv[m + 2], p2);
-        p3 = fmaf(S[m + 3], kv[m + 3], p3);
-      }
-      float p = (p0 + p1) + (p2 + p3);
-      p += __shfl_xor_sync(0xffffffffu, p, 4);
-      p += __shfl_xor_sync(0xffffffffu, p, 8);
-      p += __shfl_xor_sync(0xffffffffu, p, 16);
-      const float delta = (vv - p) * bt;
-#pragma unroll
-      for (int m = 0; m < 16; ++m) S[m] = fmaf(kv[m], delta, S[m]);
-      float o0 = S[0] * qv[0], o1 = S[1] * qv[1], o2 = S[2] * qv[2], o3 = S[3] * qv[3];
+      float pk0 = S[0] * kv[0], pk1 = S[1] * kv[1], pk2 = S[2] * kv[2], pk3 = S[3] * kv[3];
+      float pq0 = S[0] * qv[0], pq1 = S[1] * qv[1], pq2 = S[2] * qv[2], pq3 = S[3] * qv[3];
 #pragma unroll
       for (int m = 4; m < 16; m += 4) {
-        o0 = fmaf(S[m], qv[m], o0);
-        o1 = fmaf(S[m + 1], qv[m + 1], o1);
-        o2 = fmaf(S[m + 2], qv[m + 2], o2);
-        o3 = fmaf(S[m + 3], qv[m + 3], o3);
+        pk0 = fmaf(S[m], kv[m], pk0);
+        pk1 = fmaf(S[m + 1], kv[m + 1], pk1);
+        pk2 = fmaf(S[m + 2], kv[m + 2], pk2);
+        pk3 = fmaf(S[m + 3], kv[m + 3], pk3);
+        pq0 = fmaf(S[m], qv[m], pq0);
+        pq1 = fmaf(S[m + 1], qv[m + 1], pq1);
+        pq2 = fmaf(S[m + 2], qv[m + 2], pq2);
+        pq3 = fmaf(S[m + 3], qv[m + 3], pq3);
       }
-      float o = (o0 + o1) + (o2 + o3);
-      o += __shfl_xor_sync(0xffffffffu, o, 4);
-      o += __shfl_xor_sync(0xffffffffu, o, 8);
-      o += __shfl_xor_sync(0xffffffffu, o, 16);
-      if (rg == 0) o_out[((size_t)(t0 + u) * nv + vh) * kDhd + col] = o;
+      float pk = (pk0 + pk1) + (pk2 + pk3);
+      float pq = (pq0 + pq1) + (pq2 + pq3);
+#pragma unroll
+      for (int x = 4; x <= 16; x <<= 1) {
+        pk += __shfl_xor_sync(0xffffffffu, pk, x);
+        pq += __shfl_xor_sync(0xffffffffu, pq, x);
+      }
+      const float delta = (vv - a * pk) * bt;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) S[m] = fmaf(kv[m], delta, S[m] * a);
+      if (rg == 0) o_s[u][4 * warp + cl] = fmaf(delta, kq, a * pq);
     }
-    __syncthreads();  // buffer buf is refilled by the next iteration's load
+    __syncthreads();  // o_s complete; buffer buf is refilled by the next iteration's load
+    for (int i = threadIdx.x; i < n * (kScanCols / 4); i += blockDim.x) {
+      const int u = i / (kScanCols / 4), p = i % (kScanCols / 4);
+      *reinterpret_cast<float4*>(o_out + ((size_t)(t0 + u) * nv + vh) * kDhd + j0 + 4 * p) =
+          *reinterpret_cast<const float4*>(&o_s[u][4 * p]);
+    }
   }
 #pragma unroll
   for (int m = 0; m < 4; ++m)
