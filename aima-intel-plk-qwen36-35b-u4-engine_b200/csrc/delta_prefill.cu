@@ -10,7 +10,7 @@
 //      beta = sigmoid(b) per (token, value head).
 //   2. delta_conv_state_kernel: carried conv state := the last four inputs.
 //   3. delta_scan_kernel: the recurrence, sequential over tokens. A warp owns
-//      four value columns of one head and keeps their 128 x 4 state slice in
+//      eight value columns of one head and keeps their 128 x 8 state slice in
 //      registers for the whole prompt; the inputs of 32 tokens at a time are
 //      staged in shared memory with cp.async, double-buffered.
 //   4. delta_gated_norm_kernel: gated RMSNorm of every (token, value head).
@@ -31,84 +31,117 @@ namespace iq36 {
 
 constexpr int kDhd = 128;       // DeltaNet head dim (key and value)
 constexpr int kScanTC = 32;     // tokens per shared-memory chunk
-constexpr int kScanWarps = 8;   // warps per CTA; 4 value columns per warp
-constexpr int kScanCols = 4 * kScanWarps;
+constexpr int kScanWarps = 4;   // warps per CTA; 8 value columns per warp
+constexpr int kScanCols = 8 * kScanWarps;
 constexpr int kScanStage = 2 * kScanTC * kDhd * 4 + kScanTC * kScanCols * 2 + 2 * kScanTC * 4;
 constexpr int kScanSmem = 2 * kScanStage;
+constexpr int kConvTok = 32;    // tokens per CTA of the conv kernel
+
+// Packed fp32 pairs (two independent round-to-nearest operations, the same
+// results as two scalar fmaf / multiplies).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;\n"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&d);
+}
 
 // ---------------------------------------------------------------------------
-// 1. conv + SiLU + q/k normalisation + gates. Grid (T, ceil(segments/8)),
-// 8 warps; warp = one 128-channel segment (a q head, a k head or a v head) of
-// one token; lane = 4 channels.
+// 1. conv + SiLU + q/k normalisation + gates. Grid (ceil(T/32), ceil(segments/8)),
+// 8 warps; warp = one 128-channel segment (a q head, a k head or a v head)
+// over 32 consecutive tokens, lane = 4 channels; the last three inputs ride
+// along in registers, so every input row is read once.
 __global__ void __launch_bounds__(256) delta_conv_batch_kernel(
     const __half* qkv, int T, int nk, int nv, const float* conv_state, const float* conv_w,
     const __half* a, const __half* b, int gate_stride, const float* a_log, const float* dtb,
     float* qk_out, __half* v_out, float* decay_out, float* beta_out) {
   pdl_wait();
-  const int t = blockIdx.x;
+  const int t0 = blockIdx.x * kConvTok, t1 = min(T, t0 + kConvTok);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (blockIdx.y == 0 && threadIdx.x < nv) {
-    const int h = threadIdx.x;
-    const float xa = __half2float(a[(size_t)t * gate_stride + h]) + dtb[h];
-    const float sp = xa > 20.f ? xa : log1pf(expf(xa));
-    const float g = -expf(a_log[h]) * sp;
-    decay_out[(size_t)t * nv + h] = expf(g);
-    beta_out[(size_t)t * nv + h] = sigmoidf_acc(__half2float(b[(size_t)t * gate_stride + h]));
+  if (blockIdx.y == 0) {
+    for (int i = threadIdx.x; i < (t1 - t0) * nv; i += blockDim.x) {
+      const int t = t0 + i / nv, h = i % nv;
+      const float xa = __half2float(a[(size_t)t * gate_stride + h]) + dtb[h];
+      const float sp = xa > 20.f ? xa : log1pf(expf(xa));
+      const float g = -expf(a_log[h]) * sp;
+      decay_out[(size_t)t * nv + h] = expf(g);
+      beta_out[(size_t)t * nv + h] = sigmoidf_acc(__half2float(b[(size_t)t * gate_stride + h]));
+    }
   }
   const int nseg = 2 * nk + nv;
   const int seg = blockIdx.y * 8 + warp;
   if (seg >= nseg) return;
   const int C = nseg * kDhd;
   const int c0 = seg * kDhd + 4 * lane;
-  // x[d][ch] = input of token t-3+d at channel c0+ch
-  float x[4][4];
-#pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    const int tt = t - 3 + d;
+  auto load_row = [&](int tt, float* x) {
     if (tt >= 0) {
       const uint2 raw = *reinterpret_cast<const uint2*>(qkv + (size_t)tt * C + c0);
       const __half2 lo = *reinterpret_cast<const __half2*>(&raw.x);
       const __half2 hi = *reinterpret_cast<const __half2*>(&raw.y);
-      x[d][0] = __low2float(lo);
-      x[d][1] = __high2float(lo);
-      x[d][2] = __low2float(hi);
-      x[d][3] = __high2float(hi);
+      x[0] = __low2float(lo);
+      x[1] = __high2float(lo);
+      x[2] = __low2float(hi);
+      x[3] = __high2float(hi);
     } else {
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) x[d][ch] = conv_state[(size_t)(c0 + ch) * 4 + 4 + tt];
+      for (int ch = 0; ch < 4; ++ch) x[ch] = conv_state[(size_t)(c0 + ch) * 4 + 4 + tt];
     }
-  }
-  float act[4];
+  };
+  float4 w[4];
 #pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    const float4 w = reinterpret_cast<const float4*>(conv_w)[c0 + ch];
-    float s = w.x * x[0][ch];
-    s = fmaf(w.y, x[1][ch], s);
-    s = fmaf(w.z, x[2][ch], s);
-    s = fmaf(w.w, x[3][ch], s);
-    const float conv = __half2float(__float2half_rn(s));
-    act[ch] = __half2float(__float2half_rn(conv / (1.0f + expf(-conv))));
-  }
-  if (seg >= 2 * nk) {
-    const __half2 lo = __floats2half2_rn(act[0], act[1]);
-    const __half2 hi = __floats2half2_rn(act[2], act[3]);
-    uint2 raw;
-    raw.x = *reinterpret_cast<const uint32_t*>(&lo);
-    raw.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(v_out + (size_t)t * nv * kDhd + (seg - 2 * nk) * kDhd + 4 * lane) =
-        raw;
-  } else {
-    const float ss = warp_sum(act[0] * act[0] + act[1] * act[1] + act[2] * act[2] +
-                              act[3] * act[3]);
-    const float r = rsqrtf(ss + 1e-6f);
-    float4 y;
-    if (seg < nk) {
-      const float qs = rsqrtf((float)kDhd);
-      y = make_float4(act[0] * r * qs, act[1] * r * qs, act[2] * r * qs, act[3] * r * qs);
-    } else {
-      y = make_float4(act[0] * r, act[1] * r, act[2] * r, act[3] * r);
+  for (int ch = 0; ch < 4; ++ch) w[ch] = reinterpret_cast<const float4*>(conv_w)[c0 + ch];
+  // x3 = input t-3, x2 = t-2, x1 = t-1
+  float x3[4], x2[4], x1[4];
+  load_row(t0 - 3, x3);
+  load_row(t0 - 2, x2);
+  load_row(t0 - 1, x1);
+  const float qscale = rsqrtf((float)kDhd);
+  for (int t = t0; t < t1; ++t) {
+    float x0[4];
+    load_row(t, x0);
+    float act[4];
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      float s = w[ch].x * x3[ch];
+      s = fmaf(w[ch].y, x2[ch], s);
+      s = fmaf(w[ch].z, x1[ch], s);
+      s = fmaf(w[ch].w, x0[ch], s);
+      const float conv = __half2float(__float2half_rn(s));
+      act[ch] = __half2float(__float2half_rn(conv / (1.0f + expf(-conv))));
+      x3[ch] = x2[ch];
+      x2[ch] = x1[ch];
+      x1[ch] = x0[ch];
     }
-    *reinterpret_cast<float4*>(qk_out + ((size_t)t * 2 * nk + seg) * kDhd + 4 * lane) = y;
+    if (seg >= 2 * nk) {
+      const __half2 lo = __floats2half2_rn(act[0], act[1]);
+      const __half2 hi = __floats2half2_rn(act[2], act[3]);
+      uint2 raw;
+      raw.x = *reinterpret_cast<const uint32_t*>(&lo);
+      raw.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(v_out + (size_t)t * nv * kDhd + (seg - 2 * nk) * kDhd +
+                                4 * lane) = raw;
+    } else {
+      const float ss = warp_sum(act[0] * act[0] + act[1] * act[1] + act[2] * act[2] +
+                                act[3] * act[3]);
+      const float r = rsqrtf(ss + 1e-6f);
+      float4 y;
+      if (seg < nk) {
+        y = make_float4(act[0] * r * qscale, act[1] * r * qscale, act[2] * r * qscale,
+                        act[3] * r * qscale);
+      } else {
+        y = make_float4(act[0] * r, act[1] * r, act[2] * r, act[3] * r);
+      }
+      *reinterpret_cast<float4*>(qk_out + ((size_t)t * 2 * nk + seg) * kDhd + 4 * lane) = y;
+    }
   }
   pdl_launch_dependents();
 }
@@ -133,33 +166,32 @@ __global__ void __launch_bounds__(256) delta_conv_state_kernel(const __half* qkv
 }
 
 // ---------------------------------------------------------------------------
-// 3. the recurrence. Grid (128/32, nv), 256 threads. Warp w owns value columns
-// j = j0 + 4w + cl (cl = lane & 3); lane group rg = lane >> 2 owns key rows
-// r = 32m + 4rg + e (m, e in 0..3), so q/k row loads are 16-byte vectors that
-// eight lane groups read as one contiguous 128-byte line. Sums over key rows
-// are a per-lane 16-term partial plus three xor-shuffles (lane bits 2..4).
-// Per token, both sums are taken on the state before the update,
+// 3. the recurrence. Grid (128/32, nv), 4 warps. Warp w owns value columns
+// j = j0 + 8w + cl (cl = lane & 7); lane group rg = lane >> 3 owns the 32 key
+// rows r = 16m + 4rg + e (m in 0..7, e in 0..3), so each q/k row load is a
+// 16-byte vector and the four lane groups read one contiguous 64-byte piece.
+// Sums over key rows are a per-lane 32-term partial (packed fp32 pairs) plus
+// two xor-shuffles (lane bits 3, 4). Per token, both sums are taken on the
+// state before the update,
 //   pk = S^T k, pq = S^T q  (reduced together),
 //   delta = beta (v - a pk),  o = a pq + delta (k . q),  S = a S + k delta^T,
 // which is the step above rearranged (S^T q after the update equals
 // a S^T q + delta (k . q)), so only pk -> delta -> S is on the token-to-token
 // chain. k . q per token is computed once per chunk; outputs are staged in
 // shared memory and written per chunk.
-__global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* __restrict__ qk,
-                                                            const __half* __restrict__ v,
-                                                            const float* __restrict__ decay,
-                                                            const float* __restrict__ beta,
-                                                            float* __restrict__ state,
-                                                            float* __restrict__ o_out, int T,
-                                                            int nk, int nv) {
+__global__ void __launch_bounds__(32 * kScanWarps, 1)
+    delta_scan_kernel(const float* __restrict__ qk, const __half* __restrict__ v,
+                      const float* __restrict__ decay, const float* __restrict__ beta,
+                      float* __restrict__ state, float* __restrict__ o_out, int T, int nk,
+                      int nv) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float kq_s[kScanTC];
   __shared__ __align__(16) float o_s[kScanTC][kScanCols];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rg = lane >> 2, cl = lane & 3;
+  const int rg = lane >> 3, cl = lane & 7;
   const int vh = blockIdx.y, j0 = blockIdx.x * kScanCols;
   const int kh = vh / (nv / nk);
-  const int col = j0 + 4 * warp + cl;
+  const int col = j0 + 8 * warp + cl;
 
   auto sq = [&](int buf) { return reinterpret_cast<float*>(smem + buf * kScanStage); };
   auto sk = [&](int buf) { return sq(buf) + kScanTC * kDhd; };
@@ -195,12 +227,16 @@ __global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* __restr
     }
   };
 
-  float S[16];
+  // S2[2m + h] = rows (16m + 4rg + 2h, +1) of column col
+  float2 S2[16];
   const size_t sbase = (size_t)vh * kDhd * kDhd;
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
+  for (int m = 0; m < 8; ++m)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) S[4 * m + e] = state[sbase + (size_t)(32 * m + 4 * rg + e) * kDhd + col];
+    for (int h = 0; h < 2; ++h) {
+      const size_t r = 16 * m + 4 * rg + 2 * h;
+      S2[2 * m + h] = make_float2(state[sbase + r * kDhd + col], state[sbase + (r + 1) * kDhd + col]);
+    }
 
   const int nchunks = (T + kScanTC - 1) / kScanTC;
   load_chunk(0, 0);
@@ -221,56 +257,52 @@ __global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* __restr
     const __half* vs = sv(buf);
     const float* ds = sd(buf);
     const float* bs = sb(buf);
-    // k . q of the chunk's tokens: warp w takes tokens w, w + 8, ...
+    // k . q of the chunk's tokens
     for (int u = warp; u < n; u += kScanWarps) {
-      const float4 a = *reinterpret_cast<const float4*>(qs + u * kDhd + 4 * lane);
-      const float4 b = *reinterpret_cast<const float4*>(ks + u * kDhd + 4 * lane);
-      const float d = warp_sum(a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w);
+      const float4 x = *reinterpret_cast<const float4*>(qs + u * kDhd + 4 * lane);
+      const float4 y = *reinterpret_cast<const float4*>(ks + u * kDhd + 4 * lane);
+      const float d = warp_sum(x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w);
       if (lane == 0) kq_s[u] = d;
     }
     __syncthreads();
 #pragma unroll 2
     for (int u = 0; u < n; ++u) {
-      float kv[16], qv[16];
+      float2 k2[16], q2[16];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float4 k4 = *reinterpret_cast<const float4*>(ks + u * kDhd + 32 * m + 4 * rg);
-        const float4 q4 = *reinterpret_cast<const float4*>(qs + u * kDhd + 32 * m + 4 * rg);
-        kv[4 * m] = k4.x;
-        kv[4 * m + 1] = k4.y;
-        kv[4 * m + 2] = k4.z;
-        kv[4 * m + 3] = k4.w;
-        qv[4 * m] = q4.x;
-        qv[4 * m + 1] = q4.y;
-        qv[4 * m + 2] = q4.z;
-        qv[4 * m + 3] = q4.w;
+      for (int m = 0; m < 8; ++m) {
+        const float4 k4 = *reinterpret_cast<const float4*>(ks + u * kDhd + 16 * m + 4 * rg);
+        const float4 q4 = *reinterpret_cast<const float4*>(qs + u * kDhd + 16 * m + 4 * rg);
+        k2[2 * m] = make_float2(k4.x, k4.y);
+        k2[2 * m + 1] = make_float2(k4.z, k4.w);
+        q2[2 * m] = make_float2(q4.x, q4.y);
+        q2[2 * m + 1] = make_float2(q4.z, q4.w);
       }
       const float a = ds[u], bt = bs[u], kq = kq_s[u];
-      const float vv = __half2float(vs[u * kScanCols + 4 * warp + cl]);
-      float pk0 = S[0] * kv[0], pk1 = S[1] * kv[1], pk2 = S[2] * kv[2], pk3 = S[3] * kv[3];
-      float pq0 = S[0] * qv[0], pq1 = S[1] * qv[1], pq2 = S[2] * qv[2], pq3 = S[3] * qv[3];
+      const float vv = __half2float(vs[u * kScanCols + 8 * warp + cl]);
+      float2 pk[4], pq[4];
 #pragma unroll
-      for (int m = 4; m < 16; m += 4) {
-        pk0 = fmaf(S[m], kv[m], pk0);
-        pk1 = fmaf(S[m + 1], kv[m + 1], pk1);
-        pk2 = fmaf(S[m + 2], kv[m + 2], pk2);
-        pk3 = fmaf(S[m + 3], kv[m + 3], pk3);
-        pq0 = fmaf(S[m], qv[m], pq0);
-        pq1 = fmaf(S[m + 1], qv[m + 1], pq1);
-        pq2 = fmaf(S[m + 2], qv[m + 2], pq2);
-        pq3 = fmaf(S[m + 3], qv[m + 3], pq3);
+      for (int i = 0; i < 4; ++i) {
+        pk[i] = fmul2(S2[i], k2[i]);
+        pq[i] = fmul2(S2[i], q2[i]);
       }
-      float pk = (pk0 + pk1) + (pk2 + pk3);
-      float pq = (pq0 + pq1) + (pq2 + pq3);
 #pragma unroll
-      for (int x = 4; x <= 16; x <<= 1) {
-        pk += __shfl_xor_sync(0xffffffffu, pk, x);
-        pq += __shfl_xor_sync(0xffffffffu, pq, x);
+      for (int i = 4; i < 16; ++i) {
+        pk[i & 3] = ffma2(S2[i], k2[i], pk[i & 3]);
+        pq[i & 3] = ffma2(S2[i], q2[i], pq[i & 3]);
       }
-      const float delta = (vv - a * pk) * bt;
+      float sk = ((pk[0].x + pk[0].y) + (pk[1].x + pk[1].y)) +
+                 ((pk[2].x + pk[2].y) + (pk[3].x + pk[3].y));
+      float sq_ = ((pq[0].x + pq[0].y) + (pq[1].x + pq[1].y)) +
+                  ((pq[2].x + pq[2].y) + (pq[3].x + pq[3].y));
+      sk += __shfl_xor_sync(0xffffffffu, sk, 8);
+      sq_ += __shfl_xor_sync(0xffffffffu, sq_, 8);
+      sk += __shfl_xor_sync(0xffffffffu, sk, 16);
+      sq_ += __shfl_xor_sync(0xffffffffu, sq_, 16);
+      const float delta = (vv - a * sk) * bt;
+      const float2 a2 = make_float2(a, a), d2 = make_float2(delta, delta);
 #pragma unroll
-      for (int m = 0; m < 16; ++m) S[m] = fmaf(kv[m], delta, S[m] * a);
-      if (rg == 0) o_s[u][4 * warp + cl] = fmaf(delta, kq, a * pq);
+      for (int i = 0; i < 16; ++i) S2[i] = ffma2(k2[i], d2, fmul2(S2[i], a2));
+      if (rg == 0) o_s[u][8 * warp + cl] = fmaf(delta, kq, a * sq_);
     }
     __syncthreads();  // o_s complete; buffer buf is refilled by the next iteration's load
     for (int i = threadIdx.x; i < n * (kScanCols / 4); i += blockDim.x) {
@@ -280,9 +312,13 @@ __global__ void __launch_bounds__(256, 1) delta_scan_kernel(const float* __restr
     }
   }
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
+  for (int m = 0; m < 8; ++m)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) state[sbase + (size_t)(32 * m + 4 * rg + e) * kDhd + col] = S[4 * m + e];
+    for (int h = 0; h < 2; ++h) {
+      const size_t r = 16 * m + 4 * rg + 2 * h;
+      state[sbase + r * kDhd + col] = S2[2 * m + h].x;
+      state[sbase + (r + 1) * kDhd + col] = S2[2 * m + h].y;
+    }
   pdl_launch_dependents();
 }
 
@@ -377,7 +413,8 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   float* o = reinterpret_cast<float*>(ws + w.o);
   const cudaStream_t s = as_stream(stream);
   const int nseg = 2 * nk + nv, C = nseg * kDhd;
-  cudaError_t e = launch(delta_conv_batch_kernel, dim3(T, ceil_div(nseg, 8)), dim3(256), 0, s,
+  cudaError_t e = launch(delta_conv_batch_kernel, dim3(ceil_div(T, kConvTok), ceil_div(nseg, 8)),
+                         dim3(256), 0, s,
                          reinterpret_cast<const __half*>(qkv_f16), T, nk, nv,
                          (const float*)conv_state, conv_w, reinterpret_cast<const __half*>(a_f16),
                          reinterpret_cast<const __half*>(b_f16), gate_stride, a_log, dt_bias, qk,
