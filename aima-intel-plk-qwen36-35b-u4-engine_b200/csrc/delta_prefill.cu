@@ -2,24 +2,31 @@
 //
 // The per-token decode path (delta_prep_kernel + delta_step_kernel) runs the
 // causal conv and the recurrence for one token per launch. Prefill runs the
-// same arithmetic over a whole prompt in four launches per layer:
+// same arithmetic over a whole prompt in five launches per layer:
 //   1. delta_conv_batch_kernel: causal depthwise conv(4) + SiLU for every
-//      (token, channel) — fully parallel, the conv is a 4-tap FIR over the
-//      previous three inputs (or the carried state before token 0) — then the
-//      per-head L2 normalisation of q and k, and the gates decay = exp(g),
+//      (token, channel) — the conv is a 4-tap FIR over the previous three
+//      inputs (or the carried state before token 0) — then the per-head L2
+//      normalisation of q and k, and the gates g (log decay) and
 //      beta = sigmoid(b) per (token, value head).
 //   2. delta_conv_state_kernel: carried conv state := the last four inputs.
-//   3. delta_scan_kernel: the recurrence, sequential over tokens. A warp owns
-//      eight value columns of one head and keeps their 128 x 8 state slice in
-//      registers for the whole prompt; the inputs of 32 tokens at a time are
-//      staged in shared memory with cp.async, double-buffered.
-//   4. delta_gated_norm_kernel: gated RMSNorm of every (token, value head).
+//   3. delta_chunk_prep_kernel: the chunked (WY) form of the recurrence,
+//      parallel over 32-token chunks x value heads: cumulative log decay G,
+//      A = beta_r e^(G_r - G_s) k_r.k_s (s < r), the triangular solve
+//      (I + A) [W | U] = [beta e^G k | beta v], and the chunk's output and
+//      state-update operands e^G q, e^(G_last - G) k, e^(G_r - G_s) q_r.k_s.
+//   4. delta_chunk_scan_kernel: the only sequential part, over chunks: per
+//      chunk Delta = U - W S, O = (e^G q) S + P Delta, S = e^G_last S + K~^T Delta,
+//      as 3xTF32 tensor-core products (fp32-accurate: hi/lo split of every
+//      operand), the state held in registers.
+//   5. delta_gated_norm_kernel: gated RMSNorm of every (token, value head).
 //
 // Semantics (same as the decode path): OpenVINO gated delta net
 // (iq36_gated_delta_net.cl:36-150) — key head = value head / (nv/nk), q and k
 // L2-normalised with rsqrt(sum + 1e-6), q additionally * 1/sqrt(D); per token
-// S = exp(g) S; sk = S^T k; delta = (v - sk) beta; S += k delta^T; o = S^T q;
-// conv with fp16 rounding points of iq36_linear_conv_swish.cl:25-63; gates of
+// S = exp(g) S; sk = S^T k; delta = (v - sk) beta; S += k delta^T; o = S^T q.
+// Unrolling that step over a chunk gives exactly the chunked products above
+// (delta_r + sum_{s<r} A_rs delta_s = beta_r v_r - beta_r e^(G_r) S0^T k_r).
+// Conv with fp16 rounding points of iq36_linear_conv_swish.cl:25-63; gates of
 // gguf_loader.cpp:4875-4912; gated RMSNorm of gguf_loader.cpp:4770-4786.
 
 #include <atomic>
@@ -30,30 +37,7 @@
 namespace iq36 {
 
 constexpr int kDhd = 128;       // DeltaNet head dim (key and value)
-constexpr int kScanTC = 32;     // tokens per shared-memory chunk
-constexpr int kScanWarps = 4;   // warps per CTA; 8 value columns per warp
-constexpr int kScanCols = 8 * kScanWarps;
-constexpr int kScanStage = 2 * kScanTC * kDhd * 4 + kScanTC * kScanCols * 2 + 2 * kScanTC * 4;
-constexpr int kScanSmem = 2 * kScanStage;
 constexpr int kConvTok = 32;    // tokens per CTA of the conv kernel
-
-// Packed fp32 pairs (two independent round-to-nearest operations, the same
-// results as two scalar fmaf / multiplies).
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;\n"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
-        "l"(*reinterpret_cast<const uint64_t*>(&c)));
-  return *reinterpret_cast<const float2*>(&d);
-}
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;\n"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&d);
-}
 
 // ---------------------------------------------------------------------------
 // 1. conv + SiLU + q/k normalisation + gates. Grid (ceil(T/32), ceil(segments/8)),
@@ -63,7 +47,7 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
 __global__ void __launch_bounds__(256) delta_conv_batch_kernel(
     const __half* qkv, int T, int nk, int nv, const float* conv_state, const float* conv_w,
     const __half* a, const __half* b, int gate_stride, const float* a_log, const float* dtb,
-    float* qk_out, __half* v_out, float* decay_out, float* beta_out) {
+    float* qk_out, __half* v_out, float* lg_out, float* beta_out) {
   pdl_wait();
   const int t0 = blockIdx.x * kConvTok, t1 = min(T, t0 + kConvTok);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -72,8 +56,7 @@ __global__ void __launch_bounds__(256) delta_conv_batch_kernel(
       const int t = t0 + i / nv, h = i % nv;
       const float xa = __half2float(a[(size_t)t * gate_stride + h]) + dtb[h];
       const float sp = xa > 20.f ? xa : log1pf(expf(xa));
-      const float g = -expf(a_log[h]) * sp;
-      decay_out[(size_t)t * nv + h] = expf(g);
+      lg_out[(size_t)t * nv + h] = -expf(a_log[h]) * sp;  // g = log of the decay
       beta_out[(size_t)t * nv + h] = sigmoidf_acc(__half2float(b[(size_t)t * gate_stride + h]));
     }
   }
@@ -166,159 +149,297 @@ __global__ void __launch_bounds__(256) delta_conv_state_kernel(const __half* qkv
 }
 
 // ---------------------------------------------------------------------------
-// 3. the recurrence. Grid (128/32, nv), 4 warps. Warp w owns value columns
-// j = j0 + 8w + cl (cl = lane & 7); lane group rg = lane >> 3 owns the 32 key
-// rows r = 16m + 4rg + e (m in 0..7, e in 0..3), so each q/k row load is a
-// 16-byte vector and the four lane groups read one contiguous 64-byte piece.
-// Sums over key rows are a per-lane 32-term partial (packed fp32 pairs) plus
-// two xor-shuffles (lane bits 3, 4). Per token, both sums are taken on the
-// state before the update,
-//   pk = S^T k, pq = S^T q  (reduced together),
-//   delta = beta (v - a pk),  o = a pq + delta (k . q),  S = a S + k delta^T,
-// which is the step above rearranged (S^T q after the update equals
-// a S^T q + delta (k . q)), so only pk -> delta -> S is on the token-to-token
-// chain. k . q per token is computed once per chunk; outputs are staged in
-// shared memory and written per chunk.
-__global__ void __launch_bounds__(32 * kScanWarps, 1)
-    delta_scan_kernel(const float* __restrict__ qk, const __half* __restrict__ v,
-                      const float* __restrict__ decay, const float* __restrict__ beta,
-                      float* __restrict__ state, float* __restrict__ o_out, int T, int nk,
-                      int nv) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ float kq_s[kScanTC];
-  __shared__ __align__(16) float o_s[kScanTC][kScanCols];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rg = lane >> 3, cl = lane & 7;
-  const int vh = blockIdx.y, j0 = blockIdx.x * kScanCols;
-  const int kh = vh / (nv / nk);
-  const int col = j0 + 8 * warp + cl;
+// 3./4. the recurrence in chunked form.
 
-  auto sq = [&](int buf) { return reinterpret_cast<float*>(smem + buf * kScanStage); };
-  auto sk = [&](int buf) { return sq(buf) + kScanTC * kDhd; };
-  auto sv = [&](int buf) { return reinterpret_cast<__half*>(sk(buf) + kScanTC * kDhd); };
-  auto sd = [&](int buf) { return reinterpret_cast<float*>(sv(buf) + kScanTC * kScanCols); };
-  auto sb = [&](int buf) { return sd(buf) + kScanTC; };
+constexpr int kCk = 32;  // tokens per chunk
+// Per (chunk, value head) operand block (floats): W [32][128], U [32][128],
+// Qg = e^G q [32][128], Kt = e^(G_last - G) k key-major [128][32], P [32][32],
+// gC = e^G_last.
+constexpr int kOffW = 0, kOffU = 4096, kOffQ = 8192, kOffKt = 12288, kOffPm = 16384,
+              kOffGc = 17408, kCkBlk = 17412;
+constexpr int kPrepSmem = (2 * kCk * 132 + kCk * 128 + kCk * 33 + 4 * kCk) * 4;
 
+__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __restrict__ qk,
+                                                               const __half* __restrict__ v,
+                                                               const float* __restrict__ lg,
+                                                               const float* __restrict__ beta,
+                                                               int T, int nk, int nv,
+                                                               float* __restrict__ blocks) {
+  extern __shared__ __align__(16) float sm[];
+  float* sk = sm;                  // k rows [32][132]
+  float* sq = sk + kCk * 132;      // q rows [32][132]
+  float* sv = sq + kCk * 132;      // v rows [32][128]
+  float* sA = sv + kCk * 128;      // A [32][33]
+  float* sB = sA + kCk * 33;       // beta [32]
+  float* sE = sB + kCk;            // e^G_r
+  float* sL = sE + kCk;            // e^(G_last - G_r)
+  float* sG = sL + kCk;            // G_r
+  const int c = blockIdx.x, h = blockIdx.y, kh = h / (nv / nk);
+  const int t0 = c * kCk, n = min(kCk, T - t0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
-  // stage the inputs of tokens [t0, t0 + kScanTC) into buffer buf
-  auto load_chunk = [&](int t0, int buf) {
-    const int n = min(kScanTC, T - t0);
-    const uint32_t q_s = smem_u32(sq(buf)), k_s = smem_u32(sk(buf)), v_s = smem_u32(sv(buf));
-    // q and k: n tokens x 32 pieces of 16 bytes each
-    for (int i = threadIdx.x; i < 2 * kScanTC * 32; i += blockDim.x) {
-      const int which = i / (kScanTC * 32), rem = i % (kScanTC * 32);
-      const int u = rem >> 5, p = rem & 31;
-      if (u < n) {
-        const float* src =
-            qk + ((size_t)(t0 + u) * 2 * nk + (which ? nk + kh : kh)) * kDhd + 4 * p;
-        cp_async_16((which ? k_s : q_s) + (u * kDhd + 4 * p) * 4, src, 16);
+  for (int i = tid; i < kCk * 32; i += blockDim.x) {
+    const int r = i >> 5, p = i & 31;
+    float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), qv4 = kv4, vv4 = kv4;
+    if (r < n) {
+      const size_t row = (size_t)(t0 + r) * 2 * nk;
+      kv4 = *reinterpret_cast<const float4*>(qk + (row + nk + kh) * kDhd + 4 * p);
+      qv4 = *reinterpret_cast<const float4*>(qk + (row + kh) * kDhd + 4 * p);
+      const uint2 raw =
+          *reinterpret_cast<const uint2*>(v + (size_t)(t0 + r) * nv * kDhd + h * kDhd + 4 * p);
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      vv4 = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    *reinterpret_cast<float4*>(sk + r * 132 + 4 * p) = kv4;
+    *reinterpret_cast<float4*>(sq + r * 132 + 4 * p) = qv4;
+    *reinterpret_cast<float4*>(sv + r * 128 + 4 * p) = vv4;
+  }
+  if (warp == 0) {
+    float x = lane < n ? lg[(size_t)(t0 + lane) * nv + h] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    const float gl = __shfl_sync(0xffffffffu, x, n - 1);
+    sG[lane] = x;
+    sE[lane] = lane < n ? expf(x) : 0.f;
+    sL[lane] = lane < n ? expf(gl - x) : 0.f;
+    sB[lane] = lane < n ? beta[(size_t)(t0 + lane) * nv + h] : 0.f;
+  }
+  __syncthreads();
+  float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+  // A (strictly lower) and P (lower including the diagonal)
+  for (int i = tid; i < kCk * kCk; i += blockDim.x) {
+    const int r = i >> 5, s2 = i & 31;
+    float kk = 0.f, qk_ = 0.f;
+    const bool lower = s2 <= r && r < n;
+    if (lower) {
+#pragma unroll 8
+      for (int d = 0; d < kDhd; d += 4) {
+        const float4 ks = *reinterpret_cast<const float4*>(sk + s2 * 132 + d);
+        const float4 kr = *reinterpret_cast<const float4*>(sk + r * 132 + d);
+        const float4 qr = *reinterpret_cast<const float4*>(sq + r * 132 + d);
+        kk = fmaf(kr.x, ks.x, kk);
+        kk = fmaf(kr.y, ks.y, kk);
+        kk = fmaf(kr.z, ks.z, kk);
+        kk = fmaf(kr.w, ks.w, kk);
+        qk_ = fmaf(qr.x, ks.x, qk_);
+        qk_ = fmaf(qr.y, ks.y, qk_);
+        qk_ = fmaf(qr.z, ks.z, qk_);
+        qk_ = fmaf(qr.w, ks.w, qk_);
       }
     }
-    // v: n tokens x 4 pieces (32 halves)
-    for (int i = threadIdx.x; i < kScanTC * 4; i += blockDim.x) {
-      const int u = i >> 2, p = i & 3;
-      if (u < n)
-        cp_async_16(v_s + (u * kScanCols + 8 * p) * 2,
-                    v + (size_t)(t0 + u) * nv * kDhd + vh * kDhd + j0 + 8 * p, 16);
+    const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
+    sA[r * 33 + s2] = s2 < r ? sB[r] * dec * kk : 0.f;
+    blk[kOffPm + r * kCk + s2] = dec * qk_;
+  }
+  __syncthreads();
+  // (I + A) X = [beta e^G k | beta v]: thread j owns column j, forward substitution
+  {
+    const int j = tid;
+    float x[kCk];
+#pragma unroll
+    for (int r = 0; r < kCk; ++r) {
+      float acc = j < kDhd ? sB[r] * sE[r] * sk[r * 132 + j] : sB[r] * sv[r * 128 + j - kDhd];
+#pragma unroll
+      for (int s2 = 0; s2 < r; ++s2) acc = fmaf(-sA[r * 33 + s2], x[s2], acc);
+      x[r] = acc;
     }
-    if (threadIdx.x < kScanTC && (int)threadIdx.x < n) {
-      sd(buf)[threadIdx.x] = decay[(size_t)(t0 + threadIdx.x) * nv + vh];
-      sb(buf)[threadIdx.x] = beta[(size_t)(t0 + threadIdx.x) * nv + vh];
+    float* dst = blk + (j < kDhd ? kOffW + j : kOffU + j - kDhd);
+#pragma unroll
+    for (int r = 0; r < kCk; ++r) dst[r * kDhd] = x[r];
+  }
+  for (int i = tid; i < kCk * kDhd; i += blockDim.x) {
+    const int r = i >> 7, d = i & 127;
+    blk[kOffQ + i] = sE[r] * sq[r * 132 + d];
+    const int dk = i >> 5, rk = i & 31;  // Kt[dk][rk]
+    blk[kOffKt + i] = sL[rk] * sk[rk * 132 + dk];
+  }
+  if (tid == 0) blk[kOffGc] = expf(sG[n - 1]);
+  pdl_launch_dependents();
+}
+
+// m16n8k8 TF32 tensor-core product with fp32 accumulate; A row-major 16x8
+// (a0 (g,t), a1 (g+8,t), a2 (g,t+4), a3 (g+8,t+4)), B 8x8 (b0 (k=t,n=g),
+// b1 (k=t+4,n=g)), C (c0,c1 (g,2t..), c2,c3 (g+8,2t..)).
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(hi) : "f"(x));
+  const float r = x - __uint_as_float(hi);
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(lo) : "f"(r));
+}
+struct Tf32Frag4 {
+  uint32_t hi[4], lo[4];
+};
+struct Tf32Frag2 {
+  uint32_t hi[2], lo[2];
+};
+__device__ __forceinline__ Tf32Frag4 frag_a(const float* p, int ld, int g, int t) {
+  Tf32Frag4 f;
+  split_tf32(p[g * ld + t], f.hi[0], f.lo[0]);
+  split_tf32(p[(g + 8) * ld + t], f.hi[1], f.lo[1]);
+  split_tf32(p[g * ld + t + 4], f.hi[2], f.lo[2]);
+  split_tf32(p[(g + 8) * ld + t + 4], f.hi[3], f.lo[3]);
+  return f;
+}
+__device__ __forceinline__ Tf32Frag2 frag_b(const float* p, int ld, int g, int t) {
+  Tf32Frag2 f;
+  split_tf32(p[t * ld + g], f.hi[0], f.lo[0]);
+  split_tf32(p[(t + 4) * ld + g], f.hi[1], f.lo[1]);
+  return f;
+}
+// c += a b with fp32-level accuracy: a_lo b_hi + a_hi b_lo + a_hi b_hi
+__device__ __forceinline__ void mma3(float (&c)[4], const Tf32Frag4& a, const Tf32Frag2& b) {
+  mma_tf32(c, a.lo, b.hi);
+  mma_tf32(c, a.hi, b.lo);
+  mma_tf32(c, a.hi, b.hi);
+}
+
+constexpr int kScCols = 32;  // value columns per CTA
+// one chunk's operands in shared memory (floats), padded for conflict-free fragments
+constexpr int kStW = 0, kStQ = kCk * 132, kStU = 2 * kCk * 132, kStPm = kStU + kCk * 36,
+              kStKt = kStPm + kCk * 36, kStFloats = kStKt + kDhd * 36;
+constexpr int kScanSmem = (2 * kStFloats + kDhd * 40 + kCk * 40) * 4;
+
+// Grid (128/32 column blocks, nv), 8 warps. Warp w keeps state rows
+// 16w..16w+15 (key) x the CTA's 32 value columns as mma accumulators.
+__global__ void __launch_bounds__(256, 1)
+    delta_chunk_scan_kernel(const float* __restrict__ blocks, float* __restrict__ state,
+                            float* __restrict__ o_out, int T, int nv) {
+  extern __shared__ __align__(16) float sm[];
+  float* sS = sm + 2 * kStFloats;  // state [128][40] (B operand)
+  float* sD = sS + kDhd * 40;      // Delta [32][40] (B operand)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int h = blockIdx.y, j0 = blockIdx.x * kScCols;
+  const int nchunks = (T + kCk - 1) / kCk;
+  auto stage = [&](int buf) { return sm + buf * kStFloats; };
+  auto load_stage = [&](int c, int buf) {
+    const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+    const uint32_t st = smem_u32(stage(buf));
+    for (int i = threadIdx.x; i < kCk * 32; i += blockDim.x) {
+      const int r = i >> 5, p = i & 31;
+      cp_async_16(st + (kStW + r * 132 + 4 * p) * 4, blk + kOffW + r * kDhd + 4 * p, 16);
+      cp_async_16(st + (kStQ + r * 132 + 4 * p) * 4, blk + kOffQ + r * kDhd + 4 * p, 16);
+    }
+    for (int i = threadIdx.x; i < kCk * 8; i += blockDim.x) {
+      const int r = i >> 3, p = i & 7;
+      cp_async_16(st + (kStU + r * 36 + 4 * p) * 4, blk + kOffU + r * kDhd + j0 + 4 * p, 16);
+      cp_async_16(st + (kStPm + r * 36 + 4 * p) * 4, blk + kOffPm + r * kCk + 4 * p, 16);
+    }
+    for (int i = threadIdx.x; i < kDhd * 8; i += blockDim.x) {
+      const int d = i >> 3, p = i & 7;
+      cp_async_16(st + (kStKt + d * 36 + 4 * p) * 4, blk + kOffKt + d * kCk + 4 * p, 16);
     }
   };
-
-  // S2[2m + h] = rows (16m + 4rg + 2h, +1) of column col
-  float2 S2[16];
-  const size_t sbase = (size_t)vh * kDhd * kDhd;
+  pdl_wait();
+  // state slice: rows 16w + g (+8), columns 8nt + 2t (+1)
+  float accS[4][4];
+  const size_t sbase = (size_t)h * kDhd * kDhd;
+  const int ra = 16 * warp + g, rb = ra + 8;
 #pragma unroll
-  for (int m = 0; m < 8; ++m)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const size_t r = 16 * m + 4 * rg + 2 * h;
-      S2[2 * m + h] = make_float2(state[sbase + r * kDhd + col], state[sbase + (r + 1) * kDhd + col]);
-    }
-
-  const int nchunks = (T + kScanTC - 1) / kScanTC;
-  load_chunk(0, 0);
+  for (int nt = 0; nt < 4; ++nt) {
+    const int cc = j0 + 8 * nt + 2 * t;
+    accS[nt][0] = state[sbase + (size_t)ra * kDhd + cc];
+    accS[nt][1] = state[sbase + (size_t)ra * kDhd + cc + 1];
+    accS[nt][2] = state[sbase + (size_t)rb * kDhd + cc];
+    accS[nt][3] = state[sbase + (size_t)rb * kDhd + cc + 1];
+    sS[ra * 40 + 8 * nt + 2 * t] = accS[nt][0];
+    sS[ra * 40 + 8 * nt + 2 * t + 1] = accS[nt][1];
+    sS[rb * 40 + 8 * nt + 2 * t] = accS[nt][2];
+    sS[rb * 40 + 8 * nt + 2 * t + 1] = accS[nt][3];
+  }
+  load_stage(0, 0);
   cp_async_commit();
+  const int mw = warp >> 2, nw = warp & 3;  // tile of Delta / O owned in steps b, c
   for (int c = 0; c < nchunks; ++c) {
     const int buf = c & 1;
     if (c + 1 < nchunks) {
-      load_chunk((c + 1) * kScanTC, buf ^ 1);
+      load_stage(c + 1, buf ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const int t0 = c * kScanTC, n = min(kScanTC, T - t0);
-    const float* qs = sq(buf);
-    const float* ks = sk(buf);
-    const __half* vs = sv(buf);
-    const float* ds = sd(buf);
-    const float* bs = sb(buf);
-    // k . q of the chunk's tokens
-    for (int u = warp; u < n; u += kScanWarps) {
-      const float4 x = *reinterpret_cast<const float4*>(qs + u * kDhd + 4 * lane);
-      const float4 y = *reinterpret_cast<const float4*>(ks + u * kDhd + 4 * lane);
-      const float d = warp_sum(x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w);
-      if (lane == 0) kq_s[u] = d;
+    const float* st = stage(buf);
+    // b: Delta = U - W S and Oa = Qg S for rows 16mw.., columns 8nw..
+    float accD[2][4] = {}, accO[2][4] = {};
+#pragma unroll 4
+    for (int ks = 0; ks < kDhd / 8; ++ks) {
+      const int hf = ks & 1;
+      const Tf32Frag2 bS = frag_b(sS + 8 * ks * 40 + 8 * nw, 40, g, t);
+      const Tf32Frag4 aW = frag_a(st + kStW + 16 * mw * 132 + 8 * ks, 132, g, t);
+      mma3(accD[hf], aW, bS);
+      const Tf32Frag4 aQ = frag_a(st + kStQ + 16 * mw * 132 + 8 * ks, 132, g, t);
+      mma3(accO[hf], aQ, bS);
+    }
+    const int r0 = 16 * mw + g, r1 = r0 + 8, cc = 8 * nw + 2 * t;
+    {
+      const float* sU = st + kStU;
+      sD[r0 * 40 + cc] = sU[r0 * 36 + cc] - (accD[0][0] + accD[1][0]);
+      sD[r0 * 40 + cc + 1] = sU[r0 * 36 + cc + 1] - (accD[0][1] + accD[1][1]);
+      sD[r1 * 40 + cc] = sU[r1 * 36 + cc] - (accD[0][2] + accD[1][2]);
+      sD[r1 * 40 + cc + 1] = sU[r1 * 36 + cc + 1] - (accD[0][3] + accD[1][3]);
     }
     __syncthreads();
-#pragma unroll 2
-    for (int u = 0; u < n; ++u) {
-      float2 k2[16], q2[16];
+    // c: O = Oa + P Delta
+    float o[4] = {accO[0][0] + accO[1][0], accO[0][1] + accO[1][1], accO[0][2] + accO[1][2],
+                  accO[0][3] + accO[1][3]};
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const float4 k4 = *reinterpret_cast<const float4*>(ks + u * kDhd + 16 * m + 4 * rg);
-        const float4 q4 = *reinterpret_cast<const float4*>(qs + u * kDhd + 16 * m + 4 * rg);
-        k2[2 * m] = make_float2(k4.x, k4.y);
-        k2[2 * m + 1] = make_float2(k4.z, k4.w);
-        q2[2 * m] = make_float2(q4.x, q4.y);
-        q2[2 * m + 1] = make_float2(q4.z, q4.w);
-      }
-      const float a = ds[u], bt = bs[u], kq = kq_s[u];
-      const float vv = __half2float(vs[u * kScanCols + 8 * warp + cl]);
-      float2 pk[4], pq[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        pk[i] = fmul2(S2[i], k2[i]);
-        pq[i] = fmul2(S2[i], q2[i]);
-      }
-#pragma unroll
-      for (int i = 4; i < 16; ++i) {
-        pk[i & 3] = ffma2(S2[i], k2[i], pk[i & 3]);
-        pq[i & 3] = ffma2(S2[i], q2[i], pq[i & 3]);
-      }
-      float sk = ((pk[0].x + pk[0].y) + (pk[1].x + pk[1].y)) +
-                 ((pk[2].x + pk[2].y) + (pk[3].x + pk[3].y));
-      float sq_ = ((pq[0].x + pq[0].y) + (pq[1].x + pq[1].y)) +
-                  ((pq[2].x + pq[2].y) + (pq[3].x + pq[3].y));
-      sk += __shfl_xor_sync(0xffffffffu, sk, 8);
-      sq_ += __shfl_xor_sync(0xffffffffu, sq_, 8);
-      sk += __shfl_xor_sync(0xffffffffu, sk, 16);
-      sq_ += __shfl_xor_sync(0xffffffffu, sq_, 16);
-      const float delta = (vv - a * sk) * bt;
-      const float2 a2 = make_float2(a, a), d2 = make_float2(delta, delta);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) S2[i] = ffma2(k2[i], d2, fmul2(S2[i], a2));
-      if (rg == 0) o_s[u][8 * warp + cl] = fmaf(delta, kq, a * sq_);
+    for (int ks = 0; ks < kCk / 8; ++ks) {
+      const Tf32Frag4 aP = frag_a(st + kStPm + 16 * mw * 36 + 8 * ks, 36, g, t);
+      const Tf32Frag2 bD = frag_b(sD + 8 * ks * 40 + 8 * nw, 40, g, t);
+      mma3(o, aP, bD);
     }
-    __syncthreads();  // o_s complete; buffer buf is refilled by the next iteration's load
-    for (int i = threadIdx.x; i < n * (kScanCols / 4); i += blockDim.x) {
-      const int u = i / (kScanCols / 4), p = i % (kScanCols / 4);
-      *reinterpret_cast<float4*>(o_out + ((size_t)(t0 + u) * nv + vh) * kDhd + j0 + 4 * p) =
-          *reinterpret_cast<const float4*>(&o_s[u][4 * p]);
+    const int t0 = c * kCk, n = min(kCk, T - t0);
+    if (r0 < n)
+      *reinterpret_cast<float2*>(o_out + ((size_t)(t0 + r0) * nv + h) * kDhd + j0 + cc) =
+          make_float2(o[0], o[1]);
+    if (r1 < n)
+      *reinterpret_cast<float2*>(o_out + ((size_t)(t0 + r1) * nv + h) * kDhd + j0 + cc) =
+          make_float2(o[2], o[3]);
+    // d: S = gC S + Kt^T Delta on this warp's key rows
+    const float gc = blocks[((size_t)c * nv + h) * kCkBlk + kOffGc];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) accS[nt][e] *= gc;
+#pragma unroll
+    for (int ks = 0; ks < kCk / 8; ++ks) {
+      const Tf32Frag4 aK = frag_a(st + kStKt + 16 * warp * 36 + 8 * ks, 36, g, t);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const Tf32Frag2 bD = frag_b(sD + 8 * ks * 40 + 8 * nt, 40, g, t);
+        mma3(accS[nt], aK, bD);
+      }
     }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      sS[ra * 40 + 8 * nt + 2 * t] = accS[nt][0];
+      sS[ra * 40 + 8 * nt + 2 * t + 1] = accS[nt][1];
+      sS[rb * 40 + 8 * nt + 2 * t] = accS[nt][2];
+      sS[rb * 40 + 8 * nt + 2 * t + 1] = accS[nt][3];
+    }
+    __syncthreads();  // sS complete for the next chunk; this stage is refilled next
   }
 #pragma unroll
-  for (int m = 0; m < 8; ++m)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const size_t r = 16 * m + 4 * rg + 2 * h;
-      state[sbase + r * kDhd + col] = S2[2 * m + h].x;
-      state[sbase + (r + 1) * kDhd + col] = S2[2 * m + h].y;
-    }
+  for (int nt = 0; nt < 4; ++nt) {
+    const int cc2 = j0 + 8 * nt + 2 * t;
+    state[sbase + (size_t)ra * kDhd + cc2] = accS[nt][0];
+    state[sbase + (size_t)ra * kDhd + cc2 + 1] = accS[nt][1];
+    state[sbase + (size_t)rb * kDhd + cc2] = accS[nt][2];
+    state[sbase + (size_t)rb * kDhd + cc2 + 1] = accS[nt][3];
+  }
   pdl_launch_dependents();
 }
 
@@ -351,9 +472,10 @@ __global__ void __launch_bounds__(256) delta_gated_norm_kernel(const float* o, c
   pdl_launch_dependents();
 }
 
-// workspace: qk fp32 [T, 2nk, D] | v fp16 [T, nv*D] | decay, beta fp32 [T, nv] | o fp32 [T, nv, D]
+// workspace: qk fp32 [T, 2nk, D] | v fp16 [T, nv*D] | g, beta fp32 [T, nv] | o fp32 [T, nv, D]
+// | chunk operand blocks [ceil(T/32), nv, kCkBlk] fp32
 struct DeltaWs {
-  size_t qk, v, decay, beta, o, total;
+  size_t qk, v, decay, beta, o, blocks, total;
 };
 static DeltaWs delta_ws(int T, int nk, int nv) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
@@ -363,7 +485,8 @@ static DeltaWs delta_ws(int T, int nk, int nv) {
   w.decay = up(w.v + (size_t)T * nv * kDhd * 2);
   w.beta = up(w.decay + (size_t)T * nv * 4);
   w.o = up(w.beta + (size_t)T * nv * 4);
-  w.total = up(w.o + (size_t)T * nv * kDhd * 4);
+  w.blocks = up(w.o + (size_t)T * nv * kDhd * 4);
+  w.total = up(w.blocks + (size_t)((T + kCk - 1) / kCk) * nv * kCkBlk * 4);
   return w;
 }
 
@@ -400,8 +523,12 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
   if (!attr_set[dev].load()) {
-    if (cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kScanSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(delta_chunk_scan_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(delta_chunk_prep_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+            cudaSuccess)
       return IQ36_ERR_CUDA;
     attr_set[dev].store(true);
   }
@@ -411,6 +538,7 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   float* dec = reinterpret_cast<float*>(ws + w.decay);
   float* bet = reinterpret_cast<float*>(ws + w.beta);
   float* o = reinterpret_cast<float*>(ws + w.o);
+  float* blocks = reinterpret_cast<float*>(ws + w.blocks);
   const cudaStream_t s = as_stream(stream);
   const int nseg = 2 * nk + nv, C = nseg * kDhd;
   cudaError_t e = launch(delta_conv_batch_kernel, dim3(ceil_div(T, kConvTok), ceil_div(nseg, 8)),
@@ -423,9 +551,12 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
     e = launch(delta_conv_state_kernel, dim3(ceil_div(C, 256)), dim3(256), 0, s,
                reinterpret_cast<const __half*>(qkv_f16), T, C, conv_state);
   if (e == cudaSuccess)
-    e = launch(delta_scan_kernel, dim3(kDhd / kScanCols, nv), dim3(32 * kScanWarps),
-               (size_t)kScanSmem, s, (const float*)qk, (const __half*)v, (const float*)dec,
-               (const float*)bet, state, o, T, nk, nv);
+    e = launch(delta_chunk_prep_kernel, dim3(ceil_div(T, kCk), nv), dim3(256), (size_t)kPrepSmem,
+               s, (const float*)qk, (const __half*)v, (const float*)dec, (const float*)bet, T, nk,
+               nv, blocks);
+  if (e == cudaSuccess)
+    e = launch(delta_chunk_scan_kernel, dim3(kDhd / kScCols, nv), dim3(256), (size_t)kScanSmem,
+               s, (const float*)blocks, state, o, T, nv);
   if (e == cudaSuccess)
     e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 8)), dim3(256), 0, s,
                (const float*)o, reinterpret_cast<const __half*>(z_f16), norm_w, eps, T * nv,

@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
 // replays the reduction of stage_x_plain's 256 threads: virtual thread
 // 32w + lane sums x[i]^2 over i = 32w + lane + 256m in order, each virtual
 // warp is butterfly-summed, then the 8 warp sums are butterfly-summed as
-// lanes 0..7 of one warp.
+// lanes 0..7 of one warp. The row is held in registers (H <= 2048).
 __global__ void __launch_bounds__(256) x_norm_plain_kernel(const float* x32, const float* nw,
                                                            float eps, int T, int H,
                                                            __half* xn) {
@@ -131,49 +131,65 @@ __global__ void __launch_bounds__(256) x_norm_plain_kernel(const float* x32, con
   const int t = blockIdx.x * 8 + warp;
   if (t < T) {
     const float* x = x32 + (size_t)t * H;
+    const int n = H / 32;  // values per lane: x[lane + 32k]
+    float xv[64];
+#pragma unroll
+    for (int k = 0; k < 64; ++k) xv[k] = k < n ? x[lane + 32 * k] : 0.f;
     float v = 0.0f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       float p = 0.0f;
-      for (int i = 32 * w + lane; i < H; i += 256) p = fmaf(x[i], x[i], p);
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+        if (w + 8 * m < n) p = fmaf(xv[w + 8 * m], xv[w + 8 * m], p);
       p = warp_sum(p);
       if (lane == w) v = p;
     }
     v = warp_sum(v);
     const float scale = rsqrtf(v / (float)H + eps);
     __half* o = xn + (size_t)t * H;
-    for (int i = lane; i < H; i += 32) o[i] = __float2half_rn(x[i] * scale * nw[i]);
+#pragma unroll
+    for (int k = 0; k < 64; ++k)
+      if (k < n) o[lane + 32 * k] = __float2half_rn(xv[k] * scale * nw[lane + 32 * k]);
   }
   pdl_launch_dependents();
 }
 
-constexpr int kRbTok = 32;   // tokens per CTA (staged in shared memory)
-constexpr int kRbRows = 16;  // router rows per CTA: 2 per warp
+constexpr int kRbTok = 32;  // tokens per CTA (staged in shared memory)
+constexpr int kRbGrp = 4;   // tokens in flight per warp (independent FMA chains)
 
 // logits[t, e] (and slogit[t] for the extra shared-gate row) for a tile of 32
-// tokens x 16 rows; each warp keeps its two weight rows in registers.
+// tokens x all rows: the tile's normalised inputs are staged once; each warp
+// walks row pairs r, r+1 (r = 2w, 2w+16, ...), the next pair's weights loaded
+// while the current pair is multiplied, 4 tokens x 2 rows = 8 independent
+// accumulation chains, each in the decode kernel's order (lane chunks
+// c = lane + 32j, fp32 FMA sequence of its dot8, the same butterfly).
 // Requires H % 256 == 0, H <= 2048.
-__global__ void __launch_bounds__(256) router_logits_batch_kernel(const __half* xn, int T, int H,
-                                                                  const __half* W, int E,
-                                                                  const __half* wsg,
-                                                                  float* logits, float* slogit) {
+__global__ void __launch_bounds__(256, 1) router_logits_batch_kernel(
+    const __half* xn, int T, int H, const __half* W, int E, const __half* wsg, float* logits,
+    float* slogit) {
   extern __shared__ __align__(16) uint4 xs4[];  // [kRbTok][H / 8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.y * kRbTok;
+  const int t0 = blockIdx.x * kRbTok;
   const int nt = min(kRbTok, T - t0);
   const int hc = H / 8, nch = H / 256;
   const int rows = E + (wsg != nullptr ? 1 : 0);
-  const int r0 = blockIdx.x * kRbRows + 2 * warp;
-  uint4 w[2][8];
+  auto row_ptr = [&](int r) -> const __half* {
+    return r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
+  };
+  auto load_pair = [&](int r, uint4 (&wv)[2][8]) {
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int r = r0 + q;
-    const __half* wr = r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
+    for (int q = 0; q < 2; ++q) {
+      const __half* wr = row_ptr(r + q);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      w[q][j] = (wr != nullptr && j < nch) ? ld_stream_v4(wr + (lane + 32 * j) * 8)
-                                           : make_uint4(0, 0, 0, 0);
-  }
+      for (int j = 0; j < 8; ++j)
+        wv[q][j] = (wr != nullptr && j < nch) ? ld_stream_v4(wr + (lane + 32 * j) * 8)
+                                              : make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 wcur[2][8], wnext[2][8];
+  int r = 2 * warp;
+  load_pair(r, wcur);
   pdl_wait();
   for (int i = threadIdx.x; i < nt * hc; i += blockDim.x)
     cp_async_16(smem_u32(xs4 + i), xn + (size_t)t0 * H + (size_t)i * 8, 16);
@@ -181,41 +197,59 @@ __global__ void __launch_bounds__(256) router_logits_batch_kernel(const __half* 
   cp_async_wait<0>();
   __syncthreads();
   pdl_launch_dependents();
-  if (r0 >= rows) return;
-  auto dot8 = [](const uint4& wv, const uint4& xv, float& acc) {
-    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
-    const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+  for (; r < rows; r += 16) {
+    if (r + 16 < rows) load_pair(r + 16, wnext);
+    for (int tg = 0; tg < nt; tg += kRbGrp) {
+      float acc[kRbGrp][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 wf = __half22float2(wh[j]);
-      const float2 xf = __half22float2(xh[j]);
-      acc = fmaf(wf.x, xf.x, acc);
-      acc = fmaf(wf.y, xf.y, acc);
-    }
-  };
-  for (int tt = 0; tt < nt; ++tt) {
-    float a0 = 0.f, a1 = 0.f;
-    const uint4* xr = xs4 + (size_t)tt * hc;
+      for (int g = 0; g < kRbGrp; ++g) acc[g][0] = acc[g][1] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (j < nch) {
-        const uint4 xv = xr[lane + 32 * j];
-        dot8(w[0][j], xv, a0);
-        dot8(w[1][j], xv, a1);
+      for (int j = 0; j < 8; ++j) {
+        if (j < nch) {
+          float2 wf[2][4];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const __half2* wh = reinterpret_cast<const __half2*>(&wcur[q][j]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) wf[q][e] = __half22float2(wh[e]);
+          }
+#pragma unroll
+          for (int g = 0; g < kRbGrp; ++g) {
+            const int tt = min(tg + g, nt - 1);
+            const uint4 xv = xs4[(size_t)tt * hc + lane + 32 * j];
+            const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 xf = __half22float2(xh[e]);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                acc[g][q] = fmaf(wf[q][e].x, xf.x, acc[g][q]);
+                acc[g][q] = fmaf(wf[q][e].y, xf.y, acc[g][q]);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kRbGrp; ++g) {
+        const float a0 = warp_sum(acc[g][0]);
+        const float a1 = warp_sum(acc[g][1]);
+        const int t = t0 + tg + g;
+        if (lane == 0 && tg + g < nt) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int rr = r + q;
+            const float a = q ? a1 : a0;
+            if (rr < E) logits[(size_t)t * E + rr] = a;
+            else if (rr == E && wsg != nullptr) slogit[t] = a;
+          }
+        }
       }
     }
-    a0 = warp_sum(a0);
-    a1 = warp_sum(a1);
-    if (lane == 0) {
-      const int t = t0 + tt;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int r = r0 + q;
-        const float a = q ? a1 : a0;
-        if (r < E) logits[(size_t)t * E + r] = a;
-        else if (r == E && wsg != nullptr) slogit[t] = a;
-      }
-    }
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wcur[q][j] = wnext[q][j];
   }
 }
 
@@ -615,10 +649,9 @@ int router_logits_batch_launch(const float* x32, const float* nw, float eps, int
   }
   cudaError_t e = launch(x_norm_plain_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream, x32, nw,
                          eps, T, H, xn);
-  const int rows = E + (w_sg ? 1 : 0);
   if (e == cudaSuccess)
-    e = launch(router_logits_batch_kernel, dim3(ceil_div(rows, kRbRows), ceil_div(T, kRbTok)),
-               dim3(256), smem, stream, (const __half*)xn, T, H,
+    e = launch(router_logits_batch_kernel, dim3(ceil_div(T, kRbTok)), dim3(256), smem, stream,
+               (const __half*)xn, T, H,
                reinterpret_cast<const __half*>(w_router), E,
                reinterpret_cast<const __half*>(w_sg), logits, slogit);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;

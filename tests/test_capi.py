@@ -119,3 +119,39 @@ def test_synth_spec_matches_oracle_header():
     assert kind.value == 2 and abs(lo.value - 1.0) < 1e-7
     assert n.lib().iq36_synth_tensor_id(-1, 2, 1) == (2 << 4) | 1
     assert n.lib().iq36_synth_tensor_id(3, 27, 0) == (4 << 16) | (27 << 4)
+
+
+def test_prompt_path_entries_reject_bad_arguments_on_host(native):
+    lib = native.lib()
+    # DeltaNet over a prompt: head_dim 64 unsupported, nv % nk != 0, workspace too small
+    ws = lib.iq36_delta_prefill_workspace_bytes(64, 16, 32)
+    assert ws > 0 and lib.iq36_delta_prefill_workspace_bytes(0, 16, 32) == 0
+    base = [16, 64, 16, 32, 128, 16, 16, 16, 16, 256, 16, 16, 16, 16, 16, 1e-6, 16, 256, ws, None]
+    bad = list(base)
+    bad[4] = 64
+    assert _status(native, "iq36_delta_prefill", *bad) == -2
+    bad = list(base)
+    bad[2] = 12
+    assert _status(native, "iq36_delta_prefill", *bad) == -2
+    bad = list(base)
+    bad[18] = ws - 1
+    assert _status(native, "iq36_delta_prefill", *bad) == -4
+    bad = list(base)
+    bad[0] = None
+    assert _status(native, "iq36_delta_prefill", *bad) == -1
+    # prompt attention: 12 query heads over 2 KV heads (group must be 8); bad dtype
+    args = [16, 16, 16, 16, 16, 16, 64, 12, 2, 256, 0.0625, None, 16, 1, None]
+    assert _status(native, "iq36_attn_prefill", *args) == -2
+    args[7], args[13] = 16, 7
+    assert _status(native, "iq36_attn_prefill", *args) == -1
+    # batched attention pre-step: zero tokens
+    assert _status(native, "iq36_attn_prep_batch", 16, 16, 16, 16, 16, 1e-6, 16, 0, 16, 2, 256,
+                   64, 1e7, 16, 16, 16, 16, 16, 16, None) == -2
+    # MoE layer over a prompt: null residual; workspace query
+    assert lib.iq36_moe_layer_prefill_workspace_bytes(4096, 8, 256, 2048, 512) > 0
+    assert lib.iq36_moe_layer_prefill_workspace_bytes(0, 8, 256, 2048, 512) == 0
+    bank = native.ExpertBankC(16, 16, 16, 16, 16, 16, 256, 2048, 512, 128)
+    assert _status(native, "iq36_moe_layer_prefill", None, 64, 2048, 16, 1e-6, 16, 16, 8,
+                   ctypes.byref(bank), None, 16, 16, 16, 256, 1 << 30, None) == -1
+    # embedding rows: T out of range
+    assert _status(native, "iq36_embed_batch", 16, 1000, 2048, 16, 0, 16, None) == -2
