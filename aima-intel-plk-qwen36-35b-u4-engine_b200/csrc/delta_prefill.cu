@@ -151,13 +151,29 @@ __global__ void __launch_bounds__(256) delta_conv_state_kernel(const __half* qkv
 // ---------------------------------------------------------------------------
 // 3./4. the recurrence in chunked form.
 
+// m16n8k8 TF32 tensor-core product with fp32 accumulate; A row-major 16x8
+// (a0 (g,t), a1 (g+8,t), a2 (g,t+4), a3 (g+8,t+4)), B 8x8 (b0 (k=t,n=g),
+// b1 (k=t+4,n=g)), C (c0,c1 (g,2t..), c2,c3 (g+8,2t..)).
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(hi) : "f"(x));
+  const float r = x - __uint_as_float(hi);
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(lo) : "f"(r));
+}
 constexpr int kCk = 32;  // tokens per chunk
 // Per (chunk, value head) operand block (floats): W [32][128], U [32][128],
 // Qg = e^G q [32][128], Kt = e^(G_last - G) k key-major [128][32], P [32][32],
 // gC = e^G_last.
 constexpr int kOffW = 0, kOffU = 4096, kOffQ = 8192, kOffKt = 12288, kOffPm = 16384,
               kOffGc = 17408, kCkBlk = 17412;
-constexpr int kPrepSmem = (2 * kCk * 132 + kCk * 128 + kCk * 33 + 4 * kCk) * 4;
+constexpr int kPrepSmem = (2 * kCk * 132 + kCk * 128 + kCk * 36 + 4 * kCk) * 4;
 
 __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __restrict__ qk,
                                                                const __half* __restrict__ v,
@@ -169,8 +185,8 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
   float* sk = sm;                  // k rows [32][132]
   float* sq = sk + kCk * 132;      // q rows [32][132]
   float* sv = sq + kCk * 132;      // v rows [32][128]
-  float* sA = sv + kCk * 128;      // A [32][33]
-  float* sB = sA + kCk * 33;       // beta [32]
+  float* sA = sv + kCk * 128;      // A [32][36]
+  float* sB = sA + kCk * 36;       // beta [32]
   float* sE = sB + kCk;            // e^G_r
   float* sL = sE + kCk;            // e^(G_last - G_r)
   float* sG = sL + kCk;            // G_r
@@ -210,30 +226,41 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
   }
   __syncthreads();
   float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
-  // A (strictly lower) and P (lower including the diagonal)
-  for (int i = tid; i < kCk * kCk; i += blockDim.x) {
-    const int r = i >> 5, s2 = i & 31;
-    float kk = 0.f, qk_ = 0.f;
-    const bool lower = s2 <= r && r < n;
-    if (lower) {
-#pragma unroll 8
-      for (int d = 0; d < kDhd; d += 4) {
-        const float4 ks = *reinterpret_cast<const float4*>(sk + s2 * 132 + d);
-        const float4 kr = *reinterpret_cast<const float4*>(sk + r * 132 + d);
-        const float4 qr = *reinterpret_cast<const float4*>(sq + r * 132 + d);
-        kk = fmaf(kr.x, ks.x, kk);
-        kk = fmaf(kr.y, ks.y, kk);
-        kk = fmaf(kr.z, ks.z, kk);
-        kk = fmaf(kr.w, ks.w, kk);
-        qk_ = fmaf(qr.x, ks.x, qk_);
-        qk_ = fmaf(qr.y, ks.y, qk_);
-        qk_ = fmaf(qr.z, ks.z, qk_);
-        qk_ = fmaf(qr.w, ks.w, qk_);
-      }
+  // K K^T and Q K^T (32 x 32, K = 128) on tensor cores, 3xTF32 (operands split
+  // on the fly); warp w: rows 16(w>>2).., columns 8(w&3)..
+  {
+    const int mt = warp >> 2, nt = warp & 3, g = lane >> 2, t = lane & 3;
+    float ck[4] = {0.f, 0.f, 0.f, 0.f}, cq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int ks = 0; ks < kDhd / 8; ++ks) {
+      uint32_t bh[2], bl[2], kh4[4], kl4[4], qh4[4], ql4[4];
+      const float* kb = sk + (8 * nt + g) * 132 + 8 * ks + t;  // B[k=d][n=s] = k_s[d]
+      split_tf32(kb[0], bh[0], bl[0]);
+      split_tf32(kb[4], bh[1], bl[1]);
+      const int o0 = (16 * mt + g) * 132 + 8 * ks + t, o1 = o0 + 8 * 132;
+      split_tf32(sk[o0], kh4[0], kl4[0]);
+      split_tf32(sk[o1], kh4[1], kl4[1]);
+      split_tf32(sk[o0 + 4], kh4[2], kl4[2]);
+      split_tf32(sk[o1 + 4], kh4[3], kl4[3]);
+      split_tf32(sq[o0], qh4[0], ql4[0]);
+      split_tf32(sq[o1], qh4[1], ql4[1]);
+      split_tf32(sq[o0 + 4], qh4[2], ql4[2]);
+      split_tf32(sq[o1 + 4], qh4[3], ql4[3]);
+      mma_tf32(ck, kl4, bh);
+      mma_tf32(ck, kh4, bl);
+      mma_tf32(ck, kh4, bh);
+      mma_tf32(cq, ql4, bh);
+      mma_tf32(cq, qh4, bl);
+      mma_tf32(cq, qh4, bh);
     }
-    const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
-    sA[r * 33 + s2] = s2 < r ? sB[r] * dec * kk : 0.f;
-    blk[kOffPm + r * kCk + s2] = dec * qk_;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = 16 * mt + g + (e >> 1) * 8, s2 = 8 * nt + 2 * t + (e & 1);
+      const bool lower = s2 <= r && r < n;
+      const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
+      sA[r * 36 + s2] = s2 < r && r < n ? sB[r] * dec * ck[e] : 0.f;
+      blk[kOffPm + r * kCk + s2] = dec * cq[e];
+    }
   }
   __syncthreads();
   // (I + A) X = [beta e^G k | beta v]: thread j owns column j, forward substitution
@@ -244,7 +271,13 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
     for (int r = 0; r < kCk; ++r) {
       float acc = j < kDhd ? sB[r] * sE[r] * sk[r * 132 + j] : sB[r] * sv[r * 128 + j - kDhd];
 #pragma unroll
-      for (int s2 = 0; s2 < r; ++s2) acc = fmaf(-sA[r * 33 + s2], x[s2], acc);
+      for (int q = 0; q < (r + 3) / 4; ++q) {
+        const float4 a4 = *reinterpret_cast<const float4*>(sA + r * 36 + 4 * q);
+        if (4 * q + 0 < r) acc = fmaf(-a4.x, x[4 * q + 0], acc);
+        if (4 * q + 1 < r) acc = fmaf(-a4.y, x[4 * q + 1], acc);
+        if (4 * q + 2 < r) acc = fmaf(-a4.z, x[4 * q + 2], acc);
+        if (4 * q + 3 < r) acc = fmaf(-a4.w, x[4 * q + 3], acc);
+      }
       x[r] = acc;
     }
     float* dst = blk + (j < kDhd ? kOffW + j : kOffU + j - kDhd);
@@ -261,22 +294,6 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
   pdl_launch_dependents();
 }
 
-// m16n8k8 TF32 tensor-core product with fp32 accumulate; A row-major 16x8
-// (a0 (g,t), a1 (g+8,t), a2 (g,t+4), a3 (g+8,t+4)), B 8x8 (b0 (k=t,n=g),
-// b1 (k=t+4,n=g)), C (c0,c1 (g,2t..), c2,c3 (g+8,2t..)).
-__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4],
-                                         const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(hi) : "f"(x));
-  const float r = x - __uint_as_float(hi);
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(lo) : "f"(r));
-}
 struct Tf32Frag4 {
   uint32_t hi[4], lo[4];
 };
@@ -307,7 +324,7 @@ __device__ __forceinline__ void mma3(float (&c)[4], const Tf32Frag4& a, const Tf
 constexpr int kScCols = 32;  // value columns per CTA
 // one chunk's operands in shared memory (floats), padded for conflict-free fragments
 constexpr int kStW = 0, kStQ = kCk * 132, kStU = 2 * kCk * 132, kStPm = kStU + kCk * 36,
-              kStKt = kStPm + kCk * 36, kStFloats = kStKt + kDhd * 36;
+              kStKt = kStPm + kCk * 36, kStGc = kStKt + kDhd * 36, kStFloats = kStGc + 4;
 constexpr int kScanSmem = (2 * kStFloats + kDhd * 40 + kCk * 40) * 4;
 
 // Grid (128/32 column blocks, nv), 8 warps. Warp w keeps state rows
@@ -340,6 +357,7 @@ __global__ void __launch_bounds__(256, 1)
       const int d = i >> 3, p = i & 7;
       cp_async_16(st + (kStKt + d * 36 + 4 * p) * 4, blk + kOffKt + d * kCk + 4 * p, 16);
     }
+    if (threadIdx.x == 0) cp_async_16(st + kStGc * 4, blk + kOffGc, 16);
   };
   pdl_wait();
   // state slice: rows 16w + g (+8), columns 8nt + 2t (+1)
@@ -409,7 +427,7 @@ __global__ void __launch_bounds__(256, 1)
       *reinterpret_cast<float2*>(o_out + ((size_t)(t0 + r1) * nv + h) * kDhd + j0 + cc) =
           make_float2(o[2], o[3]);
     // d: S = gC S + Kt^T Delta on this warp's key rows
-    const float gc = blocks[((size_t)c * nv + h) * kCkBlk + kOffGc];
+    const float gc = st[kStGc];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
