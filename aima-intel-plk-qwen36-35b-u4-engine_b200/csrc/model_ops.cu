@@ -575,3 +575,80 @@ extern "C" int iq36_decode_positions(int32_t* pos_dev, int32_t* ctx_dev, int32_t
                                pos_dev, ctx_dev, (int)advance);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------
+// u4 layout adapter: the reference's fixed-FC custom op takes each projection's
+// scales and zero points transposed to group-major order
+// (tools/intel_qwen36_openvino_fixed_fc.py:218-258: scale [groups, M] fp16,
+// zero points [groups, M] u4 packed low nibble first; the weight bytes
+// unchanged). These kernels map that form to and from the row-major
+// (OpenVINO compressed-constant) layout the kernels here read.
+namespace iq36 {
+// scale transpose through a 32 x 33 tile: out[c][r] = in[r][c], in [R, C]
+__global__ void __launch_bounds__(256) transpose_f16_kernel(const __half* in, int R, int C,
+                                                            __half* out) {
+  __shared__ __half tile[32][34];
+  pdl_wait();
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int y = ty; y < 32; y += 8) {
+    const int r = r0 + y, c = c0 + tx;
+    if (r < R && c < C) tile[y][tx] = in[(size_t)r * C + c];
+  }
+  __syncthreads();
+  for (int y = ty; y < 32; y += 8) {
+    const int c = c0 + y, r = r0 + tx;
+    if (c < C && r < R) out[(size_t)c * R + r] = tile[tx][y];
+  }
+  pdl_launch_dependents();
+}
+// nibble transpose: logical out[c * R + r] = in[r * C + c] (in [R, C], u4
+// packed two per byte, low nibble = even element); thread per output byte
+__global__ void __launch_bounds__(256) transpose_u4_kernel(const uint8_t* in, int R, int C,
+                                                           uint8_t* out) {
+  pdl_wait();
+  const size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t n = (size_t)R * C;
+  if (2 * j < n) {
+    uint32_t b = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const size_t e = 2 * j + h;  // output element (c, r)
+      if (e < n) {
+        const size_t c = e / R, r = e % R;
+        const size_t s = r * C + c;  // input element
+        b |= (uint32_t)((in[s >> 1] >> ((s & 1) * 4)) & 15u) << (4 * h);
+      }
+    }
+    out[j] = (uint8_t)b;
+  }
+  pdl_launch_dependents();
+}
+static int u4_layout_transpose(const void* scale_in, const uint8_t* zp_in, int R, int C,
+                               void* scale_out, uint8_t* zp_out, iq36_stream_t stream) {
+  if (!scale_in || !zp_in || !scale_out || !zp_out) return IQ36_ERR_ARG;
+  if (R < 1 || C < 1 || ((int64_t)R * C) % 2 || (int64_t)R * C > (1ll << 31)) return IQ36_ERR_SHAPE;
+  const cudaStream_t s = as_stream(stream);
+  cudaError_t e = launch(transpose_f16_kernel, dim3(ceil_div(C, 32), ceil_div(R, 32)), dim3(256),
+                         0, s, reinterpret_cast<const __half*>(scale_in), R, C,
+                         reinterpret_cast<__half*>(scale_out));
+  const int64_t nb = (int64_t)R * C / 2;
+  if (e == cudaSuccess)
+    e = launch(transpose_u4_kernel, dim3((unsigned)((nb + 255) / 256)), dim3(256), 0, s, zp_in, R,
+               C, zp_out);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+}  // namespace iq36
+
+extern "C" int iq36_u4_layout_from_group_major(const void* scale_gm_f16, const uint8_t* zp_gm,
+                                               int32_t rows, int32_t groups, void* scale_f16,
+                                               uint8_t* zp, iq36_stream_t stream) {
+  // group-major [groups, rows] -> row-major [rows, groups]
+  return iq36::u4_layout_transpose(scale_gm_f16, zp_gm, groups, rows, scale_f16, zp, stream);
+}
+
+extern "C" int iq36_u4_layout_to_group_major(const void* scale_f16, const uint8_t* zp,
+                                             int32_t rows, int32_t groups, void* scale_gm_f16,
+                                             uint8_t* zp_gm, iq36_stream_t stream) {
+  return iq36::u4_layout_transpose(scale_f16, zp, rows, groups, scale_gm_f16, zp_gm, stream);
+}

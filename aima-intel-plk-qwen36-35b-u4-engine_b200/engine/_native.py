@@ -103,6 +103,8 @@ _SIGS: dict[str, tuple] = {
     "iq36_embed_batch": (c_int, [_P, c_int32, c_int32, _P, c_int32, _P, _P]),
     "iq36_decode_positions": (c_int, [_P, _P, c_int32, _P]),
     "iq36_argmax": (c_int, [_P, c_int32, _P, _P, c_size_t, _P]),
+    "iq36_u4_layout_from_group_major": (c_int, [_P, _P, c_int32, c_int32, _P, _P, _P]),
+    "iq36_u4_layout_to_group_major": (c_int, [_P, _P, c_int32, c_int32, _P, _P, _P]),
     "iq36_argmax_workspace_bytes": (c_size_t, []),
     "iq36_synth_fill": (c_int, [_P, c_int64, c_int32, c_uint64, c_uint64, c_float, c_float, _P]),
     "iq36_synth_tensor_id": (c_uint64, [c_int32, c_int32, c_int32]),

@@ -387,6 +387,21 @@ int iq36_embed(const void* table_f16, int32_t vocab, int32_t hidden, const int32
 int iq36_embed_batch(const void* table_f16, int32_t vocab, int32_t hidden,
                      const int32_t* tokens_dev, int32_t T, float* h, iq36_stream_t stream);
 
+/* u4 layout adapter. The reference's fixed-FC custom op consumes each
+ * projection's scales and zero points in group-major order
+ * (tools/intel_qwen36_openvino_fixed_fc.py:218-258: scale fp16 [groups, rows],
+ * zero points u4 [groups, rows] packed two per byte, low nibble first; the u4
+ * weight bytes unchanged). from_group_major writes the row-major layout of
+ * this header (scale [rows, groups], zp [rows*groups] packed) from that form;
+ * to_group_major is the inverse. rows*groups must be even. No counterpart
+ * call in the reference (it repacks on the host while building the graph). */
+int iq36_u4_layout_from_group_major(const void* scale_gm_f16, const uint8_t* zp_gm,
+                                    int32_t rows, int32_t groups, void* scale_f16, uint8_t* zp,
+                                    iq36_stream_t stream);
+int iq36_u4_layout_to_group_major(const void* scale_f16, const uint8_t* zp, int32_t rows,
+                                  int32_t groups, void* scale_gm_f16, uint8_t* zp_gm,
+                                  iq36_stream_t stream);
+
 /* Greedy top-1 over fp32 logits, lowest id on ties: per-block maxima of the
  * 64-bit key (order-preserving fp32 bits, inverted id), then one merge block
  * (engine/openvino/custom/iq36_greedy_top1.cl:8-46 and
