@@ -321,20 +321,50 @@ __device__ __forceinline__ void mma3(float (&c)[4], const Tf32Frag4& a, const Tf
   mma_tf32(c, a.hi, b.hi);
 }
 
+// fragments from operands already split (hi bits and lo bits in two arrays of one layout)
+__device__ __forceinline__ Tf32Frag2 frag_b_pre(const float* hi, const float* lo, int ld, int g,
+                                                int t) {
+  Tf32Frag2 f;
+  f.hi[0] = __float_as_uint(hi[t * ld + g]);
+  f.hi[1] = __float_as_uint(hi[(t + 4) * ld + g]);
+  f.lo[0] = __float_as_uint(lo[t * ld + g]);
+  f.lo[1] = __float_as_uint(lo[(t + 4) * ld + g]);
+  return f;
+}
+__device__ __forceinline__ void put_split(float* hi, float* lo, int i, float x) {
+  uint32_t h, l;
+  split_tf32(x, h, l);
+  hi[i] = __uint_as_float(h);
+  lo[i] = __uint_as_float(l);
+}
+
 constexpr int kScCols = 32;  // value columns per CTA
 // one chunk's operands in shared memory (floats), padded for conflict-free fragments
 constexpr int kStW = 0, kStQ = kCk * 132, kStU = 2 * kCk * 132, kStPm = kStU + kCk * 36,
               kStKt = kStPm + kCk * 36, kStGc = kStKt + kDhd * 36, kStFloats = kStGc + 4;
-constexpr int kScanSmem = (2 * kStFloats + kDhd * 40 + kCk * 40) * 4;
+constexpr int kPartLd = 40;                             // partial-sum row stride
+constexpr int kPartFloats = 8 * 2 * 16 * kPartLd;       // [warp][product][16][40]
+constexpr int kScanSmem =
+    (2 * kStFloats + 2 * kDhd * 40 + 2 * kCk * 40 + kCk * 40 + kPartFloats) * 4;
 
 // Grid (128/32 column blocks, nv), 8 warps. Warp w keeps state rows
-// 16w..16w+15 (key) x the CTA's 32 value columns as mma accumulators.
+// 16w..16w+15 (key) x the CTA's 32 value columns as mma accumulators. Per chunk:
+//  b. Delta = U - W S and Oa = Qg S: warp w multiplies rows 16(w&1).. over the
+//     key quarter 32(w>>1).. for all 32 columns (its W / Qg fragments split
+//     once), then the four key-quarter partials are summed in shared memory;
+//  c. O = Oa + P Delta on a 16 x 8 tile per warp;
+//  d. S = gC S + Kt^T Delta on the warp's own state rows.
+// S and Delta are stored split (tf32 hi / lo) by the threads that produce them.
 __global__ void __launch_bounds__(256, 1)
     delta_chunk_scan_kernel(const float* __restrict__ blocks, float* __restrict__ state,
                             float* __restrict__ o_out, int T, int nv) {
   extern __shared__ __align__(16) float sm[];
-  float* sS = sm + 2 * kStFloats;  // state [128][40] (B operand)
-  float* sD = sS + kDhd * 40;      // Delta [32][40] (B operand)
+  float* sSh = sm + 2 * kStFloats;  // state hi [128][40] (B operand)
+  float* sSl = sSh + kDhd * 40;     // state lo
+  float* sDh = sSl + kDhd * 40;     // Delta hi [32][40] (B operand)
+  float* sDl = sDh + kCk * 40;      // Delta lo
+  float* sOa = sDl + kCk * 40;      // Oa [32][40]
+  float* sPart = sOa + kCk * 40;    // step-b partials
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y, j0 = blockIdx.x * kScCols;
@@ -364,6 +394,16 @@ __global__ void __launch_bounds__(256, 1)
   float accS[4][4];
   const size_t sbase = (size_t)h * kDhd * kDhd;
   const int ra = 16 * warp + g, rb = ra + 8;
+  auto put_state = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int cc = 8 * nt + 2 * t;
+      put_split(sSh, sSl, ra * 40 + cc, accS[nt][0]);
+      put_split(sSh, sSl, ra * 40 + cc + 1, accS[nt][1]);
+      put_split(sSh, sSl, rb * 40 + cc, accS[nt][2]);
+      put_split(sSh, sSl, rb * 40 + cc + 1, accS[nt][3]);
+    }
+  };
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     const int cc = j0 + 8 * nt + 2 * t;
@@ -371,14 +411,12 @@ __global__ void __launch_bounds__(256, 1)
     accS[nt][1] = state[sbase + (size_t)ra * kDhd + cc + 1];
     accS[nt][2] = state[sbase + (size_t)rb * kDhd + cc];
     accS[nt][3] = state[sbase + (size_t)rb * kDhd + cc + 1];
-    sS[ra * 40 + 8 * nt + 2 * t] = accS[nt][0];
-    sS[ra * 40 + 8 * nt + 2 * t + 1] = accS[nt][1];
-    sS[rb * 40 + 8 * nt + 2 * t] = accS[nt][2];
-    sS[rb * 40 + 8 * nt + 2 * t + 1] = accS[nt][3];
   }
+  put_state();
   load_stage(0, 0);
   cp_async_commit();
-  const int mw = warp >> 2, nw = warp & 3;  // tile of Delta / O owned in steps b, c
+  const int mt = warp & 1, kq = warp >> 1;  // step b: row tile, key quarter
+  const int mw = warp >> 2, nw = warp & 3;  // step c: O tile
   for (int c = 0; c < nchunks; ++c) {
     const int buf = c & 1;
     if (c + 1 < nchunks) {
@@ -390,33 +428,62 @@ __global__ void __launch_bounds__(256, 1)
     }
     __syncthreads();
     const float* st = stage(buf);
-    // b: Delta = U - W S and Oa = Qg S for rows 16mw.., columns 8nw..
-    float accD[2][4] = {}, accO[2][4] = {};
-#pragma unroll 4
-    for (int ks = 0; ks < kDhd / 8; ++ks) {
-      const int hf = ks & 1;
-      const Tf32Frag2 bS = frag_b(sS + 8 * ks * 40 + 8 * nw, 40, g, t);
-      const Tf32Frag4 aW = frag_a(st + kStW + 16 * mw * 132 + 8 * ks, 132, g, t);
-      mma3(accD[hf], aW, bS);
-      const Tf32Frag4 aQ = frag_a(st + kStQ + 16 * mw * 132 + 8 * ks, 132, g, t);
-      mma3(accO[hf], aQ, bS);
-    }
-    const int r0 = 16 * mw + g, r1 = r0 + 8, cc = 8 * nw + 2 * t;
+    // b: partial W S and Qg S over this warp's key quarter
     {
-      const float* sU = st + kStU;
-      sD[r0 * 40 + cc] = sU[r0 * 36 + cc] - (accD[0][0] + accD[1][0]);
-      sD[r0 * 40 + cc + 1] = sU[r0 * 36 + cc + 1] - (accD[0][1] + accD[1][1]);
-      sD[r1 * 40 + cc] = sU[r1 * 36 + cc] - (accD[0][2] + accD[1][2]);
-      sD[r1 * 40 + cc + 1] = sU[r1 * 36 + cc + 1] - (accD[0][3] + accD[1][3]);
+      float pd[4][4] = {}, po[4][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int k0 = 32 * kq + 8 * ks;
+        const Tf32Frag4 aW = frag_a(st + kStW + 16 * mt * 132 + k0, 132, g, t);
+        const Tf32Frag4 aQ = frag_a(st + kStQ + 16 * mt * 132 + k0, 132, g, t);
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const Tf32Frag2 bS = frag_b_pre(sSh + k0 * 40 + 8 * nt, sSl + k0 * 40 + 8 * nt, 40, g, t);
+          mma3(pd[nt], aW, bS);
+          mma3(po[nt], aQ, bS);
+        }
+      }
+      float* pw = sPart + warp * 2 * 16 * kPartLd;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int cc = 8 * nt + 2 * t;
+        *reinterpret_cast<float2*>(pw + g * kPartLd + cc) = make_float2(pd[nt][0], pd[nt][1]);
+        *reinterpret_cast<float2*>(pw + (g + 8) * kPartLd + cc) = make_float2(pd[nt][2], pd[nt][3]);
+        *reinterpret_cast<float2*>(pw + 16 * kPartLd + g * kPartLd + cc) =
+            make_float2(po[nt][0], po[nt][1]);
+        *reinterpret_cast<float2*>(pw + 16 * kPartLd + (g + 8) * kPartLd + cc) =
+            make_float2(po[nt][2], po[nt][3]);
+      }
+    }
+    __syncthreads();
+    // sum the key quarters: thread -> row r (0..31), columns 4c4..4c4+3
+    {
+      const int r = threadIdx.x >> 3, c4 = threadIdx.x & 7;
+      const int m = r >> 4, rr = r & 15;
+      float4 d = make_float4(0.f, 0.f, 0.f, 0.f), o = d;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float* pw = sPart + (2 * q + m) * 2 * 16 * kPartLd;
+        const float4 a = *reinterpret_cast<const float4*>(pw + rr * kPartLd + 4 * c4);
+        const float4 b = *reinterpret_cast<const float4*>(pw + 16 * kPartLd + rr * kPartLd + 4 * c4);
+        d.x += a.x; d.y += a.y; d.z += a.z; d.w += a.w;
+        o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
+      }
+      const float4 u = *reinterpret_cast<const float4*>(st + kStU + r * 36 + 4 * c4);
+      const float dv[4] = {u.x - d.x, u.y - d.y, u.z - d.z, u.w - d.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) put_split(sDh, sDl, r * 40 + 4 * c4 + e, dv[e]);
+      *reinterpret_cast<float4*>(sOa + r * 40 + 4 * c4) = o;
     }
     __syncthreads();
     // c: O = Oa + P Delta
-    float o[4] = {accO[0][0] + accO[1][0], accO[0][1] + accO[1][1], accO[0][2] + accO[1][2],
-                  accO[0][3] + accO[1][3]};
+    const int r0 = 16 * mw + g, r1 = r0 + 8, cc = 8 * nw + 2 * t;
+    float o[4] = {sOa[r0 * 40 + cc], sOa[r0 * 40 + cc + 1], sOa[r1 * 40 + cc],
+                  sOa[r1 * 40 + cc + 1]};
 #pragma unroll
     for (int ks = 0; ks < kCk / 8; ++ks) {
       const Tf32Frag4 aP = frag_a(st + kStPm + 16 * mw * 36 + 8 * ks, 36, g, t);
-      const Tf32Frag2 bD = frag_b(sD + 8 * ks * 40 + 8 * nw, 40, g, t);
+      const Tf32Frag2 bD = frag_b_pre(sDh + 8 * ks * 40 + 8 * nw, sDl + 8 * ks * 40 + 8 * nw, 40, g, t);
       mma3(o, aP, bD);
     }
     const int t0 = c * kCk, n = min(kCk, T - t0);
@@ -437,18 +504,14 @@ __global__ void __launch_bounds__(256, 1)
       const Tf32Frag4 aK = frag_a(st + kStKt + 16 * warp * 36 + 8 * ks, 36, g, t);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        const Tf32Frag2 bD = frag_b(sD + 8 * ks * 40 + 8 * nt, 40, g, t);
+        const Tf32Frag2 bD =
+            frag_b_pre(sDh + 8 * ks * 40 + 8 * nt, sDl + 8 * ks * 40 + 8 * nt, 40, g, t);
         mma3(accS[nt], aK, bD);
       }
     }
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      sS[ra * 40 + 8 * nt + 2 * t] = accS[nt][0];
-      sS[ra * 40 + 8 * nt + 2 * t + 1] = accS[nt][1];
-      sS[rb * 40 + 8 * nt + 2 * t] = accS[nt][2];
-      sS[rb * 40 + 8 * nt + 2 * t + 1] = accS[nt][3];
-    }
-    __syncthreads();  // sS complete for the next chunk; this stage is refilled next
+    __syncthreads();  // every warp is done reading S (step b) and Delta before they change
+    put_state();
+    // the next iteration's first barrier publishes S; this stage is refilled after it
   }
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {

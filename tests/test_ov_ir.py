@@ -93,9 +93,9 @@ def test_layout_adapter_kernels_match_reference_repack(cuda, case):
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
     s_out = torch.empty(m, groups, dtype=torch.float16, device=cuda)
     z_out = torch.empty(m * groups // 2, dtype=torch.uint8, device=cuda)
-    N.call("iq36_u4_layout_from_group_major", t(G[f"{case}_scale_gm"]).data_ptr(),
-           t(G[f"{case}_zp_gm"]).data_ptr(), m, groups, s_out.data_ptr(), z_out.data_ptr(),
-           _stream(cuda))
+    s_in, z_in = t(G[f"{case}_scale_gm"]), t(G[f"{case}_zp_gm"])  # held across the launch
+    N.call("iq36_u4_layout_from_group_major", s_in.data_ptr(), z_in.data_ptr(), m, groups,
+           s_out.data_ptr(), z_out.data_ptr(), _stream(cuda))
     np.testing.assert_array_equal(s_out.cpu().numpy(), G[f"{case}_scale"])
     np.testing.assert_array_equal(z_out.cpu().numpy(), G[f"{case}_zp"])
     s_gm = torch.empty(groups * m, dtype=torch.float16, device=cuda)
