@@ -155,101 +155,93 @@ __global__ void __launch_bounds__(256) x_norm_plain_kernel(const float* x32, con
   pdl_launch_dependents();
 }
 
-constexpr int kRbTok = 32;  // tokens per CTA (staged in shared memory)
-constexpr int kRbGrp = 4;   // tokens in flight per warp (independent FMA chains)
+constexpr int kRbTok = 28;  // tokens per CTA (fp32 tile in shared memory: 224 KB at H = 2048)
+constexpr int kRbRows = 4;  // router rows per warp and round
 
-// logits[t, e] (and slogit[t] for the extra shared-gate row) for a tile of 32
-// tokens x all rows: the tile's normalised inputs are staged once; each warp
-// walks row pairs r, r+1 (r = 2w, 2w+16, ...), the next pair's weights loaded
-// while the current pair is multiplied, 4 tokens x 2 rows = 8 independent
-// accumulation chains, each in the decode kernel's order (lane chunks
-// c = lane + 32j, fp32 FMA sequence of its dot8, the same butterfly).
+// logits[t, e] (and slogit[t] for the extra shared-gate row) for a tile of 28
+// tokens x all rows. The tile's normalised inputs are staged once as fp32
+// (exact: they are fp16 values), so the inner loop is loads and FMAs only;
+// each warp takes 4 rows per round, converts their 8-element weight chunk once
+// and applies it to all 28 tokens: 112 independent accumulation chains, each
+// in the decode kernel's order (lane chunks c = lane + 32j, the element order
+// of its dot8, the same butterfly), so the logits are bit-identical to it.
 // Requires H % 256 == 0, H <= 2048.
 __global__ void __launch_bounds__(256, 1) router_logits_batch_kernel(
     const __half* xn, int T, int H, const __half* W, int E, const __half* wsg, float* logits,
     float* slogit) {
-  extern __shared__ __align__(16) uint4 xs4[];  // [kRbTok][H / 8]
+  extern __shared__ __align__(16) float xtile[];  // [kRbTok][H] fp32
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRbTok;
   const int nt = min(kRbTok, T - t0);
-  const int hc = H / 8, nch = H / 256;
+  const int nch = H / 256;
   const int rows = E + (wsg != nullptr ? 1 : 0);
-  auto row_ptr = [&](int r) -> const __half* {
-    return r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
-  };
-  auto load_pair = [&](int r, uint4 (&wv)[2][8]) {
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const __half* wr = row_ptr(r + q);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        wv[q][j] = (wr != nullptr && j < nch) ? ld_stream_v4(wr + (lane + 32 * j) * 8)
-                                              : make_uint4(0, 0, 0, 0);
-    }
-  };
-  uint4 wcur[2][8], wnext[2][8];
-  int r = 2 * warp;
-  load_pair(r, wcur);
   pdl_wait();
-  for (int i = threadIdx.x; i < nt * hc; i += blockDim.x)
-    cp_async_16(smem_u32(xs4 + i), xn + (size_t)t0 * H + (size_t)i * 8, 16);
-  cp_async_commit();
-  cp_async_wait<0>();
+  for (int i = threadIdx.x; i < nt * H / 8; i += blockDim.x) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(xn + (size_t)t0 * H + (size_t)i * 8);
+    const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+    // chunk i's elements 0..3 and 4..7 go to the first and second half of the
+    // token's row, so a warp's 16-byte loads are consecutive (no bank conflicts)
+    const int tt = i / (H / 8), cidx = i % (H / 8);
+    float* row = xtile + (size_t)tt * H;
+    const float2 a = __half22float2(hp[0]), b = __half22float2(hp[1]);
+    const float2 c = __half22float2(hp[2]), e = __half22float2(hp[3]);
+    *reinterpret_cast<float4*>(row + 4 * cidx) = make_float4(a.x, a.y, b.x, b.y);
+    *reinterpret_cast<float4*>(row + H / 2 + 4 * cidx) = make_float4(c.x, c.y, e.x, e.y);
+  }
   __syncthreads();
   pdl_launch_dependents();
-  for (; r < rows; r += 16) {
-    if (r + 16 < rows) load_pair(r + 16, wnext);
-    for (int tg = 0; tg < nt; tg += kRbGrp) {
-      float acc[kRbGrp][2];
+  for (int r0 = kRbRows * warp; r0 < rows; r0 += kRbRows * 8) {
+    const __half* wr[kRbRows];
 #pragma unroll
-      for (int g = 0; g < kRbGrp; ++g) acc[g][0] = acc[g][1] = 0.f;
+    for (int q = 0; q < kRbRows; ++q) {
+      const int r = r0 + q;
+      wr[q] = r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
+    }
+    float acc[kRbTok][kRbRows];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < nch) {
-          float2 wf[2][4];
+    for (int tt = 0; tt < kRbTok; ++tt)
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const __half2* wh = reinterpret_cast<const __half2*>(&wcur[q][j]);
+      for (int q = 0; q < kRbRows; ++q) acc[tt][q] = 0.f;
+    for (int j = 0; j < nch; ++j) {
+      const int c = lane + 32 * j;  // this lane's 8-element chunk
+      float wf[kRbRows][8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) wf[q][e] = __half22float2(wh[e]);
-          }
+      for (int q = 0; q < kRbRows; ++q) {
+        const uint4 raw = wr[q] != nullptr ? ld_stream_v4(wr[q] + c * 8) : make_uint4(0, 0, 0, 0);
+        const __half2* wh = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-          for (int g = 0; g < kRbGrp; ++g) {
-            const int tt = min(tg + g, nt - 1);
-            const uint4 xv = xs4[(size_t)tt * hc + lane + 32 * j];
-            const __half2* xh = reinterpret_cast<const __half2*>(&xv);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 xf = __half22float2(xh[e]);
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                acc[g][q] = fmaf(wf[q][e].x, xf.x, acc[g][q]);
-                acc[g][q] = fmaf(wf[q][e].y, xf.y, acc[g][q]);
-              }
-            }
-          }
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(wh[e]);
+          wf[q][2 * e] = f.x;
+          wf[q][2 * e + 1] = f.y;
         }
       }
 #pragma unroll
-      for (int g = 0; g < kRbGrp; ++g) {
-        const float a0 = warp_sum(acc[g][0]);
-        const float a1 = warp_sum(acc[g][1]);
-        const int t = t0 + tg + g;
-        if (lane == 0 && tg + g < nt) {
+      for (int tt = 0; tt < kRbTok; ++tt) {
+        if (tt < nt) {
+          const float4 x0 = *reinterpret_cast<const float4*>(xtile + (size_t)tt * H + c * 4);
+          const float4 x1 =
+              *reinterpret_cast<const float4*>(xtile + (size_t)tt * H + H / 2 + c * 4);
+          const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int rr = r + q;
-            const float a = q ? a1 : a0;
-            if (rr < E) logits[(size_t)t * E + rr] = a;
-            else if (rr == E && wsg != nullptr) slogit[t] = a;
-          }
+          for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int q = 0; q < kRbRows; ++q) acc[tt][q] = fmaf(wf[q][e], xv[e], acc[tt][q]);
         }
       }
     }
 #pragma unroll
-    for (int q = 0; q < 2; ++q)
+    for (int tt = 0; tt < kRbTok; ++tt) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wcur[q][j] = wnext[q][j];
+      for (int q = 0; q < kRbRows; ++q) {
+        const float a = warp_sum(acc[tt][q]);
+        const int r = r0 + q;
+        if (lane == 0 && tt < nt) {
+          if (r < E) logits[(size_t)(t0 + tt) * E + r] = a;
+          else if (r == E && wsg != nullptr) slogit[t0 + tt] = a;
+        }
+      }
+    }
   }
 }
 
@@ -636,14 +628,14 @@ int router_logits_batch_launch(const float* x32, const float* nw, float eps, int
   if (H < 256 || H % 256 || H > 2048) return IQ36_ERR_SHAPE;
   if (!aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) || !aligned(xn, 16))
     return IQ36_ERR_ALIGN;
-  const size_t smem = (size_t)kRbTok * H * 2;
+  const size_t smem = (size_t)kRbTok * H * 4;
   static std::atomic<bool> attr_set[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
   if (!attr_set[dev].load()) {
     if (cudaFuncSetAttribute(router_logits_batch_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kRbTok * 2048 * 2) != cudaSuccess)
+                             kRbTok * 2048 * 4) != cudaSuccess)
       return IQ36_ERR_CUDA;
     attr_set[dev].store(true);
   }
