@@ -415,7 +415,24 @@ struct GemmArgs {
   int out_dtype;        // MODE 2: IQ36_F16 store or IQ36_F32
   int accumulate;       // MODE 2, fp32: out += f16(x W^T)
   const float* row_gate;  // MODE 2: optional per-row logit; output *= sigmoid(logit)
+  // MODE 2 over up to 4 projections sharing x: N tile n belongs to projection p
+  // with tile_base[p] <= n < tile_base[p + 1] (H = the projections' total rows)
+  int n_proj;
+  int tile_base[5];
+  const __half* ps[4];
+  const uint8_t* pz[4];
+  void* pout[4];
+  int prow[4], pdt[4], pacc[4];
 };
+
+// projection of a MODE-2 N tile and the tile's index inside it
+__device__ __forceinline__ void pf_proj(const GemmArgs& g, int nt, int& p, int& ntl) {
+  p = 0;
+#pragma unroll
+  for (int i = 1; i < 4; ++i)
+    if (i < g.n_proj && nt >= g.tile_base[i]) p = i;
+  ntl = nt - g.tile_base[p];
+}
 
 template <int MODE>
 __device__ __forceinline__ int pf_units(const GemmArgs& g) {
@@ -440,6 +457,7 @@ __device__ __forceinline__ void pf_rows(const GemmArgs& g, int mt, int& row0, in
 struct PfUnit {
   int row0, rows;
   int64_t wr0, wr1;  // first weight row of each 128-row half of the B tile
+  int proj;          // MODE 2: projection of the tile
 };
 
 template <int MODE>
@@ -447,8 +465,11 @@ __device__ __forceinline__ PfUnit pf_unit(const GemmArgs& g, int u, int nN) {
   const int mt = u / nN, nt = u - mt * nN;
   PfUnit r;
   pf_rows<MODE>(g, mt, r.row0, r.rows);
+  r.proj = 0;
   if (MODE == 2) {
-    r.wr0 = (int64_t)nt * kPfBN;
+    int ntl;
+    pf_proj(g, nt, r.proj, ntl);
+    r.wr0 = (int64_t)ntl * kPfBN;
     r.wr1 = r.wr0 + 128;
     return r;
   }
@@ -471,7 +492,9 @@ __device__ __forceinline__ PfUnit pf_unit(const GemmArgs& g, int u, int nN) {
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
     pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmW1,
+                   const __grid_constant__ CUtensorMap tmW2,
+                   const __grid_constant__ CUtensorMap tmW3, GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
@@ -588,10 +611,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t sdst = base + kPfOffScale + b * kPfScaleBuf;
         const uint32_t zdst = base + kPfOffZp + b * kPfZpBuf;
         mbar_arrive_tx(bar_sfull + 8 * b, 2u * (sbytes + zbytes));
-        bulk_load(sdst, g.s + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
-        bulk_load(sdst + sbytes, g.s + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
-        bulk_load(zdst, g.z + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
-        bulk_load(zdst + zbytes, g.z + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
+        const __half* sp = MODE == 2 ? g.ps[un.proj] : g.s;
+        const uint8_t* zp = MODE == 2 ? g.pz[un.proj] : g.z;
+        const CUtensorMap* wmap = un.proj == 0 ? &tmW : un.proj == 1 ? &tmW1 : un.proj == 2 ? &tmW2 : &tmW3;
+        bulk_load(sdst, sp + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
+        bulk_load(sdst + sbytes, sp + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
+        bulk_load(zdst, zp + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
+        bulk_load(zdst + zbytes, zp + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
         // nkb is a multiple of kPfCodeKB, so code blocks never straddle units
         for (int cb = 0; cb < nkb / kPfCodeKB; ++cb, ++it) {
           const int cs = it % kPfCodeStages;
@@ -599,8 +625,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           if (!ok) break;
           const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
           mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
-          tma_load_2d(dst, &tmW, cb * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
-          tma_load_2d(dst + kPfCodeStage / 2, &tmW, cb * kPfCodeRow, (int)un.wr1,
+          tma_load_2d(dst, wmap, cb * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
+          tma_load_2d(dst + kPfCodeStage / 2, wmap, cb * kPfCodeRow, (int)un.wr1,
                       bar_cfull + 8 * cs);
         }
       }
@@ -725,6 +751,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
       } else if (MODE == 2) {
+        int pj, ntl;
+        pf_proj(g, nt, pj, ntl);
+        void* const pout = g.pout[pj];
+        const int prow = g.prow[pj], pdt = g.pdt[pj], pacc = g.pacc[pj];
         const float rg =
             (g.row_gate != nullptr && m < rows) ? sigmoidf_acc(g.row_gate[row0 + m]) : 1.f;
         for (int j = 0; j < kPfBN; j += 16) {
@@ -736,25 +766,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int q = 0; q < 16; ++q) yv[q] = __float_as_uint(__uint_as_float(yv[q]) * rg);
           }
           if (m < rows) {
-            const size_t o = (size_t)(row0 + m) * g.H + nt * kPfBN + j;
-            if (g.out_dtype == IQ36_F16) {
+            const size_t o = (size_t)(row0 + m) * prow + ntl * kPfBN + j;
+            if (pdt == IQ36_F16) {
               uint4 h[2];
               uint32_t* hw = reinterpret_cast<uint32_t*>(h);
 #pragma unroll
               for (int q = 0; q < 8; ++q)
                 hw[q] = pack_half2(__float2half_rn(__uint_as_float(yv[2 * q])),
                                    __float2half_rn(__uint_as_float(yv[2 * q + 1])));
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g.out) + o);
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(pout) + o);
               dst[0] = h[0];
               dst[1] = h[1];
             } else {
-              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(g.out) + o);
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(pout) + o);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 float4 v = make_float4(__uint_as_float(yv[4 * q]), __uint_as_float(yv[4 * q + 1]),
                                        __uint_as_float(yv[4 * q + 2]),
                                        __uint_as_float(yv[4 * q + 3]));
-                if (g.accumulate) {
+                if (pacc) {
                   // residual += the fp16-rounded projection output
                   const float4 r = dst[q];
                   v.x = r.x + __half2float(__float2half_rn(v.x));
@@ -962,11 +992,11 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
   const int grid2 = std::max(1, std::min(sms, maxt * (H / kPfBN)));
   if (e == cudaSuccess)
     e = launch(pf_gemm_kernel<0>, dim3(grid1), dim3(kPfThreads), (size_t)kPfSmem, stream,
-               map_x, map_gu, g1);
+               map_x, map_gu, map_gu, map_gu, map_gu, g1);
   GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
   if (e == cudaSuccess)
     e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
-               map_act, map_d, g2);
+               map_act, map_d, map_d, map_d, map_d, g2);
   if (e == cudaSuccess)
     e = launch(pf_scatter_kernel, dim3(T), dim3(256), 0, stream, (const int32_t*)w.inv,
                (const __half*)w.y, T, H, k, out, out_dtype, accumulate);
@@ -1027,35 +1057,47 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const void* x, int x_dt
 
 size_t u4_gemm_ws(int T, int K) { return up256((size_t)(T + kPfBM) * K * 2) + 256; }
 
-// swiglu: W holds [gate; up] (2I rows); out[T, I] fp16 = SwiGLU of the two halves.
-// row_gate (fp32 [T], optional, fp32 out only): each output row * sigmoid(row_gate[t]).
-int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T, int K, int G,
-                   const iq36_u4_matrix* w, void* out, int out_dtype, int accumulate, void* ws,
-                   size_t ws_bytes, cudaStream_t stream, int swiglu = 0,
-                   const float* row_gate = nullptr) {
-  if (!x || !w || !w->weight || !w->scale || !w->zp || !out) return IQ36_ERR_ARG;
-  if (swiglu && (out_dtype != IQ36_F16 || accumulate || row_gate || w->rows % 256))
-    return IQ36_ERR_ARG;
-  if (row_gate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
+// Up to 4 projections sharing x (all K columns): out_p[T, rows_p] = x W_p^T.
+// swiglu (one projection): W holds [gate; up] (2I rows); out[T, I] fp16 = SwiGLU
+// of the two halves. row_gate (fp32 [T], optional, fp32 out only): each output
+// row * sigmoid(row_gate[t]).
+int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps, int T, int K,
+                         int G, int n_proj, const iq36_u4_projection* proj, void* ws,
+                         size_t ws_bytes, cudaStream_t stream, int swiglu = 0,
+                         const float* row_gate = nullptr) {
+  if (!x || !proj || n_proj < 1 || n_proj > 4) return IQ36_ERR_ARG;
   if (x_dtype != IQ36_F32 && x_dtype != IQ36_F16) return IQ36_ERR_ARG;
   if (nw && x_dtype != IQ36_F32) return IQ36_ERR_ARG;
-  if (out_dtype != IQ36_F32 && out_dtype != IQ36_F16) return IQ36_ERR_ARG;
-  if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
-  if (G != 128 || T < 1 || K < 256 || K % 256 || K > 4096 || w->rows < kPfBN ||
-      w->rows % kPfBN)
-    return IQ36_ERR_SHAPE;
-  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w->weight, 16) ||
-      !aligned(w->scale, 16) || !aligned(w->zp, 16))
-    return IQ36_ERR_ALIGN;
+  if (swiglu && n_proj != 1) return IQ36_ERR_ARG;
+  if (row_gate && n_proj != 1) return IQ36_ERR_ARG;
+  if (G != 128 || T < 1 || K < 256 || K % 256 || K > 4096) return IQ36_ERR_SHAPE;
+  if (!aligned(x, 16)) return IQ36_ERR_ALIGN;
+  int total_rows = 0;
+  for (int p = 0; p < n_proj; ++p) {
+    const iq36_u4_projection& q = proj[p];
+    const iq36_u4_matrix* w = &q.m;
+    if (!w->weight || !w->scale || !w->zp || !q.out) return IQ36_ERR_ARG;
+    if (q.out_dtype != IQ36_F32 && q.out_dtype != IQ36_F16) return IQ36_ERR_ARG;
+    if (q.accumulate && q.out_dtype != IQ36_F32) return IQ36_ERR_ARG;
+    if (swiglu && (q.out_dtype != IQ36_F16 || q.accumulate)) return IQ36_ERR_ARG;
+    if (row_gate && q.out_dtype != IQ36_F32) return IQ36_ERR_ARG;
+    if (w->rows < kPfBN || w->rows % kPfBN) return IQ36_ERR_SHAPE;
+    if (!aligned(q.out, 16) || !aligned(w->weight, 16) || !aligned(w->scale, 16) ||
+        !aligned(w->zp, 16))
+      return IQ36_ERR_ALIGN;
+    total_rows += w->rows;
+  }
   if (!ws || ws_bytes < u4_gemm_ws(T, K)) return IQ36_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return IQ36_ERR_ALIGN;
   __half* xp = reinterpret_cast<__half*>(ws);
   int32_t* err = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) +
                                             up256((size_t)(T + kPfBM) * K * 2));
-  CUtensorMap map_x, map_w;
-  if (!make_act_map(&map_x, xp, (uint64_t)T + kPfBM, (uint64_t)K) ||
-      !make_code_map(&map_w, w->weight, (uint64_t)w->rows, (uint64_t)K / 2))
-    return IQ36_ERR_CUDA;
+  CUtensorMap map_x, map_w[4];
+  if (!make_act_map(&map_x, xp, (uint64_t)T + kPfBM, (uint64_t)K)) return IQ36_ERR_CUDA;
+  for (int p = 0; p < n_proj; ++p)
+    if (!make_code_map(&map_w[p], proj[p].m.weight, (uint64_t)proj[p].m.rows, (uint64_t)K / 2))
+      return IQ36_ERR_CUDA;
+  for (int p = n_proj; p < 4; ++p) map_w[p] = map_w[0];
   static std::atomic<bool> attr_set[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
@@ -1075,14 +1117,37 @@ int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T
                          xp);
   PfWork wk{};
   wk.err = err;
-  GemmArgs g{reinterpret_cast<const __half*>(w->scale), w->zp, 0, K, w->rows / 2, w->rows, wk,
-             T, out, out_dtype, accumulate, row_gate};
-  const int units = (T + kPfBM - 1) / kPfBM * (w->rows / kPfBN);
+  const iq36_u4_matrix* w0 = &proj[0].m;
+  GemmArgs g{reinterpret_cast<const __half*>(w0->scale), w0->zp, 0, K, w0->rows / 2,
+             total_rows, wk, T, proj[0].out, proj[0].out_dtype, proj[0].accumulate, row_gate};
+  g.n_proj = n_proj;
+  g.tile_base[0] = 0;
+  for (int p = 0; p < 4; ++p) {
+    const bool have = p < n_proj;
+    g.ps[p] = reinterpret_cast<const __half*>(have ? proj[p].m.scale : w0->scale);
+    g.pz[p] = have ? proj[p].m.zp : w0->zp;
+    g.pout[p] = have ? proj[p].out : proj[0].out;
+    g.prow[p] = have ? proj[p].m.rows : w0->rows;
+    g.pdt[p] = have ? proj[p].out_dtype : proj[0].out_dtype;
+    g.pacc[p] = have ? proj[p].accumulate : 0;
+    g.tile_base[p + 1] = g.tile_base[p] + (have ? proj[p].m.rows / kPfBN : 0);
+  }
+  const int units = (T + kPfBM - 1) / kPfBM * (total_rows / kPfBN);
   if (e == cudaSuccess)
     e = launch(swiglu ? pf_gemm_kernel<3> : pf_gemm_kernel<2>,
                dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads), (size_t)kPfSmem, stream,
-               map_x, map_w, g);
+               map_x, map_w[0], map_w[1], map_w[2], map_w[3], g);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+int u4_gemm_launch(const void* x, int x_dtype, const float* nw, float eps, int T, int K, int G,
+                   const iq36_u4_matrix* w, void* out, int out_dtype, int accumulate, void* ws,
+                   size_t ws_bytes, cudaStream_t stream, int swiglu = 0,
+                   const float* row_gate = nullptr) {
+  if (!w) return IQ36_ERR_ARG;
+  const iq36_u4_projection p{*w, out, out_dtype, accumulate};
+  return u4_gemm_multi_launch(x, x_dtype, nw, eps, T, K, G, 1, &p, ws, ws_bytes, stream, swiglu,
+                              row_gate);
 }
 
 }  // namespace iq36
@@ -1098,6 +1163,14 @@ extern "C" int iq36_u4_gemm(const void* x, int32_t x_dtype, const float* norm_we
                             iq36_stream_t stream) {
   return iq36::u4_gemm_launch(x, x_dtype, norm_weight, norm_eps, T, K, group, w, out, out_dtype,
                               accumulate, workspace, workspace_bytes, iq36::as_stream(stream));
+}
+
+extern "C" int iq36_u4_gemm_multi(const void* x, int32_t x_dtype, const float* norm_weight,
+                                  float norm_eps, int32_t T, int32_t K, int32_t group,
+                                  int32_t n_proj, const iq36_u4_projection* proj, void* workspace,
+                                  size_t workspace_bytes, iq36_stream_t stream) {
+  return iq36::u4_gemm_multi_launch(x, x_dtype, norm_weight, norm_eps, T, K, group, n_proj, proj,
+                                    workspace, workspace_bytes, iq36::as_stream(stream));
 }
 
 extern "C" int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int32_t T,

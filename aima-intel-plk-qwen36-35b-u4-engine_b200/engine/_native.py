@@ -78,6 +78,8 @@ _SIGS: dict[str, tuple] = {
     "iq36_u4_gemm": (c_int, [_P, c_int32, _P, c_float, c_int32, c_int32, c_int32,
                              POINTER(U4Matrix), _P, c_int32, c_int32, _P, c_size_t, _P]),
     "iq36_u4_gemm_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "iq36_u4_gemm_multi": (c_int, [_P, c_int32, _P, c_float, c_int32, c_int32, c_int32, c_int32,
+                                   POINTER(U4Projection), _P, c_size_t, _P]),
     "iq36_moe_combine": (c_int, [_P, _P, c_int32, c_int32, c_int32, _P, c_int32, _P]),
     "iq36_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32,
                                                     c_int32]),

@@ -383,6 +383,30 @@ def u4_gemm(x: torch.Tensor, w: U4Weight, out: torch.Tensor | None = None,
     return out
 
 
+def u4_gemm_multi(x: torch.Tensor, ws: list[U4Weight], outs: list[torch.Tensor],
+                  accumulate: list[bool] | None = None,
+                  norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+                  workspace: torch.Tensor | None = None) -> None:
+    """Up to 4 batched u4 projections of one input x [T, K] in one launch:
+    outs[p] [T, rows_p] = x W_p^T (fp16, or fp32 with accumulate)."""
+    _cuda(x, "x")
+    _need(x.dim() == 2 and x.dtype in (torch.float16, torch.float32), "x must be [T, K] fp16/fp32")
+    _need(1 <= len(ws) == len(outs) <= 4, "1..4 projections with one output each")
+    t, k = x.shape
+    accumulate = accumulate or [False] * len(ws)
+    arr = (N.U4Projection * len(ws))()
+    for i, (w, o, acc) in enumerate(zip(ws, outs, accumulate)):
+        _cuda(o, f"out[{i}]")
+        _need(o.shape == (t, w.rows), f"out[{i}] must be [{t}, {w.rows}]")
+        arr[i] = N.U4Projection(w.c(), o.data_ptr(), _dtype_code(o.dtype), int(acc))
+    if workspace is None:
+        workspace = torch.empty(N.lib().iq36_u4_gemm_workspace_bytes(t, k), dtype=torch.uint8,
+                                device=x.device)
+    N.call("iq36_u4_gemm_multi", x.data_ptr(), _dtype_code(x.dtype), _ptr(norm_weight), norm_eps,
+           t, k, ws[0].group, len(ws), arr, workspace.data_ptr(), workspace.numel(),
+           _stream(x.device))
+
+
 def moe_combine(contrib: torch.Tensor, inv: torch.Tensor, k: int,
                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """out[t] = sum_r float(contrib[inv[t*k + r]]) in rank order (fp16 rows)."""

@@ -414,9 +414,8 @@ class Qwen36Runtime:
         for l in range(c.layers):
             L = W.layers[l]
             if c.is_attn(l):
-                for name, wt in (("qfull", L["q"]), ("k", L["k"]), ("v", L["v"])):
-                    ops.u4_gemm(h, wt, out=sl(name), norm_weight=L["in_norm"], norm_eps=c.eps,
-                                workspace=ws)
+                ops.u4_gemm_multi(h, [L["q"], L["k"], L["v"]], [sl("qfull"), sl("k"), sl("v")],
+                                  norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
                 kc, vc = self.kv[l]
                 ops.attn_prep_batch(sl("qfull"), sl("k"), sl("v"), L["qn"], L["kn"], c.eps,
                                     self.pos, self.block_table, kc, vc, sl("q"), sl("gate"),
@@ -425,18 +424,17 @@ class Qwen36Runtime:
                                  1.0 / math.sqrt(hd), gate=sl("gate").view(T, c.nq, hd),
                                  out=sl("attn").view(T, c.nq, hd))
                 ops.u4_gemm(sl("attn"), L["o"], out=h, accumulate=True, workspace=ws)
-                n += 10
+                n += 6
             else:
-                for name, wt in (("qkv", L["qkv"]), ("z", L["z"]), ("ab", L["ab"])):
-                    ops.u4_gemm(h, wt, out=sl(name), norm_weight=L["in_norm"], norm_eps=c.eps,
-                                workspace=ws)
+                ops.u4_gemm_multi(h, [L["qkv"], L["z"], L["ab"]], [sl("qkv"), sl("z"), sl("ab")],
+                                  norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
                 ab = sl("ab")
                 ops.delta_prefill(sl("qkv"), self.conv_state[l], L["conv_w"], ab[:, :c.nv],
                                   ab[:, c.nv:2 * c.nv], L["a_log"], L["dt_bias"],
                                   self.rec_state[l], sl("z"), L["dnorm"], c.eps, c.nk, c.nv,
                                   sl("dout"), workspace=B["dws"])
                 ops.u4_gemm(sl("dout"), L["out"], out=h, accumulate=True, workspace=ws)
-                n += 12
+                n += 9
             ops.moe_layer_prefill(h, L["post_norm"], L["router"], L["sgate"], L["bank"],
                                   L["shared"], sl("ids"), sl("wts"), sl("logits_r"),
                                   workspace=B["mws"], k=c.topk, norm_eps=c.eps)

@@ -231,6 +231,18 @@ int iq36_u4_gemm(const void* x, int32_t x_dtype, const float* norm_weight, float
                  iq36_stream_t stream);
 size_t iq36_u4_gemm_workspace_bytes(int32_t T, int32_t K);
 
+/* iq36_u4_gemm for 1..4 projections that share the input x (same K), in one
+ * input preparation and one persistent GEMM launch whose units span all of
+ * them: proj[p].out [T, proj[p].m.rows] (fp16, or fp32 with accumulate).
+ * Each m.rows a multiple of 256. The batched form of the reference's
+ * multi-output fixed-FC groups (iq36_fixed_fc_multi_output.cl:6-29,45-85;
+ * grouping fixed_fc.py:180-215) over a prompt chunk. Workspace as
+ * iq36_u4_gemm_workspace_bytes(T, K). */
+int iq36_u4_gemm_multi(const void* x, int32_t x_dtype, const float* norm_weight, float norm_eps,
+                       int32_t T, int32_t K, int32_t group, int32_t n_proj,
+                       const iq36_u4_projection* proj, void* workspace, size_t workspace_bytes,
+                       iq36_stream_t stream);
+
 /* out[t] = sum_{r<k} float(contrib[inv[t*k + r]]) in rank order (fp32 sums of
  * fp16 contribution rows [*, H]); out fp32, bf16 or fp16 [T, H]. The
  * contribution scatter of the grouped prefill on its own, for callers that

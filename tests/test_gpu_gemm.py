@@ -61,3 +61,35 @@ def test_u4_gemm_rejects_bad_shapes(cuda):
     w, s, z = make_u4(rng, 128, 2048)                  # N not a multiple of 256
     with pytest.raises(N.Iq36Error):
         u4_gemm(torch.zeros(4, 2048, dtype=torch.float16, device=cuda), u4_to_torch(w, s, z, cuda))
+
+
+def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda):
+    """Three projections of one input in one launch (the DeltaNet in-projection
+    shape family): each output equals its own iq36_u4_gemm bit for bit, and the
+    oracle's GEMV per row; a fourth, fp32-accumulating output checks the
+    residual form."""
+    import torch
+    from engine.ops import u4_gemm, u4_gemm_multi
+    rng = np.random.default_rng(77)
+    T, K = 200, 2048
+    mats = [make_u4(rng, n, K) for n in (512, 256, 768)]
+    ws = [u4_to_torch(w, s, z, cuda) for w, s, z in mats]
+    x = (rng.standard_normal((T, K)) * 2).astype(np.float32)
+    nw = rng.uniform(0.9, 1.1, K).astype(np.float32)
+    outs = [torch.empty(T, w.rows, dtype=torch.float16, device=cuda) for w in ws]
+    acc_w = u4_to_torch(*make_u4(rng, 256, K), cuda)
+    res0 = rng.standard_normal((T, 256)).astype(np.float32)
+    res = _t(res0.copy(), cuda)
+    u4_gemm_multi(_t(x, cuda), ws + [acc_w], outs + [res], accumulate=[False] * 3 + [True],
+                  norm_weight=_t(nw, cuda))
+    for w, o in zip(ws, outs):
+        single = u4_gemm(_t(x, cuda), w, out_dtype=torch.float16, norm_weight=_t(nw, cuda))
+        assert torch.equal(single, o)
+    got = [o.float().cpu().numpy() for o in outs]
+    for t in (0, 77, T - 1):
+        x16 = oracle.rms_norm(x[t], nw, 1e-6).astype(np.float16)
+        for (w, s, z), g in zip(mats, got):
+            assert_close(g[t], oracle.u4_gemv(x16, w, s, z, 128), f"multi row {t}")
+    single_res = _t(res0.copy(), cuda)
+    u4_gemm(_t(x, cuda), acc_w, out=single_res, accumulate=True, norm_weight=_t(nw, cuda))
+    assert torch.equal(single_res, res)
