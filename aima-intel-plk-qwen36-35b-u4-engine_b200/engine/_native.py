@@ -93,8 +93,8 @@ _SIGS: dict[str, tuple] = {
                                c_int32, c_float, _P, c_int32, _P, _P, _P, _P, _P]),
     "iq36_attn_prep_batch": (c_int, [_P, _P, _P, _P, _P, c_float, _P, c_int32, c_int32, c_int32,
                                      c_int32, c_int32, c_float, _P, c_int32, _P, _P, _P, _P, _P]),
-    "iq36_attn_prefill": (c_int, [_P, _P, _P, _P, c_int32, _P, c_int32, c_int32, c_int32, c_int32,
-                                  c_float, _P, _P, c_int32, _P]),
+    "iq36_attn_prefill": (c_int, [_P, _P, _P, _P, c_int32, c_int32, _P, c_int32, c_int32,
+                                  c_int32, c_int32, c_float, _P, _P, c_int32, _P]),
     "iq36_delta_prep": (c_int, [_P, c_int32, _P, _P, _P, _P, _P, _P, c_int32, _P, _P, _P, _P]),
     "iq36_delta_step": (c_int, [_P, _P, _P, _P, _P, _P, c_float, c_int32, c_int32, c_int32, _P,
                                 _P]),

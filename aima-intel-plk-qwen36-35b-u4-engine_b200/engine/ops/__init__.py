@@ -517,8 +517,8 @@ def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     if out is None:
         out = torch.empty(T, nq, d, dtype=out_dtype, device=q.device)
     N.call("iq36_attn_prefill", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-           block_table.data_ptr(), bs, pos_dev.data_ptr(), T, nq, nkv, d, scale, _ptr(gate),
-           out.data_ptr(), _dtype_code(out.dtype), _stream(q.device))
+           block_table.data_ptr(), bs, k_cache.shape[0], pos_dev.data_ptr(), T, nq, nkv, d,
+           scale, _ptr(gate), out.data_ptr(), _dtype_code(out.dtype), _stream(q.device))
     return out
 
 

@@ -334,12 +334,13 @@ int iq36_attn_prep_batch(const void* q_full_f16, const void* k_f16, const void* 
  * softmax(q k^T * scale) v, times sigmoid(gate [T, n_q, D]) when gate_f16 is
  * not NULL. Equal to iq36_paged_gqa_decode run for each prompt token in turn
  * (run_qwen36_full_attention_core, gguf_loader.cpp:6071-6137; gate :6034-6069).
- * head_dim 256, n_q_heads == 8 * n_kv_heads. Allocates nothing. */
+ * head_dim 256, n_q_heads == 8 * n_kv_heads, block_size 16; num_blocks = the
+ * caches' block count (a table entry past it reads zeros). Allocates nothing. */
 int iq36_attn_prefill(const void* q_f16, const void* k_cache, const void* v_cache,
-                      const int32_t* block_table, int32_t block_size, const int32_t* pos_dev,
-                      int32_t tokens, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
-                      float scale, const void* gate_f16, void* out, int32_t out_dtype,
-                      iq36_stream_t stream);
+                      const int32_t* block_table, int32_t block_size, int32_t num_blocks,
+                      const int32_t* pos_dev, int32_t tokens, int32_t n_q_heads,
+                      int32_t n_kv_heads, int32_t head_dim, float scale, const void* gate_f16,
+                      void* out, int32_t out_dtype, iq36_stream_t stream);
 
 /* DeltaNet pre-step for one token: causal depthwise conv (width 4, carried
  * state [C,4]) + SiLU with the fp16 rounding points of

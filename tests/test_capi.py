@@ -140,9 +140,9 @@ def test_prompt_path_entries_reject_bad_arguments_on_host(native):
     bad[0] = None
     assert _status(native, "iq36_delta_prefill", *bad) == -1
     # prompt attention: 12 query heads over 2 KV heads (group must be 8); bad dtype
-    args = [16, 16, 16, 16, 16, 16, 64, 12, 2, 256, 0.0625, None, 16, 1, None]
+    args = [16, 16, 16, 16, 16, 64, 16, 64, 12, 2, 256, 0.0625, None, 16, 1, None]
     assert _status(native, "iq36_attn_prefill", *args) == -2
-    args[7], args[13] = 16, 7
+    args[8], args[14] = 16, 7
     assert _status(native, "iq36_attn_prefill", *args) == -1
     # batched attention pre-step: zero tokens
     assert _status(native, "iq36_attn_prep_batch", 16, 16, 16, 16, 16, 1e-6, 16, 0, 16, 2, 256,
