@@ -13,7 +13,9 @@
 // M dimension), so every K/V tile serves all 8 heads. Warp roles:
 //   warp 0    TMA: the Q tile once (3-D boxes 64 dims x 8 heads x 16 tokens),
 //             then 64-key K and V tiles gathered page by page through the block
-//             table (boxes 64 dims x 1 head x 16 keys), double-buffered;
+//             table (boxes 64 dims x 1 head x 16 keys), K and V in separate
+//             double-buffered rings so a K stage refills as soon as its S
+//             product is done;
 //   warp 1    TMEM allocator and the single MMA-issuing thread:
 //             S = Q K^T (M128 N64 K256) into one of two TMEM S buffers, and
 //             O += P V (M128 N256 K64, V read MN-major) into TMEM O;
@@ -79,14 +81,16 @@ __global__ void __launch_bounds__(kApThreads, 1)
   const uint32_t q_s = base, k_s = base + kApOffK, v_s = base + kApOffV, p_s = base + kApOffP;
   const uint32_t bar = base + kApOffBar;
   const uint32_t bar_q = bar;          // Q landed (tx)
-  const uint32_t bar_kv = bar + 8;     // [2] K/V stage landed (tx)
-  const uint32_t bar_kve = bar + 24;   // [2] K/V stage consumed (tcgen05.commit)
+  const uint32_t bar_k = bar + 8;      // [2] K stage landed (tx)
+  const uint32_t bar_ke = bar + 24;    // [2] K stage consumed by S (tcgen05.commit)
   const uint32_t bar_s = bar + 40;     // [2] S buffer written (commit)
   const uint32_t bar_se = bar + 56;    // [2] S buffer read (128 softmax threads)
   const uint32_t bar_p = bar + 72;     // P written and O corrected (128 softmax threads)
   const uint32_t bar_o = bar + 80;     // PV of a tile done (commit)
   const uint32_t bar_done = bar + 88;  // every MMA done (teardown)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kApOffBar + 128);
+  const uint32_t bar_v = bar + 96;     // [2] V stage landed (tx)
+  const uint32_t bar_ve = bar + 112;   // [2] V stage consumed by PV (commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kApOffBar + 192);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (T + kApTok - 1) / kApTok;
   const int tile = n_tiles - 1 - (int)(blockIdx.x / nkv);  // longest first
@@ -95,8 +99,10 @@ __global__ void __launch_bounds__(kApThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar_kv + 8 * s, 1);
-      mbar_init(bar_kve + 8 * s, 1);
+      mbar_init(bar_k + 8 * s, 1);
+      mbar_init(bar_ke + 8 * s, 1);
+      mbar_init(bar_v + 8 * s, 1);
+      mbar_init(bar_ve + 8 * s, 1);
       mbar_init(bar_s + 8 * s, 1);
       mbar_init(bar_se + 8 * s, 128);
     }
@@ -124,22 +130,27 @@ __global__ void __launch_bounds__(kApThreads, 1)
       mbar_arrive_tx(bar_q, kApQ);
       for (int dc = 0; dc < 4; ++dc)
         tma_load_3d(q_s + dc * (kApRows * 128), &tmQ, dc * 64, kvh * kApGrp, t0, bar_q);
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        ok = mbar_wait(bar_kve + 8 * st, ((j >> 1) & 1) ^ 1u);
-        if (!ok) break;
-        mbar_arrive_tx(bar_kv + 8 * st, 2 * kApKV);
+      // per 16-key page and 64-dim chunk one box (64 dims x 1 head x 16 keys)
+      // into chunk dc's [64 keys][128 B] operand tile
+      auto load_tile = [&](const CUtensorMap* map, uint32_t dst, uint32_t full, int j) {
+        mbar_arrive_tx(full, kApKV);
         for (int pg = 0; pg < kApKeys / 16; ++pg) {
           const int key0 = j * kApKeys + pg * 16;
           // a page wholly past the context is read outside the tensor: zeros
           const int row = key0 < kend ? bt[key0 / 16] * 16 : n_blocks * 16;
 #pragma unroll
-          for (int dc = 0; dc < 4; ++dc) {
-            const uint32_t off = st * kApKV + dc * (kApKeys * 128) + pg * 16 * 128;
-            tma_load_3d(k_s + off, &tmK, dc * 64, kvh, row, bar_kv + 8 * st);
-            tma_load_3d(v_s + off, &tmV, dc * 64, kvh, row, bar_kv + 8 * st);
-          }
+          for (int dc = 0; dc < 4; ++dc)
+            tma_load_3d(dst + dc * (kApKeys * 128) + pg * 16 * 128, map, dc * 64, kvh, row, full);
         }
+      };
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1, ph = ((j >> 1) & 1) ^ 1u;
+        ok = mbar_wait(bar_ke + 8 * st, ph);
+        if (!ok) break;
+        load_tile(&tmK, k_s + st * kApKV, bar_k + 8 * st, j);
+        ok = mbar_wait(bar_ve + 8 * st, ph);
+        if (!ok) break;
+        load_tile(&tmV, v_s + st * kApKV, bar_v + 8 * st, j);
       }
     }
   } else if (warp == 1) {
@@ -148,7 +159,7 @@ __global__ void __launch_bounds__(kApThreads, 1)
       auto issue_s = [&](int j) -> bool {
         const int b = j & 1;
         if (!mbar_wait(bar_se + 8 * b, ((j >> 1) & 1) ^ 1u) ||
-            !mbar_wait(bar_kv + 8 * b, (j >> 1) & 1))
+            !mbar_wait(bar_k + 8 * b, (j >> 1) & 1))
           return false;
         tc_fence_after();
         const uint32_t ks = k_s + b * kApKV;
@@ -159,12 +170,13 @@ __global__ void __launch_bounds__(kApThreads, 1)
                    sw128_desc(ks + dc * (kApKeys * 128) + sub * 32), kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar_s + 8 * b);
+        umma_commit(bar_ke + 8 * b);  // K of this stage read
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
-        ok = mbar_wait(bar_p, j & 1);
+        ok = mbar_wait(bar_p, j & 1) && mbar_wait(bar_v + 8 * (j & 1), (j >> 1) & 1);
         if (!ok) break;
         tc_fence_after();
         const uint32_t vs = v_s + (j & 1) * kApKV;
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(kApThreads, 1)
           umma_f16(tmem + 256, sw128_desc(p_s + kk * 32),
                    sw128_desc_mn(vs + kk * 16 * 128, kApKeys * 128), kIdescO,
                    (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar_kve + 8 * (j & 1));  // K and V of this stage fully read
+        umma_commit(bar_ve + 8 * (j & 1));  // V of this stage read
         umma_commit(bar_o);
       }
       umma_commit(bar_done);
