@@ -216,12 +216,18 @@ __global__ void __launch_bounds__(256, 1) router_logits_batch_kernel(
           wf[q][2 * e + 1] = f.y;
         }
       }
+      // the next token's inputs are loaded while the current token's FMAs run
+      float4 n0 = *reinterpret_cast<const float4*>(xtile + c * 4);
+      float4 n1 = *reinterpret_cast<const float4*>(xtile + H / 2 + c * 4);
 #pragma unroll
       for (int tt = 0; tt < kRbTok; ++tt) {
+        const float4 x0 = n0, x1 = n1;
+        if (tt + 1 < kRbTok) {
+          const int tn = min(tt + 1, nt - 1);
+          n0 = *reinterpret_cast<const float4*>(xtile + (size_t)tn * H + c * 4);
+          n1 = *reinterpret_cast<const float4*>(xtile + (size_t)tn * H + H / 2 + c * 4);
+        }
         if (tt < nt) {
-          const float4 x0 = *reinterpret_cast<const float4*>(xtile + (size_t)tt * H + c * 4);
-          const float4 x1 =
-              *reinterpret_cast<const float4*>(xtile + (size_t)tt * H + H / 2 + c * 4);
           const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e)
