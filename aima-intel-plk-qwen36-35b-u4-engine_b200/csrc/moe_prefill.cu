@@ -286,6 +286,9 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(const int32_t* inv, con
 // ---------------------------------------------------------------------------
 // Grouped GEMM
 
+// Count of bounded waits that gave up in the GEMM kernels (read by iq36_wait_timeouts).
+__device__ int g_gemm_wait_timeouts;
+
 // MODE 0: grouped gate_up + SwiGLU; MODE 1: grouped down x router weight
 // (fp16 contributions); MODE 2: dense u4 GEMM out[T, N] = x W^T (tiles of the
 // T rows in order, weight rows nt*256 ..), fp16 store or fp32 accumulate,
@@ -714,7 +717,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_arrive(bar_acce + 8 * a);  // this accumulator may be overwritten
     }
   }
-  if (!ok) atomicExch(g.work.err, 1);
+  if (!ok) {
+    atomicExch(g.work.err, 1);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&g_gemm_wait_timeouts, 1);
+  }
   pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
@@ -800,6 +806,17 @@ static bool make_code_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64
 }
 
 size_t moe_prefill_ws(int T, int k, int E, int H, int I) { return pf_layout(T, k, E, H, I).total; }
+
+int gemm_wait_timeouts(int* count, int reset) {
+  if (cudaMemcpyFromSymbol(count, g_gemm_wait_timeouts, sizeof(int)) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_gemm_wait_timeouts, &zero, sizeof(int)) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+  }
+  return IQ36_OK;
+}
 
 int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
                        const float* weights, int k, const iq36_expert_bank* b, void* out,

@@ -437,9 +437,10 @@ void iq36_synth_tensor_spec(int32_t slot, int32_t sub, int32_t* kind, float* lo,
  * of this library in the process. */
 void iq36_set_pdl(int enabled);
 
-/* Number of bounded device waits (weight-streaming rings) that gave up on the
- * current device since the last reset; a non-zero count means some output of
- * those launches is invalid. reset != 0 clears the counter after reading.
+/* Number of bounded device waits that gave up on the current device since the
+ * last reset (decode weight-streaming rings, the tcgen05 GEMM and attention
+ * pipelines); a non-zero count means some output of those launches is
+ * invalid. reset != 0 clears the counters after reading.
  * No counterpart in the reference (its kernels hold no cross-warp waits). */
 int iq36_wait_timeouts(int32_t* count, int32_t reset);
 
