@@ -21,6 +21,7 @@ the data path), value summed over ranks.
 
 Other workloads: --workload prefill (BASELINE config 4 prefill tok/s: the batched
 prefill of a --ctx-token prompt, 4096 or 32768; a step is one whole prompt),
+--workload attn_prefill / delta_prefill (one prompt-path op alone over --tokens),
 --workload moe_prefill (grouped MoE
 prefill; replicas at --gpus > 1, expert-parallel over NCCL with --ep) and --workload gemv
 (one u4 GEMV per step, --rows / --k for other shapes).
@@ -469,6 +470,97 @@ def run_prefill(args, world, rank, local) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_op_prefill(args, world, rank, local) -> None:
+    """One prompt-path op alone over --tokens T tokens (BASELINE config 4 shapes):
+    --workload attn_prefill: causal GQA attention (16 q / 2 kv heads, D 256,
+    16-token paged cache, random block table, p0 = 0; tensor roofline);
+    --workload delta_prefill: the DeltaNet block (32 v / 16 k heads, D 128;
+    reported as tokens/s, the recurrence is sequential over 32-token chunks).
+    --profile-step runs one call between cudaProfilerStart/Stop."""
+    import torch
+    from engine import ops
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    T = args.tokens
+    g = torch.Generator(dev).manual_seed(11 + rank)
+    if args.workload == "attn_prefill":
+        nblk = (T + 15) // 16 + 2
+        q = torch.randn(T, 16, 256, device=dev, generator=g).half()
+        kc = torch.randn(nblk, 16, 2, 256, device=dev, generator=g).half()
+        vc = torch.randn(nblk, 16, 2, 256, device=dev, generator=g).half()
+        bt = torch.randperm(nblk, device=dev, generator=g).int()
+        gate = torch.randn(T, 16, 256, device=dev, generator=g).half()
+        pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = torch.empty(T, 16, 256, dtype=torch.float16, device=dev)
+
+        def call():
+            ops.attn_prefill(q, kc, vc, bt, pos, 1 / 16, gate=gate, out=out)
+        flops = 2 * 2 * T * (T + 16) / 2 * 256 * 16
+        metric, launches = "prompt attention tok/s (config 4 shapes)", 1
+    else:
+        nk, nv, d = 16, 32, 128
+        c = (2 * nk + nv) * d
+        qkv = (torch.randn(T, c, device=dev, generator=g) * 2).half()
+        st = torch.randn(c, 4, device=dev, generator=g).half().float()
+        cw = torch.rand(c, 4, device=dev, generator=g) - 0.5
+        ab = torch.randn(T, 256, device=dev, generator=g).half()
+        alog = torch.rand(nv, device=dev, generator=g) * 3 - 2
+        dtb = torch.rand(nv, device=dev, generator=g) * 2 - 1
+        state = torch.randn(nv, d, d, device=dev, generator=g) * 0.05
+        z = torch.randn(T, nv * d, device=dev, generator=g).half()
+        nw = torch.rand(d, device=dev, generator=g) * 0.2 + 0.9
+        out = torch.empty(T, nv * d, dtype=torch.float16, device=dev)
+        ws = ops.delta_prefill_workspace(T, nk, nv, dev)
+
+        def call():
+            ops.delta_prefill(qkv, st, cw, ab[:, :nv], ab[:, nv:2 * nv], alog, dtb, state, z, nw,
+                              1e-6, nk, nv, out, workspace=ws)
+        flops = None
+        metric, launches = "DeltaNet prefill tok/s (config 4 shapes)", 5
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    if args.profile_step:
+        torch.cuda.profiler.start()
+        call()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profile_step": "done", "workload": args.workload, "T": T}))
+        return
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        call()
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    per = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    line = {"metric": metric, "value": round(world * T / per, 1), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16" if flops else "f32 state, 3xTF32 products",
+            "data": "synthetic",
+            "config": {"workload": f"{args.workload} T={T}", "T": T,
+                       "l2": "inputs resident; the op's working set is what a layer sees"},
+            "gpu_launches": launches * args.steps, "clocks": clocks}
+    if flops:
+        peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+        tf = flops / per / 1e12
+        line["roofline"] = {"bound": "tensor", "kernel": "attn_prefill_kernel",
+                            "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                            "frac": round(tf / peak, 4), "traffic": None}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_moe_prefill(args, world, rank, local) -> None:
     """grouped MoE prefill of T tokens (bf16 ~N(0,1)) over
     256 u4 g128 experts, router logits N(0,1) + Zipf(1.1)-ranked bias (+-2),
@@ -710,11 +802,13 @@ def run_gemv(args, world, rank, local) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["decode", "prefill", "moe_prefill", "gemv"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "moe_prefill", "gemv",
+                                           "attn_prefill", "delta_prefill"],
                     default="decode")
     ap.add_argument("--rows", type=int, default=1024, help="output rows for --workload gemv")
     ap.add_argument("--k", type=int, default=2048, help="input length for --workload gemv")
-    ap.add_argument("--tokens", type=int, default=4096, help="T for --workload moe_prefill")
+    ap.add_argument("--tokens", type=int, default=4096,
+                    help="T for --workload moe_prefill / attn_prefill / delta_prefill")
     ap.add_argument("--ep", action="store_true",
                     help="--workload moe_prefill at --gpus > 1: expert parallel instead of replicas")
     ap.add_argument("--gpus", type=int, default=1)
@@ -735,6 +829,8 @@ def main() -> None:
             run_prefill(args, world, rank, local)
         elif args.workload == "moe_prefill":
             run_moe_prefill(args, world, rank, local)
+        elif args.workload in ("attn_prefill", "delta_prefill"):
+            run_op_prefill(args, world, rank, local)
         elif args.workload == "gemv":
             run_gemv(args, world, rank, local)
         else:
