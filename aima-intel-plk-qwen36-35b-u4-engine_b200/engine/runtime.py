@@ -457,6 +457,12 @@ class Qwen36Runtime:
         to 8192 tokens and the tail needs no special case."""
         toks = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1)
         total = toks.numel()
+        if total < 1:
+            raise ValueError("empty prompt")
+        p0 = int(self.pos.item())
+        if p0 + total > self.max_ctx:
+            raise ValueError(f"prompt of {total} tokens at position {p0} exceeds the "
+                             f"{self.max_ctx}-token cache")
         B = self._prefill_buffers(min(chunk, total))
         src = toks if toks.is_cuda else toks.pin_memory()
         n = 0

@@ -154,3 +154,12 @@ def test_batched_prefill_state_equals_token_serial(cuda):
         vs = np.stack([serial["kv"][l][1][b, s].float().cpu().numpy() for b, s in rows])
         _close_stats(kb, ks, f"K cache layer {l}")
         _close_stats(vb, vs, f"V cache layer {l}")
+
+
+def test_batched_prefill_rejects_prompt_past_the_cache(cuda):
+    from engine.runtime import Qwen36Runtime
+    rt = Qwen36Runtime(_small_cfg(), seed=3, max_ctx=32, device=cuda)
+    with pytest.raises(ValueError):
+        rt.prefill_batched(list(range(33)))
+    with pytest.raises(ValueError):
+        rt.prefill_batched([])
