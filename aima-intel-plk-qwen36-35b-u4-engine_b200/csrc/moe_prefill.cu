@@ -81,7 +81,8 @@ constexpr int kPfDqWarps = 16, kPfEpiWarps = 4;
 constexpr int kPfWarpDq0 = 3, kPfWarpEpi0 = kPfWarpDq0 + kPfDqWarps;
 constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 736
 constexpr int kPfDqThreads = kPfDqWarps * 32;                 // half a B-tile row each
-constexpr int kPfChunk = 2048;  // assignments per schedule CTA
+constexpr int kPfChunk = 512;  // assignments per schedule CTA (64 CTAs at 4096 tokens x top-8)
+static_assert(kPfChunk % 256 == 0, "placement ranks 256 assignments per round");
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 
 // ---------------------------------------32, A and B fp16, both K-major,
@@ -124,38 +125,43 @@ __global__ void __launch_bounds__(256) pf_hist_kernel(const int32_t* ids, int P,
   for (int e = threadIdx.x; e < E; e += blockDim.x) w.hist[(size_t)blockIdx.x * E + e] = h[e];
 }
 
-// One CTA, thread e = expert (E <= 256).
+// One CTA, thread e = expert (E <= 256). Exclusive scans of the per-expert
+// assignment and tile counts: warp shuffles, then the 8 warp totals.
 __global__ void __launch_bounds__(256) pf_scan_kernel(int nC, int E, PfWork w) {
-  __shared__ int32_t s_tot[256], s_tiles[256];
+  __shared__ int32_t s_wtot[8], s_wtiles[8];
   pdl_wait();
-  const int e = threadIdx.x;
+  const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   int tot = 0;
   if (e < E)
     for (int c = 0; c < nC; ++c) tot += w.hist[(size_t)c * E + e];
-  s_tot[e] = e < E ? tot : 0;
-  s_tiles[e] = e < E ? (tot + kPfBM - 1) / kPfBM : 0;
-  __syncthreads();
-  if (e == 0) {  // sequential exclusive scans over <= 256 experts
-    int run = 0, trun = 0;
-    for (int i = 0; i < 256; ++i) {
-      const int t0 = s_tot[i], n0 = s_tiles[i];
-      s_tot[i] = run;
-      s_tiles[i] = trun;
-      run += t0;
-      trun += n0;
+  const int tiles = (tot + kPfBM - 1) / kPfBM;
+  int inc = tot, tinc = tiles;  // inclusive within the warp
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, inc, d), b = __shfl_up_sync(0xffffffffu, tinc, d);
+    if (lane >= d) {
+      inc += a;
+      tinc += b;
     }
-    *w.tile_count = trun;
+  }
+  if (lane == 31) {
+    s_wtot[warp] = inc;
+    s_wtiles[warp] = tinc;
   }
   __syncthreads();
+  int off = inc - tot, t0 = tinc - tiles;
+  for (int v = 0; v < warp; ++v) {
+    off += s_wtot[v];
+    t0 += s_wtiles[v];
+  }
+  if (e == 255) *w.tile_count = t0 + tiles;
   if (e < E) {
-    const int off = s_tot[e];
     w.offset[e] = off;
     int run = off;
     for (int c = 0; c < nC; ++c) {
       w.cbase[(size_t)c * E + e] = run;
       run += w.hist[(size_t)c * E + e];
     }
-    const int t0 = s_tiles[e];
     for (int i = 0; off + i * kPfBM < run; ++i) {
       w.tile_expert[t0 + i] = e;
       w.tile_row0[t0 + i] = off + i * kPfBM;
@@ -165,8 +171,9 @@ __global__ void __launch_bounds__(256) pf_scan_kernel(int nC, int E, PfWork w) {
   pdl_launch_dependents();
 }
 
-// Stable placement: CTA c owns assignments [c*2048, (c+1)*2048) in order; in
-// 8 rounds of 256 it ranks each assignment among earlier ones of its expert.
+// Stable placement: CTA c owns assignments [c*kPfChunk, (c+1)*kPfChunk) in
+// order; in rounds of 256 it ranks each assignment among earlier ones of its
+// expert.
 __global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* ids, const float* weights,
                                                        int P, int E, int k, PfWork w) {
   __shared__ int32_t run[256];
