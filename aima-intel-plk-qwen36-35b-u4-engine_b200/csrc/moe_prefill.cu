@@ -173,9 +173,12 @@ __global__ void __launch_bounds__(256) pf_scan_kernel(int nC, int E, PfWork w) {
 
 // Stable placement: CTA c owns assignments [c*kPfChunk, (c+1)*kPfChunk) in
 // order; in rounds of 256 it ranks each assignment among earlier ones of its
-// expert.
+// expert. The input row of assignment a is a / k, or row_of[a] (clamped to
+// the n_rows rows) when the rows are given per assignment.
 __global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* ids, const float* weights,
-                                                       int P, int E, int k, PfWork w) {
+                                                       int P, int E, int k,
+                                                       const int32_t* row_of, int n_rows,
+                                                       PfWork w) {
   __shared__ int32_t run[256];
   __shared__ int32_t wc[8][256];
   pdl_wait();
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(256) pf_place_kernel(const int32_t* ids, const
       for (int v = 0; v < warp; ++v) before += wc[v][e];
       const int p = run[e] + before + rank_w;
       w.inv[a] = p;
-      w.perm_tok[p] = a / k;
+      w.perm_tok[p] = row_of ? min(max(row_of[a], 0), n_rows - 1) : a / k;
       w.perm_w[p] = weights[a];
     }
     __syncthreads();
@@ -825,11 +828,14 @@ int gemm_wait_timeouts(int* count, int reset) {
   return IQ36_OK;
 }
 
+// row_of == nullptr: x is [T, H] and assignment t*k+j reads row t. Otherwise
+// (k must be 1) x is [n_rows, H] and assignment a reads row row_of[a].
 int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
                        const float* weights, int k, const iq36_expert_bank* b, void* out,
                        int out_dtype, int accumulate, void* ws, size_t ws_bytes,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const int32_t* row_of = nullptr, int n_rows = 0) {
   if (!x || !ids || !weights || !b || !out) return IQ36_ERR_ARG;
+  if (row_of && (k != 1 || n_rows < 1)) return IQ36_ERR_SHAPE;
   if (x_dtype != IQ36_BF16 && x_dtype != IQ36_F16) return IQ36_ERR_ARG;
   if (accumulate && out_dtype != IQ36_F32) return IQ36_ERR_ARG;
   if (!b->gate_up_weight || !b->gate_up_scale || !b->gate_up_zp || !b->down_weight ||
@@ -891,7 +897,8 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
   cudaError_t e = launch(pf_hist_kernel, dim3(nC), dim3(256), 0, stream, ids, P, E, w);
   if (e == cudaSuccess) e = launch(pf_scan_kernel, dim3(1), dim3(256), 0, stream, nC, E, w);
   if (e == cudaSuccess)
-    e = launch(pf_place_kernel, dim3(nC), dim3(256), 0, stream, ids, weights, P, E, k, w);
+    e = launch(pf_place_kernel, dim3(nC), dim3(256), 0, stream, ids, weights, P, E, k, row_of,
+               n_rows, w);
   if (e == cudaSuccess)
     e = launch(pf_gather_kernel, dim3(ceil_div(P, 8)), dim3(256), 0, stream, x,
                x_dtype == IQ36_F16 ? 1 : 0, P, H, w);
@@ -1113,6 +1120,25 @@ extern "C" int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* id
                                 size_t workspace_bytes, iq36_stream_t stream) {
   return iq36::moe_prefill_launch(x_bf16, IQ36_BF16, T, ids, weights, k, routed, out, out_dtype,
                                   0, workspace, workspace_bytes, iq36::as_stream(stream));
+}
+
+extern "C" size_t iq36_moe_prefill_rows_workspace_bytes(int32_t n_assign, int32_t num_experts,
+                                                        int32_t hidden, int32_t intermediate) {
+  return iq36::moe_prefill_ws(n_assign, 1, num_experts, hidden, intermediate);
+}
+
+extern "C" int iq36_moe_prefill_rows(const void* x_bf16, int32_t n_rows, int32_t n_assign,
+                                     const int32_t* row_of, const int32_t* ids,
+                                     const float* weights, const iq36_expert_bank* routed,
+                                     void* contrib_f16, void* workspace, size_t workspace_bytes,
+                                     iq36_stream_t stream) {
+  if (!x_bf16 || !row_of || !ids || !weights || !routed || !contrib_f16) return IQ36_ERR_ARG;
+  if (n_rows < 0 || n_assign < 0) return IQ36_ERR_SHAPE;
+  if (n_assign == 0) return IQ36_OK;
+  if (n_rows == 0) return IQ36_ERR_SHAPE;
+  return iq36::moe_prefill_launch(x_bf16, IQ36_BF16, n_assign, ids, weights, 1, routed,
+                                  contrib_f16, IQ36_F16, 0, workspace, workspace_bytes,
+                                  iq36::as_stream(stream), row_of, n_rows);
 }
 
 // ---------------------------------------------------------------------------

@@ -81,6 +81,9 @@ _SIGS: dict[str, tuple] = {
     "iq36_u4_gemm_multi": (c_int, [_P, c_int32, _P, c_float, c_int32, c_int32, c_int32, c_int32,
                                    POINTER(U4Projection), _P, c_size_t, _P]),
     "iq36_moe_combine": (c_int, [_P, _P, c_int32, c_int32, c_int32, _P, c_int32, _P]),
+    "iq36_moe_prefill_rows": (c_int, [_P, c_int32, c_int32, _P, _P, _P, POINTER(ExpertBankC),
+                                      _P, _P, c_size_t, _P]),
+    "iq36_moe_prefill_rows_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "iq36_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32,
                                                     c_int32]),
     "iq36_paged_gqa_decode": (c_int, [_P, _P, _P, _P, c_int32, _P, c_int32, c_int32, c_int32,

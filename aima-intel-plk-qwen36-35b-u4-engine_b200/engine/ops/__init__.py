@@ -407,6 +407,32 @@ def u4_gemm_multi(x: torch.Tensor, ws: list[U4Weight], outs: list[torch.Tensor],
            _stream(x.device))
 
 
+def moe_prefill_rows(x_rows: torch.Tensor, row_of: torch.Tensor, ids: torch.Tensor,
+                     weights: torch.Tensor, routed: ExpertBank,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-assignment fp16 contributions over deduplicated rows: out[a] =
+    fp16(weights[a] * Expert_{ids[a]}(x_rows[row_of[a]])), out [n_assign, H]."""
+    _cuda(x_rows, "x_rows", torch.bfloat16)
+    for t, name in ((row_of, "row_of"), (ids, "ids")):
+        _cuda(t, name, torch.int32)
+    _cuda(weights, "weights", torch.float32)
+    n_rows, h = x_rows.shape
+    n = ids.numel()
+    _need(row_of.numel() == n and weights.numel() == n, "row_of/ids/weights must match")
+    if out is None:
+        out = torch.empty(n, h, dtype=torch.float16, device=x_rows.device)
+    if n == 0:
+        return out
+    nbytes = N.lib().iq36_moe_prefill_rows_workspace_bytes(n, routed.num_experts, h,
+                                                           routed.intermediate)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x_rows.device)
+    rb = routed.c()
+    N.call("iq36_moe_prefill_rows", x_rows.data_ptr(), n_rows, n, row_of.data_ptr(),
+           ids.data_ptr(), weights.data_ptr(), ctypes.byref(rb), out.data_ptr(), ws.data_ptr(),
+           ws.numel(), _stream(x_rows.device))
+    return out
+
+
 def moe_combine(contrib: torch.Tensor, inv: torch.Tensor, k: int,
                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """out[t] = sum_r float(contrib[inv[t*k + r]]) in rank order (fp16 rows)."""

@@ -631,6 +631,12 @@ def run_moe_prefill(args, world, rank, local) -> None:
     barrier(world)
     torch.cuda.synchronize(dev)
     sampler.start()
+    # one more untimed call once the clock sampler runs: the expert-parallel
+    # path reads split sizes on the host every call, and its first call after
+    # the sampler starts was measured 3-20 ms slower than the steady ~1.9 ms
+    call()
+    barrier(world)
+    torch.cuda.synchronize(dev)
     evs = []
     for _ in range(args.steps):
         flush.zero_()

@@ -253,6 +253,21 @@ int iq36_moe_combine(const void* contrib_f16, const int32_t* inv, int32_t T, int
 size_t iq36_moe_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_experts,
                                         int32_t hidden, int32_t intermediate);
 
+/* Per-assignment contributions over deduplicated input rows, for the owner
+ * side of expert-parallel prefill (no counterpart in the single-device
+ * reference): contrib[a] = fp16(weights[a] * Expert_{ids[a]}(x[row_of[a]]))
+ * for a < n_assign, x bf16 [n_rows, H], contrib fp16 [n_assign, H] — the same
+ * fp16 values iq36_moe_prefill sums, so combining them in slot order with
+ * iq36_moe_combine reproduces it bit for bit. row_of entries are clamped to
+ * [0, n_rows). n_assign == 0 enqueues nothing. Workspace:
+ * iq36_moe_prefill_rows_workspace_bytes. */
+int iq36_moe_prefill_rows(const void* x_bf16, int32_t n_rows, int32_t n_assign,
+                          const int32_t* row_of, const int32_t* ids, const float* weights,
+                          const iq36_expert_bank* routed, void* contrib_f16, void* workspace,
+                          size_t workspace_bytes, iq36_stream_t stream);
+size_t iq36_moe_prefill_rows_workspace_bytes(int32_t n_assign, int32_t num_experts,
+                                             int32_t hidden, int32_t intermediate);
+
 /* ---- (3) paged GQA decode attention ----------------------------------------
  * o[h] = sum_t softmax_t(q[h].k[t,h/grp] * scale) v[t,h/grp], then
  * o *= sigmoid(gate[h]) when gate != NULL. KV cache fp16

@@ -62,15 +62,17 @@ def _ep_prefill_cpu_body(rank, world):
     xb = oracle.bf16_bits(x)
     xf = oracle.bf16_to_f32(xb)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
-    w = rng.uniform(0.05, 0.5, (T, k)).astype(np.float32)
     e_local = E // world
+    for t in range(0, T, 5):  # tokens whose experts all live on one rank (no row to the other)
+        ids[t] = (t // 5) % world * e_local + rng.permutation(e_local)[:k]
+    w = rng.uniform(0.05, 0.5, (T, k)).astype(np.float32)
     local = {key: v[rank * e_local:(rank + 1) * e_local] for key, v in bank.items()}
 
-    def expert_fn(x_rows, local_ids, weights):
-        n = x_rows.shape[0]
+    def expert_fn(x_rows, row_of, local_ids, weights):
+        n = local_ids.shape[0]
         if n == 0:
             return torch.zeros(0, H)
-        xr = oracle.bf16_bits(x_rows.numpy())
+        xr = oracle.bf16_bits(x_rows.numpy()[row_of.numpy()])
         y = oracle.moe_prefill(xr, np.arange(n), local_ids.numpy().reshape(n, 1),
                                weights.numpy().reshape(n, 1), local, 128)
         return torch.from_numpy(y)

@@ -153,5 +153,13 @@ def test_prompt_path_entries_reject_bad_arguments_on_host(native):
     bank = native.ExpertBankC(16, 16, 16, 16, 16, 16, 256, 2048, 512, 128)
     assert _status(native, "iq36_moe_layer_prefill", None, 64, 2048, 16, 1e-6, 16, 16, 8,
                    ctypes.byref(bank), None, 16, 16, 16, 256, 1 << 30, None) == -1
+    # expert-parallel owner side: null rows; no assignments is a no-op; rows missing
+    assert _status(native, "iq36_moe_prefill_rows", None, 4, 8, 16, 16, 16, ctypes.byref(bank),
+                   16, 16, 1 << 30, None) == -1
+    assert _status(native, "iq36_moe_prefill_rows", 16, 4, 0, 16, 16, 16, ctypes.byref(bank),
+                   16, 16, 1 << 30, None) == 0
+    assert _status(native, "iq36_moe_prefill_rows", 16, 0, 8, 16, 16, 16, ctypes.byref(bank),
+                   16, 16, 1 << 30, None) == -2
+    assert lib.iq36_moe_prefill_rows_workspace_bytes(4096, 128, 2048, 512) > 0
     # embedding rows: T out of range
     assert _status(native, "iq36_embed_batch", 16, 1000, 2048, 16, 0, 16, None) == -2

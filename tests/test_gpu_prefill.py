@@ -109,3 +109,36 @@ def test_prefill_fp16_output_is_the_contribution(cuda):
     o32 = moe_expert_ffn_prefill(x, ids, w, bank, out_dtype=torch.float32)
     o16 = moe_expert_ffn_prefill(x, ids, w, bank, out_dtype=torch.float16)
     assert torch.equal(o16.float(), o32)
+
+
+def test_prefill_rows_contributions_combine_to_the_grouped_result(cuda):
+    """iq36_moe_prefill_rows over deduplicated rows (each assignment names its
+    row): the contributions equal the k = 1 grouped prefill on materialised
+    rows bit for bit, and combined in slot order they give iq36_moe_prefill's
+    k = 8 output bit for bit."""
+    import torch
+    from engine.ops import moe_combine, moe_expert_ffn_prefill, moe_prefill_rows, router_select
+    rng = np.random.default_rng(21)
+    E, T, k = 32, 300, 8
+    bank = bank_to_torch(make_bank(rng, E, 2048, 512), cuda)
+    ids, w = router_select(_t(zipf_router_logits(rng, T, E), cuda), k)
+    x = torch.randn(T, 2048, device=cuda).to(torch.bfloat16)
+    # assignments in a shuffled order, each pointing at its token's row
+    perm = torch.from_numpy(rng.permutation(T * k)).to(cuda)
+    row_of = torch.div(perm, k, rounding_mode="floor").to(torch.int32)
+    a_ids = ids.reshape(-1)[perm].contiguous()
+    a_w = w.reshape(-1)[perm].contiguous()
+    contrib = moe_prefill_rows(x, row_of, a_ids, a_w, bank)
+    mat = moe_expert_ffn_prefill(x[row_of.long()].contiguous(), a_ids.view(-1, 1),
+                                 a_w.view(-1, 1), bank, out_dtype=torch.float16)
+    assert torch.equal(contrib, mat)
+    inv = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    inv[perm] = torch.arange(T * k, dtype=torch.int32, device=cuda)
+    out = moe_combine(contrib, inv, k)
+    ref = moe_expert_ffn_prefill(x, ids, w, bank)
+    torch.cuda.synchronize(cuda)
+    assert torch.equal(out, ref)
+    # no assignments: nothing enqueued, empty result
+    empty = torch.empty(0, dtype=torch.int32, device=cuda)
+    got = moe_prefill_rows(x, empty, empty, empty.float(), bank)
+    assert got.shape == (0, 2048)
