@@ -113,10 +113,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __half* x16, c
 }
 
 // ---------------------------------------------------------------------------
-// Router over T prompt tokens. Same arithmetic, bit for bit, as
-// router_logits_kernel run once per token: the RMS-normalised fp16 input of
-// stage_x_plain (256-thread reduction order), the per-lane chunk order and
-// fp32 FMA sequence of its dot product, and the same warp butterfly.
+// The prompt path's router input: the decode router's normalised fp16 input,
+// bit for bit, for T tokens at once.
 
 // xn[t] = fp16(x[t] * rsqrt(mean(x[t]^2) + eps) * nw). One warp per token
 // replays the reduction of stage_x_plain's 256 threads: virtual thread
@@ -153,102 +151,6 @@ __global__ void __launch_bounds__(256) x_norm_plain_kernel(const float* x32, con
       if (k < n) o[lane + 32 * k] = __float2half_rn(xv[k] * scale * nw[lane + 32 * k]);
   }
   pdl_launch_dependents();
-}
-
-constexpr int kRbTok = 28;  // tokens per CTA (fp32 tile in shared memory: 224 KB at H = 2048)
-constexpr int kRbRows = 4;  // router rows per warp and round
-
-// logits[t, e] (and slogit[t] for the extra shared-gate row) for a tile of 28
-// tokens x all rows. The tile's normalised inputs are staged once as fp32
-// (exact: they are fp16 values), so the inner loop is loads and FMAs only;
-// each warp takes 4 rows per round, converts their 8-element weight chunk once
-// and applies it to all 28 tokens: 112 independent accumulation chains, each
-// in the decode kernel's order (lane chunks c = lane + 32j, the element order
-// of its dot8, the same butterfly), so the logits are bit-identical to it.
-// Requires H % 256 == 0, H <= 2048.
-__global__ void __launch_bounds__(256, 1) router_logits_batch_kernel(
-    const __half* xn, int T, int H, const __half* W, int E, const __half* wsg, float* logits,
-    float* slogit) {
-  extern __shared__ __align__(16) float xtile[];  // [kRbTok][H] fp32
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * kRbTok;
-  const int nt = min(kRbTok, T - t0);
-  const int nch = H / 256;
-  const int rows = E + (wsg != nullptr ? 1 : 0);
-  pdl_wait();
-  for (int i = threadIdx.x; i < nt * H / 8; i += blockDim.x) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(xn + (size_t)t0 * H + (size_t)i * 8);
-    const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-    // chunk i's elements 0..3 and 4..7 go to the first and second half of the
-    // token's row, so a warp's 16-byte loads are consecutive (no bank conflicts)
-    const int tt = i / (H / 8), cidx = i % (H / 8);
-    float* row = xtile + (size_t)tt * H;
-    const float2 a = __half22float2(hp[0]), b = __half22float2(hp[1]);
-    const float2 c = __half22float2(hp[2]), e = __half22float2(hp[3]);
-    *reinterpret_cast<float4*>(row + 4 * cidx) = make_float4(a.x, a.y, b.x, b.y);
-    *reinterpret_cast<float4*>(row + H / 2 + 4 * cidx) = make_float4(c.x, c.y, e.x, e.y);
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-  for (int r0 = kRbRows * warp; r0 < rows; r0 += kRbRows * 8) {
-    const __half* wr[kRbRows];
-#pragma unroll
-    for (int q = 0; q < kRbRows; ++q) {
-      const int r = r0 + q;
-      wr[q] = r < E ? W + (size_t)r * H : (r == E && wsg != nullptr ? wsg : nullptr);
-    }
-    float acc[kRbTok][kRbRows];
-#pragma unroll
-    for (int tt = 0; tt < kRbTok; ++tt)
-#pragma unroll
-      for (int q = 0; q < kRbRows; ++q) acc[tt][q] = 0.f;
-    for (int j = 0; j < nch; ++j) {
-      const int c = lane + 32 * j;  // this lane's 8-element chunk
-      float wf[kRbRows][8];
-#pragma unroll
-      for (int q = 0; q < kRbRows; ++q) {
-        const uint4 raw = wr[q] != nullptr ? ld_stream_v4(wr[q] + c * 8) : make_uint4(0, 0, 0, 0);
-        const __half2* wh = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(wh[e]);
-          wf[q][2 * e] = f.x;
-          wf[q][2 * e + 1] = f.y;
-        }
-      }
-      // the next token's inputs are loaded while the current token's FMAs run
-      float4 n0 = *reinterpret_cast<const float4*>(xtile + c * 4);
-      float4 n1 = *reinterpret_cast<const float4*>(xtile + H / 2 + c * 4);
-#pragma unroll
-      for (int tt = 0; tt < kRbTok; ++tt) {
-        const float4 x0 = n0, x1 = n1;
-        if (tt + 1 < kRbTok) {
-          const int tn = min(tt + 1, nt - 1);
-          n0 = *reinterpret_cast<const float4*>(xtile + (size_t)tn * H + c * 4);
-          n1 = *reinterpret_cast<const float4*>(xtile + (size_t)tn * H + H / 2 + c * 4);
-        }
-        if (tt < nt) {
-          const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-#pragma unroll
-            for (int q = 0; q < kRbRows; ++q) acc[tt][q] = fmaf(wf[q][e], xv[e], acc[tt][q]);
-        }
-      }
-    }
-#pragma unroll
-    for (int tt = 0; tt < kRbTok; ++tt) {
-#pragma unroll
-      for (int q = 0; q < kRbRows; ++q) {
-        const float a = warp_sum(acc[tt][q]);
-        const int r = r0 + q;
-        if (lane == 0 && tt < nt) {
-          if (r < E) logits[(size_t)(t0 + tt) * E + r] = a;
-          else if (r == E && wsg != nullptr) slogit[t0 + tt] = a;
-        }
-      }
-    }
-  }
 }
 
 // Top-k of one token's E router logits by one warp (E <= 256: 8 logits per
@@ -624,34 +526,15 @@ int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw,
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
-// xn [T, H] fp16 = the router's normalised input; logits / slogit as
-// router_logits_launch with x_f32 + nw, bit for bit.
-int router_logits_batch_launch(const float* x32, const float* nw, float eps, int T, int H,
-                               const void* w_router, int E, const void* w_sg, float* logits,
-                               float* slogit, __half* xn, cudaStream_t stream) {
-  if (!x32 || !nw || !w_router || !logits || !xn || T < 1 || E < 1) return IQ36_ERR_ARG;
-  if (w_sg && !slogit) return IQ36_ERR_ARG;
+// xn [T, H] fp16 = the decode router's normalised input (stage_x_plain), bit
+// for bit. Requires H % 32 == 0, H <= 2048.
+int x_norm_launch(const float* x32, const float* nw, float eps, int T, int H, __half* xn,
+                  cudaStream_t stream) {
+  if (!x32 || !nw || !xn || T < 1) return IQ36_ERR_ARG;
   if (H < 256 || H % 256 || H > 2048) return IQ36_ERR_SHAPE;
-  if (!aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) || !aligned(xn, 16))
-    return IQ36_ERR_ALIGN;
-  const size_t smem = (size_t)kRbTok * H * 4;
-  static std::atomic<bool> attr_set[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
-  if (!attr_set[dev].load()) {
-    if (cudaFuncSetAttribute(router_logits_batch_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kRbTok * 2048 * 4) != cudaSuccess)
-      return IQ36_ERR_CUDA;
-    attr_set[dev].store(true);
-  }
-  cudaError_t e = launch(x_norm_plain_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream, x32, nw,
-                         eps, T, H, xn);
-  if (e == cudaSuccess)
-    e = launch(router_logits_batch_kernel, dim3(ceil_div(T, kRbTok)), dim3(256), smem, stream,
-               (const __half*)xn, T, H,
-               reinterpret_cast<const __half*>(w_router), E,
-               reinterpret_cast<const __half*>(w_sg), logits, slogit);
+  if (!aligned(xn, 16)) return IQ36_ERR_ALIGN;
+  const cudaError_t e = launch(x_norm_plain_kernel, dim3(ceil_div(T, 8)), dim3(256), 0, stream,
+                               x32, nw, eps, T, H, xn);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 

@@ -741,6 +741,133 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Router logits over T prompt tokens on tcgen05: logits[t, e] = xn[t] . W[e]
+// (fp16 operands, fp32 accumulation in the tensor core), slogit[t] = xn[t] .
+// w_sg. One CTA per 128-token tile: warp 0 streams 64-wide K blocks of xn
+// (128 rows), W (256 rows; rows past E read as zeros) and the shared-gate row
+// (a 16-row box, rows past the first read as zeros) into a 4-stage ring;
+// warp 1 issues M128 x N256 and M128 x N16 MMAs into TMEM columns [0, 256)
+// and [256, 272); warps 2-5 (thread = token = TMEM lane) store the rows.
+// The logits equal the decode router's up to fp32 summation order (the
+// reference's own router check: max-abs <= 1e-4).
+constexpr int kRtM = 128, kRtN = 256, kRtNs = 16, kRtBK = 64, kRtStages = 4;
+constexpr int kRtA = kRtM * 128, kRtB = kRtN * 128, kRtBs = kRtNs * 128;
+constexpr int kRtStage = kRtA + kRtB + kRtBs;  // 51200 B, every piece 1024-aligned
+constexpr int kRtOffBar = kRtStages * kRtStage;
+constexpr int kRtSmem = kRtOffBar + 256 + 1024;
+constexpr uint32_t kRtIdesc = (1u << 4) | ((uint32_t)(kRtN >> 3) << 17) | ((uint32_t)(kRtM >> 4) << 24);
+constexpr uint32_t kRtIdescS = (1u << 4) | ((uint32_t)(kRtNs >> 3) << 17) | ((uint32_t)(kRtM >> 4) << 24);
+
+__global__ void __launch_bounds__(192, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmS, int has_sg, int T, int H, int E,
+                     float* logits, float* slogit) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_raw = smem_u32(smem_raw);
+  const uint32_t base = (base_raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - base_raw);
+  const uint32_t bar = base + kRtOffBar;
+  const uint32_t bar_full = bar, bar_empty = bar + 8 * kRtStages, bar_done = bar + 16 * kRtStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kRtOffBar + 192);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kRtM;
+  const int nk = H / kRtBK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRtStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  bool ok = true;
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t tx = kRtA + kRtB + (has_sg ? kRtBs : 0);
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % kRtStages;
+        ok = mbar_wait(bar_empty + 8 * s, ((kb / kRtStages) & 1) ^ 1u);
+        if (!ok) break;
+        const uint32_t st = base + s * kRtStage;
+        mbar_arrive_tx(bar_full + 8 * s, tx);
+        tma_load_2d(st, &tmX, kb * kRtBK, m0, bar_full + 8 * s);
+        tma_load_2d(st + kRtA, &tmW, kb * kRtBK, 0, bar_full + 8 * s);
+        if (has_sg) tma_load_2d(st + kRtA + kRtB, &tmS, kb * kRtBK, 0, bar_full + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % kRtStages;
+        ok = mbar_wait(bar_full + 8 * s, (kb / kRtStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t st = base + s * kRtStage;
+#pragma unroll
+        for (int kk = 0; kk < kRtBK / 16; ++kk) {
+          const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+          umma_f16(tmem, sw128_desc(st + kk * 32), sw128_desc(st + kRtA + kk * 32), kRtIdesc, acc);
+          if (has_sg)
+            umma_f16(tmem + kRtN, sw128_desc(st + kk * 32), sw128_desc(st + kRtA + kRtB + kk * 32),
+                     kRtIdescS, acc);
+        }
+        umma_commit(bar_empty + 8 * s);
+      }
+      umma_commit(bar_done);
+    }
+  } else {
+    // thread = token row = TMEM lane; warps 2,3,4,5 own lanes 64.., 96.., 0.., 32..
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane, t = m0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    ok = mbar_wait(bar_done, 0);
+    if (ok) {
+      tc_fence_after();
+      for (int c = 0; c < (E + 15) / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_off + c * 16, v);
+        tmem_ld_wait();
+        if (t < T) {
+          float* dst = logits + (size_t)t * E + c * 16;
+          if ((E & 3) == 0 && c * 16 + 16 <= E) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              reinterpret_cast<float4*>(dst)[q] =
+                  make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                              __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+          } else {
+            for (int j = 0; j < 16 && c * 16 + j < E; ++j) dst[j] = __uint_as_float(v[j]);
+          }
+        }
+      }
+      if (has_sg) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_off + kRtN, v);
+        tmem_ld_wait();
+        if (t < T) slogit[t] = __uint_as_float(v[0]);
+      }
+    }
+  }
+  if (!ok && lane == 0) atomicAdd(&g_gemm_wait_timeouts, 1);
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 
 struct PfLayout {
@@ -800,6 +927,49 @@ static bool make_act_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D fp16 tensor [rows, cols], box 64 columns x box_rows rows, SWIZZLE_128B;
+// a box reaching past the rows reads zeros.
+static bool make_f16_map(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
+                         uint32_t box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64u, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// logits [T, E] fp32 (and slogit [T] when w_sg is set) from xn [T, H] fp16.
+int router_tc_launch(const __half* xn, int T, int H, const void* w_router, int E,
+                     const void* w_sg, float* logits, float* slogit, cudaStream_t stream) {
+  if (!xn || !w_router || !logits || (w_sg && !slogit)) return IQ36_ERR_ARG;
+  if (T < 1 || E < 1 || E > kRtN || H < kRtBK || H % kRtBK) return IQ36_ERR_SHAPE;
+  if (!aligned(xn, 16) || !aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) ||
+      !aligned(logits, 16))
+    return IQ36_ERR_ALIGN;
+  CUtensorMap mx, mw, ms;
+  if (!make_f16_map(&mx, xn, (uint64_t)T, (uint64_t)H, kRtM) ||
+      !make_f16_map(&mw, w_router, (uint64_t)E, (uint64_t)H, kRtN) ||
+      !make_f16_map(&ms, w_sg ? w_sg : w_router, 1, (uint64_t)H, kRtNs))
+    return IQ36_ERR_CUDA;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (!attr_set[dev].load()) {
+    if (cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRtSmem) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+    attr_set[dev].store(true);
+  }
+  const cudaError_t e = launch(router_tc_kernel, dim3((T + kRtM - 1) / kRtM), dim3(192),
+                               (size_t)kRtSmem, stream, mx, mw, ms, w_sg ? 1 : 0, T, H, E, logits,
+                               slogit);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
 // 2-D u8 code tensor [rows, bytes_per_row], box 64 bytes x 128 rows, no swizzle.
@@ -1143,9 +1313,9 @@ extern "C" int iq36_moe_prefill_rows(const void* x_bf16, int32_t n_rows, int32_t
 
 // ---------------------------------------------------------------------------
 // The MoE block of one layer over T prompt tokens, residual updated in place:
-// router logits on the RMS-normalised fp32 residual (same arithmetic, bit for
-// bit, as the decode step's router, so the routing matches token for token;
-// the normalised fp16 input also feeds the experts), top-k
+// router logits on the RMS-normalised fp32 residual (the decode router's fp16
+// input bit for bit, logits on tcgen05: equal to the decode step's up to fp32
+// summation order; the normalised fp16 input also feeds the experts), top-k
 // selection, the grouped routed experts (fp16 contributions summed in rank
 // order into the residual), and the shared expert as two dense u4 GEMMs
 // (gate_up with SwiGLU, then down scaled by sigmoid(shared logit) and added to
@@ -1158,9 +1328,10 @@ int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw,
                          float* slogit, cudaStream_t stream);
 int router_select_launch(const float* logits, int T, int E, int k, int32_t* ids, float* weights,
                          cudaStream_t stream);
-int router_logits_batch_launch(const float* x32, const float* nw, float eps, int T, int H,
-                               const void* w_router, int E, const void* w_sg, float* logits,
-                               float* slogit, __half* xn, cudaStream_t stream);
+int x_norm_launch(const float* x32, const float* nw, float eps, int T, int H, __half* xn,
+                  cudaStream_t stream);
+int router_tc_launch(const __half* xn, int T, int H, const void* w_router, int E,
+                     const void* w_sg, float* logits, float* slogit, cudaStream_t stream);
 
 struct MoeLayerPfLayout {
   size_t slogit, xn, act, gemm, moe, total;
@@ -1208,9 +1379,10 @@ extern "C" int iq36_moe_layer_prefill(float* residual, int32_t T, int32_t hidden
   __half* xn = reinterpret_cast<__half*>(ws + L.xn);
   __half* act = reinterpret_cast<__half*>(ws + L.act);
   const cudaStream_t s = as_stream(stream);
-  int st = router_logits_batch_launch(residual, norm_weight, norm_eps, T, H, w_router_f16, E,
-                                      shared ? w_shared_gate_f16 : nullptr, logits,
-                                      shared ? slogit : nullptr, xn, s);
+  int st = x_norm_launch(residual, norm_weight, norm_eps, T, H, xn, s);
+  if (st == IQ36_OK)
+    st = router_tc_launch(xn, T, H, w_router_f16, E, shared ? w_shared_gate_f16 : nullptr, logits,
+                          shared ? slogit : nullptr, s);
   if (st == IQ36_OK) st = router_select_launch(logits, T, E, k, ids, weights, s);
   if (st == IQ36_OK)
     st = moe_prefill_launch(xn, IQ36_F16, T, ids, weights, k, routed, residual, IQ36_F32, 1,

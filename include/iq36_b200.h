@@ -195,7 +195,9 @@ int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids, const fl
                      void* workspace, size_t workspace_bytes, iq36_stream_t stream);
 /* The MoE block of one decoder layer over T prompt tokens, fp32 residual
  * [T, hidden] updated in place: router logits on RMSNorm(residual) (the
- * iq36_router_logits kernel, so routing equals the decode step's), top-k
+ * decode router's fp16 input bit for bit; the logits on tensor cores, equal
+ * to the decode router's up to fp32 summation order, within the reference's
+ * 1e-4 router gate), top-k
  * selection (ids, weights [T, k]; logits [T, E] kept for inspection), the
  * routed experts as in iq36_moe_prefill (x = fp16 RMSNorm(residual); fp16
  * contributions summed in rank order, added to the residual), and the shared

@@ -1,7 +1,8 @@
 """Batched prefill (the whole prompt per launch) against the CPU oracle.
 
 The MoE block over T tokens (iq36_moe_layer_prefill) is checked per token
-against the oracle's MoE FFN with bit-exact routing; the batched model prefill
+against the oracle's MoE FFN (selection bit-exact on the kernel's logits,
+logits within the reference's 1e-4 router gate); the batched model prefill
 is checked end to end against the oracle model fed the prompt token by token:
 greedy token after the prompt equal, KL divergence of the next-token
 distribution <= 0.005, then a greedy decode continuation from the state the
@@ -52,7 +53,8 @@ def test_moe_layer_prefill_matches_oracle(cuda, config1):
     got = res.cpu().numpy()
     g_logits, g_ids, g_wts = logits.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy()
     # the decode step's router (fused norm from the fp32 residual, one token per
-    # call) gives the same logits bit for bit, so prefill and decode route alike
+    # call, CUDA-core FMAs) agrees with the tensor-core prompt router up to the
+    # fp32 summation order: the reference's router gate, max-abs <= 1e-4
     from engine import _native as N
     from engine.ops import _stream
     dl = torch.empty(256, dtype=torch.float32, device=cuda)
@@ -61,7 +63,7 @@ def test_moe_layer_prefill_matches_oracle(cuda, config1):
     for t in (0, 17, T - 1):
         N.call("iq36_router_logits", None, r0[t].data_ptr(), nwd.data_ptr(), 1e-6, 1, 2048,
                wr.data_ptr(), 256, wsg.data_ptr(), dl.data_ptr(), dsl.data_ptr(), _stream(cuda))
-        np.testing.assert_array_equal(g_logits[t], dl.cpu().numpy())
+        assert np.max(np.abs(g_logits[t] - dl.cpu().numpy())) <= 1e-4
     sh0 = {k: v[0] for k, v in c["shared"].items()}
     for t in range(T):
         x16 = oracle.rms_norm(res0[t], nw, 1e-6).astype(np.float16)
