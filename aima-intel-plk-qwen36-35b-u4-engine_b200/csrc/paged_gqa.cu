@@ -235,11 +235,25 @@ __global__ void __launch_bounds__(kCombWarps * 32) gqa_combine_kernel(
   l = warp_sum(l);
   if (lane == 0) red_l[warp] = l;
   __syncthreads();
+  // Eight partial rows per batch are loaded before any is used (rows of
+  // splits without pages are read but not added), then added in split order.
   float o = 0.f;
-#pragma unroll 4
-  for (int s = warp; s < S; s += kCombWarps) {
-    const float w = sw[s];
-    if (w != 0.f) o = fmaf(ws_acc[(mbase + (size_t)s * kGrp) * kD + d], w, o);
+  constexpr int kBatch = 8;
+  for (int s0 = warp; s0 < S; s0 += kBatch * kCombWarps) {
+    float v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int s = s0 + j * kCombWarps;
+      v[j] = s < S ? ws_acc[(mbase + (size_t)s * kGrp) * kD + d] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int s = s0 + j * kCombWarps;
+      if (s < S) {
+        const float w = sw[s];
+        if (w != 0.f) o = fmaf(v[j], w, o);
+      }
+    }
   }
   red_o[warp][lane] = o;
   __syncthreads();

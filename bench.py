@@ -23,8 +23,10 @@ Other workloads: --workload prefill (BASELINE config 4 prefill tok/s: the batche
 prefill of a --ctx-token prompt, 4096 or 32768; a step is one whole prompt),
 --workload attn_prefill / delta_prefill (one prompt-path op alone over --tokens),
 --workload moe_prefill (grouped MoE
-prefill; replicas at --gpus > 1, expert-parallel over NCCL with --ep) and --workload gemv
-(one u4 GEMV per step, --rows / --k for other shapes).
+prefill; replicas at --gpus > 1, expert-parallel over NCCL with --ep), --workload gemv
+(one u4 GEMV per step, --rows / --k for other shapes), --workload
+moe_decode (the batch-1 MoE block, HBM GB/s) and --workload gqa_decode
+(paged GQA decode at --ctx, HBM GB/s).
 """
 
 from __future__ import annotations
@@ -626,7 +628,7 @@ def run_moe_prefill(args, world, rank, local) -> None:
             print(json.dumps({"profile_step": "done", "workload": "moe_prefill", "T": T}))
         return
     # the expert weights (418 MB) exceed L2; flush L2 between calls anyway
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     sampler = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize(dev)
@@ -639,7 +641,7 @@ def run_moe_prefill(args, world, rank, local) -> None:
     torch.cuda.synchronize(dev)
     evs = []
     for _ in range(args.steps):
-        flush.zero_()
+        flush()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         call()
@@ -687,6 +689,249 @@ def run_moe_prefill(args, world, rank, local) -> None:
                      "frac": round(tflops / peak, 4), "traffic": None},
         "clocks": clocks,
     }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+class L2Flush:
+    """Flush L2 between timed calls: write a buffer larger than L2 (126 MB),
+    then read another one, so the dirty lines of the write are written back
+    before the timed call instead of during it."""
+
+    def __init__(self, dev):
+        import torch
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.r = torch.zeros(64 << 20, dtype=torch.int32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
+def _flushed_call_times(call, steps, flush, dev):
+    """Device time of each call, L2 flushed before it (L2Flush)."""
+    import torch
+    evs = []
+    for i in range(steps):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        call(i)
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize(dev)
+    return [s.elapsed_time(e) / 1e3 for s, e in evs]
+
+
+def run_moe_decode(args, world, rank, local) -> None:
+    """the batch-1 MoE block (router 2048 -> 256 fp16
+    ~N(0, 0.02), top-8, 8 routed + 1 shared u4 g128 experts, shared gate) in
+    one iq36_moe_block_decode call per step on a fresh x ~N(0,1) from a pool of
+    64 (so the routed experts change step to step). L2 flushed before every
+    step; value = algorithmic bytes (15,761,408 + 8 KB in/out) / device time."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    from engine import _native as N
+    from engine import ops
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    E, H, I, k, G = 256, 2048, 512, 8, 128
+
+    def make_bank(n, seed):
+        t = [torch.empty(n, 2 * I, H // 2, dtype=torch.uint8, device=dev),
+             torch.empty(n, 2 * I, H // G, dtype=torch.float16, device=dev),
+             torch.empty(n, 2 * I * H // G // 2, dtype=torch.uint8, device=dev),
+             torch.empty(n, H, I // 2, dtype=torch.uint8, device=dev),
+             torch.empty(n, H, I // G, dtype=torch.float16, device=dev),
+             torch.empty(n, H * I // G // 2, dtype=torch.uint8, device=dev)]
+        for j, v in enumerate(t):
+            ops.synth_fill(v, 1 if v.dtype == torch.float16 else 0, seed, 100 + j, 0.005, 0.02)
+        return ops.ExpertBank(*t, G)
+
+    bank, shared = make_bank(E, 21), make_bank(1, 22)
+    g = torch.Generator(dev).manual_seed(23 + rank)
+    w_router = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.float16)
+    w_sg = (torch.randn(1, H, device=dev, generator=g) * 0.02).to(torch.float16)
+    xs = torch.randn(64, H, device=dev, generator=g).to(torch.float16)
+    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    wts = torch.empty(k, dtype=torch.float32, device=dev)
+    logits = torch.empty(E, dtype=torch.float32, device=dev)
+    out = torch.empty(H, dtype=torch.float16, device=dev)
+    ws = torch.empty(N.lib().iq36_moe_block_decode_workspace_bytes(k, H, I), dtype=torch.uint8,
+                     device=dev)
+    rb, sb = bank.c(), shared.c()
+    stream = torch.cuda.current_stream(dev)
+
+    def call(i):
+        N.call("iq36_moe_block_decode", xs[i % 64].data_ptr(), w_router.data_ptr(),
+               w_sg.data_ptr(), k, ctypes.byref(rb), ctypes.byref(sb), ids.data_ptr(),
+               wts.data_ptr(), logits.data_ptr(), out.data_ptr(), 1, ws.data_ptr(), ws.numel(),
+               stream.cuda_stream)
+
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize(dev)
+    flush = L2Flush(dev)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    times = _flushed_call_times(call, args.steps, flush, dev)
+    clocks = sampler.stop()
+    barrier(world)
+    per_call = max_over_ranks(sum(times) / len(times), world)
+    step_bytes = 15761408 + 2 * H * 2
+    hbm, src = peaks()
+    gbs = step_bytes / per_call / 1e9
+    # end to end: x from pinned host memory, the block output read back, every step
+    x_host = xs.cpu().pin_memory()
+    out_host = torch.empty(H, dtype=torch.float16).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        xs[i % 64].copy_(x_host[i % 64], non_blocking=True)
+        call(i)
+        out_host.copy_(out, non_blocking=True)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    line = {
+        "metric": "MoE decode block HBM GB/s (BASELINE config 1)",
+        "value": round(world * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_call * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4xf16",
+        "data": "synthetic",
+        "config": {"workload": "config1 MoE decode block: router 2048->256 + top-8 + 8 routed "
+                               "and 1 shared u4 g128 experts (I=512) + shared gate, fp16 out",
+                   "bytes_per_step": step_bytes, "l2": "flushed before every step",
+                   "parallelism": "replicas" if world > 1 else "single GPU"},
+        "e2e": {"value": round(world * step_bytes / t_e2e / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "iq36_moe_block_decode (router, select, gate_up, "
+                     "down: 4 launches)", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        torch.cuda.synchronize(dev)
+        sel = ids.cpu().numpy()
+        keys = ("gu_w", "gu_s", "gu_z", "d_w", "d_s", "d_z")
+
+        def parts(b):
+            return (b.gate_up_weight, b.gate_up_scale, b.gate_up_zp, b.down_weight,
+                    b.down_scale, b.down_zp)
+        b8 = {key: t[torch.from_numpy(sel.astype(np.int64)).to(dev)].cpu().numpy()
+              for key, t in zip(keys, parts(bank))}
+        sh = {key: t[0].cpu().numpy() for key, t in zip(keys, parts(shared))}
+        wr, wg = w_router.cpu().numpy(), w_sg.cpu().numpy()
+        x0 = xs[(args.steps - 1) % 64].cpu().numpy()
+        reps, t0 = 0, time.time()
+        while time.time() - t0 < 10.0 and reps < 500:
+            lg = oracle.f16_linear(x0, wr)
+            oid, ow = oracle.router_select(lg[None], k)
+            sl = oracle.f16_linear(x0, wg)[0]
+            oracle.moe_decode(x0, np.arange(k, dtype=np.int32), ow[0], b8, sh, sl, G,
+                              threads=os.cpu_count() or 1)
+            reps += 1
+        dt = (time.time() - t0) / reps
+        line["cpu_baseline"] = {"value": round(step_bytes / dt / 1e9, 3), "unit": "GB/s",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"{reps} oracle MoE blocks (router, top-8, 8 routed + "
+                                          "1 shared expert) on one x"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_gqa_decode(args, world, rank, local) -> None:
+    """paged GQA decode, 16 q heads over 2 KV heads, head
+    dim 256, fp16 KV cache in 16-token blocks behind a seeded permuted block
+    table, output gate, scale 1/16, at --ctx tokens. L2 flushed before every
+    call; value = algorithmic bytes (ctx * 2048 + block table + q/gate/out) /
+    device time."""
+    import numpy as np
+    import torch
+    from engine import ops
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    ctx, nq, nkv, d, bs = args.ctx, 16, 2, 256, 16
+    nb = ctx // bs
+    g = torch.Generator(dev).manual_seed(31 + rank)
+    kc = torch.randn(nb, bs, nkv, d, device=dev, generator=g).to(torch.float16)
+    vc = torch.randn(nb, bs, nkv, d, device=dev, generator=g).to(torch.float16)
+    bt = torch.from_numpy(np.random.default_rng(ctx + rank).permutation(nb).astype(np.int32)).to(dev)
+    q = torch.randn(nq, d, device=dev, generator=g).to(torch.float16)
+    gate = torch.randn(nq, d, device=dev, generator=g).to(torch.float16)
+    ws = ops.paged_gqa_workspace(ctx, nq, nkv, d, dev)
+    out = torch.empty(nq, d, dtype=torch.float32, device=dev)
+
+    def call(i):
+        ops.paged_gqa_decode(q, kc, vc, bt, ctx, 1.0 / 16, gate=gate, workspace=ws, out=out)
+
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize(dev)
+    flush = L2Flush(dev)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    times = _flushed_call_times(call, args.steps, flush, dev)
+    clocks = sampler.stop()
+    barrier(world)
+    per_call = max_over_ranks(sum(times) / len(times), world)
+    step_bytes = ctx * 2048 + nb * 4 + 2 * nq * d * 2 + nq * d * 4
+    hbm, src = peaks()
+    gbs = step_bytes / per_call / 1e9
+    q_host, out_host = q.cpu().pin_memory(), torch.empty(nq, d).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        q.copy_(q_host, non_blocking=True)
+        call(i)
+        out_host.copy_(out, non_blocking=True)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    line = {
+        "metric": "paged GQA decode HBM GB/s (BASELINE config 2)",
+        "value": round(world * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_call * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": f"config2 paged GQA decode, ctx {ctx}, 16 q / 2 KV heads, D 256, "
+                               "16-token blocks, permuted block table, output gate",
+                   "ctx": ctx, "bytes_per_step": step_bytes, "l2": "flushed before every call",
+                   "parallelism": "replicas" if world > 1 else "single GPU"},
+        "e2e": {"value": round(world * step_bytes / t_e2e / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": nq * d * 2, "d2h_bytes_per_step": nq * d * 4},
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "gqa_split_kernel + gqa_combine_kernel",
+                     "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": src},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        qn, kn, vn = q.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy()
+        btn, gn = bt.cpu().numpy(), gate.cpu().numpy()
+        reps, t0 = 0, time.time()
+        while time.time() - t0 < 10.0 and reps < 200:
+            oracle.paged_gqa(qn, kn, vn, btn, ctx, 1.0 / 16, gn, threads=os.cpu_count() or 1)
+            reps += 1
+        dt = (time.time() - t0) / reps
+        line["cpu_baseline"] = {"value": round(step_bytes / dt / 1e9, 3), "unit": "GB/s",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"{reps} oracle paged-GQA decodes at ctx {ctx}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -809,7 +1054,8 @@ def run_gemv(args, world, rank, local) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--workload", choices=["decode", "prefill", "moe_prefill", "gemv",
-                                           "attn_prefill", "delta_prefill"],
+                                           "attn_prefill", "delta_prefill", "moe_decode",
+                                           "gqa_decode"],
                     default="decode")
     ap.add_argument("--rows", type=int, default=1024, help="output rows for --workload gemv")
     ap.add_argument("--k", type=int, default=2048, help="input length for --workload gemv")
@@ -839,6 +1085,10 @@ def main() -> None:
             run_op_prefill(args, world, rank, local)
         elif args.workload == "gemv":
             run_gemv(args, world, rank, local)
+        elif args.workload == "moe_decode":
+            run_moe_decode(args, world, rank, local)
+        elif args.workload == "gqa_decode":
+            run_gqa_decode(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
