@@ -205,41 +205,63 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     pdl_launch_dependents();
     const int g = lane >> 2, t = lane & 3;
     const int gb = warp * geo.ng / kStreamConsumers, ge = (warp + 1) * geo.ng / kStreamConsumers;
-    for (int c = 0; c < nloc; ++c) {
-      const int s = c % geo.stages, j = c % kRedChunks;
-      float accA = 0.f, accB = 0.f;
-      if (__all_sync(0xffffffffu, ring_wait(seq, sbase + L.full + 8 * s, s, c, geo.stages))) {
-        chunk_dot_range<G>(geo, smem + L.ring + s * geo.stage_bytes, xs, xc, lane, gb, ge, accA,
-                           accB);
-        // generic reads of the stage before the producer's next bulk copy
-        // (async proxy) into it
+    // With four or more ring stages the warps take chunks in pairs (two
+    // independent mma chains per group); the sums per chunk are unchanged.
+    const bool pair = geo.stages >= 4;
+    int c = 0;
+    while (c < nloc && ok) {
+      const int n = (pair && c + 1 < nloc) ? 2 : 1;
+      const int s0 = c % geo.stages, s1 = (c + 1) % geo.stages;
+      float a0 = 0.f, b0 = 0.f, a1 = 0.f, b1 = 0.f;
+      bool got = __all_sync(0xffffffffu, ring_wait(seq, sbase + L.full + 8 * s0, s0, c, geo.stages));
+      if (got && n == 2)
+        got = __all_sync(0xffffffffu,
+                         ring_wait(seq, sbase + L.full + 8 * s1, s1, c + 1, geo.stages));
+      if (got) {
+        if (n == 2)
+          chunk_dot_pair<G>(geo, smem + L.ring + s0 * geo.stage_bytes,
+                            smem + L.ring + s1 * geo.stage_bytes, xs, xc, lane, gb, ge, a0, b0, a1,
+                            b1);
+        else
+          chunk_dot_range<G>(geo, smem + L.ring + s0 * geo.stage_bytes, xs, xc, lane, gb, ge, a0,
+                             b0);
+        // generic reads of the stages before the producer's next bulk copies
+        // (async proxy) into them
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         __syncwarp();
-        if (lane == 0) sm_mbar_arrive(sbase + L.empty + 8 * s);
+        if (lane == 0) {
+          sm_mbar_arrive(sbase + L.empty + 8 * s0);
+          if (n == 2) sm_mbar_arrive(sbase + L.empty + 8 * s1);
+        }
       } else if (lane == 0) {
         seq[8] = 1;  // shared so that every consumer warp leaves at the barrier below
       }
-      float* rbuf = red + ((c / kRedChunks) & 1) * kRedChunks * kStreamConsumers * 16;
-      if (t == 0) {
-        rbuf[(j * kStreamConsumers + warp) * 16 + g] = accA;
-        rbuf[(j * kStreamConsumers + warp) * 16 + g + 8] = accB;
-      }
-      if (j == kRedChunks - 1 || c == nloc - 1) {
-        consumer_sync();
-        if (seq[8] != 0) {
-          ok = false;
-          break;
+      for (int u = 0; u < n && ok; ++u) {
+        const int cc = c + u, j = cc % kRedChunks;
+        float* rbuf = red + ((cc / kRedChunks) & 1) * kRedChunks * kStreamConsumers * 16;
+        if (t == 0) {
+          rbuf[(j * kStreamConsumers + warp) * 16 + g] = u ? a1 : a0;
+          rbuf[(j * kStreamConsumers + warp) * 16 + g + 8] = u ? b1 : b0;
         }
-        for (int i = threadIdx.x; i < (j + 1) * 16; i += kStreamConsumers * 32) {
-          const int jj = i >> 4, r = i & 15;
-          float v = 0.f;
+        if (j == kRedChunks - 1 || cc == nloc - 1) {
+          consumer_sync();
+          if (seq[8] != 0) {
+            ok = false;
+            break;
+          }
+          for (int i = threadIdx.x; i < (j + 1) * 16; i += kStreamConsumers * 32) {
+            const int jj = i >> 4, r = i & 15;
+            float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < kStreamConsumers; ++w) v += rbuf[(jj * kStreamConsumers + w) * 16 + r];
-          int p, r0;
-          proj_chunk(ps, c0 + c - j + jj, K, geo.ng, p, r0);
-          store_row(ps.out[p], ps.dtype[p], ps.acc[p], r0 + r, v);
+            for (int w = 0; w < kStreamConsumers; ++w)
+              v += rbuf[(jj * kStreamConsumers + w) * 16 + r];
+            int p, r0;
+            proj_chunk(ps, c0 + cc - j + jj, K, geo.ng, p, r0);
+            store_row(ps.out[p], ps.dtype[p], ps.acc[p], r0 + r, v);
+          }
         }
       }
+      c += n;
     }
   }
   if (!ok) stream_note_timeout(err);

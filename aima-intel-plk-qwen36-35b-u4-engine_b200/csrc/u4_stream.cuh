@@ -26,7 +26,7 @@ namespace iq36 {
 
 constexpr int kStreamConsumers = 16;                      // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;
-constexpr int kStreamRingBytes = 96 * 1024;
+constexpr int kStreamRingBytes = 128 * 1024;
 constexpr uint32_t kStreamSpinLimit = 1u << 26;
 
 // ---- mbarrier / bulk-copy wrappers --------------------------------------
@@ -226,6 +226,58 @@ __device__ __forceinline__ void chunk_dot_range(const StreamGeom& geo, const uin
     const float zz = (float)((zb[(eB + gi) >> 1] >> (((eB + gi) & 1) * 4)) & 15u);
     accA = fmaf(__half2float(sA[gi]), fmaf(-za, cr.y, c0 - cr.x), accA);
     accB = fmaf(__half2float(sB[gi]), fmaf(-zz, cr.y, c2 - cr.x), accB);
+  }
+}
+
+// Two chunks at once (stages st0, st1; same group range): two independent
+// mma chains per group, each with chunk_dot_range's arithmetic.
+template <int G>
+__device__ __forceinline__ void chunk_dot_pair(const StreamGeom& geo, const uint8_t* st0,
+                                               const uint8_t* st1, const uint4* __restrict__ xs,
+                                               const float2* __restrict__ xc, int lane,
+                                               int g_begin, int g_end, float& accA0,
+                                               float& accB0, float& accA1, float& accB1) {
+  static_assert(G == 128, "pair consumption is built for group 128");
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* st[2] = {st0, st1};
+  const int eA = g * geo.ng, eB = (g + 8) * geo.ng;
+  for (int gi = g_begin; gi < g_end; ++gi) {
+    uint4 va[2], vb[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      va[u] = *reinterpret_cast<const uint4*>(st[u] + g * geo.row_pitch + t * (G / 8) + gi * (G / 2));
+      vb[u] = *reinterpret_cast<const uint4*>(st[u] + (g + 8) * geo.row_pitch + t * (G / 8) +
+                                              gi * (G / 2));
+    }
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 xv = xs[gi * (G / 8) + t * 4 + i];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        uint32_t a = (&va[u].x)[i], b = (&vb[u].x)[i];
+        mma_16816(c[u][0], c[u][1], c[u][2], c[u][3], lop3_and_or(a, 0x000F000Fu, kMagic),
+                  lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                  lop3_and_or(b, 0x00F000F0u, kMagic), xv.x, xv.y);
+        a >>= 8;
+        b >>= 8;
+        mma_16816(c[u][0], c[u][1], c[u][2], c[u][3], lop3_and_or(a, 0x000F000Fu, kMagic),
+                  lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                  lop3_and_or(b, 0x00F000F0u, kMagic), xv.z, xv.w);
+      }
+    }
+    const float2 cr = xc[gi];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const __half* sc = reinterpret_cast<const __half*>(st[u] + geo.off_scale);
+      const uint8_t* zb = st[u] + geo.off_zp;
+      const float za = (float)((zb[(eA + gi) >> 1] >> (((eA + gi) & 1) * 4)) & 15u);
+      const float zz = (float)((zb[(eB + gi) >> 1] >> (((eB + gi) & 1) * 4)) & 15u);
+      float& aA = u ? accA1 : accA0;
+      float& aB = u ? accB1 : accB0;
+      aA = fmaf(__half2float(sc[g * geo.ng + gi]), fmaf(-za, cr.y, c[u][0] - cr.x), aA);
+      aB = fmaf(__half2float(sc[(g + 8) * geo.ng + gi]), fmaf(-zz, cr.y, c[u][2] - cr.x), aB);
+    }
   }
 }
 
