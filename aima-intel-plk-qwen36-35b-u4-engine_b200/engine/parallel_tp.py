@@ -12,7 +12,11 @@ star's decode split:
 * MoE decode, expert-sharded: each rank holds E/P experts; the router runs
   replicated (identical ids everywhere), each rank computes only the routed
   experts it owns (``iq36_moe_decode_sharded``), rank 0 adds the shared
-  expert, and one all-reduce of the [H] fp32 partial sums completes the block.
+  expert, and one all-reduce of the [H] fp32 partial sums completes the block;
+* MoE decode, row-sharded inside every expert: each rank holds I/P
+  intermediate rows of every expert (gate and up rows, the matching K slice
+  of down) and computes all routed experts on them (``iq36_moe_decode``);
+  one all-reduce of the [H] fp32 partial sums completes the block.
 
 Sharding helpers work on host or device tensors (plain slicing and nibble
 repacking); the collectives are torch.distributed (NCCL on GPUs, gloo on CPU).
@@ -94,6 +98,49 @@ def tp_u4_gemv_colparallel(x: torch.Tensor, w_rows: U4Weight,
     parts = [torch.empty_like(y) for _ in range(dist.get_world_size(group))]
     dist.all_gather(parts, y, group=group)
     return torch.cat(parts)
+
+
+def shard_expert_bank_rows(b: ExpertBank, rank: int, world: int) -> ExpertBank:
+    """Tensor parallel inside every expert: intermediate rows [rank*I/P,
+    (rank+1)*I/P) of gate and of up (gate_up rows), and the matching K slice of
+    down (whole quant groups). SwiGLU is elementwise over the intermediate
+    rows, so the down partial sums of all ranks add up to the block."""
+    e, i, g = b.num_experts, b.intermediate, b.group
+    h = b.hidden
+    i0, i1 = _split(i, world, rank, g)
+    rows = torch.cat([torch.arange(i0, i1), torch.arange(i + i0, i + i1)]).to(
+        b.gate_up_weight.device)
+    ngh, ngi = h // g, i // g
+    gu_z = _unpack_nibbles(b.gate_up_zp.reshape(-1)).view(e, 2 * i, ngh)[:, rows]
+    d_z = _unpack_nibbles(b.down_zp.reshape(-1)).view(e, h, ngi)[:, :, i0 // g:i1 // g]
+    return ExpertBank(b.gate_up_weight[:, rows].contiguous(), b.gate_up_scale[:, rows].contiguous(),
+                      _pack_nibbles(gu_z.reshape(-1)).view(e, -1),
+                      b.down_weight[:, :, i0 // 2:i1 // 2].contiguous(),
+                      b.down_scale[:, :, i0 // g:i1 // g].contiguous(),
+                      _pack_nibbles(d_z.reshape(-1)).view(e, -1), g)
+
+
+def tp_moe_decode(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                  bank_rows: ExpertBank, shared_rows: ExpertBank | None,
+                  shared_logit: torch.Tensor | None, group: dist.ProcessGroup | None = None,
+                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-sharded batch-1 MoE block: every routed (and the shared) expert over
+    this rank's intermediate rows as an fp32 partial sum, then one all-reduce."""
+    dev = x.device
+    k = ids.numel()
+    h, i = bank_rows.hidden, bank_rows.intermediate
+    partial = torch.empty(h, dtype=torch.float32, device=dev)
+    if workspace is None:
+        workspace = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(k, h, i),
+                                dtype=torch.uint8, device=dev)
+    rb = bank_rows.c()
+    sb = shared_rows.c() if shared_rows is not None else None
+    N.call("iq36_moe_decode", x.data_ptr(), None, None, 0.0, ids.data_ptr(), weights.data_ptr(),
+           k, ctypes.byref(rb), ctypes.byref(sb) if sb is not None else None,
+           _ptr(shared_logit) if shared_rows is not None else None, partial.data_ptr(),
+           _dtype_code(torch.float32), 0, workspace.data_ptr(), workspace.numel(), _stream(dev))
+    dist.all_reduce(partial, group=group)
+    return partial
 
 
 def ep_moe_decode(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,

@@ -765,11 +765,39 @@ def run_moe_decode(args, world, rank, local) -> None:
     rb, sb = bank.c(), shared.c()
     stream = torch.cuda.current_stream(dev)
 
-    def call(i):
-        N.call("iq36_moe_block_decode", xs[i % 64].data_ptr(), w_router.data_ptr(),
-               w_sg.data_ptr(), k, ctypes.byref(rb), ctypes.byref(sb), ids.data_ptr(),
-               wts.data_ptr(), logits.data_ptr(), out.data_ptr(), 1, ws.data_ptr(), ws.numel(),
-               stream.cuda_stream)
+    sharded = world > 1 and (args.ep or args.tp)
+    if sharded:
+        # one block split over the ranks: router replicated, experts sharded
+        # (--ep: E/P experts per rank; --tp: I/P intermediate rows of every
+        # expert), one NCCL all-reduce of the [H] fp32 partial sums
+        from engine import parallel_tp as PT
+        if args.ep:
+            local, e0 = PT.shard_expert_bank(bank, rank, world)
+            sh_local = shared if rank == 0 else None
+        else:
+            local = PT.shard_expert_bank_rows(bank, rank, world)
+            sh_local = PT.shard_expert_bank_rows(shared, rank, world)
+        slog = torch.empty(1, dtype=torch.float32, device=dev)
+        ws_l = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(k, H, local.intermediate),
+                           dtype=torch.uint8, device=dev)
+
+        def call(i):
+            x = xs[i % 64]
+            N.call("iq36_router_logits", x.data_ptr(), None, None, 0.0, 1, H, w_router.data_ptr(),
+                   E, w_sg.data_ptr(), logits.data_ptr(), slog.data_ptr(), stream.cuda_stream)
+            N.call("iq36_router_select", logits.data_ptr(), 1, E, k, ids.data_ptr(),
+                   wts.data_ptr(), stream.cuda_stream)
+            if args.ep:
+                part = PT.ep_moe_decode(x, ids, wts, local, e0, sh_local, slog, workspace=ws_l)
+            else:
+                part = PT.tp_moe_decode(x, ids, wts, local, sh_local, slog, workspace=ws_l)
+            out.copy_(part)
+    else:
+        def call(i):
+            N.call("iq36_moe_block_decode", xs[i % 64].data_ptr(), w_router.data_ptr(),
+                   w_sg.data_ptr(), k, ctypes.byref(rb), ctypes.byref(sb), ids.data_ptr(),
+                   wts.data_ptr(), logits.data_ptr(), out.data_ptr(), 1, ws.data_ptr(),
+                   ws.numel(), stream.cuda_stream)
 
     for i in range(args.warmup):
         call(i)
@@ -800,17 +828,20 @@ def run_moe_decode(args, world, rank, local) -> None:
     e.record()
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world)
+    agg = 1 if sharded else world
     line = {
         "metric": "MoE decode block HBM GB/s (BASELINE config 1)",
-        "value": round(world * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "value": round(agg * gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(per_call * 1e3, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4xf16",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None, "dtype": "u4xf16", "data": "synthetic",
         "config": {"workload": "config1 MoE decode block: router 2048->256 + top-8 + 8 routed "
                                "and 1 shared u4 g128 experts (I=512) + shared gate, fp16 out",
                    "bytes_per_step": step_bytes, "l2": "flushed before every step",
-                   "parallelism": "replicas" if world > 1 else "single GPU"},
-        "e2e": {"value": round(world * step_bytes / t_e2e / 1e9, 1), "unit": "GB/s",
+                   "parallelism": (f"ep{world} (experts sharded, NCCL all-reduce)" if args.ep
+                                   else f"tp{world} (expert rows sharded, NCCL all-reduce)")
+                   if sharded else ("replicas" if world > 1 else "single GPU")},
+        "e2e": {"value": round(agg * step_bytes / t_e2e / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
         "gpu_launches": 4 * args.steps,
         "roofline": {"bound": "hbm", "kernel": "iq36_moe_block_decode (router, select, gate_up, "
@@ -1062,7 +1093,10 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=4096,
                     help="T for --workload moe_prefill / attn_prefill / delta_prefill")
     ap.add_argument("--ep", action="store_true",
-                    help="--workload moe_prefill at --gpus > 1: expert parallel instead of replicas")
+                    help="--workload moe_prefill / moe_decode at --gpus > 1: expert parallel "
+                         "instead of replicas")
+    ap.add_argument("--tp", action="store_true",
+                    help="--workload moe_decode at --gpus > 1: every expert's rows sharded")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)

@@ -178,3 +178,31 @@ def _ep_decode_gpu_body(rank, world):
     torch.cuda.synchronize(dev)
     err = float(((out - ref).abs().max() / ref.abs().max()).item())
     assert err < 1e-5, err
+
+
+def tp_decode_gpu(rank, world, port, q):
+    _init(rank, world, port, "nccl")
+    _finish(q, rank, _tp_decode_gpu_body, rank, world)
+
+
+def _tp_decode_gpu_body(rank, world):
+    import numpy as np
+    import torch
+    from engine.ops import moe_expert_ffn
+    from engine.parallel_tp import shard_expert_bank_rows, tp_moe_decode
+    from helpers import bank_to_torch, make_bank
+
+    dev = torch.device(f"cuda:{rank}")
+    rng = np.random.default_rng(12)
+    bank = bank_to_torch(make_bank(rng, 64, 2048, 512), dev)
+    shared = bank_to_torch(make_bank(rng, 1, 2048, 512), dev)
+    x = torch.from_numpy(rng.standard_normal(2048).astype(np.float16)).to(dev)
+    ids = torch.tensor([3, 60, 17, 33, 8, 41, 25, 50], dtype=torch.int32, device=dev)
+    w = torch.tensor([0.3, 0.2, 0.15, 0.1, 0.1, 0.06, 0.05, 0.04], device=dev)
+    sl = torch.tensor([0.3], device=dev)
+    out = tp_moe_decode(x, ids, w, shard_expert_bank_rows(bank, rank, world),
+                        shard_expert_bank_rows(shared, rank, world), sl)
+    ref = moe_expert_ffn(x, ids, w, bank, shared, sl, out_dtype=torch.float32)
+    torch.cuda.synchronize(dev)
+    err = float(((out - ref).abs().max() / ref.abs().max()).item())
+    assert err < 1e-5, err

@@ -63,3 +63,9 @@ def test_ep_prefill_nccl_matches_single_gpu():
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
 def test_ep_decode_nccl_matches_single_gpu():
     _run(W.ep_decode_gpu, 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_tp_decode_nccl_matches_single_gpu():
+    _run(W.tp_decode_gpu, 2)
