@@ -285,7 +285,10 @@ __device__ __forceinline__ U4Rows gate_up_rows(const ExpertArgs& a, const int32_
                 s + (size_t)rowB * ng, z, zbase + (int64_t)rowA * ng, zbase + (int64_t)rowB * ng};
 }
 
-template <int G>
+// ONE: every warp's group range fits one 4-group chunk, loaded at once (one
+// memory round trip); otherwise 2-group chunks, software-pipelined. Both
+// accumulate the groups in the same order.
+template <int G, bool ONE>
 __global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const int32_t* ids,
                                                           const __half* x16, const float* x32,
                                                           const float* nw, float eps,
@@ -304,22 +307,28 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const in
   const int j0 = (rb - slot * rb_per_exp) * 8;
   float accA = 0.f, accB = 0.f;
   U4Rows rows{};
-  U4Chunk<G, 2> first;
+  constexpr int U = ONE ? 4 : 2;
+  U4Chunk<G, U> first;
   // The shared expert's weights are known up front: stream them before the
   // wait. Routed experts depend on the router output of the previous kernel.
   if (valid && slot >= a.k) {
     rows = gate_up_rows<G>(a, ids, slot, j0, g);
-    u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
+    u4_load_chunk<G, U>(first, rows, ks * per, (ks + 1) * per, t);
   }
   pdl_wait();
   const bool work = valid && (slot >= a.k || owned_expert(a, ids, slot) >= 0);
   if (work && slot < a.k) {
     rows = gate_up_rows<G>(a, ids, slot, j0, g);
-    u4_load_chunk<G, 2>(first, rows, ks * per, (ks + 1) * per, t);
+    u4_load_chunk<G, U>(first, rows, ks * per, (ks + 1) * per, t);
   }
   stage_x_perm(xs, x16, x32, nw, eps, a.H, nred);
   pdl_launch_dependents();
-  if (work) u4_dot2_pipelined<G, 2>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
+  if (work) {
+    if constexpr (ONE)
+      u4_compute_chunk<G, U>(first, xs, ks * per, (ks + 1) * per, t, accA, accB);
+    else
+      u4_dot2_pipelined<G, U>(first, rows, xs, ks * per, (ks + 1) * per, t, accA, accB);
+  }
   if (KS > 1) {
     if (t == 0) {
       red[warp][g] = accA;
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(ExpertArgs a, const in
   }
 }
 
-template <int G>
+template <int G, bool ONE>
 __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* wts,
                                 const float* slogit, const __half* act, void* out, int out_dtype,
                                 int accumulate) {
@@ -376,14 +385,19 @@ __global__ void moe_down_kernel(ExpertArgs a, const int32_t* ids, const float* w
   const U4Rows rows{w + (size_t)rowA * (I / 2), w + (size_t)rowB * (I / 2),
                     s + (size_t)rowA * ngi, s + (size_t)rowB * ngi, z,
                     zbase + (int64_t)rowA * ngi, zbase + (int64_t)rowB * ngi};
-  U4Chunk<G, 2> first;
-  if (owned >= 0) u4_load_chunk<G, 2>(first, rows, 0, ngi, t);
+  constexpr int U = ONE ? 4 : 2;
+  U4Chunk<G, U> first;
+  if (owned >= 0) u4_load_chunk<G, U>(first, rows, 0, ngi, t);
   pdl_wait();
   stage_x_perm(xs, act, nullptr, nullptr, 0.f, a.n_slots * I, nred);
   pdl_launch_dependents();
   float accA = 0.f, accB = 0.f;
-  if (owned >= 0)
-    u4_dot2_pipelined<G, 2>(first, rows, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+  if (owned >= 0) {
+    if constexpr (ONE)
+      u4_compute_chunk<G, U>(first, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+    else
+      u4_dot2_pipelined<G, U>(first, rows, xs + (size_t)slot * (I / 8), 0, ngi, t, accA, accB);
+  }
   if (t == 0) {
     red[slot][g] = accA;
     red[slot][g + 8] = accB;
@@ -486,22 +500,32 @@ int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, fl
   const size_t smem1 = (size_t)a.H / 8 * sizeof(uint4);
   const __half* xh = reinterpret_cast<const __half*>(x_f16);
   cudaError_t e;
+  const bool one1 = (ng >> ks_log2) <= 4;
   if (G == 128)
-    e = launch(moe_gate_up_kernel<128>, grid1, dim3(256), smem1, stream, a, ids, xh, x_f32, nw,
-               eps, act, ks_log2);
+    e = one1 ? launch(moe_gate_up_kernel<128, true>, grid1, dim3(256), smem1, stream, a, ids, xh,
+                      x_f32, nw, eps, act, ks_log2)
+             : launch(moe_gate_up_kernel<128, false>, grid1, dim3(256), smem1, stream, a, ids, xh,
+                      x_f32, nw, eps, act, ks_log2);
   else
-    e = launch(moe_gate_up_kernel<64>, grid1, dim3(256), smem1, stream, a, ids, xh, x_f32, nw, eps,
-               act, ks_log2);
+    e = one1 ? launch(moe_gate_up_kernel<64, true>, grid1, dim3(256), smem1, stream, a, ids, xh,
+                      x_f32, nw, eps, act, ks_log2)
+             : launch(moe_gate_up_kernel<64, false>, grid1, dim3(256), smem1, stream, a, ids, xh,
+                      x_f32, nw, eps, act, ks_log2);
   if (e != cudaSuccess) return IQ36_ERR_CUDA;
   const dim3 grid2(ceil_div(a.H, 16));
   const size_t smem2 = (size_t)a.n_slots * a.I / 8 * sizeof(uint4);
   const __half* acth = act;
+  const bool one2 = a.I / G <= 4;
   if (G == 128)
-    e = launch(moe_down_kernel<128>, grid2, dim3(32 * a.n_slots), smem2, stream, a, ids, weights,
-               shared_logit, acth, out, out_dtype, accumulate);
+    e = one2 ? launch(moe_down_kernel<128, true>, grid2, dim3(32 * a.n_slots), smem2, stream, a,
+                      ids, weights, shared_logit, acth, out, out_dtype, accumulate)
+             : launch(moe_down_kernel<128, false>, grid2, dim3(32 * a.n_slots), smem2, stream, a,
+                      ids, weights, shared_logit, acth, out, out_dtype, accumulate);
   else
-    e = launch(moe_down_kernel<64>, grid2, dim3(32 * a.n_slots), smem2, stream, a, ids, weights,
-               shared_logit, acth, out, out_dtype, accumulate);
+    e = one2 ? launch(moe_down_kernel<64, true>, grid2, dim3(32 * a.n_slots), smem2, stream, a,
+                      ids, weights, shared_logit, acth, out, out_dtype, accumulate)
+             : launch(moe_down_kernel<64, false>, grid2, dim3(32 * a.n_slots), smem2, stream, a,
+                      ids, weights, shared_logit, acth, out, out_dtype, accumulate);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
