@@ -12,6 +12,9 @@
 // sums go to shared memory and are summed in fixed warp order every
 // kRedChunks chunks (double-buffered, one named barrier per batch).
 
+#include <algorithm>
+#include <atomic>
+
 #include "launch.cuh"
 #include "u4_stream.cuh"
 
@@ -270,11 +273,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 // ---------------------------------------------------------------------------
 // Host launchers
 
-static int stream_attr(const void* fn, int bytes) {
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
-                 cudaSuccess
-             ? IQ36_OK
-             : IQ36_ERR_CUDA;
+// The dynamic shared-memory opt-in is a per-device function attribute: set it
+// once per device to the largest layout any K (<= 4096) needs.
+static int stream_attr(const void* fn) {
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
+  if (attr_set[dev].load(std::memory_order_acquire)) return IQ36_OK;
+  int bytes = 0;
+  for (int K = 512; K <= 4096; K += 512)
+    bytes = std::max(bytes, stream_smem(stream_geom(K, 128), K, 128).total);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  attr_set[dev].store(true, std::memory_order_release);
+  return IQ36_OK;
 }
 
 bool stream_proj_ok(int K, int G, int n_proj, const iq36_u4_projection* proj) {
@@ -307,7 +319,7 @@ int stream_proj_launch(const void* x_f16, const float* x_f32, const float* nw, f
   const StreamGeom geo = stream_geom(K, G);
   const StreamSmem L = stream_smem(geo, K, G);
   const int grid = std::min(kStreamCtas, ch);
-  if (stream_attr((const void*)u4_stream_proj_kernel<128>, L.total) != IQ36_OK)
+  if (stream_attr((const void*)u4_stream_proj_kernel<128>) != IQ36_OK)
     return IQ36_ERR_CUDA;
   const cudaError_t e =
       launch(u4_stream_proj_kernel<128>, dim3(grid), dim3(kStreamThreads), (size_t)L.total, stream,
