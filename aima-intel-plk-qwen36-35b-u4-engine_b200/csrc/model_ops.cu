@@ -48,8 +48,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* in, int dim,
 // key heads); lane owns dims [8*lane, 8*lane+8) of a 256-dim head.
 // Split q/gate (gguf_loader.cpp:5928-5950), per-head RMSNorm, rotate-half RoPE
 // on the first rope_dim dims (iq36_qk_rope_layout.cl:37-60) with angles
-// evaluated in fp64, fp16 store; K/V appended at *pos_dev through the block
-// table (iq36_hot_ring_update.cl:7-28). Block x handles token x of a batch
+// evaluated in fp64 once per token (shared memory), fp16 store; K/V appended
+// at *pos_dev through the block table (iq36_hot_ring_update.cl:7-28). Block x handles token x of a batch
 // (position *pos_dev + x; rows of q_full, k, v, q_out, gate_out per token);
 // the decode step launches one block.
 __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __half* v,
@@ -57,11 +57,23 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
                                  const int32_t* pos_dev, int n_q, int n_kv, int rope_dim,
                                  float rope_base, const int32_t* bt, int bs, __half* kc,
                                  __half* vc, __half* q_out, __half* gate_out) {
+  __shared__ float rope_c[128], rope_s[128];
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp >= n_q + n_kv) return;
   const int D = 256;
   const int pos = *pos_dev + blockIdx.x;
+  const int half = rope_dim / 2;
+  // Frequency i's angle is computed once per token, in fp64, by thread
+  // i mod blockDim; element d takes frequency d % half.
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const double inv = pow((double)rope_base, -2.0 * (double)i / (double)rope_dim);
+    double sn, cs;
+    sincos((double)pos * inv, &sn, &cs);
+    rope_c[i] = (float)cs;
+    rope_s[i] = (float)sn;
+  }
+  __syncthreads();
+  if (warp >= n_q + n_kv) return;
   q_full += (size_t)blockIdx.x * 2 * n_q * D;
   k += (size_t)blockIdx.x * n_kv * D;
   v += (size_t)blockIdx.x * n_kv * D;
@@ -85,45 +97,17 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
   const float sc = rsqrtf(ss / (float)D + eps);
 #pragma unroll
   for (int j = 0; j < 8; ++j) x[j] = x[j] * sc * nw[8 * lane + j];
-  const int half = rope_dim / 2;
   const int xo = half / 8;  // partner lane offset
-  // Frequency i's angle is computed in fp64 by lane i % 32 (register i / 32):
-  // at most four pow + sincos per lane, all lanes at once; element d takes
-  // frequency d % half.
-  const int nr = (half + 31) / 32;  // <= 4 (rope_dim <= 256)
-  float cr[4], sr[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    cr[r] = 1.f;
-    sr[r] = 0.f;
-    const int i = lane + 32 * r;
-    if (r < nr && i < half) {
-      const double inv = pow((double)rope_base, -2.0 * (double)i / (double)rope_dim);
-      double sn, cs;
-      sincos((double)pos * inv, &sn, &cs);
-      cr[r] = (float)cs;
-      sr[r] = (float)sn;
-    }
-  }
   float y[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float partner = __shfl_xor_sync(0xffffffffu, x[j], xo);
-    const int d = 8 * lane + j, i = d % half;
-    float c = 1.f, sn = 0.f;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      if (r < nr) {  // warp-uniform
-        const float cc = __shfl_sync(0xffffffffu, cr[r], i & 31);
-        const float ss = __shfl_sync(0xffffffffu, sr[r], i & 31);
-        if ((i >> 5) == r) {
-          c = cc;
-          sn = ss;
-        }
-      }
-    }
+    const int d = 8 * lane + j;
     y[j] = x[j];
-    if (d < rope_dim) y[j] = d < half ? x[j] * c - partner * sn : x[j] * c + partner * sn;
+    if (d < rope_dim) {
+      const float c = rope_c[d % half], sn = rope_s[d % half];
+      y[j] = d < half ? x[j] * c - partner * sn : x[j] * c + partner * sn;
+    }
   }
   uint4 packed;
   __half* ph = reinterpret_cast<__half*>(&packed);
