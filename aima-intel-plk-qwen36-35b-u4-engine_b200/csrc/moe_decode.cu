@@ -216,6 +216,9 @@ __device__ __forceinline__ void router_topk_warp(const float* l, int E, int k, u
 // Warp per token. E <= 256, k <= 16.
 __global__ void __launch_bounds__(256) router_select_kernel(const float* logits, int T, int E,
                                                             int k, int32_t* ids, float* weights) {
+  // the expert kernel that follows may launch now: before its wait it only
+  // prefetches the shared expert's weights
+  pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
