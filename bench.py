@@ -49,6 +49,7 @@ for p in (str(ROOT), str(PKG)):
 
 BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
+DECODE_GEMV_TRAFFIC = 11551662  # B per launch, ncu dram__bytes_read+write over one step's 81
 PUBLISHED_DECODE_4K = 50.57  # reference's published figure: Arc B390, 4k prompt, batch-1 decode tok/s
 PUBLISHED_PREFILL = {4096: 2367.89, 32768: 2065.28}  # reference prefill tok/s, Arc B390
 
@@ -341,7 +342,11 @@ def run_ours(args, world, rank, local) -> None:
                      "kernel": "u4 multi-output GEMV (u4_stream_proj_kernel; ragged shapes "
                                "u4_gemv_multi_kernel), all launches of one step",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "frac": round(achieved / hbm, 4),
+                     # DRAM bytes per launch of these 81 launches from one ncu capture
+                     # (profiles/decode_gemv_traffic_ctx256.md): equal to the algorithmic
+                     # bytes, no re-reads
+                     "traffic": DECODE_GEMV_TRAFFIC if cfg.layers == 40 else None,
                      "peak_source": src,
                      "bytes_per_launch": gemv_bytes // gemv_launches,
                      "launches": gemv_launches},
