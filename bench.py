@@ -49,6 +49,7 @@ for p in (str(ROOT), str(PKG)):
 
 BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
+PREFILL_CHUNK = 16384  # tokens per batched-prefill launch sequence (Qwen36Runtime default)
 DECODE_GEMV_TRAFFIC = 11551662  # B per launch, ncu dram__bytes_read+write over one step's 81
 PUBLISHED_DECODE_4K = 50.57  # reference's published figure: Arc B390, 4k prompt, batch-1 decode tok/s
 PUBLISHED_PREFILL = {4096: 2367.89, 32768: 2065.28}  # reference prefill tok/s, Arc B390
@@ -236,12 +237,12 @@ def run_ours(args, world, rank, local) -> None:
     prompt = torch.randint(0, cfg.vocab, (args.ctx,), generator=gen, dtype=torch.int32)
 
     # batched prefill of the prompt (one untimed pass sizes the buffers)
-    rt.prefill_batched(prompt)
+    rt.prefill_batched(prompt, chunk=PREFILL_CHUNK)
     rt.reset()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    rt.prefill_batched(prompt)
+    rt.prefill_batched(prompt, chunk=PREFILL_CHUNK)
     e1.record()
     torch.cuda.synchronize(dev)
     prefill_s = e0.elapsed_time(e1) / 1e3
@@ -378,13 +379,13 @@ def run_prefill(args, world, rank, local) -> None:
     launches = 0
     for _ in range(args.warmup):
         rt.reset()
-        launches = rt.prefill_batched(dprompt)
+        launches = rt.prefill_batched(dprompt, chunk=PREFILL_CHUNK)
     torch.cuda.synchronize(dev)
     if args.profile_step:
         rt.reset()
         torch.cuda.synchronize(dev)
         torch.cuda.profiler.start()
-        rt.prefill_batched(dprompt)
+        rt.prefill_batched(dprompt, chunk=PREFILL_CHUNK)
         torch.cuda.synchronize(dev)
         torch.cuda.profiler.stop()
         if rank == 0:
@@ -399,7 +400,7 @@ def run_prefill(args, world, rank, local) -> None:
         rt.reset()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        rt.prefill_batched(dprompt)
+        rt.prefill_batched(dprompt, chunk=PREFILL_CHUNK)
         e.record()
         e.synchronize()
         total += s.elapsed_time(e) / 1e3
@@ -414,15 +415,15 @@ def run_prefill(args, world, rank, local) -> None:
         torch.cuda.synchronize(dev)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        rt.prefill_batched(prompt)
+        rt.prefill_batched(prompt, chunk=PREFILL_CHUNK)
         pin_out.copy_(rt.token, non_blocking=True)
         e.record()
         e.synchronize()
         t_e2e += s.elapsed_time(e) / 1e3
     t_e2e = max_over_ranks(t_e2e / args.steps, world)
-    # dominant kernel group: the MoE block of one layer over the whole prompt
+    # dominant kernel group: the MoE block of one layer over one prefill chunk
     # (router + grouped routed experts + shared expert), timed alone
-    T = min(args.ctx, 8192)
+    T = min(args.ctx, PREFILL_CHUNK)
     h = torch.randn(T, cfg.hidden, device=dev, generator=torch.Generator(dev).manual_seed(3))
     L = rt.w.layers[0]
     from engine import ops
@@ -458,7 +459,7 @@ def run_prefill(args, world, rank, local) -> None:
                                "(Qwen3.6-35B-A3B-shaped, random-init u4 g128), batched",
                    "ctx": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (17.6 GB of weights per pass)",
-                   "chunk_tokens": 8192},
+                   "chunk_tokens": PREFILL_CHUNK},
         "e2e": {"value": round(world * args.ctx / t_e2e, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": args.ctx * 4, "d2h_bytes_per_step": 4},
         "gpu_launches": launches * args.steps,
