@@ -55,7 +55,7 @@ def _ep_prefill_cpu_body(rank, world):
     from helpers import make_bank
     from oracle import oracle
 
-    H, I, E, k, T = 256, 128, 8, 4, 24
+    H, I, E, k, T = 256, 128, 4 * world, 4, 24
     bank = make_bank(np.random.default_rng(7), E, H, I)      # same on every rank
     rng = np.random.default_rng(100 + rank)                  # rank's own tokens
     x = rng.standard_normal((T, H)).astype(np.float32)

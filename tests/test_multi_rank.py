@@ -40,8 +40,9 @@ def _run(fn, world: int, timeout: float = 240.0):
     assert not bad, "\n".join(f"rank {r}:\n{s}" for r, s in bad.items())
 
 
-def test_ep_prefill_exchange_gloo():
-    _run(W.ep_prefill_cpu, 2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_prefill_exchange_gloo(world):
+    _run(W.ep_prefill_cpu, world)
 
 
 def test_tp_gemv_sharding_gloo():
