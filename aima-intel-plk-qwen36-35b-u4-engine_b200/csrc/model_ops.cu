@@ -58,6 +58,9 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
                                  float rope_base, const int32_t* bt, int bs, __half* kc,
                                  __half* vc, __half* q_out, __half* gate_out) {
   __shared__ float rope_c[128], rope_s[128];
+  // the attention split kernel may launch now: before its wait it only
+  // prefetches cache pages that precede the token appended here
+  pdl_launch_dependents();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = 256;

@@ -74,7 +74,6 @@ __device__ __forceinline__ void gqa_issue_page(const GqaArgs& a, int kvh, int pa
 
 __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int kvh = blockIdx.y;
   const int split = blockIdx.x * 4 + warp;
@@ -84,6 +83,15 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaArgs a) {
   const int p_begin = min(split * pps, n_pages);
   const int p_end = min(p_begin + pps, n_pages);
   const size_t meta = ((size_t)kvh * a.S + split) * kGrp;
+  const uint32_t wbase = smem_u32(smem) + warp * kWarpSmem;
+  // pages wholly before the newest token do not depend on the previous kernel
+  bool pre[kStages - 1];
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    pre[s] = p_begin + s < p_end && (p_begin + s + 1) * kBS <= ctx - 1;
+    if (pre[s]) gqa_issue_page(a, kvh, p_begin + s, ctx, wbase + s * kStageBytes, lane);
+  }
+  pdl_wait();
 
   // Q^T as the B operand: b0 = q[head g][16kk + 2t..], b1 = q[head g][16kk+8+2t..].
   uint32_t qb[16][2];
@@ -100,10 +108,10 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaArgs a) {
   for (int mt = 0; mt < 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-  const uint32_t wbase = smem_u32(smem) + warp * kWarpSmem;
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
-    if (p_begin + s < p_end) gqa_issue_page(a, kvh, p_begin + s, ctx, wbase + s * kStageBytes, lane);
+    if (!pre[s] && p_begin + s < p_end)
+      gqa_issue_page(a, kvh, p_begin + s, ctx, wbase + s * kStageBytes, lane);
     cp_async_commit();
   }
   pdl_launch_dependents();
