@@ -139,12 +139,16 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const __half* qkv, int 
                                                          const float* a_log, const float* dtb,
                                                          int nv, __half* act, float* g_out,
                                                          float* beta_out) {
-  pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  // the conv state and weights do not depend on the projection: load them first
+  float4 st = make_float4(0.f, 0.f, 0.f, 0.f), w = st;
+  if (c < C) {
+    st = reinterpret_cast<const float4*>(conv_state)[c];
+    w = reinterpret_cast<const float4*>(conv_w)[c];
+  }
+  pdl_wait();
   if (c < C) {
     const float xv = __half2float(qkv[c]);
-    const float4 st = reinterpret_cast<const float4*>(conv_state)[c];
-    const float4 w = reinterpret_cast<const float4*>(conv_w)[c];
     float s = w.x * st.y;
     s = fmaf(w.y, st.z, s);
     s = fmaf(w.z, st.w, s);
