@@ -61,13 +61,14 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
   // the attention split kernel may launch now: before its wait it only
   // prefetches cache pages that precede the token appended here
   pdl_launch_dependents();
-  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = 256;
+  // The positions are written before the step (never by the projection this
+  // kernel waits on), so the angles are computed before the wait. Frequency
+  // i's angle is computed once per token, in fp64, by thread i mod blockDim;
+  // element d takes frequency d % half.
   const int pos = *pos_dev + blockIdx.x;
   const int half = rope_dim / 2;
-  // Frequency i's angle is computed once per token, in fp64, by thread
-  // i mod blockDim; element d takes frequency d % half.
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const double inv = pow((double)rope_base, -2.0 * (double)i / (double)rope_dim);
     double sn, cs;
@@ -75,6 +76,7 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
     rope_c[i] = (float)cs;
     rope_s[i] = (float)sn;
   }
+  pdl_wait();
   __syncthreads();
   if (warp >= n_q + n_kv) return;
   q_full += (size_t)blockIdx.x * 2 * n_q * D;
