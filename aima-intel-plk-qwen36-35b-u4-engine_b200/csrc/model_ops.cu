@@ -149,6 +149,9 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const __half* qkv, int 
     w = reinterpret_cast<const float4*>(conv_w)[c];
   }
   pdl_wait();
+  // the recurrence kernel may launch now (the projection has completed): it
+  // loads its state slice before its own wait while this kernel runs
+  pdl_launch_dependents();
   if (c < C) {
     const float xv = __half2float(qkv[c]);
     float s = w.x * st.y;
@@ -224,19 +227,10 @@ __global__ void __cluster_dims__(1, 8, 1) __launch_bounds__(128)
   __shared__ float qk_red[2][4];
   __shared__ float part;
   cg::cluster_group cluster = cg::this_cluster();
-  pdl_wait();
   const int vh = blockIdx.x, j0 = blockIdx.y * NC;
   const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
   const int kh = vh / (nv / nk);
-  float q = __half2float(act[(size_t)kh * D + i]);
-  float kk = __half2float(act[(size_t)(nk + kh) * D + i]);
-  {
-    const float qs = warp_sum(q * q), ks = warp_sum(kk * kk);
-    if (lane == 0) {
-      qk_red[0][warp] = qs;
-      qk_red[1][warp] = ks;
-    }
-  }
+  // the state slice is written only by this kernel's previous token
   float s[NC];
   float* srow = state + ((size_t)vh * D + i) * D + j0;
 #pragma unroll
@@ -246,6 +240,16 @@ __global__ void __cluster_dims__(1, 8, 1) __launch_bounds__(128)
     s[j + 1] = v4.y;
     s[j + 2] = v4.z;
     s[j + 3] = v4.w;
+  }
+  pdl_wait();
+  float q = __half2float(act[(size_t)kh * D + i]);
+  float kk = __half2float(act[(size_t)(nk + kh) * D + i]);
+  {
+    const float qs = warp_sum(q * q), ks = warp_sum(kk * kk);
+    if (lane == 0) {
+      qk_red[0][warp] = qs;
+      qk_red[1][warp] = ks;
+    }
   }
   __syncthreads();
   const float qs = qk_red[0][0] + qk_red[0][1] + qk_red[0][2] + qk_red[0][3];
