@@ -9,7 +9,14 @@
  *   - the return value is 0 (IQ36_OK) or a negative iq36_status; shape and
  *     pointer checks happen on the host before any launch, so a failed call has
  *     enqueued nothing;
- *   - fp16 tensors are IEEE binary16 passed as uint16_t / void*.
+ *   - fp16 tensors are IEEE binary16 passed as uint16_t / void*;
+ *   - kernels are launched with programmatic dependent launch: each reads the
+ *     outputs of the previous launch on the stream only after waiting for it,
+ *     but reads data that launch does not produce (weights; the positions,
+ *     recurrent / conv state and earlier cache pages of the decode entries)
+ *     before that wait. Such inputs must therefore not be written by the
+ *     immediately preceding launch on the stream (a decode step writes them
+ *     once per step, at its end or many launches earlier).
  *
  * u4 matrix layout (the OpenVINO compressed-constant layout before the
  * reference's group-major repack; reference
