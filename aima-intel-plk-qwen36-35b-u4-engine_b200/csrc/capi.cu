@@ -32,14 +32,16 @@ extern "C" void iq36_set_pdl(int enabled) { iq36::g_pdl.store(enabled ? 1 : 0); 
 namespace iq36 {
 int attn_wait_timeouts(int* count, int reset);
 int gemm_wait_timeouts(int* count, int reset);
+int moe_wait_timeouts(int* count, int reset);
 }
 
 extern "C" int iq36_wait_timeouts(int32_t* count, int32_t reset) {
   if (count == nullptr) return IQ36_ERR_ARG;
-  int c = 0, a = 0, g = 0;
+  int c = 0, a = 0, g = 0, m = 0;
   int st = iq36::stream_wait_timeouts(&c, reset);
   if (st == IQ36_OK) st = iq36::attn_wait_timeouts(&a, reset);
   if (st == IQ36_OK) st = iq36::gemm_wait_timeouts(&g, reset);
-  *count = c + a + g;
+  if (st == IQ36_OK) st = iq36::moe_wait_timeouts(&m, reset);
+  *count = c + a + g + m;
   return st;
 }

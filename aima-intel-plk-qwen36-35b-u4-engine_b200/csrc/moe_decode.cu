@@ -24,6 +24,7 @@
 #include <atomic>
 
 #include "launch.cuh"
+#include "sync_sm100.cuh"
 #include "u4_core.cuh"
 
 namespace iq36 {
@@ -443,8 +444,10 @@ size_t moe_decode_ws(int k, int hidden, int intermediate) {
   return (((size_t)(k + 1) * intermediate * 2) + 255) / 256 * 256;
 }
 
+// Layer workspace: the SwiGLU activations [k+1, I] fp16, then 256 bytes of
+// grid-barrier words for the one-launch form (zero before first use).
 size_t moe_layer_ws(int k, int hidden, int intermediate) {
-  return moe_decode_ws(k, hidden, intermediate);
+  return moe_decode_ws(k, hidden, intermediate) + 256;
 }
 
 int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, float eps,
@@ -530,6 +533,433 @@ int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, fl
              : launch(moe_down_kernel<64, false>, grid2, dim3(32 * a.n_slots), smem2, stream, a,
                       ids, weights, shared_logit, acth, out, out_dtype, accumulate);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// The decode MoE FFN layer as ONE persistent launch (iq36_moe_layer_decode).
+//
+// One CTA of 16 warps per SM runs the layer's four dependent steps as three
+// phases separated by two grid barriers:
+//   A  x = f16(RMSNorm(residual)); the router logits, one warp per row, rows
+//      spread over the CTAs; the shared expert's gate_up + SwiGLU, whose
+//      weights (and its down rows) were fetched before griddepcontrol.wait;
+//   -- barrier 1: every logit written --
+//   B  every CTA selects the top-k from the logits itself (no broadcast step),
+//      starts the bulk copies of its 16 down-projection rows of the k selected
+//      experts into shared memory, then runs its gate_up units of those
+//      experts (unit = 8 gate rows + the matching 8 up rows, K split over the
+//      4 warps of a quad);
+//   -- barrier 2: every SwiGLU activation written --
+//   C  CTAs with a down row block: the k+1 slots' dot products from the copies
+//      already in shared memory, rank-order combine, residual update.
+// CTAs without a row block arrive at barrier 2 and exit, so the next kernel
+// (released once every CTA is past barrier 2) starts streaming its weights on
+// their SMs while phase C runs.
+//
+// Reduction orders, dot engine and rounding points are those of the
+// four-launch form (router_logits_kernel, router_topk_warp,
+// moe_gate_up_kernel<128, true> with a 4-way K split, moe_down_kernel<128,
+// true>), so both forms produce the same bits.
+//
+// Grid barrier: {count, generation} words in the caller's workspace (zeroed
+// before first use). A CTA reads the generation, then adds itself to the
+// count; the last arrival resets the count and publishes generation + 1, so
+// the words are back in their resting state after every barrier and across
+// launches. Waits are bounded (kWaitLimitNs): on expiry the CTA counts a
+// timeout (iq36_wait_timeouts) and skips the rest of its work.
+
+constexpr int kLayerThreads = 512;  // 16 warps = 4 gate_up quads
+constexpr int kLayerQuads = kLayerThreads / 128;
+
+__device__ int g_moe_wait_timeouts;
+
+struct LayerArgs {
+  ExpertArgs e;
+  float* residual;
+  const float* nw;
+  float eps;
+  const __half* w_router;
+  const __half* w_sg;  // shared-expert gate row (nullptr without a shared expert)
+  int E;
+  float* logits;
+  float* slogit;
+  int32_t* ids_out;
+  float* wts_out;
+  __half* act;     // [n_slots, I] SwiGLU activations (workspace)
+  unsigned* bar;   // grid barrier words (workspace)
+};
+
+struct LayerSmem {
+  int xplain, xperm, act, logit, stage, slot_bytes, total;
+};
+
+__host__ __device__ inline LayerSmem layer_smem(int H, int I, int n_slots) {
+  LayerSmem s;
+  const int ngi = I / 128;
+  s.xplain = 0;
+  s.xperm = s.xplain + H * 2;
+  s.act = s.xperm + H * 2;
+  s.logit = s.act + n_slots * I * 2;
+  s.stage = (s.logit + 256 * 4 + 127) / 128 * 128;
+  s.slot_bytes = 8 * I + 40 * ngi;  // 16 rows: codes, scales, zero points
+  s.total = s.stage + n_slots * s.slot_bytes;
+  return s;
+}
+
+__device__ __forceinline__ unsigned layer_bar_arrive(unsigned* bar, unsigned nb) {
+  unsigned g0;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g0) : "l"(bar + 1) : "memory");
+  __threadfence();  // this CTA's writes (ordered before by bar.sync) before the arrival
+  if (atomicAdd(bar, 1u) == nb - 1) {
+    atomicExch(bar, 0u);
+    __threadfence();
+    asm volatile("st.release.gpu.global.u32 [%0], %1;\n" ::"l"(bar + 1), "r"(g0 + 1u) : "memory");
+  }
+  return g0;
+}
+
+__device__ __forceinline__ bool layer_bar_wait(const unsigned* bar, unsigned g0) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    unsigned g;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(bar + 1) : "memory");
+    if (g != g0) return true;
+    if (i == 0) t0 = globaltimer_ns();
+    else if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return false;
+}
+
+// Eight fp16 values into the permuted operand order of u4_core.cuh (odd
+// positions pre-divided by 16), as stage_x_perm writes them.
+__device__ __forceinline__ uint4 perm8(const __half h[8]) {
+  const __half2 sixteenth = __float2half2_rn(0.0625f);
+  __half2 p0 = __halves2half2(h[0], h[4]);
+  __half2 p1 = __hmul2(__halves2half2(h[1], h[5]), sixteenth);
+  __half2 p2 = __halves2half2(h[2], h[6]);
+  __half2 p3 = __hmul2(__halves2half2(h[3], h[7]), sixteenth);
+  uint4 o;
+  o.x = *reinterpret_cast<uint32_t*>(&p0);
+  o.y = *reinterpret_cast<uint32_t*>(&p1);
+  o.z = *reinterpret_cast<uint32_t*>(&p2);
+  o.w = *reinterpret_cast<uint32_t*>(&p3);
+  return o;
+}
+
+// Rows g and g+8 of a 16-row down block held in shared memory (codes
+// [16][I/2], scales [16][ngi], zero points [16*ngi/2]) into a register chunk,
+// as u4_load_chunk<128, 4> loads them from global memory.
+__device__ __forceinline__ void load_chunk_smem(U4Chunk<128, 4>& c, const uint8_t* st, int I,
+                                                int ngi, int g, int t) {
+  const __half* sc = reinterpret_cast<const __half*>(st + 8 * I);
+  const uint8_t* zp = st + 8 * I + 32 * ngi;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int gi = min(u, ngi - 1);
+    const uint4 va = *reinterpret_cast<const uint4*>(st + g * (I / 2) + gi * 64 + t * 16);
+    const uint4 vb = *reinterpret_cast<const uint4*>(st + (g + 8) * (I / 2) + gi * 64 + t * 16);
+    c.ra[u][0] = va.x; c.ra[u][1] = va.y; c.ra[u][2] = va.z; c.ra[u][3] = va.w;
+    c.rb[u][0] = vb.x; c.rb[u][1] = vb.y; c.rb[u][2] = vb.z; c.rb[u][3] = vb.w;
+    const int ea = g * ngi + gi, eb = (g + 8) * ngi + gi;
+    c.sa[u] = __half2float(sc[ea]);
+    c.sb[u] = __half2float(sc[eb]);
+    c.za[u] = (uint32_t)(zp[ea >> 1] >> ((ea & 1) * 4)) & 15u;
+    c.zb[u] = (uint32_t)(zp[eb >> 1] >> ((eb & 1) * 4)) & 15u;
+  }
+}
+
+// Bulk copies of rows h0..h0+15 of one expert's down matrix into a slot stage.
+__device__ __forceinline__ void issue_down_rows(const uint8_t* w, const __half* s, const uint8_t* z,
+                                                int64_t e, int H, int I, int h0, uint32_t dst,
+                                                uint32_t bar) {
+  const int ngi = I / 128;
+  const int64_t row = e * H + h0;
+  bulk_load(dst, w + row * (I / 2), 16 * (I / 2), bar);
+  bulk_load(dst + 8 * I, s + row * ngi, 32 * ngi, bar);
+  bulk_load(dst + 8 * I + 32 * ngi, z + row * ngi / 2, 8 * ngi, bar);
+}
+
+__global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a) {
+  extern __shared__ __align__(128) uint8_t lsm[];
+  __shared__ float red[16][16];
+  __shared__ float nred[33];
+  __shared__ int32_t s_ids[16];
+  __shared__ float s_wts[16];
+  __shared__ __align__(8) uint64_t mbar[2];  // 0: shared-slot down rows, 1: routed slots
+  __shared__ int s_ok;
+  const ExpertArgs& e = a.e;
+  const int H = e.H, I = e.I, ngi = I / 128, k = e.k, n_slots = e.n_slots;
+  const LayerSmem L = layer_smem(H, I, n_slots);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int cta = blockIdx.x, nb = gridDim.x;
+  const int quad = warp >> 2, ks = warp & 3;
+  const int ups = I / 8;  // gate_up units per slot
+  const int n_routed_units = k * ups, n_units = n_slots * ups;
+  const int unit = cta + quad * nb;  // host: kLayerQuads * nb >= n_units
+  const bool has_unit = unit < n_units;
+  const bool shared_unit = has_unit && unit >= n_routed_units;
+  const int uslot = has_unit ? unit / ups : 0;
+  const int j0 = (unit % ups) * 8;
+  const int drb = nb - 1 - cta;  // down row block (the last H/16 CTAs)
+  const bool has_down = drb < H / 16;
+  const int h0 = drb * 16;
+  const int n_rows = a.E + (a.w_sg != nullptr ? 1 : 0);
+  const int rrow = cta + warp * nb;  // router row of this warp
+  const bool has_row = rrow < n_rows;
+  const uint32_t sbase = smem_u32(lsm);
+  const uint32_t bar_s = smem_u32(&mbar[0]), bar_r = smem_u32(&mbar[1]);
+
+  // ---- prologue: weights only (nothing here depends on earlier launches)
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_r, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && has_down && n_slots > k) {
+    mbar_arrive_tx(bar_s, 8 * I + 40 * ngi);
+    issue_down_rows(e.sd_w, e.sd_s, e.sd_z, 0, H, I, h0, sbase + L.stage + k * L.slot_bytes, bar_s);
+  }
+  const __half* wr = nullptr;
+  if (has_row) wr = rrow < a.E ? a.w_router + (size_t)rrow * H : a.w_sg;
+  constexpr int kPre = 8;
+  uint4 pre[kPre];
+  if (has_row) {
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = lane + 32 * j;
+      if (c < H / 8) pre[j] = ld_stream_v4(wr + c * 8);
+    }
+  }
+  U4Chunk<128, 4> ch;
+  U4Rows rows{};
+  if (shared_unit) {
+    rows = gate_up_rows<128>(e, nullptr, uslot, j0, g);
+    u4_load_chunk<128, 4>(ch, rows, ks * 4, ks * 4 + 4, t);
+  }
+  pdl_wait();
+
+  // ---- phase A: x, router logits, shared expert gate_up
+  const float* res = a.residual;
+  {
+    // the 256-thread reduction order of stage_x_plain / stage_x_perm
+    if (tid < 256) {
+      float ss = 0.f;
+      for (int i = tid; i < H; i += 256) ss = fmaf(res[i], res[i], ss);
+      ss = warp_sum(ss);
+      if (lane == 0) nred[warp] = ss;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      float v = lane < 8 ? nred[lane] : 0.f;
+      v = warp_sum(v);
+      if (lane == 0) nred[32] = rsqrtf(v / (float)H + a.eps);
+    }
+    __syncthreads();
+    const float scale = nred[32];
+    __half* xp = reinterpret_cast<__half*>(lsm + L.xplain);
+    uint4* xq = reinterpret_cast<uint4*>(lsm + L.xperm);
+    for (int c = tid; c < H / 8; c += kLayerThreads) {
+      __half h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(res[c * 8 + j] * scale * a.nw[c * 8 + j]);
+      *reinterpret_cast<uint4*>(xp + c * 8) = *reinterpret_cast<const uint4*>(h);
+      xq[c] = perm8(h);
+    }
+    __syncthreads();
+  }
+  if (has_row) {
+    const uint4* xv4 = reinterpret_cast<const uint4*>(lsm + L.xplain);
+    float acc = 0.f;
+    auto dot8 = [&](const uint4& wv, const uint4& xv) {
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 wf = __half22float2(wh[j]);
+        const float2 xf = __half22float2(xh[j]);
+        acc = fmaf(wf.x, xf.x, acc);
+        acc = fmaf(wf.y, xf.y, acc);
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int c = lane + 32 * j;
+      if (c < H / 8) dot8(pre[j], xv4[c]);
+    }
+    for (int c = lane + 32 * kPre; c < H / 8; c += 32) dot8(ld_stream_v4(wr + c * 8), xv4[c]);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      if (rrow < a.E) a.logits[rrow] = acc;
+      else a.slogit[0] = acc;
+    }
+  }
+  __syncthreads();
+  unsigned gen = 0;
+  if (tid == 0) gen = layer_bar_arrive(a.bar, nb);
+  const uint4* xs = reinterpret_cast<const uint4*>(lsm + L.xperm);
+  float accA = 0.f, accB = 0.f;
+  if (shared_unit) u4_compute_chunk<128, 4>(ch, xs, ks * 4, ks * 4 + 4, t, accA, accB);
+  if (shared_unit && t == 0) {
+    red[warp][g] = accA;
+    red[warp][g + 8] = accB;
+  }
+  if (tid == 0) s_ok = layer_bar_wait(a.bar, gen) ? 1 : 0;
+  __syncthreads();
+  if (shared_unit && ks == 0 && t == 0) {
+    float ga = 0.f, ub = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      ga += red[warp + j][g];
+      ub += red[warp + j][g + 8];
+    }
+    a.act[(size_t)uslot * I + j0 + g] = __float2half_rn(ga * sigmoidf_acc(ga) * ub);
+  }
+  if (!s_ok) {
+    // leave no bulk copy in flight into this CTA's shared memory
+    if (tid == 0) {
+      atomicAdd(&g_moe_wait_timeouts, 1);
+      if (has_down && n_slots > k) (void)mbar_wait(bar_s, 0);
+    }
+    return;
+  }
+
+  // ---- phase B: top-k, routed down copies, routed gate_up
+  if (warp == 0) {
+    float* sl = reinterpret_cast<float*>(lsm + L.logit);
+    for (int i = lane; i < a.E; i += 32) sl[i] = __ldcg(a.logits + i);
+    __syncwarp();
+    uint32_t sel_id[16];
+    float sel_w[16];
+    router_topk_warp(sl, a.E, k, sel_id, sel_w);
+    if (lane == 0) {
+      for (int r = 0; r < k; ++r) {
+        s_ids[r] = (int32_t)sel_id[r];
+        s_wts[r] = sel_w[r];
+      }
+      if (cta == 0) {
+        for (int r = 0; r < k; ++r) {
+          a.ids_out[r] = (int32_t)sel_id[r];
+          a.wts_out[r] = sel_w[r];
+        }
+      }
+      if (has_down) {
+        mbar_arrive_tx(bar_r, (uint32_t)k * (8 * I + 40 * ngi));
+        for (int r = 0; r < k; ++r)
+          issue_down_rows(e.d_w, e.d_s, e.d_z, (int64_t)sel_id[r], H, I, h0,
+                          sbase + L.stage + r * L.slot_bytes, bar_r);
+      }
+    }
+  }
+  __syncthreads();
+  const bool routed_unit = has_unit && !shared_unit;
+  accA = 0.f;
+  accB = 0.f;
+  if (routed_unit) {
+    rows = gate_up_rows<128>(e, s_ids, uslot, j0, g);
+    u4_load_chunk<128, 4>(ch, rows, ks * 4, ks * 4 + 4, t);
+    u4_compute_chunk<128, 4>(ch, xs, ks * 4, ks * 4 + 4, t, accA, accB);
+    if (t == 0) {
+      red[warp][g] = accA;
+      red[warp][g + 8] = accB;
+    }
+  }
+  __syncthreads();
+  if (routed_unit && ks == 0 && t == 0) {
+    float ga = 0.f, ub = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      ga += red[warp + j][g];
+      ub += red[warp + j][g + 8];
+    }
+    a.act[(size_t)uslot * I + j0 + g] = __float2half_rn(ga * sigmoidf_acc(ga) * ub);
+  }
+  __syncthreads();
+  if (tid == 0) gen = layer_bar_arrive(a.bar, nb);
+  if (!has_down) return;
+  if (tid == 0) s_ok = layer_bar_wait(a.bar, gen) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) {
+    if (tid == 0) {
+      atomicAdd(&g_moe_wait_timeouts, 1);
+      if (n_slots > k) (void)mbar_wait(bar_s, 0);
+      (void)mbar_wait(bar_r, 0);
+    }
+    return;
+  }
+  // every CTA is past barrier 2, hence resident: the next kernel may launch
+  pdl_launch_dependents();
+
+  // ---- phase C: down projections of this CTA's 16 rows, combine, residual
+  uint4* xa = reinterpret_cast<uint4*>(lsm + L.act);
+  for (int c = tid; c < n_slots * I / 8; c += kLayerThreads) {
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(a.act) + c);
+    xa[c] = perm8(reinterpret_cast<const __half*>(&raw));
+  }
+  __syncthreads();
+  if (warp < n_slots) {
+    const bool got = mbar_wait(warp < k ? bar_r : bar_s, 0);
+    accA = 0.f;
+    accB = 0.f;
+    if (got) {
+      load_chunk_smem(ch, lsm + L.stage + warp * L.slot_bytes, I, ngi, g, t);
+      u4_compute_chunk<128, 4>(ch, xa + (size_t)warp * (I / 8), 0, ngi, t, accA, accB);
+    } else if (lane == 0) {
+      atomicAdd(&g_moe_wait_timeouts, 1);
+    }
+    if (t == 0) {
+      red[warp][g] = accA;
+      red[warp][g + 8] = accB;
+    }
+  }
+  __syncthreads();
+  if (tid < 16) {
+    const int row = h0 + tid;
+    float y = 0.0f;
+    for (int j = 0; j < k; ++j) y = __fadd_rn(y, __fmul_rn(red[j][tid], s_wts[j]));
+    if (n_slots > k) y = __fadd_rn(y, __fmul_rn(red[k][tid], sigmoidf_acc(__ldcg(a.slogit))));
+    a.residual[row] = a.residual[row] + __half2float(__float2half_rn(y));
+  }
+}
+
+// Whether the one-launch form covers this layer on `sms` SMs (otherwise the
+// four-launch form runs).
+static bool layer_fused_ok(const iq36_expert_bank* r, const iq36_expert_bank* s, int k, int E,
+                           int sms) {
+  const int H = r->hidden, I = r->intermediate;
+  const int n_slots = k + (s ? 1 : 0);
+  if (r->group != 128 || H % 512 || H > 2048 || I % 256 || I > 512 || E > 256 || k > 15)
+    return false;
+  if (n_slots * (I / 8) > kLayerQuads * sms || H / 16 > sms || E + 1 > 16 * sms) return false;
+  if (!aligned(r->down_scale, 16) || !aligned(r->down_zp, 16)) return false;
+  if (s && (!aligned(s->down_weight, 16) || !aligned(s->down_scale, 16) ||
+            !aligned(s->down_zp, 16)))
+    return false;
+  return layer_smem(H, I, n_slots).total <= 200 * 1024;
+}
+
+static int device_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  int v = cache[dev].load(std::memory_order_acquire);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (cudaFuncSetAttribute(moe_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024) != cudaSuccess)
+      return -1;
+    cache[dev].store(v, std::memory_order_release);
+  }
+  return v;
+}
+
+int moe_wait_timeouts(int* count, int reset) {
+  if (cudaMemcpyFromSymbol(count, g_moe_wait_timeouts, sizeof(int)) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_moe_wait_timeouts, &zero, sizeof(int)) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+  }
+  return IQ36_OK;
 }
 
 int router_logits_launch(const void* x_f16, const float* x_f32, const float* nw, float eps, int T,
@@ -689,6 +1119,50 @@ extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const floa
   if (workspace_bytes < moe_layer_ws(k, routed->hidden, routed->intermediate))
     return IQ36_ERR_WORKSPACE;
   const cudaStream_t s = as_stream(stream);
+  const int sms = device_sms();
+  if (sms < 1) return IQ36_ERR_CUDA;
+  if (layer_fused_ok(routed, shared, k, routed->num_experts, sms)) {
+    LayerArgs la = {};
+    ExpertArgs& a = la.e;
+    a.gu_w = routed->gate_up_weight;
+    a.gu_s = reinterpret_cast<const __half*>(routed->gate_up_scale);
+    a.gu_z = routed->gate_up_zp;
+    a.d_w = routed->down_weight;
+    a.d_s = reinterpret_cast<const __half*>(routed->down_scale);
+    a.d_z = routed->down_zp;
+    a.H = hidden;
+    a.I = routed->intermediate;
+    a.k = k;
+    a.n_slots = k;
+    a.num_experts = routed->num_experts;
+    a.e_lo = 0;
+    if (shared) {
+      a.sgu_w = shared->gate_up_weight;
+      a.sgu_s = reinterpret_cast<const __half*>(shared->gate_up_scale);
+      a.sgu_z = shared->gate_up_zp;
+      a.sd_w = shared->down_weight;
+      a.sd_s = reinterpret_cast<const __half*>(shared->down_scale);
+      a.sd_z = shared->down_zp;
+      a.n_slots = k + 1;
+      la.w_sg = reinterpret_cast<const __half*>(w_shared_gate_f16);
+      la.slogit = shared_logit;
+    }
+    la.residual = residual;
+    la.nw = norm_weight;
+    la.eps = norm_eps;
+    la.w_router = reinterpret_cast<const __half*>(w_router_f16);
+    la.E = routed->num_experts;
+    la.logits = logits;
+    la.ids_out = ids;
+    la.wts_out = weights;
+    la.act = reinterpret_cast<__half*>(workspace);
+    la.bar = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
+                                         moe_decode_ws(k, hidden, routed->intermediate));
+    const LayerSmem L = layer_smem(hidden, routed->intermediate, a.n_slots);
+    const cudaError_t e =
+        launch(moe_layer_kernel, dim3(sms), dim3(kLayerThreads), (size_t)L.total, s, la);
+    return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+  }
   int st = router_logits_launch(nullptr, residual, norm_weight, norm_eps, 1, hidden, w_router_f16,
                                 routed->num_experts, shared ? w_shared_gate_f16 : nullptr, logits,
                                 shared_logit, s);

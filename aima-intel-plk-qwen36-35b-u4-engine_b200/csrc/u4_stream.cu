@@ -174,8 +174,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int c0 = blockIdx.x * per, nloc = max(min(c0 + per, total) - c0, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < geo.stages; ++s) {
-      sm_mbar_init(sbase + L.full + 8 * s, 1);
-      sm_mbar_init(sbase + L.empty + 8 * s, kStreamConsumers);
+      mbar_init(sbase + L.full + 8 * s, 1);
+      mbar_init(sbase + L.empty + 8 * s, kStreamConsumers);
     }
     for (int s = 0; s < 8; ++s) seq[s] = -1;  // no chunk armed yet
     seq[8] = 0;                                // abort flag
@@ -190,11 +190,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       for (int c = 0; c < nloc && ok; ++c) {
         const int s = c % geo.stages;
         const uint32_t ph = (uint32_t)((c / geo.stages) & 1);
-        ok = sm_mbar_wait(sbase + L.empty + 8 * s, ph ^ 1u);
+        ok = mbar_wait(sbase + L.empty + 8 * s, ph ^ 1u);
         if (!ok) break;
         int p, r0;
         const ChunkSrc src = proj_chunk(ps, c0 + c, K, geo.ng, p, r0);
-        sm_mbar_arrive_tx(sbase + L.full + 8 * s, chunk_bytes(geo, src));
+        mbar_arrive_tx(sbase + L.full + 8 * s, chunk_bytes(geo, src));
         ring_publish(seq, s, c);
         issue_chunk(geo, src, sbase + L.ring + s * geo.stage_bytes, sbase + L.full + 8 * s);
       }
@@ -230,11 +230,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                              b0);
         // generic reads of the stages before the producer's next bulk copies
         // (async proxy) into them
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          sm_mbar_arrive(sbase + L.empty + 8 * s0);
-          if (n == 2) sm_mbar_arrive(sbase + L.empty + 8 * s1);
+          mbar_arrive(sbase + L.empty + 8 * s0);
+          if (n == 2) mbar_arrive(sbase + L.empty + 8 * s1);
         }
       } else if (lane == 0) {
         seq[8] = 1;  // shared so that every consumer warp leaves at the barrier below

@@ -20,6 +20,7 @@
 // stream delivers per chunk.
 #pragma once
 
+#include "sync_sm100.cuh"
 #include "u4_core.cuh"
 
 namespace iq36 {
@@ -27,44 +28,6 @@ namespace iq36 {
 constexpr int kStreamConsumers = 16;                      // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;
 constexpr int kStreamRingBytes = 128 * 1024;
-constexpr uint32_t kStreamSpinLimit = 1u << 26;
-
-// ---- mbarrier / bulk-copy wrappers --------------------------------------
-__device__ __forceinline__ void sm_mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void sm_mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void sm_mbar_arrive_tx(uint32_t bar, uint32_t tx) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(tx)
-               : "memory");
-}
-__device__ __forceinline__ bool sm_mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t sm_globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
-  return t;
-}
-// Bounded wait (200 ms or kStreamSpinLimit polls): false on expiry.
-__device__ __forceinline__ bool sm_mbar_wait(uint32_t bar, uint32_t parity) {
-  if (sm_mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = sm_globaltimer();
-  for (uint32_t i = 0; i < kStreamSpinLimit; ++i) {
-    if (sm_mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && sm_globaltimer() - t0 > 200000000ull) return false;
-  }
-  return false;
-}
 // Rings whose chunks are taken by several independent consumer warps: a fast
 // warp can reach chunk c while the stage still holds chunk c - stages (its
 // consumer has not released it yet), and an mbarrier's parity cannot tell
@@ -80,24 +43,14 @@ __device__ __forceinline__ void ring_publish(volatile int* seq, int s, int c) {
 __device__ __forceinline__ bool ring_wait(volatile int* seq, uint32_t full_bar, int s, int c,
                                           int stages) {
   if (seq[s] != c) {
-    const uint64_t t0 = sm_globaltimer();
+    const uint64_t t0 = globaltimer_ns();
     uint32_t i = 0;
     while (seq[s] != c) {
-      if ((++i & 255u) == 0 && sm_globaltimer() - t0 > 200000000ull) return false;
+      if ((++i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
     }
   }
   __threadfence_block();
-  return sm_mbar_wait(full_bar, (uint32_t)((c / stages) & 1));
-}
-
-// 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
+  return mbar_wait(full_bar, (uint32_t)((c / stages) & 1));
 }
 
 bool stream_proj_ok(int K, int G, int n_proj, const iq36_u4_projection* proj);
@@ -152,17 +105,17 @@ __device__ __forceinline__ void issue_chunk(const StreamGeom& g, const ChunkSrc&
   const uint32_t rb = g.K / 2, sb = g.ng * 2, zb = g.ng / 2;  // bytes per row
   if (c.rows[0] == 8 && c.rows[1] == 8 && c.w[1] == c.w[0] + 8 * rb &&
       c.s[1] == c.s[0] + 8 * g.ng && c.z[1] == c.z[0] + 8 * zb) {
-    bulk_g2s(stage, c.w[0], 16 * rb, bar);
-    bulk_g2s(stage + g.off_scale, c.s[0], 16 * sb, bar);
-    bulk_g2s(stage + g.off_zp, c.z[0], 16 * zb, bar);
+    bulk_load(stage, c.w[0], 16 * rb, bar);
+    bulk_load(stage + g.off_scale, c.s[0], 16 * sb, bar);
+    bulk_load(stage + g.off_zp, c.z[0], 16 * zb, bar);
     return;
   }
   for (int h = 0; h < 2; ++h) {
     const int n = c.rows[h];
     if (n == 0) continue;
-    bulk_g2s(stage + h * 8 * g.row_pitch, c.w[h], n * rb, bar);
-    bulk_g2s(stage + g.off_scale + h * 8 * sb, c.s[h], n * sb, bar);
-    bulk_g2s(stage + g.off_zp + h * 8 * zb, c.z[h], n * zb, bar);
+    bulk_load(stage + h * 8 * g.row_pitch, c.w[h], n * rb, bar);
+    bulk_load(stage + g.off_scale + h * 8 * sb, c.s[h], n * sb, bar);
+    bulk_load(stage + g.off_zp + h * 8 * zb, c.z[h], n * zb, bar);
   }
 }
 

@@ -276,9 +276,10 @@ def moe_block_decode(x: torch.Tensor, w_router: torch.Tensor, w_shared_gate: tor
 
 
 def moe_layer_workspace(k: int, hidden: int, intermediate: int, device) -> torch.Tensor:
-    """Workspace of iq36_moe_layer_decode (reusable across calls on one stream)."""
+    """Workspace of iq36_moe_layer_decode (reusable across calls on one stream).
+    Zero-filled: its grid-barrier words must start at zero."""
     n = N.lib().iq36_moe_layer_decode_workspace_bytes(k, hidden, intermediate)
-    return torch.empty(n, dtype=torch.uint8, device=device)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
 def moe_layer_decode(residual: torch.Tensor, norm_weight: torch.Tensor, w_router: torch.Tensor,

@@ -239,6 +239,12 @@ class Qwen36Runtime:
         self.ws_argmax = torch.empty(N.lib().iq36_argmax_workspace_bytes(), dtype=torch.uint8,
                                      device=dev)
         self._pf: dict | None = None  # batched-prefill buffers (sized on first use)
+        # Optional step trace (tests): when set before capture(), every step
+        # also copies the residual entering each layer (and leaving the last)
+        # into trace [layers + 1, hidden] and each layer's routed ids into
+        # trace_ids [layers, topk].
+        self.trace: torch.Tensor | None = None
+        self.trace_ids: torch.Tensor | None = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(device=dev)
         self.launches_per_step = 0
@@ -260,47 +266,60 @@ class Qwen36Runtime:
         """Enqueue one decode step on the current stream; returns the number of
         kernel launches."""
         c, W = self.cfg, self.w
-        n = 0
         ops.embed(W.embed, self.token, self.hres)
-        n += 1
+        n = 1
         for l in range(c.layers):
-            L = W.layers[l]
-            if c.is_attn(l):
-                ops.u4_matvec_multi(None, [L["q"], L["k"], L["v"]],
-                                    [self.b_qfull, self.b_k, self.b_v], x_f32=self.hres,
-                                    norm_weight=L["in_norm"], norm_eps=c.eps)
-                kc, vc = self.kv[l]
-                ops.attn_prep(self.b_qfull, self.b_k, self.b_v, L["qn"], L["kn"], c.eps, self.pos,
-                              self.block_table, kc, vc, self.b_q, self.b_gate,
-                              rope_dim=c.rope_dim, rope_base=c.rope_base)
-                ops.paged_gqa_decode(self.b_q.view(c.nq, c.head_dim), kc, vc, self.block_table,
-                                     self.max_ctx, 1.0 / math.sqrt(c.head_dim),
-                                     gate=self.b_gate, ctx_len_dev=self.ctx,
-                                     workspace=self.ws_gqa, out=self.b_attn)
-                ops.u4_matvec_multi(self.b_attn, [L["o"]], [self.hres], accumulate=[True])
-                n += 5
-            else:
-                ops.u4_matvec_multi(None, [L["qkv"], L["z"], L["a"], L["b"]],
-                                    [self.b_qkv, self.b_z, self.b_a, self.b_b], x_f32=self.hres,
-                                    norm_weight=L["in_norm"], norm_eps=c.eps)
-                ops.delta_prep(self.b_qkv, self.conv_state[l], L["conv_w"], self.b_a, self.b_b,
-                               L["a_log"], L["dt_bias"], self.b_act, self.b_g, self.b_beta)
-                ops.delta_step(self.b_act, self.b_g, self.b_beta, self.rec_state[l], self.b_z,
-                               L["dnorm"], c.eps, c.nk, c.nv, self.b_dout, head_dim=c.dk)
-                ops.u4_matvec_multi(self.b_dout, [L["out"]], [self.hres], accumulate=[True])
-                n += 4
-            # post-attention RMSNorm fused into the router and gate_up prologues
-            # (reference run_qwen36_moe_ffn_layer)
-            ops.moe_layer_decode(self.hres, L["post_norm"], L["router"], L["sgate"], L["bank"],
-                                 L["shared"], self.b_ids, self.b_wts, self.b_logits_r,
-                                 self.b_slogit, workspace=self.ws_moe, k=c.topk, norm_eps=c.eps)
-            n += 4
+            if self.trace is not None:
+                self.trace[l].copy_(self.hres)
+            n += self.enqueue_layer(l)
+            if self.trace is not None:
+                self.trace_ids[l].copy_(self.b_ids)
+        if self.trace is not None:
+            self.trace[c.layers].copy_(self.hres)
         ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
                             norm_weight=W.final_norm, norm_eps=c.eps)
         ops.argmax(self.logits, self.token, self.ws_argmax)
         N.call("iq36_decode_positions", self.pos.data_ptr(), self.ctx.data_ptr(), 1,
                ops._stream(self.dev))
-        n += 4
+        return n + 3
+
+    def enqueue_layer(self, l: int) -> int:
+        """Enqueue decoder layer l of the decode step on the fp32 residual
+        ``hres`` at the device position ``pos`` (attention or DeltaNet block,
+        then the MoE block); returns the number of launches."""
+        c, W = self.cfg, self.w
+        n = 0
+        L = W.layers[l]
+        if c.is_attn(l):
+            ops.u4_matvec_multi(None, [L["q"], L["k"], L["v"]],
+                                [self.b_qfull, self.b_k, self.b_v], x_f32=self.hres,
+                                norm_weight=L["in_norm"], norm_eps=c.eps)
+            kc, vc = self.kv[l]
+            ops.attn_prep(self.b_qfull, self.b_k, self.b_v, L["qn"], L["kn"], c.eps, self.pos,
+                          self.block_table, kc, vc, self.b_q, self.b_gate,
+                          rope_dim=c.rope_dim, rope_base=c.rope_base)
+            ops.paged_gqa_decode(self.b_q.view(c.nq, c.head_dim), kc, vc, self.block_table,
+                                 self.max_ctx, 1.0 / math.sqrt(c.head_dim),
+                                 gate=self.b_gate, ctx_len_dev=self.ctx,
+                                 workspace=self.ws_gqa, out=self.b_attn)
+            ops.u4_matvec_multi(self.b_attn, [L["o"]], [self.hres], accumulate=[True])
+            n += 5
+        else:
+            ops.u4_matvec_multi(None, [L["qkv"], L["z"], L["a"], L["b"]],
+                                [self.b_qkv, self.b_z, self.b_a, self.b_b], x_f32=self.hres,
+                                norm_weight=L["in_norm"], norm_eps=c.eps)
+            ops.delta_prep(self.b_qkv, self.conv_state[l], L["conv_w"], self.b_a, self.b_b,
+                           L["a_log"], L["dt_bias"], self.b_act, self.b_g, self.b_beta)
+            ops.delta_step(self.b_act, self.b_g, self.b_beta, self.rec_state[l], self.b_z,
+                           L["dnorm"], c.eps, c.nk, c.nv, self.b_dout, head_dim=c.dk)
+            ops.u4_matvec_multi(self.b_dout, [L["out"]], [self.hres], accumulate=[True])
+            n += 4
+        # post-attention RMSNorm fused into the router and gate_up prologues
+        # (reference run_qwen36_moe_ffn_layer)
+        ops.moe_layer_decode(self.hres, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                             L["shared"], self.b_ids, self.b_wts, self.b_logits_r,
+                             self.b_slogit, workspace=self.ws_moe, k=c.topk, norm_eps=c.eps)
+        n += 1
         return n
 
     def enqueue_gemvs_only(self) -> tuple[int, int]:
@@ -339,8 +358,16 @@ class Qwen36Runtime:
         return nbytes, n
 
     def capture(self) -> None:
-        """Record one decode step as a CUDA graph (state read from device)."""
+        """Record one decode step as a CUDA graph (state read from device).
+
+        Capturing runs one warm-up step eagerly and then resets the sequence
+        (KV cache, conv and recurrent states zeroed, position 0), so it must be
+        called before the prompt: a runtime whose position is not 0 raises
+        instead of silently dropping its state."""
         torch.cuda.synchronize(self.dev)
+        if int(self.pos.item()) != 0:
+            raise RuntimeError("capture() resets the sequence; call it before prefill "
+                               f"(position is {int(self.pos.item())})")
         saved = (self.pos.clone(), self.token.clone())
         with torch.cuda.stream(self.stream):
             self.enqueue_step()  # warm-up outside capture (also runs lazy init)
@@ -405,46 +432,55 @@ class Qwen36Runtime:
         Returns the number of launches."""
         c, W, B = self.cfg, self.w, self._pf
         assert B is not None and B["T"] >= T
-        hd = c.head_dim
-        sl = lambda name: B[name][:T]
-        h = sl("h")
-        ws = B["gws"]
-        ops.embed_batch(W.embed, sl("tok"), h)
+        h = B["h"][:T]
+        ops.embed_batch(W.embed, B["tok"][:T], h)
         n = 1
         for l in range(c.layers):
-            L = W.layers[l]
-            if c.is_attn(l):
-                ops.u4_gemm_multi(h, [L["q"], L["k"], L["v"]], [sl("qfull"), sl("k"), sl("v")],
-                                  norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
-                kc, vc = self.kv[l]
-                ops.attn_prep_batch(sl("qfull"), sl("k"), sl("v"), L["qn"], L["kn"], c.eps,
-                                    self.pos, self.block_table, kc, vc, sl("q"), sl("gate"),
-                                    rope_dim=c.rope_dim, rope_base=c.rope_base)
-                ops.attn_prefill(sl("q").view(T, c.nq, hd), kc, vc, self.block_table, self.pos,
-                                 1.0 / math.sqrt(hd), gate=sl("gate").view(T, c.nq, hd),
-                                 out=sl("attn").view(T, c.nq, hd))
-                ops.u4_gemm(sl("attn"), L["o"], out=h, accumulate=True, workspace=ws)
-                n += 6
-            else:
-                ops.u4_gemm_multi(h, [L["qkv"], L["z"], L["ab"]], [sl("qkv"), sl("z"), sl("ab")],
-                                  norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
-                ab = sl("ab")
-                ops.delta_prefill(sl("qkv"), self.conv_state[l], L["conv_w"], ab[:, :c.nv],
-                                  ab[:, c.nv:2 * c.nv], L["a_log"], L["dt_bias"],
-                                  self.rec_state[l], sl("z"), L["dnorm"], c.eps, c.nk, c.nv,
-                                  sl("dout"), workspace=B["dws"])
-                ops.u4_gemm(sl("dout"), L["out"], out=h, accumulate=True, workspace=ws)
-                n += 9
-            ops.moe_layer_prefill(h, L["post_norm"], L["router"], L["sgate"], L["bank"],
-                                  L["shared"], sl("ids"), sl("wts"), sl("logits_r"),
-                                  workspace=B["mws"], k=c.topk, norm_eps=c.eps)
-            n += 14
+            n += self.enqueue_prefill_layer(l, T)
         ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=h[T - 1],
                             norm_weight=W.final_norm, norm_eps=c.eps)
         ops.argmax(self.logits, self.token, self.ws_argmax)
         N.call("iq36_decode_positions", self.pos.data_ptr(), self.ctx.data_ptr(), T,
                ops._stream(self.dev))
         return n + 4
+
+    def enqueue_prefill_layer(self, l: int, T: int) -> int:
+        """Enqueue decoder layer l over the T prompt rows of the prefill
+        buffer's fp32 residual ``h`` at positions pos .. pos+T-1 (the batched
+        form of ``enqueue_layer``); returns the number of launches."""
+        c, W, B = self.cfg, self.w, self._pf
+        assert B is not None and B["T"] >= T
+        hd = c.head_dim
+        sl = lambda name: B[name][:T]
+        h = sl("h")
+        ws = B["gws"]
+        L = W.layers[l]
+        if c.is_attn(l):
+            ops.u4_gemm_multi(h, [L["q"], L["k"], L["v"]], [sl("qfull"), sl("k"), sl("v")],
+                              norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
+            kc, vc = self.kv[l]
+            ops.attn_prep_batch(sl("qfull"), sl("k"), sl("v"), L["qn"], L["kn"], c.eps,
+                                self.pos, self.block_table, kc, vc, sl("q"), sl("gate"),
+                                rope_dim=c.rope_dim, rope_base=c.rope_base)
+            ops.attn_prefill(sl("q").view(T, c.nq, hd), kc, vc, self.block_table, self.pos,
+                             1.0 / math.sqrt(hd), gate=sl("gate").view(T, c.nq, hd),
+                             out=sl("attn").view(T, c.nq, hd))
+            ops.u4_gemm(sl("attn"), L["o"], out=h, accumulate=True, workspace=ws)
+            n = 6
+        else:
+            ops.u4_gemm_multi(h, [L["qkv"], L["z"], L["ab"]], [sl("qkv"), sl("z"), sl("ab")],
+                              norm_weight=L["in_norm"], norm_eps=c.eps, workspace=ws)
+            ab = sl("ab")
+            ops.delta_prefill(sl("qkv"), self.conv_state[l], L["conv_w"], ab[:, :c.nv],
+                              ab[:, c.nv:2 * c.nv], L["a_log"], L["dt_bias"],
+                              self.rec_state[l], sl("z"), L["dnorm"], c.eps, c.nk, c.nv,
+                              sl("dout"), workspace=B["dws"])
+            ops.u4_gemm(sl("dout"), L["out"], out=h, accumulate=True, workspace=ws)
+            n = 9
+        ops.moe_layer_prefill(h, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                              L["shared"], sl("ids"), sl("wts"), sl("logits_r"),
+                              workspace=B["mws"], k=c.topk, norm_eps=c.eps)
+        return n + 14
 
     def prefill_batched(self, tokens: list[int] | torch.Tensor, chunk: int = 16384) -> int:
         """Batched prefill of the prompt in chunks of at most ``chunk`` tokens

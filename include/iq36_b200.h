@@ -10,13 +10,33 @@
  *     pointer checks happen on the host before any launch, so a failed call has
  *     enqueued nothing;
  *   - fp16 tensors are IEEE binary16 passed as uint16_t / void*;
- *   - kernels are launched with programmatic dependent launch: each reads the
- *     outputs of the previous launch on the stream only after waiting for it,
- *     but reads data that launch does not produce (weights; the positions,
- *     recurrent / conv state and earlier cache pages of the decode entries)
- *     before that wait. Such inputs must therefore not be written by the
- *     immediately preceding launch on the stream (a decode step writes them
- *     once per step, at its end or many launches earlier).
+ *   - kernels are launched with programmatic dependent launch (PDL). A kernel
+ *     reads what earlier launches produce only after griddepcontrol.wait,
+ *     except for its EARLY inputs, which it reads before that wait: weights
+ *     (every entry point), and for the decode entries the position words
+ *     (iq36_attn_prep), the conv state (iq36_delta_prep), the recurrent state
+ *     (iq36_delta_step), the cache pages before the appended token
+ *     (iq36_paged_gqa_decode) and the expert ids (the down-projection kernel
+ *     of iq36_moe_decode).
+ *     Rule for early inputs: let W be the most recent earlier launch on the
+ *     stream that WAITS BEFORE IT RELEASES its dependents. An early input must
+ *     not be written by W or by any launch after W. Everything launched before
+ *     W has completed when the early read runs: W released only after its
+ *     wait, i.e. after its predecessor completed, and every kernel of this
+ *     library waits on its predecessor before it exits, so completion carries
+ *     back through the whole stream (the early read relies on that completion
+ *     having made the writes visible, as it does through L2; PTX promises
+ *     visibility only after griddepcontrol.wait, and only for the prerequisite
+ *     grid).
+ *     Launches that RELEASE BEFORE THEY WAIT: the weight-streaming kernel of
+ *     iq36_u4_gemv / iq36_u4_gemv_multi (G = 128, rows % 16 == 0, K % 512 ==
+ *     0), iq36_attn_prep, and iq36_router_select (also the selection launch
+ *     inside iq36_moe_block_decode and the four-launch form of
+ *     iq36_moe_layer_decode). Every other launch waits first.
+ *     Example: iq36_delta_prep reads the conv state early, so the sequence
+ *     iq36_delta_prep, iq36_u4_gemv_multi, iq36_delta_prep on one stream needs
+ *     a waiting launch between the two pre-steps (a decode step has several
+ *     per layer: the recurrence, the embedding, the MoE layer's router).
  *
  * u4 matrix layout (the OpenVINO compressed-constant layout before the
  * reference's group-major repack; reference
@@ -175,9 +195,18 @@ size_t iq36_moe_block_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t 
  *   ids, weights = top-k of softmax(logits) (as iq36_router_select);
  *   residual += f16(sum_r weights[r] * Expert_{ids[r]}(x)
  *                   + sigmoid(shared_logit) * Shared(x)).
- * Four launches (router, top-k, gate_up + SwiGLU, down + combine). ids /
- * weights / logits / shared_logit are device outputs; workspace: 16-byte
- * aligned, iq36_moe_layer_decode_workspace_bytes long. */
+ * ids / weights / logits / shared_logit are device outputs.
+ * At the config-4 shapes (group 128, hidden <= 2048 and a multiple of 512,
+ * intermediate 256 or 512, E <= 256, k <= 15, 16-byte aligned down scales and
+ * zero points) this is ONE persistent launch, one CTA per SM, whose phases
+ * (router | top-k + routed gate_up | down + combine) are separated by two grid
+ * barriers kept in the workspace; other shapes run four launches (router,
+ * top-k, gate_up + SwiGLU, down + combine). Both forms give the same bits.
+ * workspace: 16-byte aligned, iq36_moe_layer_decode_workspace_bytes long,
+ * ZERO-FILLED before its first use; it stays valid across calls (the barrier
+ * words return to rest after each call). Calls sharing one workspace must be
+ * ordered on one stream. If iq36_wait_timeouts reports a timeout, zero the
+ * workspace again before the next call. */
 int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_weight,
                           float norm_eps, const void* w_router_f16, const void* w_shared_gate_f16,
                           int32_t k, const iq36_expert_bank* routed,

@@ -177,19 +177,26 @@ void orc_f32_to_f16(const float* in, int64_t n, uint16_t* out) {
 
 // Host twin of the device generator (include/iq36_synth.h); same kinds as
 // iq36_synth_fill.
-void orc_synth_fill(void* dst, int64_t count, int kind, uint64_t seed, uint64_t tensor, float lo,
-                    float hi) {
+// Elements [offset, offset + count) of one synthetic tensor into dst[0..count).
+void orc_synth_fill_at(void* dst, int64_t offset, int64_t count, int kind, uint64_t seed,
+                       uint64_t tensor, float lo, float hi) {
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < count; ++i) {
+    const uint64_t j = (uint64_t)(offset + i);
     switch (kind) {
-      case 0: ((uint8_t*)dst)[i] = iq36_synth_u8(seed, tensor, (uint64_t)i); break;
-      case 1: ((uint16_t*)dst)[i] = f2h(iq36_synth_uniform(seed, tensor, (uint64_t)i, lo, hi)); break;
-      case 2: ((uint16_t*)dst)[i] = f2h(iq36_synth_normal(seed, tensor, (uint64_t)i, lo)); break;
-      case 3: ((float*)dst)[i] = iq36_synth_uniform(seed, tensor, (uint64_t)i, lo, hi); break;
-      case 4: ((float*)dst)[i] = iq36_synth_normal(seed, tensor, (uint64_t)i, lo); break;
+      case 0: ((uint8_t*)dst)[i] = iq36_synth_u8(seed, tensor, j); break;
+      case 1: ((uint16_t*)dst)[i] = f2h(iq36_synth_uniform(seed, tensor, j, lo, hi)); break;
+      case 2: ((uint16_t*)dst)[i] = f2h(iq36_synth_normal(seed, tensor, j, lo)); break;
+      case 3: ((float*)dst)[i] = iq36_synth_uniform(seed, tensor, j, lo, hi); break;
+      case 4: ((float*)dst)[i] = iq36_synth_normal(seed, tensor, j, lo); break;
       default: break;
     }
   }
+}
+
+void orc_synth_fill(void* dst, int64_t count, int kind, uint64_t seed, uint64_t tensor, float lo,
+                    float hi) {
+  orc_synth_fill_at(dst, 0, count, kind, seed, tensor, lo, hi);
 }
 
 // u4 GEMV, fp16 activation. Restates iq36_fixed_fc_multi_output.cl:112-167

@@ -13,6 +13,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -21,6 +22,8 @@
 extern "C" {
 void orc_synth_fill(void* dst, int64_t count, int kind, uint64_t seed, uint64_t tensor, float lo,
                     float hi);
+void orc_synth_fill_at(void* dst, int64_t offset, int64_t count, int kind, uint64_t seed,
+                       uint64_t tensor, float lo, float hi);
 void orc_u4_gemv(const uint16_t* x_f16, int K, int G, const uint8_t* w, const uint16_t* scale,
                  const uint8_t* zp, int64_t N, float* out, int precise, int threads);
 void orc_f16_linear(const uint16_t* x_f16, int H, const uint16_t* W, int E, float* out);
@@ -90,7 +93,7 @@ struct Layer {
   U4 qkv, z, a, b, out;                           // DeltaNet
   std::vector<float> conv_w, a_log, dt_bias, dnorm;
   std::vector<uint16_t> router, sgate;            // MoE
-  U4 gu, down, sgu, sdown;
+  U4 gu, down, sgu, sdown;  // gu/down hold all experts, or (lazy) the k selected ones
   // state
   std::vector<float> conv_state, rec_state;
   std::vector<uint16_t> kc, vc;
@@ -100,6 +103,16 @@ struct Model {
   OrcModelConfig c;
   uint64_t seed;
   int max_ctx;
+  // Lazy expert banks: above kLazyBankBytes per layer the routed experts are
+  // not materialised; each step regenerates only the k selected experts'
+  // rows from the counter-based generator (same values, element for element),
+  // so the full 256-expert model needs ~1 GB of host memory instead of ~17 GB.
+  bool lazy = false;
+  // GEMV and expert accumulation in fp64 instead of the fp32 mirror
+  // (IQ36_ORACLE_PRECISE=1): a second checker that differs from the first only
+  // in summation rounding, used to measure how far the deep random-init model
+  // amplifies rounding differences.
+  int precise = 0;
   std::vector<Layer> layers;
   std::vector<float> final_norm;
   U4 lm_head;
@@ -139,9 +152,38 @@ void fill_u4(U4& m, int64_t rows, int K, int G, uint64_t seed, int layer, int sl
   orc_synth_fill(m.z.data(), nz, kind, seed, iq36_tensor_id(layer, slot, 2), lo, hi);
 }
 
-void gemv16(const U4& m, const uint16_t* x, int G, std::vector<float>& y, int threads) {
+constexpr int64_t kLazyBankBytes = 256ll << 20;
+
+// Rows [row0, row0 + rows) of a u4 matrix tensor (codes, scales, zero
+// points) into slot `dst_row0` of m (m already sized).
+void fill_u4_rows(U4& m, int64_t dst_row0, int64_t row0, int64_t rows, int K, int G,
+                  uint64_t seed, int layer, int slot) {
+  const int ng = K / G;
+  int kind;
+  float lo, hi;
+  iq36_synth_spec(slot, 0, &kind, &lo, &hi);
+  orc_synth_fill_at(m.w.data() + dst_row0 * (K / 2), row0 * (K / 2), rows * (K / 2), kind, seed,
+                    iq36_tensor_id(layer, slot, 0), lo, hi);
+  iq36_synth_spec(slot, 1, &kind, &lo, &hi);
+  orc_synth_fill_at(m.s.data() + dst_row0 * ng, row0 * ng, rows * ng, kind, seed,
+                    iq36_tensor_id(layer, slot, 1), lo, hi);
+  iq36_synth_spec(slot, 2, &kind, &lo, &hi);
+  orc_synth_fill_at(m.z.data() + dst_row0 * ng / 2, row0 * ng / 2, rows * ng / 2, kind, seed,
+                    iq36_tensor_id(layer, slot, 2), lo, hi);
+}
+
+void size_u4(U4& m, int64_t rows, int K, int G) {
+  m.rows = rows;
+  m.K = K;
+  m.w.resize(rows * K / 2);
+  m.s.resize(rows * K / G);
+  m.z.resize(rows * K / G / 2);
+}
+
+void gemv16(const U4& m, const uint16_t* x, int G, std::vector<float>& y, int threads,
+            int precise) {
   y.resize(m.rows);
-  orc_u4_gemv(x, m.K, G, m.w.data(), m.s.data(), m.z.data(), m.rows, y.data(), 0, threads);
+  orc_u4_gemv(x, m.K, G, m.w.data(), m.s.data(), m.z.data(), m.rows, y.data(), precise, threads);
 }
 
 std::vector<uint16_t> to_f16(const std::vector<float>& v) {
@@ -193,8 +235,16 @@ void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
     }
     fill_f16(L.router, (int64_t)c.experts * H, seed, l, IQ36_T_ROUTER);
     fill_f16(L.sgate, H, seed, l, IQ36_T_SGATE);
-    fill_u4(L.gu, (int64_t)c.experts * 2 * c.inter, H, G, seed, l, IQ36_T_GU);
-    fill_u4(L.down, (int64_t)c.experts * H, c.inter, G, seed, l, IQ36_T_DOWN);
+    M->lazy = (int64_t)c.experts * 3 * c.inter * H / 2 > kLazyBankBytes;
+    if (const char* f = std::getenv("IQ36_ORACLE_LAZY")) M->lazy = f[0] == '1';
+    if (const char* f = std::getenv("IQ36_ORACLE_PRECISE")) M->precise = f[0] == '1';
+    if (M->lazy) {
+      size_u4(L.gu, (int64_t)c.topk * 2 * c.inter, H, G);
+      size_u4(L.down, (int64_t)c.topk * H, c.inter, G);
+    } else {
+      fill_u4(L.gu, (int64_t)c.experts * 2 * c.inter, H, G, seed, l, IQ36_T_GU);
+      fill_u4(L.down, (int64_t)c.experts * H, c.inter, G, seed, l, IQ36_T_DOWN);
+    }
     fill_u4(L.sgu, (int64_t)2 * c.shared_inter, H, G, seed, l, IQ36_T_SGU);
     fill_u4(L.sdown, H, c.shared_inter, G, seed, l, IQ36_T_SDOWN);
   }
@@ -210,7 +260,29 @@ void orc_model_destroy(void* m) { delete static_cast<Model*>(m); }
 // One decode step at position pos (the KV cache and recurrent states hold
 // positions < pos). Writes fp32 logits [vocab] when logits != NULL and returns
 // the greedy token.
+int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads, int lm_head,
+                       float* hidden, int32_t* ids_out);
+
 int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
+  return orc_model_step_opt(mp, token, pos, logits, threads, 1, nullptr, nullptr);
+}
+
+// The step without the final norm and LM head (returns -1): feeds a prompt
+// token whose next-token distribution is not needed.
+int orc_model_feed(void* mp, int token, int pos, int threads) {
+  return orc_model_step_opt(mp, token, pos, nullptr, threads, 0, nullptr, nullptr);
+}
+
+// The step with its trace: hidden [(layers + 1) * hidden] receives the fp32
+// residual stream entering each layer and, last, leaving the final layer;
+// ids_out [layers * topk] the routed expert ids of every layer (rank order).
+int orc_model_step_trace(void* mp, int token, int pos, float* logits, int threads, float* hidden,
+                         int32_t* ids_out) {
+  return orc_model_step_opt(mp, token, pos, logits, threads, 1, hidden, ids_out);
+}
+
+int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads, int lm_head,
+                       float* hidden, int32_t* ids_out) {
   Model& M = *static_cast<Model*>(mp);
   const OrcModelConfig& c = M.c;
   const int H = c.hidden, G = c.group;
@@ -229,13 +301,14 @@ int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
   }
   for (int l = 0; l < c.layers; ++l) {
     Layer& L = M.layers[l];
+    if (hidden) std::memcpy(hidden + (int64_t)l * H, h.data(), sizeof(float) * H);
     orc_rms_norm(h.data(), 1, H, L.in_norm.data(), H, c.eps, xn.data());
     const auto x16 = to_f16(xn);
     if (L.attn) {
       const int D = c.head_dim;
-      gemv16(L.q, x16.data(), G, y, threads);
-      gemv16(L.k, x16.data(), G, y2, threads);
-      gemv16(L.v, x16.data(), G, y3, threads);
+      gemv16(L.q, x16.data(), G, y, threads, M.precise);
+      gemv16(L.k, x16.data(), G, y2, threads, M.precise);
+      gemv16(L.v, x16.data(), G, y3, threads, M.precise);
       const auto qf = to_f16(y), kf = to_f16(y2), vf = to_f16(y3);
       std::vector<float> qo(c.nq * D), go(c.nq * D), kn(c.nkv * D), vn(c.nkv * D);
       orc_attn_prep(qf.data(), kf.data(), vf.data(), L.qn.data(), L.kn.data(), c.eps, pos, c.nq,
@@ -251,14 +324,14 @@ int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
       orc_paged_gqa(q16.data(), L.kc.data(), L.vc.data(), M.bt.data(), pos + 1, c.nq, c.nkv, D,
                     16, 1.0f / std::sqrt((float)D), g16.data(), att.data(), threads);
       const auto a16 = to_f16(att);
-      gemv16(L.o, a16.data(), G, y4, threads);
+      gemv16(L.o, a16.data(), G, y4, threads, M.precise);
     } else {
       const int C = (2 * c.nk + c.nv) * c.dk;
-      gemv16(L.qkv, x16.data(), G, y, threads);
-      gemv16(L.z, x16.data(), G, y2, threads);
+      gemv16(L.qkv, x16.data(), G, y, threads, M.precise);
+      gemv16(L.z, x16.data(), G, y2, threads, M.precise);
       std::vector<float> ya, yb;
-      gemv16(L.a, x16.data(), G, ya, threads);
-      gemv16(L.b, x16.data(), G, yb, threads);
+      gemv16(L.a, x16.data(), G, ya, threads, M.precise);
+      gemv16(L.b, x16.data(), G, yb, threads, M.precise);
       const auto qkv16 = to_f16(y), z16 = to_f16(y2), a16 = to_f16(ya), b16 = to_f16(yb);
       std::vector<float> act(C), g(c.nv), beta(c.nv), o(c.nv * c.dk);
       orc_delta_prep(qkv16.data(), C, L.conv_state.data(), L.conv_w.data(), a16.data(),
@@ -267,7 +340,7 @@ int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
       orc_delta_step(act.data(), g.data(), beta.data(), L.rec_state.data(), z16.data(),
                      L.dnorm.data(), c.eps, c.nk, c.nv, c.dk, o.data());
       const auto o16 = to_f16(o);
-      gemv16(L.out, o16.data(), G, y4, threads);
+      gemv16(L.out, o16.data(), G, y4, threads, M.precise);
     }
     for (int i = 0; i < H; ++i) h[i] += h2f(f2h(y4[i]));
     orc_rms_norm(h.data(), 1, H, L.post_norm.data(), H, c.eps, xn.data());
@@ -278,17 +351,30 @@ int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
     orc_f16_linear(x2.data(), H, L.router.data(), c.experts, lg.data());
     orc_f16_linear(x2.data(), H, L.sgate.data(), 1, &sl);
     orc_router_select(lg.data(), 1, c.experts, c.topk, ids.data(), w.data());
+    if (ids_out) std::memcpy(ids_out + (int64_t)l * c.topk, ids.data(), sizeof(int32_t) * c.topk);
+    if (M.lazy) {
+      // the selected experts' rows into slots 0..k-1, then index by slot
+      for (int r = 0; r < c.topk; ++r) {
+        fill_u4_rows(L.gu, (int64_t)r * 2 * c.inter, (int64_t)ids[r] * 2 * c.inter, 2 * c.inter, H,
+                     G, M.seed, l, IQ36_T_GU);
+        fill_u4_rows(L.down, (int64_t)r * H, (int64_t)ids[r] * H, H, c.inter, G, M.seed, l,
+                     IQ36_T_DOWN);
+        ids[r] = r;
+      }
+    }
     orc_moe_decode(x2.data(), ids.data(), w.data(), c.topk, L.gu.w.data(), L.gu.s.data(),
                    L.gu.z.data(), L.down.w.data(), L.down.s.data(), L.down.z.data(),
                    L.sgu.w.data(), L.sgu.s.data(), L.sgu.z.data(), L.sdown.w.data(),
-                   L.sdown.s.data(), L.sdown.z.data(), &sl, H, c.inter, G, mo.data(), 0,
+                   L.sdown.s.data(), L.sdown.z.data(), &sl, H, c.inter, G, mo.data(), M.precise,
                    threads);
     for (int i = 0; i < H; ++i) h[i] += h2f(f2h(mo[i]));
   }
+  if (hidden) std::memcpy(hidden + (int64_t)c.layers * H, h.data(), sizeof(float) * H);
+  if (!lm_head) return -1;
   orc_rms_norm(h.data(), 1, H, M.final_norm.data(), H, c.eps, xn.data());
   const auto xf = to_f16(xn);
   std::vector<float> lo;
-  gemv16(M.lm_head, xf.data(), G, lo, threads);
+  gemv16(M.lm_head, xf.data(), G, lo, threads, M.precise);
   if (logits) std::memcpy(logits, lo.data(), sizeof(float) * c.vocab);
   return orc_argmax(lo.data(), c.vocab);
 }

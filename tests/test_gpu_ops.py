@@ -177,6 +177,63 @@ def test_moe_layer_decode_matches_oracle(cuda, config1):
     assert_close(_np(res), res0 + ref.astype(np.float16).astype(np.float32), "moe layer")
 
 
+def _moe_layer_four_launches(res, nw, w_router, w_sg, rb, sb, k, stream):
+    """The layer composed from the separate entry points (router logits on the
+    normalised residual, top-k selection, routed + shared experts adding into
+    the residual): the four-launch form of iq36_moe_layer_decode."""
+    import ctypes
+    import torch
+    from engine import _native as N
+    dev = res.device
+    logits = torch.empty(256, dtype=torch.float32, device=dev)
+    sl = torch.empty(1, dtype=torch.float32, device=dev)
+    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    wts = torch.empty(k, dtype=torch.float32, device=dev)
+    N.call("iq36_router_logits", None, res.data_ptr(), nw.data_ptr(), 1e-6, 1, 2048,
+           w_router.data_ptr(), 256, w_sg.data_ptr(), logits.data_ptr(), sl.data_ptr(), stream)
+    N.call("iq36_router_select", logits.data_ptr(), 1, 256, k, ids.data_ptr(), wts.data_ptr(),
+           stream)
+    ws = torch.empty(N.lib().iq36_moe_decode_workspace_bytes(k, 2048, 512), dtype=torch.uint8,
+                     device=dev)
+    r, s = rb.c(), sb.c()
+    N.call("iq36_moe_decode", None, res.data_ptr(), nw.data_ptr(), 1e-6, ids.data_ptr(),
+           wts.data_ptr(), k, ctypes.byref(r), ctypes.byref(s), sl.data_ptr(), res.data_ptr(),
+           0, 1, ws.data_ptr(), ws.numel(), stream)
+    return logits, ids, wts
+
+
+def test_moe_layer_one_launch_equals_four_launches(cuda, config1):
+    """The one-launch layer (grid barriers in the workspace) gives the same bits
+    as the four separate launches, over several calls in a row that reuse one
+    workspace (its barrier words must come back to rest after every call)."""
+    import torch
+    from engine.ops import moe_layer_decode, moe_layer_workspace
+    c = config1
+    rng = np.random.default_rng(12)
+    rb, sb = bank_to_torch(c["bank"], cuda), bank_to_torch(c["shared"], cuda)
+    nw = _t(rng.uniform(0.9, 1.1, 2048).astype(np.float32), cuda)
+    wr, wsg = _t(c["w_router"], cuda), _t(c["w_sg"], cuda)
+    res0 = (rng.standard_normal(2048) * 3).astype(np.float32)
+    a = _t(res0.copy(), cuda)
+    b = _t(res0.copy(), cuda)
+    ws = moe_layer_workspace(8, 2048, 512, cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    ids = torch.empty(8, dtype=torch.int32, device=cuda)
+    wts = torch.empty(8, dtype=torch.float32, device=cuda)
+    logits = torch.empty(256, dtype=torch.float32, device=cuda)
+    sl = torch.empty(1, dtype=torch.float32, device=cuda)
+    for step in range(6):
+        moe_layer_decode(a, nw, wr, wsg, rb, sb, ids, wts, logits, sl, workspace=ws)
+        l4, i4, w4 = _moe_layer_four_launches(b, nw, wr, wsg, rb, sb, 8, stream)
+        torch.cuda.synchronize(cuda)
+        assert torch.equal(logits, l4), f"call {step}: router logits differ"
+        assert torch.equal(ids, i4) and torch.equal(wts, w4), f"call {step}: selection differs"
+        assert torch.equal(a, b), f"call {step}: residual differs"
+    # the barrier words are back at rest: count 0
+    bar = ws[-256:].view(torch.int32)
+    assert int(bar[0].item()) == 0
+
+
 def test_moe_decode_without_shared_and_accumulate(cuda, config1):
     import torch
     from engine.ops import moe_expert_ffn

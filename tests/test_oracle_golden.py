@@ -139,3 +139,21 @@ def test_u4_gemv_fast_and_precise_agree():
     a = oracle.u4_gemv(x, w, s, z, 128, precise=True)
     b = oracle.u4_gemv(x, w, s, z, 128, precise=False)
     assert max_rel_err(b, a) < 1e-5
+
+
+def test_model_lazy_expert_banks_equal_materialised(monkeypatch):
+    """The checker's full-size model regenerates only the selected experts per
+    step (counter-based generator); a one-layer, 256-expert model must give the
+    same greedy tokens and logits, bit for bit, as with every expert held."""
+    cfg = dict(hidden=2048, layers=1, attn_interval=4, nq=16, nkv=2, head_dim=256, rope_dim=64,
+               nk=16, nv=32, dk=128, conv=4, experts=256, topk=8, inter=512, shared_inter=512,
+               vocab=4096, group=128, rope_base=1e7, eps=1e-6)
+    runs = {}
+    for lazy in ("0", "1"):
+        monkeypatch.setenv("IQ36_ORACLE_LAZY", lazy)
+        m = oracle.OracleModel(cfg, 5, 16)
+        runs[lazy] = [m.step(t, pos) for pos, t in enumerate([3, 77, 1000])]
+        m.close()
+    for (ta, la), (tb, lb) in zip(runs["0"], runs["1"]):
+        assert ta == tb
+        np.testing.assert_array_equal(la, lb)
