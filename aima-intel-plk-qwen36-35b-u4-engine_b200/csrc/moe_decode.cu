@@ -444,8 +444,8 @@ size_t moe_decode_ws(int k, int hidden, int intermediate) {
   return (((size_t)(k + 1) * intermediate * 2) + 255) / 256 * 256;
 }
 
-// Layer workspace: the SwiGLU activations [k+1, I] fp16, then 256 bytes of
-// grid-barrier words for the one-launch form (zero before first use).
+// Layer workspace: the SwiGLU activations [k+1, I] fp16, then 256 bytes
+// holding the one-launch form's grid-barrier counter (zero before first use).
 size_t moe_layer_ws(int k, int hidden, int intermediate) {
   return moe_decode_ws(k, hidden, intermediate) + 256;
 }
@@ -561,12 +561,17 @@ int moe_decode_launch(const void* x_f16, const float* x_f32, const float* nw, fl
 // moe_gate_up_kernel<128, true> with a 4-way K split, moe_down_kernel<128,
 // true>), so both forms produce the same bits.
 //
-// Grid barrier: {count, generation} words in the caller's workspace (zeroed
-// before first use). A CTA reads the generation, then adds itself to the
-// count; the last arrival resets the count and publishes generation + 1, so
-// the words are back in their resting state after every barrier and across
-// launches. Waits are bounded (kWaitLimitNs): on expiry the CTA counts a
-// timeout (iq36_wait_timeouts) and skips the rest of its work.
+// Grid barrier: one 64-bit arrival counter in the caller's workspace (zero
+// before first use). It only grows: every launch adds exactly 2 x gridDim
+// arrivals, so after its griddepcontrol.wait (the previous launch sharing the
+// workspace has completed) a CTA reads the counter and rounds it down to a
+// multiple of gridDim — fewer than gridDim arrivals of this launch can
+// precede that read — to get the launch's base; barrier j is passed when the
+// counter reaches base + j * gridDim. An arrival is one fire-and-forget
+// red.release after the CTA's bar.sync (release is cumulative over the
+// writes that bar.sync ordered before it); waiters poll with ld.acquire.
+// Waits are bounded (kWaitLimitNs): on expiry the CTA counts a timeout
+// (iq36_wait_timeouts) and skips the rest of its work.
 
 constexpr int kLayerThreads = 512;  // 16 warps = 4 gate_up quads
 constexpr int kLayerQuads = kLayerThreads / 128;
@@ -585,8 +590,8 @@ struct LayerArgs {
   float* slogit;
   int32_t* ids_out;
   float* wts_out;
-  __half* act;     // [n_slots, I] SwiGLU activations (workspace)
-  unsigned* bar;   // grid barrier words (workspace)
+  __half* act;               // [n_slots, I] SwiGLU activations (workspace)
+  unsigned long long* bar;   // grid-barrier arrival counter (workspace)
 };
 
 struct LayerSmem {
@@ -601,33 +606,152 @@ __host__ __device__ inline LayerSmem layer_smem(int H, int I, int n_slots) {
   s.act = s.xperm + H * 2;
   s.logit = s.act + n_slots * I * 2;
   s.stage = (s.logit + 256 * 4 + 127) / 128 * 128;
-  s.slot_bytes = 8 * I + 40 * ngi;  // 16 rows: codes, scales, zero points
+  // 16 rows per slot: codes [16][I/2] (one bulk copy), scales [16][ngi],
+  // zero points [16*ngi/2]
+  s.slot_bytes = 8 * I + 40 * ngi;
   s.total = s.stage + n_slots * s.slot_bytes;
   return s;
 }
 
-__device__ __forceinline__ unsigned layer_bar_arrive(unsigned* bar, unsigned nb) {
-  unsigned g0;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g0) : "l"(bar + 1) : "memory");
-  __threadfence();  // this CTA's writes (ordered before by bar.sync) before the arrival
-  if (atomicAdd(bar, 1u) == nb - 1) {
-    atomicExch(bar, 0u);
-    __threadfence();
-    asm volatile("st.release.gpu.global.u32 [%0], %1;\n" ::"l"(bar + 1), "r"(g0 + 1u) : "memory");
-  }
-  return g0;
+__host__ __device__ inline int down_pitch(int I) { return I / 2; }
+
+__device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__device__ __forceinline__ bool layer_bar_wait(const unsigned* bar, unsigned g0) {
+__device__ __forceinline__ void layer_bar_arrive(unsigned long long* bar) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], 1;\n" ::"l"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool layer_bar_wait(const unsigned long long* bar,
+                                               unsigned long long target) {
   uint64_t t0 = 0;
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    unsigned g;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(g) : "l"(bar + 1) : "memory");
-    if (g != g0) return true;
+    if (ld_acquire_u64(bar) >= target) return true;
     if (i == 0) t0 = globaltimer_ns();
     else if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
   return false;
+}
+
+// Top-k of the E <= 256 router logits in shared memory by the whole CTA, with
+// exactly the arithmetic of router_topk_warp: max, fp64 exp(l - max), the fp64
+// sum in that function's order (lane l adds elements l + 32i for i = 0..7,
+// then a butterfly over the lanes), probabilities rounded to fp32, the k
+// largest (probability bits, inverted id) keys in order, fp32 renormalisation
+// in rank order. The exponentials and divisions run one element per thread;
+// for k <= 8 the selection ranks a small candidate set in parallel, otherwise
+// warp 0 selects with two redux.sync rounds per rank. Ends with sel_id /
+// sel_w in shared memory and a __syncthreads.
+__device__ __forceinline__ void router_topk_cta(const float* l, int E, int k, double* ev,
+                                                uint64_t* key, float* red /* >= 80 floats */,
+                                                int32_t* sel_id, float* sel_w) {
+  uint64_t* ev_scratch = reinterpret_cast<uint64_t*>(ev);  // reused once the keys exist
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 256) {
+    const float v = tid < E ? l[tid] : -INFINITY;
+    const float m = warp_max(v);
+    if (lane == 0) red[warp] = m;
+  }
+  __syncthreads();
+  float mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  if (tid < 256) ev[tid] = tid < E ? exp((double)l[tid] - (double)mx) : 0.0;
+  __syncthreads();
+  // lane l's butterfly result divides the elements l + 32i, as in
+  // router_topk_warp (the lanes' sums may differ in the last bit)
+  double* lane_sum = reinterpret_cast<double*>(red) + 8;
+  if (warp == 0) {
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += ev[lane + 32 * i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    lane_sum[lane] = s;
+  }
+  __syncthreads();
+  if (tid < 256) {
+    const double s = lane_sum[tid & 31];
+    const float p = (float)(ev[tid] / s);
+    key[tid] = tid < E ? (((uint64_t)__float_as_uint(p) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)tid))
+                       : 0ull;
+  }
+  __syncthreads();
+  if (k <= 8) {
+    // Candidates: the smallest of the 8 per-warp maximum keys bounds the k-th
+    // largest key from below (8 distinct keys reach it), so the top k are
+    // among the keys at or above it — usually a few more than k. Each
+    // candidate counts the candidates above it: that count is its rank.
+    uint64_t* wmax = reinterpret_cast<uint64_t*>(red) + 24;  // [8]
+    int* ncand = reinterpret_cast<int*>(red) + 64;
+    uint64_t* cand = ev_scratch;
+    if (tid < 256) {
+      const uint64_t my = key[tid];
+      const uint32_t hi = __reduce_max_sync(0xffffffffu, (uint32_t)(my >> 32));
+      const uint32_t lo =
+          __reduce_max_sync(0xffffffffu, (uint32_t)(my >> 32) == hi ? (uint32_t)my : 0u);
+      if (lane == 0) wmax[warp] = ((uint64_t)hi << 32) | lo;
+    }
+    if (tid == 0) *ncand = 0;
+    __syncthreads();
+    if (tid < 256) {
+      uint64_t th = wmax[0];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) th = wmax[w] < th ? wmax[w] : th;
+      const uint64_t my = key[tid];
+      if (my >= th && my != 0ull) cand[atomicAdd(ncand, 1)] = my;
+    }
+    __syncthreads();
+    const int n = *ncand;
+    if (tid < n) {
+      const uint64_t my = cand[tid];
+      int r = 0;
+      for (int j = 0; j < n; ++j) r += cand[j] > my;
+      if (r < k) {
+        sel_id[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)my);
+        sel_w[r] = __uint_as_float((uint32_t)(my >> 32));
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float sum = 0.0f;
+      for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sel_w[r]);
+      const float den = fmaxf(sum, 6.103515625e-5f);
+      const float w = lane < k ? __fdiv_rn(sel_w[lane], den) : 0.f;
+      __syncwarp();
+      if (lane < k) sel_w[lane] = w;
+    }
+  } else if (warp == 0) {
+    uint64_t kk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kk[i] = key[lane + 32 * i];
+    float sum = 0.0f;
+    for (int r = 0; r < k; ++r) {
+      uint64_t best = 0ull;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) best = kk[i] > best ? kk[i] : best;
+      const uint32_t hi = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
+      const uint32_t lo =
+          __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32) == hi ? (uint32_t)best : 0u);
+      const uint64_t win = ((uint64_t)hi << 32) | lo;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (kk[i] == win) kk[i] = 0ull;
+      const float p = __uint_as_float(hi);
+      if (lane == 0) {
+        sel_id[r] = (int32_t)(0xFFFFFFFFu - lo);
+        sel_w[r] = p;
+      }
+      sum = __fadd_rn(sum, p);
+    }
+    const float den = fmaxf(sum, 6.103515625e-5f);
+    __syncwarp();
+    if (lane < k) sel_w[lane] = __fdiv_rn(sel_w[lane], den);
+  }
+  __syncthreads();
 }
 
 // Eight fp16 values into the permuted operand order of u4_core.cuh (odd
@@ -651,13 +775,14 @@ __device__ __forceinline__ uint4 perm8(const __half h[8]) {
 // as u4_load_chunk<128, 4> loads them from global memory.
 __device__ __forceinline__ void load_chunk_smem(U4Chunk<128, 4>& c, const uint8_t* st, int I,
                                                 int ngi, int g, int t) {
-  const __half* sc = reinterpret_cast<const __half*>(st + 8 * I);
-  const uint8_t* zp = st + 8 * I + 32 * ngi;
+  const int pitch = down_pitch(I);
+  const __half* sc = reinterpret_cast<const __half*>(st + 16 * pitch);
+  const uint8_t* zp = st + 16 * pitch + 32 * ngi;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int gi = min(u, ngi - 1);
-    const uint4 va = *reinterpret_cast<const uint4*>(st + g * (I / 2) + gi * 64 + t * 16);
-    const uint4 vb = *reinterpret_cast<const uint4*>(st + (g + 8) * (I / 2) + gi * 64 + t * 16);
+    const uint4 va = *reinterpret_cast<const uint4*>(st + g * pitch + gi * 64 + t * 16);
+    const uint4 vb = *reinterpret_cast<const uint4*>(st + (g + 8) * pitch + gi * 64 + t * 16);
     c.ra[u][0] = va.x; c.ra[u][1] = va.y; c.ra[u][2] = va.z; c.ra[u][3] = va.w;
     c.rb[u][0] = vb.x; c.rb[u][1] = vb.y; c.rb[u][2] = vb.z; c.rb[u][3] = vb.w;
     const int ea = g * ngi + gi, eb = (g + 8) * ngi + gi;
@@ -668,27 +793,94 @@ __device__ __forceinline__ void load_chunk_smem(U4Chunk<128, 4>& c, const uint8_
   }
 }
 
-// Bulk copies of rows h0..h0+15 of one expert's down matrix into a slot stage.
-__device__ __forceinline__ void issue_down_rows(const uint8_t* w, const __half* s, const uint8_t* z,
-                                                int64_t e, int H, int I, int h0, uint32_t dst,
-                                                uint32_t bar) {
+// Rows h0..h0+15 of one expert's down matrix into a slot stage: the codes
+// (16 x I/2 contiguous bytes) as one bulk copy completing on `bar` (issued by
+// the calling lane), the scales and zero points (2*ngi + ngi/2 16-byte
+// pieces) as cp.async pieces spread over the calling warp's lanes. Bulk
+// copies take no load/store-unit requests, which the gate_up loads saturate.
+__device__ __forceinline__ void down_codes_bulk(const uint8_t* w, int64_t e, int H, int I, int h0,
+                                                uint32_t dst, uint32_t bar) {
+  bulk_load(dst, w + (e * H + h0) * (I / 2), 8 * I, bar);
+}
+__device__ __forceinline__ void down_meta_async(const __half* s, const uint8_t* z, int64_t e,
+                                                int H, int I, int h0, uint8_t* dst, int piece) {
   const int ngi = I / 128;
   const int64_t row = e * H + h0;
-  bulk_load(dst, w + row * (I / 2), 16 * (I / 2), bar);
-  bulk_load(dst + 8 * I, s + row * ngi, 32 * ngi, bar);
-  bulk_load(dst + 8 * I + 32 * ngi, z + row * ngi / 2, 8 * ngi, bar);
+  if (piece < 2 * ngi)
+    cp_async_16(smem_u32(dst + 8 * I + piece * 16),
+                reinterpret_cast<const uint8_t*>(s + row * ngi) + piece * 16, 16);
+  else if (piece < 2 * ngi + ngi / 2)
+    cp_async_16(smem_u32(dst + 8 * I + 32 * ngi + (piece - 2 * ngi) * 16),
+                z + row * ngi / 2 + (piece - 2 * ngi) * 16, 16);
+}
+
+// One gate_up quarter-unit into registers, values as u4_load_chunk<128, 4>
+// loads them: the lane's codes of gate row rowA0 + g and up row rowB0 + g
+// over groups gb..gb+3 directly, while the 16 rows' scales (one 8-byte load
+// per row) and zero points (one 2-byte load per row) are fetched by lanes
+// 0..15 and handed to the lane groups by shuffles: 10 load requests per lane
+// instead of 24. quarter_issue only issues the loads (nothing waits on
+// them); quarter_finish does the shuffles, so it is called where the values
+// are about to be used.
+struct QuarterRaw {
+  uint2 sc;
+  uint32_t zz;
+};
+
+__device__ __forceinline__ void quarter_issue(U4Chunk<128, 4>& c, QuarterRaw& q, const uint8_t* w,
+                                              const __half* s, const uint8_t* z, int64_t zbase,
+                                              int rowA0, int rowB0, int H, int gb, int lane) {
+  const int g = lane >> 2, t = lane & 3, ng = H / 128;
+  const uint8_t* wA = w + (size_t)(rowA0 + g) * (H / 2) + t * 16;
+  const uint8_t* wB = w + (size_t)(rowB0 + g) * (H / 2) + t * 16;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint4 va = ld_stream_v4(wA + (gb + u) * 64);
+    const uint4 vb = ld_stream_v4(wB + (gb + u) * 64);
+    c.ra[u][0] = va.x; c.ra[u][1] = va.y; c.ra[u][2] = va.z; c.ra[u][3] = va.w;
+    c.rb[u][0] = vb.x; c.rb[u][1] = vb.y; c.rb[u][2] = vb.z; c.rb[u][3] = vb.w;
+  }
+  q.sc = make_uint2(0u, 0u);
+  q.zz = 0u;
+  if (lane < 16) {
+    const int row = lane < 8 ? rowA0 + lane : rowB0 + lane - 8;
+    q.sc = ld_stream_v2(s + (size_t)row * ng + gb);
+    const int64_t e0 = zbase + (int64_t)row * ng + gb;  // multiple of 4: 4 nibbles in 2 bytes
+    q.zz = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(z + (e0 >> 1)));
+  }
+}
+
+__device__ __forceinline__ void quarter_finish(U4Chunk<128, 4>& c, const QuarterRaw& q, int lane) {
+  const int g = lane >> 2;
+  const uint32_t sAx = __shfl_sync(0xffffffffu, q.sc.x, g), sAy = __shfl_sync(0xffffffffu, q.sc.y, g);
+  const uint32_t sBx = __shfl_sync(0xffffffffu, q.sc.x, g + 8),
+                 sBy = __shfl_sync(0xffffffffu, q.sc.y, g + 8);
+  const uint32_t zA = __shfl_sync(0xffffffffu, q.zz, g), zB = __shfl_sync(0xffffffffu, q.zz, g + 8);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t wa = u < 2 ? sAx : sAy, wb = u < 2 ? sBx : sBy;
+    c.sa[u] = __half2float(__ushort_as_half((unsigned short)(wa >> (16 * (u & 1)))));
+    c.sb[u] = __half2float(__ushort_as_half((unsigned short)(wb >> (16 * (u & 1)))));
+    c.za[u] = (zA >> (4 * u)) & 15u;
+    c.zb[u] = (zB >> (4 * u)) & 15u;
+  }
 }
 
 __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a) {
   extern __shared__ __align__(128) uint8_t lsm[];
   __shared__ float red[16][16];
-  __shared__ float nred[33];
+  __shared__ __align__(8) float nred[80];
+  __shared__ double s_ev[256];
+  __shared__ uint64_t s_key[256];
   __shared__ int32_t s_ids[16];
   __shared__ float s_wts[16];
-  __shared__ __align__(8) uint64_t mbar[2];  // 0: shared-slot down rows, 1: routed slots
+  __shared__ __align__(8) uint64_t mbar[2];  // down codes: 0 shared slot, 1 routed slots
   __shared__ int s_ok;
+  __shared__ unsigned long long s_base;
+  __shared__ float s_res[16];  // this CTA's residual rows h0..h0+15 (phase C)
   const ExpertArgs& e = a.e;
   const int H = e.H, I = e.I, ngi = I / 128, k = e.k, n_slots = e.n_slots;
+  const int ng = H / 128;
   const LayerSmem L = layer_smem(H, I, n_slots);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int cta = blockIdx.x, nb = gridDim.x;
@@ -702,12 +894,15 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
   const int j0 = (unit % ups) * 8;
   const int drb = nb - 1 - cta;  // down row block (the last H/16 CTAs)
   const bool has_down = drb < H / 16;
+  const bool shared_down = has_down && n_slots > k;
   const int h0 = drb * 16;
   const int n_rows = a.E + (a.w_sg != nullptr ? 1 : 0);
   const int rrow = cta + warp * nb;  // router row of this warp
   const bool has_row = rrow < n_rows;
-  const uint32_t sbase = smem_u32(lsm);
+  const int meta = 2 * ngi + ngi / 2;  // 16-byte scale / zero-point pieces per slot
   const uint32_t bar_s = smem_u32(&mbar[0]), bar_r = smem_u32(&mbar[1]);
+  uint8_t* stage = lsm + L.stage;
+  constexpr int kRes = 8;  // residual values per thread (threads < 256; H <= 2048)
 
   // ---- prologue: weights only (nothing here depends on earlier launches)
   if (tid == 0) {
@@ -716,9 +911,18 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
-  if (tid == 0 && has_down && n_slots > k) {
-    mbar_arrive_tx(bar_s, 8 * I + 40 * ngi);
-    issue_down_rows(e.sd_w, e.sd_s, e.sd_z, 0, H, I, h0, sbase + L.stage + k * L.slot_bytes, bar_s);
+  if (warp == k && shared_down) {
+    if (lane == 0) {
+      mbar_arrive_tx(bar_s, 8 * I);
+      down_codes_bulk(e.sd_w, 0, H, I, h0, smem_u32(stage + k * L.slot_bytes), bar_s);
+    }
+    down_meta_async(e.sd_s, e.sd_z, 0, H, I, h0, stage + k * L.slot_bytes, lane);
+    cp_async_commit();
+  }
+  float nwv[kRes];
+  if (tid < 256) {
+#pragma unroll
+    for (int m = 0; m < kRes; ++m) nwv[m] = tid + 256 * m < H ? a.nw[tid + 256 * m] : 0.f;
   }
   const __half* wr = nullptr;
   if (has_row) wr = rrow < a.E ? a.w_router + (size_t)rrow * H : a.w_sg;
@@ -732,39 +936,60 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     }
   }
   U4Chunk<128, 4> ch;
-  U4Rows rows{};
-  if (shared_unit) {
-    rows = gate_up_rows<128>(e, nullptr, uslot, j0, g);
-    u4_load_chunk<128, 4>(ch, rows, ks * 4, ks * 4 + 4, t);
-  }
+  QuarterRaw qr;
+  if (shared_unit)
+    quarter_issue(ch, qr, e.sgu_w, e.sgu_s, e.sgu_z, 0, j0, I + j0, H, ks * 4, lane);
   pdl_wait();
 
   // ---- phase A: x, router logits, shared expert gate_up
-  const float* res = a.residual;
+  if (tid == kLayerThreads - 32) {
+    // the barrier base, by a thread with no residual loads to delay
+    unsigned long long c0;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(c0) : "l"(a.bar) : "memory");
+    s_base = c0 / (unsigned long long)nb * nb;
+  }
+  float resv[kRes];
   {
     // the 256-thread reduction order of stage_x_plain / stage_x_perm
     if (tid < 256) {
       float ss = 0.f;
-      for (int i = tid; i < H; i += 256) ss = fmaf(res[i], res[i], ss);
+#pragma unroll
+      for (int m = 0; m < kRes; ++m) {
+        resv[m] = tid + 256 * m < H ? a.residual[tid + 256 * m] : 0.f;
+        if (tid + 256 * m < H) ss = fmaf(resv[m], resv[m], ss);
+      }
       ss = warp_sum(ss);
       if (lane == 0) nred[warp] = ss;
-    }
-    __syncthreads();
-    if (tid < 32) {
-      float v = lane < 8 ? nred[lane] : 0.f;
-      v = warp_sum(v);
-      if (lane == 0) nred[32] = rsqrtf(v / (float)H + a.eps);
-    }
-    __syncthreads();
-    const float scale = nred[32];
-    __half* xp = reinterpret_cast<__half*>(lsm + L.xplain);
-    uint4* xq = reinterpret_cast<uint4*>(lsm + L.xperm);
-    for (int c = tid; c < H / 8; c += kLayerThreads) {
-      __half h[8];
+      if (has_down) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(res[c * 8 + j] * scale * a.nw[c * 8 + j]);
-      *reinterpret_cast<uint4*>(xp + c * 8) = *reinterpret_cast<const uint4*>(h);
-      xq[c] = perm8(h);
+        for (int m = 0; m < kRes; ++m) {
+          const int i = tid + 256 * m;
+          if (i >= h0 && i < h0 + 16) s_res[i - h0] = resv[m];
+        }
+      }
+    }
+    __syncthreads();
+    // every warp sums the 8 warp totals as warp 0 of the 256-thread kernels
+    // did, and takes lane 0's butterfly result (the value those kernels used)
+    float v = lane < 8 ? nred[lane] : 0.f;
+    v = __shfl_sync(0xffffffffu, warp_sum(v), 0);
+    const float scale = rsqrtf(v / (float)H + a.eps);
+    // each value straight into both layouts: plain, and the permuted operand
+    // order of perm8 (element j of chunk c at half 2(j%4) + j/4, odd j / 16)
+    __half* xp = reinterpret_cast<__half*>(lsm + L.xplain);
+    __half* xq = reinterpret_cast<__half*>(lsm + L.xperm);
+    const __half sixteenth = __float2half_rn(0.0625f);
+    if (tid < 256) {
+#pragma unroll
+      for (int m = 0; m < kRes; ++m) {
+        const int i = tid + 256 * m;
+        if (i < H) {
+          const __half hv = __float2half_rn(resv[m] * scale * nwv[m]);
+          const int j = i & 7;
+          xp[i] = hv;
+          xq[(i & ~7) + 2 * (j & 3) + (j >> 2)] = (j & 1) ? __hmul(hv, sixteenth) : hv;
+        }
+      }
     }
     __syncthreads();
   }
@@ -794,17 +1019,19 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
       else a.slogit[0] = acc;
     }
   }
-  __syncthreads();
-  unsigned gen = 0;
-  if (tid == 0) gen = layer_bar_arrive(a.bar, nb);
+  __syncthreads();  // logits stored
+  if (tid == 0) layer_bar_arrive(a.bar);
   const uint4* xs = reinterpret_cast<const uint4*>(lsm + L.xperm);
   float accA = 0.f, accB = 0.f;
-  if (shared_unit) u4_compute_chunk<128, 4>(ch, xs, ks * 4, ks * 4 + 4, t, accA, accB);
+  if (shared_unit) {
+    quarter_finish(ch, qr, lane);
+    u4_compute_chunk<128, 4>(ch, xs, ks * 4, ks * 4 + 4, t, accA, accB);
+  }
   if (shared_unit && t == 0) {
     red[warp][g] = accA;
     red[warp][g + 8] = accB;
   }
-  if (tid == 0) s_ok = layer_bar_wait(a.bar, gen) ? 1 : 0;
+  if (tid == 0) s_ok = layer_bar_wait(a.bar, s_base + (unsigned long long)nb) ? 1 : 0;
   __syncthreads();
   if (shared_unit && ks == 0 && t == 0) {
     float ga = 0.f, ub = 0.f;
@@ -815,48 +1042,49 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     a.act[(size_t)uslot * I + j0 + g] = __float2half_rn(ga * sigmoidf_acc(ga) * ub);
   }
   if (!s_ok) {
-    // leave no bulk copy in flight into this CTA's shared memory
+    // leave no copy in flight into this CTA's shared memory
+    cp_async_wait<0>();
     if (tid == 0) {
       atomicAdd(&g_moe_wait_timeouts, 1);
-      if (has_down && n_slots > k) (void)mbar_wait(bar_s, 0);
+      if (shared_down) (void)mbar_wait(bar_s, 0);
     }
     return;
   }
 
   // ---- phase B: top-k, routed down copies, routed gate_up
+  float* sl = reinterpret_cast<float*>(lsm + L.logit);
+  if (tid < a.E) sl[tid] = __ldcg(a.logits + tid);
+  const float slogit = (n_slots > k && tid == 0) ? __ldcg(a.slogit) : 0.f;
+  router_topk_cta(sl, a.E, k, s_ev, s_key, nred, s_ids, s_wts);
+  const bool routed_unit = has_unit && !shared_unit;
+  if (routed_unit) {
+    const int64_t ex = s_ids[uslot];
+    quarter_issue(ch, qr, e.gu_w + ex * (2 * I) * (H / 2), e.gu_s + ex * (2 * I) * ng, e.gu_z,
+                  ex * (2 * I) * ng, j0, I + j0, H, ks * 4, lane);
+  }
+  // the down rows are needed only after barrier 2: issued after this warp's
+  // own gate_up loads
   if (warp == 0) {
-    float* sl = reinterpret_cast<float*>(lsm + L.logit);
-    for (int i = lane; i < a.E; i += 32) sl[i] = __ldcg(a.logits + i);
-    __syncwarp();
-    uint32_t sel_id[16];
-    float sel_w[16];
-    router_topk_warp(sl, a.E, k, sel_id, sel_w);
-    if (lane == 0) {
-      for (int r = 0; r < k; ++r) {
-        s_ids[r] = (int32_t)sel_id[r];
-        s_wts[r] = sel_w[r];
-      }
-      if (cta == 0) {
-        for (int r = 0; r < k; ++r) {
-          a.ids_out[r] = (int32_t)sel_id[r];
-          a.wts_out[r] = sel_w[r];
-        }
-      }
-      if (has_down) {
-        mbar_arrive_tx(bar_r, (uint32_t)k * (8 * I + 40 * ngi));
-        for (int r = 0; r < k; ++r)
-          issue_down_rows(e.d_w, e.d_s, e.d_z, (int64_t)sel_id[r], H, I, h0,
-                          sbase + L.stage + r * L.slot_bytes, bar_r);
-      }
+    if (cta == 0 && lane < k) {
+      a.ids_out[lane] = s_ids[lane];
+      a.wts_out[lane] = s_wts[lane];
+    }
+    if (has_down) {
+      if (lane == 0) mbar_arrive_tx(bar_r, (uint32_t)k * 8 * I);
+      __syncwarp();
+      if (lane < k)
+        down_codes_bulk(e.d_w, (int64_t)s_ids[lane], H, I, h0,
+                        smem_u32(stage + lane * L.slot_bytes), bar_r);
+      for (int p = lane; p < k * meta; p += 32)
+        down_meta_async(e.d_s, e.d_z, (int64_t)s_ids[p / meta], H, I, h0,
+                        stage + (p / meta) * L.slot_bytes, p % meta);
+      cp_async_commit();
     }
   }
-  __syncthreads();
-  const bool routed_unit = has_unit && !shared_unit;
   accA = 0.f;
   accB = 0.f;
   if (routed_unit) {
-    rows = gate_up_rows<128>(e, s_ids, uslot, j0, g);
-    u4_load_chunk<128, 4>(ch, rows, ks * 4, ks * 4 + 4, t);
+    quarter_finish(ch, qr, lane);
     u4_compute_chunk<128, 4>(ch, xs, ks * 4, ks * 4 + 4, t, accA, accB);
     if (t == 0) {
       red[warp][g] = accA;
@@ -873,14 +1101,15 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     a.act[(size_t)uslot * I + j0 + g] = __float2half_rn(ga * sigmoidf_acc(ga) * ub);
   }
   __syncthreads();
-  if (tid == 0) gen = layer_bar_arrive(a.bar, nb);
+  if (tid == 0) layer_bar_arrive(a.bar);
   if (!has_down) return;
-  if (tid == 0) s_ok = layer_bar_wait(a.bar, gen) ? 1 : 0;
+  if (tid == 0) s_ok = layer_bar_wait(a.bar, s_base + 2ull * nb) ? 1 : 0;
   __syncthreads();
   if (!s_ok) {
+    cp_async_wait<0>();
     if (tid == 0) {
       atomicAdd(&g_moe_wait_timeouts, 1);
-      if (n_slots > k) (void)mbar_wait(bar_s, 0);
+      if (shared_down) (void)mbar_wait(bar_s, 0);
       (void)mbar_wait(bar_r, 0);
     }
     return;
@@ -894,13 +1123,15 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(a.act) + c);
     xa[c] = perm8(reinterpret_cast<const __half*>(&raw));
   }
+  cp_async_wait<0>();  // scale / zero-point pieces (warps 0 and k issued them)
+  if (tid == 0) nred[33] = slogit;
   __syncthreads();
   if (warp < n_slots) {
     const bool got = mbar_wait(warp < k ? bar_r : bar_s, 0);
     accA = 0.f;
     accB = 0.f;
     if (got) {
-      load_chunk_smem(ch, lsm + L.stage + warp * L.slot_bytes, I, ngi, g, t);
+      load_chunk_smem(ch, stage + warp * L.slot_bytes, I, ngi, g, t);
       u4_compute_chunk<128, 4>(ch, xa + (size_t)warp * (I / 8), 0, ngi, t, accA, accB);
     } else if (lane == 0) {
       atomicAdd(&g_moe_wait_timeouts, 1);
@@ -915,8 +1146,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     const int row = h0 + tid;
     float y = 0.0f;
     for (int j = 0; j < k; ++j) y = __fadd_rn(y, __fmul_rn(red[j][tid], s_wts[j]));
-    if (n_slots > k) y = __fadd_rn(y, __fmul_rn(red[k][tid], sigmoidf_acc(__ldcg(a.slogit))));
-    a.residual[row] = a.residual[row] + __half2float(__float2half_rn(y));
+    if (n_slots > k) y = __fadd_rn(y, __fmul_rn(red[k][tid], sigmoidf_acc(nred[33])));
+    // s_res: this CTA's rows as read in phase A (no CTA writes the residual
+    // before barrier 2)
+    a.residual[row] = s_res[tid] + __half2float(__float2half_rn(y));
   }
 }
 
@@ -929,9 +1162,12 @@ static bool layer_fused_ok(const iq36_expert_bank* r, const iq36_expert_bank* s,
   if (r->group != 128 || H % 512 || H > 2048 || I % 256 || I > 512 || E > 256 || k > 15)
     return false;
   if (n_slots * (I / 8) > kLayerQuads * sms || H / 16 > sms || E + 1 > 16 * sms) return false;
-  if (!aligned(r->down_scale, 16) || !aligned(r->down_zp, 16)) return false;
+  if (!aligned(r->down_scale, 16) || !aligned(r->down_zp, 16) || !aligned(r->gate_up_scale, 8) ||
+      !aligned(r->gate_up_zp, 2))
+    return false;
   if (s && (!aligned(s->down_weight, 16) || !aligned(s->down_scale, 16) ||
-            !aligned(s->down_zp, 16)))
+            !aligned(s->down_zp, 16) || !aligned(s->gate_up_scale, 8) ||
+            !aligned(s->gate_up_zp, 2)))
     return false;
   return layer_smem(H, I, n_slots).total <= 200 * 1024;
 }
@@ -1156,8 +1392,8 @@ extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const floa
     la.ids_out = ids;
     la.wts_out = weights;
     la.act = reinterpret_cast<__half*>(workspace);
-    la.bar = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
-                                         moe_decode_ws(k, hidden, routed->intermediate));
+    la.bar = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) +
+                                                   moe_decode_ws(k, hidden, routed->intermediate));
     const LayerSmem L = layer_smem(hidden, routed->intermediate, a.n_slots);
     const cudaError_t e =
         launch(moe_layer_kernel, dim3(sms), dim3(kLayerThreads), (size_t)L.total, s, la);

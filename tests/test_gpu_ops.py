@@ -229,9 +229,10 @@ def test_moe_layer_one_launch_equals_four_launches(cuda, config1):
         assert torch.equal(logits, l4), f"call {step}: router logits differ"
         assert torch.equal(ids, i4) and torch.equal(wts, w4), f"call {step}: selection differs"
         assert torch.equal(a, b), f"call {step}: residual differs"
-    # the barrier words are back at rest: count 0
-    bar = ws[-256:].view(torch.int32)
-    assert int(bar[0].item()) == 0
+    # the grid-barrier counter took exactly two arrivals per CTA per call
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    bar = ws[-256:].view(torch.int64)
+    assert int(bar[0].item()) == 6 * 2 * sms
 
 
 def test_moe_decode_without_shared_and_accumulate(cuda, config1):
