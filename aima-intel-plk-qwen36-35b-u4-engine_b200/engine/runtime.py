@@ -241,10 +241,12 @@ class Qwen36Runtime:
         self._pf: dict | None = None  # batched-prefill buffers (sized on first use)
         # Optional step trace (tests): when set before capture(), every step
         # also copies the residual entering each layer (and leaving the last)
-        # into trace [layers + 1, hidden] and each layer's routed ids into
-        # trace_ids [layers, topk].
+        # into trace [layers + 1, hidden], each layer's routed ids into
+        # trace_ids [layers, topk] and its router logits into trace_router
+        # [layers, experts].
         self.trace: torch.Tensor | None = None
         self.trace_ids: torch.Tensor | None = None
+        self.trace_router: torch.Tensor | None = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.stream = torch.cuda.Stream(device=dev)
         self.launches_per_step = 0
@@ -274,6 +276,7 @@ class Qwen36Runtime:
             n += self.enqueue_layer(l)
             if self.trace is not None:
                 self.trace_ids[l].copy_(self.b_ids)
+                self.trace_router[l].copy_(self.b_logits_r)
         if self.trace is not None:
             self.trace[c.layers].copy_(self.hres)
         ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,

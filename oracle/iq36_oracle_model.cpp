@@ -261,28 +261,29 @@ void orc_model_destroy(void* m) { delete static_cast<Model*>(m); }
 // positions < pos). Writes fp32 logits [vocab] when logits != NULL and returns
 // the greedy token.
 int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads, int lm_head,
-                       float* hidden, int32_t* ids_out);
+                       float* hidden, int32_t* ids_out, float* router_out);
 
 int orc_model_step(void* mp, int token, int pos, float* logits, int threads) {
-  return orc_model_step_opt(mp, token, pos, logits, threads, 1, nullptr, nullptr);
+  return orc_model_step_opt(mp, token, pos, logits, threads, 1, nullptr, nullptr, nullptr);
 }
 
 // The step without the final norm and LM head (returns -1): feeds a prompt
 // token whose next-token distribution is not needed.
 int orc_model_feed(void* mp, int token, int pos, int threads) {
-  return orc_model_step_opt(mp, token, pos, nullptr, threads, 0, nullptr, nullptr);
+  return orc_model_step_opt(mp, token, pos, nullptr, threads, 0, nullptr, nullptr, nullptr);
 }
 
 // The step with its trace: hidden [(layers + 1) * hidden] receives the fp32
 // residual stream entering each layer and, last, leaving the final layer;
-// ids_out [layers * topk] the routed expert ids of every layer (rank order).
+// ids_out [layers * topk] the routed expert ids of every layer (rank order);
+// router_out [layers * experts] every layer's router logits.
 int orc_model_step_trace(void* mp, int token, int pos, float* logits, int threads, float* hidden,
-                         int32_t* ids_out) {
-  return orc_model_step_opt(mp, token, pos, logits, threads, 1, hidden, ids_out);
+                         int32_t* ids_out, float* router_out) {
+  return orc_model_step_opt(mp, token, pos, logits, threads, 1, hidden, ids_out, router_out);
 }
 
 int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads, int lm_head,
-                       float* hidden, int32_t* ids_out) {
+                       float* hidden, int32_t* ids_out, float* router_out) {
   Model& M = *static_cast<Model*>(mp);
   const OrcModelConfig& c = M.c;
   const int H = c.hidden, G = c.group;
@@ -352,6 +353,8 @@ int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads,
     orc_f16_linear(x2.data(), H, L.sgate.data(), 1, &sl);
     orc_router_select(lg.data(), 1, c.experts, c.topk, ids.data(), w.data());
     if (ids_out) std::memcpy(ids_out + (int64_t)l * c.topk, ids.data(), sizeof(int32_t) * c.topk);
+    if (router_out)
+      std::memcpy(router_out + (int64_t)l * c.experts, lg.data(), sizeof(float) * c.experts);
     if (M.lazy) {
       // the selected experts' rows into slots 0..k-1, then index by slot
       for (int r = 0; r < c.topk; ++r) {

@@ -67,7 +67,7 @@ def port() -> ctypes.CDLL:
         lib.orc_model_feed.argtypes = [c_void_p, c_int, c_int, c_int]
         lib.orc_model_feed.restype = c_int
         lib.orc_model_step_trace.argtypes = [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
-                                             c_void_p]
+                                             c_void_p, c_void_p]
         lib.orc_model_step_trace.restype = c_int
         lib.orc_synth_fill.argtypes = [c_void_p, c_int64, c_int, c_uint64, c_uint64, c_float,
                                        c_float]
@@ -278,14 +278,16 @@ class OracleModel:
 
     def step_trace(self, token: int, pos: int, threads: int = 0):
         """step() plus its trace: the fp32 residual entering every layer and
-        leaving the last ([layers + 1, hidden]) and the routed ids [layers, topk]."""
+        leaving the last ([layers + 1, hidden]), the routed ids [layers, topk]
+        and the router logits [layers, experts]."""
         c = self.cfg
         logits = np.empty(self.vocab, np.float32)
         hidden = np.empty((c.layers + 1, c.hidden), np.float32)
         ids = np.empty((c.layers, c.topk), np.int32)
+        router = np.empty((c.layers, c.experts), np.float32)
         tok = port().orc_model_step_trace(self.h, token, pos, _p(logits), threads, _p(hidden),
-                                          _p(ids))
-        return tok, logits, hidden, ids
+                                          _p(ids), _p(router))
+        return tok, logits, hidden, ids, router
 
     def feed(self, token: int, pos: int, threads: int = 0) -> None:
         """A step without the LM head (a prompt token whose logits are not needed)."""

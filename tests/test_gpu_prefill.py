@@ -53,7 +53,7 @@ def test_prefill_small_all_tokens(cuda):
         assert_close(got[t], ref[t], f"prefill token {t}")
 
 
-@pytest.mark.parametrize("T", [4096])
+@pytest.mark.parametrize("T", [4096, 16384])
 def test_prefill_config3_sampled(cuda, T):
     got, ref, ids, _ = _run(cuda, T=T, E=256, seed=T, sample=24)
     counts = np.bincount(ids.ravel(), minlength=256)
@@ -142,3 +142,23 @@ def test_prefill_rows_contributions_combine_to_the_grouped_result(cuda):
     empty = torch.empty(0, dtype=torch.int32, device=cuda)
     got = moe_prefill_rows(x, empty, empty, empty.float(), bank)
     assert got.shape == (0, 2048)
+
+
+def test_prefill_16384_rows_independent_of_batch(cuda):
+    """Size-independent property at BASELINE's largest T: a token's output
+    depends only on its own row and routing, so the 16384-token call equals,
+    bit for bit, the two 8192-token halves run separately (different tile
+    packing, schedule and grid)."""
+    import torch
+    from engine.ops import moe_expert_ffn_prefill, router_select
+    rng = np.random.default_rng(16384)
+    bank = bank_to_torch(make_bank(rng, 256, 2048, 512), cuda)
+    logits = _t(zipf_router_logits(rng, 16384, 256), cuda)
+    ids, wts = router_select(logits, 8)
+    x = torch.randn(16384, 2048, device=cuda).to(torch.bfloat16)
+    full = moe_expert_ffn_prefill(x, ids, wts, bank)
+    a = moe_expert_ffn_prefill(x[:8192].contiguous(), ids[:8192].contiguous(),
+                               wts[:8192].contiguous(), bank)
+    b = moe_expert_ffn_prefill(x[8192:].contiguous(), ids[8192:].contiguous(),
+                               wts[8192:].contiguous(), bank)
+    assert torch.equal(full[:8192], a) and torch.equal(full[8192:], b)
