@@ -51,6 +51,9 @@ BASELINE = json.loads((ROOT / "BASELINE.json").read_text())
 METRIC = BASELINE["metric"]
 PREFILL_CHUNK = 16384  # tokens per batched-prefill launch sequence (Qwen36Runtime default)
 DECODE_GEMV_TRAFFIC = 11551662  # B per launch, ncu dram__bytes_read+write over one step's 81
+# B per launch, ncu dram__bytes_read + dram__bytes_write of moe_layer_kernel at the config-1 /
+# config-4 layer shape (profiles/moe_layer_decode_config1.md): 15,857,152 read, 0 written
+DECODE_MOE_TRAFFIC = 15857152
 PUBLISHED_DECODE_4K = 50.57  # reference's published figure: Arc B390, 4k prompt, batch-1 decode tok/s
 PUBLISHED_PREFILL = {4096: 2367.89, 32768: 2065.28}  # reference prefill tok/s, Arc B390
 
@@ -64,7 +67,12 @@ def peaks() -> tuple[float, str]:
 
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and clock-event reasons sampled DURING the timed region.
+
+    An NVML thread polls every ~1 ms (a decode timed region can last only tens
+    of milliseconds; nvidia-smi's loop mode samples every 100 ms at best), on
+    the GPU that holds this process's CUDA device (matched by PCI bus id);
+    falls back to an `nvidia-smi -lms 100` subprocess when NVML is missing."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -74,8 +82,47 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.path = None
+        self.thread = None
+        self.rows: list[tuple[int, int]] = []
+        self.max_mhz = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
+        import threading
+        try:
+            import pynvml
+            h = self._nvml_handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return self._start_smi()
+        self.stop_flag = threading.Event()
+
+        def poll():
+            while not self.stop_flag.is_set():
+                try:
+                    self.rows.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                      pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:
+                    pass
+                time.sleep(0.001)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.rows and time.time() - t0 < 2.0:
+            time.sleep(0.001)
+
+    def _start_smi(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -86,13 +133,24 @@ class ClockSampler:
         except OSError:
             self.proc = None
             return
-        # nvidia-smi takes a moment to start: wait for its first sample so the
-        # samples cover the timed region that follows.
         t0 = time.time()
         while time.time() - t0 < 5.0 and os.path.getsize(self.path) == 0:
             time.sleep(0.02)
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            import pynvml
+            self.stop_flag.set()
+            self.thread.join()
+            bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            sm = sorted(r[0] for r in self.rows)
+            reasons = sorted(n for n, b in bits.items() if any(r[1] & b for r in self.rows))
+            return {"sm_mhz": float(sm[len(sm) // 2]) if sm else None,
+                    "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None,
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml 1 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -110,7 +168,7 @@ class ClockSampler:
                         reasons.add(n)
         return {"sm_mhz": sm[len(sm) // 2] if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi 100 ms"}
 
 
 # ---------------------------------------------------------------------------
@@ -145,39 +203,62 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 # ---------------------------------------------------------------------------
-def cpu_baseline(ctx: int, threads: int) -> dict:
-    """Time the CPU restatement on a bounded sample of the decode step: a
-    4-layer slice (3 DeltaNet + 1 attention, all 256 experts, full vocab) and a
-    0-layer model (embedding + LM head), plus the attention op at ctx; the
-    40-layer step is extrapolated as t0 + 10 * (t4 - t0) + 10 * t_attn(ctx)."""
+def _oracle_timing_model(layers: int):
+    """The CPU restatement (oracle/) of a `layers`-layer slice of the config-4
+    model with every expert held in host memory, as the reference's CPU model
+    holds its weights (the checker's lazy mode, which regenerates the selected
+    experts each step, is off: that cost is not the reference's). The banks
+    are timing banks: one generated expert copied to all 256, so each step
+    still reads 8 + 1 distinct experts' bytes per layer."""
+    from engine.runtime import ModelConfig
+    from oracle import oracle
+    env = {"IQ36_ORACLE_LAZY": "0", "IQ36_ORACLE_REPLICATED": "1"}
+    prev = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        return oracle.OracleModel(ModelConfig(layers=layers).as_dict(), 1234, 64)
+    finally:
+        for k, v in prev.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
+
+
+def cpu_sample(ctx: int, threads: int, steps: int, warm: int) -> dict:
+    """Time the CPU restatement on a bounded sample of the decode step: the
+    median of `steps` timed decode steps (after `warm` untimed ones) of a
+    4-layer slice (3 DeltaNet + 1 GQA layer, 256 experts, full vocab) and of a
+    0-layer model (embedding + LM head), plus one config-2 paged attention at
+    ctx; per token t0 + 10 (t4 - t0) + 10 t_attn(ctx). Medians over 12 steps
+    keep the sample within a few percent run to run (the 10x extrapolation
+    of a 3-step mean varied by 30%)."""
     import numpy as np
     from engine.runtime import ModelConfig
     from oracle import oracle
-
     full = ModelConfig()
-    c4 = ModelConfig(layers=4).as_dict()
-    c0 = ModelConfig(layers=0).as_dict()
-    m4 = oracle.OracleModel(c4, 1234, 32)
-    m0 = oracle.OracleModel(c0, 1234, 32)
     rng = np.random.default_rng(0)
-    toks = rng.integers(0, full.vocab, 8).tolist()
+    toks = rng.integers(0, full.vocab, steps + warm + 1).tolist()
 
-    def tstep(m, n):
-        m.step(toks[0], 0, want_logits=False, threads=threads)  # warm
-        t = time.perf_counter()
-        for i in range(n):
-            m.step(toks[i + 1], i + 1, want_logits=False, threads=threads)
-        return (time.perf_counter() - t) / n
+    def timed(layers):
+        m = _oracle_timing_model(layers)
+        for i in range(warm):
+            m.step(toks[i], i, want_logits=False, threads=threads)
+        ts = []
+        for i in range(warm, warm + steps):
+            t = time.perf_counter()
+            m.step(toks[i], i, want_logits=False, threads=threads)
+            ts.append(time.perf_counter() - t)
+        m.close()
+        return float(np.median(ts))
 
-    t4 = tstep(m4, 3)
-    t0 = tstep(m0, 3)
-    m4.close()
-    m0.close()
+    t4, t0 = timed(4), timed(0)
     q = rng.standard_normal((16, 256)).astype(np.float16)
     nblk = (ctx + 15) // 16
     kc = rng.standard_normal((nblk, 16, 2, 256)).astype(np.float16)
     vc = rng.standard_normal((nblk, 16, 2, 256)).astype(np.float16)
     bt = np.arange(nblk, dtype=np.int32)
+    oracle.paged_gqa(q, kc, vc, bt, ctx, 1 / 16, threads=threads)  # warm
     t = time.perf_counter()
     oracle.paged_gqa(q, kc, vc, bt, ctx, 1 / 16, threads=threads)
     ta = time.perf_counter() - t
@@ -185,32 +266,40 @@ def cpu_baseline(ctx: int, threads: int) -> dict:
     per_tok = t0 + (full.layers / 4) * (t4 - t0) + n_attn * ta
     return {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": threads,
             "kind": "port",
-            "sample": (f"3 decode steps of a 4-layer slice (3 DeltaNet + 1 GQA, 256 experts) and "
-                       f"of a 0-layer model (LM head), plus one {ctx}-token attention, "
-                       f"extrapolated to 40 layers: {per_tok * 1e3:.1f} ms/token")}
+            "sample": (f"median of {steps} decode steps (after {warm} warm-up) of a 4-layer slice "
+                       f"(3 DeltaNet + 1 GQA, 256 experts) and of a 0-layer model (LM head), plus "
+                       f"one {ctx}-token paged attention, extrapolated to 40 layers: "
+                       f"{t0 * 1e3:.1f} + 10 x {(t4 - t0) * 1e3:.1f} + {n_attn} x "
+                       f"{ta * 1e3:.2f} = {per_tok * 1e3:.1f} ms/token")}
+
+
+def cpu_baseline(ctx: int, threads: int) -> dict:
+    return cpu_sample(ctx, threads, steps=12, warm=1)
 
 
 # ---------------------------------------------------------------------------
 def run_reference(args, world, rank) -> None:
+    """The reference path's CPU implementation (the oracle port; OpenVINO is not
+    installable here) on all host threads: the same bounded sample as the
+    cpu_baseline of the default line (cpu_sample), with --warmup untimed and
+    --steps timed steps per slice, bounded to 2 and 12 so the run stays within
+    a few minutes."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    steps = max(1, args.steps)
-    vals = []
-    for _ in range(max(1, min(args.warmup, 1))):
-        cpu_baseline(args.ctx, threads)  # warm-up sample (untimed)
+    warm = max(1, min(args.warmup, 2))
+    steps = max(3, min(args.steps, 12))
     t = time.perf_counter()
-    for _ in range(min(steps, 2)):
-        vals.append(cpu_baseline(args.ctx, threads))
+    v = cpu_sample(args.ctx, threads, steps=steps, warm=warm)
     elapsed = time.perf_counter() - t
-    v = vals[-1]
     line = {
         "impl": "reference", "metric": METRIC, "value": v["value"], "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": len(vals), "warmup": 1,
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
         "ms_per_step": round(1e3 / v["value"], 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": round(v["value"] / PUBLISHED_DECODE_4K, 4), "dtype": "u4xf16",
         "data": "synthetic",
-        "config": {"workload": f"config4 batch-1 decode, ctx {args.ctx}",
+        "config": {"workload": f"config4 batch-1 greedy decode after a {args.ctx}-token prompt "
+                               "(Qwen3.6-35B-A3B-shaped, random-init u4 g128)",
                    "note": "OpenVINO CPU u4 path unavailable here (not installable); the "
                            "reference arm is the CPU restatement in oracle/",
                    "wall_s": round(elapsed, 2)},
@@ -219,6 +308,136 @@ def run_reference(args, world, rank) -> None:
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# The rest of BASELINE's metric, measured after the decode timed region of the
+# default line (rank 0 at N = 1): each on its own small budget.
+
+def _device_time(fn, reps, dev, flush=None) -> float:
+    """Mean seconds per call of fn() over reps calls (CUDA events on the
+    current stream; L2 flushed before each call when flush is given)."""
+    import torch
+    tot = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize(dev)
+        tot += s.elapsed_time(e) / 1e3
+    return tot / reps
+
+
+def part_gemv_config0(dev) -> dict:
+    """1024 x 2048 u4 g128 GEMV, 512 weight copies rotated
+    in one CUDA graph of 512 launches (as --workload gemv)."""
+    import ctypes
+    import torch
+    from engine import _native as N
+    from engine import ops
+    rows, K, G, copies = 1024, 2048, 128, 512
+    one = rows * K // 2 + rows * (K // G) * 2 + rows * (K // G) // 2
+    step_bytes = one + K * 2 + rows * 4
+    w = torch.empty(copies, rows, K // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(copies, rows, K // G, dtype=torch.float16, device=dev)
+    z = torch.empty(copies, rows * (K // G) // 2, dtype=torch.uint8, device=dev)
+    ops.synth_fill(w, 0, 11, 1, 0, 0)
+    ops.synth_fill(sc, 1, 11, 2, 0.005, 0.02)
+    ops.synth_fill(z, 0, 11, 3, 0, 0)
+    x = torch.randn(K, device=dev).to(torch.float16)
+    out = torch.empty(rows, dtype=torch.float32, device=dev)
+    mats = [N.U4Matrix(w[c].data_ptr(), sc[c].data_ptr(), z[c].data_ptr(), rows)
+            for c in range(copies)]
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        for c in range(copies):
+            N.call("iq36_u4_gemv", x.data_ptr(), K, G, ctypes.byref(mats[c]), out.data_ptr(), 0,
+                   cap.cuda_stream)
+    graph.replay()
+    t = _device_time(graph.replay, 3, dev) / copies
+    hbm, src = peaks()
+    gbs = step_bytes / t / 1e9
+    del graph
+    return {"gemv_config0_gbs": round(gbs, 1), "gemv_config0_frac": round(gbs / hbm, 4),
+            "gemv_config0_us": round(t * 1e6, 3)}
+
+
+def part_moe_prefill_config3(dev, T: int = 4096) -> dict:
+    """BASELINE config 3 at T tokens: grouped MoE prefill, L2 flushed before
+    each call; tensor roofline against the measured bf16 peak."""
+    import ctypes
+    import numpy as np
+    import torch
+    from engine import _native as N
+    from engine import ops
+    E, H, I, k = 256, 2048, 512, 8
+    t = [torch.empty(E, 2 * I, H // 2, dtype=torch.uint8, device=dev),
+         torch.empty(E, 2 * I, H // 128, dtype=torch.float16, device=dev),
+         torch.empty(E, 2 * I * H // 256, dtype=torch.uint8, device=dev),
+         torch.empty(E, H, I // 2, dtype=torch.uint8, device=dev),
+         torch.empty(E, H, I // 128, dtype=torch.float16, device=dev),
+         torch.empty(E, H * I // 256, dtype=torch.uint8, device=dev)]
+    for j, v in enumerate(t):
+        ops.synth_fill(v, 1 if v.dtype == torch.float16 else 0, 77, 1000 + j, 0.005, 0.02)
+    bank = ops.ExpertBank(*t, 128)
+    rng = np.random.default_rng(T)
+    zw = (rng.permutation(E) + 1).astype(np.float64) ** -1.1
+    bias = -2 + 4 * (zw - zw.min()) / (zw.max() - zw.min())
+    logits = torch.from_numpy((rng.standard_normal((T, E)) + bias).astype(np.float32)).to(dev)
+    ids, wts = ops.router_select(logits, k)
+    x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.float32, device=dev)
+    ws = torch.empty(N.lib().iq36_moe_prefill_workspace_bytes(T, k, E, H, I), dtype=torch.uint8,
+                     device=dev)
+    rb = bank.c()
+    stream = torch.cuda.current_stream(dev)
+
+    def call():
+        N.call("iq36_moe_prefill", x.data_ptr(), T, ids.data_ptr(), wts.data_ptr(), k,
+               ctypes.byref(rb), out.data_ptr(), 0, ws.data_ptr(), ws.numel(),
+               stream.cuda_stream)
+
+    for _ in range(3):
+        call()
+    per = _device_time(call, 5, dev, flush=L2Flush(dev))
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    tf = T * 50331648 / per / 1e12
+    return {f"moe_prefill_config3_T{T}_tok_s": round(T / per, 1),
+            f"moe_prefill_config3_T{T}_tflops": round(tf, 1),
+            f"moe_prefill_config3_T{T}_frac": round(tf / peak, 4)}
+
+
+def part_long_context(weights, dev, ctx: int = 32768, steps: int = 32) -> dict:
+    """BASELINE config 4 at a 32768-token prompt: batched prefill tok/s, then
+    greedy decode tok/s at that context (CUDA-graph replays)."""
+    import torch
+    from engine.runtime import ModelConfig, Qwen36Runtime
+    cfg = ModelConfig()
+    rt = Qwen36Runtime(cfg, max_ctx=ctx + steps + 40, device=dev, weights=weights)
+    rt.capture()
+    gen = torch.Generator().manual_seed(32768)
+    prompt = torch.randint(0, cfg.vocab, (ctx,), generator=gen, dtype=torch.int32)
+    rt.prefill_batched(prompt, chunk=PREFILL_CHUNK)  # sizes the buffers
+    rt.reset()
+    torch.cuda.synchronize(dev)
+    t_pf = _device_time(lambda: rt.prefill_batched(prompt, chunk=PREFILL_CHUNK), 1, dev)
+    for _ in range(4):
+        rt.step()
+    t_dec = _device_time(lambda: [rt.step() for _ in range(steps)], 1, dev) / steps
+    out = {f"prefill_{ctx}_tok_s": round(ctx / t_pf, 1),
+           f"decode_ctx{ctx}_tok_s": round(1.0 / t_dec, 2),
+           f"decode_ctx{ctx}_ms_per_step": round(t_dec * 1e3, 4),
+           f"decode_ctx{ctx}_step_hbm_frac": round(
+               cfg.decode_bytes_per_token(ctx + 20) / t_dec / 1e9 / peaks()[0], 4)}
+    del rt
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -300,7 +519,33 @@ def run_ours(args, world, rank, local) -> None:
     e2e = {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s",
            "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
 
-    # dominant kernel: every multi-output u4 GEMV of one step, replayed alone
+    # dominant kernel by time: the one-launch MoE layer, its 40 launches of one
+    # step replayed alone (algorithmic bytes: BASELINE config 1 per layer)
+    moe_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(moe_graph, stream=rt.stream):
+        for l in range(cfg.layers):
+            L = rt.w.layers[l]
+            ops.moe_layer_decode(rt.hres, L["post_norm"], L["router"], L["sgate"], L["bank"],
+                                 L["shared"], rt.b_ids, rt.b_wts, rt.b_logits_r, rt.b_slogit,
+                                 workspace=rt.ws_moe, k=cfg.topk, norm_eps=cfg.eps)
+    for _ in range(3):
+        moe_graph.replay()
+    torch.cuda.synchronize(dev)
+    s.record()
+    for _ in range(10):
+        moe_graph.replay()
+    e.record()
+    torch.cuda.synchronize(dev)
+    moe_launch_s = s.elapsed_time(e) / 1e3 / (10 * cfg.layers)
+    del moe_graph
+    h2 = cfg.hidden
+
+    def u4b(rows, kk):
+        return rows * kk // 2 + rows * (kk // cfg.group) * 5 // 2
+    moe_bytes = (cfg.experts * h2 * 2 + h2 * 2 + (cfg.topk + 1) *
+                 (u4b(2 * cfg.inter, h2) + u4b(h2, cfg.inter)))
+
+    # every multi-output u4 GEMV of one step, replayed alone
     gemv_bytes, gemv_launches = 0, 0
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=rt.stream):
@@ -340,19 +585,36 @@ def run_ours(args, world, rank, local) -> None:
         "e2e": e2e,
         "gpu_launches": rt.launches_per_step * args.steps,
         "roofline": {"bound": "hbm",
-                     "kernel": "u4 multi-output GEMV (u4_stream_proj_kernel; ragged shapes "
-                               "u4_gemv_multi_kernel), all launches of one step",
-                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4),
-                     # DRAM bytes per launch of these 81 launches from one ncu capture
-                     # (profiles/decode_gemv_traffic_ctx256.md): equal to the algorithmic
-                     # bytes, no re-reads
-                     "traffic": DECODE_GEMV_TRAFFIC if cfg.layers == 40 else None,
-                     "peak_source": src,
-                     "bytes_per_launch": gemv_bytes // gemv_launches,
-                     "launches": gemv_launches},
+                     "kernel": "moe_layer_kernel (one-launch MoE decode layer: router, top-8, "
+                               "8 routed + 1 shared expert), its 40 launches of one step",
+                     "achieved": round(moe_bytes / moe_launch_s / 1e9, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(moe_bytes / moe_launch_s / 1e9 / hbm, 4),
+                     # DRAM bytes per launch from one ncu capture of this kernel at the
+                     # config-1 layer shape (profiles/moe_layer_decode_config1.md)
+                     "traffic": DECODE_MOE_TRAFFIC if cfg.layers == 40 else None,
+                     "peak_source": src, "bytes_per_launch": moe_bytes,
+                     "us_per_launch": round(moe_launch_s * 1e6, 3), "launches": cfg.layers},
+        "roofline_gemv": {"bound": "hbm",
+                          "kernel": "u4 multi-output GEMV (u4_stream_proj_kernel; ragged shapes "
+                                    "u4_gemv_multi_kernel), all launches of one step",
+                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                          "frac": round(achieved / hbm, 4),
+                          # DRAM bytes per launch of these 81 launches from one ncu capture
+                          # (profiles/decode_gemv_traffic_ctx256.md)
+                          "traffic": DECODE_GEMV_TRAFFIC if cfg.layers == 40 else None,
+                          "bytes_per_launch": gemv_bytes // gemv_launches,
+                          "launches": gemv_launches},
         "clocks": clocks,
     }
+    if rank == 0 and world == 1 and not args.no_parts:
+        # the rest of BASELINE's metric ("decode & prefill tok/s (4k/32k ctx); u4
+        # GEMV HBM GB/s vs peak"), measured after the timed region
+        parts = {"decode_ctx4096_tok_s": round(value, 3),
+                 "prefill_4096_tok_s": line["config"]["prefill_tok_s"]}
+        parts.update(part_long_context(rt.w, dev))
+        parts.update(part_gemv_config0(dev))
+        parts.update(part_moe_prefill_config3(dev))
+        line["metric_parts"] = parts
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ctx, os.cpu_count() or 1)
     if rank == 0:
@@ -1121,6 +1383,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parts", action="store_true",
+                    help="decode line only: skip the 32k / config-0 / config-3 parts")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one decode step inside cudaProfilerStart/Stop and exit")
     args = ap.parse_args()

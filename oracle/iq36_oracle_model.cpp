@@ -172,6 +172,18 @@ void fill_u4_rows(U4& m, int64_t dst_row0, int64_t row0, int64_t rows, int K, in
                     iq36_tensor_id(layer, slot, 2), lo, hi);
 }
 
+// Copies rows [0, per) of m (codes, scales, zero points) to the n - 1 blocks
+// of `per` rows that follow.
+void replicate_rows(U4& m, int64_t per, int n) {
+  const int64_t bw = per * m.K / 2, bs = (int64_t)m.s.size() / n, bz = (int64_t)m.z.size() / n;
+#pragma omp parallel for schedule(static)
+  for (int e = 1; e < n; ++e) {
+    std::memcpy(m.w.data() + e * bw, m.w.data(), bw);
+    std::memcpy(m.s.data() + e * bs, m.s.data(), bs * sizeof(uint16_t));
+    std::memcpy(m.z.data() + e * bz, m.z.data(), bz);
+  }
+}
+
 void size_u4(U4& m, int64_t rows, int K, int G) {
   m.rows = rows;
   m.K = K;
@@ -238,9 +250,22 @@ void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
     M->lazy = (int64_t)c.experts * 3 * c.inter * H / 2 > kLazyBankBytes;
     if (const char* f = std::getenv("IQ36_ORACLE_LAZY")) M->lazy = f[0] == '1';
     if (const char* f = std::getenv("IQ36_ORACLE_PRECISE")) M->precise = f[0] == '1';
+    // Timing-only banks (IQ36_ORACLE_REPLICATED=1): expert 0 generated, then
+    // copied to every other expert. The router still spreads tokens over all
+    // experts, so each step reads the same bytes and does the same arithmetic
+    // as with distinct experts; only the values differ. Used by the timed CPU
+    // baseline, whose model would otherwise take minutes to generate.
+    const char* rep = std::getenv("IQ36_ORACLE_REPLICATED");
     if (M->lazy) {
       size_u4(L.gu, (int64_t)c.topk * 2 * c.inter, H, G);
       size_u4(L.down, (int64_t)c.topk * H, c.inter, G);
+    } else if (rep && rep[0] == '1') {
+      size_u4(L.gu, (int64_t)c.experts * 2 * c.inter, H, G);
+      size_u4(L.down, (int64_t)c.experts * H, c.inter, G);
+      fill_u4_rows(L.gu, 0, 0, 2 * c.inter, H, G, seed, l, IQ36_T_GU);
+      fill_u4_rows(L.down, 0, 0, H, c.inter, G, seed, l, IQ36_T_DOWN);
+      replicate_rows(L.gu, 2 * c.inter, c.experts);
+      replicate_rows(L.down, H, c.experts);
     } else {
       fill_u4(L.gu, (int64_t)c.experts * 2 * c.inter, H, G, seed, l, IQ36_T_GU);
       fill_u4(L.down, (int64_t)c.experts * H, c.inter, G, seed, l, IQ36_T_DOWN);
