@@ -592,6 +592,7 @@ struct LayerArgs {
   float* wts_out;
   __half* act;               // [n_slots, I] SwiGLU activations (workspace)
   unsigned long long* bar;   // grid-barrier arrival counter (workspace)
+  float* partial_out;        // tensor-parallel rank: fp32 share of the output, residual read-only
 };
 
 struct LayerSmem {
@@ -1149,7 +1150,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(LayerArgs a
     if (n_slots > k) y = __fadd_rn(y, __fmul_rn(red[k][tid], sigmoidf_acc(nred[33])));
     // s_res: this CTA's rows as read in phase A (no CTA writes the residual
     // before barrier 2)
-    a.residual[row] = s_res[tid] + __half2float(__float2half_rn(y));
+    if (a.partial_out != nullptr) a.partial_out[row] = y;
+    else a.residual[row] = s_res[tid] + __half2float(__float2half_rn(y));
   }
 }
 
@@ -1328,14 +1330,15 @@ extern "C" int iq36_moe_block_decode(const void* x_f16, const void* w_router_f16
                            s);
 }
 
-extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_weight,
-                                     float norm_eps, const void* w_router_f16,
-                                     const void* w_shared_gate_f16, int32_t k,
-                                     const iq36_expert_bank* routed,
-                                     const iq36_expert_bank* shared, int32_t* ids, float* weights,
-                                     float* logits, float* shared_logit, void* workspace,
-                                     size_t workspace_bytes, iq36_stream_t stream) {
-  using namespace iq36;
+namespace iq36 {
+// The decode MoE layer: residual += f16(layer output), or, with partial_out,
+// partial_out = the fp32 layer output over this bank's rows (residual read).
+static int moe_layer_impl(float* residual, int32_t hidden, const float* norm_weight,
+                          float norm_eps, const void* w_router_f16, const void* w_shared_gate_f16,
+                          int32_t k, const iq36_expert_bank* routed,
+                          const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                          float* logits, float* shared_logit, float* partial_out, void* workspace,
+                          size_t workspace_bytes, iq36_stream_t stream) {
   if (!residual || !norm_weight || !w_router_f16 || !routed || !ids || !weights || !logits ||
       !workspace)
     return IQ36_ERR_ARG;
@@ -1392,6 +1395,7 @@ extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const floa
     la.ids_out = ids;
     la.wts_out = weights;
     la.act = reinterpret_cast<__half*>(workspace);
+    la.partial_out = partial_out;
     la.bar = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) +
                                                    moe_decode_ws(k, hidden, routed->intermediate));
     const LayerSmem L = layer_smem(hidden, routed->intermediate, a.n_slots);
@@ -1407,9 +1411,42 @@ extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const floa
   // the router's last CTA or inside the expert kernels.
   st = router_select_launch(logits, 1, routed->num_experts, k, ids, weights, s);
   if (st != IQ36_OK) return st;
+  if (partial_out)
+    return moe_decode_launch(nullptr, residual, norm_weight, norm_eps, ids, weights, k, routed,
+                             shared, shared ? shared_logit : nullptr, partial_out, IQ36_F32, 0,
+                             workspace, workspace_bytes, s);
   return moe_decode_launch(nullptr, residual, norm_weight, norm_eps, ids, weights, k, routed,
                            shared, shared ? shared_logit : nullptr, residual, IQ36_F32, 1,
                            workspace, workspace_bytes, s);
+}
+}  // namespace iq36
+
+extern "C" int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_weight,
+                                     float norm_eps, const void* w_router_f16,
+                                     const void* w_shared_gate_f16, int32_t k,
+                                     const iq36_expert_bank* routed,
+                                     const iq36_expert_bank* shared, int32_t* ids, float* weights,
+                                     float* logits, float* shared_logit, void* workspace,
+                                     size_t workspace_bytes, iq36_stream_t stream) {
+  return iq36::moe_layer_impl(residual, hidden, norm_weight, norm_eps, w_router_f16,
+                              w_shared_gate_f16, k, routed, shared, ids, weights, logits,
+                              shared_logit, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int iq36_moe_layer_decode_partial(const float* residual, int32_t hidden,
+                                             const float* norm_weight, float norm_eps,
+                                             const void* w_router_f16,
+                                             const void* w_shared_gate_f16, int32_t k,
+                                             const iq36_expert_bank* routed,
+                                             const iq36_expert_bank* shared, int32_t* ids,
+                                             float* weights, float* logits, float* shared_logit,
+                                             float* partial_out, void* workspace,
+                                             size_t workspace_bytes, iq36_stream_t stream) {
+  if (!partial_out) return IQ36_ERR_ARG;
+  return iq36::moe_layer_impl(const_cast<float*>(residual), hidden, norm_weight, norm_eps,
+                              w_router_f16, w_shared_gate_f16, k, routed, shared, ids, weights,
+                              logits, shared_logit, partial_out, workspace, workspace_bytes,
+                              stream);
 }
 
 extern "C" size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden,

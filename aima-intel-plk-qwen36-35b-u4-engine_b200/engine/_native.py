@@ -41,6 +41,14 @@ class ExpertBankC(Structure):
                 ("hidden", c_int32), ("intermediate", c_int32), ("group", c_int32)]
 
 
+class TpCommC(Structure):
+    """iq36_tp_comm: every rank's exchange buffers as mapped in this process."""
+    _fields_ = [("rank", c_int32), ("world", c_int32), ("hidden", c_int32),
+                ("peer_recv", c_void_p * 8), ("peer_flags", c_void_p * 8),
+                ("peer_keys", c_void_p * 8), ("local_recv", c_void_p),
+                ("local_flags", c_void_p), ("local_keys", c_void_p), ("counter", c_void_p)]
+
+
 # name -> (restype, argtypes)
 _P = c_void_p
 _SIGS: dict[str, tuple] = {
@@ -68,6 +76,18 @@ _SIGS: dict[str, tuple] = {
                                       POINTER(ExpertBankC), POINTER(ExpertBankC), _P, _P, _P, _P,
                                       _P, c_size_t, _P]),
     "iq36_moe_layer_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "iq36_moe_layer_decode_partial": (c_int, [_P, c_int32, _P, c_float, _P, _P, c_int32,
+                                              POINTER(ExpertBankC), POINTER(ExpertBankC), _P, _P,
+                                              _P, _P, _P, _P, c_size_t, _P]),
+    "iq36_tp_comm_bytes": (c_size_t, [c_int32, c_int32]),
+    "iq36_tp_comm_alloc": (c_int, [c_size_t, POINTER(c_void_p)]),
+    "iq36_tp_comm_free": (c_int, [_P]),
+    "iq36_ipc_get_handle": (c_int, [_P, _P]),
+    "iq36_ipc_open_handle": (c_int, [_P, POINTER(c_void_p)]),
+    "iq36_ipc_close_handle": (c_int, [_P]),
+    "iq36_tp_allreduce_residual": (c_int, [POINTER(TpCommC), _P, _P, _P]),
+    "iq36_tp_argmax": (c_int, [POINTER(TpCommC), _P, c_int32, c_int32, _P, _P, _P]),
+    "iq36_tp_argmax_workspace_bytes": (c_size_t, []),
     "iq36_moe_prefill": (c_int, [_P, c_int32, _P, _P, c_int32, POINTER(ExpertBankC), _P, c_int32,
                                  _P, c_size_t, _P]),
     "iq36_moe_layer_prefill": (c_int, [_P, c_int32, c_int32, _P, c_float, _P, _P, c_int32,

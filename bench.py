@@ -440,6 +440,47 @@ def part_long_context(weights, dev, ctx: int = 32768, steps: int = 32) -> dict:
     return out
 
 
+def tp_decode_part(args, cfg, weights, world: int, rank: int, dev) -> dict:
+    """Tensor-parallel decode of ONE sequence over all ranks (the north star's
+    decode split, engine/tp_decode.py), timed like the replicas: --warmup
+    untimed and --steps timed graph replays, max over ranks. The context is
+    set to --ctx over a zero-filled cache: a decode step reads the same cache
+    bytes and weights whatever the cache holds."""
+    import torch
+    from engine.tp_decode import TPRuntime
+    tp = TPRuntime(cfg, rank, world, dev, max_ctx=args.ctx + args.warmup + args.steps + 32,
+                   full=weights)
+    tp.capture()
+    tp.pos.fill_(args.ctx)
+    tp.ctx.fill_(args.ctx + 1)
+    for _ in range(args.warmup):
+        tp.step()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        tp.step()
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    from engine import _native
+    timeouts = _native.wait_timeouts(reset=True)
+    launches = tp.launches_per_step
+    tp.close()
+    del tp
+    torch.cuda.empty_cache()
+    return {"tok_s": round(args.steps / t, 3), "ms_per_step": round(t / args.steps * 1e3, 4),
+            "ctx": args.ctx, "ranks": world, "launches_per_step": launches,
+            "exchanges_per_step": 2 * cfg.layers + 1, "wait_timeouts": timeouts,
+            "partition": ("q/k/v by KV head, DeltaNet in-proj by head, LM head by vocab "
+                          "(column-parallel); o/out proj and experts row-parallel "
+                          + ("(I/P rows of every expert)" if cfg.inter % (world * cfg.group) == 0
+                             else "(experts sharded, 256/P per rank)")
+                          + "; one-shot CUDA-IPC allreduce per sub-block")}
+
+
 # ---------------------------------------------------------------------------
 def run_ours(args, world, rank, local) -> None:
     import torch
@@ -606,6 +647,8 @@ def run_ours(args, world, rank, local) -> None:
                           "launches": gemv_launches},
         "clocks": clocks,
     }
+    if world > 1 and not args.no_tp:
+        line["tp_decode"] = tp_decode_part(args, cfg, rt.w, world, rank, dev)
     if rank == 0 and world == 1 and not args.no_parts:
         # the rest of BASELINE's metric ("decode & prefill tok/s (4k/32k ctx); u4
         # GEMV HBM GB/s vs peak"), measured after the timed region
@@ -1383,6 +1426,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="N > 1: skip the tensor-parallel decode of one sequence")
     ap.add_argument("--no-parts", action="store_true",
                     help="decode line only: skip the 32k / config-0 / config-3 parts")
     ap.add_argument("--profile-step", action="store_true",

@@ -215,6 +215,22 @@ int iq36_moe_layer_decode(float* residual, int32_t hidden, const float* norm_wei
                           size_t workspace_bytes, iq36_stream_t stream);
 size_t iq36_moe_layer_decode_workspace_bytes(int32_t k, int32_t hidden, int32_t intermediate);
 
+/* iq36_moe_layer_decode for a rank of tensor-parallel decode (no counterpart
+ * in the single-device reference): the banks hold this rank's slice of every
+ * expert's intermediate rows (gate and up rows, the matching K slice of down),
+ * and instead of updating the residual the call writes this rank's fp32 share
+ * of the layer output, partial_out[hidden] = sum_r w_r Down_r(SwiGLU(..)) +
+ * sigmoid(g) Shared(..) over its rows; the residual is only read. The ranks'
+ * partials summed (iq36_tp_allreduce_residual) give the layer output. Same
+ * workspace rules as iq36_moe_layer_decode. */
+int iq36_moe_layer_decode_partial(const float* residual, int32_t hidden, const float* norm_weight,
+                                  float norm_eps, const void* w_router_f16,
+                                  const void* w_shared_gate_f16, int32_t k,
+                                  const iq36_expert_bank* routed, const iq36_expert_bank* shared,
+                                  int32_t* ids, float* weights, float* logits,
+                                  float* shared_logit, float* partial_out, void* workspace,
+                                  size_t workspace_bytes, iq36_stream_t stream);
+
 /* ---- (2b) grouped MoE prefill ----------------------------------------------
  * For T tokens with top-k routing (ids, weights [T,k]): permute token rows by
  * expert (stable: by expert, then token, then rank), per expert
@@ -485,6 +501,61 @@ int iq36_synth_fill(void* dst, int64_t count, int32_t kind, uint64_t seed, uint6
 /* Tensor naming and distributions of the synthetic model (iq36_synth.h). */
 uint64_t iq36_synth_tensor_id(int32_t layer, int32_t slot, int32_t sub);
 void iq36_synth_tensor_spec(int32_t slot, int32_t sub, int32_t* kind, float* lo, float* hi);
+
+/* ---- tensor-parallel decode exchange ---------------------------------------
+ * No counterpart in the reference (it runs on one device). The north star
+ * row-shards the decode GEMVs across 2/4/8 GPUs and completes every
+ * row-parallel sub-block with an allreduce over NVLink; these entry points
+ * are that exchange, one small kernel each. Every rank owns one device buffer
+ * of iq36_tp_comm_bytes(world, hidden) bytes, ZERO-FILLED before first use:
+ *   [recv: 2 x world x hidden fp32][flags: world u32, 256-byte region]
+ *   [keys: 2 x world u64][counter: u32]
+ * shared with the other ranks through CUDA IPC (iq36_ipc_get_handle /
+ * iq36_ipc_open_handle). iq36_tp_comm holds, for every rank q, rank q's
+ * receive buffer, flag words and key slots as mapped in this process
+ * (peer_*[rank] = this rank's own), plus this rank's own buffers and its
+ * counter. Exchanges are one-shot: plain peer stores of this rank's data into
+ * every rank's slot, then a system-scope release of a per-call sequence
+ * number in every rank's flag word, then bounded polling (200 ms) of the
+ * world flags of this rank's own buffer; double-buffered by the call parity.
+ * All ranks must issue the same sequence of exchanges. A wait that expires is
+ * counted by iq36_wait_timeouts and leaves the output untouched; the comm
+ * buffers must then be zeroed again on every rank. */
+typedef struct {
+  int32_t rank, world, hidden;
+  float* peer_recv[8];
+  uint32_t* peer_flags[8];
+  unsigned long long* peer_keys[8];
+  float* local_recv;
+  uint32_t* local_flags;
+  unsigned long long* local_keys;
+  uint32_t* counter;
+} iq36_tp_comm;
+size_t iq36_tp_comm_bytes(int32_t world, int32_t hidden);
+/* Set-up only (the one allocating call of this library, made once per rank
+ * before any exchange): a zero-filled cudaMalloc allocation of `bytes` for
+ * the exchange buffer (an IPC handle must name a whole allocation), and its
+ * release after every rank has unmapped it. Synchronises the device. */
+int iq36_tp_comm_alloc(size_t bytes, void** dev_ptr);
+int iq36_tp_comm_free(void* dev_ptr);
+/* 64-byte CUDA IPC handle of a device allocation / its mapping in this
+ * process (peer access enabled lazily) / unmapping. */
+int iq36_ipc_get_handle(const void* dev_ptr, void* handle_64);
+int iq36_ipc_open_handle(const void* handle_64, void** dev_ptr);
+int iq36_ipc_close_handle(void* dev_ptr);
+/* residual[i] += f16(sum over ranks q, in rank order, of partial_q[i]) on
+ * every rank: the allreduce that completes a row-parallel sub-block, with the
+ * single-GPU step's fp16 rounding of the sub-block output. partial [hidden]
+ * fp32, 16-byte aligned; hidden % 4 == 0; world <= 8. */
+int iq36_tp_allreduce_residual(const iq36_tp_comm* comm, float* residual, const float* partial,
+                               iq36_stream_t stream);
+/* Greedy top-1 over a vocab split: this rank's logits_local [n_local] hold
+ * global ids id0 .. id0 + n_local - 1; every rank ends with the global argmax
+ * (lowest id on ties, iq36_greedy_top1.cl:8-13) in token_out. key_ws:
+ * iq36_tp_argmax_workspace_bytes() device bytes. */
+int iq36_tp_argmax(const iq36_tp_comm* comm, const float* logits_local, int32_t n_local,
+                   int32_t id0, int32_t* token_out, void* key_ws, iq36_stream_t stream);
+size_t iq36_tp_argmax_workspace_bytes(void);
 
 /* Programmatic dependent launch on (default) or off for every later launch
  * of this library in the process. */

@@ -206,3 +206,64 @@ def _tp_decode_gpu_body(rank, world):
     torch.cuda.synchronize(dev)
     err = float(((out - ref).abs().max() / ref.abs().max()).item())
     assert err < 1e-5, err
+
+
+# ---------------------------------------------------------------------------
+# GPU (NCCL + CUDA IPC exchange): the tensor-parallel decode runtime against
+# the single-GPU runtime on the same weights
+
+def tp_runtime_gpu(rank, world, port, q):
+    _init(rank, world, port, "nccl")
+    _finish(q, rank, _tp_runtime_gpu_body, rank, world)
+
+
+def _kld(p_logits, q_logits) -> float:
+    import numpy as np
+    p = np.exp(p_logits - p_logits.max())
+    p /= p.sum()
+    q = np.exp(q_logits - q_logits.max())
+    q /= q.sum()
+    return float(np.sum(p * (np.log(p + 1e-30) - np.log(q + 1e-30))))
+
+
+def _tp_runtime_gpu_body(rank, world):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from engine import _native
+    from engine.runtime import ModelConfig, Qwen36Runtime, SyntheticWeights
+    from engine.tp_decode import TPRuntime
+
+    dev = torch.device(f"cuda:{rank}")
+    cfg = ModelConfig(layers=4, experts=16, vocab=4096)
+    full = SyntheticWeights(cfg, 4242, dev)
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab, 20).tolist()
+    steps = 8
+    # single GPU on every rank (identical): reference tokens and logits
+    ref = Qwen36Runtime(cfg, max_ctx=64, device=dev, weights=full)
+    ref.capture()
+    ref.prefill(prompt)
+    ref_tok, ref_logits = [int(ref.token.item())], [ref.logits.cpu().numpy()]
+    for _ in range(steps):
+        ref.step()
+        ref_tok.append(int(ref.token.item()))
+        ref_logits.append(ref.logits.cpu().numpy())
+    del ref
+    # tensor parallel
+    tp = TPRuntime(cfg, rank, world, dev, max_ctx=64, full=full)
+    tp.capture()
+    tp.prefill(prompt)
+    got_tok, got_logits = [], []
+    for i in range(steps + 1):
+        if i:
+            tp.step()
+        torch.cuda.synchronize(dev)
+        parts = [torch.empty_like(tp.logits) for _ in range(world)]
+        dist.all_gather(parts, tp.logits)
+        got_tok.append(int(tp.token.item()))
+        got_logits.append(torch.cat(parts).cpu().numpy())
+    assert _native.wait_timeouts(reset=True) == 0
+    tp.close()
+    assert got_tok == ref_tok, (got_tok, ref_tok)
+    worst = max(_kld(r, g) for r, g in zip(ref_logits, got_logits))
+    assert worst <= 1e-3, worst

@@ -70,3 +70,14 @@ def test_ep_decode_nccl_matches_single_gpu():
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
 def test_tp_decode_nccl_matches_single_gpu():
     _run(W.tp_decode_gpu, 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_tp_decode_runtime_matches_single_gpu():
+    """The tensor-parallel decode runtime (column/row-parallel projections,
+    row-sharded experts, one-shot IPC allreduce per sub-block, vocab-split
+    argmax) on 2 GPUs: greedy tokens equal to the single-GPU runtime's and
+    per-position KL divergence within 1e-3 (sharded partial sums change only
+    the summation order)."""
+    _run(W.tp_runtime_gpu, 2)

@@ -41,3 +41,26 @@ def test_row_shards_sum_to_the_block():
             tot += oracle.moe_decode(x, ids, w, b, s, sl, 128)
         err = np.max(np.abs(tot - ref)) / np.max(np.abs(ref))
         assert err < 1e-5, (world, err)
+
+
+def test_u4_row_ranges_and_k_slices_dequantise_to_the_slices():
+    """The tensor-parallel slicing helpers: gathered row ranges and K slices of
+    a u4 matrix dequantise to the same rows / columns of the full matrix
+    (zero-point nibbles repacked exactly)."""
+    import numpy as np
+    import torch
+    from engine.tp_decode import u4_cols, u4_rows
+    from engine.ops import U4Weight
+    from helpers import dequant_u4, make_u4
+    rng = np.random.default_rng(3)
+    w, s, z = make_u4(rng, 96, 1024)
+    full = dequant_u4(w, s, z)
+    t = U4Weight(torch.from_numpy(w), torch.from_numpy(s), torch.from_numpy(z), 128)
+    ranges = [(0, 16), (48, 64), (80, 96)]
+    r = u4_rows(t, ranges)
+    got = dequant_u4(r.weight.numpy(), r.scale.numpy(), r.zp.numpy())
+    want = np.concatenate([full[a:b] for a, b in ranges])
+    np.testing.assert_array_equal(got, want)
+    c = u4_cols(t, 256, 768)
+    got = dequant_u4(c.weight.numpy(), c.scale.numpy(), c.zp.numpy())
+    np.testing.assert_array_equal(got, full[:, 256:768])
