@@ -97,8 +97,8 @@ __device__ __forceinline__ void stream_stage_x(uint4* xs, float2* xc, const __ha
 // Shared-memory layout of every streaming kernel:
 //   [ring: stages x stage_bytes][xs: K/8 x 16 B][xc: K/G x 8 B]
 //   [red: 2 x kRedChunks x consumer warps x 16 floats][misc: 16 floats]
-//   [barriers: full[8], empty[8]]
-//   [seq: chunk armed per stage [8], abort flag]
+//   [barriers: full[kStreamMaxStages], empty[kStreamMaxStages]]
+//   [seq: chunk armed per stage [kStreamMaxStages], abort flag]
 struct StreamSmem {
   uint32_t ring, xs, xc, red, misc, full, empty, seq;
   int total;
@@ -112,9 +112,9 @@ __host__ __device__ inline StreamSmem stream_smem(const StreamGeom& g, int xs_k,
   s.red = s.xc + (xs_k / G) * 8;
   s.misc = s.red + 2 * kRedChunks * kStreamConsumers * 16 * 4;
   s.full = s.misc + 64;
-  s.empty = s.full + 64;
-  s.seq = s.empty + 64;
-  s.total = s.seq + 64;
+  s.empty = s.full + 8 * kStreamMaxStages;
+  s.seq = s.empty + 8 * kStreamMaxStages;
+  s.total = s.seq + 4 * (kStreamMaxStages + 1);
   return s;
 }
 
@@ -177,8 +177,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       mbar_init(sbase + L.full + 8 * s, 1);
       mbar_init(sbase + L.empty + 8 * s, kStreamConsumers);
     }
-    for (int s = 0; s < 8; ++s) seq[s] = -1;  // no chunk armed yet
-    seq[8] = 0;                                // abort flag
+    for (int s = 0; s < kStreamMaxStages; ++s) seq[s] = -1;  // no chunk armed yet
+    seq[kStreamMaxStages] = 0;                                // abort flag
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
@@ -208,6 +208,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     pdl_launch_dependents();
     const int g = lane >> 2, t = lane & 3;
     const int gb = warp * geo.ng / kStreamConsumers, ge = (warp + 1) * geo.ng / kStreamConsumers;
+    XSlice xr;
+    load_xslice(xr, xs, xc, t, gb, ge);
     // With four or more ring stages the warps take chunks in pairs (two
     // independent mma chains per group); the sums per chunk are unchanged.
     const bool pair = geo.stages >= 4;
@@ -222,12 +224,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                          ring_wait(seq, sbase + L.full + 8 * s1, s1, c + 1, geo.stages));
       if (got) {
         if (n == 2)
-          chunk_dot_pair<G>(geo, smem + L.ring + s0 * geo.stage_bytes,
-                            smem + L.ring + s1 * geo.stage_bytes, xs, xc, lane, gb, ge, a0, b0, a1,
-                            b1);
+          chunk_dot_pair_x(geo, smem + L.ring + s0 * geo.stage_bytes,
+                           smem + L.ring + s1 * geo.stage_bytes, xr, lane, gb, ge, a0, b0, a1, b1);
         else
-          chunk_dot_range<G>(geo, smem + L.ring + s0 * geo.stage_bytes, xs, xc, lane, gb, ge, a0,
-                             b0);
+          chunk_dot_range_x(geo, smem + L.ring + s0 * geo.stage_bytes, xr, lane, gb, ge, a0, b0);
         // generic reads of the stages before the producer's next bulk copies
         // (async proxy) into them
         fence_proxy_async_smem();
@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           if (n == 2) mbar_arrive(sbase + L.empty + 8 * s1);
         }
       } else if (lane == 0) {
-        seq[8] = 1;  // shared so that every consumer warp leaves at the barrier below
+        seq[kStreamMaxStages] = 1;  // shared so every consumer warp leaves at the barrier below
       }
       for (int u = 0; u < n && ok; ++u) {
         const int cc = c + u, j = cc % kRedChunks;
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
         if (j == kRedChunks - 1 || cc == nloc - 1) {
           consumer_sync();
-          if (seq[8] != 0) {
+          if (seq[kStreamMaxStages] != 0) {
             ok = false;
             break;
           }

@@ -28,6 +28,7 @@ namespace iq36 {
 constexpr int kStreamConsumers = 16;                      // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;
 constexpr int kStreamRingBytes = 128 * 1024;
+constexpr int kStreamMaxStages = 8;  // mbarrier pairs and stage sequence words reserved
 // Rings whose chunks are taken by several independent consumer warps: a fast
 // warp can reach chunk c while the stage still holds chunk c - stages (its
 // consumer has not released it yet), and an mbarrier's parity cannot tell
@@ -85,7 +86,7 @@ __host__ __device__ inline StreamGeom stream_geom(int K, int G) {
   g.off_zp = g.off_scale + 16 * g.ng * 2;
   g.stage_bytes = ((g.off_zp + 16 * g.ng / 2) + 127) / 128 * 128;
   g.stages = kStreamRingBytes / g.stage_bytes;
-  if (g.stages > 8) g.stages = 8;
+  if (g.stages > kStreamMaxStages) g.stages = kStreamMaxStages;
   return g;
 }
 
@@ -231,6 +232,120 @@ __device__ __forceinline__ void chunk_dot_pair(const StreamGeom& geo, const uint
       aA = fmaf(__half2float(sc[g * geo.ng + gi]), fmaf(-za, cr.y, c[u][0] - cr.x), aA);
       aB = fmaf(__half2float(sc[(g + 8) * geo.ng + gi]), fmaf(-zz, cr.y, c[u][2] - cr.x), aB);
     }
+  }
+}
+
+// A consumer warp's activation slice: its quant groups [gb, gb + 2) (16
+// consumer warps cover K <= 4096 with at most two groups each) held in
+// registers for every chunk, instead of re-read from shared memory per chunk.
+struct XSlice {
+  uint4 x[2][4];
+  float2 c[2];
+};
+
+__device__ __forceinline__ void load_xslice(XSlice& xr, const uint4* __restrict__ xs,
+                                            const float2* __restrict__ xc, int t, int gb,
+                                            int ge) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int gi = min(gb + j, ge - 1);
+    if (gi < gb) continue;  // empty slice
+#pragma unroll
+    for (int i = 0; i < 4; ++i) xr.x[j][i] = xs[gi * 16 + t * 4 + i];
+    xr.c[j] = xc[gi];
+  }
+}
+
+// chunk_dot_pair / chunk_dot_range with the activation slice in registers
+// (G = 128, ge - gb <= 2): the same arithmetic in the same order.
+__device__ __forceinline__ void chunk_dot_pair_x(const StreamGeom& geo, const uint8_t* st0,
+                                                 const uint8_t* st1, const XSlice& xr, int lane,
+                                                 int gb, int ge, float& accA0, float& accB0,
+                                                 float& accA1, float& accB1) {
+  constexpr int G = 128;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* st[2] = {st0, st1};
+  const int eA = g * geo.ng, eB = (g + 8) * geo.ng;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int gi = gb + j;
+    if (gi >= ge) break;
+    uint4 va[2], vb[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      va[u] = *reinterpret_cast<const uint4*>(st[u] + g * geo.row_pitch + t * (G / 8) + gi * (G / 2));
+      vb[u] = *reinterpret_cast<const uint4*>(st[u] + (g + 8) * geo.row_pitch + t * (G / 8) +
+                                              gi * (G / 2));
+    }
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 xv = xr.x[j][i];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        uint32_t a = (&va[u].x)[i], b = (&vb[u].x)[i];
+        mma_16816(c[u][0], c[u][1], c[u][2], c[u][3], lop3_and_or(a, 0x000F000Fu, kMagic),
+                  lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                  lop3_and_or(b, 0x00F000F0u, kMagic), xv.x, xv.y);
+        a >>= 8;
+        b >>= 8;
+        mma_16816(c[u][0], c[u][1], c[u][2], c[u][3], lop3_and_or(a, 0x000F000Fu, kMagic),
+                  lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                  lop3_and_or(b, 0x00F000F0u, kMagic), xv.z, xv.w);
+      }
+    }
+    const float2 cr = xr.c[j];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const __half* sc = reinterpret_cast<const __half*>(st[u] + geo.off_scale);
+      const uint8_t* zb = st[u] + geo.off_zp;
+      const float za = (float)((zb[(eA + gi) >> 1] >> (((eA + gi) & 1) * 4)) & 15u);
+      const float zz = (float)((zb[(eB + gi) >> 1] >> (((eB + gi) & 1) * 4)) & 15u);
+      float& aA = u ? accA1 : accA0;
+      float& aB = u ? accB1 : accB0;
+      aA = fmaf(__half2float(sc[g * geo.ng + gi]), fmaf(-za, cr.y, c[u][0] - cr.x), aA);
+      aB = fmaf(__half2float(sc[(g + 8) * geo.ng + gi]), fmaf(-zz, cr.y, c[u][2] - cr.x), aB);
+    }
+  }
+}
+
+__device__ __forceinline__ void chunk_dot_range_x(const StreamGeom& geo, const uint8_t* stage,
+                                                  const XSlice& xr, int lane, int gb, int ge,
+                                                  float& accA, float& accB) {
+  constexpr int G = 128;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* rowA = stage + g * geo.row_pitch + t * (G / 8);
+  const uint8_t* rowB = stage + (g + 8) * geo.row_pitch + t * (G / 8);
+  const __half* sA = reinterpret_cast<const __half*>(stage + geo.off_scale) + g * geo.ng;
+  const __half* sB = reinterpret_cast<const __half*>(stage + geo.off_scale) + (g + 8) * geo.ng;
+  const uint8_t* zb = stage + geo.off_zp;
+  const int eA = g * geo.ng, eB = (g + 8) * geo.ng;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int gi = gb + j;
+    if (gi >= ge) break;
+    const uint4 va = *reinterpret_cast<const uint4*>(rowA + gi * (G / 2));
+    const uint4 vb = *reinterpret_cast<const uint4*>(rowB + gi * (G / 2));
+    const uint32_t ra[4] = {va.x, va.y, va.z, va.w}, rb[4] = {vb.x, vb.y, vb.z, vb.w};
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 xv = xr.x[j][i];
+      uint32_t a = ra[i], b = rb[i];
+      mma_16816(c0, c1, c2, c3, lop3_and_or(a, 0x000F000Fu, kMagic),
+                lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                lop3_and_or(b, 0x00F000F0u, kMagic), xv.x, xv.y);
+      a >>= 8;
+      b >>= 8;
+      mma_16816(c0, c1, c2, c3, lop3_and_or(a, 0x000F000Fu, kMagic),
+                lop3_and_or(b, 0x000F000Fu, kMagic), lop3_and_or(a, 0x00F000F0u, kMagic),
+                lop3_and_or(b, 0x00F000F0u, kMagic), xv.z, xv.w);
+    }
+    const float2 cr = xr.c[j];
+    const float za = (float)((zb[(eA + gi) >> 1] >> (((eA + gi) & 1) * 4)) & 15u);
+    const float zz = (float)((zb[(eB + gi) >> 1] >> (((eB + gi) & 1) * 4)) & 15u);
+    accA = fmaf(__half2float(sA[gi]), fmaf(-za, cr.y, c0 - cr.x), accA);
+    accB = fmaf(__half2float(sB[gi]), fmaf(-zz, cr.y, c2 - cr.x), accB);
   }
 }
 
