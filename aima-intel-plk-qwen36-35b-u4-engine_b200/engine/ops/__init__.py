@@ -617,3 +617,8 @@ def synth_fill(dst: torch.Tensor, kind: int, seed: int, tensor_id: int, lo: floa
     N.call("iq36_synth_fill", dst.data_ptr(), dst.numel(), kind, seed, tensor_id, lo, hi,
            _stream(dst.device))
     return dst
+
+
+# the same operators registered as torch.ops.iq36.* custom ops (schemas and
+# fake kernels over these functions)
+from . import library  # noqa: E402,F401
