@@ -130,6 +130,11 @@ struct StreamProj {
   int acc[4];
   int chunk_start[5];
   int n_proj;
+  // Chunk-list mode (the certified LM head): only the chunks chunk_list[0 ..
+  // *chunk_count) are computed, each exactly as in a full launch. Both words
+  // come from the previous launch, so this mode waits before it streams.
+  const int* chunk_list;
+  const int* chunk_count;
 };
 
 __device__ __forceinline__ void store_row(void* out, int dtype, int acc, int row, float v) {
@@ -145,6 +150,7 @@ __device__ __forceinline__ void store_row(void* out, int dtype, int acc, int row
 
 __device__ __forceinline__ ChunkSrc proj_chunk(const StreamProj& ps, int q, int K, int ng, int& p,
                                                int& r0) {
+  if (ps.chunk_list != nullptr) q = ps.chunk_list[q];
   p = 0;
   while (p + 1 < ps.n_proj && q >= ps.chunk_start[p + 1]) ++p;
   r0 = (q - ps.chunk_start[p]) * 16;
@@ -169,7 +175,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   volatile int* seq = reinterpret_cast<volatile int*>(smem + L.seq);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = ps.chunk_start[ps.n_proj];
+  int total = ps.chunk_start[ps.n_proj];
+  if (ps.chunk_list != nullptr) {
+    pdl_wait();
+    total = *ps.chunk_count;
+  }
   const int per = (total + gridDim.x - 1) / gridDim.x;
   const int c0 = blockIdx.x * per, nloc = max(min(c0 + per, total) - c0, 0);
   if (threadIdx.x == 0) {
@@ -339,3 +349,337 @@ int stream_wait_timeouts(int* count, int reset) {
 }
 
 }  // namespace iq36
+
+// ---------------------------------------------------------------------------
+// LM-head certified greedy top-1
+//
+// Greedy decode needs only the argmax of the head. Every row's logit is
+// bounded by Cauchy-Schwarz per quant group, sum_g |s_rg| ||q_rg - zp_rg||_2
+// ||x_g||_2, plus a guard for the fp32 rounding of the full head's group sums.
+// The 16-row chunk of a seed token is computed exactly first; rows whose bound
+// reaches its largest logit flag their chunk, and the flagged chunks are
+// computed by the streaming kernel above in chunk-list mode, i.e. with the
+// full head's own arithmetic, so the winner (lowest id on ties) is the full
+// head's argmax bit for bit. Too many flagged chunks: every chunk.
+
+namespace iq36 {
+
+constexpr float kCertGuardRel = 1.0f / 4096.0f;  // > 16 fp32 ulps of the group sums' terms
+// An odd activation below 2^-10 loses bits when staged as x/16 (fp16
+// subnormal); each such element moves the group sum by at most (64 + 15) * 2^-21.
+constexpr float kCertGuardAbs = 64.0f * 80.0f / 2097152.0f;
+constexpr int kCertArgmaxBlocks = 148;
+
+// table[r, g] = |s_rg| * ||q_rg - zp_rg||_2, rounded up to fp16.
+__global__ void __launch_bounds__(256) cert_table_kernel(const uint8_t* w, const __half* s,
+                                                         const uint8_t* z, int rows, int K,
+                                                         __half* table) {
+  const int ng = K / 128;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)rows * ng) return;
+  const int64_t r = idx / ng;
+  const int g = (int)(idx % ng);
+  const uint8_t* row = w + r * (K / 2) + g * 64;
+  const int zp = (z[idx >> 1] >> ((idx & 1) * 4)) & 15;
+  int ss = 0;  // exact: at most 128 * 225
+  for (int i = 0; i < 64; ++i) {
+    const int lo = (row[i] & 15) - zp, hi = (row[i] >> 4) - zp;
+    ss += lo * lo + hi * hi;
+  }
+  const float n =
+      sqrtf((float)ss) * fabsf(__half2float(s[r * ng + g])) * (1.0f + 1.0f / 1048576.0f);
+  table[idx] = __float2half_ru(n);
+}
+
+// One CTA of the streaming kernel's 16 consumer warps: the same staged
+// activation (stream_stage_x), then per quant group ||x_g|| (rounded up) and
+// the guard; the seed chunk as a one-entry chunk list; the chunk flags cleared.
+__global__ void __launch_bounds__(kStreamConsumers * 32) cert_prep_kernel(
+    const __half* x16, const float* x32, const float* nw, float eps, int K, int rows,
+    const int32_t* seed_token, float* xnorm, float* xguard, int* list, int* count,
+    uint8_t* flags) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint4* xs = reinterpret_cast<uint4*>(sm);
+  float2* xc = reinterpret_cast<float2*>(sm + K / 8 * 16);
+  float* red = reinterpret_cast<float*>(sm + K / 8 * 16 + K / 128 * 8);
+  pdl_wait();
+  stream_stage_x<128>(xs, xc, x16, x32, nw, eps, K, red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng = K / 128;
+  for (int g = warp; g < ng; g += kStreamConsumers) {
+    // 16 staged uint4 per group, one per lane l < 16. A staged uint4 holds the
+    // pairs (x0,x4), (x1,x5)/16, (x2,x6), (x3,x7)/16: words 0 and 2 carry even
+    // k, words 1 and 3 odd k divided by 16 (multiplied back here).
+    float sq = 0.f, ae = 0.f, ao = 0.f;
+    if (lane < 16) {
+      const uint4 v = xs[g * 16 + lane];
+      const __half2* hp = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(hp[j]);
+        const float m = (j & 1) ? 16.f : 1.f;
+        const float a = f.x * m, b = f.y * m;
+        sq += a * a + b * b;
+        if (j & 1) ao += fabsf(a) + fabsf(b);
+        else ae += fabsf(a) + fabsf(b);
+      }
+    }
+    sq = warp_sum(sq);
+    ae = warp_sum(ae);
+    ao = warp_sum(ao);
+    if (lane == 0) {
+      xnorm[g] = sqrtf(sq * (1.0f + 1.0f / 65536.0f)) * (1.0f + 1.0f / 1048576.0f);
+      xguard[g] = kCertGuardRel * (1024.f * ae + 64.f * ao + 16.f * (ae + ao)) + kCertGuardAbs;
+    }
+  }
+  const int nchunks = rows / 16;
+  for (int i = threadIdx.x; i < nchunks; i += blockDim.x) flags[i] = 0;
+  if (threadIdx.x == 0) {
+    const int t = min(max(*seed_token, 0), rows - 1);
+    list[0] = t / 16;
+    *count = 1;
+  }
+  pdl_launch_dependents();
+}
+
+// Upper bound of every row against the seed chunk's largest exact logit;
+// surviving rows flag their chunk.
+__global__ void __launch_bounds__(256) cert_scan_kernel(const __half* table, const __half* s,
+                                                        int rows, int K, const float* xnorm,
+                                                        const float* xguard, const int* list,
+                                                        const float* logits, uint8_t* flags) {
+  __shared__ float xn[32], xg[32];
+  __shared__ float seed;
+  pdl_wait();
+  const int ng = K / 128;
+  if (threadIdx.x < ng) {
+    xn[threadIdx.x] = xnorm[threadIdx.x];
+    xg[threadIdx.x] = xguard[threadIdx.x];
+  }
+  if (threadIdx.x == 0) {
+    const float* l = logits + (size_t)list[0] * 16;
+    float m = l[0];
+    for (int i = 1; i < 16; ++i) m = fmaxf(m, l[i]);
+    seed = m;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const __half* tr = table + (size_t)r * ng;
+    const __half* sr = s + (size_t)r * ng;
+    float up = 0.f;
+    for (int g = 0; g < ng; ++g)
+      up += __half2float(tr[g]) * xn[g] + fabsf(__half2float(sr[g])) * xg[g];
+    up *= 1.0f + 1.0f / 65536.0f;
+    if (up >= seed) flags[r / 16] = 1;
+  }
+}
+
+// Flagged chunks in index order (one CTA, block prefix sums); more than
+// `capacity` of them: every chunk (the full head).
+__global__ void __launch_bounds__(1024) cert_compact_kernel(const uint8_t* flags, int nchunks,
+                                                            int capacity, int* list, int* count) {
+  __shared__ int wsum[32];
+  __shared__ int base;
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < nchunks; c0 += 1024) {
+    const int c = c0 + tid;
+    const int f = (c < nchunks && flags[c]) ? 1 : 0;
+    const unsigned m = __ballot_sync(0xffffffffu, f);
+    const int before = __popc(m & ((1u << lane) - 1u));
+    if (lane == 0) wsum[warp] = __popc(m);
+    __syncthreads();
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += wsum[w];
+    if (f) list[base + off + before] = c;
+    __syncthreads();
+    if (tid == 0) {
+      int t = 0;
+      for (int w = 0; w < 32; ++w) t += wsum[w];
+      base += t;
+    }
+    __syncthreads();
+  }
+  if (base > capacity) {
+    for (int c = tid; c < nchunks; c += 1024) list[c] = c;
+    if (tid == 0) *count = nchunks;
+  } else if (tid == 0) {
+    *count = base;
+  }
+  pdl_launch_dependents();
+}
+
+// Order-preserving key: larger logit first, then the lower row id.
+__device__ __forceinline__ uint64_t cert_key(float v, uint32_t id) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b ^ 0x80000000u);
+  return ((uint64_t)ord << 32) | (uint64_t)(~id);
+}
+
+__global__ void __launch_bounds__(256) cert_argmax_kernel(const float* logits, const int* list,
+                                                          const int* count, uint64_t* partial) {
+  __shared__ uint64_t red[8];
+  pdl_wait();
+  const int n = *count * 16;
+  uint64_t best = 0ull;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int row = list[i >> 4] * 16 + (i & 15);
+    const uint64_t k = cert_key(logits[row], (uint32_t)row);
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < 8; ++w) best = red[w] > best ? red[w] : best;
+    partial[blockIdx.x] = best;
+  }
+  pdl_launch_dependents();
+}
+
+__global__ void __launch_bounds__(32) cert_final_kernel(const uint64_t* partial, int np,
+                                                        const int* count, int32_t* token,
+                                                        int32_t* evaluated) {
+  pdl_wait();
+  uint64_t best = 0ull;
+  for (int i = threadIdx.x; i < np; i += 32) best = partial[i] > best ? partial[i] : best;
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if (threadIdx.x == 0) {
+    *token = (int32_t)(~(uint32_t)(best & 0xFFFFFFFFull));
+    if (evaluated) *evaluated = *count;
+  }
+}
+
+struct CertWs {
+  float* xnorm;
+  float* xguard;
+  uint8_t* flags;
+  int* list;
+  int* count;
+  uint64_t* partial;
+  size_t bytes;
+};
+
+static CertWs cert_ws(void* base, int rows, int K) {
+  CertWs w;
+  char* p = reinterpret_cast<char*>(base);
+  auto take = [&](size_t n) {
+    char* q = p;
+    p += (n + 255) / 256 * 256;
+    return q;
+  };
+  const int nchunks = rows / 16;
+  w.xnorm = reinterpret_cast<float*>(take(K / 128 * 4));
+  w.xguard = reinterpret_cast<float*>(take(K / 128 * 4));
+  w.flags = reinterpret_cast<uint8_t*>(take(nchunks));
+  w.list = reinterpret_cast<int*>(take((size_t)nchunks * 4));
+  w.count = reinterpret_cast<int*>(take(16));
+  w.partial = reinterpret_cast<uint64_t*>(take(kCertArgmaxBlocks * 8));
+  w.bytes = (size_t)(p - reinterpret_cast<char*>(base));
+  return w;
+}
+
+}  // namespace iq36
+
+extern "C" size_t iq36_lm_head_cert_table_bytes(int32_t rows, int32_t K, int32_t G) {
+  if (rows < 1 || G != 128 || K % 128) return 0;
+  return (size_t)rows * (K / 128) * 2;
+}
+
+extern "C" int iq36_lm_head_cert_table(const iq36_u4_matrix* w, int32_t K, int32_t G,
+                                       void* table_f16, iq36_stream_t stream) {
+  using namespace iq36;
+  if (!w || !w->weight || !w->scale || !w->zp || !table_f16) return IQ36_ERR_ARG;
+  if (G != 128 || K % 512 || K > 4096 || w->rows < 16 || w->rows % 16) return IQ36_ERR_SHAPE;
+  const int64_t n = (int64_t)w->rows * (K / 128);
+  cert_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(
+      w->weight, reinterpret_cast<const __half*>(w->scale), w->zp, w->rows, K,
+      reinterpret_cast<__half*>(table_f16));
+  return cudaGetLastError() == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}
+
+extern "C" size_t iq36_lm_head_top1_certified_workspace_bytes(int32_t rows, int32_t K) {
+  if (rows < 16 || K < 128) return 0;
+  return iq36::cert_ws(nullptr, rows, K).bytes;
+}
+
+extern "C" int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32,
+                                           const float* norm_weight, float norm_eps, int32_t K,
+                                           int32_t G, const iq36_u4_matrix* w,
+                                           const void* table_f16, const int32_t* seed_token,
+                                           int32_t capacity_chunks, float* logits,
+                                           int32_t* token_out, int32_t* evaluated_chunks,
+                                           void* workspace, size_t workspace_bytes,
+                                           iq36_stream_t stream) {
+  using namespace iq36;
+  if (!w || !w->weight || !w->scale || !w->zp || !table_f16 || !seed_token || !logits ||
+      !token_out || !workspace)
+    return IQ36_ERR_ARG;
+  if (x_f32) {
+    if (x_f16 || !norm_weight) return IQ36_ERR_ARG;
+  } else if (!x_f16) {
+    return IQ36_ERR_ARG;
+  }
+  iq36_u4_projection proj{*w, logits, IQ36_F32, 0};
+  if (G != 128 || !stream_proj_ok(K, G, 1, &proj) || w->rows < 16) return IQ36_ERR_SHAPE;
+  if (capacity_chunks < 1) return IQ36_ERR_SHAPE;
+  const CertWs ws = cert_ws(workspace, w->rows, K);
+  if (workspace_bytes < ws.bytes) return IQ36_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return IQ36_ERR_ALIGN;
+  const cudaStream_t s = as_stream(stream);
+  const int nchunks = w->rows / 16;
+  const size_t prep_smem = (size_t)K / 8 * 16 + K / 128 * 8 + 33 * 4;
+  cudaError_t e = launch(cert_prep_kernel, dim3(1), dim3(kStreamConsumers * 32), prep_smem, s,
+                         reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
+                         w->rows, seed_token, ws.xnorm, ws.xguard, ws.list, ws.count, ws.flags);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  StreamProj ps = {};
+  ps.n_proj = 1;
+  ps.w[0] = w->weight;
+  ps.s[0] = reinterpret_cast<const __half*>(w->scale);
+  ps.z[0] = w->zp;
+  ps.out[0] = logits;
+  ps.dtype[0] = IQ36_F32;
+  ps.acc[0] = 0;
+  ps.chunk_start[0] = 0;
+  ps.chunk_start[1] = nchunks;
+  ps.chunk_list = ws.list;
+  ps.chunk_count = ws.count;
+  const StreamGeom geo = stream_geom(K, G);
+  const StreamSmem L = stream_smem(geo, K, G);
+  if (stream_attr((const void*)u4_stream_proj_kernel<128>) != IQ36_OK) return IQ36_ERR_CUDA;
+  // the seed chunk, exactly (one CTA)
+  e = launch(u4_stream_proj_kernel<128>, dim3(1), dim3(kStreamThreads), (size_t)L.total, s, ps,
+             reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
+             (int*)nullptr);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  e = launch(cert_scan_kernel, dim3(kStreamCtas * 4), dim3(256), 0, s,
+             reinterpret_cast<const __half*>(table_f16), reinterpret_cast<const __half*>(w->scale),
+             w->rows, K, (const float*)ws.xnorm, (const float*)ws.xguard, (const int*)ws.list,
+             (const float*)logits, ws.flags);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  e = launch(cert_compact_kernel, dim3(1), dim3(1024), 0, s, (const uint8_t*)ws.flags, nchunks,
+             (int)capacity_chunks, ws.list, ws.count);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  // the flagged chunks, exactly
+  e = launch(u4_stream_proj_kernel<128>, dim3(std::min(kStreamCtas, nchunks)),
+             dim3(kStreamThreads), (size_t)L.total, s, ps,
+             reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
+             (int*)nullptr);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  e = launch(cert_argmax_kernel, dim3(kCertArgmaxBlocks), dim3(256), 0, s, (const float*)logits,
+             (const int*)ws.list, (const int*)ws.count, ws.partial);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  e = launch(cert_final_kernel, dim3(1), dim3(32), 0, s, (const uint64_t*)ws.partial,
+             kCertArgmaxBlocks, (const int*)ws.count, token_out, evaluated_chunks);
+  return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
+}

@@ -88,6 +88,12 @@ _SIGS: dict[str, tuple] = {
     "iq36_tp_allreduce_residual": (c_int, [POINTER(TpCommC), _P, _P, _P]),
     "iq36_tp_argmax": (c_int, [POINTER(TpCommC), _P, c_int32, c_int32, _P, _P, _P]),
     "iq36_tp_argmax_workspace_bytes": (c_size_t, []),
+    "iq36_lm_head_cert_table_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "iq36_lm_head_cert_table": (c_int, [POINTER(U4Matrix), c_int32, c_int32, _P, _P]),
+    "iq36_lm_head_top1_certified_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "iq36_lm_head_top1_certified": (c_int, [_P, _P, _P, c_float, c_int32, c_int32,
+                                            POINTER(U4Matrix), _P, _P, c_int32, _P, _P, _P, _P,
+                                            c_size_t, _P]),
     "iq36_moe_prefill": (c_int, [_P, c_int32, _P, _P, c_int32, POINTER(ExpertBankC), _P, c_int32,
                                  _P, c_size_t, _P]),
     "iq36_moe_layer_prefill": (c_int, [_P, c_int32, c_int32, _P, c_float, _P, _P, c_int32,

@@ -611,6 +611,47 @@ def argmax(logits: torch.Tensor, token_out: torch.Tensor, workspace: torch.Tenso
     return token_out
 
 
+def lm_head_cert_table(w: U4Weight) -> torch.Tensor:
+    """Per-row, per-group fp16 bound table of the certified LM-head top-1
+    (|s| times the group's ||q - zp||, rounded up); built once per head."""
+    w.validate()
+    n = N.lib().iq36_lm_head_cert_table_bytes(w.rows, w.k, w.group)
+    _need(n > 0, "the certified top-1 needs a group-128 head")
+    table = torch.empty(n // 2, dtype=torch.float16, device=w.weight.device)
+    m = w.c()
+    N.call("iq36_lm_head_cert_table", ctypes.byref(m), w.k, w.group, table.data_ptr(),
+           _stream(w.weight.device))
+    return table
+
+
+def lm_head_top1_certified(w: U4Weight, table: torch.Tensor, seed_token: torch.Tensor,
+                           logits: torch.Tensor, token_out: torch.Tensor,
+                           x: torch.Tensor | None = None, x_f32: torch.Tensor | None = None,
+                           norm_weight: torch.Tensor | None = None, norm_eps: float = 1e-6,
+                           capacity_chunks: int = 1024, evaluated: torch.Tensor | None = None,
+                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy top-1 of the LM head by the bound certificate: the same token as
+    the full head's argmax; only the evaluated 16-row chunks' logits are
+    written (their count into ``evaluated``)."""
+    w.validate()
+    dev = w.weight.device
+    _cuda(logits, "logits", torch.float32)
+    _need(logits.numel() == w.rows, f"logits must have {w.rows} elements")
+    _cuda(token_out, "token_out", torch.int32)
+    _cuda(seed_token, "seed_token", torch.int32)
+    _need(table.numel() * 2 == N.lib().iq36_lm_head_cert_table_bytes(w.rows, w.k, w.group),
+          "table does not match the head")
+    if workspace is None:
+        workspace = torch.empty(N.lib().iq36_lm_head_top1_certified_workspace_bytes(w.rows, w.k),
+                                dtype=torch.uint8, device=dev)
+    m = w.c()
+    N.call("iq36_lm_head_top1_certified", _ptr(x), _ptr(x_f32), _ptr(norm_weight), norm_eps, w.k,
+           w.group, ctypes.byref(m), table.data_ptr(), seed_token.data_ptr(), capacity_chunks,
+           logits.data_ptr(), token_out.data_ptr(), _ptr(evaluated), workspace.data_ptr(),
+           workspace.numel(), _stream(dev))
+    return token_out
+
+
 def synth_fill(dst: torch.Tensor, kind: int, seed: int, tensor_id: int, lo: float,
                hi: float = 0.0) -> torch.Tensor:
     _cuda(dst, "dst")

@@ -187,7 +187,10 @@ class Qwen36Runtime:
 
     def __init__(self, cfg: ModelConfig, seed: int = 0, max_ctx: int = 4608,
                  device: str | torch.device = "cuda:0", block_seed: int = 1,
-                 weights: SyntheticWeights | None = None):
+                 weights: SyntheticWeights | None = None, lm_head: str = "full",
+                 lm_head_capacity: int = 1024):
+        if lm_head not in ("full", "certified"):
+            raise ValueError("lm_head must be 'full' or 'certified'")
         self.cfg = cfg
         self.dev = torch.device(device)
         self.w = weights or SyntheticWeights(cfg, seed, self.dev)
@@ -238,6 +241,18 @@ class Qwen36Runtime:
         self.ws_moe = ops.moe_layer_workspace(c.topk, h, c.inter, dev)
         self.ws_argmax = torch.empty(N.lib().iq36_argmax_workspace_bytes(), dtype=torch.uint8,
                                      device=dev)
+        # LM head: "full" computes every logit; "certified" computes the chunk
+        # of the step's input token, bounds every other row and computes only
+        # the chunks that can still win (same greedy token; only the evaluated
+        # chunks' logits are written, their count lands in lm_evaluated).
+        self.lm_mode = lm_head
+        self.lm_capacity = lm_head_capacity
+        if lm_head == "certified":
+            self.lm_table = ops.lm_head_cert_table(self.w.lm_head)
+            self.ws_cert = torch.empty(
+                N.lib().iq36_lm_head_top1_certified_workspace_bytes(c.vocab, h),
+                dtype=torch.uint8, device=dev)
+            self.lm_evaluated = torch.zeros(1, dtype=i32, device=dev)
         self._pf: dict | None = None  # batched-prefill buffers (sized on first use)
         # Optional step trace (tests): when set before capture(), every step
         # also copies the residual entering each layer (and leaving the last)
@@ -279,12 +294,22 @@ class Qwen36Runtime:
                 self.trace_router[l].copy_(self.b_logits_r)
         if self.trace is not None:
             self.trace[c.layers].copy_(self.hres)
-        ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
-                            norm_weight=W.final_norm, norm_eps=c.eps)
-        ops.argmax(self.logits, self.token, self.ws_argmax)
+        if self.lm_mode == "certified":
+            # the input token seeds the certificate; the token buffer is
+            # rewritten only by the last kernel, after the seed was read
+            ops.lm_head_top1_certified(W.lm_head, self.lm_table, self.token, self.logits,
+                                       self.token, x_f32=self.hres, norm_weight=W.final_norm,
+                                       norm_eps=c.eps, capacity_chunks=self.lm_capacity,
+                                       evaluated=self.lm_evaluated, workspace=self.ws_cert)
+            n += 7
+        else:
+            ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
+                                norm_weight=W.final_norm, norm_eps=c.eps)
+            ops.argmax(self.logits, self.token, self.ws_argmax)
+            n += 2
         N.call("iq36_decode_positions", self.pos.data_ptr(), self.ctx.data_ptr(), 1,
                ops._stream(self.dev))
-        return n + 3
+        return n + 1
 
     def enqueue_layer(self, l: int) -> int:
         """Enqueue decoder layer l of the decode step on the fp32 residual

@@ -493,6 +493,34 @@ int iq36_argmax(const float* logits, int32_t n, int32_t* token_out, void* worksp
                 size_t workspace_bytes, iq36_stream_t stream);
 size_t iq36_argmax_workspace_bytes(void);
 
+/* ---- LM-head certified greedy top-1 -----------------------------------------
+ * The reference's certificate (engine/gpu/opencl/
+ * iq36_lm_head_affine_q4_group128_component.cl:126-217 bound scan and
+ * candidate selection, :219-300 exact candidates and top-1, the full path as
+ * capacity fallback) for the u4 group-128 head: every row's logit is bounded
+ * by sum_g |s_rg| ||q_rg - zp_rg||_2 ||x_g||_2 plus a guard covering the fp32
+ * rounding of the full head's group sums; the 16-row chunk of *seed_token is
+ * computed exactly first, rows whose bound reaches its largest logit flag
+ * their chunk, and the flagged chunks are computed exactly by the full head's
+ * own kernel in chunk-list mode, so token_out equals the full head's argmax
+ * (lowest id on ties) bit for bit. More than capacity_chunks flagged chunks:
+ * every chunk (the full head). logits [rows] receives the evaluated chunks'
+ * logits only; *evaluated_chunks (optional, device) their number.
+ * Requirements: those of the weight-streaming GEMV (G 128, rows % 16 == 0,
+ * K % 512 == 0, K <= 4096). table: iq36_lm_head_cert_table_bytes, written
+ * once by iq36_lm_head_cert_table (fp16 |s| * group norm, rounded up).
+ * seed_token may alias token_out (it is read before token_out is written). */
+size_t iq36_lm_head_cert_table_bytes(int32_t rows, int32_t K, int32_t G);
+int iq36_lm_head_cert_table(const iq36_u4_matrix* w, int32_t K, int32_t G, void* table_f16,
+                            iq36_stream_t stream);
+size_t iq36_lm_head_top1_certified_workspace_bytes(int32_t rows, int32_t K);
+int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32, const float* norm_weight,
+                                float norm_eps, int32_t K, int32_t G, const iq36_u4_matrix* w,
+                                const void* table_f16, const int32_t* seed_token,
+                                int32_t capacity_chunks, float* logits, int32_t* token_out,
+                                int32_t* evaluated_chunks, void* workspace,
+                                size_t workspace_bytes, iq36_stream_t stream);
+
 /* Fill device buffers with the synthetic generator of iq36_synth.h.
  * kind: 0 = u8 codes, 1 = fp16 uniform [lo,hi), 2 = fp16 normal(std=lo),
  * 3 = fp32 uniform [lo,hi), 4 = fp32 normal(std=lo). */

@@ -126,6 +126,41 @@ def u4_gemv(x_f16: np.ndarray, w: np.ndarray, scale: np.ndarray, zp: np.ndarray,
     return out
 
 
+def lm_head_top1_certified(x_f16: np.ndarray, w: np.ndarray, scale: np.ndarray, zp: np.ndarray,
+                           seed_token: int, capacity_chunks: int, group: int = 128):
+    """Certified greedy top-1 of a u4 LM head, restated in fp64 (numpy).
+
+    Follows the reference's certificate (engine/gpu/opencl/
+    iq36_lm_head_affine_q4_group128_component.cl:126-217: a per-row upper
+    bound sum_g |s_g| ||q_g - zp_g||_2 ||x_g||_2 compared against the seed's
+    exact value, rows at or above it become candidates; :219-300: candidates
+    evaluated exactly, the top-1 taken with the lowest id on ties; the full
+    head when the candidates overflow the capacity), at the granularity of
+    16-row chunks: the seed is the largest logit of seed_token's chunk.
+    Returns (token, evaluated_chunks, fp64 logits of every row)."""
+    rows, k = w.shape[0], w.shape[1] * 2
+    ng = k // group
+    q = np.empty((rows, k), np.float64)
+    q[:, 0::2] = w & 15
+    q[:, 1::2] = w >> 4
+    zz = np.empty(zp.size * 2, np.float64)
+    zz[0::2] = zp & 15
+    zz[1::2] = zp >> 4
+    d = q.reshape(rows, ng, group) - zz.reshape(rows, ng)[:, :, None]
+    x = x_f16.astype(np.float64).reshape(ng, group)
+    sc = scale.astype(np.float64)
+    logits = (np.einsum("rgk,gk->rg", d, x) * sc).sum(axis=1)
+    upper = (np.abs(sc) * np.sqrt((d * d).sum(axis=2)) * np.sqrt((x * x).sum(axis=1))).sum(axis=1)
+    nchunks = rows // 16
+    seed_chunk = min(max(seed_token, 0), rows - 1) // 16
+    seed = logits[seed_chunk * 16:seed_chunk * 16 + 16].max()
+    flagged = np.unique(np.nonzero(upper >= seed)[0] // 16)
+    chunks = flagged if flagged.size <= capacity_chunks else np.arange(nchunks)
+    cand = (chunks[:, None] * 16 + np.arange(16)[None, :]).reshape(-1)
+    best = cand[np.argmax(logits[cand])]  # first maximum = lowest id among sorted candidates
+    return int(best), int(chunks.size), logits
+
+
 def f16_linear(x_f16: np.ndarray, w_f16: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x_f16.astype(np.float16)).view(np.uint16)
     e, h = w_f16.shape
