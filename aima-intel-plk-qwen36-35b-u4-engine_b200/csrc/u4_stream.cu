@@ -131,10 +131,12 @@ struct StreamProj {
   int chunk_start[5];
   int n_proj;
   // Chunk-list mode (the certified LM head): only the chunks chunk_list[0 ..
-  // *chunk_count) are computed, each exactly as in a full launch. Both words
-  // come from the previous launch, so this mode waits before it streams.
+  // *chunk_count) are computed, each exactly as in a full launch; a count above
+  // chunk_capacity means every chunk. Both words come from the previous
+  // launch, so this mode waits before it streams.
   const int* chunk_list;
   const int* chunk_count;
+  int chunk_capacity;
 };
 
 __device__ __forceinline__ void store_row(void* out, int dtype, int acc, int row, float v) {
@@ -148,9 +150,9 @@ __device__ __forceinline__ void store_row(void* out, int dtype, int acc, int row
   }
 }
 
-__device__ __forceinline__ ChunkSrc proj_chunk(const StreamProj& ps, int q, int K, int ng, int& p,
-                                               int& r0) {
-  if (ps.chunk_list != nullptr) q = ps.chunk_list[q];
+__device__ __forceinline__ ChunkSrc proj_chunk(const StreamProj& ps, const int* list, int q, int K,
+                                               int ng, int& p, int& r0) {
+  if (list != nullptr) q = list[q];
   p = 0;
   while (p + 1 < ps.n_proj && q >= ps.chunk_start[p + 1]) ++p;
   r0 = (q - ps.chunk_start[p]) * 16;
@@ -176,9 +178,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   volatile int* seq = reinterpret_cast<volatile int*>(smem + L.seq);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int total = ps.chunk_start[ps.n_proj];
+  const int* list = nullptr;
   if (ps.chunk_list != nullptr) {
     pdl_wait();
-    total = *ps.chunk_count;
+    const int n = *ps.chunk_count;
+    if (n <= ps.chunk_capacity) {
+      total = n;
+      list = ps.chunk_list;
+    }
   }
   const int per = (total + gridDim.x - 1) / gridDim.x;
   const int c0 = blockIdx.x * per, nloc = max(min(c0 + per, total) - c0, 0);
@@ -203,7 +210,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         ok = mbar_wait(sbase + L.empty + 8 * s, ph ^ 1u);
         if (!ok) break;
         int p, r0;
-        const ChunkSrc src = proj_chunk(ps, c0 + c, K, geo.ng, p, r0);
+        const ChunkSrc src = proj_chunk(ps, list, c0 + c, K, geo.ng, p, r0);
         mbar_arrive_tx(sbase + L.full + 8 * s, chunk_bytes(geo, src));
         ring_publish(seq, s, c);
         issue_chunk(geo, src, sbase + L.ring + s * geo.stage_bytes, sbase + L.full + 8 * s);
@@ -269,7 +276,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             for (int w = 0; w < kStreamConsumers; ++w)
               v += rbuf[(jj * kStreamConsumers + w) * 16 + r];
             int p, r0;
-            proj_chunk(ps, c0 + cc - j + jj, K, geo.ng, p, r0);
+            proj_chunk(ps, list, c0 + cc - j + jj, K, geo.ng, p, r0);
             store_row(ps.out[p], ps.dtype[p], ps.acc[p], r0 + r, v);
           }
         }
@@ -350,17 +357,19 @@ int stream_wait_timeouts(int* count, int reset) {
 
 }  // namespace iq36
 
+
 // ---------------------------------------------------------------------------
 // LM-head certified greedy top-1
 //
-// Greedy decode needs only the argmax of the head. Every row's logit is
-// bounded by Cauchy-Schwarz per quant group, sum_g |s_rg| ||q_rg - zp_rg||_2
-// ||x_g||_2, plus a guard for the fp32 rounding of the full head's group sums.
-// The 16-row chunk of a seed token is computed exactly first; rows whose bound
-// reaches its largest logit flag their chunk, and the flagged chunks are
-// computed by the streaming kernel above in chunk-list mode, i.e. with the
-// full head's own arithmetic, so the winner (lowest id on ties) is the full
-// head's argmax bit for bit. Too many flagged chunks: every chunk.
+// Greedy decode needs only the argmax of the head. Each row's logit is bounded
+// by Cauchy-Schwarz per quant group, sum_g |s_rg| ||q_rg - zp_rg||_2 ||x_g||_2,
+// plus max_g |s_rg| * sum_g guard_g for the fp32 rounding of the group sums.
+// A lower bound on the logit of some row (the best row of the seed token's
+// 16-row chunk, computed here in fp32 minus twice its rounding guard) sets the
+// bar; chunks holding a row whose bound reaches it are computed by the
+// streaming kernel above in chunk-list mode, i.e. with the full head's own
+// arithmetic, so their argmax (lowest id on ties) is the full head's argmax
+// bit for bit. More chunks than the capacity: every chunk.
 
 namespace iq36 {
 
@@ -370,38 +379,57 @@ constexpr float kCertGuardRel = 1.0f / 4096.0f;  // > 16 fp32 ulps of the group 
 constexpr float kCertGuardAbs = 64.0f * 80.0f / 2097152.0f;
 constexpr int kCertArgmaxBlocks = 148;
 
-// table[r, g] = |s_rg| * ||q_rg - zp_rg||_2, rounded up to fp16.
+// table[r * ng + g] = |s_rg| * ||q_rg - zp_rg||_2 rounded up, then
+// table[rows * ng + r] = max_g |s_rg| (one thread per row; built once).
 __global__ void __launch_bounds__(256) cert_table_kernel(const uint8_t* w, const __half* s,
                                                          const uint8_t* z, int rows, int K,
                                                          __half* table) {
   const int ng = K / 128;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)rows * ng) return;
-  const int64_t r = idx / ng;
-  const int g = (int)(idx % ng);
-  const uint8_t* row = w + r * (K / 2) + g * 64;
-  const int zp = (z[idx >> 1] >> ((idx & 1) * 4)) & 15;
-  int ss = 0;  // exact: at most 128 * 225
-  for (int i = 0; i < 64; ++i) {
-    const int lo = (row[i] & 15) - zp, hi = (row[i] >> 4) - zp;
-    ss += lo * lo + hi * hi;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float smax = 0.f;
+  for (int g = 0; g < ng; ++g) {
+    const int64_t idx = (int64_t)r * ng + g;
+    const uint4* row = reinterpret_cast<const uint4*>(w + (int64_t)r * (K / 2) + g * 64);
+    const int zp = (z[idx >> 1] >> ((idx & 1) * 4)) & 15;
+    int ss = 0;  // exact: at most 128 * 225
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = row[i];
+      const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+      for (int j = 0; j < 4; ++j)
+        for (int b = 0; b < 8; ++b) {
+          const int d = (int)((words[j] >> (4 * b)) & 15u) - zp;
+          ss += d * d;
+        }
+    }
+    const float a = fabsf(__half2float(s[idx]));
+    smax = fmaxf(smax, a);
+    table[idx] = __float2half_ru(sqrtf((float)ss) * a * (1.0f + 1.0f / 1048576.0f));
   }
-  const float n =
-      sqrtf((float)ss) * fabsf(__half2float(s[r * ng + g])) * (1.0f + 1.0f / 1048576.0f);
-  table[idx] = __float2half_ru(n);
+  table[(int64_t)rows * ng + r] = __float2half_ru(smax);
 }
 
+struct CertMisc {
+  float guard_sum;  // sum_g guard_g
+  float bar;        // lower bound on the best logit of the seed chunk
+  int count;        // chunks appended by the scan
+  int done;         // argmax blocks finished
+};
+
 // One CTA of the streaming kernel's 16 consumer warps: the same staged
-// activation (stream_stage_x), then per quant group ||x_g|| (rounded up) and
-// the guard; the seed chunk as a one-entry chunk list; the chunk flags cleared.
+// activation (stream_stage_x); per quant group ||x_g|| (rounded up) and the
+// rounding guard; the seed chunk's 16 logits in fp32 (one warp per row) and
+// the bar; the counters cleared.
 __global__ void __launch_bounds__(kStreamConsumers * 32) cert_prep_kernel(
     const __half* x16, const float* x32, const float* nw, float eps, int K, int rows,
-    const int32_t* seed_token, float* xnorm, float* xguard, int* list, int* count,
-    uint8_t* flags) {
+    const __half* s, const uint8_t* z, const uint8_t* w, const __half* table,
+    const int32_t* seed_token, float* xnorm, CertMisc* misc) {
   extern __shared__ __align__(16) uint8_t sm[];
   uint4* xs = reinterpret_cast<uint4*>(sm);
   float2* xc = reinterpret_cast<float2*>(sm + K / 8 * 16);
-  float* red = reinterpret_cast<float*>(sm + K / 8 * 16 + K / 128 * 8);
+  float* red = reinterpret_cast<float*>(sm + K / 8 * 16 + K / 128 * 8);  // 16 floats
+  float* gsm = red + 16;                                                 // 32 guards
+  float* lbs = gsm + 32;                                                 // 16 row bars
   pdl_wait();
   stream_stage_x<128>(xs, xc, x16, x32, nw, eps, K, red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -429,87 +457,106 @@ __global__ void __launch_bounds__(kStreamConsumers * 32) cert_prep_kernel(
     ao = warp_sum(ao);
     if (lane == 0) {
       xnorm[g] = sqrtf(sq * (1.0f + 1.0f / 65536.0f)) * (1.0f + 1.0f / 1048576.0f);
-      xguard[g] = kCertGuardRel * (1024.f * ae + 64.f * ao + 16.f * (ae + ao)) + kCertGuardAbs;
+      gsm[g] = kCertGuardRel * (1024.f * ae + 64.f * ao + 16.f * (ae + ao)) + kCertGuardAbs;
     }
   }
-  const int nchunks = rows / 16;
-  for (int i = threadIdx.x; i < nchunks; i += blockDim.x) flags[i] = 0;
+  consumer_sync();
+  float gsum = 0.f;
+  for (int g = 0; g < ng; ++g) gsum += gsm[g];
+  gsum *= 1.0f + 1.0f / 65536.0f;
+  // the seed chunk: warp = row within the chunk
+  const int r = min(max(*seed_token, 0), rows - 1) / 16 * 16 + warp;
+  float acc = 0.f;
+  for (int c = lane; c < K / 8; c += 32) {
+    const int g = c / 16;
+    const int64_t gi = (int64_t)r * ng + g;
+    const int zp = (z[gi >> 1] >> ((gi & 1) * 4)) & 15;
+    const uint32_t wb = *reinterpret_cast<const uint32_t*>(w + (int64_t)r * (K / 2) + c * 4);
+    const uint4 v = xs[c];
+    const __half2* hp = reinterpret_cast<const __half2*>(&v);
+    // staged order: k = 0,4 | 1,5 (/16) | 2,6 | 3,7 (/16)
+    const float2 p0 = __half22float2(hp[0]), p1 = __half22float2(hp[1]);
+    const float2 p2 = __half22float2(hp[2]), p3 = __half22float2(hp[3]);
+    const float xv[8] = {p0.x, 16.f * p1.x, p2.x, 16.f * p3.x, p0.y, 16.f * p1.y, p2.y, 16.f * p3.y};
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d = fmaf((float)((int)((wb >> (4 * j)) & 15u) - zp), xv[j], d);
+    acc = fmaf(__half2float(s[gi]), d, acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const float guard = __half2float(table[(int64_t)rows * ng + r]) * gsum;
+    lbs[warp] = acc - 2.0f * guard * (1.0f + 1.0f / 1024.0f);
+  }
+  consumer_sync();
   if (threadIdx.x == 0) {
-    const int t = min(max(*seed_token, 0), rows - 1);
-    list[0] = t / 16;
-    *count = 1;
+    float bar = lbs[0];
+    for (int i = 1; i < 16; ++i) bar = fmaxf(bar, lbs[i]);
+    misc->guard_sum = gsum;
+    misc->bar = bar;
+    misc->count = 0;
+    misc->done = 0;
   }
   pdl_launch_dependents();
 }
 
-// Upper bound of every row against the seed chunk's largest exact logit;
-// surviving rows flag their chunk.
-__global__ void __launch_bounds__(256) cert_scan_kernel(const __half* table, const __half* s,
-                                                        int rows, int K, const float* xnorm,
-                                                        const float* xguard, const int* list,
-                                                        const float* logits, uint8_t* flags) {
-  __shared__ float xn[32], xg[32];
-  __shared__ float seed;
-  pdl_wait();
+// One thread per row: the bound against the bar; flagged chunks appended to
+// the list, one atomic per CTA (16 chunks). The table is constant per head and
+// read before the wait.
+__global__ void __launch_bounds__(256) cert_scan_kernel(const __half* table, int rows, int K,
+                                                        const float* xnorm, CertMisc* misc,
+                                                        int* list) {
+  __shared__ float xn[32];
+  __shared__ int fl[16];
   const int ng = K / 128;
-  if (threadIdx.x < ng) {
-    xn[threadIdx.x] = xnorm[threadIdx.x];
-    xg[threadIdx.x] = xguard[threadIdx.x];
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  float t[32];
+  float smax = 0.f;
+  if (r < rows) {
+    const uint2* tr = reinterpret_cast<const uint2*>(table + (int64_t)r * ng);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < ng / 4) {
+        const uint2 v = tr[i];
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        t[4 * i] = a.x;
+        t[4 * i + 1] = a.y;
+        t[4 * i + 2] = b.x;
+        t[4 * i + 3] = b.y;
+      }
+    smax = __half2float(table[(int64_t)rows * ng + r]);
   }
-  if (threadIdx.x == 0) {
-    const float* l = logits + (size_t)list[0] * 16;
-    float m = l[0];
-    for (int i = 1; i < 16; ++i) m = fmaxf(m, l[i]);
-    seed = m;
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
-    const __half* tr = table + (size_t)r * ng;
-    const __half* sr = s + (size_t)r * ng;
-    float up = 0.f;
-    for (int g = 0; g < ng; ++g)
-      up += __half2float(tr[g]) * xn[g] + fabsf(__half2float(sr[g])) * xg[g];
-    up *= 1.0f + 1.0f / 65536.0f;
-    if (up >= seed) flags[r / 16] = 1;
-  }
-}
-
-// Flagged chunks in index order (one CTA, block prefix sums); more than
-// `capacity` of them: every chunk (the full head).
-__global__ void __launch_bounds__(1024) cert_compact_kernel(const uint8_t* flags, int nchunks,
-                                                            int capacity, int* list, int* count) {
-  __shared__ int wsum[32];
-  __shared__ int base;
   pdl_wait();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) base = 0;
+  if (threadIdx.x < ng) xn[threadIdx.x] = xnorm[threadIdx.x];
   __syncthreads();
-  for (int c0 = 0; c0 < nchunks; c0 += 1024) {
-    const int c = c0 + tid;
-    const int f = (c < nchunks && flags[c]) ? 1 : 0;
-    const unsigned m = __ballot_sync(0xffffffffu, f);
-    const int before = __popc(m & ((1u << lane) - 1u));
-    if (lane == 0) wsum[warp] = __popc(m);
-    __syncthreads();
-    int off = 0;
-    for (int w = 0; w < warp; ++w) off += wsum[w];
-    if (f) list[base + off + before] = c;
-    __syncthreads();
-    if (tid == 0) {
-      int t = 0;
-      for (int w = 0; w < 32; ++w) t += wsum[w];
-      base += t;
-    }
-    __syncthreads();
+  bool f = false;
+  if (r < rows) {
+    float up = 0.f;
+#pragma unroll
+    for (int g = 0; g < 32; ++g)
+      if (g < ng) up = fmaf(t[g], xn[g], up);
+    up = fmaf(smax, misc->guard_sum, up) * (1.0f + 1.0f / 65536.0f);
+    f = up >= misc->bar;
   }
-  if (base > capacity) {
-    for (int c = tid; c < nchunks; c += 1024) list[c] = c;
-    if (tid == 0) *count = nchunks;
-  } else if (tid == 0) {
-    *count = base;
+  const unsigned m = __ballot_sync(0xffffffffu, f);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    fl[2 * warp] = (m & 0xFFFFu) != 0u;
+    fl[2 * warp + 1] = (m >> 16) != 0u;
   }
+  __syncthreads();
   pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int i = 0; i < 16; ++i) n += fl[i];
+    if (n > 0) {
+      int slot = atomicAdd(&misc->count, n);
+      const int nchunks = rows / 16;
+      for (int i = 0; i < 16; ++i)
+        if (fl[i] && slot < nchunks) list[slot++] = blockIdx.x * 16 + i;
+    }
+  }
 }
 
 // Order-preserving key: larger logit first, then the lower row id.
@@ -519,57 +566,67 @@ __device__ __forceinline__ uint64_t cert_key(float v, uint32_t id) {
   return ((uint64_t)ord << 32) | (uint64_t)(~id);
 }
 
-__global__ void __launch_bounds__(256) cert_argmax_kernel(const float* logits, const int* list,
-                                                          const int* count, uint64_t* partial) {
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, v, o);
+    v = other > v ? other : v;
+  }
+  return v;
+}
+
+// Argmax over the evaluated chunks; the last CTA to finish merges the
+// per-CTA keys (no waiting: the others have published theirs before counting).
+__global__ void __launch_bounds__(256) cert_argmax_kernel(const float* logits, int rows,
+                                                          const int* list, int capacity,
+                                                          CertMisc* misc, uint64_t* partial,
+                                                          int32_t* token, int32_t* evaluated) {
   __shared__ uint64_t red[8];
+  __shared__ bool last;
   pdl_wait();
-  const int n = *count * 16;
+  const int count = misc->count;
+  const bool all = count > capacity;
+  const int n = all ? rows : count * 16;
   uint64_t best = 0ull;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int row = list[i >> 4] * 16 + (i & 15);
+    const int row = all ? i : list[i >> 4] * 16 + (i & 15);
     const uint64_t k = cert_key(logits[row], (uint32_t)row);
     best = k > best ? k : best;
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-    best = other > best ? other : best;
-  }
+  best = warp_max_u64(best);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 0; w < 8; ++w) best = red[w] > best ? red[w] : best;
     partial[blockIdx.x] = best;
+    __threadfence();
+    last = atomicAdd(&misc->done, 1) == (int)gridDim.x - 1;
   }
-  pdl_launch_dependents();
-}
-
-__global__ void __launch_bounds__(32) cert_final_kernel(const uint64_t* partial, int np,
-                                                        const int* count, int32_t* token,
-                                                        int32_t* evaluated) {
-  pdl_wait();
-  uint64_t best = 0ull;
-  for (int i = threadIdx.x; i < np; i += 32) best = partial[i] > best ? partial[i] : best;
-  for (int o = 16; o > 0; o >>= 1) {
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-    best = other > best ? other : best;
-  }
-  if (threadIdx.x == 0) {
-    *token = (int32_t)(~(uint32_t)(best & 0xFFFFFFFFull));
-    if (evaluated) *evaluated = *count;
+  __syncthreads();
+  if (last && threadIdx.x < 32) {
+    __threadfence();
+    uint64_t b = 0ull;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += 32) {
+      const uint64_t v = __ldcg(reinterpret_cast<const unsigned long long*>(partial) + i);
+      b = v > b ? v : b;
+    }
+    b = warp_max_u64(b);
+    if (threadIdx.x == 0) {
+      *token = (int32_t)(~(uint32_t)(b & 0xFFFFFFFFull));
+      if (evaluated) *evaluated = all ? rows / 16 : count;
+      misc->done = 0;
+    }
   }
 }
 
 struct CertWs {
   float* xnorm;
-  float* xguard;
-  uint8_t* flags;
+  CertMisc* misc;
   int* list;
-  int* count;
   uint64_t* partial;
   size_t bytes;
 };
 
-static CertWs cert_ws(void* base, int rows, int K) {
+static CertWs cert_ws(void* base, int rows) {
   CertWs w;
   char* p = reinterpret_cast<char*>(base);
   auto take = [&](size_t n) {
@@ -577,12 +634,9 @@ static CertWs cert_ws(void* base, int rows, int K) {
     p += (n + 255) / 256 * 256;
     return q;
   };
-  const int nchunks = rows / 16;
-  w.xnorm = reinterpret_cast<float*>(take(K / 128 * 4));
-  w.xguard = reinterpret_cast<float*>(take(K / 128 * 4));
-  w.flags = reinterpret_cast<uint8_t*>(take(nchunks));
-  w.list = reinterpret_cast<int*>(take((size_t)nchunks * 4));
-  w.count = reinterpret_cast<int*>(take(16));
+  w.xnorm = reinterpret_cast<float*>(take(32 * 4));
+  w.misc = reinterpret_cast<CertMisc*>(take(sizeof(CertMisc)));
+  w.list = reinterpret_cast<int*>(take((size_t)(rows / 16) * 4));
   w.partial = reinterpret_cast<uint64_t*>(take(kCertArgmaxBlocks * 8));
   w.bytes = (size_t)(p - reinterpret_cast<char*>(base));
   return w;
@@ -591,25 +645,25 @@ static CertWs cert_ws(void* base, int rows, int K) {
 }  // namespace iq36
 
 extern "C" size_t iq36_lm_head_cert_table_bytes(int32_t rows, int32_t K, int32_t G) {
-  if (rows < 1 || G != 128 || K % 128) return 0;
-  return (size_t)rows * (K / 128) * 2;
+  if (rows < 16 || rows % 16 || G != 128 || K % 512 || K > 4096) return 0;
+  return (size_t)rows * (K / 128 + 1) * 2;
 }
 
 extern "C" int iq36_lm_head_cert_table(const iq36_u4_matrix* w, int32_t K, int32_t G,
                                        void* table_f16, iq36_stream_t stream) {
   using namespace iq36;
   if (!w || !w->weight || !w->scale || !w->zp || !table_f16) return IQ36_ERR_ARG;
-  if (G != 128 || K % 512 || K > 4096 || w->rows < 16 || w->rows % 16) return IQ36_ERR_SHAPE;
-  const int64_t n = (int64_t)w->rows * (K / 128);
-  cert_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(
+  if (iq36_lm_head_cert_table_bytes(w->rows, K, G) == 0) return IQ36_ERR_SHAPE;
+  if (!aligned(w->weight, 16) || !aligned(table_f16, 16)) return IQ36_ERR_ALIGN;
+  cert_table_kernel<<<(unsigned)((w->rows + 255) / 256), 256, 0, as_stream(stream)>>>(
       w->weight, reinterpret_cast<const __half*>(w->scale), w->zp, w->rows, K,
       reinterpret_cast<__half*>(table_f16));
   return cudaGetLastError() == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
 extern "C" size_t iq36_lm_head_top1_certified_workspace_bytes(int32_t rows, int32_t K) {
-  if (rows < 16 || K < 128) return 0;
-  return iq36::cert_ws(nullptr, rows, K).bytes;
+  if (rows < 16 || rows % 16 || K < 512) return 0;
+  return iq36::cert_ws(nullptr, rows).bytes;
 }
 
 extern "C" int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32,
@@ -630,22 +684,29 @@ extern "C" int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32
     return IQ36_ERR_ARG;
   }
   iq36_u4_projection proj{*w, logits, IQ36_F32, 0};
-  if (G != 128 || !stream_proj_ok(K, G, 1, &proj) || w->rows < 16) return IQ36_ERR_SHAPE;
+  if (iq36_lm_head_cert_table_bytes(w->rows, K, G) == 0 || !stream_proj_ok(K, G, 1, &proj))
+    return IQ36_ERR_SHAPE;
   if (capacity_chunks < 1) return IQ36_ERR_SHAPE;
-  const CertWs ws = cert_ws(workspace, w->rows, K);
+  const CertWs ws = cert_ws(workspace, w->rows);
   if (workspace_bytes < ws.bytes) return IQ36_ERR_WORKSPACE;
-  if (!aligned(workspace, 256)) return IQ36_ERR_ALIGN;
+  if (!aligned(workspace, 256) || !aligned(table_f16, 16)) return IQ36_ERR_ALIGN;
+  if (x_f16 && !aligned(x_f16, 16)) return IQ36_ERR_ALIGN;
   const cudaStream_t s = as_stream(stream);
   const int nchunks = w->rows / 16;
-  const size_t prep_smem = (size_t)K / 8 * 16 + K / 128 * 8 + 33 * 4;
+  const __half* sc = reinterpret_cast<const __half*>(w->scale);
+  const __half* tb = reinterpret_cast<const __half*>(table_f16);
+  const size_t prep_smem = (size_t)K / 8 * 16 + K / 128 * 8 + 64 * 4;
   cudaError_t e = launch(cert_prep_kernel, dim3(1), dim3(kStreamConsumers * 32), prep_smem, s,
                          reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
-                         w->rows, seed_token, ws.xnorm, ws.xguard, ws.list, ws.count, ws.flags);
+                         w->rows, sc, w->zp, w->weight, tb, seed_token, ws.xnorm, ws.misc);
+  if (e != cudaSuccess) return IQ36_ERR_CUDA;
+  e = launch(cert_scan_kernel, dim3((w->rows + 255) / 256), dim3(256), 0, s, tb, w->rows, K,
+             (const float*)ws.xnorm, ws.misc, ws.list);
   if (e != cudaSuccess) return IQ36_ERR_CUDA;
   StreamProj ps = {};
   ps.n_proj = 1;
   ps.w[0] = w->weight;
-  ps.s[0] = reinterpret_cast<const __half*>(w->scale);
+  ps.s[0] = sc;
   ps.z[0] = w->zp;
   ps.out[0] = logits;
   ps.dtype[0] = IQ36_F32;
@@ -653,33 +714,18 @@ extern "C" int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32
   ps.chunk_start[0] = 0;
   ps.chunk_start[1] = nchunks;
   ps.chunk_list = ws.list;
-  ps.chunk_count = ws.count;
+  ps.chunk_count = &ws.misc->count;
+  ps.chunk_capacity = capacity_chunks;
   const StreamGeom geo = stream_geom(K, G);
   const StreamSmem L = stream_smem(geo, K, G);
   if (stream_attr((const void*)u4_stream_proj_kernel<128>) != IQ36_OK) return IQ36_ERR_CUDA;
-  // the seed chunk, exactly (one CTA)
-  e = launch(u4_stream_proj_kernel<128>, dim3(1), dim3(kStreamThreads), (size_t)L.total, s, ps,
-             reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
-             (int*)nullptr);
-  if (e != cudaSuccess) return IQ36_ERR_CUDA;
-  e = launch(cert_scan_kernel, dim3(kStreamCtas * 4), dim3(256), 0, s,
-             reinterpret_cast<const __half*>(table_f16), reinterpret_cast<const __half*>(w->scale),
-             w->rows, K, (const float*)ws.xnorm, (const float*)ws.xguard, (const int*)ws.list,
-             (const float*)logits, ws.flags);
-  if (e != cudaSuccess) return IQ36_ERR_CUDA;
-  e = launch(cert_compact_kernel, dim3(1), dim3(1024), 0, s, (const uint8_t*)ws.flags, nchunks,
-             (int)capacity_chunks, ws.list, ws.count);
-  if (e != cudaSuccess) return IQ36_ERR_CUDA;
-  // the flagged chunks, exactly
   e = launch(u4_stream_proj_kernel<128>, dim3(std::min(kStreamCtas, nchunks)),
              dim3(kStreamThreads), (size_t)L.total, s, ps,
              reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
              (int*)nullptr);
   if (e != cudaSuccess) return IQ36_ERR_CUDA;
   e = launch(cert_argmax_kernel, dim3(kCertArgmaxBlocks), dim3(256), 0, s, (const float*)logits,
-             (const int*)ws.list, (const int*)ws.count, ws.partial);
-  if (e != cudaSuccess) return IQ36_ERR_CUDA;
-  e = launch(cert_final_kernel, dim3(1), dim3(32), 0, s, (const uint64_t*)ws.partial,
-             kCertArgmaxBlocks, (const int*)ws.count, token_out, evaluated_chunks);
+             w->rows, (const int*)ws.list, (int)capacity_chunks, ws.misc, ws.partial, token_out,
+             evaluated_chunks);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }

@@ -301,7 +301,7 @@ class Qwen36Runtime:
                                        self.token, x_f32=self.hres, norm_weight=W.final_norm,
                                        norm_eps=c.eps, capacity_chunks=self.lm_capacity,
                                        evaluated=self.lm_evaluated, workspace=self.ws_cert)
-            n += 7
+            n += 4
         else:
             ops.u4_matvec_multi(None, [W.lm_head], [self.logits], x_f32=self.hres,
                                 norm_weight=W.final_norm, norm_eps=c.eps)

@@ -497,18 +497,20 @@ size_t iq36_argmax_workspace_bytes(void);
  * The reference's certificate (engine/gpu/opencl/
  * iq36_lm_head_affine_q4_group128_component.cl:126-217 bound scan and
  * candidate selection, :219-300 exact candidates and top-1, the full path as
- * capacity fallback) for the u4 group-128 head: every row's logit is bounded
+ * capacity fallback) for the u4 group-128 head. Every row's logit is bounded
  * by sum_g |s_rg| ||q_rg - zp_rg||_2 ||x_g||_2 plus a guard covering the fp32
- * rounding of the full head's group sums; the 16-row chunk of *seed_token is
- * computed exactly first, rows whose bound reaches its largest logit flag
- * their chunk, and the flagged chunks are computed exactly by the full head's
- * own kernel in chunk-list mode, so token_out equals the full head's argmax
- * (lowest id on ties) bit for bit. More than capacity_chunks flagged chunks:
- * every chunk (the full head). logits [rows] receives the evaluated chunks'
- * logits only; *evaluated_chunks (optional, device) their number.
+ * rounding of the full head's group sums. The best row of *seed_token's
+ * 16-row chunk, computed in fp32 and lowered by twice its guard, sets the
+ * bar; every chunk holding a row whose bound reaches the bar is computed by
+ * the full head's own kernel (chunk-list mode), so token_out equals the full
+ * head's argmax (lowest id on ties) bit for bit. More than capacity_chunks
+ * such chunks: every chunk (the full head). logits [rows] receives the
+ * evaluated chunks' logits only; *evaluated_chunks (optional, device) their
+ * number. Four launches (prep, bound scan, GEMV, argmax), PDL-chained.
  * Requirements: those of the weight-streaming GEMV (G 128, rows % 16 == 0,
- * K % 512 == 0, K <= 4096). table: iq36_lm_head_cert_table_bytes, written
- * once by iq36_lm_head_cert_table (fp16 |s| * group norm, rounded up).
+ * K % 512 == 0, K <= 4096). table: iq36_lm_head_cert_table_bytes bytes,
+ * written once per head by iq36_lm_head_cert_table ([rows, K/128] fp16
+ * |s| * group norm rounded up, then [rows] fp16 max |s|).
  * seed_token may alias token_out (it is read before token_out is written). */
 size_t iq36_lm_head_cert_table_bytes(int32_t rows, int32_t K, int32_t G);
 int iq36_lm_head_cert_table(const iq36_u4_matrix* w, int32_t K, int32_t G, void* table_f16,
