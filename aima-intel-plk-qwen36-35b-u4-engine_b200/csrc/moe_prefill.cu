@@ -325,6 +325,11 @@ struct GemmArgs {
   const uint8_t* pz[4];
   void* pout[4];
   int prow[4], pdt[4], pacc[4];
+  // MODE 2/3 only: group 64 (one quant group per 64-wide k-block). The scales
+  // and zero points are then read by the dequant threads from global memory
+  // one k-block ahead (a unit's 64 groups per row would not fit the staging
+  // buffers); group 128 stages them per unit in shared memory.
+  int g64;
 };
 
 // projection of a MODE-2 N tile and the tile's index inside it
@@ -448,7 +453,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int nN = (MODE == 0 || MODE == 3) ? g.I / 128 : g.H / kPfBN;
   const int total = pf_units<MODE>(g);
   const int nkb = g.K / kPfBK;
-  const int ng = g.K / 128;
+  const bool g64 = (MODE == 2 || MODE == 3) && g.g64;
+  const int ng = g64 ? g.K / 64 : g.K / 128;
   bool ok = true;
 
   if (warp == 0) {
@@ -507,19 +513,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int it = 0, i = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
         const PfUnit un = pf_unit<MODE>(g, u, nN);
-        const int b = i & 1;
-        ok = mbar_wait(bar_sempty + 8 * b, ((i >> 1) & 1) ^ 1u);
-        if (!ok) break;
-        const uint32_t sdst = base + kPfOffScale + b * kPfScaleBuf;
-        const uint32_t zdst = base + kPfOffZp + b * kPfZpBuf;
-        mbar_arrive_tx(bar_sfull + 8 * b, 2u * (sbytes + zbytes));
-        const __half* sp = MODE == 2 ? g.ps[un.proj] : g.s;
-        const uint8_t* zp = MODE == 2 ? g.pz[un.proj] : g.z;
         const CUtensorMap* wmap = un.proj == 0 ? &tmW : un.proj == 1 ? &tmW1 : un.proj == 2 ? &tmW2 : &tmW3;
-        bulk_load(sdst, sp + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
-        bulk_load(sdst + sbytes, sp + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
-        bulk_load(zdst, zp + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
-        bulk_load(zdst + zbytes, zp + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
+        if (!g64) {
+          const int b = i & 1;
+          ok = mbar_wait(bar_sempty + 8 * b, ((i >> 1) & 1) ^ 1u);
+          if (!ok) break;
+          const uint32_t sdst = base + kPfOffScale + b * kPfScaleBuf;
+          const uint32_t zdst = base + kPfOffZp + b * kPfZpBuf;
+          mbar_arrive_tx(bar_sfull + 8 * b, 2u * (sbytes + zbytes));
+          const __half* sp = MODE == 2 ? g.ps[un.proj] : g.s;
+          const uint8_t* zp = MODE == 2 ? g.pz[un.proj] : g.z;
+          bulk_load(sdst, sp + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
+          bulk_load(sdst + sbytes, sp + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
+          bulk_load(zdst, zp + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
+          bulk_load(zdst + zbytes, zp + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
+        }
         // nkb is a multiple of kPfCodeKB, so code blocks never straddle units
         for (int cb = 0; cb < nkb / kPfCodeKB; ++cb, ++it) {
           const int cs = it % kPfCodeStages;
@@ -542,12 +550,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     int it = 0, i = 0;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
       const int b = i & 1;
-      ok = mbar_wait(bar_sfull + 8 * b, (i >> 1) & 1);
-      if (!ok) break;
-      // rows 0..127 then 128..255 are consecutive in both buffers
-      const __half* ssc =
-          reinterpret_cast<const __half*>(smem + kPfOffScale + b * kPfScaleBuf) + n * ng;
-      const uint8_t* szp = smem + kPfOffZp + b * kPfZpBuf + n * ng / 2;
+      const __half* ssc;
+      const uint8_t* szp;
+      __half gsc = __ushort_as_half((unsigned short)0);
+      uint32_t gzb = 0;
+      if (!g64) {
+        ok = mbar_wait(bar_sfull + 8 * b, (i >> 1) & 1);
+        if (!ok) break;
+        // rows 0..127 then 128..255 are consecutive in both buffers
+        ssc = reinterpret_cast<const __half*>(smem + kPfOffScale + b * kPfScaleBuf) + n * ng;
+        szp = smem + kPfOffZp + b * kPfZpBuf + n * ng / 2;
+      } else {
+        // this thread's weight row in global memory: rows wr0.. then wr1..
+        const PfUnit un = pf_unit<MODE>(g, u, nN);
+        const int64_t row = n < 128 ? un.wr0 + n : un.wr1 + (n - 128);
+        ssc = (MODE == 2 ? g.ps[un.proj] : g.s) + row * ng;
+        szp = (MODE == 2 ? g.pz[un.proj] : g.z) + row * ng / 2;
+        gsc = __ldg(ssc);
+        gzb = __ldg(szp);
+      }
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % kPfBStages;
         const int ic = it / kPfCodeKB, cs = ic % kPfCodeStages, sub = it % kPfCodeKB;
@@ -558,11 +579,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         ok = mbar_wait(bar_empty + 8 * s, ((it / kPfBStages) & 1) ^ 1u);
         if (!ok) break;
         uint8_t* bst = smem + kPfOffB + s * kPfBStage + n * 128;
-        const int grp = kb >> 1;
-        const __half sc = ssc[grp];
+        __half sc;
+        uint32_t zz;
+        if (!g64) {
+          const int grp = kb >> 1;
+          sc = ssc[grp];
+          zz = (uint32_t)(szp[grp >> 1] >> ((grp & 1) * 4)) & 15u;
+        } else {
+          // group kb; the next k-block's scale and zero-point byte are
+          // requested now and arrive while this one is dequantised
+          sc = gsc;
+          zz = (gzb >> ((kb & 1) * 4)) & 15u;
+          if (kb + 1 < nkb) {
+            gsc = __ldg(ssc + kb + 1);
+            if (kb & 1) gzb = __ldg(szp + ((kb + 1) >> 1));
+          }
+        }
         const __half2 s2 = __halves2half2(sc, sc);
         const __half2 s16 = __hmul2(s2, sixteenth);
-        const uint32_t zz = (uint32_t)(szp[grp >> 1] >> ((grp & 1) * 4)) & 15u;
         const uint32_t zlo = 0x64006400u | zz | (zz << 16);
         const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
         const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v);
@@ -595,7 +629,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (sub == kPfCodeKB - 1) mbar_arrive(bar_cempty + 8 * cs);  // release the code slot
         mbar_arrive(bar_full + 8 * s);
       }
-      if (ok) mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales (fenced above)
+      if (ok && !g64) mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales (fenced above)
     }
   } else {
     // ---- epilogue: TMEM -> registers -> global, one tile row per thread ----
@@ -1160,7 +1194,7 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
   if (nw && x_dtype != IQ36_F32) return IQ36_ERR_ARG;
   if (swiglu && n_proj != 1) return IQ36_ERR_ARG;
   if (row_gate && n_proj != 1) return IQ36_ERR_ARG;
-  if (G != 128 || T < 1 || K < 256 || K % 256 || K > 4096) return IQ36_ERR_SHAPE;
+  if ((G != 128 && G != 64) || T < 1 || K < 256 || K % 256 || K > 4096) return IQ36_ERR_SHAPE;
   if (!aligned(x, 16)) return IQ36_ERR_ALIGN;
   int total_rows = 0;
   for (int p = 0; p < n_proj; ++p) {
@@ -1211,6 +1245,7 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
   GemmArgs g{reinterpret_cast<const __half*>(w0->scale), w0->zp, 0, K, w0->rows / 2,
              total_rows, wk, T, proj[0].out, proj[0].out_dtype, proj[0].accumulate, row_gate};
   g.n_proj = n_proj;
+  g.g64 = G == 64;
   g.tile_base[0] = 0;
   for (int p = 0; p < 4; ++p) {
     const bool have = p < n_proj;

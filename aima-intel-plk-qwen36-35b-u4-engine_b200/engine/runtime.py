@@ -55,9 +55,16 @@ class ModelConfig:
     inter: int = 512
     shared_inter: int = 512
     vocab: int = 248320
-    group: int = 128
+    group: int = 128      # experts, shared expert, LM head
     rope_base: float = 1e7
     eps: float = 1e-6
+    # attention q/k/v/o and DeltaNet in/out projections (the reference's fixed
+    # FCs; its checkpoint quantises them at group 64, fixed_fc.py:26); 0 = group
+    fc_group: int = 0
+
+    @property
+    def proj_group(self) -> int:
+        return self.fc_group or self.group
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -70,17 +77,20 @@ class ModelConfig:
         weight (codes + scales + zero points) read once, fp16 router/shared-gate
         weights, the KV cache of the attention layers, and the DeltaNet state
         read and written once."""
-        h, g = self.hidden, self.group
+        h = self.hidden
 
-        def u4(rows, k):
+        def u4(rows, k, g=self.group):
             return rows * k // 2 + rows * (k // g) * 2 + rows * (k // g) // 2
+
+        def fc(rows, k):
+            return u4(rows, k, self.proj_group)
 
         n_attn = sum(self.is_attn(l) for l in range(self.layers))
         n_delta = self.layers - n_attn
-        attn = u4(2 * self.nq * self.head_dim, h) + 2 * u4(self.nkv * self.head_dim, h) + u4(
+        attn = fc(2 * self.nq * self.head_dim, h) + 2 * fc(self.nkv * self.head_dim, h) + fc(
             h, self.nq * self.head_dim)
         c = (2 * self.nk + self.nv) * self.dk
-        delta = u4(c, h) + u4(self.nv * self.dk, h) + 2 * u4(self.nv, h) + u4(h, self.nv * self.dk)
+        delta = fc(c, h) + fc(self.nv * self.dk, h) + 2 * fc(self.nv, h) + fc(h, self.nv * self.dk)
         moe = (self.experts * h * 2 + h * 2 + (self.topk + 1) * (
             u4(2 * self.inter, h) + u4(h, self.inter)))
         lm = u4(self.vocab, h)
@@ -106,24 +116,25 @@ class SyntheticWeights:
     def __init__(self, cfg: ModelConfig, seed: int, device: torch.device):
         self.cfg, self.seed, self.dev = cfg, seed, device
         c, h, g = cfg, cfg.hidden, cfg.group
+        fc = cfg.proj_group
         self.layers = []
         for l in range(c.layers):
             L = {"in_norm": self._f32(h, l, T_IN_NORM), "post_norm": self._f32(h, l, T_POST_NORM)}
             if c.is_attn(l):
-                L["q"] = self._u4(2 * c.nq * c.head_dim, h, l, T_Q)
-                L["k"] = self._u4(c.nkv * c.head_dim, h, l, T_K)
-                L["v"] = self._u4(c.nkv * c.head_dim, h, l, T_V)
-                L["o"] = self._u4(h, c.nq * c.head_dim, l, T_O)
+                L["q"] = self._u4(2 * c.nq * c.head_dim, h, l, T_Q, fc)
+                L["k"] = self._u4(c.nkv * c.head_dim, h, l, T_K, fc)
+                L["v"] = self._u4(c.nkv * c.head_dim, h, l, T_V, fc)
+                L["o"] = self._u4(h, c.nq * c.head_dim, l, T_O, fc)
                 L["qn"] = self._f32(c.head_dim, l, T_QNORM)
                 L["kn"] = self._f32(c.head_dim, l, T_KNORM)
             else:
                 ch = (2 * c.nk + c.nv) * c.dk
-                L["qkv"] = self._u4(ch, h, l, T_QKV)
-                L["z"] = self._u4(c.nv * c.dk, h, l, T_Z)
-                L["a"] = self._u4(c.nv, h, l, T_A)
-                L["b"] = self._u4(c.nv, h, l, T_B)
+                L["qkv"] = self._u4(ch, h, l, T_QKV, fc)
+                L["z"] = self._u4(c.nv * c.dk, h, l, T_Z, fc)
+                L["a"] = self._u4(c.nv, h, l, T_A, fc)
+                L["b"] = self._u4(c.nv, h, l, T_B, fc)
                 L["ab"] = self._gate_pair(L["a"], L["b"])
-                L["out"] = self._u4(h, c.nv * c.dk, l, T_OUT)
+                L["out"] = self._u4(h, c.nv * c.dk, l, T_OUT, fc)
                 L["conv_w"] = self._f32(ch * c.conv, l, T_CONV)
                 L["a_log"] = self._f32(c.nv, l, T_ALOG)
                 L["dt_bias"] = self._f32(c.nv, l, T_DTB)
@@ -173,8 +184,8 @@ class SyntheticWeights:
                         a.zp.new_zeros(pad * a.scale.shape[1] // 2)])
         return ops.U4Weight(w, sc, zp, a.group)
 
-    def _u4(self, rows, k, layer, slot) -> ops.U4Weight:
-        g = self.cfg.group
+    def _u4(self, rows, k, layer, slot, group: int = 0) -> ops.U4Weight:
+        g = group or self.cfg.group
         w = self._fill(torch.empty(rows, k // 2, dtype=torch.uint8, device=self.dev), layer, slot, 0)
         s = self._fill(torch.empty(rows, k // g, dtype=torch.float16, device=self.dev), layer, slot, 1)
         z = self._fill(torch.empty(rows * (k // g) // 2, dtype=torch.uint8, device=self.dev),

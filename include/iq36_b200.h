@@ -270,14 +270,15 @@ size_t iq36_moe_layer_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_
                                               int32_t hidden, int32_t intermediate);
 
 /* Dense u4 GEMM for batched (prefill) projections: out[T, N] = x W^T with
- * W = (q - zp) * s (group 128 along K), fp16 operands on tcgen05 tensor cores,
+ * W = (q - zp) * s (group 128 or 64 along K: the reference's fixed FCs are
+ * group 64, fixed_fc.py:26), fp16 operands on tcgen05 tensor cores,
  * fp32 accumulate. x is fp16 [T, K], or fp32 [T, K] optionally RMS-normalised
  * in the prologue with norm_weight / norm_eps and rounded to fp16 (as the
  * decode projections do). out: fp16 [T, N] store, or fp32 [T, N] store
  * (accumulate = 0) or residual update out += f16(x W^T) (accumulate = 1).
  * The batched form of the fixed-FC projections (IQ36FixedFC over [T, K],
  * tools/intel_qwen36_openvino_fixed_fc.py:31-92; the prefill buckets of the
- * OpenVINO graph run the same FCs with M = T). Requirements: group 128,
+ * OpenVINO graph run the same FCs with M = T). Requirements: group 128 or 64,
  * K % 256 == 0, K <= 4096, N % 256 == 0. */
 int iq36_u4_gemm(const void* x, int32_t x_dtype, const float* norm_weight, float norm_eps,
                  int32_t T, int32_t K, int32_t group, const iq36_u4_matrix* w, void* out,

@@ -74,6 +74,7 @@ struct OrcModelConfig {
   int32_t hidden, layers, attn_interval, nq, nkv, head_dim, rope_dim, nk, nv, dk, conv, experts,
       topk, inter, shared_inter, vocab, group;
   float rope_base, eps;
+  int32_t fc_group;  // attention and DeltaNet projections (0: group)
 };
 
 namespace {
@@ -214,7 +215,7 @@ void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
   M->seed = seed;
   M->max_ctx = max_ctx;
   const OrcModelConfig& c = *cfg;
-  const int H = c.hidden, G = c.group;
+  const int H = c.hidden, G = c.group, FG = c.fc_group > 0 ? c.fc_group : c.group;
   M->layers.resize(c.layers);
   for (int l = 0; l < c.layers; ++l) {
     Layer& L = M->layers[l];
@@ -222,10 +223,10 @@ void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
     fill_f32(L.in_norm, H, seed, l, IQ36_T_IN_NORM);
     fill_f32(L.post_norm, H, seed, l, IQ36_T_POST_NORM);
     if (L.attn) {
-      fill_u4(L.q, (int64_t)2 * c.nq * c.head_dim, H, G, seed, l, IQ36_T_Q);
-      fill_u4(L.k, (int64_t)c.nkv * c.head_dim, H, G, seed, l, IQ36_T_K);
-      fill_u4(L.v, (int64_t)c.nkv * c.head_dim, H, G, seed, l, IQ36_T_V);
-      fill_u4(L.o, H, c.nq * c.head_dim, G, seed, l, IQ36_T_O);
+      fill_u4(L.q, (int64_t)2 * c.nq * c.head_dim, H, FG, seed, l, IQ36_T_Q);
+      fill_u4(L.k, (int64_t)c.nkv * c.head_dim, H, FG, seed, l, IQ36_T_K);
+      fill_u4(L.v, (int64_t)c.nkv * c.head_dim, H, FG, seed, l, IQ36_T_V);
+      fill_u4(L.o, H, c.nq * c.head_dim, FG, seed, l, IQ36_T_O);
       fill_f32(L.qn, c.head_dim, seed, l, IQ36_T_QNORM);
       fill_f32(L.kn, c.head_dim, seed, l, IQ36_T_KNORM);
       const int64_t blocks = (max_ctx + 15) / 16;
@@ -233,11 +234,11 @@ void* orc_model_create(const OrcModelConfig* cfg, uint64_t seed, int max_ctx) {
       L.vc.assign(blocks * 16 * c.nkv * c.head_dim, 0);
     } else {
       const int64_t C = (int64_t)(2 * c.nk + c.nv) * c.dk;
-      fill_u4(L.qkv, C, H, G, seed, l, IQ36_T_QKV);
-      fill_u4(L.z, (int64_t)c.nv * c.dk, H, G, seed, l, IQ36_T_Z);
-      fill_u4(L.a, c.nv, H, G, seed, l, IQ36_T_A);
-      fill_u4(L.b, c.nv, H, G, seed, l, IQ36_T_B);
-      fill_u4(L.out, H, c.nv * c.dk, G, seed, l, IQ36_T_OUT);
+      fill_u4(L.qkv, C, H, FG, seed, l, IQ36_T_QKV);
+      fill_u4(L.z, (int64_t)c.nv * c.dk, H, FG, seed, l, IQ36_T_Z);
+      fill_u4(L.a, c.nv, H, FG, seed, l, IQ36_T_A);
+      fill_u4(L.b, c.nv, H, FG, seed, l, IQ36_T_B);
+      fill_u4(L.out, H, c.nv * c.dk, FG, seed, l, IQ36_T_OUT);
       fill_f32(L.conv_w, C * c.conv, seed, l, IQ36_T_CONV);
       fill_f32(L.a_log, c.nv, seed, l, IQ36_T_ALOG);
       fill_f32(L.dt_bias, c.nv, seed, l, IQ36_T_DTB);
@@ -311,7 +312,7 @@ int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads,
                        float* hidden, int32_t* ids_out, float* router_out) {
   Model& M = *static_cast<Model*>(mp);
   const OrcModelConfig& c = M.c;
-  const int H = c.hidden, G = c.group;
+  const int H = c.hidden, G = c.group, FG = c.fc_group > 0 ? c.fc_group : c.group;
   std::vector<float> h(H), xn(H), y, y2, y3, y4;
   {
     int kind;
@@ -332,9 +333,9 @@ int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads,
     const auto x16 = to_f16(xn);
     if (L.attn) {
       const int D = c.head_dim;
-      gemv16(L.q, x16.data(), G, y, threads, M.precise);
-      gemv16(L.k, x16.data(), G, y2, threads, M.precise);
-      gemv16(L.v, x16.data(), G, y3, threads, M.precise);
+      gemv16(L.q, x16.data(), FG, y, threads, M.precise);
+      gemv16(L.k, x16.data(), FG, y2, threads, M.precise);
+      gemv16(L.v, x16.data(), FG, y3, threads, M.precise);
       const auto qf = to_f16(y), kf = to_f16(y2), vf = to_f16(y3);
       std::vector<float> qo(c.nq * D), go(c.nq * D), kn(c.nkv * D), vn(c.nkv * D);
       orc_attn_prep(qf.data(), kf.data(), vf.data(), L.qn.data(), L.kn.data(), c.eps, pos, c.nq,
@@ -350,14 +351,14 @@ int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads,
       orc_paged_gqa(q16.data(), L.kc.data(), L.vc.data(), M.bt.data(), pos + 1, c.nq, c.nkv, D,
                     16, 1.0f / std::sqrt((float)D), g16.data(), att.data(), threads);
       const auto a16 = to_f16(att);
-      gemv16(L.o, a16.data(), G, y4, threads, M.precise);
+      gemv16(L.o, a16.data(), FG, y4, threads, M.precise);
     } else {
       const int C = (2 * c.nk + c.nv) * c.dk;
-      gemv16(L.qkv, x16.data(), G, y, threads, M.precise);
-      gemv16(L.z, x16.data(), G, y2, threads, M.precise);
+      gemv16(L.qkv, x16.data(), FG, y, threads, M.precise);
+      gemv16(L.z, x16.data(), FG, y2, threads, M.precise);
       std::vector<float> ya, yb;
-      gemv16(L.a, x16.data(), G, ya, threads, M.precise);
-      gemv16(L.b, x16.data(), G, yb, threads, M.precise);
+      gemv16(L.a, x16.data(), FG, ya, threads, M.precise);
+      gemv16(L.b, x16.data(), FG, yb, threads, M.precise);
       const auto qkv16 = to_f16(y), z16 = to_f16(y2), a16 = to_f16(ya), b16 = to_f16(yb);
       std::vector<float> act(C), g(c.nv), beta(c.nv), o(c.nv * c.dk);
       orc_delta_prep(qkv16.data(), C, L.conv_state.data(), L.conv_w.data(), a16.data(),
@@ -366,7 +367,7 @@ int orc_model_step_opt(void* mp, int token, int pos, float* logits, int threads,
       orc_delta_step(act.data(), g.data(), beta.data(), L.rec_state.data(), z16.data(),
                      L.dnorm.data(), c.eps, c.nk, c.nv, c.dk, o.data());
       const auto o16 = to_f16(o);
-      gemv16(L.out, o16.data(), G, y4, threads, M.precise);
+      gemv16(L.out, o16.data(), FG, y4, threads, M.precise);
     }
     for (int i = 0; i < H; ++i) h[i] += h2f(f2h(y4[i]));
     orc_rms_norm(h.data(), 1, H, L.post_norm.data(), H, c.eps, xn.data());

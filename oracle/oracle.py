@@ -43,7 +43,7 @@ class ModelConfig(Structure):
     _fields_ = [(n, c_int32) for n in (
         "hidden", "layers", "attn_interval", "nq", "nkv", "head_dim", "rope_dim", "nk", "nv",
         "dk", "conv", "experts", "topk", "inter", "shared_inter", "vocab", "group")] + [
-        ("rope_base", c_float), ("eps", c_float)]
+        ("rope_base", c_float), ("eps", c_float), ("fc_group", c_int32)]
 
 
 def _p(a: np.ndarray | None):

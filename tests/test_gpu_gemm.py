@@ -21,35 +21,39 @@ def _t(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-@pytest.mark.parametrize("T,N", [(300, 512), (129, 256), (1, 768)])
-def test_u4_gemm_fused_norm_f16_out(cuda, T, N):
+@pytest.mark.parametrize("T,N,G", [(300, 512, 128), (129, 256, 128), (1, 768, 128),
+                                   (300, 512, 64), (129, 768, 64)])
+def test_u4_gemm_fused_norm_f16_out(cuda, T, N, G):
     import torch
     from engine.ops import u4_gemm
-    rng = np.random.default_rng(T * 31 + N)
+    rng = np.random.default_rng(T * 31 + N + G)
     K = 2048
-    w, s, z = make_u4(rng, N, K)
+    w, s, z = make_u4(rng, N, K, G)
     x = (rng.standard_normal((T, K)) * 2).astype(np.float32)
     nw = rng.uniform(0.9, 1.1, K).astype(np.float32)
-    out = u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda), out_dtype=torch.float16,
+    out = u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda, G), out_dtype=torch.float16,
                   norm_weight=_t(nw, cuda))
     got = out.float().cpu().numpy()
     for t in range(T):
         x16 = oracle.rms_norm(x[t], nw, 1e-6).astype(np.float16)
-        assert_close(got[t], oracle.u4_gemv(x16, w, s, z, 128), f"gemm row {t}")
+        assert_close(got[t], oracle.u4_gemv(x16, w, s, z, G), f"gemm row {t}")
 
 
-def test_u4_gemm_k4096_residual_accumulate(cuda):
+@pytest.mark.parametrize("G", [128, 64])
+def test_u4_gemm_k4096_residual_accumulate(cuda, G):
+    """K = 4096 at group 64 is 64 groups per row: the case the shared-memory
+    scale staging of group 128 cannot hold."""
     from engine.ops import u4_gemm
-    rng = np.random.default_rng(9)
+    rng = np.random.default_rng(9 + G)
     T, K, N = 200, 4096, 512
-    w, s, z = make_u4(rng, N, K)
+    w, s, z = make_u4(rng, N, K, G)
     x = rng.standard_normal((T, K)).astype(np.float16)
     res0 = rng.standard_normal((T, N)).astype(np.float32)
     res = _t(res0.copy(), cuda)
-    u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda), out=res, accumulate=True)
+    u4_gemm(_t(x, cuda), u4_to_torch(w, s, z, cuda, G), out=res, accumulate=True)
     got = res.cpu().numpy()
     for t in range(0, T, 7):
-        ref = res0[t] + oracle.u4_gemv(x[t], w, s, z, 128).astype(np.float16).astype(np.float32)
+        ref = res0[t] + oracle.u4_gemv(x[t], w, s, z, G).astype(np.float16).astype(np.float32)
         assert_close(got[t], ref, f"gemm accumulate row {t}")
 
 
@@ -63,7 +67,8 @@ def test_u4_gemm_rejects_bad_shapes(cuda):
         u4_gemm(torch.zeros(4, 2048, dtype=torch.float16, device=cuda), u4_to_torch(w, s, z, cuda))
 
 
-def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda):
+@pytest.mark.parametrize("G", [128, 64])
+def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda, G):
     """Three projections of one input in one launch (the DeltaNet in-projection
     shape family): each output equals its own iq36_u4_gemm bit for bit, and the
     oracle's GEMV per row; a fourth, fp32-accumulating output checks the
@@ -72,12 +77,12 @@ def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda):
     from engine.ops import u4_gemm, u4_gemm_multi
     rng = np.random.default_rng(77)
     T, K = 200, 2048
-    mats = [make_u4(rng, n, K) for n in (512, 256, 768)]
-    ws = [u4_to_torch(w, s, z, cuda) for w, s, z in mats]
+    mats = [make_u4(rng, n, K, G) for n in (512, 256, 768)]
+    ws = [u4_to_torch(w, s, z, cuda, G) for w, s, z in mats]
     x = (rng.standard_normal((T, K)) * 2).astype(np.float32)
     nw = rng.uniform(0.9, 1.1, K).astype(np.float32)
     outs = [torch.empty(T, w.rows, dtype=torch.float16, device=cuda) for w in ws]
-    acc_w = u4_to_torch(*make_u4(rng, 256, K), cuda)
+    acc_w = u4_to_torch(*make_u4(rng, 256, K, G), cuda, G)
     res0 = rng.standard_normal((T, 256)).astype(np.float32)
     res = _t(res0.copy(), cuda)
     u4_gemm_multi(_t(x, cuda), ws + [acc_w], outs + [res], accumulate=[False] * 3 + [True],
@@ -89,7 +94,7 @@ def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda):
     for t in (0, 77, T - 1):
         x16 = oracle.rms_norm(x[t], nw, 1e-6).astype(np.float16)
         for (w, s, z), g in zip(mats, got):
-            assert_close(g[t], oracle.u4_gemv(x16, w, s, z, 128), f"multi row {t}")
+            assert_close(g[t], oracle.u4_gemv(x16, w, s, z, G), f"multi row {t}")
     single_res = _t(res0.copy(), cuda)
     u4_gemm(_t(x, cuda), acc_w, out=single_res, accumulate=True, norm_weight=_t(nw, cuda))
     assert torch.equal(single_res, res)

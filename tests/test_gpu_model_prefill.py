@@ -82,10 +82,14 @@ def _small_cfg():
     return ModelConfig(layers=4, experts=16, vocab=4096)
 
 
-@pytest.mark.parametrize("prompt_len,chunk", [(40, 8192), (40, 16), (1, 8192)])
-def test_batched_prefill_matches_oracle_then_decodes(cuda, prompt_len, chunk):
-    from engine.runtime import Qwen36Runtime
-    cfg = _small_cfg()
+@pytest.mark.parametrize("prompt_len,chunk,fc_group", [(40, 8192, 0), (40, 16, 0), (1, 8192, 0),
+                                                      (40, 8192, 64)])
+def test_batched_prefill_matches_oracle_then_decodes(cuda, prompt_len, chunk, fc_group):
+    """fc_group 64: the attention and DeltaNet projections at the reference
+    checkpoint's group size (prompt GEMMs and decode GEMVs at group 64; experts
+    and LM head stay at 128)."""
+    from engine.runtime import ModelConfig, Qwen36Runtime
+    cfg = ModelConfig(layers=4, experts=16, vocab=4096, fc_group=fc_group)
     seed = 4242
     rt = Qwen36Runtime(cfg, seed=seed, max_ctx=96, device=cuda)
     rt.capture()
