@@ -34,16 +34,18 @@ int attn_wait_timeouts(int* count, int reset);
 int gemm_wait_timeouts(int* count, int reset);
 int moe_wait_timeouts(int* count, int reset);
 int tp_wait_timeouts(int* count, int reset);
+int delta_wait_timeouts(int* count, int reset);
 }
 
 extern "C" int iq36_wait_timeouts(int32_t* count, int32_t reset) {
   if (count == nullptr) return IQ36_ERR_ARG;
-  int c = 0, a = 0, g = 0, m = 0, t = 0;
+  int c = 0, a = 0, g = 0, m = 0, t = 0, d = 0;
   int st = iq36::stream_wait_timeouts(&c, reset);
   if (st == IQ36_OK) st = iq36::attn_wait_timeouts(&a, reset);
   if (st == IQ36_OK) st = iq36::gemm_wait_timeouts(&g, reset);
   if (st == IQ36_OK) st = iq36::moe_wait_timeouts(&m, reset);
   if (st == IQ36_OK) st = iq36::tp_wait_timeouts(&t, reset);
-  *count = c + a + g + m + t;
+  if (st == IQ36_OK) st = iq36::delta_wait_timeouts(&d, reset);
+  *count = c + a + g + m + t + d;
   return st;
 }

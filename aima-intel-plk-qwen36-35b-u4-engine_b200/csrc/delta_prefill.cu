@@ -33,6 +33,7 @@
 
 #include "launch.cuh"
 #include "common.cuh"
+#include "tc_sm100.cuh"
 
 namespace iq36 {
 
@@ -168,19 +169,33 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
   asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(lo) : "f"(r));
 }
 constexpr int kCk = 32;  // tokens per chunk
-// Per (chunk, value head) operand block (floats): W [32][128], U [32][128],
-// Qg = e^G q [32][128], Kt = e^(G_last - G) k key-major [128][32], P [32][32],
-// gC = e^G_last.
-constexpr int kOffW = 0, kOffU = 4096, kOffQ = 8192, kOffKt = 12288, kOffPm = 16384,
-              kOffGc = 17408, kCkBlk = 17412;
+// Per (chunk, value head) operand block (floats), laid out as the scan's
+// shared-memory images so that one bulk copy places each:
+//   B1 [4 slabs][64 rows][32]: rows 0..31 W_t, rows 32..63 Qg_t = e^G q_t,
+//      slab j = keys 32j..32j+31 (SWIZZLE_128B K-major, 8 KB per slab)
+//   Kt [128 rows (key)][32 (t)]: e^(G_last - G_t) k_t, SWIZZLE_128B
+//   P  [32 rows (t)][32 (s)]: e^(G_t - G_s) q_t.k_s (s <= t), SWIZZLE_128B
+//   U  [32][128] plain
+// and gC = e^G_last per (chunk, head) in a separate array.
+constexpr int kBlkB1 = 0, kBlkKt = 8192, kBlkP = 12288, kBlkU = 13312, kCkBlk = 17408;
 constexpr int kPrepSmem = (2 * kCk * 132 + kCk * 128 + kCk * 36 + 4 * kCk) * 4;
+
+// float index of (row, col) in a SWIZZLE_128B K-major tile of 32-float rows:
+// the 16-byte chunk col/4 of row `row` sits at chunk position (col/4) ^ (row % 8)
+__host__ __device__ __forceinline__ int sw128_f(int row, int col) {
+  return row * 32 + ((((col >> 2) ^ (row & 7))) << 2) + (col & 3);
+}
+__host__ __device__ __forceinline__ int blk_b1(int r, int k) {
+  return kBlkB1 + (k >> 5) * 2048 + sw128_f(r, k & 31);
+}
 
 __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __restrict__ qk,
                                                                const __half* __restrict__ v,
                                                                const float* __restrict__ lg,
                                                                const float* __restrict__ beta,
                                                                int T, int nk, int nv,
-                                                               float* __restrict__ blocks) {
+                                                               float* __restrict__ blocks,
+                                                               float* __restrict__ gcs) {
   extern __shared__ __align__(16) float sm[];
   float* sk = sm;                  // k rows [32][132]
   float* sq = sk + kCk * 132;      // q rows [32][132]
@@ -259,7 +274,7 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
       const bool lower = s2 <= r && r < n;
       const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
       sA[r * 36 + s2] = s2 < r && r < n ? sB[r] * dec * ck[e] : 0.f;
-      blk[kOffPm + r * kCk + s2] = dec * cq[e];
+      blk[kBlkP + sw128_f(r, s2)] = dec * cq[e];
     }
   }
   __syncthreads();
@@ -280,248 +295,394 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
       }
       x[r] = acc;
     }
-    float* dst = blk + (j < kDhd ? kOffW + j : kOffU + j - kDhd);
+    if (j < kDhd) {
 #pragma unroll
-    for (int r = 0; r < kCk; ++r) dst[r * kDhd] = x[r];
+      for (int r = 0; r < kCk; ++r) blk[blk_b1(r, j)] = x[r];
+    } else {
+#pragma unroll
+      for (int r = 0; r < kCk; ++r) blk[kBlkU + r * kDhd + j - kDhd] = x[r];
+    }
   }
   for (int i = tid; i < kCk * kDhd; i += blockDim.x) {
     const int r = i >> 7, d = i & 127;
-    blk[kOffQ + i] = sE[r] * sq[r * 132 + d];
+    blk[blk_b1(kCk + r, d)] = sE[r] * sq[r * 132 + d];
     const int dk = i >> 5, rk = i & 31;  // Kt[dk][rk]
-    blk[kOffKt + i] = sL[rk] * sk[rk * 132 + dk];
+    blk[kBlkKt + sw128_f(dk, rk)] = sL[rk] * sk[rk * 132 + dk];
   }
-  if (tid == 0) blk[kOffGc] = expf(sG[n - 1]);
+  if (tid == 0) gcs[(size_t)c * nv + h] = expf(sG[n - 1]);
   pdl_launch_dependents();
 }
 
-struct Tf32Frag4 {
-  uint32_t hi[4], lo[4];
-};
-struct Tf32Frag2 {
-  uint32_t hi[2], lo[2];
-};
-__device__ __forceinline__ Tf32Frag4 frag_a(const float* p, int ld, int g, int t) {
-  Tf32Frag4 f;
-  split_tf32(p[g * ld + t], f.hi[0], f.lo[0]);
-  split_tf32(p[(g + 8) * ld + t], f.hi[1], f.lo[1]);
-  split_tf32(p[g * ld + t + 4], f.hi[2], f.lo[2]);
-  split_tf32(p[(g + 8) * ld + t + 4], f.hi[3], f.lo[3]);
-  return f;
-}
-__device__ __forceinline__ Tf32Frag2 frag_b(const float* p, int ld, int g, int t) {
-  Tf32Frag2 f;
-  split_tf32(p[t * ld + g], f.hi[0], f.lo[0]);
-  split_tf32(p[(t + 4) * ld + g], f.hi[1], f.lo[1]);
-  return f;
-}
-// c += a b with fp32-level accuracy: a_lo b_hi + a_hi b_lo + a_hi b_hi
-__device__ __forceinline__ void mma3(float (&c)[4], const Tf32Frag4& a, const Tf32Frag2& b) {
-  mma_tf32(c, a.lo, b.hi);
-  mma_tf32(c, a.hi, b.lo);
-  mma_tf32(c, a.hi, b.hi);
-}
-
-// fragments from operands already split (hi bits and lo bits in two arrays of one layout)
-__device__ __forceinline__ Tf32Frag2 frag_b_pre(const float* hi, const float* lo, int ld, int g,
-                                                int t) {
-  Tf32Frag2 f;
-  f.hi[0] = __float_as_uint(hi[t * ld + g]);
-  f.hi[1] = __float_as_uint(hi[(t + 4) * ld + g]);
-  f.lo[0] = __float_as_uint(lo[t * ld + g]);
-  f.lo[1] = __float_as_uint(lo[(t + 4) * ld + g]);
-  return f;
-}
-__device__ __forceinline__ void put_split(float* hi, float* lo, int i, float x) {
-  uint32_t h, l;
-  split_tf32(x, h, l);
-  hi[i] = __uint_as_float(h);
-  lo[i] = __uint_as_float(l);
+// 4. the chunk scan on tcgen05 tensor cores: one CTA per value head.
+//
+// The state is kept transposed, S^T [128 value rows x 128 keys], as an fp32
+// TMEM accumulator (lanes = value rows), so every product has M = 128:
+//   (1) X = S^T [W | Qg]^T          M 128, N 64, K 128, A = S^T from TMEM
+//   (2) Delta^T = U^T - X[:, 0:32]  epilogue warps, into shared memory
+//   (4) S^T = gC S^T + Delta^T Kt^T M 128, N 128, K 32
+//   (3) X[:, 32:64] += Delta^T P^T  M 128, N 32,  K 32  -> O^T
+// Every product is 3xTF32: the tensor cores truncate fp32 operands to tf32, so
+// an fp32 value x is its own hi operand and lo = rna(x - trunc(x)) the second
+// (a_hi b_hi + a_hi b_lo + a_lo b_hi; the dropped a_lo b_lo is below 2^-20
+// relative). After each update the epilogue writes the A copies of the new
+// state (x and its lo part) and the gC-scaled accumulator, key quarter by key
+// quarter, and (1) of the next chunk starts on each quarter as it is released;
+// the splitters write the lo parts of the B operands one chunk ahead and copy
+// each chunk's output rows out of TMEM once its (3) has completed.
+//
+// Warps: 0 bulk-copy loader, 1 TMEM owner + MMA issuer, 2-5 splitters, 6-13
+// epilogue in two groups of four (warp w reads TMEM lanes 32 (w % 4) ..; group
+// g takes tokens 16 g .. 16 g + 15 of Delta and keys 32 q + 16 g .. + 15 of each
+// key quarter q). TMEM columns: 0 S^T accumulator, 128 the A copy of S^T, 256
+// its lo part, 384 and 448 X of even and odd chunks.
+constexpr int kScThreads = 448;
+constexpr int kScEpiWarps = 8;
+constexpr uint32_t kScB1Raw = 0, kScB1Lo = 65536, kScKtRaw = 131072, kScKtLo = 147456,
+                   kScPRaw = 163840, kScPLo = 167936, kScDHi = 172032, kScDLo = 188416,
+                   kScStg = 204800, kScBar = 225280;
+constexpr int kScanSmem = (int)kScBar + 256 + 1024;
+constexpr uint32_t kTmAcc = 0, kTmHi = 128, kTmLo = 256, kTmX = 384;  // X: 2 x 64 columns
+// instruction descriptors: D fp32, A and B tf32, both K-major, M 128
+__host__ __device__ constexpr uint32_t tf32_idesc(int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-constexpr int kScCols = 32;  // value columns per CTA
-// one chunk's operands in shared memory (floats), padded for conflict-free fragments
-constexpr int kStW = 0, kStQ = kCk * 132, kStU = 2 * kCk * 132, kStPm = kStU + kCk * 36,
-              kStKt = kStPm + kCk * 36, kStGc = kStKt + kDhd * 36, kStFloats = kStGc + 4;
-constexpr int kPartLd = 40;                             // partial-sum row stride
-constexpr int kPartFloats = 8 * 2 * 16 * kPartLd;       // [warp][product][16][40]
-constexpr int kScanSmem =
-    (2 * kStFloats + 2 * kDhd * 40 + 2 * kCk * 40 + kCk * 40 + kPartFloats) * 4;
+__device__ int g_delta_wait_timeouts;
 
-// Grid (128/32 column blocks, nv), 8 warps. Warp w keeps state rows
-// 16w..16w+15 (key) x the CTA's 32 value columns as mma accumulators. Per chunk:
-//  b. Delta = U - W S and Oa = Qg S: warp w multiplies rows 16(w&1).. over the
-//     key quarter 32(w>>1).. for all 32 columns (its W / Qg fragments split
-//     once), then the four key-quarter partials are summed in shared memory;
-//  c. O = Oa + P Delta on a 16 x 8 tile per warp;
-//  d. S = gC S + Kt^T Delta on the warp's own state rows.
-// S and Delta are stored split (tf32 hi / lo) by the threads that produce them.
-__global__ void __launch_bounds__(256, 1)
-    delta_chunk_scan_kernel(const float* __restrict__ blocks, float* __restrict__ state,
-                            float* __restrict__ o_out, int T, int nv) {
-  extern __shared__ __align__(16) float sm[];
-  float* sSh = sm + 2 * kStFloats;  // state hi [128][40] (B operand)
-  float* sSl = sSh + kDhd * 40;     // state lo
-  float* sDh = sSl + kDhd * 40;     // Delta hi [32][40] (B operand)
-  float* sDl = sDh + kCk * 40;      // Delta lo
-  float* sOa = sDl + kCk * 40;      // Oa [32][40]
-  float* sPart = sOa + kCk * 40;    // step-b partials
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int h = blockIdx.y, j0 = blockIdx.x * kScCols;
-  const int nchunks = (T + kCk - 1) / kCk;
-  auto stage = [&](int buf) { return sm + buf * kStFloats; };
-  auto load_stage = [&](int c, int buf) {
-    const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
-    const uint32_t st = smem_u32(stage(buf));
-    for (int i = threadIdx.x; i < kCk * 32; i += blockDim.x) {
-      const int r = i >> 5, p = i & 31;
-      cp_async_16(st + (kStW + r * 132 + 4 * p) * 4, blk + kOffW + r * kDhd + 4 * p, 16);
-      cp_async_16(st + (kStQ + r * 132 + 4 * p) * 4, blk + kOffQ + r * kDhd + 4 * p, 16);
-    }
-    for (int i = threadIdx.x; i < kCk * 8; i += blockDim.x) {
-      const int r = i >> 3, p = i & 7;
-      cp_async_16(st + (kStU + r * 36 + 4 * p) * 4, blk + kOffU + r * kDhd + j0 + 4 * p, 16);
-      cp_async_16(st + (kStPm + r * 36 + 4 * p) * 4, blk + kOffPm + r * kCk + 4 * p, 16);
-    }
-    for (int i = threadIdx.x; i < kDhd * 8; i += blockDim.x) {
-      const int d = i >> 3, p = i & 7;
-      cp_async_16(st + (kStKt + d * 36 + 4 * p) * 4, blk + kOffKt + d * kCk + 4 * p, 16);
-    }
-    if (threadIdx.x == 0) cp_async_16(st + kStGc * 4, blk + kOffGc, 16);
-  };
-  pdl_wait();
-  // state slice: rows 16w + g (+8), columns 8nt + 2t (+1)
-  float accS[4][4];
-  const size_t sbase = (size_t)h * kDhd * kDhd;
-  const int ra = 16 * warp + g, rb = ra + 8;
-  auto put_state = [&]() {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int cc = 8 * nt + 2 * t;
-      put_split(sSh, sSl, ra * 40 + cc, accS[nt][0]);
-      put_split(sSh, sSl, ra * 40 + cc + 1, accS[nt][1]);
-      put_split(sSh, sSl, rb * 40 + cc, accS[nt][2]);
-      put_split(sSh, sSl, rb * 40 + cc + 1, accS[nt][3]);
-    }
-  };
-#pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    const int cc = j0 + 8 * nt + 2 * t;
-    accS[nt][0] = state[sbase + (size_t)ra * kDhd + cc];
-    accS[nt][1] = state[sbase + (size_t)ra * kDhd + cc + 1];
-    accS[nt][2] = state[sbase + (size_t)rb * kDhd + cc];
-    accS[nt][3] = state[sbase + (size_t)rb * kDhd + cc + 1];
+// second tf32 operand of x: the part below tf32 precision, itself rounded to tf32
+__device__ __forceinline__ uint32_t tf32_lo(float x) {
+  const float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x - hi));
+  return r;
+}
+// D (TMEM) (+)= A (TMEM) * B (shared-memory descriptor)
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+// D (TMEM) (+)= A (shared-memory descriptor) * B (shared-memory descriptor)
+__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+// lo parts of `n4` float4s into a buffer of the same layout (128 threads)
+__device__ __forceinline__ void split_lo(const float* src, float* lo, int n4, int t) {
+  for (int i = t; i < n4; i += 128) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    reinterpret_cast<uint4*>(lo)[i] = make_uint4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
   }
-  put_state();
-  load_stage(0, 0);
-  cp_async_commit();
-  const int mt = warp & 1, kq = warp >> 1;  // step b: row tile, key quarter
-  const int mw = warp >> 2, nw = warp & 3;  // step c: O tile
-  for (int c = 0; c < nchunks; ++c) {
-    const int buf = c & 1;
-    if (c + 1 < nchunks) {
-      load_stage(c + 1, buf ^ 1);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+}
+// raw copy and lo parts
+__device__ __forceinline__ void split_copy(const float* src, float* raw, float* lo, int n4, int t) {
+  for (int i = t; i < n4; i += 128) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    reinterpret_cast<float4*>(raw)[i] = v;
+    reinterpret_cast<uint4*>(lo)[i] = make_uint4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+  }
+}
+
+__global__ void __launch_bounds__(kScThreads, 1)
+    delta_chunk_scan_kernel(const float* __restrict__ blocks, const float* __restrict__ gcs,
+                            float* __restrict__ state, float* __restrict__ o_out, int T, int nv) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_raw = smem_u32(smem_raw);
+  const uint32_t base = (base_raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - base_raw);
+  const uint32_t bar = base + kScBar;
+  const uint32_t b1_full = bar, b1_ready = bar + 16, b1_empty = bar + 32;  // [2] each
+  const uint32_t stg_full = bar + 48, stg_empty = bar + 56, kp_ready = bar + 64,
+                 kp_empty = bar + 72, x_done = bar + 88, d_ready = bar + 96, u_done = bar + 104,
+                 done = bar + 112;
+  const uint32_t a_ready = bar + 128;  // [4]: key quarters of the state copies
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kScBar + 192);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int nchunks = (T + kCk - 1) / kCk;
+  if (threadIdx.x == 0) {
+    // commits and the loader count 1; thread groups arrive once per warp
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(b1_full + 8 * b, 1);
+      mbar_init(b1_ready + 8 * b, 4);
+      mbar_init(b1_empty + 8 * b, 1);
     }
-    __syncthreads();
-    const float* st = stage(buf);
-    // b: partial W S and Qg S over this warp's key quarter
+    mbar_init(stg_full, 1);
+    mbar_init(stg_empty, 4);
+    mbar_init(kp_ready, 4);
+    mbar_init(kp_empty, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(a_ready + 8 * q, kScEpiWarps);
+    mbar_init(x_done, 1);
+    mbar_init(d_ready, kScEpiWarps);
+    mbar_init(u_done, 1);
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // operand blocks, gC values and the state come from earlier launches
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---- loader: B1 images (double-buffered) and the raw Kt / P staging ----
+    if (lane == 0) {
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+        const int b = c & 1;
+        ok = mbar_wait(b1_empty + 8 * b, ((c >> 1) & 1) ^ 1u);
+        if (!ok) break;
+        mbar_arrive_tx(b1_full + 8 * b, 32768u);
+        bulk_load(base + kScB1Raw + b * 32768u, blk + kBlkB1, 32768u, b1_full + 8 * b);
+        ok = mbar_wait(stg_empty, (c & 1) ^ 1u);
+        if (!ok) break;
+        mbar_arrive_tx(stg_full, 20480u);
+        bulk_load(base + kScStg, blk + kBlkKt, 20480u, stg_full);  // Kt then P (contiguous)
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t acc = tmem + kTmAcc, ahi = tmem + kTmHi, alo = tmem + kTmLo;
+      // descriptors differ only in the start-address field (16-byte units)
+      const uint64_t ddh = sw128_desc(base + kScDHi), ddl = sw128_desc(base + kScDLo);
+      const uint64_t dkh = sw128_desc(base + kScKtRaw), dkl = sw128_desc(base + kScKtLo);
+      const uint64_t dph = sw128_desc(base + kScPRaw), dpl = sw128_desc(base + kScPLo);
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int b = c & 1;
+        const uint32_t xd = tmem + kTmX + 64u * (uint32_t)b;
+        ok = mbar_wait(b1_ready + 8 * b, (c >> 1) & 1);
+        if (!ok) break;
+        // (1) X = S^T [W | Qg]^T, one key quarter (32 keys = one B1 slab) at a
+        // time as the epilogue releases the state copies
+        const uint64_t dbh = sw128_desc(base + kScB1Raw + b * 32768u);
+        const uint64_t dbl = sw128_desc(base + kScB1Lo + b * 32768u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          ok = mbar_wait(a_ready + 8 * q, c & 1);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int j = 4 * q + jj;
+            const uint64_t off = (uint64_t)(q * 8192 + jj * 32) >> 4;
+            umma_tf32_ts(xd, ahi + 8 * j, dbh + off, tf32_idesc(64), j > 0 ? 1u : 0u);
+            umma_tf32_ts(xd, ahi + 8 * j, dbl + off, tf32_idesc(64), 1u);
+            umma_tf32_ts(xd, alo + 8 * j, dbh + off, tf32_idesc(64), 1u);
+          }
+        }
+        if (!ok) break;
+        umma_commit(x_done);
+        umma_commit(b1_empty + 8 * b);
+        ok = mbar_wait(d_ready, c & 1) && mbar_wait(kp_ready, c & 1);
+        if (!ok) break;
+        tc_fence_after();
+        // (4) S^T = gC S^T + Delta^T Kt^T first (the next chunk waits on it),
+        // then (3) O^T = Oa^T + Delta^T P^T
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t o = (uint64_t)(32 * j) >> 4;
+          umma_tf32_ss(acc, ddh + o, dkh + o, tf32_idesc(128), 1u);
+          umma_tf32_ss(acc, ddh + o, dkl + o, tf32_idesc(128), 1u);
+          umma_tf32_ss(acc, ddl + o, dkh + o, tf32_idesc(128), 1u);
+        }
+        umma_commit(u_done);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t o = (uint64_t)(32 * j) >> 4;
+          umma_tf32_ss(xd + 32, ddh + o, dph + o, tf32_idesc(32), 1u);
+          umma_tf32_ss(xd + 32, ddh + o, dpl + o, tf32_idesc(32), 1u);
+          umma_tf32_ss(xd + 32, ddl + o, dph + o, tf32_idesc(32), 1u);
+        }
+        umma_commit(kp_empty);
+      }
+      // every MMA issued above has completed before the teardown
+      umma_commit(done);
+      if (!mbar_wait(done, 0)) ok = false;
+    }
+  } else if (warp < 6) {
+    // ---- splitters: lo parts of every B operand, one chunk ahead; then the
+    // previous chunk's output rows (warp w reads TMEM lanes 32 (w % 4)..,
+    // all 32 tokens) ----
+    const int t = threadIdx.x - 64;
+    const int v = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const float* stg = reinterpret_cast<const float*>(smem + kScStg);
+    auto store_o = [&](int cc) {
+      const int t0 = cc * kCk, n = min(kCk, T - t0);
+      uint32_t oa[32];
+      tmem_ld32(tmem + kTmX + 64u * (uint32_t)(cc & 1) + lane_off + 32, oa);
+      tmem_ld_wait();
+#pragma unroll
+      for (int tt = 0; tt < kCk; ++tt)
+        if (tt < n) o_out[((size_t)(t0 + tt) * nv + h) * kDhd + v] = __uint_as_float(oa[tt]);
+    };
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int b = c & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(b1_full + 8 * b, (c >> 1) & 1));
+      if (!ok) break;
+      split_lo(reinterpret_cast<const float*>(smem + kScB1Raw + b * 32768u),
+               reinterpret_cast<float*>(smem + kScB1Lo + b * 32768u), 2048, t);
+      fence_proxy_async_smem();  // generic writes before the MMAs read them
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b1_ready + 8 * b);
+      // Kt / P: the staged raw copy, once the previous chunk's products are done
+      ok = __all_sync(0xffffffffu, mbar_wait(stg_full, c & 1) && mbar_wait(kp_empty, (c & 1) ^ 1u));
+      if (!ok) break;
+      split_copy(stg, reinterpret_cast<float*>(smem + kScKtRaw),
+                 reinterpret_cast<float*>(smem + kScKtLo), 1024, t);
+      split_copy(stg + 4096, reinterpret_cast<float*>(smem + kScPRaw),
+                 reinterpret_cast<float*>(smem + kScPLo), 256, t);
+      fence_proxy_async_smem();  // the staging reads before the next bulk copy into it
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(stg_empty);
+        mbar_arrive(kp_ready);
+      }
+      // chunk c - 1's (3) has completed (kp_empty above): its O^T leaves TMEM;
+      // its X buffer is rewritten only by chunk c + 1's (1), which waits for
+      // this warp's next b1_ready
+      if (c > 0) store_o(c - 1);
+    }
+    if (ok && nchunks > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(kp_empty, (nchunks - 1) & 1));
+      if (ok) store_o(nchunks - 1);
+    }
+  } else {
+    // ---- epilogue: thread = value row v (TMEM lane) ----
+    const int sp = warp & 3;
+    const int eg = (warp - 6) >> 2;
+    const int v = sp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
+    const uint32_t kofs = 16u * (uint32_t)eg;
+    const int tofs = 16 * eg;
+    const uint32_t tacc = tmem + kTmAcc + lane_off + kofs, thi = tmem + kTmHi + lane_off + kofs,
+                   tlo = tmem + kTmLo + lane_off + kofs;
+    float* sdh = reinterpret_cast<float*>(smem + kScDHi);
+    float* sdl = reinterpret_cast<float*>(smem + kScDLo);
+    float* sth = state + (size_t)h * kDhd * kDhd;
+    // key quarter q of the state: A copy (x, its lo part) and g x as the
+    // accumulator, then the quarter is released to (1)
+    auto put_quarter = [&](int q, const uint32_t (&src)[16], float g) {
+      uint32_t vh[16], vl[16], vs[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = __uint_as_float(src[e]);
+        vh[e] = src[e];
+        vl[e] = tf32_lo(x);
+        vs[e] = __float_as_uint(g * x);
+      }
+      tmem_st16(thi + 32 * q, vh);
+      tmem_st16(tlo + 32 * q, vl);
+      tmem_st16(tacc + 32 * q, vs);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_ready + 8 * q);
+    };
     {
-      float pd[4][4] = {}, po[4][4] = {};
+      const float g0 = gcs[h];
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        uint32_t x0[16];
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int k0 = 32 * kq + 8 * ks;
-        const Tf32Frag4 aW = frag_a(st + kStW + 16 * mt * 132 + k0, 132, g, t);
-        const Tf32Frag4 aQ = frag_a(st + kStQ + 16 * mt * 132 + k0, 132, g, t);
+        for (int e = 0; e < 16; ++e) x0[e] = __float_as_uint(sth[(size_t)(kofs + 32 * q + e) * kDhd + v]);
+        put_quarter(q, x0, g0);
+      }
+    }
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+      const uint32_t tx = tmem + kTmX + 64u * (uint32_t)(c & 1) + lane_off;
+      float u[16];
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          const Tf32Frag2 bS = frag_b_pre(sSh + k0 * 40 + 8 * nt, sSl + k0 * 40 + 8 * nt, 40, g, t);
-          mma3(pd[nt], aW, bS);
-          mma3(po[nt], aQ, bS);
+      for (int tt = 0; tt < 16; ++tt) u[tt] = blk[kBlkU + (tofs + tt) * kDhd + v];
+      const float gnext = c + 1 < nchunks ? gcs[(size_t)(c + 1) * nv + h] : 0.f;
+      ok = __all_sync(0xffffffffu, mbar_wait(x_done, c & 1));
+      if (!ok) break;
+      tc_fence_after();
+      // (2) Delta^T row v, this group's 16 tokens = U^T - (W S)^T: the raw value
+      // and its lo part as the A operand of (3) and (4)
+      {
+        uint32_t xa[16];
+        tmem_ld16(tx + tofs, xa);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t hh[4], ll[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float d = u[4 * q + e] - __uint_as_float(xa[4 * q + e]);
+            hh[e] = __float_as_uint(d);
+            ll[e] = tf32_lo(d);
+          }
+          const int qq = (tofs >> 2) + q;  // 16-byte chunk of the 128-byte row
+          const int pos = v * 32 + ((qq ^ (v & 7)) << 2);
+          *reinterpret_cast<uint4*>(sdh + pos) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+          *reinterpret_cast<uint4*>(sdl + pos) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
         }
       }
-      float* pw = sPart + warp * 2 * 16 * kPartLd;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(d_ready);
+      ok = __all_sync(0xffffffffu, mbar_wait(u_done, c & 1));
+      if (!ok) break;
+      tc_fence_after();
+      // S_{c+1}: all four quarters' loads in flight at once, then each quarter
+      // is written and released before the next; the last chunk stores the
+      // final state
+      uint32_t va[16], vb[16], vc[16], vd[16];
+      tmem_ld16(tacc, va);
+      tmem_ld16(tacc + 32, vb);
+      tmem_ld16(tacc + 64, vc);
+      tmem_ld16(tacc + 96, vd);
+      tmem_ld_wait();
+      if (c + 1 == nchunks) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int cc = 8 * nt + 2 * t;
-        *reinterpret_cast<float2*>(pw + g * kPartLd + cc) = make_float2(pd[nt][0], pd[nt][1]);
-        *reinterpret_cast<float2*>(pw + (g + 8) * kPartLd + cc) = make_float2(pd[nt][2], pd[nt][3]);
-        *reinterpret_cast<float2*>(pw + 16 * kPartLd + g * kPartLd + cc) =
-            make_float2(po[nt][0], po[nt][1]);
-        *reinterpret_cast<float2*>(pw + 16 * kPartLd + (g + 8) * kPartLd + cc) =
-            make_float2(po[nt][2], po[nt][3]);
+        for (int e = 0; e < 16; ++e) {
+          sth[(size_t)(kofs + e) * kDhd + v] = __uint_as_float(va[e]);
+          sth[(size_t)(kofs + 32 + e) * kDhd + v] = __uint_as_float(vb[e]);
+          sth[(size_t)(kofs + 64 + e) * kDhd + v] = __uint_as_float(vc[e]);
+          sth[(size_t)(kofs + 96 + e) * kDhd + v] = __uint_as_float(vd[e]);
+        }
+      } else {
+        put_quarter(0, va, gnext);
+        put_quarter(1, vb, gnext);
+        put_quarter(2, vc, gnext);
+        put_quarter(3, vd, gnext);
       }
     }
-    __syncthreads();
-    // sum the key quarters: thread -> row r (0..31), columns 4c4..4c4+3
-    {
-      const int r = threadIdx.x >> 3, c4 = threadIdx.x & 7;
-      const int m = r >> 4, rr = r & 15;
-      float4 d = make_float4(0.f, 0.f, 0.f, 0.f), o = d;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float* pw = sPart + (2 * q + m) * 2 * 16 * kPartLd;
-        const float4 a = *reinterpret_cast<const float4*>(pw + rr * kPartLd + 4 * c4);
-        const float4 b = *reinterpret_cast<const float4*>(pw + 16 * kPartLd + rr * kPartLd + 4 * c4);
-        d.x += a.x; d.y += a.y; d.z += a.z; d.w += a.w;
-        o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
-      }
-      const float4 u = *reinterpret_cast<const float4*>(st + kStU + r * 36 + 4 * c4);
-      const float dv[4] = {u.x - d.x, u.y - d.y, u.z - d.z, u.w - d.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) put_split(sDh, sDl, r * 40 + 4 * c4 + e, dv[e]);
-      *reinterpret_cast<float4*>(sOa + r * 40 + 4 * c4) = o;
-    }
-    __syncthreads();
-    // c: O = Oa + P Delta
-    const int r0 = 16 * mw + g, r1 = r0 + 8, cc = 8 * nw + 2 * t;
-    float o[4] = {sOa[r0 * 40 + cc], sOa[r0 * 40 + cc + 1], sOa[r1 * 40 + cc],
-                  sOa[r1 * 40 + cc + 1]};
-#pragma unroll
-    for (int ks = 0; ks < kCk / 8; ++ks) {
-      const Tf32Frag4 aP = frag_a(st + kStPm + 16 * mw * 36 + 8 * ks, 36, g, t);
-      const Tf32Frag2 bD = frag_b_pre(sDh + 8 * ks * 40 + 8 * nw, sDl + 8 * ks * 40 + 8 * nw, 40, g, t);
-      mma3(o, aP, bD);
-    }
-    const int t0 = c * kCk, n = min(kCk, T - t0);
-    if (r0 < n)
-      *reinterpret_cast<float2*>(o_out + ((size_t)(t0 + r0) * nv + h) * kDhd + j0 + cc) =
-          make_float2(o[0], o[1]);
-    if (r1 < n)
-      *reinterpret_cast<float2*>(o_out + ((size_t)(t0 + r1) * nv + h) * kDhd + j0 + cc) =
-          make_float2(o[2], o[3]);
-    // d: S = gC S + Kt^T Delta on this warp's key rows
-    const float gc = st[kStGc];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) accS[nt][e] *= gc;
-#pragma unroll
-    for (int ks = 0; ks < kCk / 8; ++ks) {
-      const Tf32Frag4 aK = frag_a(st + kStKt + 16 * warp * 36 + 8 * ks, 36, g, t);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const Tf32Frag2 bD =
-            frag_b_pre(sDh + 8 * ks * 40 + 8 * nt, sDl + 8 * ks * 40 + 8 * nt, 40, g, t);
-        mma3(accS[nt], aK, bD);
-      }
-    }
-    __syncthreads();  // every warp is done reading S (step b) and Delta before they change
-    put_state();
-    // the next iteration's first barrier publishes S; this stage is refilled after it
   }
-#pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    const int cc2 = j0 + 8 * nt + 2 * t;
-    state[sbase + (size_t)ra * kDhd + cc2] = accS[nt][0];
-    state[sbase + (size_t)ra * kDhd + cc2 + 1] = accS[nt][1];
-    state[sbase + (size_t)rb * kDhd + cc2] = accS[nt][2];
-    state[sbase + (size_t)rb * kDhd + cc2 + 1] = accS[nt][3];
-  }
+  if (!ok && lane == 0) atomicAdd(&g_delta_wait_timeouts, 1);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   pdl_launch_dependents();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+int delta_wait_timeouts(int* count, int reset) {
+  if (cudaMemcpyFromSymbol(count, g_delta_wait_timeouts, sizeof(int)) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_delta_wait_timeouts, &zero, sizeof(int)) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+  }
+  return IQ36_OK;
 }
 
 // 4. gated RMSNorm: one warp per (token, value head), lane = 4 columns.
@@ -556,7 +717,7 @@ __global__ void __launch_bounds__(256) delta_gated_norm_kernel(const float* o, c
 // workspace: qk fp32 [T, 2nk, D] | v fp16 [T, nv*D] | g, beta fp32 [T, nv] | o fp32 [T, nv, D]
 // | chunk operand blocks [ceil(T/32), nv, kCkBlk] fp32
 struct DeltaWs {
-  size_t qk, v, decay, beta, o, blocks, total;
+  size_t qk, v, decay, beta, o, blocks, gcs, total;
 };
 static DeltaWs delta_ws(int T, int nk, int nv) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
@@ -567,7 +728,8 @@ static DeltaWs delta_ws(int T, int nk, int nv) {
   w.beta = up(w.decay + (size_t)T * nv * 4);
   w.o = up(w.beta + (size_t)T * nv * 4);
   w.blocks = up(w.o + (size_t)T * nv * kDhd * 4);
-  w.total = up(w.blocks + (size_t)((T + kCk - 1) / kCk) * nv * kCkBlk * 4);
+  w.gcs = up(w.blocks + (size_t)((T + kCk - 1) / kCk) * nv * kCkBlk * 4);
+  w.total = up(w.gcs + (size_t)((T + kCk - 1) / kCk) * nv * 4);
   return w;
 }
 
@@ -620,6 +782,7 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   float* bet = reinterpret_cast<float*>(ws + w.beta);
   float* o = reinterpret_cast<float*>(ws + w.o);
   float* blocks = reinterpret_cast<float*>(ws + w.blocks);
+  float* gcs = reinterpret_cast<float*>(ws + w.gcs);
   const cudaStream_t s = as_stream(stream);
   const int nseg = 2 * nk + nv, C = nseg * kDhd;
   cudaError_t e = launch(delta_conv_batch_kernel, dim3(ceil_div(T, kConvTok), ceil_div(nseg, 8)),
@@ -634,10 +797,10 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   if (e == cudaSuccess)
     e = launch(delta_chunk_prep_kernel, dim3(ceil_div(T, kCk), nv), dim3(256), (size_t)kPrepSmem,
                s, (const float*)qk, (const __half*)v, (const float*)dec, (const float*)bet, T, nk,
-               nv, blocks);
+               nv, blocks, gcs);
   if (e == cudaSuccess)
-    e = launch(delta_chunk_scan_kernel, dim3(kDhd / kScCols, nv), dim3(256), (size_t)kScanSmem,
-               s, (const float*)blocks, state, o, T, nv);
+    e = launch(delta_chunk_scan_kernel, dim3(nv), dim3(kScThreads), (size_t)kScanSmem, s,
+               (const float*)blocks, (const float*)gcs, state, o, T, nv);
   if (e == cudaSuccess)
     e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 8)), dim3(256), 0, s,
                (const float*)o, reinterpret_cast<const __half*>(z_f16), norm_w, eps, T * nv,

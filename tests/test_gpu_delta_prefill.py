@@ -77,12 +77,19 @@ def test_delta_prefill_matches_sequential_oracle(cuda, T, nk, nv):
     assert_close(gstate, rstate, "recurrent state", max_rel=1e-3)
 
 
-def test_delta_prefill_equals_token_serial_decode_path(cuda):
+@pytest.mark.parametrize("T", [45, 1000])
+def test_delta_prefill_equals_token_serial_decode_path(cuda, T):
     """Prefill over T tokens == the decode kernels run T times (same fp32
-    arithmetic, only the order of the sums over key rows differs)."""
+    arithmetic, only the order of the sums over key rows differs). T = 1000:
+    32 chunks with a ragged last one, the state carried through every chunk
+    of the tensor-core scan; no bounded device wait expires."""
     import torch
+    from engine import _native as N
     from engine.ops import delta_prep, delta_step
-    T, nk, nv = 45, 16, 32
+    import ctypes
+    nk, nv = 16, 32
+    before = ctypes.c_int32()
+    N.call("iq36_wait_timeouts", ctypes.byref(before), 0)
     cs = _case(np.random.default_rng(11), T, nk, nv)
     got, gconv, gstate = _gpu(cs, T, nk, nv, cuda)
     c = cs["qkv"].shape[1]
@@ -101,6 +108,9 @@ def test_delta_prefill_equals_token_serial_decode_path(cuda):
     np.testing.assert_array_equal(gconv, conv.cpu().numpy())
     assert_close(got, outs.float().cpu().numpy(), "prefill vs decode path", max_rel=2e-3)
     assert_close(gstate, state.cpu().numpy(), "state prefill vs decode path", max_rel=1e-4)
+    after = ctypes.c_int32()
+    N.call("iq36_wait_timeouts", ctypes.byref(after), 0)
+    assert after.value == before.value
 
 
 def test_delta_prefill_rejects_bad_shapes(cuda):
