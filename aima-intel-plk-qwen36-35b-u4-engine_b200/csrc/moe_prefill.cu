@@ -325,9 +325,9 @@ struct GemmArgs {
   const uint8_t* pz[4];
   void* pout[4];
   int prow[4], pdt[4], pacc[4];
-  // MODE 2/3 only: group 64 (one quant group per 64-wide k-block). The scales
-  // and zero points are then read by the dequant threads from global memory
-  // one k-block ahead (a unit's 64 groups per row would not fit the staging
+  // Group 64 (one quant group per 64-wide k-block): the scales and zero
+  // points are then read by the dequant threads from global memory one
+  // k-block ahead (a unit's 64 groups per row would not fit the staging
   // buffers); group 128 stages them per unit in shared memory.
   int g64;
 };
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int nN = (MODE == 0 || MODE == 3) ? g.I / 128 : g.H / kPfBN;
   const int total = pf_units<MODE>(g);
   const int nkb = g.K / kPfBK;
-  const bool g64 = (MODE == 2 || MODE == 3) && g.g64;
+  const bool g64 = g.g64 != 0;
   const int ng = g64 ? g.K / 64 : g.K / 128;
   bool ok = true;
 
@@ -1046,7 +1046,8 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
       !b->down_scale || !b->down_zp)
     return IQ36_ERR_ARG;
   const int E = b->num_experts, H = b->hidden, I = b->intermediate;
-  if (b->group != 128 || T < 1 || k < 1 || k > 16 || E < 1 || E > 256) return IQ36_ERR_SHAPE;
+  if ((b->group != 128 && b->group != 64) || T < 1 || k < 1 || k > 16 || E < 1 || E > 256)
+    return IQ36_ERR_SHAPE;
   if (H % 256 || I % 128 || H < 256 || I < 128 || H > 2048 || I > 2048 ||
       (int64_t)T * k > (1 << 28))
     return IQ36_ERR_SHAPE;
@@ -1108,6 +1109,7 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
                x_dtype == IQ36_F16 ? 1 : 0, P, H, w);
   GemmArgs g1{reinterpret_cast<const __half*>(b->gate_up_scale), b->gate_up_zp, (int64_t)2 * I,
               H, I, H, w};
+  g1.g64 = b->group == 64;
   // persistent grids: at most one CTA per SM, never more than the units
   int sms = 148;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -1118,6 +1120,7 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
     e = launch(pf_gemm_kernel<0>, dim3(grid1), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_x, map_gu, map_gu, map_gu, map_gu, g1);
   GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
+  g2.g64 = b->group == 64;
   if (e == cudaSuccess)
     e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_act, map_d, map_d, map_d, map_d, g2);

@@ -241,7 +241,7 @@ int iq36_moe_layer_decode_partial(const float* residual, int32_t hidden, const f
  * contribution scatter :831-845, and the stock gather/GEMM/scatter of
  * iq36-pr35924-grouped-postops.patch:15-124. x bf16 [T, H]; out fp32, bf16 or
  * fp16 (with k = 1 the fp16 output is the contribution itself, exactly).
- * Requirements: H % 256 == 0, I % 128 == 0, H, I <= 2048, G == 128. */
+ * Requirements: H % 256 == 0, I % 128 == 0, H, I <= 2048, G == 128 or 64. */
 int iq36_moe_prefill(const void* x_bf16, int32_t T, const int32_t* ids, const float* weights,
                      int32_t k, const iq36_expert_bank* routed, void* out, int32_t out_dtype,
                      void* workspace, size_t workspace_bytes, iq36_stream_t stream);

@@ -3,7 +3,8 @@
 bf16 activations ~N(0,1), router logits N(0,1) plus a
 Zipf(1.1)-ranked per-expert bias scaled to +-2 (skewed expert load: some
 experts get several 128-row tiles, some none), top-8, u4 g128 experts,
-SwiGLU, weighted scatter-add. Each token's output depends only on its own
+SwiGLU, weighted scatter-add (u4 group 64 as well: the checkpoint's fixed-FC
+group size). Each token's output depends only on its own
 routing, so at T = 4096 parity is checked on a random sample of tokens; the
 small case checks every token. Tolerance: tests/helpers.py (max rel 2e-3).
 """
@@ -22,29 +23,30 @@ def _t(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-def _run(cuda, T, E, seed, sample=None, out_dtype="f32"):
+def _run(cuda, T, E, seed, sample=None, out_dtype="f32", group=128):
     import torch
     from engine.ops import moe_expert_ffn_prefill, router_select
     rng = np.random.default_rng(seed)
     h, i = 2048, 512
-    bank = make_bank(rng, E, h, i)
+    bank = make_bank(rng, E, h, i, group)
     logits = zipf_router_logits(rng, T, E)
     x = rng.standard_normal((T, h)).astype(np.float32)
     xb = oracle.bf16_bits(x)
     ids, wts = router_select(_t(logits, cuda), 8)
     dt = torch.float32 if out_dtype == "f32" else torch.bfloat16
     xt = torch.from_numpy(xb.view(np.int16)).to(cuda).view(torch.bfloat16)
-    out = moe_expert_ffn_prefill(xt, ids, wts, bank_to_torch(bank, cuda), out_dtype=dt)
+    out = moe_expert_ffn_prefill(xt, ids, wts, bank_to_torch(bank, cuda, group), out_dtype=dt)
     torch.cuda.synchronize(cuda)
     tokens = np.arange(T) if sample is None else np.sort(rng.choice(T, sample, replace=False))
     ref = oracle.moe_prefill(xb.reshape(T, h), tokens, ids.cpu().numpy(), wts.cpu().numpy(),
-                             bank, 128)
+                             bank, group)
     got = out.float().cpu().numpy()[tokens]
     return got, ref, ids.cpu().numpy(), out
 
 
-def test_prefill_small_all_tokens(cuda):
-    got, ref, ids, _ = _run(cuda, T=300, E=16, seed=1)
+@pytest.mark.parametrize("group", [128, 64])
+def test_prefill_small_all_tokens(cuda, group):
+    got, ref, ids, _ = _run(cuda, T=300, E=16, seed=1, group=group)
     # an expert takes each token at most once, so T = 300 lets the most loaded
     # expert span several 128-row tiles (ragged last tile included)
     counts = np.bincount(ids.ravel(), minlength=16)
@@ -53,9 +55,11 @@ def test_prefill_small_all_tokens(cuda):
         assert_close(got[t], ref[t], f"prefill token {t}")
 
 
-@pytest.mark.parametrize("T", [4096, 16384])
-def test_prefill_config3_sampled(cuda, T):
-    got, ref, ids, _ = _run(cuda, T=T, E=256, seed=T, sample=24)
+@pytest.mark.parametrize("T,group", [(4096, 128), (16384, 128), (4096, 64)])
+def test_prefill_config3_sampled(cuda, T, group):
+    """group 64: the expert GEMMs read per-row scales and zero points from
+    global memory one 64-wide k-block ahead instead of the staged unit buffer."""
+    got, ref, ids, _ = _run(cuda, T=T, E=256, seed=T, sample=24, group=group)
     counts = np.bincount(ids.ravel(), minlength=256)
     assert counts.max() > 128  # skewed load -> multi-tile experts
     for j in range(got.shape[0]):
