@@ -20,26 +20,28 @@
 // GEMM kernel: persistent, one CTA per SM (grid min(148, units)); a unit is
 // one 128x256 output tile (M tile of one expert x N tile), taken round-robin.
 // Warp roles (23 warps):
-//   warp 0      TMA producer of the activation tile (SWIZZLE_128B, 64 fp16 of
-//               K per row per stage, no multicast) into its own 3-deep ring,
-//               so activation fetches run ahead of the dequantised B tiles;
+//   warp 0      TMA producer of the activation tile (SWIZZLE_128B, two
+//               64-wide k-blocks per stage, no multicast) into a 2-deep ring;
 //   warp 1      TMEM allocator (2 x 256 columns) and the single-thread
 //               tcgen05.mma issuer (kind::f16, M=128 N=256 K=16, fp32
-//               accumulate); units alternate accumulators;
-//   warp 2      B-side producer: per unit the scales and zero points of its
-//               256 weight rows (contiguous runs, cp.async.bulk, double
-//               buffer), then the raw u4 codes (TMA, 64 bytes x 256 rows per
-//               two k-blocks) into a 3-deep ring;
-//   warps 3-18  dequant, half a B-tile row per thread: (q - zp) * scale with
-//               one fp16 rounding, written in the canonical SW128 K-major
-//               layout;
+//               accumulate, eight MMAs per stage); units alternate
+//               accumulators;
+//   warp 2      B-side producer: the raw u4 codes (TMA, 64 bytes x 256 rows
+//               per stage) into a 2-deep ring;
+//   warps 3-18  dequant, one k-block of a B-tile row per thread and stage:
+//               (q - zp) * scale with one fp16 rounding, written in the
+//               canonical SW128 K-major layout; each row's scales and zero
+//               points are read from global memory one stage ahead;
 //   warps 19-22 epilogue of the previous unit (tcgen05.ld -> registers ->
 //               global) while the next unit's mainloop runs.
-// A ring 3 x 16 KB, B ring 3 x 32 KB (a third B stage measured +3-6% over two), code ring
-// 2 x 16 KB (two k-blocks per stage); all rings are synchronised with
-// mbarriers; every wait is time-bounded and writes an error word on expiry.
-// Buffers that threads read with generic loads and the TMA / bulk-copy engine
-// refills (codes, scales) are released only after fence.proxy.async.
+// A ring 2 x 32 KB, B ring 2 x 64 KB, code ring 2 x 16 KB, each stage two
+// k-blocks: per-k-block stages spent as many dequant cycles on waits, proxy
+// fences and barrier arrivals as on the arithmetic, and the MMA thread's
+// per-stage waits left the tensor pipe idle between its 4-MMA bursts. All
+// rings are synchronised with mbarriers; every wait is time-bounded and
+// writes an error word on expiry.
+// Buffers that threads read with generic loads and the TMA engine refills
+// (codes) are released only after fence.proxy.async.
 // GEMM2 stores fp16 contributions (the reference's f16-contribution scatter).
 
 // Operand order: inside each 8-element K chunk both operands hold the
@@ -60,34 +62,35 @@
 namespace iq36 {
 
 constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64;
-constexpr int kPfAStages = 3, kPfBStages = 3, kPfCodeStages = 2;
-// A code stage holds kPfCodeKB k-blocks of u4 codes for the 256 B-tile rows:
-// TMA rows of 64 bytes (two k-blocks) halve the row requests of 32-byte rows,
-// and the TMA engine's row-request rate, not bytes, bounded the GEMMs.
-constexpr int kPfCodeKB = 2;
-constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;  // 64 bytes per row
-constexpr int kPfAStage = kPfBM * kPfBK * 2;  // 16 KB
-constexpr int kPfBStage = kPfBN * kPfBK * 2;  // 32 KB
-constexpr int kPfCodeStage = kPfBN * kPfCodeRow;  // 16 KB of u4 codes
-constexpr int kPfMaxGroups = 32;                   // K <= 4096 with G = 128
-constexpr int kPfScaleBuf = kPfBN * kPfMaxGroups * 2;  // one unit's scales, 16 KB
-constexpr int kPfZpBuf = kPfBN * kPfMaxGroups / 2;     // one unit's zero points, 4 KB
-constexpr int kPfOffB = kPfAStages * kPfAStage;  // B ring after the A ring
+// Every ring stage holds two 64-wide k-blocks: a stage costs each dequant
+// thread one wait per ring, one proxy fence and one arrival, and the MMA
+// thread one wait pair for eight MMAs. Per-k-block stages spent about as many
+// cycles on those as on the dequant arithmetic.
+constexpr int kPfStageKB = 2;
+constexpr int kPfAStages = 2, kPfBStages = 2, kPfCodeStages = 2;
+constexpr int kPfCodeKB = kPfStageKB;
+constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;  // 64 bytes of codes per row
+constexpr int kPfASub = kPfBM * kPfBK * 2;         // one k-block of activations, 16 KB
+constexpr int kPfBSub = kPfBN * kPfBK * 2;         // one dequantised k-block, 32 KB
+constexpr int kPfAStage = kPfStageKB * kPfASub;    // 32 KB
+constexpr int kPfBStage = kPfStageKB * kPfBSub;    // 64 KB
+constexpr int kPfCodeStage = kPfBN * kPfCodeRow;   // 16 KB of u4 codes
+constexpr int kPfOffB = kPfAStages * kPfAStage;    // B ring after the A ring
 constexpr int kPfOffCodes = kPfOffB + kPfBStages * kPfBStage;
-constexpr int kPfOffScale = kPfOffCodes + kPfCodeStages * kPfCodeStage;
-constexpr int kPfOffZp = kPfOffScale + 2 * kPfScaleBuf;
-constexpr int kPfOffBar = kPfOffZp + 2 * kPfZpBuf;
+constexpr int kPfOffBar = kPfOffCodes + kPfCodeStages * kPfCodeStage;
 constexpr int kPfSmem = kPfOffBar + 256 + 1024;
+static_assert(kPfCodeStages == kPfBStages && kPfCodeKB == kPfStageKB,
+              "the dequant threads advance the code and B rings together");
 constexpr int kPfDqWarps = 16, kPfEpiWarps = 4;
 constexpr int kPfWarpDq0 = 3, kPfWarpEpi0 = kPfWarpDq0 + kPfDqWarps;
 constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 736
-constexpr int kPfDqThreads = kPfDqWarps * 32;                 // half a B-tile row each
+constexpr int kPfDqThreads = kPfDqWarps * 32;                 // one k-block of a B row each
 constexpr int kPfChunk = 512;  // assignments per schedule CTA (64 CTAs at 4096 tokens x top-8)
 static_assert(kPfChunk % 256 == 0, "placement ranks 256 assignments per round");
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 
-// ---------------------------------------32, A and B fp16, both K-major,
-// N = 256, M = 128.
+// Instruction descriptor of tcgen05.mma kind::f16: D fp32, A and B fp16, both
+// K-major, N = 256, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPfBN >> 3) << 17) | ((uint32_t)(kPfBM >> 4) << 24);
 
 // ---------------------------------------------------------------------------
@@ -326,10 +329,9 @@ struct GemmArgs {
   const uint8_t* pz[4];
   void* pout[4];
   int prow[4], pdt[4], pacc[4];
-  // Group 64 (one quant group per 64-wide k-block): the scales and zero
-  // points are then read by the dequant threads from global memory one
-  // k-block ahead (a unit's 64 groups per row would not fit the staging
-  // buffers); group 128 stages them per unit in shared memory.
+  // Group 64 (one quant group per 64-wide k-block) or 128 (one per ring
+  // stage); the dequant threads read a row's scales and zero points from
+  // global memory one stage ahead either way.
   int g64;
 };
 
@@ -413,9 +415,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t bar_empty = bar_full + 8 * kPfBStages;        // [kPfBStages]
   const uint32_t bar_cfull = bar_empty + 8 * kPfBStages;       // [kPfCodeStages]
   const uint32_t bar_cempty = bar_cfull + 8 * kPfCodeStages;   // [kPfCodeStages]
-  const uint32_t bar_sfull = bar_cempty + 8 * kPfCodeStages;   // [2]
-  const uint32_t bar_sempty = bar_sfull + 16;                  // [2]
-  const uint32_t bar_accf = bar_sempty + 16;                   // [2]
+  const uint32_t bar_accf = bar_cempty + 8 * kPfCodeStages;    // [2]
   const uint32_t bar_acce = bar_accf + 16;                     // [2]
   const uint32_t bar_done = bar_acce + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_done + 8 - base));
@@ -434,8 +434,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(bar_cempty + 8 * s, kPfDqThreads);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar_sfull + 8 * b, 1);                // scale / zp producer (with tx)
-      mbar_init(bar_sempty + 8 * b, kPfDqThreads);
       mbar_init(bar_accf + 8 * b, 1);                 // tcgen05.commit
       mbar_init(bar_acce + 8 * b, kPfEpiWarps * 32);  // epilogue threads
     }
@@ -453,24 +451,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   pdl_wait();  // the tile table and both operands come from earlier launches
   const int nN = (MODE == 0 || MODE == 3) ? g.I / 128 : g.H / kPfBN;
   const int total = pf_units<MODE>(g);
-  const int nkb = g.K / kPfBK;
+  const int nst = g.K / (kPfBK * kPfStageKB);  // ring stages per unit (K % 128 == 0)
   const bool g64 = g.g64 != 0;
   const int ng = g64 ? g.K / 64 : g.K / 128;
   bool ok = true;
 
   if (warp == 0) {
-    // ---- activation producer (TMA, SWIZZLE_128B) ----
+    // ---- activation producer (TMA, SWIZZLE_128B, two k-blocks a stage) ----
     if (lane == 0) {
-      int it = 0;
+      int s = 0;
+      uint32_t ph = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         int row0, rows_unused;
         pf_rows<MODE>(g, u / nN, row0, rows_unused);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kPfAStages;
-          ok = mbar_wait(bar_aempty + 8 * s, ((it / kPfAStages) & 1) ^ 1u);
+        for (int j = 0; j < nst; ++j) {
+          ok = mbar_wait(bar_aempty + 8 * s, ph ^ 1u);
           if (!ok) break;
+          const uint32_t dst = base + s * kPfAStage;
           mbar_arrive_tx(bar_afull + 8 * s, kPfAStage);
-          tma_load_2d(base + s * kPfAStage, &tmA, kb * kPfBK, row0, bar_afull + 8 * s);
+#pragma unroll
+          for (int sb = 0; sb < kPfStageKB; ++sb)
+            tma_load_2d(dst + sb * kPfASub, &tmA, (j * kPfStageKB + sb) * kPfBK, row0,
+                        bar_afull + 8 * s);
+          if (++s == kPfAStages) s = 0, ph ^= 1u;
         }
       }
     }
@@ -478,27 +481,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ---- MMA issuer: one thread, accumulators alternate between two
     // 256-column TMEM buffers so the epilogue of a unit overlaps the next ----
     if (lane == 0) {
-      int it = 0, i = 0;
+      int sa = 0, sb_ = 0, i = 0;
+      uint32_t pha = 0, phb = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
         const int a = i & 1;
         ok = mbar_wait(bar_acce + 8 * a, ((i >> 1) & 1) ^ 1u);
         if (!ok) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(a * kPfBN);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int sa = it % kPfAStages, s = it % kPfBStages;
-          ok = mbar_wait(bar_afull + 8 * sa, (it / kPfAStages) & 1) &&
-               mbar_wait(bar_full + 8 * s, (it / kPfBStages) & 1);
+        for (int j = 0; j < nst; ++j) {
+          ok = mbar_wait(bar_afull + 8 * sa, pha) && mbar_wait(bar_full + 8 * sb_, phb);
           if (!ok) break;
           tc_fence_after();
           const uint32_t a_s = base + sa * kPfAStage;
-          const uint32_t b_s = base + kPfOffB + s * kPfBStage;
+          const uint32_t b_s = base + kPfOffB + sb_ * kPfBStage;
 #pragma unroll
-          for (int kk = 0; kk < kPfBK / 16; ++kk)
-            umma_f16(acc, sw128_desc(a_s + kk * 32), sw128_desc(b_s + kk * 32), kIdesc,
-                     (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int sub = 0; sub < kPfStageKB; ++sub)
+#pragma unroll
+            for (int kk = 0; kk < kPfBK / 16; ++kk)
+              umma_f16(acc, sw128_desc(a_s + sub * kPfASub + kk * 32),
+                       sw128_desc(b_s + sub * kPfBSub + kk * 32), kIdesc,
+                       (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
           umma_commit(bar_aempty + 8 * sa);  // stages free once these MMAs complete
-          umma_commit(bar_empty + 8 * s);
+          umma_commit(bar_empty + 8 * sb_);
+          if (++sa == kPfAStages) sa = 0, pha ^= 1u;
+          if (++sb_ == kPfBStages) sb_ = 0, phb ^= 1u;
         }
         if (ok) umma_commit(bar_accf + 8 * a);  // accumulator complete
       }
@@ -507,130 +514,109 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (!mbar_wait(bar_done, 0)) ok = false;
     }
   } else if (warp == 2) {
-    // ---- B-side producer: each unit's scales and zero points (bulk copies,
-    // double-buffered), then its raw u4 codes (TMA, 4 k-blocks deep) ----
+    // ---- B-side producer: the unit's raw u4 codes by TMA, a stage of two
+    // k-blocks per 64-byte row ----
     if (lane == 0) {
-      const uint32_t sbytes = 128u * ng * 2u, zbytes = 128u * ng / 2u;
-      int it = 0, i = 0;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
+      int cs = 0;
+      uint32_t ph = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const PfUnit un = pf_unit<MODE>(g, u, nN);
         const CUtensorMap* wmap = un.proj == 0 ? &tmW : un.proj == 1 ? &tmW1 : un.proj == 2 ? &tmW2 : &tmW3;
-        if (!g64) {
-          const int b = i & 1;
-          ok = mbar_wait(bar_sempty + 8 * b, ((i >> 1) & 1) ^ 1u);
-          if (!ok) break;
-          const uint32_t sdst = base + kPfOffScale + b * kPfScaleBuf;
-          const uint32_t zdst = base + kPfOffZp + b * kPfZpBuf;
-          mbar_arrive_tx(bar_sfull + 8 * b, 2u * (sbytes + zbytes));
-          const __half* sp = MODE == 2 ? g.ps[un.proj] : g.s;
-          const uint8_t* zp = MODE == 2 ? g.pz[un.proj] : g.z;
-          bulk_load(sdst, sp + un.wr0 * ng, sbytes, bar_sfull + 8 * b);
-          bulk_load(sdst + sbytes, sp + un.wr1 * ng, sbytes, bar_sfull + 8 * b);
-          bulk_load(zdst, zp + un.wr0 * ng / 2, zbytes, bar_sfull + 8 * b);
-          bulk_load(zdst + zbytes, zp + un.wr1 * ng / 2, zbytes, bar_sfull + 8 * b);
-        }
-        // nkb is a multiple of kPfCodeKB, so code blocks never straddle units
-        for (int cb = 0; cb < nkb / kPfCodeKB; ++cb, ++it) {
-          const int cs = it % kPfCodeStages;
-          ok = mbar_wait(bar_cempty + 8 * cs, ((it / kPfCodeStages) & 1) ^ 1u);
+        for (int j = 0; j < nst; ++j) {
+          ok = mbar_wait(bar_cempty + 8 * cs, ph ^ 1u);
           if (!ok) break;
           const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
           mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
-          tma_load_2d(dst, wmap, cb * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
-          tma_load_2d(dst + kPfCodeStage / 2, wmap, cb * kPfCodeRow, (int)un.wr1,
+          tma_load_2d(dst, wmap, j * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
+          tma_load_2d(dst + kPfCodeStage / 2, wmap, j * kPfCodeRow, (int)un.wr1,
                       bar_cfull + 8 * cs);
+          if (++cs == kPfCodeStages) cs = 0, ph ^= 1u;
         }
       }
     }
   } else if (warp < kPfWarpEpi0) {
-    // ---- dequant: thread pair (2n, 2n+1) owns row n of the 256-row B tile,
-    // k 0..31 and 32..63 of each k-block ----
+    // ---- dequant: thread pair (2n, 2n+1) owns row n of the 256-row B tile;
+    // thread hk dequantises k-block hk of each stage into the canonical SW128
+    // K-major image. Scales and zero points come from global memory, one
+    // stage ahead (a row's 2 bytes of scale per group hit L1 after the first
+    // stage). The two 16-byte code loads go in an order that alternates every
+    // two rows, which spreads a warp's loads over all 32 banks. ----
     const int dt = threadIdx.x - kPfWarpDq0 * 32;
     const int n = dt >> 1, hk = dt & 1;
+    const int x8 = n & 7, lsw = (n >> 1) & 1;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
-    int it = 0, i = 0;
-    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
-      const int b = i & 1;
-      const __half* ssc;
-      const uint8_t* szp;
-      __half gsc = __ushort_as_half((unsigned short)0);
-      uint32_t gzb = 0;
-      if (!g64) {
-        ok = mbar_wait(bar_sfull + 8 * b, (i >> 1) & 1);
+    const uint8_t* const csrc = smem + kPfOffCodes + n * kPfCodeRow + hk * (kPfBK / 2);
+    uint8_t* const bdst = smem + kPfOffB + hk * kPfBSub + n * 128;
+    const int gstep = g64 ? 2 : 1;  // this thread's group advances per stage by
+    int s = 0;                      // code and B rings advance together
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      const PfUnit un = pf_unit<MODE>(g, u, nN);
+      const int64_t row = n < 128 ? un.wr0 + n : un.wr1 + (n - 128);
+      const __half* ssc = (MODE == 2 ? g.ps[un.proj] : g.s) + row * ng;
+      const uint8_t* szp = (MODE == 2 ? g.pz[un.proj] : g.z) + row * (ng / 2);
+      int grp = g64 ? hk : 0;
+      __half sc = __ldg(ssc + grp);
+      uint32_t zb = __ldg(szp + (grp >> 1));
+      for (int j = 0; j < nst; ++j) {
+        ok = mbar_wait(bar_cfull + 8 * s, ph);
         if (!ok) break;
-        // rows 0..127 then 128..255 are consecutive in both buffers
-        ssc = reinterpret_cast<const __half*>(smem + kPfOffScale + b * kPfScaleBuf) + n * ng;
-        szp = smem + kPfOffZp + b * kPfZpBuf + n * ng / 2;
-      } else {
-        // this thread's weight row in global memory: rows wr0.. then wr1..
-        const PfUnit un = pf_unit<MODE>(g, u, nN);
-        const int64_t row = n < 128 ? un.wr0 + n : un.wr1 + (n - 128);
-        ssc = (MODE == 2 ? g.ps[un.proj] : g.s) + row * ng;
-        szp = (MODE == 2 ? g.pz[un.proj] : g.z) + row * ng / 2;
-        gsc = __ldg(ssc);
-        gzb = __ldg(szp);
-      }
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % kPfBStages;
-        const int ic = it / kPfCodeKB, cs = ic % kPfCodeStages, sub = it % kPfCodeKB;
-        ok = mbar_wait(bar_cfull + 8 * cs, (ic / kPfCodeStages) & 1);
-        if (!ok) break;
-        const uint4 v = *reinterpret_cast<const uint4*>(smem + kPfOffCodes + cs * kPfCodeStage +
-                                                        n * kPfCodeRow + sub * 32 + hk * 16);
-        ok = mbar_wait(bar_empty + 8 * s, ((it / kPfBStages) & 1) ^ 1u);
-        if (!ok) break;
-        uint8_t* bst = smem + kPfOffB + s * kPfBStage + n * 128;
-        __half sc;
-        uint32_t zz;
-        if (!g64) {
-          const int grp = kb >> 1;
-          sc = ssc[grp];
-          zz = (uint32_t)(szp[grp >> 1] >> ((grp & 1) * 4)) & 15u;
-        } else {
-          // group kb; the next k-block's scale and zero-point byte are
-          // requested now and arrive while this one is dequantised
-          sc = gsc;
-          zz = (gzb >> ((kb & 1) * 4)) & 15u;
-          if (kb + 1 < nkb) {
-            gsc = __ldg(ssc + kb + 1);
-            if (kb & 1) gzb = __ldg(szp + ((kb + 1) >> 1));
-          }
+        const uint8_t* cp = csrc + s * kPfCodeStage;
+        uint4 v[2];
+        v[0] = *reinterpret_cast<const uint4*>(cp + (lsw << 4));
+        v[1] = *reinterpret_cast<const uint4*>(cp + ((lsw ^ 1) << 4));
+        const int gn = grp + gstep;
+        __half sc_n = sc;
+        uint32_t zb_n = zb;
+        if (j + 1 < nst) {
+          sc_n = __ldg(ssc + gn);
+          zb_n = __ldg(szp + (gn >> 1));
         }
+        ok = mbar_wait(bar_empty + 8 * s, ph ^ 1u);
+        if (!ok) break;
+        const uint32_t zz = (zb >> ((grp & 1) * 4)) & 15u;
         const __half2 s2 = __halves2half2(sc, sc);
         const __half2 s16 = __hmul2(s2, sixteenth);
         const uint32_t zlo = 0x64006400u | zz | (zz << 16);
         const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
-        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v);
+        uint8_t* bst = bdst + s * kPfBStage;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = hk * 4 + cc;  // 16-byte chunk of the 128-byte B row
-          uint32_t wd = wv[cc];
-          uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
-          uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
-          wd >>= 8;
-          uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
-          uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
-          __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2);
-          __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16);
-          __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2);
-          __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16);
-          uint4 o;
-          o.x = *reinterpret_cast<uint32_t*>(&r0);
-          o.y = *reinterpret_cast<uint32_t*>(&r1);
-          o.z = *reinterpret_cast<uint32_t*>(&r2);
-          o.w = *reinterpret_cast<uint32_t*>(&r3);
-          *reinterpret_cast<uint4*>(bst + ((c ^ (n & 7)) << 4)) = o;
+        for (int L = 0; L < 2; ++L) {
+          const int c0 = (L ^ lsw) * 4;  // first 16-byte chunk of the k-block v[L] covers
+          const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[L]);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t wd = wv[cc];
+            uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+            uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+            wd >>= 8;
+            uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+            uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+            __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2);
+            __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16);
+            __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2);
+            __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16);
+            uint4 o;
+            o.x = *reinterpret_cast<uint32_t*>(&r0);
+            o.y = *reinterpret_cast<uint32_t*>(&r1);
+            o.z = *reinterpret_cast<uint32_t*>(&r2);
+            o.w = *reinterpret_cast<uint32_t*>(&r3);
+            *reinterpret_cast<uint4*>(bst + (((c0 + cc) ^ x8) << 4)) = o;
+          }
         }
-        // One proxy fence orders this k-block's generic accesses against the
+        // One proxy fence orders this stage's generic accesses against the
         // async proxy both ways: the B-tile stores before the MMA reads them,
-        // and the code / scale loads before the next TMA or bulk copy
-        // overwrites their slot (without it such a write was observed to
-        // land first, corrupting rows once units ran back to back).
+        // and the code loads before the next TMA overwrites their slot
+        // (without it such a write was observed to land first, corrupting
+        // rows once units ran back to back).
         fence_proxy_async_smem();
-        if (sub == kPfCodeKB - 1) mbar_arrive(bar_cempty + 8 * cs);  // release the code slot
+        mbar_arrive(bar_cempty + 8 * s);  // release the code slot
         mbar_arrive(bar_full + 8 * s);
+        grp = gn;
+        sc = sc_n;
+        zb = zb_n;
+        if (++s == kPfBStages) s = 0, ph ^= 1u;
       }
-      if (ok && !g64) mbar_arrive(bar_sempty + 8 * b);  // done with this unit's scales (fenced above)
     }
   } else {
     // ---- epilogue: TMEM -> registers -> global, one tile row per thread ----
