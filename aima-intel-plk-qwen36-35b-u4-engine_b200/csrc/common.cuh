@@ -104,6 +104,19 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// 32 contiguous bytes to global memory: one 256-bit store when p is 32-byte
+// aligned (a warp then writes 32 full sectors per instruction), else two
+// 128-bit stores.
+__device__ __forceinline__ void st_global_32b(void* p, const uint4& a, const uint4& b, bool a32) {
+  if (a32) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(p), "r"(a.x),
+                 "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                 : "memory");
+  } else {
+    reinterpret_cast<uint4*>(p)[0] = a;
+    reinterpret_cast<uint4*>(p)[1] = b;
+  }
+}
 __device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
   __half2 h = __halves2half2(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -18,26 +18,28 @@
 //   7. pf_scatter  out[t] = sum over ranks r (in order) of Y[inv(t, r)].
 //
 // GEMM kernel: persistent, one CTA per SM (grid min(148, units)); a unit is
-// one 128x256 output tile (M tile of one expert x N tile), taken round-robin.
+// one or two 128-row M tiles (the grouped modes: one tile of one expert) x
+// one 256-wide N tile, taken round-robin.
 // Warp roles (23 warps):
-//   warp 0      TMA producer of the activation tile (SWIZZLE_128B, two
-//               64-wide k-blocks per stage, no multicast) into a 2-deep ring;
+//   warp 0      TMA producer of the activation tiles (SWIZZLE_128B, one
+//               64-wide k-block of each of the unit's tiles per stage, no
+//               multicast) into a 3-deep ring;
 //   warp 1      TMEM allocator (2 x 256 columns) and the single-thread
 //               tcgen05.mma issuer (kind::f16, M=128 N=256 K=16, fp32
-//               accumulate, eight MMAs per stage); units alternate
-//               accumulators;
+//               accumulate, four MMAs per tile and k-block): a two-tile unit
+//               fills both accumulator slots, one-tile units alternate them;
 //   warp 2      B-side producer: the raw u4 codes (TMA, 64 bytes x 256 rows
-//               per stage) into a 2-deep ring;
-//   warps 3-18  dequant, one k-block of a B-tile row per thread and stage:
-//               (q - zp) * scale with one fp16 rounding, written in the
-//               canonical SW128 K-major layout; each row's scales and zero
-//               points are read from global memory one stage ahead;
-//   warps 19-22 epilogue of the previous unit (tcgen05.ld -> registers ->
-//               global) while the next unit's mainloop runs.
-// A ring 2 x 32 KB, B ring 2 x 64 KB, code ring 2 x 16 KB, each stage two
-// k-blocks: per-k-block stages spent as many dequant cycles on waits, proxy
-// fences and barrier arrivals as on the arithmetic, and the MMA thread's
-// per-stage waits left the tensor pipe idle between its 4-MMA bursts. All
+//               per two k-blocks) into a 2-deep ring;
+//   warps 3-18  dequant, half a B-tile row per thread: (q - zp) * scale with
+//               one fp16 rounding, written in the canonical SW128 K-major
+//               layout; each row's scales and zero points are read from
+//               global memory, the next group's one group ahead;
+//   warps 19-22 epilogue (tcgen05.ld -> registers -> global); for one-tile
+//               units it overlaps the next unit's mainloop.
+// A ring 3 x 32 KB, B ring 3 x 32 KB, code ring 2 x 16 KB. Per-thread clock
+// stamps showed the dequant warps bound a one-tile unit (about 1150 cycles
+// per k-block of dequant against 512 of MMA work), so a second tile that
+// reuses each dequantised k-block nearly halves the time per FLOP. All
 // rings are synchronised with mbarriers; every wait is time-bounded and
 // writes an error word on expiry.
 // Buffers that threads read with generic loads and the TMA engine refills
@@ -62,29 +64,28 @@
 namespace iq36 {
 
 constexpr int kPfBM = 128, kPfBN = 256, kPfBK = 64;
-// Every ring stage holds two 64-wide k-blocks: a stage costs each dequant
-// thread one wait per ring, one proxy fence and one arrival, and the MMA
-// thread one wait pair for eight MMAs. Per-k-block stages spent about as many
-// cycles on those as on the dequant arithmetic.
-constexpr int kPfStageKB = 2;
-constexpr int kPfAStages = 2, kPfBStages = 2, kPfCodeStages = 2;
-constexpr int kPfCodeKB = kPfStageKB;
-constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;  // 64 bytes of codes per row
-constexpr int kPfASub = kPfBM * kPfBK * 2;         // one k-block of activations, 16 KB
-constexpr int kPfBSub = kPfBN * kPfBK * 2;         // one dequantised k-block, 32 KB
-constexpr int kPfAStage = kPfStageKB * kPfASub;    // 32 KB
-constexpr int kPfBStage = kPfStageKB * kPfBSub;    // 64 KB
-constexpr int kPfCodeStage = kPfBN * kPfCodeRow;   // 16 KB of u4 codes
-constexpr int kPfOffB = kPfAStages * kPfAStage;    // B ring after the A ring
+// A unit's M extent is one or two 128-row tiles that share each dequantised
+// B k-block (eight MMAs per B stage for two tiles): the dequant, not the
+// tensor pipe, bounds a one-tile unit, and a second tile's MMAs cost about a
+// quarter more time per stage for twice the work.
+constexpr int kPfMaxTiles = 2;
+constexpr int kPfAStages = 3, kPfBStages = 3, kPfCodeStages = 2;
+// A code stage holds two k-blocks of u4 codes for the 256 B-tile rows (TMA
+// rows of 64 bytes, half the row requests of 32-byte rows).
+constexpr int kPfCodeKB = 2;
+constexpr int kPfCodeRow = kPfCodeKB * kPfBK / 2;   // 64 bytes of codes per row
+constexpr int kPfASub = kPfBM * kPfBK * 2;          // one k-block of one tile, 16 KB
+constexpr int kPfAStage = kPfMaxTiles * kPfASub;    // 32 KB
+constexpr int kPfBStage = kPfBN * kPfBK * 2;        // one dequantised k-block, 32 KB
+constexpr int kPfCodeStage = kPfBN * kPfCodeRow;    // 16 KB of u4 codes
+constexpr int kPfOffB = kPfAStages * kPfAStage;     // B ring after the A ring
 constexpr int kPfOffCodes = kPfOffB + kPfBStages * kPfBStage;
 constexpr int kPfOffBar = kPfOffCodes + kPfCodeStages * kPfCodeStage;
 constexpr int kPfSmem = kPfOffBar + 256 + 1024;
-static_assert(kPfCodeStages == kPfBStages && kPfCodeKB == kPfStageKB,
-              "the dequant threads advance the code and B rings together");
 constexpr int kPfDqWarps = 16, kPfEpiWarps = 4;
 constexpr int kPfWarpDq0 = 3, kPfWarpEpi0 = kPfWarpDq0 + kPfDqWarps;
 constexpr int kPfThreads = (kPfWarpEpi0 + kPfEpiWarps) * 32;  // 736
-constexpr int kPfDqThreads = kPfDqWarps * 32;                 // one k-block of a B row each
+constexpr int kPfDqThreads = kPfDqWarps * 32;                 // half a B-tile row each
 constexpr int kPfChunk = 512;  // assignments per schedule CTA (64 CTAs at 4096 tokens x top-8)
 static_assert(kPfChunk % 256 == 0, "placement ranks 256 assignments per round");
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
@@ -329,10 +330,12 @@ struct GemmArgs {
   const uint8_t* pz[4];
   void* pout[4];
   int prow[4], pdt[4], pacc[4];
-  // Group 64 (one quant group per 64-wide k-block) or 128 (one per ring
-  // stage); the dequant threads read a row's scales and zero points from
-  // global memory one stage ahead either way.
+  // Group 64 (one quant group per 64-wide k-block) or 128 (one per two);
+  // the dequant threads read a row's scales and zero points from global
+  // memory, the next group's while the current one is dequantised.
   int g64;
+  // MODE 2/3: 128-row tiles per unit (1 or 2); the grouped modes use 1.
+  int mt;
 };
 
 // projection of a MODE-2 N tile and the tile's index inside it
@@ -346,15 +349,16 @@ __device__ __forceinline__ void pf_proj(const GemmArgs& g, int nt, int& p, int& 
 
 template <int MODE>
 __device__ __forceinline__ int pf_units(const GemmArgs& g) {
-  if (MODE == 2) return (g.T + kPfBM - 1) / kPfBM * (g.H / kPfBN);
-  if (MODE == 3) return (g.T + kPfBM - 1) / kPfBM * (g.I / 128);
+  const int um = kPfBM * g.mt;  // rows per unit
+  if (MODE == 2) return (g.T + um - 1) / um * (g.H / kPfBN);
+  if (MODE == 3) return (g.T + um - 1) / um * (g.I / 128);
   return *g.work.tile_count * (MODE == 0 ? g.I / 128 : g.H / kPfBN);
 }
 template <int MODE>
 __device__ __forceinline__ void pf_rows(const GemmArgs& g, int mt, int& row0, int& rows) {
   if (MODE >= 2) {
-    row0 = mt * kPfBM;
-    rows = min(kPfBM, g.T - row0);
+    row0 = mt * kPfBM * g.mt;
+    rows = min(kPfBM * g.mt, g.T - row0);
   } else {
     row0 = g.work.tile_row0[mt];
     rows = g.work.tile_rows[mt];
@@ -415,7 +419,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t bar_empty = bar_full + 8 * kPfBStages;        // [kPfBStages]
   const uint32_t bar_cfull = bar_empty + 8 * kPfBStages;       // [kPfCodeStages]
   const uint32_t bar_cempty = bar_cfull + 8 * kPfCodeStages;   // [kPfCodeStages]
-  const uint32_t bar_accf = bar_cempty + 8 * kPfCodeStages;    // [2]
+  const uint32_t bar_accf = bar_cempty + 8 * kPfCodeStages;    // [2] per accumulator slot
   const uint32_t bar_acce = bar_accf + 16;                     // [2]
   const uint32_t bar_done = bar_acce + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_done + 8 - base));
@@ -451,124 +455,132 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   pdl_wait();  // the tile table and both operands come from earlier launches
   const int nN = (MODE == 0 || MODE == 3) ? g.I / 128 : g.H / kPfBN;
   const int total = pf_units<MODE>(g);
-  const int nst = g.K / (kPfBK * kPfStageKB);  // ring stages per unit (K % 128 == 0)
+  const int nkb = g.K / kPfBK;
   const bool g64 = g.g64 != 0;
   const int ng = g64 ? g.K / 64 : g.K / 128;
   bool ok = true;
 
   if (warp == 0) {
-    // ---- activation producer (TMA, SWIZZLE_128B, two k-blocks a stage) ----
+    // ---- activation producer (TMA, SWIZZLE_128B, one k-block of each of
+    // the unit's 128-row tiles per stage) ----
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        int row0, rows_unused;
-        pf_rows<MODE>(g, u / nN, row0, rows_unused);
-        for (int j = 0; j < nst; ++j) {
+        int row0, rows;
+        pf_rows<MODE>(g, u / nN, row0, rows);
+        const int mtn = rows > kPfBM ? 2 : 1;
+        for (int kb = 0; kb < nkb; ++kb) {
           ok = mbar_wait(bar_aempty + 8 * s, ph ^ 1u);
           if (!ok) break;
           const uint32_t dst = base + s * kPfAStage;
-          mbar_arrive_tx(bar_afull + 8 * s, kPfAStage);
-#pragma unroll
-          for (int sb = 0; sb < kPfStageKB; ++sb)
-            tma_load_2d(dst + sb * kPfASub, &tmA, (j * kPfStageKB + sb) * kPfBK, row0,
-                        bar_afull + 8 * s);
+          mbar_arrive_tx(bar_afull + 8 * s, (uint32_t)(mtn * kPfASub));
+          for (int t = 0; t < mtn; ++t)
+            tma_load_2d(dst + t * kPfASub, &tmA, kb * kPfBK, row0 + t * kPfBM, bar_afull + 8 * s);
           if (++s == kPfAStages) s = 0, ph ^= 1u;
         }
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer: one thread, accumulators alternate between two
-    // 256-column TMEM buffers so the epilogue of a unit overlaps the next ----
+    // ---- MMA issuer: one thread. A two-tile unit accumulates its tiles in
+    // both 256-column TMEM slots (its epilogue then runs after the mainloop);
+    // one-tile units alternate slots, so their epilogue overlaps the next
+    // unit's mainloop. ----
     if (lane == 0) {
-      int sa = 0, sb_ = 0, i = 0;
-      uint32_t pha = 0, phb = 0;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
-        const int a = i & 1;
-        ok = mbar_wait(bar_acce + 8 * a, ((i >> 1) & 1) ^ 1u);
+      int sa = 0, sb = 0, last = 1;
+      uint32_t pha = 0, phb = 0, pu = 0;  // pu bit l: parity of slot l's uses so far
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        int row0, rows;
+        pf_rows<MODE>(g, u / nN, row0, rows);
+        const int mtn = rows > kPfBM ? 2 : 1;
+        const int s0 = mtn == 2 ? 0 : (last ^ 1);
+        last = mtn == 2 ? 1 : s0;
+        for (int t = 0; t < mtn && ok; ++t) {
+          const int sl = s0 + t;
+          ok = mbar_wait(bar_acce + 8 * sl, ((pu >> sl) & 1u) ^ 1u);  // previous use drained
+          pu ^= 1u << sl;
+        }
         if (!ok) break;
         tc_fence_after();
-        const uint32_t acc = tmem + (uint32_t)(a * kPfBN);
-        for (int j = 0; j < nst; ++j) {
-          ok = mbar_wait(bar_afull + 8 * sa, pha) && mbar_wait(bar_full + 8 * sb_, phb);
+        const uint32_t acc = tmem + (uint32_t)(s0 * kPfBN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          ok = mbar_wait(bar_afull + 8 * sa, pha) && mbar_wait(bar_full + 8 * sb, phb);
           if (!ok) break;
           tc_fence_after();
           const uint32_t a_s = base + sa * kPfAStage;
-          const uint32_t b_s = base + kPfOffB + sb_ * kPfBStage;
-#pragma unroll
-          for (int sub = 0; sub < kPfStageKB; ++sub)
+          const uint32_t b_s = base + kPfOffB + sb * kPfBStage;
+          for (int t = 0; t < mtn; ++t) {
 #pragma unroll
             for (int kk = 0; kk < kPfBK / 16; ++kk)
-              umma_f16(acc, sw128_desc(a_s + sub * kPfASub + kk * 32),
-                       sw128_desc(b_s + sub * kPfBSub + kk * 32), kIdesc,
-                       (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+              umma_f16(acc + (uint32_t)(t * kPfBN), sw128_desc(a_s + t * kPfASub + kk * 32),
+                       sw128_desc(b_s + kk * 32), kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
           umma_commit(bar_aempty + 8 * sa);  // stages free once these MMAs complete
-          umma_commit(bar_empty + 8 * sb_);
+          umma_commit(bar_empty + 8 * sb);
           if (++sa == kPfAStages) sa = 0, pha ^= 1u;
-          if (++sb_ == kPfBStages) sb_ = 0, phb ^= 1u;
+          if (++sb == kPfBStages) sb = 0, phb ^= 1u;
         }
-        if (ok) umma_commit(bar_accf + 8 * a);  // accumulator complete
+        if (ok)
+          for (int t = 0; t < mtn; ++t) umma_commit(bar_accf + 8 * (s0 + t));  // tile complete
       }
       // every MMA issued above has completed before the teardown
       umma_commit(bar_done);
       if (!mbar_wait(bar_done, 0)) ok = false;
     }
   } else if (warp == 2) {
-    // ---- B-side producer: the unit's raw u4 codes by TMA, a stage of two
-    // k-blocks per 64-byte row ----
+    // ---- B-side producer: the unit's raw u4 codes by TMA, two k-blocks per
+    // 64-byte row ----
     if (lane == 0) {
       int cs = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const PfUnit un = pf_unit<MODE>(g, u, nN);
         const CUtensorMap* wmap = un.proj == 0 ? &tmW : un.proj == 1 ? &tmW1 : un.proj == 2 ? &tmW2 : &tmW3;
-        for (int j = 0; j < nst; ++j) {
+        // nkb is a multiple of kPfCodeKB, so code stages never straddle units
+        for (int cb = 0; cb < nkb / kPfCodeKB; ++cb) {
           ok = mbar_wait(bar_cempty + 8 * cs, ph ^ 1u);
           if (!ok) break;
           const uint32_t dst = base + kPfOffCodes + cs * kPfCodeStage;
           mbar_arrive_tx(bar_cfull + 8 * cs, kPfCodeStage);
-          tma_load_2d(dst, wmap, j * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
-          tma_load_2d(dst + kPfCodeStage / 2, wmap, j * kPfCodeRow, (int)un.wr1,
+          tma_load_2d(dst, wmap, cb * kPfCodeRow, (int)un.wr0, bar_cfull + 8 * cs);
+          tma_load_2d(dst + kPfCodeStage / 2, wmap, cb * kPfCodeRow, (int)un.wr1,
                       bar_cfull + 8 * cs);
           if (++cs == kPfCodeStages) cs = 0, ph ^= 1u;
         }
       }
     }
   } else if (warp < kPfWarpEpi0) {
-    // ---- dequant: thread pair (2n, 2n+1) owns row n of the 256-row B tile;
-    // thread hk dequantises k-block hk of each stage into the canonical SW128
-    // K-major image. Scales and zero points come from global memory, one
-    // stage ahead (a row's 2 bytes of scale per group hit L1 after the first
-    // stage). The two 16-byte code loads go in an order that alternates every
-    // two rows, which spreads a warp's loads over all 32 banks. ----
+    // ---- dequant: thread pair (2n, 2n+1) owns row n of the 256-row B tile,
+    // k 0..31 and 32..63 of each k-block, written in the canonical SW128
+    // K-major layout. Scales and zero points come from global memory, the
+    // next group's requested while the current one is dequantised (a row's
+    // scales hit L1 after the first k-block). ----
     const int dt = threadIdx.x - kPfWarpDq0 * 32;
     const int n = dt >> 1, hk = dt & 1;
-    const int x8 = n & 7, lsw = (n >> 1) & 1;
+    const int x8 = n & 7;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
-    const uint8_t* const csrc = smem + kPfOffCodes + n * kPfCodeRow + hk * (kPfBK / 2);
-    uint8_t* const bdst = smem + kPfOffB + hk * kPfBSub + n * 128;
-    const int gstep = g64 ? 2 : 1;  // this thread's group advances per stage by
-    int s = 0;                      // code and B rings advance together
-    uint32_t ph = 0;
+    const uint8_t* const csrc = smem + kPfOffCodes + n * kPfCodeRow + hk * 16;
+    uint8_t* const bdst = smem + kPfOffB + n * 128;
+    const int gsh = g64 ? 0 : 1;  // k-block -> quant group shift
+    int s = 0, cs = 0, sub = 0;
+    uint32_t ph = 0, cph = 0;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
       const PfUnit un = pf_unit<MODE>(g, u, nN);
       const int64_t row = n < 128 ? un.wr0 + n : un.wr1 + (n - 128);
       const __half* ssc = (MODE == 2 ? g.ps[un.proj] : g.s) + row * ng;
       const uint8_t* szp = (MODE == 2 ? g.pz[un.proj] : g.z) + row * (ng / 2);
-      int grp = g64 ? hk : 0;
-      __half sc = __ldg(ssc + grp);
-      uint32_t zb = __ldg(szp + (grp >> 1));
-      for (int j = 0; j < nst; ++j) {
-        ok = mbar_wait(bar_cfull + 8 * s, ph);
+      int grp = 0;
+      __half sc = __ldg(ssc);
+      uint32_t zb = __ldg(szp);
+      for (int kb = 0; kb < nkb; ++kb) {
+        ok = mbar_wait(bar_cfull + 8 * cs, cph);
         if (!ok) break;
-        const uint8_t* cp = csrc + s * kPfCodeStage;
-        uint4 v[2];
-        v[0] = *reinterpret_cast<const uint4*>(cp + (lsw << 4));
-        v[1] = *reinterpret_cast<const uint4*>(cp + ((lsw ^ 1) << 4));
-        const int gn = grp + gstep;
+        const uint4 v =
+            *reinterpret_cast<const uint4*>(csrc + cs * kPfCodeStage + sub * (kPfBK / 2));
+        const int gn = (kb + 1) >> gsh;
         __half sc_n = sc;
         uint32_t zb_n = zb;
-        if (j + 1 < nst) {
+        if (kb + 1 < nkb && gn != grp) {
           sc_n = __ldg(ssc + gn);
           zb_n = __ldg(szp + (gn >> 1));
         }
@@ -580,172 +592,189 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t zlo = 0x64006400u | zz | (zz << 16);
         const uint32_t zhi = 0x64006400u | (zz << 4) | (zz << 20);
         uint8_t* bst = bdst + s * kPfBStage;
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
-        for (int L = 0; L < 2; ++L) {
-          const int c0 = (L ^ lsw) * 4;  // first 16-byte chunk of the k-block v[L] covers
-          const uint32_t* wv = reinterpret_cast<const uint32_t*>(&v[L]);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t wd = wv[cc];
-            uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
-            uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
-            wd >>= 8;
-            uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
-            uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
-            __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2);
-            __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16);
-            __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2);
-            __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16);
-            uint4 o;
-            o.x = *reinterpret_cast<uint32_t*>(&r0);
-            o.y = *reinterpret_cast<uint32_t*>(&r1);
-            o.z = *reinterpret_cast<uint32_t*>(&r2);
-            o.w = *reinterpret_cast<uint32_t*>(&r3);
-            *reinterpret_cast<uint4*>(bst + (((c0 + cc) ^ x8) << 4)) = o;
-          }
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = hk * 4 + cc;  // 16-byte chunk of the 128-byte B row
+          uint32_t wd = wv[cc];
+          uint32_t q0 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+          uint32_t q1 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+          wd >>= 8;
+          uint32_t q2 = hsub2_u32(lop3_and_or(wd, 0x000F000Fu, 0x64006400u), zlo);
+          uint32_t q3 = hsub2_u32(lop3_and_or(wd, 0x00F000F0u, 0x64006400u), zhi);
+          __half2 r0 = __hmul2(*reinterpret_cast<__half2*>(&q0), s2);
+          __half2 r1 = __hmul2(*reinterpret_cast<__half2*>(&q1), s16);
+          __half2 r2 = __hmul2(*reinterpret_cast<__half2*>(&q2), s2);
+          __half2 r3 = __hmul2(*reinterpret_cast<__half2*>(&q3), s16);
+          uint4 o;
+          o.x = *reinterpret_cast<uint32_t*>(&r0);
+          o.y = *reinterpret_cast<uint32_t*>(&r1);
+          o.z = *reinterpret_cast<uint32_t*>(&r2);
+          o.w = *reinterpret_cast<uint32_t*>(&r3);
+          *reinterpret_cast<uint4*>(bst + ((c ^ x8) << 4)) = o;
         }
-        // One proxy fence orders this stage's generic accesses against the
+        // One proxy fence orders this k-block's generic accesses against the
         // async proxy both ways: the B-tile stores before the MMA reads them,
         // and the code loads before the next TMA overwrites their slot
         // (without it such a write was observed to land first, corrupting
         // rows once units ran back to back).
         fence_proxy_async_smem();
-        mbar_arrive(bar_cempty + 8 * s);  // release the code slot
+        if (sub == kPfCodeKB - 1) mbar_arrive(bar_cempty + 8 * cs);  // release the code slot
         mbar_arrive(bar_full + 8 * s);
         grp = gn;
         sc = sc_n;
         zb = zb_n;
         if (++s == kPfBStages) s = 0, ph ^= 1u;
+        if (++sub == kPfCodeKB) {
+          sub = 0;
+          if (++cs == kPfCodeStages) cs = 0, cph ^= 1u;
+        }
       }
     }
   } else {
-    // ---- epilogue: TMEM -> registers -> global, one tile row per thread ----
+    // ---- epilogue: TMEM -> registers -> global, one tile row per thread,
+    // the unit's tiles in slot order ----
     const int sp = warp & 3;       // TMEM sub-partition of this warp
     const int m = sp * 32 + lane;  // tile row = TMEM lane
-    int i = 0;
-    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++i) {
-      const int a = i & 1;
-      // warp-uniform: the TMEM loads below are warp-collective
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_accf + 8 * a, (i >> 1) & 1));
-      if (!ok) break;
-      tc_fence_after();
+    int last = 1;
+    uint32_t pu = 0;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
       const int mt = u / nN, nt = u - mt * nN;
-      int row0, rows;
-      pf_rows<MODE>(g, mt, row0, rows);
-      const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
-      if (MODE == 0 || MODE == 3) {
-        for (int j = 0; j < 128; j += 16) {
-          uint32_t gv[16], uv[16];
-          tmem_ld16(tl + j, gv);
-          tmem_ld16(tl + 128 + j, uv);
-          tmem_ld_wait();
-          if (m < rows && MODE == 3) {
-            // natural column order, [T, I] fp16
-            __half* dst = reinterpret_cast<__half*>(g.out) + (size_t)(row0 + m) * g.I + nt * 128 + j;
-            uint32_t hw[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const float g0 = __uint_as_float(gv[2 * c]), u0 = __uint_as_float(uv[2 * c]);
-              const float g1 = __uint_as_float(gv[2 * c + 1]), u1 = __uint_as_float(uv[2 * c + 1]);
-              hw[c] = pack_half2(__float2half_rn(g0 * sigmoidf_acc(g0) * u0),
-                                 __float2half_rn(g1 * sigmoidf_acc(g1) * u1));
-            }
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-            d4[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            d4[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-          } else if (m < rows) {
-            __half* dst = g.work.act + (size_t)(row0 + m) * g.I + nt * 128 + j;
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              __half a8[8];
+      int urow0, urows;
+      pf_rows<MODE>(g, mt, urow0, urows);
+      const int mtn = urows > kPfBM ? 2 : 1;
+      const int s0 = mtn == 2 ? 0 : (last ^ 1);
+      last = mtn == 2 ? 1 : s0;
+      for (int t = 0; t < mtn; ++t) {
+        const int a = s0 + t;
+        // warp-uniform: the TMEM loads below are warp-collective
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_accf + 8 * a, (pu >> a) & 1u));
+        if (!ok) break;
+        pu ^= 1u << a;
+        tc_fence_after();
+        const int row0 = urow0 + t * kPfBM, rows = min(kPfBM, urows - t * kPfBM);
+        const uint32_t tl = tmem + (uint32_t)(a * kPfBN) + ((uint32_t)(sp * 32) << 16);
+        if (MODE == 0 || MODE == 3) {
+          for (int j = 0; j < 128; j += 16) {
+            uint32_t gv[16], uv[16];
+            tmem_ld16(tl + j, gv);
+            tmem_ld16(tl + 128 + j, uv);
+            tmem_ld_wait();
+            if (m < rows && MODE == 3) {
+              // natural column order, [T, I] fp16
+              __half* dst = reinterpret_cast<__half*>(g.out) + (size_t)(row0 + m) * g.I + nt * 128 + j;
+              uint32_t hw[8];
 #pragma unroll
               for (int c = 0; c < 8; ++c) {
-                const float gt = __uint_as_float(gv[8 * q + c]);
-                const float up = __uint_as_float(uv[8 * q + c]);
-                a8[c] = __float2half_rn(gt * sigmoidf_acc(gt) * up);
+                const float g0 = __uint_as_float(gv[2 * c]), u0 = __uint_as_float(uv[2 * c]);
+                const float g1 = __uint_as_float(gv[2 * c + 1]), u1 = __uint_as_float(uv[2 * c + 1]);
+                hw[c] = pack_half2(__float2half_rn(g0 * sigmoidf_acc(g0) * u0),
+                                   __float2half_rn(g1 * sigmoidf_acc(g1) * u1));
               }
-              uint4 o;
-              o.x = pack_half2(a8[0], a8[4]);
-              o.y = pack_half2(a8[1], a8[5]);
-              o.z = pack_half2(a8[2], a8[6]);
-              o.w = pack_half2(a8[3], a8[7]);
-              *reinterpret_cast<uint4*>(dst + 8 * q) = o;
-            }
-          }
-        }
-      } else if (MODE == 2) {
-        int pj, ntl;
-        pf_proj(g, nt, pj, ntl);
-        void* const pout = g.pout[pj];
-        const int prow = g.prow[pj], pdt = g.pdt[pj], pacc = g.pacc[pj];
-        const float rg =
-            (g.row_gate != nullptr && m < rows) ? sigmoidf_acc(g.row_gate[row0 + m]) : 1.f;
-        for (int j = 0; j < kPfBN; j += 16) {
-          uint32_t yv[16];
-          tmem_ld16(tl + j, yv);
-          tmem_ld_wait();
-          if (g.row_gate != nullptr) {
+              st_global_32b(dst, make_uint4(hw[0], hw[1], hw[2], hw[3]),
+                            make_uint4(hw[4], hw[5], hw[6], hw[7]),
+                            (reinterpret_cast<uintptr_t>(g.out) & 31) == 0);
+            } else if (m < rows) {
+              __half* dst = g.work.act + (size_t)(row0 + m) * g.I + nt * 128 + j;
+              uint4 o2[2];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) yv[q] = __float_as_uint(__uint_as_float(yv[q]) * rg);
-          }
-          if (m < rows) {
-            const size_t o = (size_t)(row0 + m) * prow + ntl * kPfBN + j;
-            if (pdt == IQ36_F16) {
-              uint4 h[2];
-              uint32_t* hw = reinterpret_cast<uint32_t*>(h);
+              for (int q = 0; q < 2; ++q) {
+                __half a8[8];
 #pragma unroll
-              for (int q = 0; q < 8; ++q)
-                hw[q] = pack_half2(__float2half_rn(__uint_as_float(yv[2 * q])),
-                                   __float2half_rn(__uint_as_float(yv[2 * q + 1])));
-              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(pout) + o);
-              dst[0] = h[0];
-              dst[1] = h[1];
-            } else {
-              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(pout) + o);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                float4 v = make_float4(__uint_as_float(yv[4 * q]), __uint_as_float(yv[4 * q + 1]),
-                                       __uint_as_float(yv[4 * q + 2]),
-                                       __uint_as_float(yv[4 * q + 3]));
-                if (pacc) {
-                  // residual += the fp16-rounded projection output
-                  const float4 r = dst[q];
-                  v.x = r.x + __half2float(__float2half_rn(v.x));
-                  v.y = r.y + __half2float(__float2half_rn(v.y));
-                  v.z = r.z + __half2float(__float2half_rn(v.z));
-                  v.w = r.w + __half2float(__float2half_rn(v.w));
+                for (int c = 0; c < 8; ++c) {
+                  const float gt = __uint_as_float(gv[8 * q + c]);
+                  const float up = __uint_as_float(uv[8 * q + c]);
+                  a8[c] = __float2half_rn(gt * sigmoidf_acc(gt) * up);
                 }
-                dst[q] = v;
+                uint4 o;
+                o.x = pack_half2(a8[0], a8[4]);
+                o.y = pack_half2(a8[1], a8[5]);
+                o.z = pack_half2(a8[2], a8[6]);
+                o.w = pack_half2(a8[3], a8[7]);
+                o2[q] = o;
+              }
+              st_global_32b(dst, o2[0], o2[1], true);  // workspace rows: 256-byte aligned
+            }
+          }
+        } else if (MODE == 2) {
+          int pj, ntl;
+          pf_proj(g, nt, pj, ntl);
+          void* const pout = g.pout[pj];
+          const bool pout32 = (reinterpret_cast<uintptr_t>(pout) & 31) == 0;
+          const int prow = g.prow[pj], pdt = g.pdt[pj], pacc = g.pacc[pj];
+          const float rg =
+              (g.row_gate != nullptr && m < rows) ? sigmoidf_acc(g.row_gate[row0 + m]) : 1.f;
+          for (int j = 0; j < kPfBN; j += 16) {
+            uint32_t yv[16];
+            tmem_ld16(tl + j, yv);
+            tmem_ld_wait();
+            if (g.row_gate != nullptr) {
+#pragma unroll
+              for (int q = 0; q < 16; ++q) yv[q] = __float_as_uint(__uint_as_float(yv[q]) * rg);
+            }
+            if (m < rows) {
+              const size_t o = (size_t)(row0 + m) * prow + ntl * kPfBN + j;
+              if (pdt == IQ36_F16) {
+                uint4 h[2];
+                uint32_t* hw = reinterpret_cast<uint32_t*>(h);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  hw[q] = pack_half2(__float2half_rn(__uint_as_float(yv[2 * q])),
+                                     __float2half_rn(__uint_as_float(yv[2 * q + 1])));
+                st_global_32b(reinterpret_cast<__half*>(pout) + o, h[0], h[1], pout32);
+              } else {
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(pout) + o);
+                float4 v4[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  float4 v = make_float4(__uint_as_float(yv[4 * q]), __uint_as_float(yv[4 * q + 1]),
+                                         __uint_as_float(yv[4 * q + 2]),
+                                         __uint_as_float(yv[4 * q + 3]));
+                  if (pacc) {
+                    // residual += the fp16-rounded projection output
+                    const float4 r = dst[q];
+                    v.x = r.x + __half2float(__float2half_rn(v.x));
+                    v.y = r.y + __half2float(__float2half_rn(v.y));
+                    v.z = r.z + __half2float(__float2half_rn(v.z));
+                    v.w = r.w + __half2float(__float2half_rn(v.w));
+                  }
+                  v4[q] = v;
+                }
+                const uint4* u4v = reinterpret_cast<const uint4*>(v4);
+                st_global_32b(dst, u4v[0], u4v[1], pout32);
+                st_global_32b(dst + 2, u4v[2], u4v[3], pout32);
               }
             }
           }
-        }
-      } else {
-        const float wt = m < rows ? g.work.perm_w[row0 + m] : 0.f;
-        for (int j = 0; j < kPfBN; j += 16) {
-          uint32_t yv[16];
-          tmem_ld16(tl + j, yv);
-          tmem_ld_wait();
-          if (m < rows) {
-            __half* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
+        } else {
+          const float wt = m < rows ? g.work.perm_w[row0 + m] : 0.f;
+          for (int j = 0; j < kPfBN; j += 16) {
+            uint32_t yv[16];
+            tmem_ld16(tl + j, yv);
+            tmem_ld_wait();
+            if (m < rows) {
+              __half* dst = g.work.y + (size_t)(row0 + m) * g.H + nt * kPfBN + j;
+              uint4 o2[2];
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              uint4 o;
-              o.x = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q]) * wt),
-                               __float2half_rn(__uint_as_float(yv[8 * q + 1]) * wt));
-              o.y = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 2]) * wt),
-                               __float2half_rn(__uint_as_float(yv[8 * q + 3]) * wt));
-              o.z = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 4]) * wt),
-                               __float2half_rn(__uint_as_float(yv[8 * q + 5]) * wt));
-              o.w = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 6]) * wt),
-                               __float2half_rn(__uint_as_float(yv[8 * q + 7]) * wt));
-              *reinterpret_cast<uint4*>(dst + 8 * q) = o;
+              for (int q = 0; q < 2; ++q) {
+                uint4 o;
+                o.x = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q]) * wt),
+                                 __float2half_rn(__uint_as_float(yv[8 * q + 1]) * wt));
+                o.y = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 2]) * wt),
+                                 __float2half_rn(__uint_as_float(yv[8 * q + 3]) * wt));
+                o.z = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 4]) * wt),
+                                 __float2half_rn(__uint_as_float(yv[8 * q + 5]) * wt));
+                o.w = pack_half2(__float2half_rn(__uint_as_float(yv[8 * q + 6]) * wt),
+                                 __float2half_rn(__uint_as_float(yv[8 * q + 7]) * wt));
+                o2[q] = o;
+              }
+              st_global_32b(dst, o2[0], o2[1], true);  // workspace rows: 256-byte aligned
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(bar_acce + 8 * a);  // this accumulator may be overwritten
       }
-      tc_fence_before();
-      mbar_arrive(bar_acce + 8 * a);  // this accumulator may be overwritten
     }
   }
   if (!ok) {
@@ -1097,6 +1126,7 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
   GemmArgs g1{reinterpret_cast<const __half*>(b->gate_up_scale), b->gate_up_zp, (int64_t)2 * I,
               H, I, H, w};
   g1.g64 = b->group == 64;
+  g1.mt = 1;
   // persistent grids: at most one CTA per SM, never more than the units
   int sms = 148;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -1108,6 +1138,7 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
                map_x, map_gu, map_gu, map_gu, map_gu, g1);
   GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
   g2.g64 = b->group == 64;
+  g2.mt = 1;
   if (e == cudaSuccess)
     e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_act, map_d, map_d, map_d, map_d, g2);
@@ -1247,7 +1278,17 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
     g.pacc[p] = have ? proj[p].accumulate : 0;
     g.tile_base[p + 1] = g.tile_base[p] + (have ? proj[p].m.rows / kPfBN : 0);
   }
-  const int units = (T + kPfBM - 1) / kPfBM * (total_rows / kPfBN);
+  // One or two 128-row tiles per unit: the one with fewer rounds of the
+  // persistent grid, a two-tile unit costing ~1.35 one-tile units (measured:
+  // +26% mainloop time for the second tile's MMAs, plus its epilogue, which
+  // does not overlap the next unit).
+  const int nt_units = total_rows / kPfBN;
+  auto rounds = [&](int mt) {
+    const int u = (T + kPfBM * mt - 1) / (kPfBM * mt) * nt_units;
+    return (double)((u + sms - 1) / sms) * (mt == 2 ? 1.35 : 1.0);
+  };
+  g.mt = rounds(2) < rounds(1) ? 2 : 1;
+  const int units = (T + kPfBM * g.mt - 1) / (kPfBM * g.mt) * nt_units;
   if (e == cudaSuccess)
     e = launch(swiglu ? pf_gemm_kernel<3> : pf_gemm_kernel<2>,
                dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads), (size_t)kPfSmem, stream,
