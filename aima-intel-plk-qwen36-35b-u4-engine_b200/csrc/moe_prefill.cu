@@ -1281,13 +1281,14 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
   // One or two 128-row tiles per unit: the one with fewer rounds of the
   // persistent grid, a two-tile unit costing ~1.35 one-tile units (measured:
   // +26% mainloop time for the second tile's MMAs, plus its epilogue, which
-  // does not overlap the next unit).
+  // does not overlap the next unit). The SwiGLU mode keeps one tile: its
+  // epilogue (an exp and a divide per output) is too long to expose.
   const int nt_units = total_rows / kPfBN;
   auto rounds = [&](int mt) {
     const int u = (T + kPfBM * mt - 1) / (kPfBM * mt) * nt_units;
     return (double)((u + sms - 1) / sms) * (mt == 2 ? 1.35 : 1.0);
   };
-  g.mt = rounds(2) < rounds(1) ? 2 : 1;
+  g.mt = !swiglu && rounds(2) < rounds(1) ? 2 : 1;
   const int units = (T + kPfBM * g.mt - 1) / (kPfBM * g.mt) * nt_units;
   if (e == cudaSuccess)
     e = launch(swiglu ? pf_gemm_kernel<3> : pf_gemm_kernel<2>,
