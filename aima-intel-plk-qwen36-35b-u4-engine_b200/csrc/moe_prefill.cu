@@ -1179,11 +1179,16 @@ __global__ void __launch_bounds__(256) gemm_xprep_kernel(const void* x, int x_dt
   }
   for (int c = tid; c < K / 8; c += 256) {
     if (x_dtype == IQ36_F32) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float v = xf[c * 8 + j];
-        h[j] = __float2half_rn(nw != nullptr ? v * scale * nw[c * 8 + j] : v);
+      // two 16-byte loads of x (and of nw) per 8-chunk (K % 256 == 0)
+      float v[8], w[8];
+      *reinterpret_cast<float4*>(v) = reinterpret_cast<const float4*>(xf + c * 8)[0];
+      *reinterpret_cast<float4*>(v + 4) = reinterpret_cast<const float4*>(xf + c * 8)[1];
+      if (nw != nullptr) {
+        *reinterpret_cast<float4*>(w) = reinterpret_cast<const float4*>(nw + c * 8)[0];
+        *reinterpret_cast<float4*>(w + 4) = reinterpret_cast<const float4*>(nw + c * 8)[1];
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(nw != nullptr ? v[j] * scale * w[j] : v[j]);
     } else {
       const uint4 raw = *reinterpret_cast<const uint4*>(xh + c * 8);
       const __half* hp = reinterpret_cast<const __half*>(&raw);
@@ -1216,7 +1221,7 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
   if (swiglu && n_proj != 1) return IQ36_ERR_ARG;
   if (row_gate && n_proj != 1) return IQ36_ERR_ARG;
   if ((G != 128 && G != 64) || T < 1 || K < 256 || K % 256 || K > 4096) return IQ36_ERR_SHAPE;
-  if (!aligned(x, 16)) return IQ36_ERR_ALIGN;
+  if (!aligned(x, 16) || (nw && !aligned(nw, 16))) return IQ36_ERR_ALIGN;
   int total_rows = 0;
   for (int p = 0; p < n_proj; ++p) {
     const iq36_u4_projection& q = proj[p];

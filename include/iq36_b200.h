@@ -279,7 +279,7 @@ size_t iq36_moe_layer_prefill_workspace_bytes(int32_t T, int32_t k, int32_t num_
  * The batched form of the fixed-FC projections (IQ36FixedFC over [T, K],
  * tools/intel_qwen36_openvino_fixed_fc.py:31-92; the prefill buckets of the
  * OpenVINO graph run the same FCs with M = T). Requirements: group 128 or 64,
- * K % 256 == 0, K <= 4096, N % 256 == 0. */
+ * K % 256 == 0, K <= 4096, N % 256 == 0; x and norm_weight 16-byte aligned. */
 int iq36_u4_gemm(const void* x, int32_t x_dtype, const float* norm_weight, float norm_eps,
                  int32_t T, int32_t K, int32_t group, const iq36_u4_matrix* w, void* out,
                  int32_t out_dtype, int32_t accumulate, void* workspace, size_t workspace_bytes,
