@@ -98,3 +98,30 @@ def test_u4_gemm_multi_matches_single_calls_and_oracle(cuda, G):
     single_res = _t(res0.copy(), cuda)
     u4_gemm(_t(x, cuda), acc_w, out=single_res, accumulate=True, norm_weight=_t(nw, cuda))
     assert torch.equal(single_res, res)
+
+
+@pytest.mark.parametrize("T", [4160, 4296])
+def test_u4_gemm_two_tile_units_bit_equal_one_tile(cuda, T):
+    """At T = 4160 / 4296 and N = 12288 the GEMM runs units of two 128-row
+    tiles that share each dequantised k-block, the last unit holding one tile
+    (64 rows) or a partial second tile (72 rows). Each output row depends only
+    on its input row, so every row equals, bit for bit, the same row from
+    calls short enough to run one-tile units; sampled rows also match the
+    oracle's GEMV."""
+    import torch
+    from engine.ops import u4_gemm
+    rng = np.random.default_rng(T)
+    K, N, G = 2048, 12288, 128
+    w, s, z = make_u4(rng, N, K, G)
+    wt = u4_to_torch(w, s, z, cuda, G)
+    x = (rng.standard_normal((T, K)) * 2).astype(np.float32)
+    nw = rng.uniform(0.9, 1.1, K).astype(np.float32)
+    xt, nwt = _t(x, cuda), _t(nw, cuda)
+    full = u4_gemm(xt, wt, out_dtype=torch.float16, norm_weight=nwt)
+    for r0, r1 in ((0, 128), (3968, 4096), (4096, T)):
+        part = u4_gemm(xt[r0:r1].contiguous(), wt, out_dtype=torch.float16, norm_weight=nwt)
+        assert torch.equal(full[r0:r1], part), f"rows {r0}..{r1}: two-tile units differ"
+    got = full.float().cpu().numpy()
+    for t in (5, 4095, T - 1):
+        x16 = oracle.rms_norm(x[t], nw, 1e-6).astype(np.float16)
+        assert_close(got[t], oracle.u4_gemv(x16, w, s, z, G), f"gemm row {t}")
