@@ -209,25 +209,41 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
   const int t0 = c * kCk, n = min(kCk, T - t0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
-  for (int i = tid; i < kCk * 32; i += blockDim.x) {
-    const int r = i >> 5, p = i & 31;
-    float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), qv4 = kv4, vv4 = kv4;
+  // Every global load of this thread is issued before any shared-memory
+  // store (one DRAM round trip for the phase instead of one per row group).
+  float lgv = 0.f, btv = 0.f;
+  if (warp == 0 && lane < n) {
+    lgv = lg[(size_t)(t0 + lane) * nv + h];
+    btv = beta[(size_t)(t0 + lane) * nv + h];
+  }
+  constexpr int kLd = kCk * 32 / 256;  // float4 columns per thread (blockDim 256)
+  float4 kv4[kLd], qv4[kLd];
+  uint2 vraw[kLd];
+#pragma unroll
+  for (int u = 0; u < kLd; ++u) {
+    const int i = tid + 256 * u, r = i >> 5, p = i & 31;
+    kv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    qv4[u] = kv4[u];
+    vraw[u] = make_uint2(0u, 0u);
     if (r < n) {
       const size_t row = (size_t)(t0 + r) * 2 * nk;
-      kv4 = *reinterpret_cast<const float4*>(qk + (row + nk + kh) * kDhd + 4 * p);
-      qv4 = *reinterpret_cast<const float4*>(qk + (row + kh) * kDhd + 4 * p);
-      const uint2 raw =
+      kv4[u] = *reinterpret_cast<const float4*>(qk + (row + nk + kh) * kDhd + 4 * p);
+      qv4[u] = *reinterpret_cast<const float4*>(qk + (row + kh) * kDhd + 4 * p);
+      vraw[u] =
           *reinterpret_cast<const uint2*>(v + (size_t)(t0 + r) * nv * kDhd + h * kDhd + 4 * p);
-      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-      vv4 = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
-    *reinterpret_cast<float4*>(sk + r * 132 + 4 * p) = kv4;
-    *reinterpret_cast<float4*>(sq + r * 132 + 4 * p) = qv4;
-    *reinterpret_cast<float4*>(sv + r * 128 + 4 * p) = vv4;
+  }
+#pragma unroll
+  for (int u = 0; u < kLd; ++u) {
+    const int i = tid + 256 * u, r = i >> 5, p = i & 31;
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&vraw[u].x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&vraw[u].y));
+    *reinterpret_cast<float4*>(sk + r * 132 + 4 * p) = kv4[u];
+    *reinterpret_cast<float4*>(sq + r * 132 + 4 * p) = qv4[u];
+    *reinterpret_cast<float4*>(sv + r * 128 + 4 * p) = make_float4(lo.x, lo.y, hi.x, hi.y);
   }
   if (warp == 0) {
-    float x = lane < n ? lg[(size_t)(t0 + lane) * nv + h] : 0.f;
+    float x = lgv;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(0xffffffffu, x, o);
@@ -237,44 +253,58 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
     sG[lane] = x;
     sE[lane] = lane < n ? expf(x) : 0.f;
     sL[lane] = lane < n ? expf(gl - x) : 0.f;
-    sB[lane] = lane < n ? beta[(size_t)(t0 + lane) * nv + h] : 0.f;
+    sB[lane] = btv;
   }
   __syncthreads();
   float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
-  // K K^T and Q K^T (32 x 32, K = 128) on tensor cores, 3xTF32 (operands split
-  // on the fly); warp w: rows 16(w>>2).., columns 8(w&3)..
-  {
-    const int mt = warp >> 2, nt = warp & 3, g = lane >> 2, t = lane & 3;
-    float ck[4] = {0.f, 0.f, 0.f, 0.f}, cq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
+  // Warps 0-3: K K^T and Q K^T (32 x 32, K = 128) on tensor cores, 3xTF32
+  // (operands split on the fly); warp w: product w >> 1 (K, then Q rows as
+  // A), rows 16 (w & 1).. against all four 8-column tiles, so each A fragment
+  // is split once per k-step. Warps 4-7 meanwhile write the e^G q and
+  // e^(G_last - G) k operand images.
+  if (warp < 4) {
+    const int pr = warp >> 1, mt = warp & 1, g = lane >> 2, t = lane & 3;
+    const float* sa = pr ? sq : sk;
+    float cc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) cc[nt][e2] = 0.f;
+#pragma unroll 2
     for (int ks = 0; ks < kDhd / 8; ++ks) {
-      uint32_t bh[2], bl[2], kh4[4], kl4[4], qh4[4], ql4[4];
-      const float* kb = sk + (8 * nt + g) * 132 + 8 * ks + t;  // B[k=d][n=s] = k_s[d]
-      split_tf32(kb[0], bh[0], bl[0]);
-      split_tf32(kb[4], bh[1], bl[1]);
+      uint32_t ah[4], al[4];
       const int o0 = (16 * mt + g) * 132 + 8 * ks + t, o1 = o0 + 8 * 132;
-      split_tf32(sk[o0], kh4[0], kl4[0]);
-      split_tf32(sk[o1], kh4[1], kl4[1]);
-      split_tf32(sk[o0 + 4], kh4[2], kl4[2]);
-      split_tf32(sk[o1 + 4], kh4[3], kl4[3]);
-      split_tf32(sq[o0], qh4[0], ql4[0]);
-      split_tf32(sq[o1], qh4[1], ql4[1]);
-      split_tf32(sq[o0 + 4], qh4[2], ql4[2]);
-      split_tf32(sq[o1 + 4], qh4[3], ql4[3]);
-      mma_tf32(ck, kl4, bh);
-      mma_tf32(ck, kh4, bl);
-      mma_tf32(ck, kh4, bh);
-      mma_tf32(cq, ql4, bh);
-      mma_tf32(cq, qh4, bl);
-      mma_tf32(cq, qh4, bh);
+      split_tf32(sa[o0], ah[0], al[0]);
+      split_tf32(sa[o1], ah[1], al[1]);
+      split_tf32(sa[o0 + 4], ah[2], al[2]);
+      split_tf32(sa[o1 + 4], ah[3], al[3]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        uint32_t bh[2], bl[2];
+        const float* kb = sk + (8 * nt + g) * 132 + 8 * ks + t;  // B[k=d][n=s] = k_s[d]
+        split_tf32(kb[0], bh[0], bl[0]);
+        split_tf32(kb[4], bh[1], bl[1]);
+        mma_tf32(cc[nt], al, bh);
+        mma_tf32(cc[nt], ah, bl);
+        mma_tf32(cc[nt], ah, bh);
+      }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = 16 * mt + g + (e >> 1) * 8, s2 = 8 * nt + 2 * t + (e & 1);
-      const bool lower = s2 <= r && r < n;
-      const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
-      sA[r * 36 + s2] = s2 < r && r < n ? sB[r] * dec * ck[e] : 0.f;
-      blk[kBlkP + sw128_f(r, s2)] = dec * cq[e];
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        const int r = 16 * mt + g + (e2 >> 1) * 8, s2 = 8 * nt + 2 * t + (e2 & 1);
+        const bool lower = s2 <= r && r < n;
+        const float dec = lower ? expf(sG[r] - sG[s2]) : 0.f;
+        if (pr == 0) sA[r * 36 + s2] = s2 < r && r < n ? sB[r] * dec * cc[nt][e2] : 0.f;
+        else blk[kBlkP + sw128_f(r, s2)] = dec * cc[nt][e2];
+      }
+  } else {
+    for (int i = tid - 128; i < kCk * kDhd; i += 128) {
+      const int r = i >> 7, d = i & 127;
+      blk[blk_b1(kCk + r, d)] = sE[r] * sq[r * 132 + d];
+      const int dk = i >> 5, rk = i & 31;  // Kt[dk][rk]
+      blk[kBlkKt + sw128_f(dk, rk)] = sL[rk] * sk[rk * 132 + dk];
     }
   }
   __syncthreads();
@@ -302,12 +332,6 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
 #pragma unroll
       for (int r = 0; r < kCk; ++r) blk[kBlkU + r * kDhd + j - kDhd] = x[r];
     }
-  }
-  for (int i = tid; i < kCk * kDhd; i += blockDim.x) {
-    const int r = i >> 7, d = i & 127;
-    blk[blk_b1(kCk + r, d)] = sE[r] * sq[r * 132 + d];
-    const int dk = i >> 5, rk = i & 31;  // Kt[dk][rk]
-    blk[kBlkKt + sw128_f(dk, rk)] = sL[rk] * sk[rk * 132 + dk];
   }
   if (tid == 0) gcs[(size_t)c * nv + h] = expf(sG[n - 1]);
   pdl_launch_dependents();
