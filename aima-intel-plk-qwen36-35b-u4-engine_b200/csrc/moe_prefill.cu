@@ -793,11 +793,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // ---------------------------------------------------------------------------
 // Router logits over T prompt tokens on tcgen05: logits[t, e] = xn[t] . W[e]
 // (fp16 operands, fp32 accumulation in the tensor core), slogit[t] = xn[t] .
-// w_sg. One CTA per 128-token tile: warp 0 streams 64-wide K blocks of xn
-// (128 rows), W (256 rows; rows past E read as zeros) and the shared-gate row
-// (a 16-row box, rows past the first read as zeros) into a 4-stage ring;
-// warp 1 issues M128 x N256 and M128 x N16 MMAs into TMEM columns [0, 256)
-// and [256, 272); warps 2-5 (thread = token = TMEM lane) store the rows.
+// w_sg. One CTA per 128-token tile and nc-column slice of the experts (nc =
+// 256, or 128 with two CTAs per tile when the tiles alone would fill fewer
+// than half the SMs): warp 0 streams 64-wide K blocks of xn (128 rows), the
+// slice of W (nc rows; rows past E read as zeros) and, in the first slice,
+// the shared-gate row (a 16-row box, rows past the first read as zeros) into
+// a 4-stage ring; warp 1 issues M128 x Nnc and M128 x N16 MMAs into TMEM
+// columns [0, nc) and [256, 272); warps 2-5 (thread = token = TMEM lane)
+// store the rows.
 // The logits equal the decode router's up to fp32 summation order (the
 // reference's own router check: max-abs <= 1e-4).
 constexpr int kRtM = 128, kRtN = 256, kRtNs = 16, kRtBK = 64, kRtStages = 4;
@@ -805,13 +808,12 @@ constexpr int kRtA = kRtM * 128, kRtB = kRtN * 128, kRtBs = kRtNs * 128;
 constexpr int kRtStage = kRtA + kRtB + kRtBs;  // 51200 B, every piece 1024-aligned
 constexpr int kRtOffBar = kRtStages * kRtStage;
 constexpr int kRtSmem = kRtOffBar + 256 + 1024;
-constexpr uint32_t kRtIdesc = (1u << 4) | ((uint32_t)(kRtN >> 3) << 17) | ((uint32_t)(kRtM >> 4) << 24);
 constexpr uint32_t kRtIdescS = (1u << 4) | ((uint32_t)(kRtNs >> 3) << 17) | ((uint32_t)(kRtM >> 4) << 24);
 
 __global__ void __launch_bounds__(192, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmS, int has_sg, int T, int H, int E,
-                     float* logits, float* slogit) {
+                     int nc, float* logits, float* slogit) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
@@ -820,8 +822,10 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t bar_full = bar, bar_empty = bar + 8 * kRtStages, bar_done = bar + 16 * kRtStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kRtOffBar + 192);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kRtM;
+  const int m0 = blockIdx.x * kRtM, n0 = blockIdx.y * nc;
   const int nk = H / kRtBK;
+  const bool sg = has_sg && blockIdx.y == 0;  // the first slice also computes the shared gate
+  const uint32_t idesc = (1u << 4) | ((uint32_t)(nc >> 3) << 17) | ((uint32_t)(kRtM >> 4) << 24);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
@@ -842,7 +846,7 @@ __global__ void __launch_bounds__(192, 1)
   bool ok = true;
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t tx = kRtA + kRtB + (has_sg ? kRtBs : 0);
+      const uint32_t tx = kRtA + (uint32_t)nc * 128u + (sg ? kRtBs : 0);
       for (int kb = 0; kb < nk && ok; ++kb) {
         const int s = kb % kRtStages;
         ok = mbar_wait(bar_empty + 8 * s, ((kb / kRtStages) & 1) ^ 1u);
@@ -850,8 +854,8 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t st = base + s * kRtStage;
         mbar_arrive_tx(bar_full + 8 * s, tx);
         tma_load_2d(st, &tmX, kb * kRtBK, m0, bar_full + 8 * s);
-        tma_load_2d(st + kRtA, &tmW, kb * kRtBK, 0, bar_full + 8 * s);
-        if (has_sg) tma_load_2d(st + kRtA + kRtB, &tmS, kb * kRtBK, 0, bar_full + 8 * s);
+        tma_load_2d(st + kRtA, &tmW, kb * kRtBK, n0, bar_full + 8 * s);
+        if (sg) tma_load_2d(st + kRtA + kRtB, &tmS, kb * kRtBK, 0, bar_full + 8 * s);
       }
     }
   } else if (warp == 1) {
@@ -865,8 +869,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int kk = 0; kk < kRtBK / 16; ++kk) {
           const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-          umma_f16(tmem, sw128_desc(st + kk * 32), sw128_desc(st + kRtA + kk * 32), kRtIdesc, acc);
-          if (has_sg)
+          umma_f16(tmem, sw128_desc(st + kk * 32), sw128_desc(st + kRtA + kk * 32), idesc, acc);
+          if (sg)
             umma_f16(tmem + kRtN, sw128_desc(st + kk * 32), sw128_desc(st + kRtA + kRtB + kk * 32),
                      kRtIdescS, acc);
         }
@@ -882,24 +886,25 @@ __global__ void __launch_bounds__(192, 1)
     ok = mbar_wait(bar_done, 0);
     if (ok) {
       tc_fence_after();
-      for (int c = 0; c < (E + 15) / 16; ++c) {
+      const int ncol = min(nc, E - n0);  // this slice's expert columns
+      for (int c = 0; c < (ncol + 15) / 16; ++c) {
         uint32_t v[16];
         tmem_ld16(tmem + lane_off + c * 16, v);
         tmem_ld_wait();
         if (t < T) {
-          float* dst = logits + (size_t)t * E + c * 16;
-          if ((E & 3) == 0 && c * 16 + 16 <= E) {
+          float* dst = logits + (size_t)t * E + n0 + c * 16;
+          if ((E & 3) == 0 && c * 16 + 16 <= ncol) {
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               reinterpret_cast<float4*>(dst)[q] =
                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
           } else {
-            for (int j = 0; j < 16 && c * 16 + j < E; ++j) dst[j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 16 && c * 16 + j < ncol; ++j) dst[j] = __uint_as_float(v[j]);
           }
         }
       }
-      if (has_sg) {
+      if (sg) {
         uint32_t v[16];
         tmem_ld16(tmem + lane_off + kRtN, v);
         tmem_ld_wait();
@@ -1002,9 +1007,15 @@ int router_tc_launch(const __half* xn, int T, int H, const void* w_router, int E
   if (!aligned(xn, 16) || !aligned(w_router, 16) || (w_sg && !aligned(w_sg, 16)) ||
       !aligned(logits, 16))
     return IQ36_ERR_ALIGN;
+  int sms = 148, dev0 = 0;
+  if (cudaGetDevice(&dev0) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev0) != cudaSuccess)
+    return IQ36_ERR_CUDA;
+  const int mtiles = (T + kRtM - 1) / kRtM;
+  const int nsplit = (E > kRtN / 2 && 2 * mtiles <= sms) ? 2 : 1, nc = kRtN / nsplit;
   CUtensorMap mx, mw, ms;
   if (!make_f16_map(&mx, xn, (uint64_t)T, (uint64_t)H, kRtM) ||
-      !make_f16_map(&mw, w_router, (uint64_t)E, (uint64_t)H, kRtN) ||
+      !make_f16_map(&mw, w_router, (uint64_t)E, (uint64_t)H, (uint32_t)nc) ||
       !make_f16_map(&ms, w_sg ? w_sg : w_router, 1, (uint64_t)H, kRtNs))
     return IQ36_ERR_CUDA;
   static std::atomic<bool> attr_set[64];
@@ -1016,9 +1027,9 @@ int router_tc_launch(const __half* xn, int T, int H, const void* w_router, int E
       return IQ36_ERR_CUDA;
     attr_set[dev].store(true);
   }
-  const cudaError_t e = launch(router_tc_kernel, dim3((T + kRtM - 1) / kRtM), dim3(192),
-                               (size_t)kRtSmem, stream, mx, mw, ms, w_sg ? 1 : 0, T, H, E, logits,
-                               slogit);
+  const cudaError_t e = launch(router_tc_kernel, dim3(mtiles, nsplit), dim3(192),
+                               (size_t)kRtSmem, stream, mx, mw, ms, w_sg ? 1 : 0, T, H, E, nc,
+                               logits, slogit);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
 
