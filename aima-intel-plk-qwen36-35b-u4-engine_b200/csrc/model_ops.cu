@@ -77,8 +77,9 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
     rope_s[i] = (float)sn;
   }
   pdl_wait();
-  __syncthreads();
-  if (warp >= n_q + n_kv) return;
+  // Each warp loads and RMS-normalises its row before the barrier that
+  // publishes the angles, so the fp64 angle latency overlaps the loads.
+  const bool active = warp < n_q + n_kv;  // warp-uniform
   q_full += (size_t)blockIdx.x * 2 * n_q * D;
   k += (size_t)blockIdx.x * n_kv * D;
   v += (size_t)blockIdx.x * n_kv * D;
@@ -88,20 +89,22 @@ __global__ void attn_prep_kernel(const __half* q_full, const __half* k, const __
   const int h = is_q ? warp : warp - n_q;
   const __half* src = is_q ? q_full + (size_t)(2 * h) * D : k + (size_t)h * D;
   const float* nw = is_q ? qn_w : kn_w;
-  float x[8];
-  {
+  float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (active) {
     const uint4 raw = *reinterpret_cast<const uint4*>(src + 8 * lane);
     const __half* hp = reinterpret_cast<const __half*>(&raw);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = __half2float(hp[j]);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(x[j], x[j], ss);
+    ss = warp_sum(ss);
+    const float sc = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = x[j] * sc * nw[8 * lane + j];
   }
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) ss = fmaf(x[j], x[j], ss);
-  ss = warp_sum(ss);
-  const float sc = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = x[j] * sc * nw[8 * lane + j];
+  __syncthreads();  // rope_c / rope_s written
+  if (!active) return;
   const int xo = half / 8;  // partner lane offset
   float y[8];
 #pragma unroll
