@@ -714,26 +714,40 @@ __global__ void __launch_bounds__(256) delta_gated_norm_kernel(const float* o, c
                                                                const float* norm_w, float eps,
                                                                int rows, __half* out) {
   pdl_wait();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row < rows) {
-    const float4 v = *reinterpret_cast<const float4*>(o + (size_t)row * kDhd + 4 * lane);
+  // Each warp normalises kRows rows (one 128-wide head row of one token
+  // each); the rows' loads are all issued before the first is used.
+  constexpr int kRows = 4;
+  const int row0 = (blockIdx.x * 8 + (threadIdx.x >> 5)) * kRows, lane = threadIdx.x & 31;
+  float4 ov4[kRows];
+  uint2 zr[kRows];
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    if (row0 + i < rows) {
+      ov4[i] = *reinterpret_cast<const float4*>(o + (size_t)(row0 + i) * kDhd + 4 * lane);
+      zr[i] = *reinterpret_cast<const uint2*>(z + (size_t)(row0 + i) * kDhd + 4 * lane);
+    }
+  }
+  const float nwv[4] = {norm_w[4 * lane], norm_w[4 * lane + 1], norm_w[4 * lane + 2],
+                        norm_w[4 * lane + 3]};
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    if (row0 + i >= rows) break;  // warp-uniform
+    const float4 v = ov4[i];
     const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
     const float nsc = rsqrtf(ss / (float)kDhd + eps);
-    const uint2 zr = *reinterpret_cast<const uint2*>(z + (size_t)row * kDhd + 4 * lane);
-    const __half2 zlo = *reinterpret_cast<const __half2*>(&zr.x);
-    const __half2 zhi = *reinterpret_cast<const __half2*>(&zr.y);
+    const __half2 zlo = *reinterpret_cast<const __half2*>(&zr[i].x);
+    const __half2 zhi = *reinterpret_cast<const __half2*>(&zr[i].y);
     const float zv[4] = {__low2float(zlo), __high2float(zlo), __low2float(zhi), __high2float(zhi)};
-    const float ov[4] = {v.x, v.y, v.z, v.w};
+    const float ovv[4] = {v.x, v.y, v.z, v.w};
     float y[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      y[i] = ov[i] * nsc * norm_w[4 * lane + i] * (zv[i] * sigmoidf_acc(zv[i]));
+    for (int j = 0; j < 4; ++j) y[j] = ovv[j] * nsc * nwv[j] * (zv[j] * sigmoidf_acc(zv[j]));
     const __half2 lo = __floats2half2_rn(y[0], y[1]);
     const __half2 hi = __floats2half2_rn(y[2], y[3]);
     uint2 raw;
     raw.x = *reinterpret_cast<const uint32_t*>(&lo);
     raw.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(out + (size_t)row * kDhd + 4 * lane) = raw;
+    *reinterpret_cast<uint2*>(out + (size_t)(row0 + i) * kDhd + 4 * lane) = raw;
   }
   pdl_launch_dependents();
 }
@@ -826,7 +840,7 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
     e = launch(delta_chunk_scan_kernel, dim3(nv), dim3(kScThreads), (size_t)kScanSmem, s,
                (const float*)blocks, (const float*)gcs, state, o, T, nv);
   if (e == cudaSuccess)
-    e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 8)), dim3(256), 0, s,
+    e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 32)), dim3(256), 0, s,
                (const float*)o, reinterpret_cast<const __half*>(z_f16), norm_w, eps, T * nv,
                reinterpret_cast<__half*>(out_f16));
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
