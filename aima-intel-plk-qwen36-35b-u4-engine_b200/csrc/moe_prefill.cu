@@ -337,6 +337,10 @@ struct GemmArgs {
   int g64;
   // MODE 2/3: 128-row tiles per unit (1 or 2); the grouped modes use 1.
   int mt;
+  // MODE 2/3 with mt = 2: the rows from row1 on run as n1 one-tile M rows,
+  // ahead of the two-tile rows [0, row1) in the unit order (n1 = 0, row1 = T
+  // when every row is in two-tile units).
+  int n1, row1;
 };
 
 // projection of a MODE-2 N tile and the tile's index inside it
@@ -351,15 +355,21 @@ __device__ __forceinline__ void pf_proj(const GemmArgs& g, int nt, int& p, int& 
 template <int MODE>
 __device__ __forceinline__ int pf_units(const GemmArgs& g) {
   const int um = kPfBM * g.mt;  // rows per unit
-  if (MODE == 2) return (g.T + um - 1) / um * (g.H / kPfBN);
-  if (MODE == 3) return (g.T + um - 1) / um * (g.I / 128);
+  const int mrows = g.n1 + (g.row1 + um - 1) / um;
+  if (MODE == 2) return mrows * (g.H / kPfBN);
+  if (MODE == 3) return mrows * (g.I / 128);
   return *g.work.tile_count * (MODE == 0 ? g.I / 128 : g.H / kPfBN);
 }
 template <int MODE>
 __device__ __forceinline__ void pf_rows(const GemmArgs& g, int mt, int& row0, int& rows) {
   if (MODE >= 2) {
-    row0 = mt * kPfBM * g.mt;
-    rows = min(kPfBM * g.mt, g.T - row0);
+    if (mt < g.n1) {  // one-tile rows at the end of the prompt, scheduled first
+      row0 = g.row1 + mt * kPfBM;
+      rows = min(kPfBM, g.T - row0);
+    } else {
+      row0 = (mt - g.n1) * kPfBM * g.mt;
+      rows = min(kPfBM * g.mt, g.row1 - row0);
+    }
   } else {
     row0 = g.work.tile_row0[mt];
     rows = g.work.tile_rows[mt];
@@ -1139,6 +1149,8 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
               H, I, H, w};
   g1.g64 = b->group == 64;
   g1.mt = 1;
+  g1.n1 = 0;
+  g1.row1 = 0;
   // persistent grids: at most one CTA per SM, never more than the units
   int sms = 148;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -1151,6 +1163,8 @@ int moe_prefill_launch(const void* x, int x_dtype, int T, const int32_t* ids,
   GemmArgs g2{reinterpret_cast<const __half*>(b->down_scale), b->down_zp, (int64_t)H, I, I, H, w};
   g2.g64 = b->group == 64;
   g2.mt = 1;
+  g2.n1 = 0;
+  g2.row1 = 0;
   if (e == cudaSuccess)
     e = launch(pf_gemm_kernel<1>, dim3(grid2), dim3(kPfThreads), (size_t)kPfSmem, stream,
                map_act, map_d, map_d, map_d, map_d, g2);
@@ -1295,18 +1309,51 @@ int u4_gemm_multi_launch(const void* x, int x_dtype, const float* nw, float eps,
     g.pacc[p] = have ? proj[p].accumulate : 0;
     g.tile_base[p + 1] = g.tile_base[p] + (have ? proj[p].m.rows / kPfBN : 0);
   }
-  // One or two 128-row tiles per unit: the one with fewer rounds of the
-  // persistent grid, a two-tile unit costing ~1.35 one-tile units (measured:
-  // +26% mainloop time for the second tile's MMAs, plus its epilogue, which
-  // does not overlap the next unit). The SwiGLU mode keeps one tile: its
-  // epilogue (an exp and a divide per output) is too long to expose.
+  // Unit shapes by a simulated makespan of the round-robin schedule: all
+  // one-tile units, or two-tile units (a two-tile unit costs ~1.43 one-tile
+  // units, measured: its second tile's MMAs plus an epilogue that cannot
+  // overlap the next unit) with the last k pairs of rows run as one-tile units
+  // first, which evens the CTAs' loads and offsets their write-bound
+  // epilogues. The SwiGLU mode keeps one tile (two measured no faster).
   const int nt_units = total_rows / kPfBN;
-  auto rounds = [&](int mt) {
-    const int u = (T + kPfBM * mt - 1) / (kPfBM * mt) * nt_units;
-    return (double)((u + sms - 1) / sms) * (mt == 2 ? 1.35 : 1.0);
+  const int pairs = (T + 2 * kPfBM - 1) / (2 * kPfBM);
+  auto makespan = [&](int mt, int k, int& n1, int& row1) {
+    n1 = 0;
+    row1 = T;
+    if (mt == 2 && k > 0) {
+      row1 = (pairs - k) * 2 * kPfBM;
+      n1 = (T - row1 + kPfBM - 1) / kPfBM;
+    }
+    const int um = kPfBM * mt;
+    const int mrows = n1 + (row1 + um - 1) / um;
+    const int units = mrows * nt_units, grid = std::max(1, std::min(sms, units));
+    double worst = 0.0;
+    for (int b = 0; b < grid; ++b) {
+      double load = 0.0;
+      for (int u = b; u < units; u += grid) {
+        const int r = u / nt_units;
+        const int rows = r < n1 ? kPfBM : std::min(um, row1 - (r - n1) * um);
+        load += rows > kPfBM ? 1.43 : 1.0;
+      }
+      worst = std::max(worst, load);
+    }
+    return worst;
   };
-  g.mt = !swiglu && rounds(2) < rounds(1) ? 2 : 1;
-  const int units = (T + kPfBM * g.mt - 1) / (kPfBM * g.mt) * nt_units;
+  int n1 = 0, row1 = T;
+  double best = makespan(1, 0, n1, row1);
+  g.mt = 1;
+  g.n1 = 0;
+  g.row1 = T;
+  for (int k = 0; !swiglu && k < pairs; ++k) {
+    const double m = makespan(2, k, n1, row1);
+    if (m < best - 1e-9) {
+      best = m;
+      g.mt = 2;
+      g.n1 = n1;
+      g.row1 = row1;
+    }
+  }
+  const int units = (g.n1 + (g.row1 + kPfBM * g.mt - 1) / (kPfBM * g.mt)) * nt_units;
   if (e == cudaSuccess)
     e = launch(swiglu ? pf_gemm_kernel<3> : pf_gemm_kernel<2>,
                dim3(std::max(1, std::min(sms, units))), dim3(kPfThreads), (size_t)kPfSmem, stream,
