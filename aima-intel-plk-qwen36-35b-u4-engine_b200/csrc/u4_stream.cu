@@ -167,7 +167,10 @@ __device__ __forceinline__ ChunkSrc proj_chunk(const StreamProj& ps, const int* 
   return c;
 }
 
-template <int G>
+// kList: chunk-list mode, compiled as its own instantiation so that the
+// list handling adds no registers to the decode projections (sharing one
+// instantiation spilled and cost ~0.7 us per launch).
+template <int G, bool kList>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     u4_stream_proj_kernel(StreamProj ps, const __half* x16, const float* x32, const float* nw,
                           float eps, int K, int* err) {
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int total = ps.chunk_start[ps.n_proj];
   const int* list = nullptr;
-  if (ps.chunk_list != nullptr) {
+  if constexpr (kList) {
     pdl_wait();
     const int n = *ps.chunk_count;
     if (n <= ps.chunk_capacity) {
@@ -292,8 +295,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
 // The dynamic shared-memory opt-in is a per-device function attribute: set it
 // once per device to the largest layout any K (<= 4096) needs.
-static int stream_attr(const void* fn) {
-  static std::atomic<bool> attr_set[64];
+template <bool kList>
+static int stream_attr() {
+  const void* fn = (const void*)u4_stream_proj_kernel<128, kList>;
+  static std::atomic<bool> attr_set[64];  // per instantiation
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return IQ36_ERR_CUDA;
   if (attr_set[dev].load(std::memory_order_acquire)) return IQ36_OK;
@@ -336,10 +341,10 @@ int stream_proj_launch(const void* x_f16, const float* x_f32, const float* nw, f
   const StreamGeom geo = stream_geom(K, G);
   const StreamSmem L = stream_smem(geo, K, G);
   const int grid = std::min(kStreamCtas, ch);
-  if (stream_attr((const void*)u4_stream_proj_kernel<128>) != IQ36_OK)
+  if (stream_attr<false>() != IQ36_OK)
     return IQ36_ERR_CUDA;
   const cudaError_t e =
-      launch(u4_stream_proj_kernel<128>, dim3(grid), dim3(kStreamThreads), (size_t)L.total, stream,
+      launch(u4_stream_proj_kernel<128, false>, dim3(grid), dim3(kStreamThreads), (size_t)L.total, stream,
              ps, reinterpret_cast<const __half*>(x_f16), x_f32, nw, eps, K, (int*)nullptr);
   return e == cudaSuccess ? IQ36_OK : IQ36_ERR_CUDA;
 }
@@ -718,8 +723,8 @@ extern "C" int iq36_lm_head_top1_certified(const void* x_f16, const float* x_f32
   ps.chunk_capacity = capacity_chunks;
   const StreamGeom geo = stream_geom(K, G);
   const StreamSmem L = stream_smem(geo, K, G);
-  if (stream_attr((const void*)u4_stream_proj_kernel<128>) != IQ36_OK) return IQ36_ERR_CUDA;
-  e = launch(u4_stream_proj_kernel<128>, dim3(std::min(kStreamCtas, nchunks)),
+  if (stream_attr<true>() != IQ36_OK) return IQ36_ERR_CUDA;
+  e = launch(u4_stream_proj_kernel<128, true>, dim3(std::min(kStreamCtas, nchunks)),
              dim3(kStreamThreads), (size_t)L.total, s, ps,
              reinterpret_cast<const __half*>(x_f16), x_f32, norm_weight, norm_eps, K,
              (int*)nullptr);
