@@ -194,8 +194,12 @@ __device__ __forceinline__ void router_topk_warp(const float* l, int E, int k, u
   }
   // top_k_indices (:3672-3697): descending probability, lower id on ties —
   // the larger 64-bit key (prob bits, inverted id) wins.
+  // ranks unrolled to the maximum k (16) and predicated, so that sel_id /
+  // sel_w stay in registers (a runtime-bounded loop put them in local memory)
   float sum = 0.0f;
-  for (int r = 0; r < k; ++r) {
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    if (r >= k) break;  // warp-uniform
     uint64_t best = 0ull;
 #pragma unroll
     for (int i = 0; i < 8; ++i) best = key[i] > best ? key[i] : best;
@@ -213,7 +217,9 @@ __device__ __forceinline__ void router_topk_warp(const float* l, int E, int k, u
   }
   // normalize_weights (:3712-3731), min sum 6.103515625e-5 (:5665).
   const float den = fmaxf(sum, 6.103515625e-5f);
-  for (int r = 0; r < k; ++r) sel_w[r] = __fdiv_rn(sel_w[r], den);
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+    if (r < k) sel_w[r] = __fdiv_rn(sel_w[r], den);
 }
 
 // Warp per token. E <= 256, k <= 16.
@@ -230,9 +236,12 @@ __global__ void __launch_bounds__(256) router_select_kernel(const float* logits,
   float sel_w[16];
   router_topk_warp(logits + (size_t)tok * E, E, k, sel_id, sel_w);
   if (lane == 0) {
-    for (int r = 0; r < k; ++r) {
-      ids[(size_t)tok * k + r] = (int32_t)sel_id[r];
-      weights[(size_t)tok * k + r] = sel_w[r];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      if (r < k) {
+        ids[(size_t)tok * k + r] = (int32_t)sel_id[r];
+        weights[(size_t)tok * k + r] = sel_w[r];
+      }
     }
   }
 }

@@ -911,7 +911,9 @@ __global__ void __launch_bounds__(192, 1)
                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
           } else {
-            for (int j = 0; j < 16 && c * 16 + j < ncol; ++j) dst[j] = __uint_as_float(v[j]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c * 16 + j < ncol) dst[j] = __uint_as_float(v[j]);
           }
         }
       }
