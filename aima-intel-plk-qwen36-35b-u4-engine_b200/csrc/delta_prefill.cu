@@ -2,7 +2,8 @@
 //
 // The per-token decode path (delta_prep_kernel + delta_step_kernel) runs the
 // causal conv and the recurrence for one token per launch. Prefill runs the
-// same arithmetic over a whole prompt in five launches per layer:
+// same arithmetic over a whole prompt in five launches per layer (six when the
+// chunk scan is split):
 //   1. delta_conv_batch_kernel: causal depthwise conv(4) + SiLU for every
 //      (token, channel) — the conv is a 4-tap FIR over the previous three
 //      inputs (or the carried state before token 0) — then the per-head L2
@@ -17,7 +18,9 @@
 //   4. delta_chunk_scan_kernel: the only sequential part, over chunks: per
 //      chunk Delta = U - W S, O = (e^G q) S + P Delta, S = e^G_last S + K~^T Delta,
 //      as 3xTF32 tensor-core products (fp32-accurate: hi/lo split of every
-//      operand), the state held in registers.
+//      operand), the state held in TMEM. From 16 chunks on, the prompt is cut
+//      in two segments scanned at the same time, and delta_scan_join_kernel
+//      applies the state at the cut to the second one.
 //   5. delta_gated_norm_kernel: gated RMSNorm of every (token, value head).
 //
 // Semantics (same as the decode path): OpenVINO gated delta net
@@ -359,6 +362,30 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
 // g takes tokens 16 g .. 16 g + 15 of Delta and keys 32 q + 16 g .. + 15 of each
 // key quarter q). TMEM columns: 0 S^T accumulator, 128 the A copy of S^T, 256
 // its lo part, 384 and 448 X of even and odd chunks.
+//
+// Segments. Per chunk the update is affine in the incoming state:
+// S^T' = S^T (gC I - W^T Kt^T) + U^T Kt^T and O^T = S^T (Qg^T - W^T P^T) + U^T P^T.
+// So a long prompt is cut at chunk m into two segments scanned at the same time
+// (grid.y): segment 0 from the real state; segment 1 twice, from a zero state
+// (outputs O_R, final state R) and as the transition scan (start I, U = 0:
+// outputs O_M, final state M). With Z the state at chunk m, the real outputs
+// of segment 1 are O_R + Z O_M and its final state Z M + R
+// (delta_scan_join_kernel), which halves the sequential chain.
+struct ScanSeg {
+  const float* s_in;  // incoming state per head [128 keys][128 values] (start 0)
+  float* s_out;       // final state, same layout
+  float* o;           // outputs: row (t - t_off) of [rows, nv, 128]
+  int c0, c1;         // chunks [c0, c1)
+  int t_off;
+  int start;          // 0: s_in, 1: zero state, 2: identity state and U = 0
+};
+struct ScanSegs {
+  ScanSeg s[3];
+};
+constexpr int kScSplitMin = 16;  // chunks: shorter prompts run one segment
+__host__ __device__ constexpr int scan_split(int T) {
+  return (T + kCk - 1) / kCk >= kScSplitMin ? ((T + kCk - 1) / kCk + 1) / 2 : 0;
+}
 constexpr int kScThreads = 448;
 constexpr int kScEpiWarps = 8;
 constexpr uint32_t kScB1Raw = 0, kScB1Lo = 65536, kScKtRaw = 131072, kScKtLo = 147456,
@@ -418,7 +445,7 @@ __device__ __forceinline__ void split_copy(const float* src, float* raw, float* 
 
 __global__ void __launch_bounds__(kScThreads, 1)
     delta_chunk_scan_kernel(const float* __restrict__ blocks, const float* __restrict__ gcs,
-                            float* __restrict__ state, float* __restrict__ o_out, int T, int nv) {
+                            const ScanSegs segs, int T, int nv) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_raw = smem_u32(smem_raw);
   const uint32_t base = (base_raw + 1023u) & ~1023u;
@@ -432,7 +459,9 @@ __global__ void __launch_bounds__(kScThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kScBar + 192);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
-  const int nchunks = (T + kCk - 1) / kCk;
+  const ScanSeg sg = blockIdx.y == 0 ? segs.s[0] : (blockIdx.y == 1 ? segs.s[1] : segs.s[2]);
+  const int c0 = sg.c0;
+  const int nchunks = sg.c1 - sg.c0;  // local chunk c is chunk c0 + c
   if (threadIdx.x == 0) {
     // commits and the loader count 1; thread groups arrive once per warp
     for (int b = 0; b < 2; ++b) {
@@ -466,7 +495,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
     // ---- loader: B1 images (double-buffered) and the raw Kt / P staging ----
     if (lane == 0) {
       for (int c = 0; c < nchunks && ok; ++c) {
-        const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+        const float* blk = blocks + ((size_t)(c0 + c) * nv + h) * kCkBlk;
         const int b = c & 1;
         ok = mbar_wait(b1_empty + 8 * b, ((c >> 1) & 1) ^ 1u);
         if (!ok) break;
@@ -547,13 +576,14 @@ __global__ void __launch_bounds__(kScThreads, 1)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float* stg = reinterpret_cast<const float*>(smem + kScStg);
     auto store_o = [&](int cc) {
-      const int t0 = cc * kCk, n = min(kCk, T - t0);
+      const int t0 = (c0 + cc) * kCk, n = min(kCk, T - t0);
+      float* orow = sg.o + ((size_t)(t0 - sg.t_off) * nv + h) * kDhd + v;
       uint32_t oa[32];
       tmem_ld32(tmem + kTmX + 64u * (uint32_t)(cc & 1) + lane_off + 32, oa);
       tmem_ld_wait();
 #pragma unroll
       for (int tt = 0; tt < kCk; ++tt)
-        if (tt < n) o_out[((size_t)(t0 + tt) * nv + h) * kDhd + v] = __uint_as_float(oa[tt]);
+        if (tt < n) orow[(size_t)tt * nv * kDhd] = __uint_as_float(oa[tt]);
     };
     for (int c = 0; c < nchunks && ok; ++c) {
       const int b = c & 1;
@@ -598,7 +628,8 @@ __global__ void __launch_bounds__(kScThreads, 1)
                    tlo = tmem + kTmLo + lane_off + kofs;
     float* sdh = reinterpret_cast<float*>(smem + kScDHi);
     float* sdl = reinterpret_cast<float*>(smem + kScDLo);
-    float* sth = state + (size_t)h * kDhd * kDhd;
+    const float* sin = sg.start == 0 ? sg.s_in + (size_t)h * kDhd * kDhd : nullptr;
+    float* sth = sg.s_out + (size_t)h * kDhd * kDhd;
     // key quarter q of the state: A copy (x, its lo part) and g x as the
     // accumulator, then the quarter is released to (1)
     auto put_quarter = [&](int q, const uint32_t (&src)[16], float g) {
@@ -619,22 +650,34 @@ __global__ void __launch_bounds__(kScThreads, 1)
       if (lane == 0) mbar_arrive(a_ready + 8 * q);
     };
     {
-      const float g0 = gcs[h];
+      const float g0 = gcs[(size_t)c0 * nv + h];
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
         uint32_t x0[16];
+        const int k0 = (int)kofs + 32 * q;
+        if (sin) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) x0[e] = __float_as_uint(sth[(size_t)(kofs + 32 * q + e) * kDhd + v]);
+          for (int e = 0; e < 16; ++e) x0[e] = __float_as_uint(sin[(size_t)(k0 + e) * kDhd + v]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            x0[e] = __float_as_uint(sg.start == 2 && k0 + e == v ? 1.f : 0.f);
+        }
         put_quarter(q, x0, g0);
       }
     }
     for (int c = 0; c < nchunks && ok; ++c) {
-      const float* blk = blocks + ((size_t)c * nv + h) * kCkBlk;
+      const float* blk = blocks + ((size_t)(c0 + c) * nv + h) * kCkBlk;
       const uint32_t tx = tmem + kTmX + 64u * (uint32_t)(c & 1) + lane_off;
       float u[16];
+      if (sg.start != 2) {
 #pragma unroll
-      for (int tt = 0; tt < 16; ++tt) u[tt] = blk[kBlkU + (tofs + tt) * kDhd + v];
-      const float gnext = c + 1 < nchunks ? gcs[(size_t)(c + 1) * nv + h] : 0.f;
+        for (int tt = 0; tt < 16; ++tt) u[tt] = blk[kBlkU + (tofs + tt) * kDhd + v];
+      } else {
+#pragma unroll
+        for (int tt = 0; tt < 16; ++tt) u[tt] = 0.f;
+      }
+      const float gnext = c + 1 < nchunks ? gcs[(size_t)(c0 + c + 1) * nv + h] : 0.f;
       ok = __all_sync(0xffffffffu, mbar_wait(x_done, c & 1));
       if (!ok) break;
       tc_fence_after();
@@ -698,6 +741,100 @@ __global__ void __launch_bounds__(kScThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// 4b. joins segment 1 of a split scan to segment 0. Per value head, row r of a
+// tile: dst[r][v] = add[r][v] + sum_k' src[r][k'] Z[k'][v], Z = the state at
+// the cut ([128 k'][128 v], segment 0's final state). Token rows: src = O_M,
+// add = dst = the zero-start outputs; state rows (the last two tiles of the
+// grid): src = M, add = R, dst = the real state. fp32 FMAs in k' order.
+// Thread = 4 rows x 8 columns (v = 4j..4j+3 and 64+4j..), Z and the tile's
+// rows in shared memory, placed by bulk copies (rows padded to 132 floats: the
+// two row groups of a warp fall in different banks).
+constexpr int kJnRows = 64, kJnLd = 132;
+constexpr int kJoinBar = (kDhd * kDhd + kJnRows * kJnLd) * 4;
+constexpr int kJoinSmem = kJoinBar + 16;
+__global__ void __launch_bounds__(256) delta_scan_join_kernel(
+    const float* __restrict__ zst, const float* __restrict__ om, float* __restrict__ o,
+    const float* __restrict__ ms, const float* __restrict__ rs, float* __restrict__ state,
+    int T1, int nv) {
+  extern __shared__ float4 jsm4[];
+  float* sz = reinterpret_cast<float*>(jsm4);
+  float* sx = sz + kDhd * kDhd;
+  const uint32_t sbase = smem_u32(jsm4), bar = sbase + kJoinBar;
+  const int h = blockIdx.y, tid = threadIdx.x;
+  const int ntt = (T1 + kJnRows - 1) / kJnRows;
+  const bool tok = (int)blockIdx.x < ntt;
+  const int r0 = (tok ? (int)blockIdx.x : (int)blockIdx.x - ntt) * kJnRows;
+  const int nrows = tok ? min(kJnRows, T1 - r0) : kJnRows;
+  auto row_off = [&](int r) -> size_t {  // float offset of row r in src / add / dst
+    return tok ? ((size_t)(r0 + r) * nv + h) * kDhd : ((size_t)h * kDhd + r0 + r) * kDhd;
+  };
+  const float* src = tok ? om : ms;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  // rows past the end are zero (generic stores; the copies write other rows)
+  for (int i = nrows * 32 + tid; i < kJnRows * 32; i += 256) {
+    const int r = i >> 5, c4 = i & 31;
+    *reinterpret_cast<float4*>(sx + r * kJnLd + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  pdl_wait();  // Z, O_M, M and R come from the scan
+  if (tid < 32) {
+    if (tid == 0) mbar_arrive_tx(bar, (uint32_t)(kDhd * kDhd * 4 + nrows * kDhd * 4));
+    __syncwarp();
+    if (tid < 4)
+      bulk_load(sbase + tid * 16384u, zst + (size_t)h * kDhd * kDhd + tid * 4096, 16384u, bar);
+    for (int r = tid; r < nrows; r += 32)
+      bulk_load(sbase + (uint32_t)(kDhd * kDhd + r * kJnLd) * 4u, src + row_off(r),
+                (uint32_t)kDhd * 4u, bar);
+  }
+  if (!mbar_wait(bar, 0)) {
+    if (tid == 0) atomicAdd(&g_delta_wait_timeouts, 1);
+    return;
+  }
+  const int rg = tid >> 4, vg = tid & 15;
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 2
+  for (int k = 0; k < kDhd; k += 4) {
+    float xa[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 x = *reinterpret_cast<const float4*>(sx + (4 * rg + i) * kJnLd + k);
+      xa[i][0] = x.x, xa[i][1] = x.y, xa[i][2] = x.z, xa[i][3] = x.w;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float4 za = *reinterpret_cast<const float4*>(sz + (k + kk) * kDhd + 4 * vg);
+      const float4 zb = *reinterpret_cast<const float4*>(sz + (k + kk) * kDhd + 64 + 4 * vg);
+      const float zv[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xa[i][kk], zv[j], acc[i][j]);
+    }
+  }
+  float* dst_base = tok ? o : state;
+  const float* add_base = tok ? o : rs;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * rg + i;
+    if (r >= nrows) break;
+    const size_t off = row_off(r);
+    const float4 a = reinterpret_cast<const float4*>(add_base + off)[vg];
+    const float4 b = reinterpret_cast<const float4*>(add_base + off)[16 + vg];
+    reinterpret_cast<float4*>(dst_base + off)[vg] =
+        make_float4(a.x + acc[i][0], a.y + acc[i][1], a.z + acc[i][2], a.w + acc[i][3]);
+    reinterpret_cast<float4*>(dst_base + off)[16 + vg] =
+        make_float4(b.x + acc[i][4], b.y + acc[i][5], b.z + acc[i][6], b.w + acc[i][7]);
+  }
+  pdl_launch_dependents();
+}
+
 int delta_wait_timeouts(int* count, int reset) {
   if (cudaMemcpyFromSymbol(count, g_delta_wait_timeouts, sizeof(int)) != cudaSuccess)
     return IQ36_ERR_CUDA;
@@ -753,9 +890,10 @@ __global__ void __launch_bounds__(256) delta_gated_norm_kernel(const float* o, c
 }
 
 // workspace: qk fp32 [T, 2nk, D] | v fp16 [T, nv*D] | g, beta fp32 [T, nv] | o fp32 [T, nv, D]
-// | chunk operand blocks [ceil(T/32), nv, kCkBlk] fp32
+// | chunk operand blocks [ceil(T/32), nv, kCkBlk] fp32 | gC [ceil(T/32), nv]; a split
+// scan adds the states Z, R, M [nv, D, D] and O_M [T - 32 m, nv, D]
 struct DeltaWs {
-  size_t qk, v, decay, beta, o, blocks, gcs, total;
+  size_t qk, v, decay, beta, o, blocks, gcs, zst, rst, mst, om, total;
 };
 static DeltaWs delta_ws(int T, int nk, int nv) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
@@ -767,7 +905,13 @@ static DeltaWs delta_ws(int T, int nk, int nv) {
   w.o = up(w.beta + (size_t)T * nv * 4);
   w.blocks = up(w.o + (size_t)T * nv * kDhd * 4);
   w.gcs = up(w.blocks + (size_t)((T + kCk - 1) / kCk) * nv * kCkBlk * 4);
-  w.total = up(w.gcs + (size_t)((T + kCk - 1) / kCk) * nv * 4);
+  w.zst = up(w.gcs + (size_t)((T + kCk - 1) / kCk) * nv * 4);
+  const int m = scan_split(T);
+  const size_t st = m ? (size_t)nv * kDhd * kDhd * 4 : 0;
+  w.rst = w.zst + st;
+  w.mst = w.rst + st;
+  w.om = w.mst + st;
+  w.total = up(w.om + (m ? (size_t)(T - m * kCk) * nv * kDhd * 4 : 0));
   return w;
 }
 
@@ -807,6 +951,9 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
     if (cudaFuncSetAttribute(delta_chunk_scan_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem) !=
             cudaSuccess ||
+        cudaFuncSetAttribute(delta_scan_join_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kJoinSmem) !=
+            cudaSuccess ||
         cudaFuncSetAttribute(delta_chunk_prep_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
             cudaSuccess)
@@ -836,9 +983,27 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
     e = launch(delta_chunk_prep_kernel, dim3(ceil_div(T, kCk), nv), dim3(256), (size_t)kPrepSmem,
                s, (const float*)qk, (const __half*)v, (const float*)dec, (const float*)bet, T, nk,
                nv, blocks, gcs);
+  const int nchunks = ceil_div(T, kCk), m = scan_split(T);
+  ScanSegs sgs = {};
+  if (!m) {
+    sgs.s[0] = ScanSeg{state, state, o, 0, nchunks, 0, 0};
+  } else {
+    float* zst = reinterpret_cast<float*>(ws + w.zst);
+    sgs.s[0] = ScanSeg{state, zst, o, 0, m, 0, 0};
+    sgs.s[1] = ScanSeg{nullptr, reinterpret_cast<float*>(ws + w.rst), o, m, nchunks, 0, 1};
+    sgs.s[2] = ScanSeg{nullptr, reinterpret_cast<float*>(ws + w.mst),
+                       reinterpret_cast<float*>(ws + w.om), m, nchunks, m * kCk, 2};
+  }
   if (e == cudaSuccess)
-    e = launch(delta_chunk_scan_kernel, dim3(nv), dim3(kScThreads), (size_t)kScanSmem, s,
-               (const float*)blocks, (const float*)gcs, state, o, T, nv);
+    e = launch(delta_chunk_scan_kernel, dim3(nv, m ? 3 : 1), dim3(kScThreads), (size_t)kScanSmem,
+               s, (const float*)blocks, (const float*)gcs, sgs, T, nv);
+  if (e == cudaSuccess && m) {
+    const int T1 = T - m * kCk;
+    e = launch(delta_scan_join_kernel, dim3(ceil_div(T1, kJnRows) + kDhd / kJnRows, nv),
+               dim3(256), (size_t)kJoinSmem, s, (const float*)(ws + w.zst),
+               (const float*)(ws + w.om), o + (size_t)m * kCk * nv * kDhd,
+               (const float*)(ws + w.mst), (const float*)(ws + w.rst), state, T1, nv);
+  }
   if (e == cudaSuccess)
     e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 32)), dim3(256), 0, s,
                (const float*)o, reinterpret_cast<const __half*>(z_f16), norm_w, eps, T * nv,

@@ -5,8 +5,8 @@ oracle.delta_step, token after token, conv and recurrent state carried), so
 the batched kernels must reproduce the sequential recurrence of the reference's
 linear-attention layer over a whole prompt. Cases: prompts shorter than the
 conv width (state taken from the carried conv state), a ragged last chunk of
-the 32-token staging, the full model head counts, and a non-zero incoming
-state. Tolerance: tests/helpers.py (max rel 2e-3 for the fp16 outputs; 1e-3
+the 32-token staging, the full model head counts, a non-zero incoming state,
+and prompts of 16 chunks and more, whose chunk scan runs as two segments. Tolerance: tests/helpers.py (max rel 2e-3 for the fp16 outputs; 1e-3
 for the fp32 recurrent state after T tokens).
 """
 
@@ -24,14 +24,14 @@ def _t(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-def _case(rng, T, nk, nv, d=128):
+def _case(rng, T, nk, nv, d=128, alog=(-2, 1)):
     c = (2 * nk + nv) * d
     return dict(
         qkv=(rng.standard_normal((T, c)) * 2).astype(np.float16),
         st=rng.standard_normal((c, 4)).astype(np.float16).astype(np.float32),
         cw=rng.uniform(-0.5, 0.5, (c, 4)).astype(np.float32),
         ab=rng.standard_normal((T, 2 * nv + 8)).astype(np.float16),  # a | b | pad
-        alog=rng.uniform(-2, 1, nv).astype(np.float32),
+        alog=rng.uniform(alog[0], alog[1], nv).astype(np.float32),
         dtb=rng.uniform(-1, 1, nv).astype(np.float32),
         state=(rng.standard_normal((nv, d, d)) * 0.05).astype(np.float32),
         z=rng.standard_normal((T, nv * d)).astype(np.float16),
@@ -66,9 +66,28 @@ def _gpu(cs, T, nk, nv, dev):
     return out.float().cpu().numpy(), conv.cpu().numpy(), state.cpu().numpy()
 
 
-@pytest.mark.parametrize("T,nk,nv", [(1, 2, 4), (3, 2, 4), (70, 2, 4), (40, 16, 32)])
+# 513 and 600 tokens (17 and 19 chunks) run the split scan: two segments at once,
+# the second from a zero state and as the transition scan, joined afterwards;
+# 513 leaves a one-token last chunk in the second segment.
+@pytest.mark.parametrize("T,nk,nv", [(1, 2, 4), (3, 2, 4), (70, 2, 4), (40, 16, 32), (513, 4, 8),
+                                     (600, 2, 4)])
 def test_delta_prefill_matches_sequential_oracle(cuda, T, nk, nv):
     cs = _case(np.random.default_rng(T * 7 + nv), T, nk, nv)
+    got, gconv, gstate = _gpu(cs, T, nk, nv, cuda)
+    ref, rconv, rstate = _oracle(cs, T, nk, nv)
+    for t in range(T):
+        assert_close(got[t], ref[t], f"delta prefill out t={t}")
+    np.testing.assert_array_equal(gconv, rconv)
+    assert_close(gstate, rstate, "recurrent state", max_rel=1e-3)
+
+
+def test_delta_prefill_split_scan_carries_the_state_across_the_cut(cuda):
+    """Slow decay (log decay ~ -1e-3 per token): the state at the segment cut
+    still weighs on every later token and on the final state, so the joined
+    second segment (zero-start outputs + Z O_M, final state Z M + R) is
+    checked where the cut matters. 600 tokens, 19 chunks, cut after 10."""
+    T, nk, nv = 600, 2, 4
+    cs = _case(np.random.default_rng(5), T, nk, nv, alog=(-9, -6))
     got, gconv, gstate = _gpu(cs, T, nk, nv, cuda)
     ref, rconv, rstate = _oracle(cs, T, nk, nv)
     for t in range(T):
