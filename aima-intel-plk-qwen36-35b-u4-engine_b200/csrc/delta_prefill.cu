@@ -789,17 +789,30 @@ __global__ void __launch_bounds__(256) delta_scan_join_kernel(
       bulk_load(sbase + (uint32_t)(kDhd * kDhd + r * kJnLd) * 4u, src + row_off(r),
                 (uint32_t)kDhd * 4u, bar);
   }
+  // the rows this thread adds to, read while the copies land and the FMAs run
+  const int rg = tid >> 4, vg = tid & 15;
+  float* dst_base = tok ? o : state;
+  const float* add_base = tok ? o : rs;
+  float4 pa[4], pb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    pa[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (4 * rg + i < nrows) {
+      const float4* a4 = reinterpret_cast<const float4*>(add_base + row_off(4 * rg + i));
+      pa[i] = a4[vg];
+      pb[i] = a4[16 + vg];
+    }
+  }
   if (!mbar_wait(bar, 0)) {
     if (tid == 0) atomicAdd(&g_delta_wait_timeouts, 1);
     return;
   }
-  const int rg = tid >> 4, vg = tid & 15;
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-#pragma unroll 2
+#pragma unroll 4
   for (int k = 0; k < kDhd; k += 4) {
     float xa[4][4];
 #pragma unroll
@@ -818,15 +831,12 @@ __global__ void __launch_bounds__(256) delta_scan_join_kernel(
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xa[i][kk], zv[j], acc[i][j]);
     }
   }
-  float* dst_base = tok ? o : state;
-  const float* add_base = tok ? o : rs;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = 4 * rg + i;
     if (r >= nrows) break;
     const size_t off = row_off(r);
-    const float4 a = reinterpret_cast<const float4*>(add_base + off)[vg];
-    const float4 b = reinterpret_cast<const float4*>(add_base + off)[16 + vg];
+    const float4 a = pa[i], b = pb[i];
     reinterpret_cast<float4*>(dst_base + off)[vg] =
         make_float4(a.x + acc[i][0], a.y + acc[i][1], a.z + acc[i][2], a.w + acc[i][3]);
     reinterpret_cast<float4*>(dst_base + off)[16 + vg] =
