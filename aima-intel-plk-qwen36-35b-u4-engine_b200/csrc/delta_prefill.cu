@@ -32,6 +32,7 @@
 // Conv with fp16 rounding points of iq36_linear_conv_swish.cl:25-63; gates of
 // gguf_loader.cpp:4875-4912; gated RMSNorm of gguf_loader.cpp:4770-4786.
 
+#include <algorithm>
 #include <atomic>
 
 #include "launch.cuh"
@@ -374,9 +375,9 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
 struct ScanSeg {
   const float* s_in;  // incoming state per head [128 keys][128 values] (start 0)
   float* s_out;       // final state, same layout
-  float* o;           // outputs: row (t - t_off) of [rows, nv, 128]
+  float* o;           // output (t, h, v) at (t - t_off) o_ts + h o_hs + v
   int c0, c1;         // chunks [c0, c1)
-  int t_off;
+  int t_off, o_ts, o_hs;
   int start;          // 0: s_in, 1: zero state, 2: identity state and U = 0
 };
 struct ScanSegs {
@@ -577,13 +578,13 @@ __global__ void __launch_bounds__(kScThreads, 1)
     const float* stg = reinterpret_cast<const float*>(smem + kScStg);
     auto store_o = [&](int cc) {
       const int t0 = (c0 + cc) * kCk, n = min(kCk, T - t0);
-      float* orow = sg.o + ((size_t)(t0 - sg.t_off) * nv + h) * kDhd + v;
+      float* orow = sg.o + (size_t)(t0 - sg.t_off) * sg.o_ts + (size_t)h * sg.o_hs + v;
       uint32_t oa[32];
       tmem_ld32(tmem + kTmX + 64u * (uint32_t)(cc & 1) + lane_off + 32, oa);
       tmem_ld_wait();
 #pragma unroll
       for (int tt = 0; tt < kCk; ++tt)
-        if (tt < n) orow[(size_t)tt * nv * kDhd] = __uint_as_float(oa[tt]);
+        if (tt < n) orow[(size_t)tt * sg.o_ts] = __uint_as_float(oa[tt]);
     };
     for (int c = 0; c < nchunks && ok; ++c) {
       const int b = c & 1;
@@ -741,108 +742,175 @@ __global__ void __launch_bounds__(kScThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-// 4b. joins segment 1 of a split scan to segment 0. Per value head, row r of a
-// tile: dst[r][v] = add[r][v] + sum_k' src[r][k'] Z[k'][v], Z = the state at
-// the cut ([128 k'][128 v], segment 0's final state). Token rows: src = O_M,
-// add = dst = the zero-start outputs; state rows (the last two tiles of the
-// grid): src = M, add = R, dst = the real state. fp32 FMAs in k' order.
-// Thread = 4 rows x 8 columns (v = 4j..4j+3 and 64+4j..), Z and the tile's
-// rows in shared memory, placed by bulk copies (rows padded to 132 floats: the
-// two row groups of a warp fall in different banks).
-constexpr int kJnRows = 64, kJnLd = 132;
-constexpr int kJoinBar = (kDhd * kDhd + kJnRows * kJnLd) * 4;
-constexpr int kJoinSmem = kJoinBar + 16;
-__global__ void __launch_bounds__(256) delta_scan_join_kernel(
-    const float* __restrict__ zst, const float* __restrict__ om, float* __restrict__ o,
-    const float* __restrict__ ms, const float* __restrict__ rs, float* __restrict__ state,
-    int T1, int nv) {
-  extern __shared__ float4 jsm4[];
-  float* sz = reinterpret_cast<float*>(jsm4);
-  float* sx = sz + kDhd * kDhd;
-  const uint32_t sbase = smem_u32(jsm4), bar = sbase + kJoinBar;
-  const int h = blockIdx.y, tid = threadIdx.x;
-  const int ntt = (T1 + kJnRows - 1) / kJnRows;
-  const bool tok = (int)blockIdx.x < ntt;
-  const int r0 = (tok ? (int)blockIdx.x : (int)blockIdx.x - ntt) * kJnRows;
-  const int nrows = tok ? min(kJnRows, T1 - r0) : kJnRows;
-  auto row_off = [&](int r) -> size_t {  // float offset of row r in src / add / dst
-    return tok ? ((size_t)(r0 + r) * nv + h) * kDhd : ((size_t)h * kDhd + r0 + r) * kDhd;
-  };
-  const float* src = tok ? om : ms;
+// 4b. joins segment 1 of a split scan to segment 0. Per value head, row r:
+// dst[r][v] = add[r][v] + sum_k' src[r][k'] Z[k'][v], Z = the state at the cut
+// ([128 k'][128 v], segment 0's final state). Token rows: src = O_M, add = dst
+// = the zero-start outputs; state rows (the last 128-row tile of each head):
+// src = M, add = R, dst = the real state.
+//
+// On tcgen05, 3xTF32 like the scan, in the scan's own shape: D^T [128 v x 128
+// rows] = Z^T X^T with A = Z^T from TMEM (lane = v, column = k'; the raw value
+// and its lo part, written once per CTA) and B = the tile's rows [128 x 128 k']
+// K-major SWIZZLE_128B in shared memory, placed by TMA (double-buffered) with
+// their lo parts written beside them; 16 k-steps x 3 MMAs of N = 128. O_M
+// ([nv][T1][128]) and M ([nv][128][128]) are one row-major block, so a tile is
+// four 32-column boxes of one tensor map. A CTA takes every gridDim.x-th tile
+// of one head. 8 warps: warp w moves lanes 32 (w % 4).. and columns
+// 64 (w / 4).. of TMEM; the epilogue's reads and writes run along v, so each
+// warp touches 128 contiguous bytes per row.
+constexpr int kJnRows = 128;
+constexpr uint32_t kJnX = 0, kJnXLo = 131072, kJnBar = 196608;  // X: 2 x 64 KB
+constexpr int kJoinSmem = (int)kJnBar + 64 + 1024;
+constexpr uint32_t kJnTmD = 0, kJnTmHi = 128, kJnTmLo = 256;
+__global__ void __launch_bounds__(256, 1) delta_scan_join_kernel(
+    const __grid_constant__ CUtensorMap tmX, const float* __restrict__ zst,
+    float* __restrict__ o, const float* __restrict__ rs, float* __restrict__ state, int T1,
+    int nv) {
+  extern __shared__ uint8_t jsm_raw[];
+  const uint32_t base_raw = smem_u32(jsm_raw);
+  const uint32_t base = (base_raw + 1023u) & ~1023u;
+  uint8_t* smem = jsm_raw + (base - base_raw);
+  const uint32_t full = base + kJnBar, mma_bar = base + kJnBar + 16;  // full[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kJnBar + 32);
+  const int h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ntt = (T1 + kJnRows - 1) / kJnRows, ntiles = ntt + 1;
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(full, 1);
+    mbar_init(full + 8, 1);
+    mbar_init(mma_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  // rows past the end are zero (generic stores; the copies write other rows)
-  for (int i = nrows * 32 + tid; i < kJnRows * 32; i += 256) {
-    const int r = i >> 5, c4 = i & 31;
-    *reinterpret_cast<float4*>(sx + r * kJnLd + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
   }
+  tc_fence_before();
   __syncthreads();
-  pdl_wait();  // Z, O_M, M and R come from the scan
-  if (tid < 32) {
-    if (tid == 0) mbar_arrive_tx(bar, (uint32_t)(kDhd * kDhd * 4 + nrows * kDhd * 4));
-    __syncwarp();
-    if (tid < 4)
-      bulk_load(sbase + tid * 16384u, zst + (size_t)h * kDhd * kDhd + tid * 4096, 16384u, bar);
-    for (int r = tid; r < nrows; r += 32)
-      bulk_load(sbase + (uint32_t)(kDhd * kDhd + r * kJnLd) * 4u, src + row_off(r),
-                (uint32_t)kDhd * 4u, bar);
-  }
-  // the rows this thread adds to, read while the copies land and the FMAs run
-  const int rg = tid >> 4, vg = tid & 15;
-  float* dst_base = tok ? o : state;
-  const float* add_base = tok ? o : rs;
-  float4 pa[4], pb[4];
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // Z, O_M, O_R, M and R come from the scan
+  // tile (in this CTA's order `it`) into X buffer it % 2 (thread 0)
+  auto load_tile = [&](int it) {
+    const int tile = blockIdx.x + it * gridDim.x;
+    const int row = tile < ntt ? h * T1 + tile * kJnRows : nv * T1 + h * kDhd;
+    const uint32_t b = (uint32_t)(it & 1);
+    mbar_arrive_tx(full + 8 * b, 65536u);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    pa[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (4 * rg + i < nrows) {
-      const float4* a4 = reinterpret_cast<const float4*>(add_base + row_off(4 * rg + i));
-      pa[i] = a4[vg];
-      pb[i] = a4[16 + vg];
+    for (int q = 0; q < 4; ++q)
+      tma_load_2d(base + kJnX + b * 65536u + q * 16384u, &tmX, 32 * q, row, full + 8 * b);
+  };
+  const int nmine = ((int)blockIdx.x < ntiles) ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  if (tid == 0) {
+    if (nmine > 0) load_tile(0);
+    if (nmine > 1) load_tile(1);
+  }
+  const int sp = warp & 3, hf = warp >> 2;
+  const int v = 32 * sp + lane;  // this thread's TMEM lane = value column
+  const uint32_t lane_off = (uint32_t)(32 * sp) << 16;
+  {
+    // A = Z^T: lane v, columns k' = 64 hf .. 64 hf + 63 (all loads in flight at once)
+    const float* z = zst + (size_t)h * kDhd * kDhd + (size_t)(64 * hf) * kDhd + v;
+    float zv[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) zv[i] = z[(size_t)i * kDhd];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      uint32_t vh[16], vl[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        vh[e] = __float_as_uint(zv[16 * g + e]);
+        vl[e] = tf32_lo(zv[16 * g + e]);
+      }
+      tmem_st16(tmem + kJnTmHi + lane_off + 64 * hf + 16 * g, vh);
+      tmem_st16(tmem + kJnTmLo + lane_off + 64 * hf + 16 * g, vl);
     }
+    tmem_st_wait();
   }
-  if (!mbar_wait(bar, 0)) {
-    if (tid == 0) atomicAdd(&g_delta_wait_timeouts, 1);
-    return;
-  }
-  float acc[4][8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  bool ok = true;
+  for (int it = 0; it < nmine; ++it) {
+    const int tile = blockIdx.x + it * gridDim.x;
+    const int b = it & 1;
+    const int r0 = tile < ntt ? tile * kJnRows : 0;
+    const int nrows = tile < ntt ? min(kJnRows, T1 - r0) : kJnRows;
+    ok = __syncthreads_and(mbar_wait(full + 8 * b, (it >> 1) & 1));
+    if (!ok) break;
+    // lo parts of the tile, same (swizzled) positions
+    {
+      const uint4* xs = reinterpret_cast<const uint4*>(smem + kJnX + b * 65536);
+      uint4* xl = reinterpret_cast<uint4*>(smem + kJnXLo);
 #pragma unroll 4
-  for (int k = 0; k < kDhd; k += 4) {
-    float xa[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 x = *reinterpret_cast<const float4*>(sx + (4 * rg + i) * kJnLd + k);
-      xa[i][0] = x.x, xa[i][1] = x.y, xa[i][2] = x.z, xa[i][3] = x.w;
+      for (int i = tid; i < 4096; i += 256) {
+        const uint4 x = xs[i];
+        xl[i] = make_uint4(tf32_lo(__uint_as_float(x.x)), tf32_lo(__uint_as_float(x.y)),
+                           tf32_lo(__uint_as_float(x.z)), tf32_lo(__uint_as_float(x.w)));
+      }
     }
+    fence_proxy_async_smem();  // generic writes before the MMAs read them
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint64_t dxh = sw128_desc(base + kJnX + b * 65536u), dxl = sw128_desc(base + kJnXLo);
+      const uint32_t d = tmem + kJnTmD, zhi = tmem + kJnTmHi, zlo = tmem + kJnTmLo;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const float4 za = *reinterpret_cast<const float4*>(sz + (k + kk) * kDhd + 4 * vg);
-      const float4 zb = *reinterpret_cast<const float4*>(sz + (k + kk) * kDhd + 64 + 4 * vg);
-      const float zv[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(xa[i][kk], zv[j], acc[i][j]);
+      for (int j = 0; j < 16; ++j) {
+        const uint64_t off = (uint64_t)((j >> 2) * 16384 + (j & 3) * 32) >> 4;
+        umma_tf32_ts(d, zhi + 8 * j, dxh + off, tf32_idesc(128), j > 0 ? 1u : 0u);
+        umma_tf32_ts(d, zhi + 8 * j, dxl + off, tf32_idesc(128), 1u);
+        umma_tf32_ts(d, zlo + 8 * j, dxh + off, tf32_idesc(128), 1u);
+      }
+      umma_commit(mma_bar);
     }
-  }
+    // the values this thread adds to (column v of rows 64 hf ..), read while the MMAs run
+    float* dst = tile < ntt ? o + ((size_t)r0 * nv + h) * kDhd + v : state + (size_t)h * kDhd * kDhd + v;
+    const float* add = tile < ntt ? (const float*)o + ((size_t)r0 * nv + h) * kDhd + v
+                                  : rs + (size_t)h * kDhd * kDhd + v;
+    const size_t rstride = tile < ntt ? (size_t)nv * kDhd : (size_t)kDhd;
+    float av[64];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = 4 * rg + i;
-    if (r >= nrows) break;
-    const size_t off = row_off(r);
-    const float4 a = pa[i], b = pb[i];
-    reinterpret_cast<float4*>(dst_base + off)[vg] =
-        make_float4(a.x + acc[i][0], a.y + acc[i][1], a.z + acc[i][2], a.w + acc[i][3]);
-    reinterpret_cast<float4*>(dst_base + off)[16 + vg] =
-        make_float4(b.x + acc[i][4], b.y + acc[i][5], b.z + acc[i][6], b.w + acc[i][7]);
+    for (int i = 0; i < 64; ++i) {
+      const int r = 64 * hf + i;
+      av[i] = r < nrows ? add[(size_t)r * rstride] : 0.f;
+    }
+    ok = __syncthreads_and(mbar_wait(mma_bar, it & 1));
+    if (!ok) break;
+    tc_fence_after();
+    // X buffer b is free again: the tile after next goes into it
+    if (tid == 0 && it + 2 < nmine) load_tile(it + 2);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      uint32_t dv[16];
+      tmem_ld16(tmem + kJnTmD + lane_off + 64 * hf + 16 * g, dv);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int r = 64 * hf + 16 * g + e;
+        if (r < nrows) dst[(size_t)r * rstride] = av[16 * g + e] + __uint_as_float(dv[e]);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // D and the lo buffer are rewritten by the next tile
   }
+  if (!ok && tid == 0) atomicAdd(&g_delta_wait_timeouts, 1);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   pdl_launch_dependents();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// 2-D fp32 row-major tensor map [rows][128], box 32 columns x 128 rows,
+// SWIZZLE_128B (each box lands as one SW128 K-major slab).
+static bool make_join_map(CUtensorMap* m, const float* ptr, uint64_t rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kDhd, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kDhd * 4};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)kJnRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int delta_wait_timeouts(int* count, int reset) {
@@ -901,7 +969,7 @@ __global__ void __launch_bounds__(256) delta_gated_norm_kernel(const float* o, c
 
 // workspace: qk fp32 [T, 2nk, D] | v fp16 [T, nv*D] | g, beta fp32 [T, nv] | o fp32 [T, nv, D]
 // | chunk operand blocks [ceil(T/32), nv, kCkBlk] fp32 | gC [ceil(T/32), nv]; a split
-// scan adds the states Z, R, M [nv, D, D] and O_M [T - 32 m, nv, D]
+// scan adds the states Z, R [nv, D, D], O_M [nv, T - 32 m, D] and M [nv, D, D]
 struct DeltaWs {
   size_t qk, v, decay, beta, o, blocks, gcs, zst, rst, mst, om, total;
 };
@@ -919,9 +987,9 @@ static DeltaWs delta_ws(int T, int nk, int nv) {
   const int m = scan_split(T);
   const size_t st = m ? (size_t)nv * kDhd * kDhd * 4 : 0;
   w.rst = w.zst + st;
-  w.mst = w.rst + st;
-  w.om = w.mst + st;
-  w.total = up(w.om + (m ? (size_t)(T - m * kCk) * nv * kDhd * 4 : 0));
+  w.om = w.rst + st;  // O_M, then M right behind it (one row-major block)
+  w.mst = w.om + (m ? (size_t)(T - m * kCk) * nv * kDhd * 4 : 0);
+  w.total = up(w.mst + st);
   return w;
 }
 
@@ -996,23 +1064,35 @@ extern "C" int iq36_delta_prefill(const void* qkv_f16, int32_t tokens, int32_t n
   const int nchunks = ceil_div(T, kCk), m = scan_split(T);
   ScanSegs sgs = {};
   if (!m) {
-    sgs.s[0] = ScanSeg{state, state, o, 0, nchunks, 0, 0};
+    sgs.s[0] = ScanSeg{state, state, o, 0, nchunks, 0, nv * kDhd, kDhd, 0};
   } else {
     float* zst = reinterpret_cast<float*>(ws + w.zst);
-    sgs.s[0] = ScanSeg{state, zst, o, 0, m, 0, 0};
-    sgs.s[1] = ScanSeg{nullptr, reinterpret_cast<float*>(ws + w.rst), o, m, nchunks, 0, 1};
+    sgs.s[0] = ScanSeg{state, zst, o, 0, m, 0, nv * kDhd, kDhd, 0};
+    sgs.s[1] = ScanSeg{nullptr, reinterpret_cast<float*>(ws + w.rst), o, m, nchunks, 0,
+                       nv * kDhd, kDhd, 1};
+    // O_M head-major: the join copies a tile's rows as one block
     sgs.s[2] = ScanSeg{nullptr, reinterpret_cast<float*>(ws + w.mst),
-                       reinterpret_cast<float*>(ws + w.om), m, nchunks, m * kCk, 2};
+                       reinterpret_cast<float*>(ws + w.om), m, nchunks, m * kCk, kDhd,
+                       (T - m * kCk) * kDhd, 2};
   }
   if (e == cudaSuccess)
     e = launch(delta_chunk_scan_kernel, dim3(nv, m ? 3 : 1), dim3(kScThreads), (size_t)kScanSmem,
                s, (const float*)blocks, (const float*)gcs, sgs, T, nv);
   if (e == cudaSuccess && m) {
     const int T1 = T - m * kCk;
-    e = launch(delta_scan_join_kernel, dim3(ceil_div(T1, kJnRows) + kDhd / kJnRows, nv),
-               dim3(256), (size_t)kJoinSmem, s, (const float*)(ws + w.zst),
-               (const float*)(ws + w.om), o + (size_t)m * kCk * nv * kDhd,
-               (const float*)(ws + w.mst), (const float*)(ws + w.rst), state, T1, nv);
+    // CTAs per head: the tiles of one head share its Z^T; one wave of CTAs
+    const int tiles = ceil_div(T1, kJnRows) + 1;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return IQ36_ERR_CUDA;
+    const int cph = std::max(1, std::min(tiles, sms / nv));
+    CUtensorMap tmx;
+    if (!make_join_map(&tmx, reinterpret_cast<const float*>(ws + w.om),
+                       (uint64_t)nv * (T1 + kDhd)))
+      return IQ36_ERR_CUDA;
+    e = launch(delta_scan_join_kernel, dim3(cph, nv), dim3(256), (size_t)kJoinSmem, s, tmx,
+               (const float*)(ws + w.zst), o + (size_t)m * kCk * nv * kDhd,
+               (const float*)(ws + w.rst), state, T1, nv);
   }
   if (e == cudaSuccess)
     e = launch(delta_gated_norm_kernel, dim3(ceil_div(T * nv, 32)), dim3(256), 0, s,
