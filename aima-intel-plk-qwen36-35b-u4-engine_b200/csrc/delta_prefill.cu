@@ -304,11 +304,18 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float* __re
         else blk[kBlkP + sw128_f(r, s2)] = dec * cc[nt][e2];
       }
   } else {
-    for (int i = tid - 128; i < kCk * kDhd; i += 128) {
-      const int r = i >> 7, d = i & 127;
-      blk[blk_b1(kCk + r, d)] = sE[r] * sq[r * 132 + d];
-      const int dk = i >> 5, rk = i & 31;  // Kt[dk][rk]
-      blk[kBlkKt + sw128_f(dk, rk)] = sL[rk] * sk[rk * 132 + dk];
+    // four consecutive columns of a row are one 16-byte chunk of the swizzled image
+    for (int i = tid - 128; i < kCk * kDhd / 4; i += 128) {
+      const int r = i >> 5, d = 4 * (i & 31);
+      const float e = sE[r];
+      const float4 x = *reinterpret_cast<const float4*>(sq + r * 132 + d);
+      *reinterpret_cast<float4*>(blk + blk_b1(kCk + r, d)) =
+          make_float4(e * x.x, e * x.y, e * x.z, e * x.w);
+      const int dk = i >> 3, rk = 4 * (i & 7);  // Kt[dk][rk .. rk + 3]
+      const float4 l = *reinterpret_cast<const float4*>(sL + rk);
+      *reinterpret_cast<float4*>(blk + kBlkKt + sw128_f(dk, rk)) =
+          make_float4(l.x * sk[rk * 132 + dk], l.y * sk[(rk + 1) * 132 + dk],
+                      l.z * sk[(rk + 2) * 132 + dk], l.w * sk[(rk + 3) * 132 + dk]);
     }
   }
   __syncthreads();
