@@ -434,7 +434,10 @@ int iq36_delta_step(const void* qkv_act_f16, const float* g, const float* beta, 
 
 /* The DeltaNet block over T prompt tokens: the arithmetic of iq36_delta_prep
  * followed by iq36_delta_step for tokens 0..T-1 in order (conv state and
- * recurrent state carried in and out), in four launches. Replaces the
+ * recurrent state carried in and out), in five launches; from 16 chunks of
+ * 32 tokens on, the recurrence runs as two segments at once plus a join
+ * launch (same result within fp32 rounding, not bit for bit, and more
+ * workspace: query it for each token count). Replaces the
  * per-token loop over the reference's linear-attention layer during prompt
  * processing (iq36_linear_conv_swish.cl:12-64, iq36_gated_delta_net.cl:36-150,
  * gguf_loader.cpp:4770-4786 and :4875-4912).
